@@ -1,0 +1,115 @@
+/* mcpm.h -- C ABI of the B200 MiniCPM5 decode engine.
+ *
+ * Drop-in boundary for the reference's hot path (astrowar/MiniCPM5.cpp):
+ *   engine : class MiniCPM5Engine           include/model.h:37-70, src/model.cpp:17-242
+ *   ops    : quantised GEMV / norm / SwiGLU include/ops.h:113-160, src/ops/ops_internal.h:15-54
+ * Plain pointers and sizes only.  Every function returns an mcpm_status; nothing throws
+ * across the ABI and nothing is silently zero-filled (the reference prints a warning and
+ * fills outputs with 0 / 0.001 on unsupported input, src/ops/ops.cpp:281-289, 341-348).
+ *
+ * Device-pointer functions take a CUDA stream as `void*` (NULL = legacy default stream)
+ * and are asynchronous with respect to the host.  Engine functions are synchronous
+ * unless their name ends in _async.
+ */
+#ifndef MCPM_H
+#define MCPM_H
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    MCPM_OK = 0,
+    MCPM_BAD_ARG = 1,          /* null pointer, size not a multiple of the block, ... */
+    MCPM_BAD_FILE = 2,         /* unreadable / truncated / malformed GGUF, wrong architecture */
+    MCPM_UNSUPPORTED_TYPE = 3, /* tensor type the path does not handle */
+    MCPM_CTX_OVERFLOW = 4,     /* pos >= max_seq (reference: warning + stale output, ops.cpp:550-553) */
+    MCPM_CUDA_ERROR = 5,
+    MCPM_NCCL_ERROR = 6,
+    MCPM_TIMEOUT = 7,          /* a bounded device-side wait gave up */
+    MCPM_OUT_OF_MEMORY = 8,
+    MCPM_BAD_TOKEN = 9,        /* token id outside [0, n_vocab) */
+    MCPM_NOT_LOADED = 10       /* engine call before mcpm_load_gguf / mcpm_init_kv */
+} mcpm_status;
+
+const char* mcpm_status_string(mcpm_status s);
+
+/* ------------------------------------------------------------------ engine */
+typedef struct mcpm_engine mcpm_engine;
+
+typedef struct {
+    int device;      /* CUDA device ordinal */
+    int max_seq;     /* KV-cache positions (reference init_kv_cache(max_seq_len), model.cpp:17-24); <= 16384 */
+    int n_ctas;      /* persistent CTAs of the decode kernel; 0 = one per SM */
+    int reserved[5];
+} mcpm_config;
+
+/* Creates an engine bound to cfg->device (MiniCPM5Engine constructor + init_kv_cache). */
+mcpm_status mcpm_engine_create(const mcpm_config* cfg, mcpm_engine** out);
+/* Parses the GGUF header, checks the MiniCPM5 tensor set, uploads every tensor's bytes
+ * unchanged into one HBM arena, builds the RoPE table and allocates the KV cache.
+ * Replaces MiniCPM5Engine::load_model (model.cpp:33-133). */
+mcpm_status mcpm_load_gguf(mcpm_engine* e, const char* path);
+/* (Re)allocates and zeroes the fp32 KV cache, layout [layer][pos][kv_head][head_dim]
+ * (reference KVCacheLayer, include/ops.h:147-150; init_kv_cache, model.cpp:17-24). */
+mcpm_status mcpm_init_kv(mcpm_engine* e, int max_seq);
+/* One decode step: embeds `token` at position `pos`, runs every layer, appends K/V at
+ * pos.  logits_out (host, n_vocab floats) and argmax_out (host) are optional.  Replaces
+ * MiniCPM5Engine::forward(token_id, pos, max_seq_len) (model.cpp:142-242); the greedy
+ * argmax (lowest index on ties) is computed on the device. */
+mcpm_status mcpm_forward(mcpm_engine* e, int token, int pos, float* logits_out, int* argmax_out);
+/* Asynchronous decode step on the engine's stream.  token < 0 reads the token id that the
+ * previous step's argmax left on the device (greedy chaining without a host round trip).
+ * write_logits = 0 skips the logits store.  Errors surface at the next mcpm_sync. */
+mcpm_status mcpm_forward_async(mcpm_engine* e, int token, int pos, int write_logits);
+mcpm_status mcpm_sync(mcpm_engine* e);
+/* Device pointers of the last step's logits (n_vocab floats) and argmax (one int). */
+const float* mcpm_logits_device(mcpm_engine* e);
+const int* mcpm_argmax_device(mcpm_engine* e);
+/* Internal state for parity checks: residual x (n_embd floats), one K and V row. */
+mcpm_status mcpm_read_x(mcpm_engine* e, float* x_host);
+mcpm_status mcpm_read_kv(mcpm_engine* e, int layer, int pos, float* k_host, float* v_host);
+/* n_layer, n_embd, n_ff, n_head, n_head_kv, n_vocab of the loaded model. */
+mcpm_status mcpm_model_dims(mcpm_engine* e, int dims[6]);
+/* The engine's CUDA stream (cudaStream_t) and decode grid size. */
+void* mcpm_engine_stream(mcpm_engine* e);
+int mcpm_engine_n_ctas(mcpm_engine* e);
+void mcpm_engine_destroy(mcpm_engine* e);
+
+/* ------------------------------------------------------------------ ops (device pointers)
+ * Block layouts are the reference's: block_q4_K 144 B, block_q6_K 210 B, block_q8_0 34 B,
+ * block_q8_K 292 B (include/ops.h:33-65).  `type` is the ggml type id (12 = Q4_K,
+ * 14 = Q6_K).  `rows` x `cols` is the matrix shape (GGUF dims[1] x dims[0]); weight
+ * pointers must be 16-byte aligned and cols <= 6144 (Q6_K: cols % 2048 == 0).
+ */
+enum { MCPM_ROUND_EVEN = 0, MCPM_ROUND_AWAY = 1 };
+
+/* fp32 -> Q8_K.  MCPM_ROUND_EVEN: quantize_row_q8_K_avx2 (ops_avx2.cpp:85-144);
+ * MCPM_ROUND_AWAY: the lround quantisers of ops.cpp:702-722.  n % 256 == 0. */
+mcpm_status mcpm_quantize_q8k(const float* x, void* y, int n, int rounding, void* stream);
+/* y = W xq for Q4_K / Q6_K weights: gemv_q4_K_q8_K_avx2 / gemv_q6_K_q8_K_avx2
+ * (ops_avx2.cpp:278-298) behind matmul_q8k (ops.cpp:317-349); bit-identical results. */
+mcpm_status mcpm_gemv_q8k(int type, const void* w, const void* xq, float* y, int rows, int cols, void* stream);
+/* Integer block sums of the same product, [rows][cols/256] each: Q4_K isum = sum_j sc_j*dot_j,
+ * aux = sum_g mn_g*(bsums[2g]+bsums[2g+1]); Q6_K isum = sum sc*q*x over unsigned q,
+ * aux = 32*sum_g sc_g*bsums_g (dot_row_q{4,6}_K_q8_K_scalar, ops_scalar_optimized.cpp:139-404). */
+mcpm_status mcpm_gemv_blocksums(int type, const void* w, const void* xq, int32_t* isum, int32_t* aux, int rows,
+                                int cols, void* stream);
+/* gate = Wg xq, up = Wu xq (gemv_gate_up_q4_K_q8_K_avx2, ops_avx2.cpp:444-460). */
+mcpm_status mcpm_gemv_gate_up_q8k(const void* wg, const void* wu, const void* xq, float* gate, float* up, int rows,
+                                  int cols, void* stream);
+/* rmsnorm_and_quantize_q8k (ops.cpp:676-723); n == 2048. */
+mcpm_status mcpm_rmsnorm_q8k(const float* x, const float* w, void* out, int n, float eps, void* stream);
+/* swiglu_and_quantize_q8k (ops.cpp:725-765); n % 256 == 0. */
+mcpm_status mcpm_swiglu_q8k(const float* gate, const float* up, void* out, int n, void* stream);
+/* GEMV throughput probe: `reps` launches of mcpm_gemv_q8k rotating over `n_copies`
+ * weight copies laid out back to back from `w` (stride rows*row_bytes), so successive
+ * launches miss in L2; writes the mean device time per launch in milliseconds. */
+mcpm_status mcpm_gemv_q8k_timed(int type, const void* w, int n_copies, const void* xq, float* y, int rows, int cols,
+                                int reps, float* ms_per_launch, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MCPM_H */

@@ -1,0 +1,665 @@
+// Persistent decode kernel: one cooperative launch computes one token of
+// MiniCPM5Engine::forward (reference src/model.cpp:142-242) on every SM.
+//
+// Per layer five phases separated by a grid barrier:
+//   QKV  : RMSNorm -> Q8_K (every CTA, redundantly), fused Q/K/V GEMV over this CTA's
+//          row pairs, RoPE on Q/K pairs, K/V appended to the cache at `pos`
+//          (ops.cpp:676-723, ops_avx2.cpp:320-374, ops.cpp:502-516, 557-563)
+//   ATT  : split-KV attention, chunk partials + last-CTA combine + Q8_K (ties-to-even)
+//          quantisation of the attention output (ops.cpp:537-628, ops_avx2.cpp:85-144)
+//   O    : o_proj GEMV + residual add (model.cpp:198-203)
+//   GU   : RMSNorm -> Q8_K, gate/up GEMV, SwiGLU (ops_avx2.cpp:444-460, ops.cpp:725-765)
+//   D    : SwiGLU output -> Q8_K (every CTA), down GEMV + residual (model.cpp:220-225)
+// then the LM head (final RMSNorm, Q8_K ties-to-even, GEMV, greedy argmax).
+//
+// Weights move with TMA bulk copies (cp.async.bulk, no multicast) into two shared
+// buffers; the copy for weight phase w+1 is issued when phase w starts, so HBM keeps
+// streaming through the grid barriers.  All waits are bounded (~1 s) and report
+// ERR_TIMEOUT instead of hanging.
+#include "mcpm_device.cuh"
+#include "mcpm_internal.h"
+
+namespace mcpm {
+namespace {
+
+struct Smem {
+    uint8_t* wbuf[2];
+    XQSmem* xq;
+    int* part;
+    float* xs;       // staged fp32 activation vector (N_EMBD)
+    float* rowval;
+    float* red;      // 32 floats
+    uint64_t* wbar;  // [2][4]
+    uint64_t* lmbar; // [4]
+    int* flag;
+};
+
+__device__ __forceinline__ void split_range(int n, int cta, int ncta, int& a, int& b) {
+    a = static_cast<int>((static_cast<long long>(n) * cta) / ncta);
+    b = static_cast<int>((static_cast<long long>(n) * (cta + 1)) / ncta);
+}
+
+// Row layout of weight phase `kind` for this CTA inside its buffer.
+struct PhaseLayout {
+    int row0[3], nrows[3];
+    uint32_t off[3], bytes[3];
+};
+
+__device__ __forceinline__ uint32_t align16(uint32_t v) { return (v + 15u) & ~15u; }
+
+__device__ PhaseLayout phase_layout(const LayerDev& L, int kind, int cta, int ncta) {
+    PhaseLayout pl;
+    for (int i = 0; i < 3; ++i) pl.row0[i] = pl.nrows[i] = 0, pl.off[i] = pl.bytes[i] = 0;
+    int a, b;
+    if (kind == 0) {   // QKV: row pairs of the combined [Q; K; V] rows
+        split_range(QKV_ROWS / 2, cta, ncta, a, b);
+        a *= 2;
+        b *= 2;
+        const int lo[3] = {0, N_EMBD, N_EMBD + KV_DIM}, hi[3] = {N_EMBD, N_EMBD + KV_DIM, QKV_ROWS};
+        const int types[3] = {L.tq, L.tk, L.tv};
+        uint32_t off = 0;
+        for (int i = 0; i < 3; ++i) {
+            const int s = max(a, lo[i]), e = min(b, hi[i]);
+            pl.row0[i] = max(0, s - lo[i]);
+            pl.nrows[i] = max(0, e - s);
+            pl.off[i] = off;
+            pl.bytes[i] = pl.nrows[i] * row_bytes(types[i], N_EMBD);
+            off = align16(off + pl.bytes[i]);
+        }
+    } else if (kind == 1 || kind == 3) {   // O, D: 2048 output rows
+        split_range(N_EMBD, cta, ncta, a, b);
+        pl.row0[0] = a;
+        pl.nrows[0] = b - a;
+        pl.bytes[0] = (b - a) * (kind == 1 ? row_bytes(L.to, N_EMBD) : row_bytes(L.td, N_FF));
+    } else {   // GU: gate rows then up rows
+        split_range(N_FF, cta, ncta, a, b);
+        pl.row0[0] = pl.row0[1] = a;
+        pl.nrows[0] = pl.nrows[1] = b - a;
+        pl.bytes[0] = (b - a) * row_bytes(L.tg, N_EMBD);
+        pl.off[1] = align16(pl.bytes[0]);
+        pl.bytes[1] = (b - a) * row_bytes(L.tu, N_EMBD);
+    }
+    return pl;
+}
+
+__device__ const uint8_t* phase_src(const LayerDev& L, int kind, int i) {
+    if (kind == 0) return i == 0 ? L.wq : i == 1 ? L.wk : L.wv;
+    if (kind == 1) return L.wo;
+    if (kind == 2) return i == 0 ? L.wg : L.wu;
+    return L.wd;
+}
+
+__device__ int phase_type(const LayerDev& L, int kind, int i) {
+    if (kind == 0) return i == 0 ? L.tq : i == 1 ? L.tk : L.tv;
+    if (kind == 1) return L.to;
+    if (kind == 2) return i == 0 ? L.tg : L.tu;
+    return L.td;
+}
+
+__device__ int phase_cols(int kind) { return kind == 3 ? N_FF : N_EMBD; }
+
+// Thread 0 only: arm the four barriers of buffer (wp & 1) and issue weight phase `wp`.
+__device__ void issue_weight_phase(const DecodeParams& p, const Smem& s, int wp, int cta, int ncta) {
+    const int buf = wp & 1;
+    uint64_t* bars = s.wbar + 4 * buf;
+    const int l = wp >> 2, kind = wp & 3;
+    const LayerDev& L = p.layers[l];
+    const PhaseLayout pl = phase_layout(L, kind, cta, ncta);
+    for (int i = 0; i < 3; ++i) {
+        mbar_expect_tx(&bars[i], pl.bytes[i]);
+        if (pl.bytes[i]) {
+            const int rb = row_bytes(phase_type(L, kind, i), phase_cols(kind));
+            bulk_g2s(s.wbuf[buf] + pl.off[i], phase_src(L, kind, i) + static_cast<size_t>(pl.row0[i]) * rb,
+                     pl.bytes[i], &bars[i]);
+        }
+    }
+    mbar_expect_tx(&bars[3], 0);
+}
+
+// LM-head ring: stage st covers rows [r0 + st*SR, ...) of this CTA's vocabulary range.
+struct LmPlan {
+    int r0, r1, sr, nstages, rb, nb;
+};
+__device__ LmPlan lm_plan(const DecodeParams& p, int cta, int ncta) {
+    LmPlan q;
+    split_range(p.n_vocab, cta, ncta, q.r0, q.r1);
+    q.rb = row_bytes(p.lm_type, N_EMBD);
+    q.nb = N_EMBD / 256;
+    q.sr = min(LM_SLOT_BYTES / q.rb, MAX_TASKS / q.nb);
+    q.nstages = (q.r1 - q.r0 + q.sr - 1) / q.sr;
+    return q;
+}
+__device__ uint8_t* lm_slot(const Smem& s, int slot) { return s.wbuf[slot >> 1] + (slot & 1) * LM_SLOT_BYTES; }
+__device__ void issue_lm_stage(const DecodeParams& p, const Smem& s, const LmPlan& q, int st) {
+    const int slot = st & 3;
+    const int a = q.r0 + st * q.sr, n = min(q.sr, q.r1 - a);
+    const uint32_t bytes = n > 0 ? static_cast<uint32_t>(n) * q.rb : 0;
+    mbar_expect_tx(&s.lmbar[slot], bytes);
+    if (bytes) bulk_g2s(lm_slot(s, slot), p.lm + static_cast<size_t>(a) * q.rb, bytes, &s.lmbar[slot]);
+}
+
+// Bounded grid barrier (all CTAs co-resident: cooperative launch).  Returns false if
+// any CTA has flagged an error; callers then return.
+__device__ bool grid_barrier(const DecodeParams& p) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned* count = p.bar;
+        unsigned* gen = p.bar + 1;
+        const unsigned g = ld_acquire_u32(gen);
+        __threadfence();
+        const unsigned arrived = atomicAdd(count, 1u);
+        if (arrived == gridDim.x - 1) {
+            atomicExch(count, 0u);
+            __threadfence();
+            st_release_u32(gen, g + 1);
+        } else {
+            const uint64_t t0 = globaltimer();
+            while (ld_acquire_u32(gen) == g) {
+                if (globaltimer() - t0 > 1000000000ull) {
+                    atomicOr(p.err, ERR_TIMEOUT);
+                    break;
+                }
+            }
+        }
+        __threadfence();
+    }
+    __syncthreads();
+    return ld_acquire_u32(p.err) == 0;
+}
+
+// Waits for this CTA's part of weight phase wp; false on timeout.
+__device__ bool wait_weights(const DecodeParams& p, const Smem& s, int wp) {
+    const int buf = wp & 1;
+    const uint32_t parity = (wp >> 1) & 1;
+    bool ok = true;
+    for (int i = 0; i < 4; ++i) ok &= mbar_wait(&s.wbar[4 * buf + i], parity, p.err);
+    return ok;
+}
+
+// ------------------------------------------------------------- activation prologues
+// xs <- embedding row of `token` (get_embedding, ops.cpp:631-673; Q4_K rows).
+__device__ void embed_row(const DecodeParams& p, int token, float* xs) {
+    const int tid = threadIdx.x;
+    if (tid < 256) {
+        const int b = tid >> 5, l = tid & 31;   // block b, elements 8l .. 8l+7
+        const uint8_t* blk = p.embd + (static_cast<size_t>(token) * (N_EMBD / 256) + b) * Q4K_BYTES;
+        const uint32_t w0 = *reinterpret_cast<const uint32_t*>(blk);
+        const float d = h2f(w0), dmin = h2f(w0 >> 16);
+        const int j = (8 * l) >> 6, i0 = (8 * l) & 63;   // 64-element chunk, offset inside it
+        const bool hi = i0 >= 32;
+        const uint8_t* q = blk + 4;
+        const int sub = 2 * j + (hi ? 1 : 0);
+        int sc, mn;
+        if (sub < 4) {
+            sc = q[sub] & 63;
+            mn = q[sub + 4] & 63;
+        } else {
+            sc = (q[sub + 4] & 15) | ((q[sub - 4] >> 6) << 4);
+            mn = (q[sub + 4] >> 4) | ((q[sub] >> 6) << 4);
+        }
+        const float d1 = __fmul_rn(d, static_cast<float>(sc)), m1 = __fmul_rn(dmin, static_cast<float>(mn));
+        const uint8_t* qs = blk + 16 + 32 * j + (i0 & 31);
+        for (int k = 0; k < 8; ++k) {
+            const int nib = hi ? (qs[k] >> 4) : (qs[k] & 15);
+            xs[256 * b + 8 * l + k] = __fsub_rn(__fmul_rn(d1, static_cast<float>(nib)), m1);
+        }
+    }
+}
+
+// xq <- Q8_K of (xs * w) * rms(xs), canonical order; rounding per template argument.
+template <bool AWAY>
+__device__ void norm_quant(const float* xs, const float* w, const Smem& s) {
+    const int tid = threadIdx.x;
+    float xv[8];
+    if (tid < 256) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) xv[i] = xs[tid + 256 * i];
+    }
+    const float ss = sumsq_2048(xv, s.red);
+    const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(N_EMBD)), 1e-6f)));
+    const int warp = tid >> 5, lane = tid & 31;
+    if (warp < N_EMBD / 256) {
+        float y[8];
+        const float* xb = xs + 256 * warp + 8 * lane;
+        const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + 256 * warp + 8 * lane));
+        const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + 256 * warp + 8 * lane + 4));
+        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) y[k] = __fmul_rn(__fmul_rn(xb[k], wv[k]), rms);
+        quant_block_warp<AWAY>(y, s.xq->qs[warp], &s.xq->d[warp], s.xq->bsums[warp]);
+    }
+    __syncthreads();
+}
+
+__device__ void load_global_vec(const float* src, float* dst, int n) {
+    for (int i = threadIdx.x * 4; i < n; i += blockDim.x * 4)
+        *reinterpret_cast<float4*>(dst + i) = __ldcg(reinterpret_cast<const float4*>(src + i));
+    __syncthreads();
+}
+
+// ------------------------------------------------------------------------ phases
+__device__ void phase_qkv(const DecodeParams& p, const Smem& s, int l, int token, int cta, int ncta) {
+    const LayerDev& L = p.layers[l];
+    if (l == 0) {
+        embed_row(p, token, s.xs);
+        __syncthreads();
+        if (cta == 0)
+            for (int i = threadIdx.x; i < N_EMBD; i += blockDim.x) p.x[i] = s.xs[i];
+    } else {
+        load_global_vec(p.x, s.xs, N_EMBD);
+    }
+    norm_quant<true>(s.xs, L.attn_norm, s);
+    if (!wait_weights(p, s, 4 * l)) return;
+    const PhaseLayout pl = phase_layout(L, 0, cta, ncta);
+    const int lo[3] = {0, N_EMBD, N_EMBD + KV_DIM};
+    int a, b;
+    split_range(QKV_ROWS / 2, cta, ncta, a, b);
+    a *= 2;
+    b *= 2;
+    float* rv = s.rowval;
+    for (int i = 0; i < 3; ++i) {
+        if (pl.nrows[i] == 0) continue;   // uniform across the CTA
+        const int base = lo[i] + pl.row0[i] - a;
+        gemv_staged(phase_type(L, 0, i), s.wbuf[0] + pl.off[i], pl.nrows[i], N_EMBD / 256, *s.xq, s.part, MAX_TASKS,
+                    [&](int r, float v) { rv[base + r] = v; });
+    }
+    // RoPE on Q/K pairs (interleaved, ops.cpp:502-516 with the build's FMA contraction),
+    // then Q to the query buffer and K/V into the cache at pos (ops.cpp:557-563).
+    const float2* cs = p.rope + static_cast<size_t>(p.pos) * (HEAD_DIM / 2);
+    float* kdst = p.kc + (static_cast<size_t>(l) * p.max_seq + p.pos) * KV_DIM;
+    float* vdst = p.vc + (static_cast<size_t>(l) * p.max_seq + p.pos) * KV_DIM;
+    for (int pr = threadIdx.x; pr < (b - a) / 2; pr += blockDim.x) {
+        const int R = a + 2 * pr;
+        const float v0 = rv[2 * pr], v1 = rv[2 * pr + 1];
+        if (R < N_EMBD + KV_DIM) {
+            const float2 c = cs[(R & (HEAD_DIM - 1)) >> 1];
+            const float r0 = __fmaf_rn(c.x, v0, -__fmul_rn(c.y, v1));
+            const float r1 = __fmaf_rn(c.y, v0, __fmul_rn(c.x, v1));
+            if (R < N_EMBD) {
+                p.q[R] = r0;
+                p.q[R + 1] = r1;
+            } else {
+                kdst[R - N_EMBD] = r0;
+                kdst[R - N_EMBD + 1] = r1;
+            }
+        } else {
+            vdst[R - N_EMBD - KV_DIM] = v0;
+            vdst[R - N_EMBD - KV_DIM + 1] = v1;
+        }
+    }
+}
+
+// Canonical q.k over 128 dims by an 8-lane group (lane j: dims 4j + 32i + c, then the
+// butterfly v += v^4, v += v^2, v += v^1).  Called by all 32 lanes of the warp.
+__device__ __forceinline__ float dot128_group(const float* q, const float* k, int j) {
+    float a = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float4 qv = *reinterpret_cast<const float4*>(q + 4 * j + 32 * i);
+        const float4 kv = *reinterpret_cast<const float4*>(k + 4 * j + 32 * i);
+        a = __fmaf_rn(qv.x, kv.x, a);
+        a = __fmaf_rn(qv.y, kv.y, a);
+        a = __fmaf_rn(qv.z, kv.z, a);
+        a = __fmaf_rn(qv.w, kv.w, a);
+    }
+    a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 4));
+    a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 2));
+    a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 1));
+    return a;
+}
+
+__device__ void phase_attention(const DecodeParams& p, const Smem& s, int l, int cta, int ncta) {
+    const int n = p.pos + 1;
+    const int P = 32 * ((n + 2047) / 2048);
+    const int C = (n + P - 1) / P;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float* qh = reinterpret_cast<float*>(s.wbuf[0]);   // [8][128]
+    float* kb = qh + 8 * HEAD_DIM;                      // [32][128] staged K or V rows
+    float* sc = kb + 32 * HEAD_DIM;                     // [8][ATT_SC_STRIDE] scores -> probabilities
+    float* stat = sc + 8 * ATT_SC_STRIDE;               // m[8], l[8], 1/L[8]
+    float* wts = stat + 32;                             // [8][ATT_MAX_CHUNKS]
+    float* ab = wts + 8 * ATT_MAX_CHUNKS;               // [1024] combined output
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(HEAD_DIM)));
+    const float* kl = p.kc + static_cast<size_t>(l) * p.max_seq * KV_DIM;
+    const float* vl = p.vc + static_cast<size_t>(l) * p.max_seq * KV_DIM;
+    for (int item = cta; item < 2 * C; item += ncta) {
+        const int g = item / C, c = item % C;
+        const int t0 = c * P, t1 = min(t0 + P, n), np = t1 - t0;
+        __syncthreads();
+        if (tid < 256)
+            reinterpret_cast<float4*>(qh)[tid] = __ldcg(reinterpret_cast<const float4*>(p.q + 8 * g * HEAD_DIM) + tid);
+        for (int s0 = t0; s0 < t1; s0 += 32) {   // scores, 32 positions at a time
+            const int ns = min(32, t1 - s0);
+            __syncthreads();
+            for (int i = tid; i < ns * 32; i += blockDim.x) {
+                const int tt = i >> 5, f = i & 31;
+                reinterpret_cast<float4*>(kb)[i] = __ldcg(
+                    reinterpret_cast<const float4*>(kl + static_cast<size_t>(s0 + tt) * KV_DIM + g * HEAD_DIM) + f);
+            }
+            __syncthreads();
+            const int ndots = ns * 8;
+            for (int it = 0; it < (ndots + 63) / 64; ++it) {
+                const int di = it * 64 + (tid >> 3);
+                const bool valid = di < ndots;
+                const int h = di & 7, tt = valid ? (di >> 3) : 0;
+                const float d = dot128_group(qh + h * HEAD_DIM, kb + tt * HEAD_DIM, tid & 7);
+                if (valid && (tid & 7) == 0) sc[h * ATT_SC_STRIDE + (s0 - t0) + tt] = __fmul_rn(d, scale);
+            }
+        }
+        __syncthreads();
+        if (warp < 8) {   // chunk max, probabilities, position-ordered sum (warp = head)
+            float m = -__int_as_float(0x7f800000);
+            for (int t = lane; t < np; t += 32) m = fmaxf(m, sc[warp * ATT_SC_STRIDE + t]);
+            for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            for (int t = lane; t < np; t += 32)
+                sc[warp * ATT_SC_STRIDE + t] = canon_expf(__fsub_rn(sc[warp * ATT_SC_STRIDE + t], m));
+            __syncwarp();
+            if (lane == 0) {
+                float sum = 0.0f;
+                for (int t = 0; t < np; ++t) sum = __fadd_rn(sum, sc[warp * ATT_SC_STRIDE + t]);
+                stat[warp] = m;
+                stat[8 + warp] = sum;
+            }
+        }
+        float acc0 = 0.0f, acc1 = 0.0f;   // o[h][d] = fma chain over positions
+        const int h0 = tid >> 7, h1 = h0 + 4, dd = tid & 127;
+        for (int s0 = t0; s0 < t1; s0 += 32) {
+            const int ns = min(32, t1 - s0);
+            __syncthreads();
+            for (int i = tid; i < ns * 32; i += blockDim.x) {
+                const int tt = i >> 5, f = i & 31;
+                reinterpret_cast<float4*>(kb)[i] = __ldcg(
+                    reinterpret_cast<const float4*>(vl + static_cast<size_t>(s0 + tt) * KV_DIM + g * HEAD_DIM) + f);
+            }
+            __syncthreads();
+            for (int tt = 0; tt < ns; ++tt) {
+                const float v = kb[tt * HEAD_DIM + dd];
+                acc0 = __fmaf_rn(sc[h0 * ATT_SC_STRIDE + (s0 - t0) + tt], v, acc0);
+                acc1 = __fmaf_rn(sc[h1 * ATT_SC_STRIDE + (s0 - t0) + tt], v, acc1);
+            }
+        }
+        // partials: [head][chunk][m, l, o[128]]
+        float* pa0 = p.att_part + (static_cast<size_t>(8 * g + h0) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
+        float* pa1 = p.att_part + (static_cast<size_t>(8 * g + h1) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
+        __stcg(pa0 + 2 + dd, acc0);
+        __stcg(pa1 + 2 + dd, acc1);
+        if (tid < 8) {
+            float* pm = p.att_part + (static_cast<size_t>(8 * g + tid) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
+            __stcg(pm, stat[tid]);
+            __stcg(pm + 1, stat[8 + tid]);
+        }
+        __syncthreads();
+        if (tid == 0) {
+            __threadfence();
+            const unsigned old = atomicAdd(&p.cnt[g], 1u);
+            *s.flag = (old == static_cast<unsigned>(C - 1));
+            if (old == static_cast<unsigned>(C - 1)) atomicExch(&p.cnt[g], 0u);
+        }
+        __syncthreads();
+        if (!*s.flag) continue;
+        // ---- last CTA of this KV group combines the chunks of its 8 heads
+        __threadfence();
+        if (warp < 8) {
+            const float* ph = p.att_part + static_cast<size_t>(8 * g + warp) * ATT_MAX_CHUNKS * ATT_PART_STRIDE;
+            const float mc0 = lane < C ? __ldcg(ph + lane * ATT_PART_STRIDE) : 0.0f;
+            const float mc1 = lane + 32 < C ? __ldcg(ph + (lane + 32) * ATT_PART_STRIDE) : 0.0f;
+            float M = -__int_as_float(0x7f800000);
+            if (lane < C) M = mc0;
+            if (lane + 32 < C) M = fmaxf(M, mc1);
+            for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+            if (lane < C) wts[warp * ATT_MAX_CHUNKS + lane] = canon_expf(__fsub_rn(mc0, M));
+            if (lane + 32 < C) wts[warp * ATT_MAX_CHUNKS + lane + 32] = canon_expf(__fsub_rn(mc1, M));
+            __syncwarp();
+            if (lane == 0) {
+                float Ls = 0.0f;
+                for (int cc = 0; cc < C; ++cc)
+                    Ls = __fmaf_rn(wts[warp * ATT_MAX_CHUNKS + cc], __ldcg(ph + cc * ATT_PART_STRIDE + 1), Ls);
+                stat[16 + warp] = __fdiv_rn(1.0f, Ls);
+            }
+        }
+        __syncthreads();
+        for (int o = tid; o < 8 * HEAD_DIM; o += blockDim.x) {
+            const int h = o >> 7, d = o & 127;
+            const float* ph = p.att_part + static_cast<size_t>(8 * g + h) * ATT_MAX_CHUNKS * ATT_PART_STRIDE;
+            float O = 0.0f;
+            for (int cc = 0; cc < C; ++cc)
+                O = __fmaf_rn(wts[h * ATT_MAX_CHUNKS + cc], __ldcg(ph + cc * ATT_PART_STRIDE + 2 + d), O);
+            const float out = __fmul_rn(O, stat[16 + h]);
+            ab[o] = out;
+            p.att[8 * g * HEAD_DIM + o] = out;
+        }
+        __syncthreads();
+        if (warp < 4) {   // four Q8_K blocks, ties-to-even (quantize_row_q8_K_avx2)
+            float y[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) y[k] = ab[256 * warp + 8 * lane + k];
+            uint8_t* blk = p.att_q8k + static_cast<size_t>(4 * g + warp) * Q8K_BYTES;
+            quant_block_warp<false>(y, reinterpret_cast<int8_t*>(blk + 4), reinterpret_cast<float*>(blk),
+                                    reinterpret_cast<int16_t*>(blk + 260));
+        }
+    }
+}
+
+// xq <- global Q8_K blocks (block_q8_K layout) written by another phase.
+__device__ void load_q8k_blocks(const uint8_t* src, int nblocks, const Smem& s) {
+    const int tid = threadIdx.x;
+    for (int i = tid; i < nblocks * 64; i += blockDim.x) {   // qs words
+        const int b = i >> 6, wd = i & 63;
+        reinterpret_cast<uint32_t*>(s.xq->qs[b])[wd] =
+            __ldcg(reinterpret_cast<const unsigned int*>(src + static_cast<size_t>(b) * Q8K_BYTES + 4) + wd);
+    }
+    for (int i = tid; i < nblocks * 8; i += blockDim.x) {    // bsums (8 words per block)
+        const int b = i >> 3, wd = i & 7;
+        reinterpret_cast<uint32_t*>(s.xq->bsums[b])[wd] =
+            __ldcg(reinterpret_cast<const unsigned int*>(src + static_cast<size_t>(b) * Q8K_BYTES + 260) + wd);
+    }
+    if (tid < nblocks) s.xq->d[tid] = __ldcg(reinterpret_cast<const float*>(src + static_cast<size_t>(tid) * Q8K_BYTES));
+    __syncthreads();
+}
+
+__device__ void phase_o(const DecodeParams& p, const Smem& s, int l, int cta, int ncta) {
+    const LayerDev& L = p.layers[l];
+    load_q8k_blocks(p.att_q8k, N_EMBD / 256, s);
+    if (!wait_weights(p, s, 4 * l + 1)) return;
+    const PhaseLayout pl = phase_layout(L, 1, cta, ncta);
+    float* x = p.x;
+    const int r0 = pl.row0[0];
+    gemv_staged(L.to, s.wbuf[1], pl.nrows[0], N_EMBD / 256, *s.xq, s.part, MAX_TASKS,
+                [&](int r, float v) { x[r0 + r] = __fadd_rn(__ldcg(x + r0 + r), v); });
+}
+
+__device__ void phase_gu(const DecodeParams& p, const Smem& s, int l, int cta, int ncta) {
+    const LayerDev& L = p.layers[l];
+    load_global_vec(p.x, s.xs, N_EMBD);
+    norm_quant<true>(s.xs, L.ffn_norm, s);
+    if (!wait_weights(p, s, 4 * l + 2)) return;
+    const PhaseLayout pl = phase_layout(L, 2, cta, ncta);
+    const int n = pl.nrows[0];
+    float* rv = s.rowval;
+    gemv_staged(L.tg, s.wbuf[0] + pl.off[0], n, N_EMBD / 256, *s.xq, s.part, MAX_TASKS,
+                [&](int r, float v) { rv[r] = v; });
+    gemv_staged(L.tu, s.wbuf[0] + pl.off[1], n, N_EMBD / 256, *s.xq, s.part, MAX_TASKS,
+                [&](int r, float v) { rv[128 + r] = v; });
+    for (int r = threadIdx.x; r < n; r += blockDim.x) p.h[pl.row0[0] + r] = canon_silu_mul(rv[r], rv[128 + r]);
+}
+
+__device__ void phase_down(const DecodeParams& p, const Smem& s, int l, int cta, int ncta) {
+    const LayerDev& L = p.layers[l];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int b = warp; b < N_FF / 256; b += blockDim.x >> 5) {   // Q8_K of h straight from L2
+        const float4 a = __ldcg(reinterpret_cast<const float4*>(p.h + 256 * b + 8 * lane));
+        const float4 c = __ldcg(reinterpret_cast<const float4*>(p.h + 256 * b + 8 * lane + 4));
+        const float y[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+        quant_block_warp<true>(y, s.xq->qs[b], &s.xq->d[b], s.xq->bsums[b]);
+    }
+    __syncthreads();
+    if (!wait_weights(p, s, 4 * l + 3)) return;
+    const PhaseLayout pl = phase_layout(L, 3, cta, ncta);
+    float* x = p.x;
+    const int r0 = pl.row0[0];
+    gemv_staged(L.td, s.wbuf[1], pl.nrows[0], N_FF / 256, *s.xq, s.part, MAX_TASKS,
+                [&](int r, float v) { x[r0 + r] = __fadd_rn(__ldcg(x + r0 + r), v); });
+}
+
+__device__ void phase_lm(const DecodeParams& p, const Smem& s, int cta, int ncta) {
+    const LmPlan q = lm_plan(p, cta, ncta);
+    if (threadIdx.x == 0)
+        for (int st = 2; st < 4; ++st) issue_lm_stage(p, s, q, st);
+    load_global_vec(p.x, s.xs, N_EMBD);
+    norm_quant<false>(s.xs, p.out_norm, s);   // rmsnorm (ops.cpp:468-481) + quantize_row_q8_K_avx2
+    float best = -__int_as_float(0x7f800000);
+    int besti = 0x7fffffff;
+    int nan0 = 0;
+    for (int st = 0; st < q.nstages; ++st) {
+        const int slot = st & 3;
+        if (!mbar_wait(&s.lmbar[slot], (st >> 2) & 1, p.err)) return;
+        const int a = q.r0 + st * q.sr, n = min(q.sr, q.r1 - a);
+        float* lg = p.logits;
+        const int wl = p.write_logits;
+        gemv_staged(p.lm_type, lm_slot(s, slot), n, q.nb, *s.xq, s.part, MAX_TASKS, [&](int r, float v) {
+            const int row = a + r;
+            if (wl) lg[row] = v;
+            if (row == 0 && v != v) nan0 = 1;
+            if (v > best || (v == best && row < besti)) best = v, besti = row;
+        });
+        if (threadIdx.x == 0 && st + 4 < q.nstages) issue_lm_stage(p, s, q, st + 4);
+    }
+    // CTA argmax (lowest index on ties; NaN never wins; a NaN logit 0 forces 0 like the
+    // reference's `if (lg[i] > lg[best])` scan)
+    float* red = s.red;
+    int* redi = reinterpret_cast<int*>(s.rowval);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int o = 16; o >= 1; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, besti, o);
+        if (ob > best || (ob == best && oi < besti)) best = ob, besti = oi;
+    }
+    nan0 = __any_sync(0xffffffffu, nan0);
+    if (lane == 0) red[warp] = best, redi[warp] = besti, redi[32 + warp] = nan0;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int anynan = 0;
+        for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) {
+            if (red[w] > best || (red[w] == best && redi[w] < besti)) best = red[w], besti = redi[w];
+            anynan |= redi[32 + w];
+        }
+        p.am_val[cta] = best;
+        p.am_idx[cta] = anynan ? -1 : besti;
+        __threadfence();
+        const unsigned old = atomicAdd(&p.cnt[2], 1u);
+        if (old == gridDim.x - 1) {
+            __threadfence();
+            atomicExch(&p.cnt[2], 0u);
+            float bv = -__int_as_float(0x7f800000);
+            int bi = 0x7fffffff;
+            bool n0 = false;
+            for (int c = 0; c < static_cast<int>(gridDim.x); ++c) {
+                const float v = __ldcg(p.am_val + c);
+                const int i = __ldcg(p.am_idx + c);
+                if (i < 0) {
+                    n0 = true;
+                    continue;
+                }
+                if (v > bv || (v == bv && i < bi)) bv = v, bi = i;
+            }
+            const int result = (n0 || bi == 0x7fffffff) ? 0 : bi;
+            *p.argmax_out = result;
+            *p.token_dev = result;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    Smem s;
+    uint8_t* ptr = smem_raw;
+    s.wbuf[0] = ptr;
+    ptr += WBUF_BYTES + WBUF_SLACK;
+    s.wbuf[1] = ptr;
+    ptr += WBUF_BYTES + WBUF_SLACK;
+    s.xq = reinterpret_cast<XQSmem*>(ptr);
+    ptr += (sizeof(XQSmem) + 127) & ~size_t(127);
+    s.part = reinterpret_cast<int*>(ptr);
+    ptr += MAX_TASKS * PART_WORDS * 4;
+    s.xs = reinterpret_cast<float*>(ptr);
+    ptr += N_EMBD * 4;
+    s.rowval = reinterpret_cast<float*>(ptr);
+    ptr += ROWVAL_FLOATS * 4;
+    s.red = reinterpret_cast<float*>(ptr);
+    ptr += 32 * 4;
+    s.wbar = reinterpret_cast<uint64_t*>(ptr);
+    ptr += 8 * 8;
+    s.lmbar = reinterpret_cast<uint64_t*>(ptr);
+    ptr += 4 * 8;
+    s.flag = reinterpret_cast<int*>(ptr);
+
+    const int cta = blockIdx.x, ncta = gridDim.x;
+    const int token = p.token >= 0 ? p.token : *reinterpret_cast<volatile int*>(p.token_dev);
+    if (token < 0 || token >= p.n_vocab) {
+        if (threadIdx.x == 0) atomicOr(p.err, ERR_BAD_TOKEN);
+        return;
+    }
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 8; ++i) mbar_init(&s.wbar[i], 1);
+        for (int i = 0; i < 4; ++i) mbar_init(&s.lmbar[i], 1);
+        fence_mbar_init();
+        issue_weight_phase(p, s, 0, cta, ncta);
+        issue_weight_phase(p, s, 1, cta, ncta);
+    }
+    __syncthreads();
+    const LmPlan lmq = lm_plan(p, cta, ncta);
+    for (int l = 0; l < p.n_layer; ++l) {
+        // weight phase 4l (QKV) is in flight since the previous D phase / kernel start
+        if (l > 0 && threadIdx.x == 0) issue_weight_phase(p, s, 4 * l + 1, cta, ncta);
+        phase_qkv(p, s, l, token, cta, ncta);
+        if (!grid_barrier(p)) return;
+        phase_attention(p, s, l, cta, ncta);
+        if (!grid_barrier(p)) return;
+        if (threadIdx.x == 0) issue_weight_phase(p, s, 4 * l + 2, cta, ncta);
+        phase_o(p, s, l, cta, ncta);
+        if (!grid_barrier(p)) return;
+        if (threadIdx.x == 0) issue_weight_phase(p, s, 4 * l + 3, cta, ncta);
+        phase_gu(p, s, l, cta, ncta);
+        if (!grid_barrier(p)) return;
+        if (threadIdx.x == 0) {
+            if (l + 1 < p.n_layer) {
+                issue_weight_phase(p, s, 4 * (l + 1), cta, ncta);
+            } else {
+                issue_lm_stage(p, s, lmq, 0);
+                issue_lm_stage(p, s, lmq, 1);
+            }
+        }
+        phase_down(p, s, l, cta, ncta);
+        if (!grid_barrier(p)) return;
+    }
+    phase_lm(p, s, cta, ncta);
+}
+
+}  // namespace
+
+size_t decode_smem_bytes() {
+    size_t b = 2 * (WBUF_BYTES + WBUF_SLACK);
+    b += (sizeof(XQSmem) + 127) & ~size_t(127);
+    b += MAX_TASKS * PART_WORDS * 4 + N_EMBD * 4 + ROWVAL_FLOATS * 4 + 32 * 4 + 12 * 8 + 16;
+    return b;
+}
+
+cudaError_t decode_prepare() {
+    return cudaFuncSetAttribute(k_decode, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(decode_smem_bytes()));
+}
+
+int decode_max_ctas_per_sm() {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_decode, DEC_THREADS, decode_smem_bytes()) != cudaSuccess)
+        return 0;
+    return n;
+}
+
+cudaError_t launch_decode(const DecodeParams& p, int n_ctas, cudaStream_t stream) {
+    void* args[] = {const_cast<DecodeParams*>(&p)};
+    return cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(&k_decode), dim3(n_ctas), dim3(DEC_THREADS), args,
+                                       decode_smem_bytes(), stream);
+}
+
+}  // namespace mcpm

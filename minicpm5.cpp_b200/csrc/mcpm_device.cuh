@@ -1,0 +1,420 @@
+// Device-side building blocks of the MiniCPM5 decode path for sm_100a.
+//
+// Numerics: every fp32 operation whose result is compared bit-for-bit with the CPU
+// restatement (oracle/mcpm_oracle.c) is written with an explicit rounding intrinsic
+// (__fadd_rn, __fmul_rn, __fmaf_rn, __fdiv_rn, __fsqrt_rn) so the compiler cannot
+// contract or reorder it.  The GEMV accumulation follows the reference's AVX2 kernels
+// (src/ops/ops_avx2.cpp:153-276) lane for lane, which makes GEMV outputs identical to
+// the reference for identical Q8_K inputs.
+#pragma once
+#include <cstdint>
+#include <cuda_fp16.h>
+
+namespace mcpm {
+
+// ---------------------------------------------------------------- block formats
+// Byte layouts of reference include/ops.h:33-65 (kept unchanged in HBM).
+constexpr int QK_K = 256;
+constexpr int Q4K_BYTES = 144;   // fp16 d, fp16 dmin, scales[12], qs[128]
+constexpr int Q6K_BYTES = 210;   // ql[128], qh[64], scales[16] (int8), fp16 d
+constexpr int Q8_0_BYTES = 34;   // fp16 d, qs[32]
+constexpr int Q8K_BYTES = 292;   // f32 d, qs[256], int16 bsums[16]
+constexpr int GGML_F32 = 0, GGML_Q8_0 = 8, GGML_Q4_K = 12, GGML_Q6_K = 14;
+
+// Error bits written to the engine's device error word.
+constexpr unsigned ERR_TIMEOUT = 1u, ERR_BAD_TOKEN = 2u, ERR_BAD_ARG = 4u;
+
+__host__ __device__ constexpr int row_bytes(int type, int cols) {
+    return type == GGML_Q4_K ? cols / 256 * Q4K_BYTES
+         : type == GGML_Q6_K ? cols / 256 * Q6K_BYTES
+         : type == GGML_Q8_0 ? cols / 32 * Q8_0_BYTES : cols * 4;
+}
+__host__ __device__ constexpr int block_bytes(int type) {
+    return type == GGML_Q4_K ? Q4K_BYTES : type == GGML_Q6_K ? Q6K_BYTES : Q8_0_BYTES;
+}
+
+// ---------------------------------------------------------------- PTX helpers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bulk global->shared copy (TMA, no tensor map, no multicast).  dst, src 16-byte aligned,
+// bytes a multiple of 16; completion is signalled on `bar` as transaction bytes.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+// L2 prefetch of a global range (TMA unit, fire and forget).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_u32(const unsigned* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_u32(unsigned* p, uint32_t v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ float h2f(uint32_t bits16) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16 & 0xffffu)));
+}
+// signed / unsigned byte i (0..3) of w
+__device__ __forceinline__ int sbyte(uint32_t w, int i) { return static_cast<int>(w << (24 - 8 * i)) >> 24; }
+__device__ __forceinline__ int ubyte(uint32_t w, int i) { return (w >> (8 * i)) & 0xff; }
+
+// Bounded wait on an mbarrier phase.  Returns false (and sets ERR_TIMEOUT) after ~1 s.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer() - t0 > 1000000000ull) {
+            atomicOr(err, ERR_TIMEOUT);
+            return false;
+        }
+    }
+    return true;
+}
+
+// ---------------------------------------------------------------- canonical scalar math
+// exp(x): k = rint(x*log2e), two-constant Cody-Waite reduction, degree-7 Taylor
+// polynomial in Horner form, 2^k applied as two exact power-of-two factors.
+// Identical operation sequence to orc_expf (oracle/mcpm_oracle.c).
+__device__ __forceinline__ float canon_expf(float x) {
+    if (x != x) return x;
+    if (x > 88.72283935546875f) return __int_as_float(0x7f800000);
+    if (x < -103.972084045410156f) return 0.0f;
+    const float kf = rintf(__fmul_rn(x, 1.44269502162933349609375f));
+    float r = __fmaf_rn(-kf, 0.693145751953125f, x);
+    r = __fmaf_rn(-kf, 1.428606765330187045e-06f, r);
+    float p = 1.98412701138295233250e-04f;
+    p = __fmaf_rn(p, r, 1.38888892251998186111e-03f);
+    p = __fmaf_rn(p, r, 8.33333376795053482056e-03f);
+    p = __fmaf_rn(p, r, 4.16666679084300994873e-02f);
+    p = __fmaf_rn(p, r, 1.66666671633720397949e-01f);
+    p = __fmaf_rn(p, r, 0.5f);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    const int k = static_cast<int>(kf);
+    const int k1 = k / 2, k2 = k - k1;
+    return __fmul_rn(__fmul_rn(p, __int_as_float((k1 + 127) << 23)), __int_as_float((k2 + 127) << 23));
+}
+
+// silu(g)*u as the reference build evaluates it (reciprocal, then products); an
+// overflowing exp(-g) yields NaN like the build's Newton-refined reciprocal estimate.
+__device__ __forceinline__ float canon_silu_mul(float g, float u) {
+    const float y = __fadd_rn(1.0f, canon_expf(-g));
+    const float r = isinf(y) ? __int_as_float(0x7fc00000) : __fdiv_rn(1.0f, y);
+    return __fmul_rn(__fmul_rn(g, r), u);
+}
+
+// lround + clamp as inlined by the reference build (ops.cpp:717); NaN/huge -> -127.
+__device__ __forceinline__ int quant_away(float v) {
+    const float a = __fadd_rn(v, copysignf(0.4999999701976776f, v));
+    if (!(a < 9223372036854775808.0f && a >= -9223372036854775808.0f)) return -127;
+    const float t = truncf(a);
+    if (t >= 127.0f) return 127;
+    if (t > -127.0f) return static_cast<int>(t);
+    return -127;
+}
+// _mm256_cvtps_epi32 (ties-to-even) + clamp (ops_avx2.cpp:118-121).
+__device__ __forceinline__ int quant_even(float v) {
+    if (!(v < 2147483648.0f && v >= -2147483648.0f)) return -127;
+    const float t = rintf(v);
+    if (t >= 127.0f) return 127;
+    if (t <= -127.0f) return -127;
+    return static_cast<int>(t);
+}
+
+// ---------------------------------------------------------------- activation staging
+// Q8_K activation in shared memory: qs rows padded to 272 B so that lanes reading
+// different blocks at the same offset hit different bank groups.
+constexpr int XQ_STRIDE = 272;
+constexpr int XQ_MAX_BLOCKS = 24;
+struct XQSmem {
+    int8_t qs[XQ_MAX_BLOCKS][XQ_STRIDE];
+    float d[XQ_MAX_BLOCKS];
+    int16_t bsums[XQ_MAX_BLOCKS][16];
+};
+
+// Quantise one 256-block held by a full warp (lane l holds y[8l .. 8l+7]) into the
+// canonical Q8_K block.  Block amax follows the reference build's NaN-sensitive
+// eight-lane maximum (orc_block_amax); d = amax*(1/127); mul = 127/amax.
+// Writes qs/d/bsums through the supplied pointers (shared or global, 4-byte aligned).
+template <bool AWAY>
+__device__ __forceinline__ void quant_block_warp(const float (&y)[8], int8_t* qs_out, float* d_out,
+                                                 int16_t* bsums_out) {
+    const int lane = threadIdx.x & 31;
+    float accs[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const float e = fabsf(y[k]);
+        const unsigned nanmask = __ballot_sync(0xffffffffu, e != e);
+        const int last = nanmask ? 31 - __clz(nanmask) : -1;
+        const unsigned bits = (lane > last) ? __float_as_uint(e) : 0u;
+        const unsigned mx = __reduce_max_sync(0xffffffffu, bits);
+        accs[k] = (last == 31) ? __int_as_float(0x7fc00000) : __uint_as_float(mx);
+    }
+    float m[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) m[i] = (accs[i + 4] > accs[i]) ? accs[i + 4] : accs[i];
+    const float n0 = (m[2] > m[0]) ? m[2] : m[0];
+    const float n1 = (m[3] > m[1]) ? m[3] : m[1];
+    const float amax = (n1 > n0) ? n1 : n0;
+    int q[8];
+    if (amax == 0.0f || amax != amax) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) q[k] = 0;
+        if (lane == 0) *d_out = 0.0f;
+    } else {
+        const float mul = __fdiv_rn(127.0f, amax);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const float v = __fmul_rn(y[k], mul);
+            q[k] = AWAY ? quant_away(v) : quant_even(v);
+        }
+        if (lane == 0) *d_out = __fmul_rn(amax, 1.0f / 127.0f);
+    }
+    const uint32_t w0 = (q[0] & 0xff) | ((q[1] & 0xff) << 8) | ((q[2] & 0xff) << 16) | ((uint32_t)(q[3] & 0xff) << 24);
+    const uint32_t w1 = (q[4] & 0xff) | ((q[5] & 0xff) << 8) | ((q[6] & 0xff) << 16) | ((uint32_t)(q[7] & 0xff) << 24);
+    uint32_t* qw = reinterpret_cast<uint32_t*>(qs_out + 8 * lane);
+    qw[0] = w0;
+    qw[1] = w1;
+    int s = q[0] + q[1] + q[2] + q[3] + q[4] + q[5] + q[6] + q[7];
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    if ((lane & 1) == 0) bsums_out[lane >> 1] = static_cast<int16_t>(s);
+}
+
+// Canonical sum of squares of x[0..2047] by the first 256 threads of the block (lane l
+// = fma chain over x[l + 256 i], 32-lane butterfly, warps combined as
+// ((w0+w1)+(w2+w3))+((w4+w5)+(w6+w7))).  xv[i] = x[tid + 256 i] already loaded.
+// `red` is 8 floats of shared scratch.  Result valid in all threads after return.
+__device__ __forceinline__ float sumsq_2048(const float (&xv)[8], float* red) {
+    const int tid = threadIdx.x;
+    if (tid < 256) {
+        float a = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) a = __fmaf_rn(xv[i], xv[i], a);
+#pragma unroll
+        for (int s = 16; s >= 1; s >>= 1) a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, s));
+        if ((tid & 31) == 0) red[tid >> 5] = a;
+    }
+    __syncthreads();
+    const float r = __fadd_rn(__fadd_rn(__fadd_rn(red[0], red[1]), __fadd_rn(red[2], red[3])),
+                              __fadd_rn(__fadd_rn(red[4], red[5]), __fadd_rn(red[6], red[7])));
+    __syncthreads();
+    return r;
+}
+
+// ---------------------------------------------------------------- GEMV pass 1
+// Integer partial sums of one (row, super-block) task, split into the eight AVX2
+// accumulator lanes of the reference kernels:
+//   Q4_K lane k: sum_j sc[2j]*sum_{i=4k}^{4k+3} lo(qs[32j+i])*x[64j+i]
+//                     + sc[2j+1]*sum hi(qs[32j+i])*x[64j+32+i]        (ops_avx2.cpp:168-181)
+//   Q6_K lane k: sum over the four quarters of both halves for l in [4k, 4k+4), minus
+//                32*(bsums[2k]*sc[2k] + bsums[2k+1]*sc[2k+1])          (ops_avx2.cpp:225-270)
+// minsum: Q4_K sum_g mn[g]*(bsums[2g]+bsums[2g+1]); Q6_K the total -32 offset.
+struct Partials {
+    int k[8];
+    int minsum;
+};
+
+__device__ __forceinline__ void q4k_task(const uint8_t* blk, const XQSmem& xq, int b, Partials& out) {
+    const uint4 hdr = *reinterpret_cast<const uint4*>(blk);   // d|dmin, scales[0..11]
+    const uint32_t s0 = hdr.y, s1 = hdr.z, s2 = hdr.w;
+    const uint32_t sc_lo = s0 & 0x3f3f3f3fu;                                       // sc[0..3]
+    const uint32_t sc_hi = (s2 & 0x0f0f0f0fu) | ((s0 >> 2) & 0x30303030u);         // sc[4..7]
+    const uint32_t mn_lo = s1 & 0x3f3f3f3fu;                                       // mn[0..3]
+    const uint32_t mn_hi = ((s2 >> 4) & 0x0f0f0f0fu) | ((s1 >> 2) & 0x30303030u);  // mn[4..7]
+    const uint4* qs = reinterpret_cast<const uint4*>(blk + 16);
+    const uint4* xs = reinterpret_cast<const uint4*>(xq.qs[b]);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) out.k[k] = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t scw = j < 2 ? sc_lo : sc_hi;
+        const int sa = ubyte(scw, 2 * (j & 1)), sb = ubyte(scw, 2 * (j & 1) + 1);
+        const uint4 w0 = qs[2 * j], w1 = qs[2 * j + 1];            // qs[32j .. 32j+31]
+        const uint4 xl0 = xs[4 * j], xl1 = xs[4 * j + 1];          // x[64j .. 64j+31]
+        const uint4 xh0 = xs[4 * j + 2], xh1 = xs[4 * j + 3];      // x[64j+32 .. 64j+63]
+        const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        const int xl[8] = {(int)xl0.x, (int)xl0.y, (int)xl0.z, (int)xl0.w, (int)xl1.x, (int)xl1.y, (int)xl1.z, (int)xl1.w};
+        const int xh[8] = {(int)xh0.x, (int)xh0.y, (int)xh0.z, (int)xh0.w, (int)xh1.x, (int)xh1.y, (int)xh1.z, (int)xh1.w};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int lo = dp4a_us(w[k] & 0x0f0f0f0fu, xl[k], 0);
+            const int hi = dp4a_us((w[k] >> 4) & 0x0f0f0f0fu, xh[k], 0);
+            out.k[k] += sa * lo + sb * hi;
+        }
+    }
+    const int* bs = reinterpret_cast<const int*>(xq.bsums[b]);   // 8 words of int16 pairs
+    int m = 0;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+        const int pair = bs[g];
+        const int sx = static_cast<int>(static_cast<int16_t>(pair & 0xffff)) + (pair >> 16);
+        m += ubyte(g < 4 ? mn_lo : mn_hi, g & 3) * sx;
+    }
+    out.minsum = m;
+}
+
+// Q6_K super-blocks sit at any 2-byte alignment: words are read aligned and funnel-shifted
+// (reads at most 4 bytes past the block, which callers keep readable).
+__device__ __forceinline__ uint32_t ld_u32_unaligned(const uint32_t* base, int i, uint32_t sh) {
+    return __funnelshift_r(base[i], base[i + 1], sh);
+}
+
+__device__ __forceinline__ void q6k_task(const uint8_t* blk, const XQSmem& xq, int b, Partials& out) {
+    const uintptr_t addr = reinterpret_cast<uintptr_t>(blk);
+    const uint32_t* base = reinterpret_cast<const uint32_t*>(addr & ~uintptr_t(3));
+    const uint32_t sh = static_cast<uint32_t>(addr & 3) * 8;
+    uint32_t scw[4];   // scales: bytes 192..207 -> words 48..51
+#pragma unroll
+    for (int i = 0; i < 4; ++i) scw[i] = ld_u32_unaligned(base, 48 + i, sh);
+    const int* bs = reinterpret_cast<const int*>(xq.bsums[b]);
+    int off = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int pair = bs[k];
+        const int b0 = static_cast<int>(static_cast<int16_t>(pair & 0xffff)), b1 = pair >> 16;
+        const int o = b0 * sbyte(scw[k >> 1], 2 * (k & 1)) + b1 * sbyte(scw[k >> 1], 2 * (k & 1) + 1);
+        out.k[k] = -32 * o;
+        off += o;
+    }
+    out.minsum = 32 * off;
+    const uint4* xs = reinterpret_cast<const uint4*>(xq.qs[b]);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        uint4 xv[8];   // x[128h .. 128h+127]; quarter kk covers words 8kk .. 8kk+7
+#pragma unroll
+        for (int i = 0; i < 8; ++i) xv[i] = xs[8 * h + i];
+        const int* xw = reinterpret_cast<const int*>(xv);
+        const uint32_t sw = scw[2 * h], sw2 = scw[2 * h + 1];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {   // t = AVX2 lane: l in [4t, 4t+4)
+            const uint32_t A = ld_u32_unaligned(base, 16 * h + t, sh);        // ql[64h + 4t]
+            const uint32_t B = ld_u32_unaligned(base, 16 * h + 8 + t, sh);    // ql[64h + 32 + 4t]
+            const uint32_t H = ld_u32_unaligned(base, 32 + 8 * h + t, sh);    // qh[32h + 4t]
+            const uint32_t q0 = (A & 0x0f0f0f0fu) | ((H << 4) & 0x30303030u);
+            const uint32_t q1 = (B & 0x0f0f0f0fu) | ((H << 2) & 0x30303030u);
+            const uint32_t q2 = ((A >> 4) & 0x0f0f0f0fu) | (H & 0x30303030u);
+            const uint32_t q3 = ((B >> 4) & 0x0f0f0f0fu) | ((H >> 2) & 0x30303030u);
+            const int si = (t >= 4) ? 1 : 0;   // scale index 8h + 2kk + (l >= 16)
+            const int sc0 = sbyte(sw, si), sc1 = sbyte(sw, 2 + si), sc2 = sbyte(sw2, si), sc3 = sbyte(sw2, 2 + si);
+            int acc = out.k[t];
+            acc += sc0 * dp4a_us(q0, xw[t], 0);
+            acc += sc1 * dp4a_us(q1, xw[8 + t], 0);
+            acc += sc2 * dp4a_us(q2, xw[16 + t], 0);
+            acc += sc3 * dp4a_us(q3, xw[24 + t], 0);
+            out.k[t] = acc;
+        }
+    }
+}
+
+// fp16 super-block scale(s) of a task: Q4_K -> (d, dmin); Q6_K -> (d, 0).
+__device__ __forceinline__ void block_scales(int type, const uint8_t* blk, float& d, float& dmin) {
+    if (type == GGML_Q4_K) {
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(blk);
+        d = h2f(w);
+        dmin = h2f(w >> 16);
+    } else {
+        const uintptr_t addr = reinterpret_cast<uintptr_t>(blk) + 208;
+        const uint32_t* base = reinterpret_cast<const uint32_t*>(addr & ~uintptr_t(3));
+        d = h2f(__funnelshift_r(base[0], base[1], static_cast<uint32_t>(addr & 3) * 8));
+        dmin = 0.0f;
+    }
+}
+
+// ---------------------------------------------------------------- GEMV over staged rows
+// Rows [0, R) of one matrix (type, nb super-blocks per row) are staged contiguously in
+// shared memory at `w`.  Pass 1: every (row, block) task's integer partials go to
+// `part` (9 ints per task).  Pass 2: lane k of a row group runs the reference's fp32
+// accumulator chain for AVX2 lane k over the blocks, the eight lanes are reduced with
+// hsum_f32_8's tree (a butterfly over lane bits 2, 1, 0) and the Q4_K min term is added.
+// The row value is handed to `epi(row, value)` by lane 0 of each row group.
+// Must be called by all threads of the CTA (contains __syncthreads).
+constexpr int PART_WORDS = 9;
+
+template <typename Epi>
+__device__ __forceinline__ void gemv_staged(int type, const uint8_t* w, int R, int nb, const XQSmem& xq, int* part,
+                                            int max_tasks, Epi epi) {
+    const int tid = threadIdx.x, nthr = blockDim.x;
+    const int rb = block_bytes(type);
+    const int mt = (max_tasks / nb) * nb;   // whole rows per chunk
+    for (int t0 = 0; t0 < R * nb; t0 += mt) {
+        const int ntask = min(mt, R * nb - t0);
+        for (int t = tid; t < ntask; t += nthr) {
+            const int task = t0 + t, b = task % nb;
+            const uint8_t* blk = w + static_cast<size_t>(task) * rb;
+            Partials p;
+            if (type == GGML_Q4_K)
+                q4k_task(blk, xq, b, p);
+            else
+                q6k_task(blk, xq, b, p);
+            int* dst = part + t * PART_WORDS;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) dst[k] = p.k[k];
+            dst[8] = p.minsum;
+        }
+        __syncthreads();
+        // pass 2: one 8-lane group per row; trip count uniform per warp for the shuffles
+        const int r_begin = t0 / nb, total = (ntask / nb) * 8;
+        for (int base = tid & ~31; base < total; base += nthr) {
+            const int g = base + (tid & 31);
+            const bool valid = g < total;
+            const int r = r_begin + (g >> 3), k = g & 7;
+            float acc = 0.0f, acc_min = 0.0f;
+            if (valid) {
+                for (int b = 0; b < nb; ++b) {
+                    const int task = r * nb + b;
+                    float d, dmin;
+                    block_scales(type, w + static_cast<size_t>(task) * rb, d, dmin);
+                    const float xd = xq.d[b];
+                    const int* src = part + (task - t0) * PART_WORDS;
+                    acc = __fmaf_rn(__fmul_rn(xd, d), __int2float_rn(src[k]), acc);
+                    if (type == GGML_Q4_K)
+                        acc_min = __fmaf_rn(-__fmul_rn(xd, dmin), __int2float_rn(src[8]), acc_min);
+                }
+            }
+            // hsum_f32_8: t_i = a_i + a_{i+4}; u = (t0+t2, t1+t3); r = u0 + u1
+            acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 4));
+            acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 2));
+            acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
+            if (valid && k == 0) epi(r, type == GGML_Q4_K ? __fadd_rn(acc, acc_min) : acc);
+        }
+        __syncthreads();
+    }
+}
+
+}  // namespace mcpm

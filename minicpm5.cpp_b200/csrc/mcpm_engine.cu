@@ -1,0 +1,573 @@
+// Host side of the engine: GGUF load into one HBM arena, KV cache, RoPE table, the
+// decode-kernel launch, and the C ABI of include/mcpm.h.
+//
+// Reference counterpart: MiniCPM5Engine (include/model.h:37-70, src/model.cpp:17-242).
+// The reference reads the whole file into one host buffer and points tensors into it by
+// absolute offset; here the tensor bytes are uploaded unchanged into one device
+// allocation at the same relative offsets (base = first tensor byte).
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/mcpm.h"
+#include "gguf.h"
+#include "mcpm_device.cuh"
+#include "mcpm_internal.h"
+
+using namespace mcpm;
+
+namespace {
+// Control words, one small device allocation (mirrored into pinned host memory).
+enum { CTL_ARGMAX = 0, CTL_TOKEN = 1, CTL_ERR = 2, CTL_BAR = 4, CTL_CNT = 8, CTL_WORDS = 16 };
+
+const char* LAYER_NAMES[9] = {"attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down",
+                              "attn_norm", "ffn_norm"};
+}  // namespace
+
+struct mcpm_engine {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int n_sm = 0;
+    int n_ctas = 0;
+    int req_ctas = 0;
+    bool loaded = false;
+    GGUFFile gguf;
+    uint8_t* arena = nullptr;
+    uint64_t arena_base = 0, arena_bytes = 0;
+    std::vector<LayerDev> layers;
+    LayerDev* d_layers = nullptr;
+    int n_layer = 0, n_vocab = 0;
+    float rope_base = 5000000.0f;
+    const uint8_t* embd = nullptr;
+    int embd_type = 0;
+    const float* out_norm = nullptr;
+    const uint8_t* lm = nullptr;
+    int lm_type = 0;
+    float *kc = nullptr, *vc = nullptr;
+    int max_seq = 0;
+    float2* rope = nullptr;
+    float *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr, *att_part = nullptr, *logits = nullptr;
+    float* am_val = nullptr;
+    int* am_idx = nullptr;
+    uint8_t* att_q8k = nullptr;
+    int* ctl = nullptr;       // device control words
+    int* ctl_host = nullptr;  // pinned mirror
+};
+
+namespace {
+
+mcpm_status cuda_status(cudaError_t e) {
+    if (e == cudaSuccess) return MCPM_OK;
+    if (e == cudaErrorMemoryAllocation) return MCPM_OUT_OF_MEMORY;
+    std::fprintf(stderr, "[mcpm] CUDA error: %s\n", cudaGetErrorString(e));
+    return MCPM_CUDA_ERROR;
+}
+
+#define MCPM_CUDA(call)                                  \
+    do {                                                 \
+        const mcpm_status st__ = cuda_status((call));    \
+        if (st__ != MCPM_OK) return st__;                \
+    } while (0)
+
+template <typename T>
+void free_dev(T*& p) {
+    if (p) cudaFree(const_cast<void*>(reinterpret_cast<const void*>(p)));
+    p = nullptr;
+}
+
+void free_kv(mcpm_engine* e) {
+    free_dev(e->kc);
+    free_dev(e->vc);
+    free_dev(e->rope);
+    e->max_seq = 0;
+}
+
+void free_model(mcpm_engine* e) {
+    free_dev(e->arena);
+    free_dev(e->d_layers);
+    free_dev(e->x);
+    free_dev(e->q);
+    free_dev(e->att);
+    free_dev(e->h);
+    free_dev(e->att_part);
+    free_dev(e->logits);
+    free_dev(e->am_val);
+    free_dev(e->am_idx);
+    free_dev(e->att_q8k);
+    e->layers.clear();
+    e->loaded = false;
+}
+
+// RoPE factors: theta_i = base^(-(i * (1/head_dim))), angle = theta * pos, (cos, sin)
+// from the C library (the reference build's pow(base, -(i/head_dim)) / cosf / sinf,
+// ops.cpp:502-516).  The CPU restatement computes the same table.
+__attribute__((noinline)) void rope_row(int pos, float base, float2* out) {
+    const float inv = 1.0f / static_cast<float>(HEAD_DIM);
+    for (int i = 0; i < HEAD_DIM; i += 2) {
+        const float theta = powf(base, -(static_cast<float>(i) * inv));
+        const float ang = theta * static_cast<float>(pos);
+        const float c = cosf(ang);
+        const float s = sinf(ang);
+        out[i / 2] = make_float2(c, s);
+    }
+}
+
+// Largest per-CTA byte counts of the decode kernel's weight phases for n CTAs.
+bool phases_fit(const mcpm_engine* e, int n, std::string& why) {
+    auto ceil_div = [](int a, int b) { return (a + b - 1) / b; };
+    int rb_qkv = 0, rb_o = 0, rb_gu = 0, rb_d = 0;
+    for (const auto& L : e->layers) {
+        rb_qkv = std::max({rb_qkv, row_bytes(L.tq, N_EMBD), row_bytes(L.tk, N_EMBD), row_bytes(L.tv, N_EMBD)});
+        rb_o = std::max(rb_o, row_bytes(L.to, N_EMBD));
+        rb_gu = std::max(rb_gu, row_bytes(L.tg, N_EMBD) + row_bytes(L.tu, N_EMBD));
+        rb_d = std::max(rb_d, row_bytes(L.td, N_FF));
+    }
+    const int qkv_rows = 2 * ceil_div(QKV_ROWS / 2, n), gu_rows = ceil_div(N_FF, n), od_rows = ceil_div(N_EMBD, n);
+    const long long need[4] = {(long long)qkv_rows * rb_qkv + 48, (long long)od_rows * rb_o,
+                               (long long)gu_rows * rb_gu + 16, (long long)od_rows * rb_d};
+    for (long long b : need)
+        if (b > WBUF_BYTES) {
+            why = "decode grid of " + std::to_string(n) + " CTAs needs " + std::to_string(b) +
+                  " B per weight buffer (limit " + std::to_string(WBUF_BYTES) + ")";
+            return false;
+        }
+    if (qkv_rows > ROWVAL_FLOATS || gu_rows > 128) {
+        why = "too few CTAs for the row buffers";
+        return false;
+    }
+    return true;
+}
+
+mcpm_status reset_ctl(mcpm_engine* e) {
+    MCPM_CUDA(cudaMemsetAsync(e->ctl, 0, CTL_WORDS * sizeof(int), e->stream));
+    MCPM_CUDA(cudaStreamSynchronize(e->stream));
+    return MCPM_OK;
+}
+
+mcpm_status check_ctl(mcpm_engine* e) {
+    MCPM_CUDA(cudaMemcpyAsync(e->ctl_host, e->ctl, 4 * sizeof(int), cudaMemcpyDeviceToHost, e->stream));
+    MCPM_CUDA(cudaStreamSynchronize(e->stream));
+    const unsigned err = static_cast<unsigned>(e->ctl_host[CTL_ERR]);
+    if (err) {
+        reset_ctl(e);   // barrier words may be mid-count after an aborted launch
+        if (err & ERR_BAD_TOKEN) return MCPM_BAD_TOKEN;
+        return MCPM_TIMEOUT;
+    }
+    return MCPM_OK;
+}
+
+DecodeParams make_params(const mcpm_engine* e, int token, int pos, int write_logits) {
+    DecodeParams p{};
+    p.layers = e->d_layers;
+    p.n_layer = e->n_layer;
+    p.embd = e->embd;
+    p.embd_type = e->embd_type;
+    p.out_norm = e->out_norm;
+    p.lm = e->lm;
+    p.lm_type = e->lm_type;
+    p.n_vocab = e->n_vocab;
+    p.kc = e->kc;
+    p.vc = e->vc;
+    p.max_seq = e->max_seq;
+    p.rope = e->rope;
+    p.x = e->x;
+    p.q = e->q;
+    p.att = e->att;
+    p.att_q8k = e->att_q8k;
+    p.h = e->h;
+    p.att_part = e->att_part;
+    p.logits = e->logits;
+    p.am_val = e->am_val;
+    p.am_idx = e->am_idx;
+    p.argmax_out = e->ctl + CTL_ARGMAX;
+    p.token_dev = e->ctl + CTL_TOKEN;
+    p.err = reinterpret_cast<unsigned*>(e->ctl + CTL_ERR);
+    p.bar = reinterpret_cast<unsigned*>(e->ctl + CTL_BAR);
+    p.cnt = reinterpret_cast<unsigned*>(e->ctl + CTL_CNT);
+    p.token = token;
+    p.pos = pos;
+    p.write_logits = write_logits;
+    return p;
+}
+
+mcpm_status launch(mcpm_engine* e, int token, int pos, int write_logits) {
+    if (!e || !e->loaded || !e->kc) return MCPM_NOT_LOADED;
+    if (pos < 0 || pos >= e->max_seq) return MCPM_CTX_OVERFLOW;
+    if (token >= e->n_vocab) return MCPM_BAD_TOKEN;
+    MCPM_CUDA(cudaSetDevice(e->device));
+    const DecodeParams p = make_params(e, token, pos, write_logits);
+    MCPM_CUDA(launch_decode(p, e->n_ctas, e->stream));
+    return MCPM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* mcpm_status_string(mcpm_status s) {
+    switch (s) {
+        case MCPM_OK: return "ok";
+        case MCPM_BAD_ARG: return "bad argument";
+        case MCPM_BAD_FILE: return "bad or unsupported model file";
+        case MCPM_UNSUPPORTED_TYPE: return "unsupported tensor type";
+        case MCPM_CTX_OVERFLOW: return "position beyond the KV cache";
+        case MCPM_CUDA_ERROR: return "CUDA error";
+        case MCPM_NCCL_ERROR: return "NCCL error";
+        case MCPM_TIMEOUT: return "device wait timed out";
+        case MCPM_OUT_OF_MEMORY: return "out of device memory";
+        case MCPM_BAD_TOKEN: return "token id out of range";
+        case MCPM_NOT_LOADED: return "model or KV cache not loaded";
+    }
+    return "unknown status";
+}
+
+mcpm_status mcpm_engine_create(const mcpm_config* cfg, mcpm_engine** out) {
+    if (!cfg || !out) return MCPM_BAD_ARG;
+    *out = nullptr;
+    if (cfg->max_seq < 0 || cfg->max_seq > MAX_SEQ || cfg->n_ctas < 0) return MCPM_BAD_ARG;
+    int ndev = 0;
+    MCPM_CUDA(cudaGetDeviceCount(&ndev));
+    if (cfg->device < 0 || cfg->device >= ndev) return MCPM_BAD_ARG;
+    auto e = std::make_unique<mcpm_engine>();
+    e->device = cfg->device;
+    e->req_ctas = cfg->n_ctas;
+    e->max_seq = 0;
+    MCPM_CUDA(cudaSetDevice(e->device));
+    MCPM_CUDA(cudaDeviceGetAttribute(&e->n_sm, cudaDevAttrMultiProcessorCount, e->device));
+    int coop = 0;
+    MCPM_CUDA(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, e->device));
+    if (!coop) return MCPM_CUDA_ERROR;
+    MCPM_CUDA(decode_prepare());
+    const int per_sm = decode_max_ctas_per_sm();
+    if (per_sm < 1) return MCPM_CUDA_ERROR;
+    e->n_ctas = e->n_sm;   // one persistent CTA per SM
+    if (cfg->n_ctas > 0) e->n_ctas = std::min(cfg->n_ctas, e->n_sm * per_sm);
+    MCPM_CUDA(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
+    MCPM_CUDA(cudaMalloc(&e->ctl, CTL_WORDS * sizeof(int)));
+    MCPM_CUDA(cudaMallocHost(&e->ctl_host, CTL_WORDS * sizeof(int)));
+    const mcpm_status st = reset_ctl(e.get());
+    if (st != MCPM_OK) return st;
+    e->max_seq = cfg->max_seq;   // allocated at load
+    *out = e.release();
+    return MCPM_OK;
+}
+
+mcpm_status mcpm_load_gguf(mcpm_engine* e, const char* path) {
+    if (!e || !path) return MCPM_BAD_ARG;
+    MCPM_CUDA(cudaSetDevice(e->device));
+    free_model(e);
+    GGUFFile g;
+    const std::string why = gguf_read(path, g);
+    if (!why.empty()) {
+        std::fprintf(stderr, "[mcpm] %s\n", why.c_str());
+        return MCPM_BAD_FILE;
+    }
+    auto find = [&](const std::string& name) -> const GGUFTensor* {
+        for (const auto& t : g.tensors)
+            if (t.name == name) return &t;
+        return nullptr;
+    };
+    int n_layer = 0;
+    while (find("blk." + std::to_string(n_layer) + ".attn_q.weight")) ++n_layer;
+    const GGUFTensor* emb = find("token_embd.weight");
+    const GGUFTensor* onorm = find("output_norm.weight");
+    const GGUFTensor* out = find("output.weight");
+    if (n_layer == 0 || n_layer > MAX_LAYERS || !emb || !onorm || !out) {
+        std::fprintf(stderr, "[mcpm] missing MiniCPM5 tensors in %s\n", path);
+        return MCPM_BAD_FILE;
+    }
+    auto dims_are = [](const GGUFTensor* t, uint64_t c, uint64_t r) {
+        return t->dims.size() >= 1 && t->dims[0] == c && (r == 0 ? t->dims.size() == 1 : t->dims.size() == 2 && t->dims[1] == r);
+    };
+    const uint64_t vocab = emb->dims.size() == 2 ? emb->dims[1] : 0;
+    if (!dims_are(emb, N_EMBD, vocab) || !dims_are(out, N_EMBD, vocab) || !dims_are(onorm, N_EMBD, 0) || vocab == 0 ||
+        vocab > (1u << 30)) {
+        std::fprintf(stderr, "[mcpm] unexpected embedding / output shapes\n");
+        return MCPM_BAD_FILE;
+    }
+    if (emb->type != GGML_Q4_K || (out->type != GGML_Q4_K && out->type != GGML_Q6_K) || onorm->type != GGML_F32) {
+        std::fprintf(stderr, "[mcpm] embedding/output types %u/%u not handled by the decode kernel\n", emb->type,
+                     out->type);
+        return MCPM_UNSUPPORTED_TYPE;
+    }
+    // Arena: [first tensor byte, end of file) uploaded unchanged.
+    uint64_t lo = ~0ull, hi = 0;
+    for (const auto& t : g.tensors) {
+        if (!t.nbytes) continue;
+        lo = std::min(lo, t.offset);
+        hi = std::max(hi, t.offset + t.nbytes);
+    }
+    e->arena_base = lo;
+    e->arena_bytes = hi - lo;
+    MCPM_CUDA(cudaMalloc(&e->arena, e->arena_bytes + 256));
+    {
+        std::unique_ptr<FILE, int (*)(FILE*)> f(std::fopen(path, "rb"), &std::fclose);
+        if (!f) return MCPM_BAD_FILE;
+        const size_t CH = 64ull << 20;
+        uint8_t* pin[2] = {nullptr, nullptr};
+        MCPM_CUDA(cudaMallocHost(&pin[0], CH));
+        MCPM_CUDA(cudaMallocHost(&pin[1], CH));
+        cudaEvent_t ev[2];
+        cudaEventCreateWithFlags(&ev[0], cudaEventDisableTiming);
+        cudaEventCreateWithFlags(&ev[1], cudaEventDisableTiming);
+        std::fseek(f.get(), static_cast<long>(lo), SEEK_SET);
+        uint64_t done = 0;
+        int k = 0;
+        bool io_ok = true;
+        while (done < e->arena_bytes) {
+            const size_t n = static_cast<size_t>(std::min<uint64_t>(CH, e->arena_bytes - done));
+            cudaEventSynchronize(ev[k]);
+            if (std::fread(pin[k], 1, n, f.get()) != n) {
+                io_ok = false;
+                break;
+            }
+            cudaMemcpyAsync(e->arena + done, pin[k], n, cudaMemcpyHostToDevice, e->stream);
+            cudaEventRecord(ev[k], e->stream);
+            done += n;
+            k ^= 1;
+        }
+        cudaStreamSynchronize(e->stream);
+        cudaEventDestroy(ev[0]);
+        cudaEventDestroy(ev[1]);
+        cudaFreeHost(pin[0]);
+        cudaFreeHost(pin[1]);
+        if (!io_ok) return MCPM_BAD_FILE;
+        MCPM_CUDA(cudaGetLastError());
+    }
+    auto dev = [&](const GGUFTensor* t) { return e->arena + (t->offset - lo); };
+    e->layers.assign(n_layer, LayerDev{});
+    for (int l = 0; l < n_layer; ++l) {
+        const GGUFTensor* t[9];
+        for (int i = 0; i < 9; ++i) {
+            t[i] = find("blk." + std::to_string(l) + "." + LAYER_NAMES[i] + ".weight");
+            if (!t[i]) {
+                std::fprintf(stderr, "[mcpm] layer %d lacks %s\n", l, LAYER_NAMES[i]);
+                return MCPM_BAD_FILE;
+            }
+        }
+        const bool shapes = dims_are(t[0], N_EMBD, N_EMBD) && dims_are(t[1], N_EMBD, KV_DIM) &&
+                            dims_are(t[2], N_EMBD, KV_DIM) && dims_are(t[3], N_EMBD, N_EMBD) &&
+                            dims_are(t[4], N_EMBD, N_FF) && dims_are(t[5], N_EMBD, N_FF) &&
+                            dims_are(t[6], N_FF, N_EMBD) && dims_are(t[7], N_EMBD, 0) && dims_are(t[8], N_EMBD, 0);
+        if (!shapes) {
+            std::fprintf(stderr, "[mcpm] layer %d has unexpected shapes\n", l);
+            return MCPM_BAD_FILE;
+        }
+        for (int i = 0; i < 7; ++i)
+            if (t[i]->type != GGML_Q4_K && t[i]->type != GGML_Q6_K) {
+                std::fprintf(stderr, "[mcpm] layer %d %s has type %u (decode kernel: Q4_K / Q6_K)\n", l,
+                             LAYER_NAMES[i], t[i]->type);
+                return MCPM_UNSUPPORTED_TYPE;
+            }
+        if (t[7]->type != GGML_F32 || t[8]->type != GGML_F32) return MCPM_UNSUPPORTED_TYPE;
+        LayerDev& L = e->layers[l];
+        L.wq = dev(t[0]), L.wk = dev(t[1]), L.wv = dev(t[2]), L.wo = dev(t[3]);
+        L.wg = dev(t[4]), L.wu = dev(t[5]), L.wd = dev(t[6]);
+        L.attn_norm = reinterpret_cast<const float*>(dev(t[7]));
+        L.ffn_norm = reinterpret_cast<const float*>(dev(t[8]));
+        L.tq = t[0]->type, L.tk = t[1]->type, L.tv = t[2]->type, L.to = t[3]->type;
+        L.tg = t[4]->type, L.tu = t[5]->type, L.td = t[6]->type;
+    }
+    for (const auto& t : g.tensors)
+        if ((t.offset - lo) % 16) return MCPM_BAD_FILE;   // TMA copies need 16-byte aligned rows
+    e->n_layer = n_layer;
+    e->n_vocab = static_cast<int>(vocab);
+    e->embd = dev(emb);
+    e->embd_type = emb->type;
+    e->out_norm = reinterpret_cast<const float*>(dev(onorm));
+    e->lm = dev(out);
+    e->lm_type = out->type;
+    auto fb = g.f_kv.find("minicpm5.rope.freq_base");
+    if (fb != g.f_kv.end()) e->rope_base = static_cast<float>(fb->second);
+    std::string why2;
+    if (!phases_fit(e, e->n_ctas, why2)) {
+        std::fprintf(stderr, "[mcpm] %s\n", why2.c_str());
+        return MCPM_UNSUPPORTED_TYPE;
+    }
+    MCPM_CUDA(cudaMalloc(&e->d_layers, sizeof(LayerDev) * n_layer));
+    MCPM_CUDA(cudaMemcpy(e->d_layers, e->layers.data(), sizeof(LayerDev) * n_layer, cudaMemcpyHostToDevice));
+    MCPM_CUDA(cudaMalloc(&e->x, N_EMBD * 4));
+    MCPM_CUDA(cudaMalloc(&e->q, N_EMBD * 4));
+    MCPM_CUDA(cudaMalloc(&e->att, N_EMBD * 4));
+    MCPM_CUDA(cudaMalloc(&e->h, N_FF * 4));
+    MCPM_CUDA(cudaMalloc(&e->att_part, sizeof(float) * N_HEAD * ATT_MAX_CHUNKS * ATT_PART_STRIDE));
+    MCPM_CUDA(cudaMalloc(&e->logits, sizeof(float) * e->n_vocab));
+    MCPM_CUDA(cudaMalloc(&e->am_val, sizeof(float) * e->n_ctas));
+    MCPM_CUDA(cudaMalloc(&e->am_idx, sizeof(int) * e->n_ctas));
+    MCPM_CUDA(cudaMalloc(&e->att_q8k, Q8K_BYTES * (N_EMBD / 256)));
+    MCPM_CUDA(cudaMemset(e->logits, 0, sizeof(float) * e->n_vocab));
+    e->gguf = std::move(g);
+    e->loaded = true;
+    if (e->max_seq > 0) return mcpm_init_kv(e, e->max_seq);
+    return MCPM_OK;
+}
+
+mcpm_status mcpm_init_kv(mcpm_engine* e, int max_seq) {
+    if (!e) return MCPM_BAD_ARG;
+    if (max_seq <= 0 || max_seq > MAX_SEQ) return MCPM_BAD_ARG;
+    if (!e->loaded) {
+        e->max_seq = max_seq;   // applied at load
+        return MCPM_OK;
+    }
+    MCPM_CUDA(cudaSetDevice(e->device));
+    free_kv(e);
+    const size_t n = static_cast<size_t>(e->n_layer) * max_seq * KV_DIM;
+    MCPM_CUDA(cudaMalloc(&e->kc, n * sizeof(float)));
+    MCPM_CUDA(cudaMalloc(&e->vc, n * sizeof(float)));
+    MCPM_CUDA(cudaMemset(e->kc, 0, n * sizeof(float)));
+    MCPM_CUDA(cudaMemset(e->vc, 0, n * sizeof(float)));
+    std::vector<float2> table(static_cast<size_t>(max_seq) * (HEAD_DIM / 2));
+    for (int p = 0; p < max_seq; ++p) rope_row(p, e->rope_base, table.data() + static_cast<size_t>(p) * (HEAD_DIM / 2));
+    MCPM_CUDA(cudaMalloc(&e->rope, table.size() * sizeof(float2)));
+    MCPM_CUDA(cudaMemcpy(e->rope, table.data(), table.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    e->max_seq = max_seq;
+    return MCPM_OK;
+}
+
+mcpm_status mcpm_forward(mcpm_engine* e, int token, int pos, float* logits_out, int* argmax_out) {
+    if (!e) return MCPM_BAD_ARG;
+    if (token < 0) return MCPM_BAD_TOKEN;
+    mcpm_status st = launch(e, token, pos, logits_out != nullptr);
+    if (st != MCPM_OK) return st;
+    if (logits_out)
+        MCPM_CUDA(cudaMemcpyAsync(logits_out, e->logits, sizeof(float) * e->n_vocab, cudaMemcpyDeviceToHost, e->stream));
+    st = check_ctl(e);
+    if (st != MCPM_OK) return st;
+    if (argmax_out) *argmax_out = e->ctl_host[CTL_ARGMAX];
+    return MCPM_OK;
+}
+
+mcpm_status mcpm_forward_async(mcpm_engine* e, int token, int pos, int write_logits) {
+    return launch(e, token, pos, write_logits);
+}
+
+mcpm_status mcpm_sync(mcpm_engine* e) {
+    if (!e) return MCPM_BAD_ARG;
+    MCPM_CUDA(cudaSetDevice(e->device));
+    return check_ctl(e);
+}
+
+const float* mcpm_logits_device(mcpm_engine* e) { return e ? e->logits : nullptr; }
+const int* mcpm_argmax_device(mcpm_engine* e) { return e ? e->ctl + CTL_ARGMAX : nullptr; }
+
+mcpm_status mcpm_read_x(mcpm_engine* e, float* x_host) {
+    if (!e || !x_host) return MCPM_BAD_ARG;
+    if (!e->loaded) return MCPM_NOT_LOADED;
+    MCPM_CUDA(cudaSetDevice(e->device));
+    MCPM_CUDA(cudaMemcpyAsync(x_host, e->x, N_EMBD * 4, cudaMemcpyDeviceToHost, e->stream));
+    MCPM_CUDA(cudaStreamSynchronize(e->stream));
+    return MCPM_OK;
+}
+
+mcpm_status mcpm_read_kv(mcpm_engine* e, int layer, int pos, float* k_host, float* v_host) {
+    if (!e || !k_host || !v_host) return MCPM_BAD_ARG;
+    if (!e->loaded || !e->kc) return MCPM_NOT_LOADED;
+    if (layer < 0 || layer >= e->n_layer || pos < 0 || pos >= e->max_seq) return MCPM_BAD_ARG;
+    MCPM_CUDA(cudaSetDevice(e->device));
+    const size_t off = (static_cast<size_t>(layer) * e->max_seq + pos) * KV_DIM;
+    MCPM_CUDA(cudaMemcpyAsync(k_host, e->kc + off, KV_DIM * 4, cudaMemcpyDeviceToHost, e->stream));
+    MCPM_CUDA(cudaMemcpyAsync(v_host, e->vc + off, KV_DIM * 4, cudaMemcpyDeviceToHost, e->stream));
+    MCPM_CUDA(cudaStreamSynchronize(e->stream));
+    return MCPM_OK;
+}
+
+mcpm_status mcpm_model_dims(mcpm_engine* e, int dims[6]) {
+    if (!e || !dims) return MCPM_BAD_ARG;
+    if (!e->loaded) return MCPM_NOT_LOADED;
+    dims[0] = e->n_layer, dims[1] = N_EMBD, dims[2] = N_FF, dims[3] = N_HEAD, dims[4] = N_HEAD_KV;
+    dims[5] = e->n_vocab;
+    return MCPM_OK;
+}
+
+void* mcpm_engine_stream(mcpm_engine* e) { return e ? reinterpret_cast<void*>(e->stream) : nullptr; }
+int mcpm_engine_n_ctas(mcpm_engine* e) { return e ? e->n_ctas : 0; }
+
+void mcpm_engine_destroy(mcpm_engine* e) {
+    if (!e) return;
+    cudaSetDevice(e->device);
+    if (e->stream) cudaStreamSynchronize(e->stream);
+    free_kv(e);
+    free_model(e);
+    free_dev(e->ctl);
+    if (e->ctl_host) cudaFreeHost(e->ctl_host);
+    if (e->stream) cudaStreamDestroy(e->stream);
+    delete e;
+}
+
+// ------------------------------------------------------------------ ops
+namespace {
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool gemv_shape_ok(int type, const void* w, int rows, int cols) {
+    if ((type != GGML_Q4_K && type != GGML_Q6_K) || rows <= 0 || cols <= 0 || cols % 256 || cols > 6144) return false;
+    if (type == GGML_Q6_K && cols % 2048) return false;   // 16-byte aligned rows for TMA
+    return aligned16(w);
+}
+}  // namespace
+
+mcpm_status mcpm_quantize_q8k(const float* x, void* y, int n, int rounding, void* stream) {
+    if (!x || !y || n <= 0 || n % 256 || (rounding != MCPM_ROUND_EVEN && rounding != MCPM_ROUND_AWAY) || !aligned16(x))
+        return MCPM_BAD_ARG;
+    return cuda_status(op_quantize_q8k(x, y, n, rounding, static_cast<cudaStream_t>(stream)));
+}
+
+mcpm_status mcpm_gemv_q8k(int type, const void* w, const void* xq, float* y, int rows, int cols, void* stream) {
+    if (!w || !xq || !y) return MCPM_BAD_ARG;
+    if (type != GGML_Q4_K && type != GGML_Q6_K) return MCPM_UNSUPPORTED_TYPE;
+    if (!gemv_shape_ok(type, w, rows, cols)) return MCPM_BAD_ARG;
+    return cuda_status(op_gemv_q8k(type, w, xq, y, nullptr, nullptr, rows, cols, static_cast<cudaStream_t>(stream)));
+}
+
+mcpm_status mcpm_gemv_blocksums(int type, const void* w, const void* xq, int32_t* isum, int32_t* aux, int rows,
+                                int cols, void* stream) {
+    if (!w || !xq || !isum || !aux) return MCPM_BAD_ARG;
+    if (type != GGML_Q4_K && type != GGML_Q6_K) return MCPM_UNSUPPORTED_TYPE;
+    if (!gemv_shape_ok(type, w, rows, cols)) return MCPM_BAD_ARG;
+    return cuda_status(op_gemv_q8k(type, w, xq, nullptr, isum, aux, rows, cols, static_cast<cudaStream_t>(stream)));
+}
+
+mcpm_status mcpm_gemv_gate_up_q8k(const void* wg, const void* wu, const void* xq, float* gate, float* up, int rows,
+                                  int cols, void* stream) {
+    mcpm_status st = mcpm_gemv_q8k(GGML_Q4_K, wg, xq, gate, rows, cols, stream);
+    if (st != MCPM_OK) return st;
+    return mcpm_gemv_q8k(GGML_Q4_K, wu, xq, up, rows, cols, stream);
+}
+
+mcpm_status mcpm_rmsnorm_q8k(const float* x, const float* w, void* out, int n, float eps, void* stream) {
+    if (!x || !w || !out || n != 2048) return MCPM_BAD_ARG;
+    return cuda_status(op_rmsnorm_q8k(x, w, out, eps, static_cast<cudaStream_t>(stream)));
+}
+
+mcpm_status mcpm_swiglu_q8k(const float* gate, const float* up, void* out, int n, void* stream) {
+    if (!gate || !up || !out || n <= 0 || n % 256) return MCPM_BAD_ARG;
+    return cuda_status(op_swiglu_q8k(gate, up, out, n, static_cast<cudaStream_t>(stream)));
+}
+
+mcpm_status mcpm_gemv_q8k_timed(int type, const void* w, int n_copies, const void* xq, float* y, int rows, int cols,
+                                int reps, float* ms_per_launch, void* stream) {
+    if (!w || !xq || !y || !ms_per_launch || n_copies <= 0 || reps <= 0) return MCPM_BAD_ARG;
+    if (!gemv_shape_ok(type, w, rows, cols)) return MCPM_BAD_ARG;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t stride = static_cast<size_t>(rows) * row_bytes(type, cols);
+    cudaEvent_t a, b;
+    MCPM_CUDA(cudaEventCreate(&a));
+    MCPM_CUDA(cudaEventCreate(&b));
+    MCPM_CUDA(op_gemv_q8k(type, w, xq, y, nullptr, nullptr, rows, cols, s));   // warm-up
+    MCPM_CUDA(cudaEventRecord(a, s));
+    for (int i = 0; i < reps; ++i)
+        MCPM_CUDA(op_gemv_q8k(type, static_cast<const uint8_t*>(w) + (i % n_copies) * stride, xq, y, nullptr, nullptr,
+                              rows, cols, s));
+    MCPM_CUDA(cudaEventRecord(b, s));
+    MCPM_CUDA(cudaEventSynchronize(b));
+    float ms = 0.0f;
+    MCPM_CUDA(cudaEventElapsedTime(&ms, a, b));
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    *ms_per_launch = ms / reps;
+    return MCPM_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,77 @@
+// Internal declarations shared by the decode kernel (mcpm_decode.cu), the op kernels
+// (mcpm_ops.cu) and the host engine (mcpm_engine.cu).
+#pragma once
+#include <cstddef>
+#include <cstdint>
+
+#include <cuda_runtime.h>
+
+namespace mcpm {
+
+constexpr int N_EMBD = 2048, N_FF = 6144, N_HEAD = 16, N_HEAD_KV = 2, HEAD_DIM = 128, KV_DIM = 256;
+constexpr int QKV_ROWS = N_EMBD + 2 * KV_DIM;   // 2560 combined rows of the fused QKV GEMV
+constexpr int MAX_LAYERS = 64;
+
+// Decode kernel geometry.
+constexpr int DEC_THREADS = 512;
+constexpr int WBUF_BYTES = 98304;          // one weight buffer (two per CTA)
+constexpr int WBUF_SLACK = 128;            // readable tail after each buffer (unaligned Q6_K reads)
+constexpr int MAX_TASKS = 384;             // (row, super-block) tasks per GEMV pass
+constexpr int ROWVAL_FLOATS = 256;
+constexpr int LM_SLOT_BYTES = WBUF_BYTES / 2;
+constexpr int ATT_MAX_CHUNKS = 64;         // attention chunks per head (chunk = 32*ceil(n/2048))
+constexpr int ATT_PART_STRIDE = 2 + HEAD_DIM;
+constexpr int ATT_SC_STRIDE = 256;         // chunk-length bound: 32*ceil(MAX_SEQ/2048)
+constexpr int MAX_SEQ = 16384;
+
+struct LayerDev {
+    const uint8_t *wq, *wk, *wv, *wo, *wg, *wu, *wd;
+    const float *attn_norm, *ffn_norm;
+    int tq, tk, tv, to, tg, tu, td;
+};
+
+struct DecodeParams {
+    const LayerDev* layers;
+    int n_layer;
+    const uint8_t* embd;
+    int embd_type;
+    const float* out_norm;
+    const uint8_t* lm;
+    int lm_type;
+    int n_vocab;
+    float* kc;          // [n_layer][max_seq][KV_DIM]
+    float* vc;
+    int max_seq;
+    const float2* rope; // [max_seq][HEAD_DIM/2] (cos, sin)
+    float* x;           // residual stream [N_EMBD]
+    float* q;           // rotated queries [N_EMBD]
+    float* att;         // attention output [N_EMBD] (fp32, for inspection)
+    uint8_t* att_q8k;   // attention output as 8 block_q8_K
+    float* h;           // SwiGLU output [N_FF]
+    float* att_part;    // [N_HEAD][ATT_MAX_CHUNKS][ATT_PART_STRIDE]
+    float* logits;      // [n_vocab]
+    float* am_val;      // per-CTA argmax partials
+    int* am_idx;
+    int* argmax_out;
+    int* token_dev;     // token id for the next step (greedy chaining)
+    unsigned* bar;      // grid barrier {count, generation}
+    unsigned* cnt;      // [0..1] attention combine counters, [2] argmax counter
+    unsigned* err;      // error bits
+    int token;          // < 0: read *token_dev
+    int pos;
+    int write_logits;
+};
+
+size_t decode_smem_bytes();
+cudaError_t decode_prepare();
+cudaError_t launch_decode(const DecodeParams& p, int n_ctas, cudaStream_t stream);
+int decode_max_ctas_per_sm();
+
+// Standalone op launchers (mcpm_ops.cu).
+cudaError_t op_quantize_q8k(const float* x, void* y, int n, int rounding, cudaStream_t s);
+cudaError_t op_gemv_q8k(int type, const void* w, const void* xq, float* y, int32_t* isum, int32_t* aux, int rows,
+                        int cols, cudaStream_t s);
+cudaError_t op_rmsnorm_q8k(const float* x, const float* w, void* out, float eps, cudaStream_t s);
+cudaError_t op_swiglu_q8k(const float* g, const float* u, void* out, int n, cudaStream_t s);
+
+}  // namespace mcpm

@@ -1,0 +1,184 @@
+// Standalone kernels behind the op entry points of include/mcpm.h: Q8_K quantisation,
+// quantised GEMV (and its integer block sums), RMSNorm->Q8_K and SwiGLU->Q8_K.  They use
+// the same device functions as the decode kernel, so the per-op parity tests cover the
+// decode path's arithmetic.
+#include "mcpm_device.cuh"
+#include "mcpm_internal.h"
+
+namespace mcpm {
+namespace {
+
+constexpr int OP_THREADS = 512;
+constexpr int RING_SLOTS = 4;
+constexpr int SLOT_BYTES = 49152;
+constexpr int SLOT_STRIDE = SLOT_BYTES + 128;   // readable tail for unaligned Q6_K reads
+
+__global__ void k_quantize_q8k(const float* __restrict__ x, uint8_t* __restrict__ y, int nblocks, int away) {
+    const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (b >= nblocks) return;   // whole warp
+    const int lane = threadIdx.x & 31;
+    const float4 a = *reinterpret_cast<const float4*>(x + 256 * b + 8 * lane);
+    const float4 c = *reinterpret_cast<const float4*>(x + 256 * b + 8 * lane + 4);
+    const float v[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+    uint8_t* blk = y + static_cast<size_t>(b) * Q8K_BYTES;
+    if (away)
+        quant_block_warp<true>(v, reinterpret_cast<int8_t*>(blk + 4), reinterpret_cast<float*>(blk),
+                               reinterpret_cast<int16_t*>(blk + 260));
+    else
+        quant_block_warp<false>(v, reinterpret_cast<int8_t*>(blk + 4), reinterpret_cast<float*>(blk),
+                                reinterpret_cast<int16_t*>(blk + 260));
+}
+
+__global__ void k_swiglu_q8k(const float* __restrict__ g, const float* __restrict__ u, uint8_t* __restrict__ y,
+                             int nblocks) {
+    const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (b >= nblocks) return;
+    const int lane = threadIdx.x & 31;
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = canon_silu_mul(g[256 * b + 8 * lane + k], u[256 * b + 8 * lane + k]);
+    uint8_t* blk = y + static_cast<size_t>(b) * Q8K_BYTES;
+    quant_block_warp<true>(v, reinterpret_cast<int8_t*>(blk + 4), reinterpret_cast<float*>(blk),
+                           reinterpret_cast<int16_t*>(blk + 260));
+}
+
+// n == 2048, one CTA of 256 threads.
+__global__ void k_rmsnorm_q8k(const float* __restrict__ x, const float* __restrict__ w, uint8_t* __restrict__ y,
+                              float eps) {
+    __shared__ float red[8];
+    const int tid = threadIdx.x;
+    float xv[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xv[i] = x[tid + 256 * i];
+    const float ss = sumsq_2048(xv, red);
+    const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 2048.0f), eps)));
+    const int warp = tid >> 5, lane = tid & 31;
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int i = 256 * warp + 8 * lane + k;
+        v[k] = __fmul_rn(__fmul_rn(x[i], w[i]), rms);
+    }
+    uint8_t* blk = y + static_cast<size_t>(warp) * Q8K_BYTES;
+    quant_block_warp<true>(v, reinterpret_cast<int8_t*>(blk + 4), reinterpret_cast<float*>(blk),
+                           reinterpret_cast<int16_t*>(blk + 260));
+}
+
+// Quantised GEMV: each CTA streams a contiguous row range through a 4-slot TMA ring.
+// isum/aux != null selects the block-sum probe (integer partials only).
+__global__ void __launch_bounds__(OP_THREADS, 1)
+    k_gemv(int type, const uint8_t* __restrict__ w, const uint8_t* __restrict__ xq_g, float* __restrict__ y,
+           int32_t* __restrict__ isum, int32_t* __restrict__ aux, int rows, int nb, unsigned* err) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* ring = smem_raw;
+    XQSmem* xq = reinterpret_cast<XQSmem*>(ring + RING_SLOTS * SLOT_STRIDE);
+    int* part = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(xq) + ((sizeof(XQSmem) + 127) & ~size_t(127)));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(part + MAX_TASKS * PART_WORDS);
+
+    const int tid = threadIdx.x;
+    const int rb = row_bytes(type, nb * 256);
+    const int sr = min(SLOT_BYTES / rb, MAX_TASKS / nb);
+    const int r0 = static_cast<int>((static_cast<long long>(rows) * blockIdx.x) / gridDim.x);
+    const int r1 = static_cast<int>((static_cast<long long>(rows) * (blockIdx.x + 1)) / gridDim.x);
+    const int nstages = (r1 - r0 + sr - 1) / sr;
+
+    for (int i = tid; i < nb * 64; i += blockDim.x) {
+        const int b = i >> 6, wd = i & 63;
+        reinterpret_cast<uint32_t*>(xq->qs[b])[wd] =
+            reinterpret_cast<const uint32_t*>(xq_g + static_cast<size_t>(b) * Q8K_BYTES + 4)[wd];
+    }
+    for (int i = tid; i < nb * 8; i += blockDim.x) {
+        const int b = i >> 3, wd = i & 7;
+        reinterpret_cast<uint32_t*>(xq->bsums[b])[wd] =
+            reinterpret_cast<const uint32_t*>(xq_g + static_cast<size_t>(b) * Q8K_BYTES + 260)[wd];
+    }
+    if (tid < nb) xq->d[tid] = *reinterpret_cast<const float*>(xq_g + static_cast<size_t>(tid) * Q8K_BYTES);
+    auto issue = [&](int st) {
+        const int slot = st % RING_SLOTS, a = r0 + st * sr, n = min(sr, r1 - a);
+        const uint32_t bytes = static_cast<uint32_t>(n) * rb;
+        mbar_expect_tx(&bars[slot], bytes);
+        bulk_g2s(ring + slot * SLOT_STRIDE, w + static_cast<size_t>(a) * rb, bytes, &bars[slot]);
+    };
+    if (tid == 0) {
+        for (int i = 0; i < RING_SLOTS; ++i) mbar_init(&bars[i], 1);
+        fence_mbar_init();
+        for (int st = 0; st < min(nstages, RING_SLOTS); ++st) issue(st);
+    }
+    __syncthreads();
+    for (int st = 0; st < nstages; ++st) {
+        const int slot = st % RING_SLOTS, a = r0 + st * sr, n = min(sr, r1 - a);
+        const uint8_t* sw = ring + slot * SLOT_STRIDE;
+        if (!mbar_wait(&bars[slot], (st / RING_SLOTS) & 1, err)) return;
+        if (isum) {
+            const int bb = block_bytes(type);
+            for (int t = tid; t < n * nb; t += blockDim.x) {
+                Partials pp;
+                if (type == GGML_Q4_K)
+                    q4k_task(sw + static_cast<size_t>(t) * bb, *xq, t % nb, pp);
+                else
+                    q6k_task(sw + static_cast<size_t>(t) * bb, *xq, t % nb, pp);
+                int tot = 0;
+#pragma unroll
+                for (int k = 0; k < 8; ++k) tot += pp.k[k];
+                const size_t o = static_cast<size_t>(a) * nb + t;
+                isum[o] = type == GGML_Q6_K ? tot + pp.minsum : tot;
+                aux[o] = pp.minsum;
+            }
+            __syncthreads();
+        } else {
+            gemv_staged(type, sw, n, nb, *xq, part, MAX_TASKS, [&](int r, float v) { y[a + r] = v; });
+        }
+        if (tid == 0 && st + RING_SLOTS < nstages) issue(st + RING_SLOTS);
+    }
+}
+
+size_t gemv_smem_bytes() {
+    return RING_SLOTS * SLOT_STRIDE + ((sizeof(XQSmem) + 127) & ~size_t(127)) + MAX_TASKS * PART_WORDS * 4 +
+           RING_SLOTS * 8;
+}
+
+int g_num_sms = 0;
+
+}  // namespace
+
+cudaError_t op_quantize_q8k(const float* x, void* y, int n, int rounding, cudaStream_t s) {
+    const int nblocks = n / 256;
+    k_quantize_q8k<<<(nblocks + 7) / 8, 256, 0, s>>>(x, static_cast<uint8_t*>(y), nblocks, rounding);
+    return cudaGetLastError();
+}
+
+cudaError_t op_swiglu_q8k(const float* g, const float* u, void* out, int n, cudaStream_t s) {
+    const int nblocks = n / 256;
+    k_swiglu_q8k<<<(nblocks + 7) / 8, 256, 0, s>>>(g, u, static_cast<uint8_t*>(out), nblocks);
+    return cudaGetLastError();
+}
+
+cudaError_t op_rmsnorm_q8k(const float* x, const float* w, void* out, float eps, cudaStream_t s) {
+    k_rmsnorm_q8k<<<1, 256, 0, s>>>(x, w, static_cast<uint8_t*>(out), eps);
+    return cudaGetLastError();
+}
+
+cudaError_t op_gemv_q8k(int type, const void* w, const void* xq, float* y, int32_t* isum, int32_t* aux, int rows,
+                        int cols, cudaStream_t s) {
+    static bool prepared = false;
+    static unsigned* d_err = nullptr;
+    if (!prepared) {
+        cudaError_t e = cudaFuncSetAttribute(k_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(gemv_smem_bytes()));
+        if (e != cudaSuccess) return e;
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+        e = cudaMalloc(&d_err, sizeof(unsigned));
+        if (e != cudaSuccess) return e;
+        cudaMemset(d_err, 0, sizeof(unsigned));
+        prepared = true;
+    }
+    const int nb = cols / 256;
+    const int grid = rows < g_num_sms ? rows : g_num_sms;
+    k_gemv<<<grid, OP_THREADS, gemv_smem_bytes(), s>>>(type, static_cast<const uint8_t*>(w),
+                                                        static_cast<const uint8_t*>(xq), y, isum, aux, rows, nb, d_err);
+    return cudaGetLastError();
+}
+
+}  // namespace mcpm
