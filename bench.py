@@ -1,0 +1,276 @@
+"""Decode throughput benchmark (MiniCPM5-2B-shaped Q4_K_M greedy decode,
+batch 1 per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one greedy decode token.  Each rank prefills its own seeded 128-token prompt
+(untimed), runs W warm-up tokens, then K timed tokens chained on the device (the argmax of
+step t is the token of step t+1).  Ranks decode independent sequences (no collective in the
+data path, weak scaling); `value` is the aggregate tokens/s over all ranks using the
+slowest rank's device time.  Every token streams all 1.41 GB of weights, far larger than
+L2, so no flush is needed between steps.
+
+Prints one JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "minicpm5.cpp_b200"))
+
+PROMPT = 128
+METRIC = "decode tokens/s (batch 1 per GPU, MiniCPM5-2B Q4_K_M shape)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def profiled_traffic():
+    """DRAM bytes per decode launch from the committed ncu summary, if present."""
+    p = os.path.join(REPO, "profiles", "decode_kernel_traffic.txt")
+    try:
+        with open(p) as f:
+            for line in f:
+                if line.startswith("bytes_per_launch"):
+                    return int(float(line.split("=")[1]))
+    except (OSError, ValueError):
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms during the timed region."""
+
+    def __init__(self, device: int):
+        self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(device), f"--query-gpu={q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=self.out, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.out.seek(0)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.out.read().splitlines():
+            f = [c.strip() for c in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.out.name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_baseline(model_path: str, n_prompt: int = 16, n_gen: int = 32):
+    """Reference CPU build (oracle/_ref, AVX2 + OpenMP) on a bounded sample of the same
+    workload, in a child process so OMP settings apply; falls back to the C restatement."""
+    cores = os.cpu_count() or 1
+    code = f"""
+import sys, time, json, numpy as np
+sys.path.insert(0, {os.path.join(REPO, 'oracle')!r}); sys.path.insert(0, {os.path.join(REPO, 'minicpm5.cpp_b200')!r})
+import oracle as O
+from mcpm import synth
+kind = 'reference' if O.have_ref() else 'port'
+if kind == 'reference':
+    e = O.RefEngine(O.Ref(), {model_path!r}, {n_prompt + n_gen + 1})
+else:
+    e = O.OracleModel(O.Oracle(), {model_path!r}, {n_prompt + n_gen + 1})
+p = synth.prompt_ids({n_prompt}, seed=4321)
+tok = 0
+for pos in range({n_prompt}):
+    tok = e.forward(int(p[pos]), pos)
+t0 = time.perf_counter()
+for pos in range({n_prompt}, {n_prompt + n_gen}):
+    tok = e.forward(tok, pos)
+dt = time.perf_counter() - t0
+print(json.dumps({{"kind": kind, "tok_s": {n_gen} / dt}}))
+"""
+    env = dict(os.environ, OMP_NUM_THREADS=str(cores), OMP_PROC_BIND="close")
+    try:
+        r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=600)
+        d = json.loads(r.stdout.strip().splitlines()[-1])
+    except Exception as ex:  # noqa: BLE001
+        return {"value": None, "unit": "tokens/s", "cores": cores, "kind": "reference", "sample": f"failed: {ex}"}
+    return {"value": round(d["tok_s"], 3), "unit": "tokens/s", "cores": cores, "kind": d["kind"],
+            "sample": f"{n_prompt}-token prompt then {n_gen} greedy tokens timed (decode only), OMP_NUM_THREADS={cores}"}
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference CPU implementation on rank 0's host cores."""
+    if rank != 0:
+        return
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    from mcpm import spec, synth
+    path = synth.ensure_model("q4_k_m", 0)
+    n_prompt = 32   # bounded prefill so the CPU run ends within minutes
+    steps = args.steps
+    cb = cpu_baseline(path, n_prompt=n_prompt, n_gen=args.warmup + steps)
+    value = cb["value"]
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": steps, "warmup": args.warmup,
+            "ms_per_step": round(1000.0 / value, 3) if value else None, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8 dot / fp32", "data": "synthetic",
+            "config": {"workload": "config0: MiniCPM5-2B Q4_K_M greedy decode, batch 1, CPU reference",
+                       "prompt": n_prompt, "parallelism": "openmp"},
+            "cpu_baseline": cb,
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    import numpy as np
+    import torch
+    from mcpm import engine as E, spec, synth
+
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        pg = dist
+    path = synth.ensure_model("q4_k_m", 0)
+    if pg:
+        pg.barrier()
+    max_seq = PROMPT + args.warmup + args.steps + 8
+    eng = E.MiniCPM5Engine(device=local, max_seq=max_seq)
+    if not eng.load_model(path):
+        raise SystemExit("load_model failed")
+    stream = torch.cuda.ExternalStream(eng.stream)
+    prompt = synth.prompt_ids(PROMPT, seed=1234 + rank)
+    for pos in range(PROMPT):                      # prefill (untimed)
+        eng.forward_async(int(prompt[pos]), pos)
+    pos = PROMPT
+    for _ in range(args.warmup):
+        eng.forward_async(-1, pos)
+        pos += 1
+    eng.sync()
+    first_pos = pos
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    clk = ClockSampler(local) if rank == 0 else None
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        eng.forward_async(-1, pos)
+        pos += 1
+    ev1.record(stream)
+    ev1.synchronize()
+    eng.sync()
+    ms = ev0.elapsed_time(ev1)
+    clocks = clk.stop() if clk else None
+    t_dev = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    if pg:
+        pg.all_reduce(t_dev, op=pg.ReduceOp.MAX)
+    ms_max = float(t_dev.item())
+
+    # e2e: the reference-facing call with host buffers (token in, argmax out), synchronous per step
+    e2e_steps = min(args.steps, 64)
+    tok = eng.forward_greedy(-1, pos)
+    pos += 1
+    if pg:
+        pg.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        tok = eng.forward_greedy(tok, pos)
+        pos += 1
+    e2e_s = time.perf_counter() - t0
+    e2e_t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+    if pg:
+        pg.all_reduce(e2e_t, op=pg.ReduceOp.MAX)
+    e2e_s = float(e2e_t.item())
+
+    if rank == 0:
+        tensors = spec.q4km_table()
+        wbytes = spec.weight_bytes_per_token(tensors)["total"]
+        kv = spec.KV_BYTES_PER_POSITION
+        n_pos = [p + 1 for p in range(first_pos, first_pos + args.steps)]
+        bytes_per_tok = wbytes + kv * (sum(n_pos) / len(n_pos))
+        peak, peak_kind = measured_peaks()
+        per_launch_ms = ms_max / args.steps
+        achieved = bytes_per_tok / (per_launch_ms * 1e-3) / 1e9
+        value = world * args.steps / (ms_max * 1e-3)
+        cb = None if args.no_cpu_baseline else cpu_baseline(path)
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_launch_ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 dot / fp32",
+            "data": "synthetic (seeded random-init GGUF, Q4_K_M layout)",
+            "config": {"workload": "config0: MiniCPM5-2B Q4_K_M greedy decode, batch 1 per GPU",
+                       "prompt": PROMPT, "positions": [first_pos, first_pos + args.steps - 1],
+                       "parallelism": f"dp{world} (independent sequences)",
+                       "l2": "inputs larger than L2 (1.41 GB of weights per token)"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": profiled_traffic(),
+                         "peak_kind": peak_kind, "kernel": "k_decode",
+                         "algorithmic_bytes_per_launch": int(bytes_per_tok)},
+            "cpu_baseline": cb,
+            "e2e": {"value": round(world * e2e_steps / e2e_s, 2), "unit": "tokens/s",
+                    "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 16},
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

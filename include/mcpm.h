@@ -57,7 +57,8 @@ mcpm_status mcpm_init_kv(mcpm_engine* e, int max_seq);
 /* One decode step: embeds `token` at position `pos`, runs every layer, appends K/V at
  * pos.  logits_out (host, n_vocab floats) and argmax_out (host) are optional.  Replaces
  * MiniCPM5Engine::forward(token_id, pos, max_seq_len) (model.cpp:142-242); the greedy
- * argmax (lowest index on ties) is computed on the device. */
+ * argmax (lowest index on ties) is computed on the device.  token < 0 uses the argmax
+ * that the previous step left on the device. */
 mcpm_status mcpm_forward(mcpm_engine* e, int token, int pos, float* logits_out, int* argmax_out);
 /* Asynchronous decode step on the engine's stream.  token < 0 reads the token id that the
  * previous step's argmax left on the device (greedy chaining without a host round trip).

@@ -173,7 +173,7 @@ __device__ bool wait_weights(const DecodeParams& p, const Smem& s, int wp) {
     const uint32_t parity = (wp >> 1) & 1;
     bool ok = true;
     for (int i = 0; i < 4; ++i) ok &= mbar_wait(&s.wbar[4 * buf + i], parity, p.err);
-    return ok;
+    return !__syncthreads_or(!ok);   // one decision for the whole CTA
 }
 
 // ------------------------------------------------------------- activation prologues
@@ -512,7 +512,8 @@ __device__ void phase_lm(const DecodeParams& p, const Smem& s, int cta, int ncta
     int nan0 = 0;
     for (int st = 0; st < q.nstages; ++st) {
         const int slot = st & 3;
-        if (!mbar_wait(&s.lmbar[slot], (st >> 2) & 1, p.err)) return;
+        const bool ok = mbar_wait(&s.lmbar[slot], (st >> 2) & 1, p.err);
+        if (__syncthreads_or(!ok)) return;
         const int a = q.r0 + st * q.sr, n = min(q.sr, q.r1 - a);
         float* lg = p.logits;
         const int wl = p.write_logits;

@@ -430,7 +430,6 @@ mcpm_status mcpm_init_kv(mcpm_engine* e, int max_seq) {
 
 mcpm_status mcpm_forward(mcpm_engine* e, int token, int pos, float* logits_out, int* argmax_out) {
     if (!e) return MCPM_BAD_ARG;
-    if (token < 0) return MCPM_BAD_TOKEN;
     mcpm_status st = launch(e, token, pos, logits_out != nullptr);
     if (st != MCPM_OK) return st;
     if (logits_out)

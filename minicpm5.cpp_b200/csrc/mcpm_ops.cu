@@ -108,7 +108,8 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
     for (int st = 0; st < nstages; ++st) {
         const int slot = st % RING_SLOTS, a = r0 + st * sr, n = min(sr, r1 - a);
         const uint8_t* sw = ring + slot * SLOT_STRIDE;
-        if (!mbar_wait(&bars[slot], (st / RING_SLOTS) & 1, err)) return;
+        const bool ok = mbar_wait(&bars[slot], (st / RING_SLOTS) & 1, err);
+        if (__syncthreads_or(!ok)) return;
         if (isum) {
             const int bb = block_bytes(type);
             for (int t = tid; t < n * nb; t += blockDim.x) {

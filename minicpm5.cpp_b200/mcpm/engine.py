@@ -1,0 +1,214 @@
+"""Python binding of the C ABI (include/mcpm.h) through ctypes.
+
+`MiniCPM5Engine` mirrors the reference class (include/model.h:37-70): `init_kv_cache`,
+`load_model`, `forward(token_id, pos, max_seq_len)` returning the logits.  Errors raise
+`MCPMError` carrying the C status.  There is no CPU fallback: without a built library
+or without a CUDA device every call fails loudly.
+
+The op functions take device pointers (ints), e.g. `torch.Tensor.data_ptr()`.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from typing import Optional
+
+import numpy as np
+
+from . import build as _build
+
+_lib = None
+
+STATUS = {0: "ok", 1: "bad argument", 2: "bad file", 3: "unsupported type", 4: "context overflow",
+          5: "CUDA error", 6: "NCCL error", 7: "timeout", 8: "out of memory", 9: "bad token", 10: "not loaded"}
+OK, BAD_ARG, BAD_FILE, UNSUPPORTED_TYPE, CTX_OVERFLOW, CUDA_ERROR, NCCL_ERROR, TIMEOUT, OOM, BAD_TOKEN, NOT_LOADED = range(11)
+ROUND_EVEN, ROUND_AWAY = 0, 1
+Q4_K, Q6_K, Q8_0 = 12, 14, 8
+
+
+class MCPMError(RuntimeError):
+    def __init__(self, status: int, what: str = ""):
+        super().__init__(f"{what}: {STATUS.get(status, status)} ({status})")
+        self.status = status
+
+
+class mcpm_config(C.Structure):
+    _fields_ = [("device", C.c_int), ("max_seq", C.c_int), ("n_ctas", C.c_int), ("reserved", C.c_int * 5)]
+
+
+P, I, F = C.c_void_p, C.c_int, C.c_float
+
+# exported symbol -> (restype, argtypes); tests check that every declared symbol exists
+SIGNATURES = {
+    "mcpm_status_string": (C.c_char_p, [I]),
+    "mcpm_engine_create": (I, [C.POINTER(mcpm_config), C.POINTER(P)]),
+    "mcpm_load_gguf": (I, [P, C.c_char_p]),
+    "mcpm_init_kv": (I, [P, I]),
+    "mcpm_forward": (I, [P, I, I, C.POINTER(F), C.POINTER(I)]),
+    "mcpm_forward_async": (I, [P, I, I, I]),
+    "mcpm_sync": (I, [P]),
+    "mcpm_logits_device": (P, [P]),
+    "mcpm_argmax_device": (P, [P]),
+    "mcpm_read_x": (I, [P, C.POINTER(F)]),
+    "mcpm_read_kv": (I, [P, I, I, C.POINTER(F), C.POINTER(F)]),
+    "mcpm_model_dims": (I, [P, C.POINTER(I)]),
+    "mcpm_engine_stream": (P, [P]),
+    "mcpm_engine_n_ctas": (I, [P]),
+    "mcpm_engine_destroy": (None, [P]),
+    "mcpm_quantize_q8k": (I, [P, P, I, I, P]),
+    "mcpm_gemv_q8k": (I, [I, P, P, P, I, I, P]),
+    "mcpm_gemv_blocksums": (I, [I, P, P, P, P, I, I, P]),
+    "mcpm_gemv_gate_up_q8k": (I, [P, P, P, P, P, I, I, P]),
+    "mcpm_rmsnorm_q8k": (I, [P, P, P, I, F, P]),
+    "mcpm_swiglu_q8k": (I, [P, P, P, I, P]),
+    "mcpm_gemv_q8k_timed": (I, [I, P, I, P, P, I, I, I, C.POINTER(F), P]),
+}
+
+
+def lib_path() -> str:
+    return _build.LIB
+
+
+def load_library(build_if_needed: bool = True) -> C.CDLL:
+    """Loads libmcpm.so (building it first when sources changed)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = _build.build() if build_if_needed else _build.LIB
+    if not os.path.exists(path):
+        raise MCPMError(CUDA_ERROR, f"native library missing: {path}")
+    lib = C.CDLL(path)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def check(status: int, what: str) -> None:
+    if status != OK:
+        raise MCPMError(status, what)
+
+
+def _fptr(a: np.ndarray):
+    assert a.dtype == np.float32 and a.flags.c_contiguous
+    return a.ctypes.data_as(C.POINTER(C.c_float))
+
+
+class MiniCPM5Engine:
+    """Device engine behind the reference's MiniCPM5Engine interface."""
+
+    def __init__(self, device: int = 0, max_seq: int = 0, n_ctas: int = 0):
+        self.lib = load_library()
+        cfg = mcpm_config(device, max_seq, n_ctas)
+        h = P()
+        check(self.lib.mcpm_engine_create(C.byref(cfg), C.byref(h)), "mcpm_engine_create")
+        self.h = h
+        self.n_vocab = 0
+        self._logits = None
+
+    # reference: void init_kv_cache(int max_seq_len)
+    def init_kv_cache(self, max_seq_len: int) -> None:
+        check(self.lib.mcpm_init_kv(self.h, max_seq_len), "mcpm_init_kv")
+
+    # reference: bool load_model(const std::string&, bool verbose)
+    def load_model(self, path: str, verbose: bool = False) -> bool:
+        st = self.lib.mcpm_load_gguf(self.h, path.encode())
+        if st != OK:
+            if verbose:
+                print(f"[mcpm] load_model failed: {STATUS.get(st, st)}")
+            return False
+        dims = (C.c_int * 6)()
+        check(self.lib.mcpm_model_dims(self.h, dims), "mcpm_model_dims")
+        self.n_vocab = dims[5]
+        self._logits = np.zeros(self.n_vocab, np.float32)
+        return True
+
+    # reference: const std::vector<float>& forward(int token_id, int pos, int max_seq_len)
+    def forward(self, token_id: int, pos: int, max_seq_len: Optional[int] = None) -> np.ndarray:
+        am = C.c_int()
+        check(self.lib.mcpm_forward(self.h, token_id, pos, _fptr(self._logits), C.byref(am)), "mcpm_forward")
+        self.last_argmax = am.value
+        return self._logits
+
+    def forward_greedy(self, token_id: int, pos: int) -> int:
+        """One step returning only the device argmax (no logits copy)."""
+        am = C.c_int()
+        check(self.lib.mcpm_forward(self.h, token_id, pos, None, C.byref(am)), "mcpm_forward")
+        return am.value
+
+    def forward_async(self, token_id: int, pos: int, write_logits: bool = False) -> None:
+        check(self.lib.mcpm_forward_async(self.h, token_id, pos, int(write_logits)), "mcpm_forward_async")
+
+    def sync(self) -> None:
+        check(self.lib.mcpm_sync(self.h), "mcpm_sync")
+
+    def read_x(self) -> np.ndarray:
+        x = np.zeros(2048, np.float32)
+        check(self.lib.mcpm_read_x(self.h, _fptr(x)), "mcpm_read_x")
+        return x
+
+    def read_kv(self, layer: int, pos: int):
+        k = np.zeros(256, np.float32)
+        v = np.zeros(256, np.float32)
+        check(self.lib.mcpm_read_kv(self.h, layer, pos, _fptr(k), _fptr(v)), "mcpm_read_kv")
+        return k, v
+
+    @property
+    def stream(self) -> int:
+        return self.lib.mcpm_engine_stream(self.h) or 0
+
+    @property
+    def n_ctas(self) -> int:
+        return self.lib.mcpm_engine_n_ctas(self.h)
+
+    @property
+    def logits_device_ptr(self) -> int:
+        return self.lib.mcpm_logits_device(self.h)
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            self.lib.mcpm_engine_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ------------------------------------------------------------------ ops on device pointers
+def quantize_q8k(x_ptr: int, y_ptr: int, n: int, rounding: int, stream: int = 0) -> None:
+    check(load_library().mcpm_quantize_q8k(x_ptr, y_ptr, n, rounding, stream), "mcpm_quantize_q8k")
+
+
+def gemv_q8k(ggml_type: int, w_ptr: int, xq_ptr: int, y_ptr: int, rows: int, cols: int, stream: int = 0) -> None:
+    check(load_library().mcpm_gemv_q8k(ggml_type, w_ptr, xq_ptr, y_ptr, rows, cols, stream), "mcpm_gemv_q8k")
+
+
+def gemv_blocksums(ggml_type: int, w_ptr: int, xq_ptr: int, isum_ptr: int, aux_ptr: int, rows: int, cols: int,
+                   stream: int = 0) -> None:
+    check(load_library().mcpm_gemv_blocksums(ggml_type, w_ptr, xq_ptr, isum_ptr, aux_ptr, rows, cols, stream),
+          "mcpm_gemv_blocksums")
+
+
+def gemv_gate_up_q8k(wg_ptr, wu_ptr, xq_ptr, g_ptr, u_ptr, rows, cols, stream=0) -> None:
+    check(load_library().mcpm_gemv_gate_up_q8k(wg_ptr, wu_ptr, xq_ptr, g_ptr, u_ptr, rows, cols, stream),
+          "mcpm_gemv_gate_up_q8k")
+
+
+def rmsnorm_q8k(x_ptr: int, w_ptr: int, out_ptr: int, n: int, eps: float = 1e-6, stream: int = 0) -> None:
+    check(load_library().mcpm_rmsnorm_q8k(x_ptr, w_ptr, out_ptr, n, eps, stream), "mcpm_rmsnorm_q8k")
+
+
+def swiglu_q8k(g_ptr: int, u_ptr: int, out_ptr: int, n: int, stream: int = 0) -> None:
+    check(load_library().mcpm_swiglu_q8k(g_ptr, u_ptr, out_ptr, n, stream), "mcpm_swiglu_q8k")
+
+
+def gemv_q8k_timed(ggml_type, w_ptr, n_copies, xq_ptr, y_ptr, rows, cols, reps, stream=0) -> float:
+    ms = C.c_float()
+    check(load_library().mcpm_gemv_q8k_timed(ggml_type, w_ptr, n_copies, xq_ptr, y_ptr, rows, cols, reps,
+                                             C.byref(ms), stream), "mcpm_gemv_q8k_timed")
+    return ms.value

@@ -1,0 +1,96 @@
+"""Whole-forward parity on the GPU through the C ABI.
+
+The CUDA decode path and the C restatement follow the same canonical numerics, so logits,
+the residual stream, K/V cache rows and greedy tokens are compared for exact equality.
+The restatement itself is checked against the reference build in test_oracle_vs_reference.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+N_PROMPT, N_GEN = 12, 8
+MAX_SEQ = 64
+
+
+@pytest.fixture(scope="module")
+def engine(cuda, model_path):
+    from mcpm import engine as E
+    e = E.MiniCPM5Engine(device=0, max_seq=MAX_SEQ)
+    assert e.load_model(model_path)
+    yield e
+    e.close()
+
+
+@pytest.fixture(scope="module")
+def oracle_model(oracle, model_path):
+    import oracle as O
+    return O.OracleModel(oracle, model_path, MAX_SEQ)
+
+
+def test_forward_bitexact_vs_restatement(engine, oracle_model):
+    from mcpm import synth
+    prompt = synth.prompt_ids(N_PROMPT)
+    ref_logits = np.zeros(engine.n_vocab, np.float32)
+    tok = None
+    for pos in range(N_PROMPT + N_GEN):
+        t = int(prompt[pos]) if pos < N_PROMPT else tok
+        got = engine.forward(t, pos).copy()
+        want_tok = oracle_model.forward(t, pos, ref_logits)
+        gx, ox = engine.read_x(), oracle_model.x()
+        assert np.array_equal(gx.view(np.uint32), ox.view(np.uint32)), \
+            f"pos {pos}: residual differs in {np.sum(gx != ox)} elements"
+        diff = np.sum(got.view(np.uint32) != ref_logits.view(np.uint32))
+        assert diff == 0, f"pos {pos}: {diff} logits differ, max {np.max(np.abs(got - ref_logits))}"
+        assert engine.last_argmax == want_tok
+        tok = want_tok
+
+
+def test_kv_rows_written_at_pos(engine, oracle):
+    k, v = engine.read_kv(3, 5)
+    assert np.all(np.isfinite(k)) and np.any(k != 0) and np.any(v != 0)
+
+
+def test_greedy_chain_on_device(cuda, model_path):
+    """token < 0 feeds the previous step's device argmax back without a host round trip;
+    the chained run must produce the same tokens as a host-driven run."""
+    from mcpm import engine as E, synth
+    prompt = synth.prompt_ids(4)
+    host = E.MiniCPM5Engine(device=0, max_seq=MAX_SEQ)
+    chain = E.MiniCPM5Engine(device=0, max_seq=MAX_SEQ)
+    assert host.load_model(model_path) and chain.load_model(model_path)
+    tok = None
+    for pos in range(10):
+        tok = host.forward_greedy(int(prompt[pos]) if pos < 4 else tok, pos)
+    for pos in range(4):
+        chain.forward_async(int(prompt[pos]), pos)
+    for pos in range(4, 9):
+        chain.forward_async(-1, pos)
+    chain.sync()
+    assert chain.forward_greedy(-1, 9) == tok
+    host.close()
+    chain.close()
+
+
+def test_errors_are_reported(engine):
+    from mcpm import engine as E
+    with pytest.raises(E.MCPMError) as ei:
+        engine.forward(0, MAX_SEQ)
+    assert ei.value.status == E.CTX_OVERFLOW
+    with pytest.raises(E.MCPMError) as ei:
+        engine.forward(engine.n_vocab, 0)
+    assert ei.value.status == E.BAD_TOKEN
+    # the engine keeps working after rejected calls
+    assert isinstance(engine.forward_greedy(1, 0), int)
+
+
+def test_bad_file(cuda, tmp_path):
+    from mcpm import engine as E
+    p = tmp_path / "bad.gguf"
+    p.write_bytes(b"GGUF\x03\x00\x00\x00" + b"\xff" * 64)
+    e = E.MiniCPM5Engine(device=0, max_seq=8)
+    assert not e.load_model(str(p))
+    with pytest.raises(E.MCPMError) as ei:
+        e.forward(1, 0)
+    assert ei.value.status == E.NOT_LOADED
+    e.close()

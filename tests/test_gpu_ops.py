@@ -1,0 +1,157 @@
+"""Kernel-level parity on the GPU, through the C ABI.
+
+Bit-exact checks: Q8_K quantisers (both rounding rules), the quantised GEMVs (Q4_K, Q6_K;
+outputs identical to the reference's AVX2 kernels and to the C restatement), their
+integer block sums, RMSNorm->Q8_K and SwiGLU->Q8_K against the restatement.
+"""
+import numpy as np
+import pytest
+
+from conftest import rand_tensor_bytes
+
+pytestmark = pytest.mark.gpu
+
+
+def _dev(cuda, arr):
+    return cuda.from_numpy(np.ascontiguousarray(arr)).cuda()
+
+
+def _q8k_from_dev(cuda, t):
+    import oracle as O
+    return t.cpu().numpy().view(O.Q8K_DTYPE)
+
+
+def _q8k_eq(a, b):
+    assert np.array_equal(a["qs"], b["qs"])
+    assert np.array_equal(a["bsums"], b["bsums"])
+    assert np.array_equal(a["d"].view(np.uint32), b["d"].view(np.uint32))
+
+
+@pytest.mark.parametrize("rounding", [0, 1])
+@pytest.mark.parametrize("kind", ["normal", "zeros", "tiny", "nan", "huge"])
+def test_quantize_q8k_exact(cuda, oracle, rounding, kind):
+    from mcpm import engine as E
+    rng = np.random.default_rng(3)
+    x = rng.normal(0, 1, 256 * 24).astype(np.float32)
+    if kind == "zeros":
+        x[:512] = 0
+    elif kind == "tiny":
+        x *= 1e-38
+    elif kind == "nan":
+        x[5] = np.nan
+        x[256 + 255] = np.nan          # last element of a block: block amax NaN -> zero block
+        x[512 + 100] = np.nan
+    elif kind == "huge":
+        x[7] = 3e38
+    xd = _dev(cuda, x)
+    yd = cuda.zeros(24 * 292, dtype=cuda.uint8, device="cuda")
+    E.quantize_q8k(xd.data_ptr(), yd.data_ptr(), x.size, rounding)
+    cuda.cuda.synchronize()
+    got = _q8k_from_dev(cuda, yd)
+    _q8k_eq(got, oracle.quantize_q8k(x, rounding, 1))
+
+
+SHAPES = [(2048, 2048), (256, 2048), (6144, 2048), (2048, 6144), (1, 2048), (37, 2048), (130560, 2048)]
+
+
+@pytest.mark.parametrize("ggml_type", [12, 14])
+@pytest.mark.parametrize("rows,cols", SHAPES)
+def test_gemv_bitexact(cuda, oracle, ggml_type, rows, cols):
+    from mcpm import engine as E
+    if ggml_type == 12 and rows == 130560:
+        pytest.skip("LM head is Q6_K")
+    w = rand_tensor_bytes(ggml_type, rows, cols, seed=rows * 7 + cols + ggml_type)
+    x = np.random.default_rng(rows + cols).normal(0, 1, cols).astype(np.float32)
+    xq = oracle.quantize_q8k(x, 0, 1)
+    wd, xqd = _dev(cuda, w), _dev(cuda, xq.view(np.uint8))
+    yd = cuda.zeros(rows, dtype=cuda.float32, device="cuda")
+    E.gemv_q8k(ggml_type, wd.data_ptr(), xqd.data_ptr(), yd.data_ptr(), rows, cols)
+    cuda.cuda.synchronize()
+    got = yd.cpu().numpy()
+    want = oracle.gemv_q8k(ggml_type, w, xq, rows, cols, order=1, fused_min=1)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), \
+        f"{np.sum(got != want)} of {rows} rows differ, max {np.max(np.abs(got - want))}"
+
+
+@pytest.mark.parametrize("ggml_type", [12, 14])
+def test_gemv_matches_reference_build(cuda, oracle, ref, ggml_type):
+    from mcpm import engine as E
+    rows, cols = 512, 6144
+    w = rand_tensor_bytes(ggml_type, rows, cols, seed=11)
+    xq = ref.quantize_q8k(np.random.default_rng(5).normal(0, 3, cols).astype(np.float32))
+    wd, xqd = _dev(cuda, w), _dev(cuda, xq.view(np.uint8))
+    yd = cuda.zeros(rows, dtype=cuda.float32, device="cuda")
+    E.gemv_q8k(ggml_type, wd.data_ptr(), xqd.data_ptr(), yd.data_ptr(), rows, cols)
+    cuda.cuda.synchronize()
+    assert np.array_equal(yd.cpu().numpy(), ref.gemv_q8k(ggml_type, w, xq, rows, cols))
+
+
+@pytest.mark.parametrize("ggml_type", [12, 14])
+def test_blocksums_exact(cuda, oracle, ggml_type):
+    from mcpm import engine as E
+    rows, cols = 300, 6144 if ggml_type == 14 else 2048
+    w = rand_tensor_bytes(ggml_type, rows, cols, seed=21)
+    xq = oracle.quantize_q8k(np.random.default_rng(9).normal(0, 1, cols).astype(np.float32), 1, 1)
+    nb = cols // 256
+    wd, xqd = _dev(cuda, w), _dev(cuda, xq.view(np.uint8))
+    isum = cuda.zeros(rows * nb, dtype=cuda.int32, device="cuda")
+    aux = cuda.zeros(rows * nb, dtype=cuda.int32, device="cuda")
+    E.gemv_blocksums(ggml_type, wd.data_ptr(), xqd.data_ptr(), isum.data_ptr(), aux.data_ptr(), rows, cols)
+    cuda.cuda.synchronize()
+    wi, wa = oracle.blocksums(ggml_type, w, xq, rows, cols)
+    assert np.array_equal(isum.cpu().numpy().reshape(rows, nb), wi)
+    assert np.array_equal(aux.cpu().numpy().reshape(rows, nb), wa)
+
+
+def test_gate_up(cuda, oracle):
+    from mcpm import engine as E
+    rows, cols = 6144, 2048
+    wg = rand_tensor_bytes(12, rows, cols, seed=31)
+    wu = rand_tensor_bytes(12, rows, cols, seed=32)
+    xq = oracle.quantize_q8k(np.random.default_rng(1).normal(0, 1, cols).astype(np.float32), 1, 1)
+    g = cuda.zeros(rows, dtype=cuda.float32, device="cuda")
+    u = cuda.zeros(rows, dtype=cuda.float32, device="cuda")
+    xqd = _dev(cuda, xq.view(np.uint8))
+    E.gemv_gate_up_q8k(_dev(cuda, wg).data_ptr(), _dev(cuda, wu).data_ptr(), xqd.data_ptr(), g.data_ptr(),
+                       u.data_ptr(), rows, cols)
+    cuda.cuda.synchronize()
+    assert np.array_equal(g.cpu().numpy(), oracle.gemv_q8k(12, wg, xq, rows, cols, 1, 1))
+    assert np.array_equal(u.cpu().numpy(), oracle.gemv_q8k(12, wu, xq, rows, cols, 1, 1))
+
+
+@pytest.mark.parametrize("scale", [1.0, 300.0, 1e-30])
+def test_rmsnorm_q8k_exact(cuda, oracle, scale):
+    from mcpm import engine as E
+    rng = np.random.default_rng(int(scale * 7) % 1000)
+    x = (rng.normal(0, 1, 2048) * scale).astype(np.float32)
+    w = (1 + rng.normal(0, 0.02, 2048)).astype(np.float32)
+    out = cuda.zeros(8 * 292, dtype=cuda.uint8, device="cuda")
+    E.rmsnorm_q8k(_dev(cuda, x).data_ptr(), _dev(cuda, w).data_ptr(), out.data_ptr(), 2048, 1e-6)
+    cuda.cuda.synchronize()
+    _q8k_eq(_q8k_from_dev(cuda, out), oracle.rmsnorm_q8k(x, w))
+
+
+@pytest.mark.parametrize("scale", [1.0, 50.0, 2000.0])
+def test_swiglu_q8k_exact(cuda, oracle, scale):
+    """Large |g| makes exp(-g) overflow: the reference build's silu is NaN there."""
+    from mcpm import engine as E
+    rng = np.random.default_rng(int(scale))
+    g = (rng.normal(0, 1, 6144) * scale).astype(np.float32)
+    u = (rng.normal(0, 1, 6144) * scale).astype(np.float32)
+    out = cuda.zeros(24 * 292, dtype=cuda.uint8, device="cuda")
+    E.swiglu_q8k(_dev(cuda, g).data_ptr(), _dev(cuda, u).data_ptr(), out.data_ptr(), 6144)
+    cuda.cuda.synchronize()
+    _q8k_eq(_q8k_from_dev(cuda, out), oracle.swiglu_q8k(g, u))
+
+
+def test_op_argument_errors(cuda):
+    from mcpm import engine as E
+    t = cuda.zeros(4096, dtype=cuda.float32, device="cuda")
+    with pytest.raises(E.MCPMError) as ei:
+        E.quantize_q8k(t.data_ptr(), t.data_ptr(), 100, 0)
+    assert ei.value.status == E.BAD_ARG
+    with pytest.raises(E.MCPMError) as ei:
+        E.gemv_q8k(8, t.data_ptr(), t.data_ptr(), t.data_ptr(), 4, 2048)
+    assert ei.value.status == E.UNSUPPORTED_TYPE
+    with pytest.raises(E.MCPMError):
+        E.gemv_q8k(14, t.data_ptr(), t.data_ptr(), t.data_ptr(), 4, 256)   # Q6_K rows must be 16-byte multiples
