@@ -36,6 +36,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--prompt", type=int, default=PROMPT, help="prefill length (untimed)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -186,15 +187,15 @@ def main():
     path = synth.ensure_model("q4_k_m", 0)
     if pg:
         pg.barrier()
-    max_seq = PROMPT + args.warmup + args.steps + 8
+    max_seq = args.prompt + args.warmup + args.steps + 80
     eng = E.MiniCPM5Engine(device=local, max_seq=max_seq)
     if not eng.load_model(path):
         raise SystemExit("load_model failed")
     stream = torch.cuda.ExternalStream(eng.stream)
-    prompt = synth.prompt_ids(PROMPT, seed=1234 + rank)
-    for pos in range(PROMPT):                      # prefill (untimed)
+    prompt = synth.prompt_ids(args.prompt, seed=1234 + rank)
+    for pos in range(args.prompt):                      # prefill (untimed)
         eng.forward_async(int(prompt[pos]), pos)
-    pos = PROMPT
+    pos = args.prompt
     for _ in range(args.warmup):
         eng.forward_async(-1, pos)
         pos += 1
@@ -252,7 +253,7 @@ def main():
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 dot / fp32",
             "data": "synthetic (seeded random-init GGUF, Q4_K_M layout)",
             "config": {"workload": "config0: MiniCPM5-2B Q4_K_M greedy decode, batch 1 per GPU",
-                       "prompt": PROMPT, "positions": [first_pos, first_pos + args.steps - 1],
+                       "prompt": args.prompt, "positions": [first_pos, first_pos + args.steps - 1],
                        "parallelism": f"dp{world} (independent sequences)",
                        "l2": "inputs larger than L2 (1.41 GB of weights per token)"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",

@@ -128,7 +128,8 @@ class MiniCPM5Engine:
     # reference: const std::vector<float>& forward(int token_id, int pos, int max_seq_len)
     def forward(self, token_id: int, pos: int, max_seq_len: Optional[int] = None) -> np.ndarray:
         am = C.c_int()
-        check(self.lib.mcpm_forward(self.h, token_id, pos, _fptr(self._logits), C.byref(am)), "mcpm_forward")
+        lg = _fptr(self._logits) if self._logits is not None else None
+        check(self.lib.mcpm_forward(self.h, token_id, pos, lg, C.byref(am)), "mcpm_forward")
         self.last_argmax = am.value
         return self._logits
 

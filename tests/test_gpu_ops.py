@@ -112,8 +112,8 @@ def test_gate_up(cuda, oracle):
     g = cuda.zeros(rows, dtype=cuda.float32, device="cuda")
     u = cuda.zeros(rows, dtype=cuda.float32, device="cuda")
     xqd = _dev(cuda, xq.view(np.uint8))
-    E.gemv_gate_up_q8k(_dev(cuda, wg).data_ptr(), _dev(cuda, wu).data_ptr(), xqd.data_ptr(), g.data_ptr(),
-                       u.data_ptr(), rows, cols)
+    wgd, wud = _dev(cuda, wg), _dev(cuda, wu)   # keep the device copies alive across the launch
+    E.gemv_gate_up_q8k(wgd.data_ptr(), wud.data_ptr(), xqd.data_ptr(), g.data_ptr(), u.data_ptr(), rows, cols)
     cuda.cuda.synchronize()
     assert np.array_equal(g.cpu().numpy(), oracle.gemv_q8k(12, wg, xq, rows, cols, 1, 1))
     assert np.array_equal(u.cpu().numpy(), oracle.gemv_q8k(12, wu, xq, rows, cols, 1, 1))
@@ -126,7 +126,8 @@ def test_rmsnorm_q8k_exact(cuda, oracle, scale):
     x = (rng.normal(0, 1, 2048) * scale).astype(np.float32)
     w = (1 + rng.normal(0, 0.02, 2048)).astype(np.float32)
     out = cuda.zeros(8 * 292, dtype=cuda.uint8, device="cuda")
-    E.rmsnorm_q8k(_dev(cuda, x).data_ptr(), _dev(cuda, w).data_ptr(), out.data_ptr(), 2048, 1e-6)
+    xd, wd = _dev(cuda, x), _dev(cuda, w)
+    E.rmsnorm_q8k(xd.data_ptr(), wd.data_ptr(), out.data_ptr(), 2048, 1e-6)
     cuda.cuda.synchronize()
     _q8k_eq(_q8k_from_dev(cuda, out), oracle.rmsnorm_q8k(x, w))
 
@@ -139,7 +140,8 @@ def test_swiglu_q8k_exact(cuda, oracle, scale):
     g = (rng.normal(0, 1, 6144) * scale).astype(np.float32)
     u = (rng.normal(0, 1, 6144) * scale).astype(np.float32)
     out = cuda.zeros(24 * 292, dtype=cuda.uint8, device="cuda")
-    E.swiglu_q8k(_dev(cuda, g).data_ptr(), _dev(cuda, u).data_ptr(), out.data_ptr(), 6144)
+    gd, ud = _dev(cuda, g), _dev(cuda, u)
+    E.swiglu_q8k(gd.data_ptr(), ud.data_ptr(), out.data_ptr(), 6144)
     cuda.cuda.synchronize()
     _q8k_eq(_q8k_from_dev(cuda, out), oracle.swiglu_q8k(g, u))
 
