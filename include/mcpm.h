@@ -73,6 +73,13 @@ mcpm_status mcpm_read_x(mcpm_engine* e, float* x_host);
 mcpm_status mcpm_read_kv(mcpm_engine* e, int layer, int pos, float* k_host, float* v_host);
 /* n_layer, n_embd, n_ff, n_head, n_head_kv, n_vocab of the loaded model. */
 mcpm_status mcpm_model_dims(mcpm_engine* e, int dims[6]);
+/* Phase trace (no reference counterpart; the reference only times whole loops,
+ * chat_session.cpp:152-187): when enabled, each decode step records globaltimer
+ * nanoseconds on CTA 0 -- [0] kernel start, then per phase i (5 per layer: QKV, attention,
+ * o_proj, gate/up, down) [2+2i] = its own work done, [3+2i] = grid barrier released, and
+ * [2+2*(5*n_layer)] = LM head done.  mcpm_trace_read copies up to n words. */
+mcpm_status mcpm_trace_enable(mcpm_engine* e, int enable);
+mcpm_status mcpm_trace_read(mcpm_engine* e, unsigned long long* out, int n);
 /* The engine's CUDA stream (cudaStream_t) and decode grid size. */
 void* mcpm_engine_stream(mcpm_engine* e);
 int mcpm_engine_n_ctas(mcpm_engine* e);
@@ -104,6 +111,15 @@ mcpm_status mcpm_gemv_gate_up_q8k(const void* wg, const void* wu, const void* xq
 mcpm_status mcpm_rmsnorm_q8k(const float* x, const float* w, void* out, int n, float eps, void* stream);
 /* swiglu_and_quantize_q8k (ops.cpp:725-765); n % 256 == 0. */
 mcpm_status mcpm_swiglu_q8k(const float* gate, const float* up, void* out, int n, void* stream);
+/* GQA decode attention for one layer (execute_attention, ops.cpp:537-628): writes k, v
+ * (256 floats each, already rotated) into kcache/vcache ([max_seq][256] fp32) at pos,
+ * then out[16*128] = softmax(q.K^T / sqrt(128)) V over positions 0..pos, 8 query heads
+ * per KV head, split into chunks of 32*ceil((pos+1)/2048) positions.  out_q8k (optional,
+ * 8 block_q8_K) receives out quantised ties-to-even, the o_proj input.  max_seq <= 16384.
+ * Uses a per-device workspace the library allocates on the first call; calls that
+ * overlap on the GPU share it and race. */
+mcpm_status mcpm_attention(const float* q, const float* k, const float* v, float* kcache, float* vcache, int pos,
+                           int max_seq, float* out, void* out_q8k, void* stream);
 /* GEMV throughput probe: `reps` launches of mcpm_gemv_q8k rotating over `n_copies`
  * weight copies laid out back to back from `w` (stride rows*row_bytes), so successive
  * launches miss in L2; writes the mean device time per launch in milliseconds. */

@@ -167,6 +167,19 @@ __device__ bool grid_barrier(const DecodeParams& p) {
     return ld_acquire_u32(p.err) == 0;
 }
 
+// Trace: CTA 0 records when phase `ph` finished its own work (slot 2+2ph) and when the
+// barrier after it released (slot 3+2ph).
+__device__ __forceinline__ void trace_mark(const DecodeParams& p, int slot) {
+    if (p.trace && blockIdx.x == 0 && threadIdx.x == 0) p.trace[slot] = globaltimer();
+}
+
+__device__ bool traced_barrier(const DecodeParams& p, int ph) {
+    trace_mark(p, 2 + 2 * ph);
+    const bool ok = grid_barrier(p);
+    trace_mark(p, 3 + 2 * ph);
+    return ok;
+}
+
 // Waits for this CTA's part of weight phase wp; false on timeout.
 __device__ bool wait_weights(const DecodeParams& p, const Smem& s, int wp) {
     const int buf = wp & 1;
@@ -608,20 +621,21 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
         issue_weight_phase(p, s, 1, cta, ncta);
     }
     __syncthreads();
+    trace_mark(p, 0);
     const LmPlan lmq = lm_plan(p, cta, ncta);
     for (int l = 0; l < p.n_layer; ++l) {
         // weight phase 4l (QKV) is in flight since the previous D phase / kernel start
         if (l > 0 && threadIdx.x == 0) issue_weight_phase(p, s, 4 * l + 1, cta, ncta);
         phase_qkv(p, s, l, token, cta, ncta);
-        if (!grid_barrier(p)) return;
+        if (!traced_barrier(p, 5 * l)) return;
         phase_attention(p, s, l, cta, ncta);
-        if (!grid_barrier(p)) return;
+        if (!traced_barrier(p, 5 * l + 1)) return;
         if (threadIdx.x == 0) issue_weight_phase(p, s, 4 * l + 2, cta, ncta);
         phase_o(p, s, l, cta, ncta);
-        if (!grid_barrier(p)) return;
+        if (!traced_barrier(p, 5 * l + 2)) return;
         if (threadIdx.x == 0) issue_weight_phase(p, s, 4 * l + 3, cta, ncta);
         phase_gu(p, s, l, cta, ncta);
-        if (!grid_barrier(p)) return;
+        if (!traced_barrier(p, 5 * l + 3)) return;
         if (threadIdx.x == 0) {
             if (l + 1 < p.n_layer) {
                 issue_weight_phase(p, s, 4 * (l + 1), cta, ncta);
@@ -631,9 +645,30 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
             }
         }
         phase_down(p, s, l, cta, ncta);
-        if (!grid_barrier(p)) return;
+        if (!traced_barrier(p, 5 * l + 4)) return;
     }
     phase_lm(p, s, cta, ncta);
+    trace_mark(p, 2 + 2 * (5 * p.n_layer));
+}
+
+// ---- standalone attention op (execute_attention, ops.cpp:537-628): K/V append at pos,
+// then the same split-KV chunks and combine as the decode kernel's attention phase.
+constexpr int ATT_SMEM_FLOATS = 8 * HEAD_DIM + 32 * HEAD_DIM + 8 * ATT_SC_STRIDE + 32 + 8 * ATT_MAX_CHUNKS + 8 * HEAD_DIM;
+
+__global__ void k_kv_append(const float* __restrict__ k, const float* __restrict__ v, float* kc, float* vc, int pos) {
+    const int i = threadIdx.x;
+    if (i < KV_DIM) {
+        kc[static_cast<size_t>(pos) * KV_DIM + i] = k[i];
+        vc[static_cast<size_t>(pos) * KV_DIM + i] = v[i];
+    }
+}
+
+__global__ void __launch_bounds__(DEC_THREADS, 1) k_attention(const DecodeParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    Smem s{};
+    s.wbuf[0] = smem_raw;
+    s.flag = reinterpret_cast<int*>(smem_raw + ATT_SMEM_FLOATS * 4);
+    phase_attention(p, s, 0, blockIdx.x, gridDim.x);
 }
 
 }  // namespace
@@ -663,4 +698,24 @@ cudaError_t launch_decode(const DecodeParams& p, int n_ctas, cudaStream_t stream
                                        decode_smem_bytes(), stream);
 }
 
+}  // namespace mcpm
+
+namespace mcpm {
+cudaError_t launch_attention(const float* q, const float* k, const float* v, float* kc, float* vc, int pos, int max_seq,
+                             float* out, uint8_t* out_q8k, float* part, unsigned* cnt, cudaStream_t stream) {
+    k_kv_append<<<1, KV_DIM, 0, stream>>>(k, v, kc, vc, pos);
+    DecodeParams p{};
+    p.q = const_cast<float*>(q);
+    p.kc = kc;
+    p.vc = vc;
+    p.max_seq = max_seq;
+    p.pos = pos;
+    p.att = out;
+    p.att_q8k = out_q8k;
+    p.att_part = part;
+    p.cnt = cnt;
+    const int n = pos + 1, P = 32 * ((n + 2047) / 2048), C = (n + P - 1) / P;
+    k_attention<<<2 * C, DEC_THREADS, ATT_SMEM_FLOATS * 4 + 16, stream>>>(p);
+    return cudaGetLastError();
+}
 }  // namespace mcpm

@@ -56,6 +56,7 @@ struct mcpm_engine {
     uint8_t* att_q8k = nullptr;
     int* ctl = nullptr;       // device control words
     int* ctl_host = nullptr;  // pinned mirror
+    unsigned long long* trace = nullptr;   // phase timestamps when tracing is on
 };
 
 namespace {
@@ -188,6 +189,7 @@ DecodeParams make_params(const mcpm_engine* e, int token, int pos, int write_log
     p.err = reinterpret_cast<unsigned*>(e->ctl + CTL_ERR);
     p.bar = reinterpret_cast<unsigned*>(e->ctl + CTL_BAR);
     p.cnt = reinterpret_cast<unsigned*>(e->ctl + CTL_CNT);
+    p.trace = e->trace;
     p.token = token;
     p.pos = pos;
     p.write_logits = write_logits;
@@ -482,6 +484,29 @@ mcpm_status mcpm_model_dims(mcpm_engine* e, int dims[6]) {
     return MCPM_OK;
 }
 
+mcpm_status mcpm_trace_enable(mcpm_engine* e, int enable) {
+    if (!e) return MCPM_BAD_ARG;
+    MCPM_CUDA(cudaSetDevice(e->device));
+    if (enable && !e->trace) {
+        MCPM_CUDA(cudaMalloc(&e->trace, TRACE_WORDS * sizeof(unsigned long long)));
+        MCPM_CUDA(cudaMemset(e->trace, 0, TRACE_WORDS * sizeof(unsigned long long)));
+    } else if (!enable) {
+        MCPM_CUDA(cudaStreamSynchronize(e->stream));
+        free_dev(e->trace);
+    }
+    return MCPM_OK;
+}
+
+mcpm_status mcpm_trace_read(mcpm_engine* e, unsigned long long* out, int n) {
+    if (!e || !out || n <= 0) return MCPM_BAD_ARG;
+    if (!e->trace) return MCPM_NOT_LOADED;
+    MCPM_CUDA(cudaSetDevice(e->device));
+    MCPM_CUDA(cudaMemcpyAsync(out, e->trace, sizeof(unsigned long long) * std::min(n, TRACE_WORDS),
+                              cudaMemcpyDeviceToHost, e->stream));
+    MCPM_CUDA(cudaStreamSynchronize(e->stream));
+    return MCPM_OK;
+}
+
 void* mcpm_engine_stream(mcpm_engine* e) { return e ? reinterpret_cast<void*>(e->stream) : nullptr; }
 int mcpm_engine_n_ctas(mcpm_engine* e) { return e ? e->n_ctas : 0; }
 
@@ -492,6 +517,7 @@ void mcpm_engine_destroy(mcpm_engine* e) {
     free_kv(e);
     free_model(e);
     free_dev(e->ctl);
+    free_dev(e->trace);
     if (e->ctl_host) cudaFreeHost(e->ctl_host);
     if (e->stream) cudaStreamDestroy(e->stream);
     delete e;
@@ -543,6 +569,38 @@ mcpm_status mcpm_rmsnorm_q8k(const float* x, const float* w, void* out, int n, f
 mcpm_status mcpm_swiglu_q8k(const float* gate, const float* up, void* out, int n, void* stream) {
     if (!gate || !up || !out || n <= 0 || n % 256) return MCPM_BAD_ARG;
     return cuda_status(op_swiglu_q8k(gate, up, out, n, static_cast<cudaStream_t>(stream)));
+}
+
+// Attention workspace (chunk partials, combine counters, Q8_K sink), one per device,
+// allocated on first use and kept until exit.
+namespace {
+struct AttWorkspace {
+    float* part = nullptr;
+    unsigned* cnt = nullptr;
+    uint8_t* q8k = nullptr;
+};
+AttWorkspace g_att_ws[64];
+}  // namespace
+
+mcpm_status mcpm_attention(const float* q, const float* k, const float* v, float* kcache, float* vcache, int pos,
+                           int max_seq, float* out, void* out_q8k, void* stream) {
+    if (!q || !k || !v || !kcache || !vcache || !out || !aligned16(q) || !aligned16(kcache) || !aligned16(vcache))
+        return MCPM_BAD_ARG;
+    if (max_seq <= 0 || max_seq > MAX_SEQ) return MCPM_BAD_ARG;
+    if (pos < 0 || pos >= max_seq) return MCPM_CTX_OVERFLOW;
+    int dev = 0;
+    MCPM_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return MCPM_BAD_ARG;
+    AttWorkspace& ws = g_att_ws[dev];
+    if (!ws.part) {
+        MCPM_CUDA(cudaMalloc(&ws.part, ATT_PART_FLOATS * sizeof(float)));
+        MCPM_CUDA(cudaMalloc(&ws.cnt, 4 * sizeof(unsigned)));
+        MCPM_CUDA(cudaMalloc(&ws.q8k, (N_EMBD / 256) * Q8K_BYTES));
+        MCPM_CUDA(cudaMemset(ws.cnt, 0, 4 * sizeof(unsigned)));
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return cuda_status(launch_attention(q, k, v, kcache, vcache, pos, max_seq, out,
+                                        out_q8k ? static_cast<uint8_t*>(out_q8k) : ws.q8k, ws.part, ws.cnt, s));
 }
 
 mcpm_status mcpm_gemv_q8k_timed(int type, const void* w, int n_copies, const void* xq, float* y, int rows, int cols,

@@ -23,6 +23,7 @@ constexpr int ATT_MAX_CHUNKS = 64;         // attention chunks per head (chunk =
 constexpr int ATT_PART_STRIDE = 2 + HEAD_DIM;
 constexpr int ATT_SC_STRIDE = 256;         // chunk-length bound: 32*ceil(MAX_SEQ/2048)
 constexpr int MAX_SEQ = 16384;
+constexpr int TRACE_WORDS = 2 + 2 * (5 * MAX_LAYERS + 1);
 
 struct LayerDev {
     const uint8_t *wq, *wk, *wv, *wo, *wg, *wu, *wd;
@@ -57,6 +58,7 @@ struct DecodeParams {
     unsigned* bar;      // grid barrier {count, generation}
     unsigned* cnt;      // [0..1] attention combine counters, [2] argmax counter
     unsigned* err;      // error bits
+    unsigned long long* trace;   // optional: CTA 0 phase timestamps (2 per phase + 2)
     int token;          // < 0: read *token_dev
     int pos;
     int write_logits;
@@ -66,6 +68,12 @@ size_t decode_smem_bytes();
 cudaError_t decode_prepare();
 cudaError_t launch_decode(const DecodeParams& p, int n_ctas, cudaStream_t stream);
 int decode_max_ctas_per_sm();
+
+// Standalone attention (mcpm_decode.cu): appends k/v at pos, then split-KV attention with
+// the decode kernel's numerics.  part: ATT_PART_FLOATS floats, cnt: 3 zeroed words.
+constexpr size_t ATT_PART_FLOATS = static_cast<size_t>(N_HEAD) * ATT_MAX_CHUNKS * ATT_PART_STRIDE;
+cudaError_t launch_attention(const float* q, const float* k, const float* v, float* kc, float* vc, int pos, int max_seq,
+                             float* out, uint8_t* out_q8k, float* part, unsigned* cnt, cudaStream_t stream);
 
 // Standalone op launchers (mcpm_ops.cu).
 cudaError_t op_quantize_q8k(const float* x, void* y, int n, int rounding, cudaStream_t s);

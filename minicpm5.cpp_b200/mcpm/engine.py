@@ -62,6 +62,9 @@ SIGNATURES = {
     "mcpm_rmsnorm_q8k": (I, [P, P, P, I, F, P]),
     "mcpm_swiglu_q8k": (I, [P, P, P, I, P]),
     "mcpm_gemv_q8k_timed": (I, [I, P, I, P, P, I, I, I, C.POINTER(F), P]),
+    "mcpm_attention": (I, [P, P, P, P, P, I, I, P, P, P]),
+    "mcpm_trace_enable": (I, [P, I]),
+    "mcpm_trace_read": (I, [P, C.POINTER(C.c_uint64), I]),
 }
 
 
@@ -156,6 +159,15 @@ class MiniCPM5Engine:
         check(self.lib.mcpm_read_kv(self.h, layer, pos, _fptr(k), _fptr(v)), "mcpm_read_kv")
         return k, v
 
+    def trace_enable(self, on: bool = True) -> None:
+        check(self.lib.mcpm_trace_enable(self.h, int(on)), "mcpm_trace_enable")
+
+    def trace_read(self, n_layer: int = 42) -> np.ndarray:
+        n = 3 + 2 * 5 * n_layer
+        buf = (C.c_uint64 * n)()
+        check(self.lib.mcpm_trace_read(self.h, buf, n), "mcpm_trace_read")
+        return np.array(buf, dtype=np.uint64)
+
     @property
     def stream(self) -> int:
         return self.lib.mcpm_engine_stream(self.h) or 0
@@ -213,3 +225,8 @@ def gemv_q8k_timed(ggml_type, w_ptr, n_copies, xq_ptr, y_ptr, rows, cols, reps, 
     check(load_library().mcpm_gemv_q8k_timed(ggml_type, w_ptr, n_copies, xq_ptr, y_ptr, rows, cols, reps,
                                              C.byref(ms), stream), "mcpm_gemv_q8k_timed")
     return ms.value
+
+
+def attention(q_ptr, k_ptr, v_ptr, kc_ptr, vc_ptr, pos, max_seq, out_ptr, out_q8k_ptr=None, stream=0) -> None:
+    check(load_library().mcpm_attention(q_ptr, k_ptr, v_ptr, kc_ptr, vc_ptr, pos, max_seq, out_ptr, out_q8k_ptr,
+                                        stream), "mcpm_attention")

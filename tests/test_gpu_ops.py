@@ -157,3 +157,43 @@ def test_op_argument_errors(cuda):
     assert ei.value.status == E.UNSUPPORTED_TYPE
     with pytest.raises(E.MCPMError):
         E.gemv_q8k(14, t.data_ptr(), t.data_ptr(), t.data_ptr(), 4, 256)   # Q6_K rows must be 16-byte multiples
+
+
+@pytest.mark.parametrize("pos", [0, 1, 31, 32, 100, 2047, 2048, 5000])
+def test_attention_exact(cuda, oracle, pos):
+    """Split-KV GQA attention (execute_attention) against the restatement, including the
+    K/V append at pos and the ties-to-even Q8_K of the output (the o_proj input)."""
+    import ctypes as C
+    import oracle as O
+    from mcpm import engine as E
+    max_seq = 6000
+    rng = np.random.default_rng(pos + 1)
+    q = (rng.normal(0, 3, 2048)).astype(np.float32)
+    k = (rng.normal(0, 3, 256)).astype(np.float32)
+    v = (rng.normal(0, 3, 256)).astype(np.float32)
+    kc = (rng.normal(0, 3, (max_seq, 256))).astype(np.float32)
+    vc = (rng.normal(0, 3, (max_seq, 256))).astype(np.float32)
+    qd, kd, vd, kcd, vcd = (_dev(cuda, a) for a in (q, k, v, kc, vc))
+    out = cuda.zeros(2048, dtype=cuda.float32, device="cuda")
+    oq = cuda.zeros(8 * 292, dtype=cuda.uint8, device="cuda")
+    E.attention(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), kcd.data_ptr(), vcd.data_ptr(), pos, max_seq,
+                out.data_ptr(), oq.data_ptr())
+    cuda.cuda.synchronize()
+    want = np.zeros(2048, np.float32)
+    assert oracle.lib.orc_attention(O._fptr(want), O._fptr(q), O._fptr(k), O._fptr(v), O._fptr(kc), O._fptr(vc),
+                                    pos, max_seq, 16, 2, 128) == 0
+    got = out.cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), np.max(np.abs(got - want))
+    assert np.array_equal(kcd.cpu().numpy()[pos], k) and np.array_equal(vcd.cpu().numpy()[pos], v)
+    _q8k_eq(_q8k_from_dev(cuda, oq), oracle.quantize_q8k(want, 0, 1))
+
+
+def test_attention_rejects_out_of_range(cuda):
+    from mcpm import engine as E
+    t = cuda.zeros(4096, dtype=cuda.float32, device="cuda")
+    with pytest.raises(E.MCPMError) as ei:
+        E.attention(t.data_ptr(), t.data_ptr(), t.data_ptr(), t.data_ptr(), t.data_ptr(), 8, 8, t.data_ptr())
+    assert ei.value.status == E.CTX_OVERFLOW
+    with pytest.raises(E.MCPMError) as ei:
+        E.attention(t.data_ptr(), t.data_ptr(), t.data_ptr(), t.data_ptr(), t.data_ptr(), 1, 20000, t.data_ptr())
+    assert ei.value.status == E.BAD_ARG
