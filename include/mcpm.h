@@ -120,6 +120,16 @@ mcpm_status mcpm_swiglu_q8k(const float* gate, const float* up, void* out, int n
  * overlap on the GPU share it and race. */
 mcpm_status mcpm_attention(const float* q, const float* k, const float* v, float* kcache, float* vcache, int pos,
                            int max_seq, float* out, void* out_q8k, void* stream);
+/* Same computation and results as mcpm_attention, for callers that cannot allocate device
+ * memory (code running inside someone else's graph capture, hosts that own every
+ * allocation, loops that must not call the allocator).  No counterpart in the reference.
+ * The split-KV workspace is a fixed 532,480-byte array in the library's static device
+ * memory (held by every GPU that loads the library until exit), so contexts are limited to
+ * pos + 1 <= 16384 and max_seq <= 16384 (MCPM_BAD_ARG beyond).  No call allocates; the
+ * first call on a device looks up the workspace address, so make it before any stream
+ * capture.  All calls on a device share the workspace: calls that overlap on the GPU race. */
+mcpm_status mcpm_attention_noalloc(const float* q, const float* k, const float* v, float* kcache, float* vcache,
+                                   int pos, int max_seq, float* out, void* out_q8k, void* stream);
 /* GEMV throughput probe: `reps` launches of mcpm_gemv_q8k rotating over `n_copies`
  * weight copies laid out back to back from `w` (stride rows*row_bytes), so successive
  * launches miss in L2; writes the mean device time per launch in milliseconds. */

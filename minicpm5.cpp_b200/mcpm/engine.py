@@ -63,6 +63,7 @@ SIGNATURES = {
     "mcpm_swiglu_q8k": (I, [P, P, P, I, P]),
     "mcpm_gemv_q8k_timed": (I, [I, P, I, P, P, I, I, I, C.POINTER(F), P]),
     "mcpm_attention": (I, [P, P, P, P, P, I, I, P, P, P]),
+    "mcpm_attention_noalloc": (I, [P, P, P, P, P, I, I, P, P, P]),
     "mcpm_trace_enable": (I, [P, I]),
     "mcpm_trace_read": (I, [P, C.POINTER(C.c_uint64), I]),
 }
