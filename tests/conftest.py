@@ -11,7 +11,7 @@ import pytest
 
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 PKG = os.path.join(REPO, "minicpm5.cpp_b200")
-for p in (PKG, os.path.join(REPO, "oracle")):
+for p in (PKG, os.path.join(REPO, "oracle"), os.path.join(REPO, "tests", "golden")):
     if p not in sys.path:
         sys.path.insert(0, p)
 
