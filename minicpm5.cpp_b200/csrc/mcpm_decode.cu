@@ -138,31 +138,34 @@ __device__ void issue_lm_stage(const DecodeParams& p, const Smem& s, const LmPla
     if (bytes) bulk_g2s(lm_slot(s, slot), p.lm + static_cast<size_t>(a) * q.rb, bytes, &s.lmbar[slot]);
 }
 
-// Bounded grid barrier (all CTAs co-resident: cooperative launch).  Returns false if
-// any CTA has flagged an error; callers then return.
-__device__ bool grid_barrier(const DecodeParams& p) {
+// Bounded grid barrier (all CTAs co-resident: cooperative launch).  A monotonic arrival
+// counter: barrier i of a launch completes when the counter reaches base + (i+1)*ncta, so
+// the last arrival costs one fire-and-forget release-add and the waiters one acquire poll.
+// `base` (bar[1]) is advanced by CTA 0 after the launch's last barrier; the host zeroes both
+// words after an error.  While waiting, thread 0 runs `during` (issues the next TMA copies).
+struct BarState {
+    unsigned base;
+    unsigned idx;
+};
+
+template <typename F>
+__device__ bool grid_barrier(const DecodeParams& p, BarState& bs, F&& during) {
     __syncthreads();
     if (threadIdx.x == 0) {
-        unsigned* count = p.bar;
-        unsigned* gen = p.bar + 1;
-        const unsigned g = ld_acquire_u32(gen);
-        __threadfence();
-        const unsigned arrived = atomicAdd(count, 1u);
-        if (arrived == gridDim.x - 1) {
-            atomicExch(count, 0u);
-            __threadfence();
-            st_release_u32(gen, g + 1);
-        } else {
+        red_release_add_u32(p.bar, 1u);
+        during();
+        const unsigned target = bs.base + (bs.idx + 1) * gridDim.x;
+        if (static_cast<int>(ld_acquire_u32(p.bar) - target) < 0) {
             const uint64_t t0 = globaltimer();
-            while (ld_acquire_u32(gen) == g) {
+            while (static_cast<int>(ld_acquire_u32(p.bar) - target) < 0) {
                 if (globaltimer() - t0 > 1000000000ull) {
                     atomicOr(p.err, ERR_TIMEOUT);
                     break;
                 }
             }
         }
-        __threadfence();
     }
+    ++bs.idx;
     __syncthreads();
     return ld_acquire_u32(p.err) == 0;
 }
@@ -173,11 +176,29 @@ __device__ __forceinline__ void trace_mark(const DecodeParams& p, int slot) {
     if (p.trace && blockIdx.x == 0 && threadIdx.x == 0) p.trace[slot] = globaltimer();
 }
 
-__device__ bool traced_barrier(const DecodeParams& p, int ph) {
+// Sub-step marks inside the phases of layer 1 (phase kind ph: 0 QKV .. 4 D, 5 LM).
+__device__ __forceinline__ void trace_step(const DecodeParams& p, int l, int ph, int step) {
+    if (l == 1) trace_mark(p, TRACE_DETAIL + 10 * ph + step);
+}
+
+template <typename F>
+__device__ bool traced_barrier(const DecodeParams& p, BarState& bs, int ph, F&& during) {
     trace_mark(p, 2 + 2 * ph);
-    const bool ok = grid_barrier(p);
+    const bool ok = grid_barrier(p, bs, during);
     trace_mark(p, 3 + 2 * ph);
     return ok;
+}
+
+// Thread 0: L2 prefetch of the K/V rows (both KV heads, contiguous) of this CTA's
+// attention chunk of layer l; the row at pos is written later by the QKV phase.
+__device__ void prefetch_attention(const DecodeParams& p, int l, int cta) {
+    const int n = p.pos + 1, P = 32 * ((n + 2047) / 2048), C = (n + P - 1) / P;
+    if (cta >= 2 * C) return;
+    const int c = cta % C, t0 = c * P, t1 = min(t0 + P, n);
+    const size_t off = (static_cast<size_t>(l) * p.max_seq + t0) * KV_DIM;
+    const uint32_t bytes = static_cast<uint32_t>(t1 - t0) * KV_DIM * 4;
+    bulk_prefetch_l2(p.kc + off, bytes);
+    bulk_prefetch_l2(p.vc + off, bytes);
 }
 
 // Waits for this CTA's part of weight phase wp; false on timeout.
@@ -219,34 +240,44 @@ __device__ void embed_row(const DecodeParams& p, int token, float* xs) {
     }
 }
 
-// xq <- Q8_K of (xs * w) * rms(xs), canonical order; rounding per template argument.
-template <bool AWAY>
-__device__ void norm_quant(const float* xs, const float* w, const Smem& s) {
-    const int tid = threadIdx.x;
-    float xv[8];
-    if (tid < 256) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) xv[i] = xs[tid + 256 * i];
+// xq <- Q8_K of (x * w) * rms(x), canonical order; rounding per template argument.
+// FROM_SMEM: x already staged in s.xs; otherwise x is read from global (L2) and staged.
+template <bool AWAY, bool FROM_SMEM>
+__device__ void norm_quant(const float* x, const float* w, const Smem& s) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    float4 w0 = make_float4(0.f, 0.f, 0.f, 0.f), w1 = w0;
+    if (warp < N_EMBD / 256) {   // norm weights first: independent of x
+        w0 = __ldg(reinterpret_cast<const float4*>(w + 256 * warp + 8 * lane));
+        w1 = __ldg(reinterpret_cast<const float4*>(w + 256 * warp + 8 * lane + 4));
     }
-    const float ss = sumsq_2048(xv, s.red);
-    const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(N_EMBD)), 1e-6f)));
-    const int warp = tid >> 5, lane = tid & 31;
+    float* red = s.red;
+    if (tid < 256) {
+        float xv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) xv[i] = FROM_SMEM ? x[tid + 256 * i] : __ldcg(x + tid + 256 * i);
+        if (!FROM_SMEM) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) s.xs[tid + 256 * i] = xv[i];
+        }
+        float a = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) a = __fmaf_rn(xv[i], xv[i], a);
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
+        if (lane == 0) red[warp] = a;
+    }
+    __syncthreads();
     if (warp < N_EMBD / 256) {
-        float y[8];
-        const float* xb = xs + 256 * warp + 8 * lane;
-        const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + 256 * warp + 8 * lane));
-        const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + 256 * warp + 8 * lane + 4));
+        const float ss = __fadd_rn(__fadd_rn(__fadd_rn(red[0], red[1]), __fadd_rn(red[2], red[3])),
+                                   __fadd_rn(__fadd_rn(red[4], red[5]), __fadd_rn(red[6], red[7])));
+        const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(N_EMBD)), 1e-6f)));
+        const float* xb = s.xs + 256 * warp + 8 * lane;
         const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        float y[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) y[k] = __fmul_rn(__fmul_rn(xb[k], wv[k]), rms);
         quant_block_warp<AWAY>(y, s.xq->qs[warp], &s.xq->d[warp], s.xq->bsums[warp]);
     }
-    __syncthreads();
-}
-
-__device__ void load_global_vec(const float* src, float* dst, int n) {
-    for (int i = threadIdx.x * 4; i < n; i += blockDim.x * 4)
-        *reinterpret_cast<float4*>(dst + i) = __ldcg(reinterpret_cast<const float4*>(src + i));
     __syncthreads();
 }
 
@@ -258,11 +289,13 @@ __device__ void phase_qkv(const DecodeParams& p, const Smem& s, int l, int token
         __syncthreads();
         if (cta == 0)
             for (int i = threadIdx.x; i < N_EMBD; i += blockDim.x) p.x[i] = s.xs[i];
+        norm_quant<true, true>(s.xs, L.attn_norm, s);
     } else {
-        load_global_vec(p.x, s.xs, N_EMBD);
+        norm_quant<true, false>(p.x, L.attn_norm, s);
     }
-    norm_quant<true>(s.xs, L.attn_norm, s);
+    trace_step(p, l, 0, 1);
     if (!wait_weights(p, s, 4 * l)) return;
+    trace_step(p, l, 0, 2);
     const PhaseLayout pl = phase_layout(L, 0, cta, ncta);
     const int lo[3] = {0, N_EMBD, N_EMBD + KV_DIM};
     int a, b;
@@ -273,9 +306,10 @@ __device__ void phase_qkv(const DecodeParams& p, const Smem& s, int l, int token
     for (int i = 0; i < 3; ++i) {
         if (pl.nrows[i] == 0) continue;   // uniform across the CTA
         const int base = lo[i] + pl.row0[i] - a;
-        gemv_staged(phase_type(L, 0, i), s.wbuf[0] + pl.off[i], pl.nrows[i], N_EMBD / 256, *s.xq, s.part, MAX_TASKS,
-                    [&](int r, float v) { rv[base + r] = v; });
+        gemv_rows(phase_type(L, 0, i), s.wbuf[0] + pl.off[i], pl.nrows[i], N_EMBD / 256, *s.xq, s.part, MAX_TASKS,
+                  rv + base);
     }
+    trace_step(p, l, 0, 3);
     // RoPE on Q/K pairs (interleaved, ops.cpp:502-516 with the build's FMA contraction),
     // then Q to the query buffer and K/V into the cache at pos (ops.cpp:557-563).
     const float2* cs = p.rope + static_cast<size_t>(p.pos) * (HEAD_DIM / 2);
@@ -321,34 +355,49 @@ __device__ __forceinline__ float dot128_group(const float* q, const float* k, in
     return a;
 }
 
-__device__ void phase_attention(const DecodeParams& p, const Smem& s, int l, int cta, int ncta) {
+// Chunk counts up to DIST_COMBINE_MAX are combined by every CTA in the o_proj prologue
+// (no atomics, no serial combiner); longer contexts use the last-CTA combine below.
+constexpr int DIST_COMBINE_MAX = 16;
+
+__device__ __forceinline__ int attn_chunks(int n) {
+    const int P = 32 * ((n + 2047) / 2048);
+    return (n + P - 1) / P;
+}
+
+__device__ void phase_attention(const DecodeParams& p, const Smem& s, int l, int cta, int ncta, bool combine_here) {
     const int n = p.pos + 1;
     const int P = 32 * ((n + 2047) / 2048);
     const int C = (n + P - 1) / P;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float* qh = reinterpret_cast<float*>(s.wbuf[0]);   // [8][128]
-    float* kb = qh + 8 * HEAD_DIM;                      // [32][128] staged K or V rows
-    float* sc = kb + 32 * HEAD_DIM;                     // [8][ATT_SC_STRIDE] scores -> probabilities
+    float* kb = qh + 8 * HEAD_DIM;                      // [32][128] staged K rows
+    float* vb = kb + 32 * HEAD_DIM;                     // [32][128] staged V rows
+    float* sc = vb + 32 * HEAD_DIM;                     // [8][ATT_SC_STRIDE] scores -> probabilities
     float* stat = sc + 8 * ATT_SC_STRIDE;               // m[8], l[8], 1/L[8]
     float* wts = stat + 32;                             // [8][ATT_MAX_CHUNKS]
     float* ab = wts + 8 * ATT_MAX_CHUNKS;               // [1024] combined output
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(HEAD_DIM)));
     const float* kl = p.kc + static_cast<size_t>(l) * p.max_seq * KV_DIM;
     const float* vl = p.vc + static_cast<size_t>(l) * p.max_seq * KV_DIM;
+    auto stage_rows = [&](const float* src, float* dst, int s0, int ns, int g) {
+        for (int i = tid; i < ns * 32; i += blockDim.x) {
+            const int tt = i >> 5, f = i & 31;
+            reinterpret_cast<float4*>(dst)[i] =
+                __ldcg(reinterpret_cast<const float4*>(src + static_cast<size_t>(s0 + tt) * KV_DIM + g * HEAD_DIM) + f);
+        }
+    };
     for (int item = cta; item < 2 * C; item += ncta) {
         const int g = item / C, c = item % C;
         const int t0 = c * P, t1 = min(t0 + P, n), np = t1 - t0;
+        const bool single = np <= 32;   // q, K and V of the chunk staged in one round trip
         __syncthreads();
         if (tid < 256)
             reinterpret_cast<float4*>(qh)[tid] = __ldcg(reinterpret_cast<const float4*>(p.q + 8 * g * HEAD_DIM) + tid);
         for (int s0 = t0; s0 < t1; s0 += 32) {   // scores, 32 positions at a time
             const int ns = min(32, t1 - s0);
-            __syncthreads();
-            for (int i = tid; i < ns * 32; i += blockDim.x) {
-                const int tt = i >> 5, f = i & 31;
-                reinterpret_cast<float4*>(kb)[i] = __ldcg(
-                    reinterpret_cast<const float4*>(kl + static_cast<size_t>(s0 + tt) * KV_DIM + g * HEAD_DIM) + f);
-            }
+            if (s0 != t0) __syncthreads();
+            stage_rows(kl, kb, s0, ns, g);
+            if (single) stage_rows(vl, vb, s0, ns, g);
             __syncthreads();
             const int ndots = ns * 8;
             for (int it = 0; it < (ndots + 63) / 64; ++it) {
@@ -360,6 +409,7 @@ __device__ void phase_attention(const DecodeParams& p, const Smem& s, int l, int
             }
         }
         __syncthreads();
+        trace_step(p, l, 1, 1);
         if (warp < 8) {   // chunk max, probabilities, position-ordered sum (warp = head)
             float m = -__int_as_float(0x7f800000);
             for (int t = lane; t < np; t += 32) m = fmaxf(m, sc[warp * ATT_SC_STRIDE + t]);
@@ -379,14 +429,12 @@ __device__ void phase_attention(const DecodeParams& p, const Smem& s, int l, int
         for (int s0 = t0; s0 < t1; s0 += 32) {
             const int ns = min(32, t1 - s0);
             __syncthreads();
-            for (int i = tid; i < ns * 32; i += blockDim.x) {
-                const int tt = i >> 5, f = i & 31;
-                reinterpret_cast<float4*>(kb)[i] = __ldcg(
-                    reinterpret_cast<const float4*>(vl + static_cast<size_t>(s0 + tt) * KV_DIM + g * HEAD_DIM) + f);
+            if (!single) {
+                stage_rows(vl, vb, s0, ns, g);
+                __syncthreads();
             }
-            __syncthreads();
             for (int tt = 0; tt < ns; ++tt) {
-                const float v = kb[tt * HEAD_DIM + dd];
+                const float v = vb[tt * HEAD_DIM + dd];
                 acc0 = __fmaf_rn(sc[h0 * ATT_SC_STRIDE + (s0 - t0) + tt], v, acc0);
                 acc1 = __fmaf_rn(sc[h1 * ATT_SC_STRIDE + (s0 - t0) + tt], v, acc1);
             }
@@ -402,6 +450,8 @@ __device__ void phase_attention(const DecodeParams& p, const Smem& s, int l, int
             __stcg(pm + 1, stat[8 + tid]);
         }
         __syncthreads();
+        trace_step(p, l, 1, 2);
+        if (!combine_here) continue;
         if (tid == 0) {
             __threadfence();
             const unsigned old = atomicAdd(&p.cnt[g], 1u);
@@ -416,25 +466,30 @@ __device__ void phase_attention(const DecodeParams& p, const Smem& s, int l, int
             const float* ph = p.att_part + static_cast<size_t>(8 * g + warp) * ATT_MAX_CHUNKS * ATT_PART_STRIDE;
             const float mc0 = lane < C ? __ldcg(ph + lane * ATT_PART_STRIDE) : 0.0f;
             const float mc1 = lane + 32 < C ? __ldcg(ph + (lane + 32) * ATT_PART_STRIDE) : 0.0f;
+            const float lc0 = lane < C ? __ldcg(ph + lane * ATT_PART_STRIDE + 1) : 0.0f;
+            const float lc1 = lane + 32 < C ? __ldcg(ph + (lane + 32) * ATT_PART_STRIDE + 1) : 0.0f;
             float M = -__int_as_float(0x7f800000);
             if (lane < C) M = mc0;
             if (lane + 32 < C) M = fmaxf(M, mc1);
             for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-            if (lane < C) wts[warp * ATT_MAX_CHUNKS + lane] = canon_expf(__fsub_rn(mc0, M));
-            if (lane + 32 < C) wts[warp * ATT_MAX_CHUNKS + lane + 32] = canon_expf(__fsub_rn(mc1, M));
-            __syncwarp();
-            if (lane == 0) {
-                float Ls = 0.0f;
-                for (int cc = 0; cc < C; ++cc)
-                    Ls = __fmaf_rn(wts[warp * ATT_MAX_CHUNKS + cc], __ldcg(ph + cc * ATT_PART_STRIDE + 1), Ls);
-                stat[16 + warp] = __fdiv_rn(1.0f, Ls);
+            const float w0 = lane < C ? canon_expf(__fsub_rn(mc0, M)) : 0.0f;
+            const float w1 = lane + 32 < C ? canon_expf(__fsub_rn(mc1, M)) : 0.0f;
+            if (lane < C) wts[warp * ATT_MAX_CHUNKS + lane] = w0;
+            if (lane + 32 < C) wts[warp * ATT_MAX_CHUNKS + lane + 32] = w1;
+            float Ls = 0.0f;   // chunk-ordered fma chain, operands gathered by shuffles
+            for (int cc = 0; cc < C; ++cc) {
+                const float wv = __shfl_sync(0xffffffffu, cc < 32 ? w0 : w1, cc & 31);
+                const float lv = __shfl_sync(0xffffffffu, cc < 32 ? lc0 : lc1, cc & 31);
+                Ls = __fmaf_rn(wv, lv, Ls);
             }
+            if (lane == 0) stat[16 + warp] = __fdiv_rn(1.0f, Ls);
         }
         __syncthreads();
         for (int o = tid; o < 8 * HEAD_DIM; o += blockDim.x) {
             const int h = o >> 7, d = o & 127;
             const float* ph = p.att_part + static_cast<size_t>(8 * g + h) * ATT_MAX_CHUNKS * ATT_PART_STRIDE;
             float O = 0.0f;
+#pragma unroll 8
             for (int cc = 0; cc < C; ++cc)
                 O = __fmaf_rn(wts[h * ATT_MAX_CHUNKS + cc], __ldcg(ph + cc * ATT_PART_STRIDE + 2 + d), O);
             const float out = __fmul_rn(O, stat[16 + h]);
@@ -450,6 +505,7 @@ __device__ void phase_attention(const DecodeParams& p, const Smem& s, int l, int
             quant_block_warp<false>(y, reinterpret_cast<int8_t*>(blk + 4), reinterpret_cast<float*>(blk),
                                     reinterpret_cast<int16_t*>(blk + 260));
         }
+        trace_step(p, l, 1, 3);
     }
 }
 
@@ -470,34 +526,95 @@ __device__ void load_q8k_blocks(const uint8_t* src, int nblocks, const Smem& s) 
     __syncthreads();
 }
 
+// Every CTA combines the attention chunks of all 16 heads (same operations and order as
+// the last-CTA combine) and quantises the result ties-to-even straight into s.xq.
+__device__ void combine_attention(const DecodeParams& p, const Smem& s, int cta) {
+    const int n = p.pos + 1, C = attn_chunks(n);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float* wts = s.rowval;   // [16][16]
+    float* invl = s.red;     // [16]
+    float* ab = s.xs;        // [2048]
+    if (warp < N_HEAD) {
+        const float* ph = p.att_part + static_cast<size_t>(warp) * ATT_MAX_CHUNKS * ATT_PART_STRIDE;
+        const float mc = lane < C ? __ldcg(ph + lane * ATT_PART_STRIDE) : 0.0f;
+        const float lc = lane < C ? __ldcg(ph + lane * ATT_PART_STRIDE + 1) : 0.0f;
+        float M = lane < C ? mc : -__int_as_float(0x7f800000);
+        for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        const float wv = lane < C ? canon_expf(__fsub_rn(mc, M)) : 0.0f;
+        if (lane < C) wts[warp * 16 + lane] = wv;
+        float Ls = 0.0f;
+        for (int cc = 0; cc < C; ++cc)
+            Ls = __fmaf_rn(__shfl_sync(0xffffffffu, wv, cc), __shfl_sync(0xffffffffu, lc, cc), Ls);
+        if (lane == 0) invl[warp] = __fdiv_rn(1.0f, Ls);
+    }
+    // outputs o = tid + 512 i; h = o >> 7, d = o & 127: load all chunk partials first
+    float v[4][DIST_COMBINE_MAX];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int o = tid + 512 * i, h = o >> 7, d = o & 127;
+        const float* ph = p.att_part + static_cast<size_t>(h) * ATT_MAX_CHUNKS * ATT_PART_STRIDE + 2 + d;
+#pragma unroll
+        for (int cc = 0; cc < DIST_COMBINE_MAX; ++cc) v[i][cc] = cc < C ? __ldcg(ph + cc * ATT_PART_STRIDE) : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int o = tid + 512 * i, h = o >> 7;
+        float O = 0.0f;
+#pragma unroll
+        for (int cc = 0; cc < DIST_COMBINE_MAX; ++cc)
+            if (cc < C) O = __fmaf_rn(wts[h * 16 + cc], v[i][cc], O);
+        const float out = __fmul_rn(O, invl[h]);
+        ab[o] = out;
+        if (cta == 0) p.att[o] = out;
+    }
+    __syncthreads();
+    if (warp < N_EMBD / 256) {
+        float y[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) y[k] = ab[256 * warp + 8 * lane + k];
+        quant_block_warp<false>(y, s.xq->qs[warp], &s.xq->d[warp], s.xq->bsums[warp]);
+    }
+    __syncthreads();
+}
+
 __device__ void phase_o(const DecodeParams& p, const Smem& s, int l, int cta, int ncta) {
     const LayerDev& L = p.layers[l];
-    load_q8k_blocks(p.att_q8k, N_EMBD / 256, s);
-    if (!wait_weights(p, s, 4 * l + 1)) return;
     const PhaseLayout pl = phase_layout(L, 1, cta, ncta);
-    float* x = p.x;
-    const int r0 = pl.row0[0];
-    gemv_staged(L.to, s.wbuf[1], pl.nrows[0], N_EMBD / 256, *s.xq, s.part, MAX_TASKS,
-                [&](int r, float v) { x[r0 + r] = __fadd_rn(__ldcg(x + r0 + r), v); });
+    const int r0 = pl.row0[0], n = pl.nrows[0];
+    const float xr = threadIdx.x < n ? __ldcg(p.x + r0 + threadIdx.x) : 0.0f;   // residual rows, early
+    if (attn_chunks(p.pos + 1) <= DIST_COMBINE_MAX)
+        combine_attention(p, s, cta);
+    else
+        load_q8k_blocks(p.att_q8k, N_EMBD / 256, s);
+    trace_step(p, l, 2, 1);
+    if (!wait_weights(p, s, 4 * l + 1)) return;
+    trace_step(p, l, 2, 2);
+    gemv_rows(L.to, s.wbuf[1], n, N_EMBD / 256, *s.xq, s.part, MAX_TASKS, s.rowval);
+    if (threadIdx.x < n) p.x[r0 + threadIdx.x] = __fadd_rn(xr, s.rowval[threadIdx.x]);
 }
 
 __device__ void phase_gu(const DecodeParams& p, const Smem& s, int l, int cta, int ncta) {
     const LayerDev& L = p.layers[l];
-    load_global_vec(p.x, s.xs, N_EMBD);
-    norm_quant<true>(s.xs, L.ffn_norm, s);
+    norm_quant<true, false>(p.x, L.ffn_norm, s);
+    trace_step(p, l, 3, 1);
     if (!wait_weights(p, s, 4 * l + 2)) return;
+    trace_step(p, l, 3, 2);
     const PhaseLayout pl = phase_layout(L, 2, cta, ncta);
     const int n = pl.nrows[0];
     float* rv = s.rowval;
-    gemv_staged(L.tg, s.wbuf[0] + pl.off[0], n, N_EMBD / 256, *s.xq, s.part, MAX_TASKS,
-                [&](int r, float v) { rv[r] = v; });
-    gemv_staged(L.tu, s.wbuf[0] + pl.off[1], n, N_EMBD / 256, *s.xq, s.part, MAX_TASKS,
-                [&](int r, float v) { rv[128 + r] = v; });
+    gemv_rows(L.tg, s.wbuf[0] + pl.off[0], n, N_EMBD / 256, *s.xq, s.part, MAX_TASKS, rv);
+    trace_step(p, l, 3, 3);
+    gemv_rows(L.tu, s.wbuf[0] + pl.off[1], n, N_EMBD / 256, *s.xq, s.part, MAX_TASKS, rv + 128);
+    trace_step(p, l, 3, 4);
     for (int r = threadIdx.x; r < n; r += blockDim.x) p.h[pl.row0[0] + r] = canon_silu_mul(rv[r], rv[128 + r]);
 }
 
 __device__ void phase_down(const DecodeParams& p, const Smem& s, int l, int cta, int ncta) {
     const LayerDev& L = p.layers[l];
+    const PhaseLayout pl = phase_layout(L, 3, cta, ncta);
+    const int r0 = pl.row0[0], n = pl.nrows[0];
+    const float xr = threadIdx.x < n ? __ldcg(p.x + r0 + threadIdx.x) : 0.0f;   // residual rows, early
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int b = warp; b < N_FF / 256; b += blockDim.x >> 5) {   // Q8_K of h straight from L2
         const float4 a = __ldcg(reinterpret_cast<const float4*>(p.h + 256 * b + 8 * lane));
@@ -506,20 +623,17 @@ __device__ void phase_down(const DecodeParams& p, const Smem& s, int l, int cta,
         quant_block_warp<true>(y, s.xq->qs[b], &s.xq->d[b], s.xq->bsums[b]);
     }
     __syncthreads();
+    trace_step(p, l, 4, 1);
     if (!wait_weights(p, s, 4 * l + 3)) return;
-    const PhaseLayout pl = phase_layout(L, 3, cta, ncta);
-    float* x = p.x;
-    const int r0 = pl.row0[0];
-    gemv_staged(L.td, s.wbuf[1], pl.nrows[0], N_FF / 256, *s.xq, s.part, MAX_TASKS,
-                [&](int r, float v) { x[r0 + r] = __fadd_rn(__ldcg(x + r0 + r), v); });
+    trace_step(p, l, 4, 2);
+    gemv_rows(L.td, s.wbuf[1], n, N_FF / 256, *s.xq, s.part, MAX_TASKS, s.rowval);
+    if (threadIdx.x < n) p.x[r0 + threadIdx.x] = __fadd_rn(xr, s.rowval[threadIdx.x]);
 }
 
 __device__ void phase_lm(const DecodeParams& p, const Smem& s, int cta, int ncta) {
     const LmPlan q = lm_plan(p, cta, ncta);
-    if (threadIdx.x == 0)
-        for (int st = 2; st < 4; ++st) issue_lm_stage(p, s, q, st);
-    load_global_vec(p.x, s.xs, N_EMBD);
-    norm_quant<false>(s.xs, p.out_norm, s);   // rmsnorm (ops.cpp:468-481) + quantize_row_q8_K_avx2
+    norm_quant<false, false>(p.x, p.out_norm, s);
+    trace_step(p, 1, 5, 1);   // rmsnorm (ops.cpp:468-481) + quantize_row_q8_K_avx2
     float best = -__int_as_float(0x7f800000);
     int besti = 0x7fffffff;
     int nan0 = 0;
@@ -530,14 +644,18 @@ __device__ void phase_lm(const DecodeParams& p, const Smem& s, int cta, int ncta
         const int a = q.r0 + st * q.sr, n = min(q.sr, q.r1 - a);
         float* lg = p.logits;
         const int wl = p.write_logits;
-        gemv_staged(p.lm_type, lm_slot(s, slot), n, q.nb, *s.xq, s.part, MAX_TASKS, [&](int r, float v) {
-            const int row = a + r;
+        gemv_rows(p.lm_type, lm_slot(s, slot), n, q.nb, *s.xq, s.part, MAX_TASKS, s.rowval);
+        if (threadIdx.x < n) {
+            const int row = a + threadIdx.x;
+            const float v = s.rowval[threadIdx.x];
             if (wl) lg[row] = v;
             if (row == 0 && v != v) nan0 = 1;
             if (v > best || (v == best && row < besti)) best = v, besti = row;
-        });
+        }
         if (threadIdx.x == 0 && st + 4 < q.nstages) issue_lm_stage(p, s, q, st + 4);
+        if (st < 4) trace_step(p, 1, 5, 2 + st);
     }
+    trace_step(p, 1, 5, 6);
     // CTA argmax (lowest index on ties; NaN never wins; a NaN logit 0 forces 0 like the
     // reference's `if (lg[i] > lg[best])` scan)
     float* red = s.red;
@@ -613,47 +731,57 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
         if (threadIdx.x == 0) atomicOr(p.err, ERR_BAD_TOKEN);
         return;
     }
+    BarState bs;
+    bs.base = *reinterpret_cast<volatile unsigned*>(p.bar + 1);
+    bs.idx = 0;
     if (threadIdx.x == 0) {
         for (int i = 0; i < 8; ++i) mbar_init(&s.wbar[i], 1);
         for (int i = 0; i < 4; ++i) mbar_init(&s.lmbar[i], 1);
         fence_mbar_init();
         issue_weight_phase(p, s, 0, cta, ncta);
-        issue_weight_phase(p, s, 1, cta, ncta);
+        prefetch_attention(p, 0, cta);
     }
     __syncthreads();
     trace_mark(p, 0);
     const LmPlan lmq = lm_plan(p, cta, ncta);
+    // Weight phase w+1 is issued while waiting at the barrier in front of phase w: its
+    // buffer was last used by phase w-1, which every thread of this CTA has finished.
     for (int l = 0; l < p.n_layer; ++l) {
-        // weight phase 4l (QKV) is in flight since the previous D phase / kernel start
-        if (l > 0 && threadIdx.x == 0) issue_weight_phase(p, s, 4 * l + 1, cta, ncta);
         phase_qkv(p, s, l, token, cta, ncta);
-        if (!traced_barrier(p, 5 * l)) return;
-        phase_attention(p, s, l, cta, ncta);
-        if (!traced_barrier(p, 5 * l + 1)) return;
-        if (threadIdx.x == 0) issue_weight_phase(p, s, 4 * l + 2, cta, ncta);
+        if (!traced_barrier(p, bs, 5 * l, [&] { issue_weight_phase(p, s, 4 * l + 1, cta, ncta); })) return;
+        phase_attention(p, s, l, cta, ncta, attn_chunks(p.pos + 1) > DIST_COMBINE_MAX);
+        if (!traced_barrier(p, bs, 5 * l + 1, [&] { issue_weight_phase(p, s, 4 * l + 2, cta, ncta); })) return;
         phase_o(p, s, l, cta, ncta);
-        if (!traced_barrier(p, 5 * l + 2)) return;
-        if (threadIdx.x == 0) issue_weight_phase(p, s, 4 * l + 3, cta, ncta);
+        if (!traced_barrier(p, bs, 5 * l + 2, [&] { issue_weight_phase(p, s, 4 * l + 3, cta, ncta); })) return;
         phase_gu(p, s, l, cta, ncta);
-        if (!traced_barrier(p, 5 * l + 3)) return;
-        if (threadIdx.x == 0) {
-            if (l + 1 < p.n_layer) {
-                issue_weight_phase(p, s, 4 * (l + 1), cta, ncta);
-            } else {
-                issue_lm_stage(p, s, lmq, 0);
-                issue_lm_stage(p, s, lmq, 1);
-            }
-        }
+        if (!traced_barrier(p, bs, 5 * l + 3, [&] {
+                if (l + 1 < p.n_layer) {
+                    issue_weight_phase(p, s, 4 * (l + 1), cta, ncta);
+                } else {
+                    issue_lm_stage(p, s, lmq, 0);
+                    issue_lm_stage(p, s, lmq, 1);
+                }
+            }))
+            return;
         phase_down(p, s, l, cta, ncta);
-        if (!traced_barrier(p, 5 * l + 4)) return;
+        if (!traced_barrier(p, bs, 5 * l + 4, [&] {
+                if (l + 1 == p.n_layer) {
+                    issue_lm_stage(p, s, lmq, 2);
+                    issue_lm_stage(p, s, lmq, 3);
+                } else {
+                    prefetch_attention(p, l + 1, cta);
+                }
+            }))
+            return;
     }
+    if (cta == 0 && threadIdx.x == 0) p.bar[1] = bs.base + bs.idx * gridDim.x;   // next launch's base
     phase_lm(p, s, cta, ncta);
     trace_mark(p, 2 + 2 * (5 * p.n_layer));
 }
 
 // ---- standalone attention op (execute_attention, ops.cpp:537-628): K/V append at pos,
 // then the same split-KV chunks and combine as the decode kernel's attention phase.
-constexpr int ATT_SMEM_FLOATS = 8 * HEAD_DIM + 32 * HEAD_DIM + 8 * ATT_SC_STRIDE + 32 + 8 * ATT_MAX_CHUNKS + 8 * HEAD_DIM;
+constexpr int ATT_SMEM_FLOATS = 8 * HEAD_DIM + 64 * HEAD_DIM + 8 * ATT_SC_STRIDE + 32 + 8 * ATT_MAX_CHUNKS + 8 * HEAD_DIM;
 
 __global__ void k_kv_append(const float* __restrict__ k, const float* __restrict__ v, float* kc, float* vc, int pos) {
     const int i = threadIdx.x;
@@ -668,7 +796,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_attention(const DecodeParams
     Smem s{};
     s.wbuf[0] = smem_raw;
     s.flag = reinterpret_cast<int*>(smem_raw + ATT_SMEM_FLOATS * 4);
-    phase_attention(p, s, 0, blockIdx.x, gridDim.x);
+    phase_attention(p, s, 0, blockIdx.x, gridDim.x, true);
 }
 
 }  // namespace
@@ -714,6 +842,15 @@ cudaError_t launch_attention(const float* q, const float* k, const float* v, flo
     p.att_q8k = out_q8k;
     p.att_part = part;
     p.cnt = cnt;
+    static int prepared_dev = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (prepared_dev != dev) {
+        const cudaError_t e = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   ATT_SMEM_FLOATS * 4 + 16);
+        if (e != cudaSuccess) return e;
+        prepared_dev = dev;
+    }
     const int n = pos + 1, P = 32 * ((n + 2047) / 2048), C = (n + P - 1) / P;
     k_attention<<<2 * C, DEC_THREADS, ATT_SMEM_FLOATS * 4 + 16, stream>>>(p);
     return cudaGetLastError();

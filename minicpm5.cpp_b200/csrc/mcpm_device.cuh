@@ -79,6 +79,9 @@ __device__ __forceinline__ uint32_t ld_acquire_u32(const unsigned* p) {
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+__device__ __forceinline__ void red_release_add_u32(unsigned* p, uint32_t v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ void st_release_u32(unsigned* p, uint32_t v) {
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -357,25 +360,26 @@ __device__ __forceinline__ void block_scales(int type, const uint8_t* blk, float
 }
 
 // ---------------------------------------------------------------- GEMV over staged rows
-// Rows [0, R) of one matrix (type, nb super-blocks per row) are staged contiguously in
-// shared memory at `w`.  Pass 1: every (row, block) task's integer partials go to
-// `part` (9 ints per task).  Pass 2: lane k of a row group runs the reference's fp32
-// accumulator chain for AVX2 lane k over the blocks, the eight lanes are reduced with
-// hsum_f32_8's tree (a butterfly over lane bits 2, 1, 0) and the Q4_K min term is added.
-// The row value is handed to `epi(row, value)` by lane 0 of each row group.
+// Rows [0, R) of one matrix (type, NB super-blocks per row) are staged contiguously in
+// shared memory at `w`.  Pass 1: every (row, block) task's integer partials, split into
+// the eight AVX2 lanes, go to `part` (9 ints per task), one task per thread.  Pass 2:
+// lane k of a row group runs the reference's fp32 accumulator chain for AVX2 lane k over
+// the blocks, the eight lanes are reduced with hsum_f32_8's tree (a butterfly over lane
+// bits 2, 1, 0) and the Q4_K min term is added.  Row r's value goes to out[r] (shared
+// memory), visible to every thread on return.  Not inlined: one copy serves every phase.
 // Must be called by all threads of the CTA (contains __syncthreads).
 constexpr int PART_WORDS = 9;
 
-template <typename Epi>
-__device__ __forceinline__ void gemv_staged(int type, const uint8_t* w, int R, int nb, const XQSmem& xq, int* part,
-                                            int max_tasks, Epi epi) {
+template <int NB>
+__device__ __noinline__ void gemv_rows_t(int type, const uint8_t* w, int R, const XQSmem& xq, int* part,
+                                         int max_tasks, float* out) {
     const int tid = threadIdx.x, nthr = blockDim.x;
     const int rb = block_bytes(type);
-    const int mt = (max_tasks / nb) * nb;   // whole rows per chunk
-    for (int t0 = 0; t0 < R * nb; t0 += mt) {
-        const int ntask = min(mt, R * nb - t0);
+    const int mt = (max_tasks / NB) * NB;   // whole rows per chunk
+    for (int t0 = 0; t0 < R * NB; t0 += mt) {
+        const int ntask = min(mt, R * NB - t0);
         for (int t = tid; t < ntask; t += nthr) {
-            const int task = t0 + t, b = task % nb;
+            const int task = t0 + t, b = task % NB;
             const uint8_t* blk = w + static_cast<size_t>(task) * rb;
             Partials p;
             if (type == GGML_Q4_K)
@@ -389,15 +393,16 @@ __device__ __forceinline__ void gemv_staged(int type, const uint8_t* w, int R, i
         }
         __syncthreads();
         // pass 2: one 8-lane group per row; trip count uniform per warp for the shuffles
-        const int r_begin = t0 / nb, total = (ntask / nb) * 8;
+        const int r_begin = t0 / NB, total = (ntask / NB) * 8;
         for (int base = tid & ~31; base < total; base += nthr) {
             const int g = base + (tid & 31);
             const bool valid = g < total;
-            const int r = r_begin + (g >> 3), k = g & 7;
+            const int r = r_begin + (valid ? (g >> 3) : 0), k = g & 7;
             float acc = 0.0f, acc_min = 0.0f;
             if (valid) {
-                for (int b = 0; b < nb; ++b) {
-                    const int task = r * nb + b;
+#pragma unroll
+                for (int b = 0; b < NB; ++b) {
+                    const int task = r * NB + b;
                     float d, dmin;
                     block_scales(type, w + static_cast<size_t>(task) * rb, d, dmin);
                     const float xd = xq.d[b];
@@ -407,14 +412,22 @@ __device__ __forceinline__ void gemv_staged(int type, const uint8_t* w, int R, i
                         acc_min = __fmaf_rn(-__fmul_rn(xd, dmin), __int2float_rn(src[8]), acc_min);
                 }
             }
-            // hsum_f32_8: t_i = a_i + a_{i+4}; u = (t0+t2, t1+t3); r = u0 + u1
             acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 4));
             acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 2));
             acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
-            if (valid && k == 0) epi(r, type == GGML_Q4_K ? __fadd_rn(acc, acc_min) : acc);
+            if (valid && k == 0) out[r] = type == GGML_Q4_K ? __fadd_rn(acc, acc_min) : acc;
         }
         __syncthreads();
     }
+}
+
+// Dispatch on the row length (8 or 24 super-blocks).
+static __device__ __forceinline__ void gemv_rows(int type, const uint8_t* w, int R, int nb, const XQSmem& xq, int* part,
+                                                 int max_tasks, float* out) {
+    if (nb == 8)
+        gemv_rows_t<8>(type, w, R, xq, part, max_tasks, out);
+    else
+        gemv_rows_t<24>(type, w, R, xq, part, max_tasks, out);
 }
 
 }  // namespace mcpm

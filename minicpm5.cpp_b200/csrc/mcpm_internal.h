@@ -23,7 +23,8 @@ constexpr int ATT_MAX_CHUNKS = 64;         // attention chunks per head (chunk =
 constexpr int ATT_PART_STRIDE = 2 + HEAD_DIM;
 constexpr int ATT_SC_STRIDE = 256;         // chunk-length bound: 32*ceil(MAX_SEQ/2048)
 constexpr int MAX_SEQ = 16384;
-constexpr int TRACE_WORDS = 2 + 2 * (5 * MAX_LAYERS + 1);
+constexpr int TRACE_WORDS = 720;          // 2 + 2*(5*layers+1) phase marks, then detail marks from 650
+constexpr int TRACE_DETAIL = 650;         // sub-step marks of layer 1: 650 + 10*phase + step
 
 struct LayerDev {
     const uint8_t *wq, *wk, *wv, *wo, *wg, *wu, *wd;

@@ -73,7 +73,8 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
     uint8_t* ring = smem_raw;
     XQSmem* xq = reinterpret_cast<XQSmem*>(ring + RING_SLOTS * SLOT_STRIDE);
     int* part = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(xq) + ((sizeof(XQSmem) + 127) & ~size_t(127)));
-    uint64_t* bars = reinterpret_cast<uint64_t*>(part + MAX_TASKS * PART_WORDS);
+    float* rowval = reinterpret_cast<float*>(part + MAX_TASKS * PART_WORDS);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(rowval + MAX_TASKS);
 
     const int tid = threadIdx.x;
     const int rb = row_bytes(type, nb * 256);
@@ -127,7 +128,8 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
             }
             __syncthreads();
         } else {
-            gemv_staged(type, sw, n, nb, *xq, part, MAX_TASKS, [&](int r, float v) { y[a + r] = v; });
+            gemv_rows(type, sw, n, nb, *xq, part, MAX_TASKS, rowval);
+            if (tid < n) y[a + tid] = rowval[tid];
         }
         if (tid == 0 && st + RING_SLOTS < nstages) issue(st + RING_SLOTS);
     }
@@ -135,7 +137,7 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
 
 size_t gemv_smem_bytes() {
     return RING_SLOTS * SLOT_STRIDE + ((sizeof(XQSmem) + 127) & ~size_t(127)) + MAX_TASKS * PART_WORDS * 4 +
-           RING_SLOTS * 8;
+           MAX_TASKS * 4 + RING_SLOTS * 8;
 }
 
 int g_num_sms = 0;
