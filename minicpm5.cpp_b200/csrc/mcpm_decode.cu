@@ -129,9 +129,9 @@ __device__ LmPlan lm_plan(const DecodeParams& p, int cta, int ncta) {
     q.nstages = (q.r1 - q.r0 + q.sr - 1) / q.sr;
     return q;
 }
-__device__ uint8_t* lm_slot(const Smem& s, int slot) { return s.wbuf[slot >> 1] + (slot & 1) * LM_SLOT_BYTES; }
+__device__ uint8_t* lm_slot(const Smem& s, int slot) { return s.wbuf[slot]; }
 __device__ void issue_lm_stage(const DecodeParams& p, const Smem& s, const LmPlan& q, int st) {
-    const int slot = st & 3;
+    const int slot = st & 1;
     const int a = q.r0 + st * q.sr, n = min(q.sr, q.r1 - a);
     const uint32_t bytes = n > 0 ? static_cast<uint32_t>(n) * q.rb : 0;
     mbar_expect_tx(&s.lmbar[slot], bytes);
@@ -199,6 +199,13 @@ __device__ void prefetch_attention(const DecodeParams& p, int l, int cta) {
     const uint32_t bytes = static_cast<uint32_t>(t1 - t0) * KV_DIM * 4;
     bulk_prefetch_l2(p.kc + off, bytes);
     bulk_prefetch_l2(p.vc + off, bytes);
+}
+
+// L2 prefetch of layer l's two norm weight vectors (8 KB each), by CTA 0 only.
+__device__ void prefetch_norms(const DecodeParams& p, int l, int cta) {
+    if (cta != 0) return;
+    bulk_prefetch_l2(p.layers[l].attn_norm, N_EMBD * 4);
+    bulk_prefetch_l2(p.layers[l].ffn_norm, N_EMBD * 4);
 }
 
 // Waits for this CTA's part of weight phase wp; false on timeout.
@@ -534,6 +541,15 @@ __device__ void combine_attention(const DecodeParams& p, const Smem& s, int cta)
     float* wts = s.rowval;   // [16][16]
     float* invl = s.red;     // [16]
     float* ab = s.xs;        // [2048]
+    // outputs o = tid + 512 i; h = o >> 7, d = o & 127: issue every chunk-partial load first
+    float v[4][DIST_COMBINE_MAX];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int o = tid + 512 * i, h = o >> 7, d = o & 127;
+        const float* ph = p.att_part + static_cast<size_t>(h) * ATT_MAX_CHUNKS * ATT_PART_STRIDE + 2 + d;
+#pragma unroll
+        for (int cc = 0; cc < DIST_COMBINE_MAX; ++cc) v[i][cc] = cc < C ? __ldcg(ph + cc * ATT_PART_STRIDE) : 0.0f;
+    }
     if (warp < N_HEAD) {
         const float* ph = p.att_part + static_cast<size_t>(warp) * ATT_MAX_CHUNKS * ATT_PART_STRIDE;
         const float mc = lane < C ? __ldcg(ph + lane * ATT_PART_STRIDE) : 0.0f;
@@ -546,15 +562,6 @@ __device__ void combine_attention(const DecodeParams& p, const Smem& s, int cta)
         for (int cc = 0; cc < C; ++cc)
             Ls = __fmaf_rn(__shfl_sync(0xffffffffu, wv, cc), __shfl_sync(0xffffffffu, lc, cc), Ls);
         if (lane == 0) invl[warp] = __fdiv_rn(1.0f, Ls);
-    }
-    // outputs o = tid + 512 i; h = o >> 7, d = o & 127: load all chunk partials first
-    float v[4][DIST_COMBINE_MAX];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int o = tid + 512 * i, h = o >> 7, d = o & 127;
-        const float* ph = p.att_part + static_cast<size_t>(h) * ATT_MAX_CHUNKS * ATT_PART_STRIDE + 2 + d;
-#pragma unroll
-        for (int cc = 0; cc < DIST_COMBINE_MAX; ++cc) v[i][cc] = cc < C ? __ldcg(ph + cc * ATT_PART_STRIDE) : 0.0f;
     }
     __syncthreads();
 #pragma unroll
@@ -590,7 +597,8 @@ __device__ void phase_o(const DecodeParams& p, const Smem& s, int l, int cta, in
     trace_step(p, l, 2, 1);
     if (!wait_weights(p, s, 4 * l + 1)) return;
     trace_step(p, l, 2, 2);
-    gemv_rows(L.to, s.wbuf[1], n, N_EMBD / 256, *s.xq, s.part, MAX_TASKS, s.rowval);
+    gemv_rows(L.to, s.wbuf[1], n, N_EMBD / 256, *s.xq, s.part, MAX_TASKS, s.rowval,
+              (p.trace && l == 1 && cta == 0) ? p.trace + TRACE_DETAIL + 60 : nullptr);
     if (threadIdx.x < n) p.x[r0 + threadIdx.x] = __fadd_rn(xr, s.rowval[threadIdx.x]);
 }
 
@@ -626,7 +634,8 @@ __device__ void phase_down(const DecodeParams& p, const Smem& s, int l, int cta,
     trace_step(p, l, 4, 1);
     if (!wait_weights(p, s, 4 * l + 3)) return;
     trace_step(p, l, 4, 2);
-    gemv_rows(L.td, s.wbuf[1], n, N_FF / 256, *s.xq, s.part, MAX_TASKS, s.rowval);
+    gemv_rows(L.td, s.wbuf[1], n, N_FF / 256, *s.xq, s.part, MAX_TASKS, s.rowval,
+              (p.trace && l == 1 && cta == 0) ? p.trace + TRACE_DETAIL + 62 : nullptr);
     if (threadIdx.x < n) p.x[r0 + threadIdx.x] = __fadd_rn(xr, s.rowval[threadIdx.x]);
 }
 
@@ -638,8 +647,8 @@ __device__ void phase_lm(const DecodeParams& p, const Smem& s, int cta, int ncta
     int besti = 0x7fffffff;
     int nan0 = 0;
     for (int st = 0; st < q.nstages; ++st) {
-        const int slot = st & 3;
-        const bool ok = mbar_wait(&s.lmbar[slot], (st >> 2) & 1, p.err);
+        const int slot = st & 1;
+        const bool ok = mbar_wait(&s.lmbar[slot], (st >> 1) & 1, p.err);
         if (__syncthreads_or(!ok)) return;
         const int a = q.r0 + st * q.sr, n = min(q.sr, q.r1 - a);
         float* lg = p.logits;
@@ -652,7 +661,7 @@ __device__ void phase_lm(const DecodeParams& p, const Smem& s, int cta, int ncta
             if (row == 0 && v != v) nan0 = 1;
             if (v > best || (v == best && row < besti)) best = v, besti = row;
         }
-        if (threadIdx.x == 0 && st + 4 < q.nstages) issue_lm_stage(p, s, q, st + 4);
+        if (threadIdx.x == 0 && st + 2 < q.nstages) issue_lm_stage(p, s, q, st + 2);
         if (st < 4) trace_step(p, 1, 5, 2 + st);
     }
     trace_step(p, 1, 5, 6);
@@ -740,6 +749,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
         fence_mbar_init();
         issue_weight_phase(p, s, 0, cta, ncta);
         prefetch_attention(p, 0, cta);
+        prefetch_norms(p, 0, cta);
     }
     __syncthreads();
     trace_mark(p, 0);
@@ -759,17 +769,17 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
                     issue_weight_phase(p, s, 4 * (l + 1), cta, ncta);
                 } else {
                     issue_lm_stage(p, s, lmq, 0);
-                    issue_lm_stage(p, s, lmq, 1);
+                    if (cta == 0) bulk_prefetch_l2(p.out_norm, N_EMBD * 4);
                 }
             }))
             return;
         phase_down(p, s, l, cta, ncta);
         if (!traced_barrier(p, bs, 5 * l + 4, [&] {
                 if (l + 1 == p.n_layer) {
-                    issue_lm_stage(p, s, lmq, 2);
-                    issue_lm_stage(p, s, lmq, 3);
+                    issue_lm_stage(p, s, lmq, 1);
                 } else {
                     prefetch_attention(p, l + 1, cta);
+                    prefetch_norms(p, l + 1, cta);
                 }
             }))
             return;

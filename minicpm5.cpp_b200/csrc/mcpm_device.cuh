@@ -372,7 +372,7 @@ constexpr int PART_WORDS = 9;
 
 template <int NB>
 __device__ __noinline__ void gemv_rows_t(int type, const uint8_t* w, int R, const XQSmem& xq, int* part,
-                                         int max_tasks, float* out) {
+                                         int max_tasks, float* out, unsigned long long* tr) {
     const int tid = threadIdx.x, nthr = blockDim.x;
     const int rb = block_bytes(type);
     const int mt = (max_tasks / NB) * NB;   // whole rows per chunk
@@ -392,6 +392,7 @@ __device__ __noinline__ void gemv_rows_t(int type, const uint8_t* w, int R, cons
             dst[8] = p.minsum;
         }
         __syncthreads();
+        if (tr && tid == 0) tr[0] = globaltimer();
         // pass 2: one 8-lane group per row; trip count uniform per warp for the shuffles
         const int r_begin = t0 / NB, total = (ntask / NB) * 8;
         for (int base = tid & ~31; base < total; base += nthr) {
@@ -418,16 +419,18 @@ __device__ __noinline__ void gemv_rows_t(int type, const uint8_t* w, int R, cons
             if (valid && k == 0) out[r] = type == GGML_Q4_K ? __fadd_rn(acc, acc_min) : acc;
         }
         __syncthreads();
+        if (tr && tid == 0) tr[1] = globaltimer();
     }
 }
 
 // Dispatch on the row length (8 or 24 super-blocks).
+// `tr` (optional): thread 0 stores globaltimer after pass 1 (tr[0]) and pass 2 (tr[1]).
 static __device__ __forceinline__ void gemv_rows(int type, const uint8_t* w, int R, int nb, const XQSmem& xq, int* part,
-                                                 int max_tasks, float* out) {
+                                                 int max_tasks, float* out, unsigned long long* tr = nullptr) {
     if (nb == 8)
-        gemv_rows_t<8>(type, w, R, xq, part, max_tasks, out);
+        gemv_rows_t<8>(type, w, R, xq, part, max_tasks, out, tr);
     else
-        gemv_rows_t<24>(type, w, R, xq, part, max_tasks, out);
+        gemv_rows_t<24>(type, w, R, xq, part, max_tasks, out, tr);
 }
 
 }  // namespace mcpm

@@ -16,9 +16,9 @@ constexpr int MAX_LAYERS = 64;
 constexpr int DEC_THREADS = 512;
 constexpr int WBUF_BYTES = 98304;          // one weight buffer (two per CTA)
 constexpr int WBUF_SLACK = 128;            // readable tail after each buffer (unaligned Q6_K reads)
-constexpr int MAX_TASKS = 384;             // (row, super-block) tasks per GEMV pass
+constexpr int MAX_TASKS = 512;             // (row, super-block) tasks per GEMV pass
 constexpr int ROWVAL_FLOATS = 256;
-constexpr int LM_SLOT_BYTES = WBUF_BYTES / 2;
+constexpr int LM_SLOT_BYTES = WBUF_BYTES;   // LM head: one stage per weight buffer
 constexpr int ATT_MAX_CHUNKS = 64;         // attention chunks per head (chunk = 32*ceil(n/2048))
 constexpr int ATT_PART_STRIDE = 2 + HEAD_DIM;
 constexpr int ATT_SC_STRIDE = 256;         // chunk-length bound: 32*ceil(MAX_SEQ/2048)
