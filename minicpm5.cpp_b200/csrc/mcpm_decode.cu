@@ -22,11 +22,14 @@
 namespace mcpm {
 namespace {
 
+// GEMV partials and the staged fp32 activation share one scratch region.
+constexpr int SCRATCH_BYTES = MAX_TASKS * PART_WORDS * 4 > N_EMBD * 4 ? MAX_TASKS * PART_WORDS * 4 : N_EMBD * 4;
+
 struct Smem {
     uint8_t* wbuf[2];
     XQSmem* xq;
     int* part;
-    float* xs;       // staged fp32 activation vector (N_EMBD)
+    float* xs;       // staged fp32 activation vector (N_EMBD); same storage as part
     float* rowval;
     float* red;      // 32 floats
     uint64_t* wbar;  // [2][4]
@@ -143,6 +146,10 @@ __device__ void issue_lm_stage(const DecodeParams& p, const Smem& s, const LmPla
 // the last arrival costs one fire-and-forget release-add and the waiters one acquire poll.
 // `base` (bar[1]) is advanced by CTA 0 after the launch's last barrier; the host zeroes both
 // words after an error.  While waiting, thread 0 runs `during` (issues the next TMA copies).
+// Only thread 0 touches global memory here: its acquire plus the closing bar.red order the
+// other CTAs' writes before every thread's later reads.  The error word is read relaxed,
+// in the shadow of the poll; an error raised during this wait is seen at the next barrier
+// (or by the bounded waits).
 struct BarState {
     unsigned base;
     unsigned idx;
@@ -151,8 +158,10 @@ struct BarState {
 template <typename F>
 __device__ bool grid_barrier(const DecodeParams& p, BarState& bs, F&& during) {
     __syncthreads();
+    int bad = 0;
     if (threadIdx.x == 0) {
         red_release_add_u32(p.bar, 1u);
+        const unsigned e = ld_relaxed_u32(p.err);
         during();
         const unsigned target = bs.base + (bs.idx + 1) * gridDim.x;
         if (static_cast<int>(ld_acquire_u32(p.bar) - target) < 0) {
@@ -160,14 +169,15 @@ __device__ bool grid_barrier(const DecodeParams& p, BarState& bs, F&& during) {
             while (static_cast<int>(ld_acquire_u32(p.bar) - target) < 0) {
                 if (globaltimer() - t0 > 1000000000ull) {
                     atomicOr(p.err, ERR_TIMEOUT);
+                    bad = 1;
                     break;
                 }
             }
         }
+        bad |= e != 0;
     }
     ++bs.idx;
-    __syncthreads();
-    return ld_acquire_u32(p.err) == 0;
+    return __syncthreads_or(bad) == 0;
 }
 
 // Trace: CTA 0 records when phase `ph` finished its own work (slot 2+2ph) and when the
@@ -184,7 +194,15 @@ __device__ __forceinline__ void trace_step(const DecodeParams& p, int l, int ph,
 template <typename F>
 __device__ bool traced_barrier(const DecodeParams& p, BarState& bs, int ph, F&& during) {
     trace_mark(p, 2 + 2 * ph);
+    const bool per_cta = p.trace && threadIdx.x == 0 && ph >= 5 && ph < 10 && blockIdx.x < 148;
+    if (per_cta) {
+        p.trace[TRACE_CTA + 148 * (ph - 5) + blockIdx.x] = globaltimer();
+        unsigned smid;
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+        p.trace[TRACE_CTA + 1480 + blockIdx.x] = smid;
+    }
     const bool ok = grid_barrier(p, bs, during);
+    if (per_cta) p.trace[TRACE_CTA + 740 + 148 * (ph - 5) + blockIdx.x] = globaltimer();
     trace_mark(p, 3 + 2 * ph);
     return ok;
 }
@@ -406,6 +424,7 @@ __device__ void phase_attention(const DecodeParams& p, const Smem& s, int l, int
             stage_rows(kl, kb, s0, ns, g);
             if (single) stage_rows(vl, vb, s0, ns, g);
             __syncthreads();
+            if (s0 == t0) trace_step(p, l, 1, 4);
             const int ndots = ns * 8;
             for (int it = 0; it < (ndots + 63) / 64; ++it) {
                 const int di = it * 64 + (tid >> 3);
@@ -535,7 +554,7 @@ __device__ void load_q8k_blocks(const uint8_t* src, int nblocks, const Smem& s) 
 
 // Every CTA combines the attention chunks of all 16 heads (same operations and order as
 // the last-CTA combine) and quantises the result ties-to-even straight into s.xq.
-__device__ void combine_attention(const DecodeParams& p, const Smem& s, int cta) {
+__device__ void combine_attention(const DecodeParams& p, const Smem& s, int l, int cta) {
     const int n = p.pos + 1, C = attn_chunks(n);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float* wts = s.rowval;   // [16][16]
@@ -563,7 +582,9 @@ __device__ void combine_attention(const DecodeParams& p, const Smem& s, int cta)
             Ls = __fmaf_rn(__shfl_sync(0xffffffffu, wv, cc), __shfl_sync(0xffffffffu, lc, cc), Ls);
         if (lane == 0) invl[warp] = __fdiv_rn(1.0f, Ls);
     }
+    if (warp == 0) trace_step(p, l, 2, 4);
     __syncthreads();
+    trace_step(p, l, 2, 5);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const int o = tid + 512 * i, h = o >> 7;
@@ -576,6 +597,7 @@ __device__ void combine_attention(const DecodeParams& p, const Smem& s, int cta)
         if (cta == 0) p.att[o] = out;
     }
     __syncthreads();
+    trace_step(p, l, 2, 6);
     if (warp < N_EMBD / 256) {
         float y[8];
 #pragma unroll
@@ -591,7 +613,7 @@ __device__ void phase_o(const DecodeParams& p, const Smem& s, int l, int cta, in
     const int r0 = pl.row0[0], n = pl.nrows[0];
     const float xr = threadIdx.x < n ? __ldcg(p.x + r0 + threadIdx.x) : 0.0f;   // residual rows, early
     if (attn_chunks(p.pos + 1) <= DIST_COMBINE_MAX)
-        combine_attention(p, s, cta);
+        combine_attention(p, s, l, cta);
     else
         load_q8k_blocks(p.att_q8k, N_EMBD / 256, s);
     trace_step(p, l, 2, 1);
@@ -611,7 +633,8 @@ __device__ void phase_gu(const DecodeParams& p, const Smem& s, int l, int cta, i
     const PhaseLayout pl = phase_layout(L, 2, cta, ncta);
     const int n = pl.nrows[0];
     float* rv = s.rowval;
-    gemv_rows(L.tg, s.wbuf[0] + pl.off[0], n, N_EMBD / 256, *s.xq, s.part, MAX_TASKS, rv);
+    gemv_rows(L.tg, s.wbuf[0] + pl.off[0], n, N_EMBD / 256, *s.xq, s.part, MAX_TASKS, rv,
+              (p.trace && l == 1 && cta == 0) ? p.trace + TRACE_DETAIL + 64 : nullptr);
     trace_step(p, l, 3, 3);
     gemv_rows(L.tu, s.wbuf[0] + pl.off[1], n, N_EMBD / 256, *s.xq, s.part, MAX_TASKS, rv + 128);
     trace_step(p, l, 3, 4);
@@ -720,10 +743,9 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
     ptr += WBUF_BYTES + WBUF_SLACK;
     s.xq = reinterpret_cast<XQSmem*>(ptr);
     ptr += (sizeof(XQSmem) + 127) & ~size_t(127);
-    s.part = reinterpret_cast<int*>(ptr);
-    ptr += MAX_TASKS * PART_WORDS * 4;
+    s.part = reinterpret_cast<int*>(ptr);   // GEMV scratch; aliased by xs (never live across a GEMV)
     s.xs = reinterpret_cast<float*>(ptr);
-    ptr += N_EMBD * 4;
+    ptr += SCRATCH_BYTES;
     s.rowval = reinterpret_cast<float*>(ptr);
     ptr += ROWVAL_FLOATS * 4;
     s.red = reinterpret_cast<float*>(ptr);
@@ -814,7 +836,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_attention(const DecodeParams
 size_t decode_smem_bytes() {
     size_t b = 2 * (WBUF_BYTES + WBUF_SLACK);
     b += (sizeof(XQSmem) + 127) & ~size_t(127);
-    b += MAX_TASKS * PART_WORDS * 4 + N_EMBD * 4 + ROWVAL_FLOATS * 4 + 32 * 4 + 12 * 8 + 16;
+    b += SCRATCH_BYTES + ROWVAL_FLOATS * 4 + 32 * 4 + 12 * 8 + 16;
     return b;
 }
 

@@ -79,6 +79,11 @@ __device__ __forceinline__ uint32_t ld_acquire_u32(const unsigned* p) {
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+__device__ __forceinline__ uint32_t ld_relaxed_u32(const unsigned* p) {
+    uint32_t v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
 __device__ __forceinline__ void red_release_add_u32(unsigned* p, uint32_t v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -360,36 +365,44 @@ __device__ __forceinline__ void block_scales(int type, const uint8_t* blk, float
 }
 
 // ---------------------------------------------------------------- GEMV over staged rows
-// Rows [0, R) of one matrix (type, NB super-blocks per row) are staged contiguously in
-// shared memory at `w`.  Pass 1: every (row, block) task's integer partials, split into
-// the eight AVX2 lanes, go to `part` (9 ints per task), one task per thread.  Pass 2:
-// lane k of a row group runs the reference's fp32 accumulator chain for AVX2 lane k over
-// the blocks, the eight lanes are reduced with hsum_f32_8's tree (a butterfly over lane
-// bits 2, 1, 0) and the Q4_K min term is added.  Row r's value goes to out[r] (shared
-// memory), visible to every thread on return.  Not inlined: one copy serves every phase.
+// Rows [0, R) of one matrix (TYPE, NB super-blocks per row) are staged contiguously in
+// shared memory at `w`.  Pass 1, one (row, block) task per thread: the task's integer
+// partials split into the eight AVX2 lanes, its min term (Q4_K) or offset (Q6_K), and
+// the two fp32 scale products dx = xd*d and dm = -(xd*dmin) go to `part` (PART_WORDS
+// words per task).  Pass 2: lane k of a row group loads every operand of its chain, then
+// runs the reference's fp32 accumulator chain for AVX2 lane k over the blocks
+// (acc = fma(dx, isum_k, acc); Q4_K also acc_min = fma(dm, minsum, acc_min)); the eight
+// lanes are reduced with hsum_f32_8's tree (a butterfly over lane bits 2, 1, 0) and the
+// min term is added.  Row r's value goes to out[r] (shared memory), visible to every
+// thread on return.  Not inlined: one copy per (TYPE, NB) serves every phase.
 // Must be called by all threads of the CTA (contains __syncthreads).
-constexpr int PART_WORDS = 9;
+constexpr int PART_WORDS = 11;   // k0..k7, minsum, dx, dm (odd stride: conflict-free stores)
 
-template <int NB>
-__device__ __noinline__ void gemv_rows_t(int type, const uint8_t* w, int R, const XQSmem& xq, int* part,
-                                         int max_tasks, float* out, unsigned long long* tr) {
+template <int TYPE, int NB>
+__device__ __noinline__ void gemv_rows_t(const uint8_t* w, int R, const XQSmem& xq, int* part, int max_tasks,
+                                         float* out, unsigned long long* tr) {
+    constexpr int RB = TYPE == GGML_Q4_K ? Q4K_BYTES : Q6K_BYTES;
     const int tid = threadIdx.x, nthr = blockDim.x;
-    const int rb = block_bytes(type);
     const int mt = (max_tasks / NB) * NB;   // whole rows per chunk
     for (int t0 = 0; t0 < R * NB; t0 += mt) {
         const int ntask = min(mt, R * NB - t0);
         for (int t = tid; t < ntask; t += nthr) {
             const int task = t0 + t, b = task % NB;
-            const uint8_t* blk = w + static_cast<size_t>(task) * rb;
+            const uint8_t* blk = w + static_cast<size_t>(task) * RB;
             Partials p;
-            if (type == GGML_Q4_K)
+            if (TYPE == GGML_Q4_K)
                 q4k_task(blk, xq, b, p);
             else
                 q6k_task(blk, xq, b, p);
+            float d, dmin;
+            block_scales(TYPE, blk, d, dmin);
+            const float xd = xq.d[b];
             int* dst = part + t * PART_WORDS;
 #pragma unroll
             for (int k = 0; k < 8; ++k) dst[k] = p.k[k];
             dst[8] = p.minsum;
+            dst[9] = __float_as_int(__fmul_rn(xd, d));
+            dst[10] = __float_as_int(-__fmul_rn(xd, dmin));
         }
         __syncthreads();
         if (tr && tid == 0) tr[0] = globaltimer();
@@ -398,39 +411,49 @@ __device__ __noinline__ void gemv_rows_t(int type, const uint8_t* w, int R, cons
         for (int base = tid & ~31; base < total; base += nthr) {
             const int g = base + (tid & 31);
             const bool valid = g < total;
-            const int r = r_begin + (valid ? (g >> 3) : 0), k = g & 7;
-            float acc = 0.0f, acc_min = 0.0f;
-            if (valid) {
+            const int r = valid ? (g >> 3) : 0, k = g & 7;
+            const int* src = part + r * NB * PART_WORDS;
+            float dx[NB], iv[NB], dm[NB], im[NB];
 #pragma unroll
-                for (int b = 0; b < NB; ++b) {
-                    const int task = r * NB + b;
-                    float d, dmin;
-                    block_scales(type, w + static_cast<size_t>(task) * rb, d, dmin);
-                    const float xd = xq.d[b];
-                    const int* src = part + (task - t0) * PART_WORDS;
-                    acc = __fmaf_rn(__fmul_rn(xd, d), __int2float_rn(src[k]), acc);
-                    if (type == GGML_Q4_K)
-                        acc_min = __fmaf_rn(-__fmul_rn(xd, dmin), __int2float_rn(src[8]), acc_min);
+            for (int b = 0; b < NB; ++b) {
+                dx[b] = __int_as_float(src[b * PART_WORDS + 9]);
+                iv[b] = __int2float_rn(src[b * PART_WORDS + k]);
+                if (TYPE == GGML_Q4_K) {
+                    dm[b] = __int_as_float(src[b * PART_WORDS + 10]);
+                    im[b] = __int2float_rn(src[b * PART_WORDS + 8]);
                 }
+            }
+            float acc = 0.0f, acc_min = 0.0f;
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+                acc = __fmaf_rn(dx[b], iv[b], acc);
+                if (TYPE == GGML_Q4_K) acc_min = __fmaf_rn(dm[b], im[b], acc_min);
             }
             acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 4));
             acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 2));
             acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
-            if (valid && k == 0) out[r] = type == GGML_Q4_K ? __fadd_rn(acc, acc_min) : acc;
+            if (valid && k == 0) out[r_begin + r] = TYPE == GGML_Q4_K ? __fadd_rn(acc, acc_min) : acc;
         }
         __syncthreads();
         if (tr && tid == 0) tr[1] = globaltimer();
     }
 }
 
-// Dispatch on the row length (8 or 24 super-blocks).
+// Dispatch on the weight type (Q4_K / Q6_K) and the row length (8 or 24 super-blocks).
 // `tr` (optional): thread 0 stores globaltimer after pass 1 (tr[0]) and pass 2 (tr[1]).
 static __device__ __forceinline__ void gemv_rows(int type, const uint8_t* w, int R, int nb, const XQSmem& xq, int* part,
                                                  int max_tasks, float* out, unsigned long long* tr = nullptr) {
-    if (nb == 8)
-        gemv_rows_t<8>(type, w, R, xq, part, max_tasks, out, tr);
-    else
-        gemv_rows_t<24>(type, w, R, xq, part, max_tasks, out, tr);
+    if (type == GGML_Q4_K) {
+        if (nb == 8)
+            gemv_rows_t<GGML_Q4_K, 8>(w, R, xq, part, max_tasks, out, tr);
+        else
+            gemv_rows_t<GGML_Q4_K, 24>(w, R, xq, part, max_tasks, out, tr);
+    } else {
+        if (nb == 8)
+            gemv_rows_t<GGML_Q6_K, 8>(w, R, xq, part, max_tasks, out, tr);
+        else
+            gemv_rows_t<GGML_Q6_K, 24>(w, R, xq, part, max_tasks, out, tr);
+    }
 }
 
 }  // namespace mcpm

@@ -23,8 +23,9 @@ constexpr int ATT_MAX_CHUNKS = 64;         // attention chunks per head (chunk =
 constexpr int ATT_PART_STRIDE = 2 + HEAD_DIM;
 constexpr int ATT_SC_STRIDE = 256;         // chunk-length bound: 32*ceil(MAX_SEQ/2048)
 constexpr int MAX_SEQ = 16384;
-constexpr int TRACE_WORDS = 720;          // 2 + 2*(5*layers+1) phase marks, then detail marks from 650
+constexpr int TRACE_WORDS = 2400;         // 2 + 2*(5*layers+1) phase marks, detail marks from 650, per-CTA from 720
 constexpr int TRACE_DETAIL = 650;         // sub-step marks of layer 1: 650 + 10*phase + step
+constexpr int TRACE_CTA = 720;            // layer-1 barrier k, CTA c: arrival 720 + 148k + c, release 1460 + 148k + c, SM id 2200 + c
 
 struct LayerDev {
     const uint8_t *wq, *wk, *wv, *wo, *wg, *wu, *wd;
