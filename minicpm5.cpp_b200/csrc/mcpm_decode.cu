@@ -296,7 +296,9 @@ __device__ void norm_quant(const float* x, const float* w, const Smem& s) {
         const float ss = __fadd_rn(__fadd_rn(__fadd_rn(red[0], red[1]), __fadd_rn(red[2], red[3])),
                                    __fadd_rn(__fadd_rn(red[4], red[5]), __fadd_rn(red[6], red[7])));
         const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(N_EMBD)), 1e-6f)));
-        const float* xb = s.xs + 256 * warp + 8 * lane;
+        const float4 xa = *reinterpret_cast<const float4*>(s.xs + 256 * warp + 8 * lane);
+        const float4 xc = *reinterpret_cast<const float4*>(s.xs + 256 * warp + 8 * lane + 4);
+        const float xb[8] = {xa.x, xa.y, xa.z, xa.w, xc.x, xc.y, xc.z, xc.w};
         const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
         float y[8];
 #pragma unroll
@@ -389,6 +391,101 @@ __device__ __forceinline__ int attn_chunks(int n) {
     return (n + P - 1) / P;
 }
 
+// One attention unit of at most 32 positions (chunk length P = 32, contexts up to 2048):
+// the 8 query heads of KV head g against positions [t0, t0+np).  q and K go straight from
+// L2 into registers (one round trip), V streams into shared memory meanwhile (cp.async).
+// Thread (warp w, group G = lane/8, j = lane%8): heads 2G, 2G+1 x positions t0+2w, t0+2w+1,
+// dims 4j + 32i + c of each dot (the canonical 8-lane split of dot128_group).
+// Same numerics as the general path below: scores, chunk max, exp, position-ordered
+// sum and fma chains, partials [head][chunk][m, l, o[128]].
+__device__ void attention_unit32(const DecodeParams& p, const Smem& s, int l, int g, int c, int t0, int np) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, j = lane & 7, G = lane >> 3;
+    float* vb = reinterpret_cast<float*>(s.wbuf[0]);   // [32][128] V rows of the chunk
+    float* sc = vb + 32 * HEAD_DIM;                     // [8][32] scores -> probabilities
+    float* stat = sc + 8 * 32;                          // m[8], l[8]
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(HEAD_DIM)));
+    const float* kl = p.kc + static_cast<size_t>(l) * p.max_seq * KV_DIM + g * HEAD_DIM;
+    const float* vl = p.vc + static_cast<size_t>(l) * p.max_seq * KV_DIM + g * HEAD_DIM;
+    for (int i = tid; i < np * 32; i += blockDim.x)
+        cp_async16(vb + 4 * i, vl + static_cast<size_t>(t0 + (i >> 5)) * KV_DIM + 4 * (i & 31));
+    cp_async_commit();
+    const int tA = 2 * warp, tB = tA + 1;
+    const bool va = tA < np, vbv = tB < np;
+    const float* q0 = p.q + (8 * g + 2 * G) * HEAD_DIM + 4 * j;
+    const float* kA = kl + static_cast<size_t>(t0 + (va ? tA : 0)) * KV_DIM + 4 * j;
+    const float* kB = kl + static_cast<size_t>(t0 + (vbv ? tB : 0)) * KV_DIM + 4 * j;
+    float4 qa[4], qb[4], ka[4], kb[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        qa[i] = ld_cg_f4(q0 + 32 * i);
+        qb[i] = ld_cg_f4(q0 + HEAD_DIM + 32 * i);
+        ka[i] = ld_cg_f4(kA + 32 * i);
+        kb[i] = ld_cg_f4(kB + 32 * i);
+    }
+    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};   // (h0,tA) (h0,tB) (h1,tA) (h1,tB)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        d[0] = __fmaf_rn(qa[i].x, ka[i].x, d[0]);
+        d[0] = __fmaf_rn(qa[i].y, ka[i].y, d[0]);
+        d[0] = __fmaf_rn(qa[i].z, ka[i].z, d[0]);
+        d[0] = __fmaf_rn(qa[i].w, ka[i].w, d[0]);
+        d[1] = __fmaf_rn(qa[i].x, kb[i].x, d[1]);
+        d[1] = __fmaf_rn(qa[i].y, kb[i].y, d[1]);
+        d[1] = __fmaf_rn(qa[i].z, kb[i].z, d[1]);
+        d[1] = __fmaf_rn(qa[i].w, kb[i].w, d[1]);
+        d[2] = __fmaf_rn(qb[i].x, ka[i].x, d[2]);
+        d[2] = __fmaf_rn(qb[i].y, ka[i].y, d[2]);
+        d[2] = __fmaf_rn(qb[i].z, ka[i].z, d[2]);
+        d[2] = __fmaf_rn(qb[i].w, ka[i].w, d[2]);
+        d[3] = __fmaf_rn(qb[i].x, kb[i].x, d[3]);
+        d[3] = __fmaf_rn(qb[i].y, kb[i].y, d[3]);
+        d[3] = __fmaf_rn(qb[i].z, kb[i].z, d[3]);
+        d[3] = __fmaf_rn(qb[i].w, kb[i].w, d[3]);
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        d[e] = __fadd_rn(d[e], __shfl_xor_sync(0xffffffffu, d[e], 4));
+        d[e] = __fadd_rn(d[e], __shfl_xor_sync(0xffffffffu, d[e], 2));
+        d[e] = __fadd_rn(d[e], __shfl_xor_sync(0xffffffffu, d[e], 1));
+    }
+    if (j == 0) {
+        if (va) sc[(2 * G) * 32 + tA] = __fmul_rn(d[0], scale), sc[(2 * G + 1) * 32 + tA] = __fmul_rn(d[2], scale);
+        if (vbv) sc[(2 * G) * 32 + tB] = __fmul_rn(d[1], scale), sc[(2 * G + 1) * 32 + tB] = __fmul_rn(d[3], scale);
+    }
+    __syncthreads();
+    trace_step(p, l, 1, 1);
+    if (warp < 8) {   // chunk max, probabilities, position-ordered sum (warp = head)
+        float v = lane < np ? sc[warp * 32 + lane] : -__int_as_float(0x7f800000);
+        float m = v;
+        for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        const float pr = lane < np ? canon_expf(__fsub_rn(v, m)) : 0.0f;
+        if (lane < np) sc[warp * 32 + lane] = pr;
+        float sum = 0.0f;
+        for (int t = 0; t < np; ++t) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, pr, t));
+        if (lane == 0) stat[warp] = m, stat[8 + warp] = sum;
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    float acc0 = 0.0f, acc1 = 0.0f;   // o[h][dd] = fma chain over positions
+    const int h0 = tid >> 7, h1 = h0 + 4, dd = tid & 127;
+    for (int t = 0; t < np; ++t) {
+        const float v = vb[t * HEAD_DIM + dd];
+        acc0 = __fmaf_rn(sc[h0 * 32 + t], v, acc0);
+        acc1 = __fmaf_rn(sc[h1 * 32 + t], v, acc1);
+    }
+    float* pa0 = p.att_part + (static_cast<size_t>(8 * g + h0) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
+    float* pa1 = p.att_part + (static_cast<size_t>(8 * g + h1) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
+    __stcg(pa0 + 2 + dd, acc0);
+    __stcg(pa1 + 2 + dd, acc1);
+    if (tid < 8) {
+        float* pm = p.att_part + (static_cast<size_t>(8 * g + tid) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
+        __stcg(pm, stat[tid]);
+        __stcg(pm + 1, stat[8 + tid]);
+    }
+    __syncthreads();
+    trace_step(p, l, 1, 2);
+}
+
 __device__ void phase_attention(const DecodeParams& p, const Smem& s, int l, int cta, int ncta, bool combine_here) {
     const int n = p.pos + 1;
     const int P = 32 * ((n + 2047) / 2048);
@@ -416,67 +513,71 @@ __device__ void phase_attention(const DecodeParams& p, const Smem& s, int l, int
         const int t0 = c * P, t1 = min(t0 + P, n), np = t1 - t0;
         const bool single = np <= 32;   // q, K and V of the chunk staged in one round trip
         __syncthreads();
-        if (tid < 256)
-            reinterpret_cast<float4*>(qh)[tid] = __ldcg(reinterpret_cast<const float4*>(p.q + 8 * g * HEAD_DIM) + tid);
-        for (int s0 = t0; s0 < t1; s0 += 32) {   // scores, 32 positions at a time
-            const int ns = min(32, t1 - s0);
-            if (s0 != t0) __syncthreads();
-            stage_rows(kl, kb, s0, ns, g);
-            if (single) stage_rows(vl, vb, s0, ns, g);
-            __syncthreads();
-            if (s0 == t0) trace_step(p, l, 1, 4);
-            const int ndots = ns * 8;
-            for (int it = 0; it < (ndots + 63) / 64; ++it) {
-                const int di = it * 64 + (tid >> 3);
-                const bool valid = di < ndots;
-                const int h = di & 7, tt = valid ? (di >> 3) : 0;
-                const float d = dot128_group(qh + h * HEAD_DIM, kb + tt * HEAD_DIM, tid & 7);
-                if (valid && (tid & 7) == 0) sc[h * ATT_SC_STRIDE + (s0 - t0) + tt] = __fmul_rn(d, scale);
-            }
-        }
-        __syncthreads();
-        trace_step(p, l, 1, 1);
-        if (warp < 8) {   // chunk max, probabilities, position-ordered sum (warp = head)
-            float m = -__int_as_float(0x7f800000);
-            for (int t = lane; t < np; t += 32) m = fmaxf(m, sc[warp * ATT_SC_STRIDE + t]);
-            for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            for (int t = lane; t < np; t += 32)
-                sc[warp * ATT_SC_STRIDE + t] = canon_expf(__fsub_rn(sc[warp * ATT_SC_STRIDE + t], m));
-            __syncwarp();
-            if (lane == 0) {
-                float sum = 0.0f;
-                for (int t = 0; t < np; ++t) sum = __fadd_rn(sum, sc[warp * ATT_SC_STRIDE + t]);
-                stat[warp] = m;
-                stat[8 + warp] = sum;
-            }
-        }
-        float acc0 = 0.0f, acc1 = 0.0f;   // o[h][d] = fma chain over positions
-        const int h0 = tid >> 7, h1 = h0 + 4, dd = tid & 127;
-        for (int s0 = t0; s0 < t1; s0 += 32) {
-            const int ns = min(32, t1 - s0);
-            __syncthreads();
-            if (!single) {
-                stage_rows(vl, vb, s0, ns, g);
+        if (P == 32) {
+            attention_unit32(p, s, l, g, c, t0, np);
+        } else {
+            if (tid < 256)
+                reinterpret_cast<float4*>(qh)[tid] = __ldcg(reinterpret_cast<const float4*>(p.q + 8 * g * HEAD_DIM) + tid);
+            for (int s0 = t0; s0 < t1; s0 += 32) {   // scores, 32 positions at a time
+                const int ns = min(32, t1 - s0);
+                if (s0 != t0) __syncthreads();
+                stage_rows(kl, kb, s0, ns, g);
+                if (single) stage_rows(vl, vb, s0, ns, g);
                 __syncthreads();
+                if (s0 == t0) trace_step(p, l, 1, 4);
+                const int ndots = ns * 8;
+                for (int it = 0; it < (ndots + 63) / 64; ++it) {
+                    const int di = it * 64 + (tid >> 3);
+                    const bool valid = di < ndots;
+                    const int h = di & 7, tt = valid ? (di >> 3) : 0;
+                    const float d = dot128_group(qh + h * HEAD_DIM, kb + tt * HEAD_DIM, tid & 7);
+                    if (valid && (tid & 7) == 0) sc[h * ATT_SC_STRIDE + (s0 - t0) + tt] = __fmul_rn(d, scale);
+                }
             }
-            for (int tt = 0; tt < ns; ++tt) {
-                const float v = vb[tt * HEAD_DIM + dd];
-                acc0 = __fmaf_rn(sc[h0 * ATT_SC_STRIDE + (s0 - t0) + tt], v, acc0);
-                acc1 = __fmaf_rn(sc[h1 * ATT_SC_STRIDE + (s0 - t0) + tt], v, acc1);
+            __syncthreads();
+            trace_step(p, l, 1, 1);
+            if (warp < 8) {   // chunk max, probabilities, position-ordered sum (warp = head)
+                float m = -__int_as_float(0x7f800000);
+                for (int t = lane; t < np; t += 32) m = fmaxf(m, sc[warp * ATT_SC_STRIDE + t]);
+                for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                for (int t = lane; t < np; t += 32)
+                    sc[warp * ATT_SC_STRIDE + t] = canon_expf(__fsub_rn(sc[warp * ATT_SC_STRIDE + t], m));
+                __syncwarp();
+                if (lane == 0) {
+                    float sum = 0.0f;
+                    for (int t = 0; t < np; ++t) sum = __fadd_rn(sum, sc[warp * ATT_SC_STRIDE + t]);
+                    stat[warp] = m;
+                    stat[8 + warp] = sum;
+                }
             }
+            float acc0 = 0.0f, acc1 = 0.0f;   // o[h][d] = fma chain over positions
+            const int h0 = tid >> 7, h1 = h0 + 4, dd = tid & 127;
+            for (int s0 = t0; s0 < t1; s0 += 32) {
+                const int ns = min(32, t1 - s0);
+                __syncthreads();
+                if (!single) {
+                    stage_rows(vl, vb, s0, ns, g);
+                    __syncthreads();
+                }
+                for (int tt = 0; tt < ns; ++tt) {
+                    const float v = vb[tt * HEAD_DIM + dd];
+                    acc0 = __fmaf_rn(sc[h0 * ATT_SC_STRIDE + (s0 - t0) + tt], v, acc0);
+                    acc1 = __fmaf_rn(sc[h1 * ATT_SC_STRIDE + (s0 - t0) + tt], v, acc1);
+                }
+            }
+            // partials: [head][chunk][m, l, o[128]]
+            float* pa0 = p.att_part + (static_cast<size_t>(8 * g + h0) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
+            float* pa1 = p.att_part + (static_cast<size_t>(8 * g + h1) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
+            __stcg(pa0 + 2 + dd, acc0);
+            __stcg(pa1 + 2 + dd, acc1);
+            if (tid < 8) {
+                float* pm = p.att_part + (static_cast<size_t>(8 * g + tid) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
+                __stcg(pm, stat[tid]);
+                __stcg(pm + 1, stat[8 + tid]);
+            }
+            __syncthreads();
+            trace_step(p, l, 1, 2);
         }
-        // partials: [head][chunk][m, l, o[128]]
-        float* pa0 = p.att_part + (static_cast<size_t>(8 * g + h0) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
-        float* pa1 = p.att_part + (static_cast<size_t>(8 * g + h1) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
-        __stcg(pa0 + 2 + dd, acc0);
-        __stcg(pa1 + 2 + dd, acc1);
-        if (tid < 8) {
-            float* pm = p.att_part + (static_cast<size_t>(8 * g + tid) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
-            __stcg(pm, stat[tid]);
-            __stcg(pm + 1, stat[8 + tid]);
-        }
-        __syncthreads();
-        trace_step(p, l, 1, 2);
         if (!combine_here) continue;
         if (tid == 0) {
             __threadfence();
@@ -567,12 +668,12 @@ __device__ void combine_attention(const DecodeParams& p, const Smem& s, int l, i
         const int o = tid + 512 * i, h = o >> 7, d = o & 127;
         const float* ph = p.att_part + static_cast<size_t>(h) * ATT_MAX_CHUNKS * ATT_PART_STRIDE + 2 + d;
 #pragma unroll
-        for (int cc = 0; cc < DIST_COMBINE_MAX; ++cc) v[i][cc] = cc < C ? __ldcg(ph + cc * ATT_PART_STRIDE) : 0.0f;
+        for (int cc = 0; cc < DIST_COMBINE_MAX; ++cc) v[i][cc] = cc < C ? ld_cg_f32(ph + cc * ATT_PART_STRIDE) : 0.0f;
     }
     if (warp < N_HEAD) {
         const float* ph = p.att_part + static_cast<size_t>(warp) * ATT_MAX_CHUNKS * ATT_PART_STRIDE;
-        const float mc = lane < C ? __ldcg(ph + lane * ATT_PART_STRIDE) : 0.0f;
-        const float lc = lane < C ? __ldcg(ph + lane * ATT_PART_STRIDE + 1) : 0.0f;
+        const float mc = lane < C ? ld_cg_f32(ph + lane * ATT_PART_STRIDE) : 0.0f;
+        const float lc = lane < C ? ld_cg_f32(ph + lane * ATT_PART_STRIDE + 1) : 0.0f;
         float M = lane < C ? mc : -__int_as_float(0x7f800000);
         for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
         const float wv = lane < C ? canon_expf(__fsub_rn(mc, M)) : 0.0f;
@@ -599,9 +700,9 @@ __device__ void combine_attention(const DecodeParams& p, const Smem& s, int l, i
     __syncthreads();
     trace_step(p, l, 2, 6);
     if (warp < N_EMBD / 256) {
-        float y[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) y[k] = ab[256 * warp + 8 * lane + k];
+        const float4 a = *reinterpret_cast<const float4*>(ab + 256 * warp + 8 * lane);
+        const float4 b = *reinterpret_cast<const float4*>(ab + 256 * warp + 8 * lane + 4);
+        const float y[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
         quant_block_warp<false>(y, s.xq->qs[warp], &s.xq->d[warp], s.xq->bsums[warp]);
     }
     __syncthreads();

@@ -74,6 +74,23 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
+// 16-byte global->shared copy (LDGSTS, L2 only); completes at cp_async_wait_all.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// 16-byte L2 load that the compiler keeps in program order (issued where written).
+__device__ __forceinline__ float4 ld_cg_f4(const float* p) {
+    float4 v;
+    asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ float ld_cg_f32(const float* p) {
+    float v;
+    asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
 __device__ __forceinline__ uint32_t ld_acquire_u32(const unsigned* p) {
     uint32_t v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -184,22 +201,34 @@ template <bool AWAY>
 __device__ __forceinline__ void quant_block_warp(const float (&y)[8], int8_t* qs_out, float* d_out,
                                                  int16_t* bsums_out) {
     const int lane = threadIdx.x & 31;
-    float accs[8];
+    bool nan = false;
+    unsigned mine = 0u;   // largest |y| of this lane, as bits (ordered like the values)
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-        const float e = fabsf(y[k]);
-        const unsigned nanmask = __ballot_sync(0xffffffffu, e != e);
-        const int last = nanmask ? 31 - __clz(nanmask) : -1;
-        const unsigned bits = (lane > last) ? __float_as_uint(e) : 0u;
-        const unsigned mx = __reduce_max_sync(0xffffffffu, bits);
-        accs[k] = (last == 31) ? __int_as_float(0x7fc00000) : __uint_as_float(mx);
+        nan |= y[k] != y[k];
+        mine = max(mine, __float_as_uint(fabsf(y[k])));
     }
-    float m[4];
+    float amax;
+    if (!__any_sync(0xffffffffu, nan)) {   // no NaN: every lane order gives the plain maximum
+        amax = __uint_as_float(__reduce_max_sync(0xffffffffu, mine));
+    } else {
+        float accs[8];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) m[i] = (accs[i + 4] > accs[i]) ? accs[i + 4] : accs[i];
-    const float n0 = (m[2] > m[0]) ? m[2] : m[0];
-    const float n1 = (m[3] > m[1]) ? m[3] : m[1];
-    const float amax = (n1 > n0) ? n1 : n0;
+        for (int k = 0; k < 8; ++k) {
+            const float e = fabsf(y[k]);
+            const unsigned nanmask = __ballot_sync(0xffffffffu, e != e);
+            const int last = nanmask ? 31 - __clz(nanmask) : -1;
+            const unsigned bits = (lane > last) ? __float_as_uint(e) : 0u;
+            const unsigned mx = __reduce_max_sync(0xffffffffu, bits);
+            accs[k] = (last == 31) ? __int_as_float(0x7fc00000) : __uint_as_float(mx);
+        }
+        float m[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) m[i] = (accs[i + 4] > accs[i]) ? accs[i + 4] : accs[i];
+        const float n0 = (m[2] > m[0]) ? m[2] : m[0];
+        const float n1 = (m[3] > m[1]) ? m[3] : m[1];
+        amax = (n1 > n0) ? n1 : n0;
+    }
     int q[8];
     if (amax == 0.0f || amax != amax) {
 #pragma unroll
