@@ -54,10 +54,9 @@ __device__ PhaseLayout phase_layout(const LayerDev& L, int kind, int cta, int nc
     PhaseLayout pl;
     for (int i = 0; i < 3; ++i) pl.row0[i] = pl.nrows[i] = 0, pl.off[i] = pl.bytes[i] = 0;
     int a, b;
-    if (kind == 0) {   // QKV: row pairs of the combined [Q; K; V] rows
-        split_range(QKV_ROWS / 2, cta, ncta, a, b);
-        a *= 2;
-        b *= 2;
+    if (kind == 0) {   // QKV: row pairs of the combined [Q; K; V] rows, cost-weighted split
+        a = 2 * qkv_pair_boundary(L.tq, L.tk, L.tv, cta, ncta);
+        b = 2 * qkv_pair_boundary(L.tq, L.tk, L.tv, cta + 1, ncta);
         const int lo[3] = {0, N_EMBD, N_EMBD + KV_DIM}, hi[3] = {N_EMBD, N_EMBD + KV_DIM, QKV_ROWS};
         const int types[3] = {L.tq, L.tk, L.tv};
         uint32_t off = 0;
@@ -108,12 +107,13 @@ __device__ void issue_weight_phase(const DecodeParams& p, const Smem& s, int wp,
     const int l = wp >> 2, kind = wp & 3;
     const LayerDev& L = p.layers[l];
     const PhaseLayout pl = phase_layout(L, kind, cta, ncta);
+    const uint64_t pol = l2_evict_first_policy();
     for (int i = 0; i < 3; ++i) {
         mbar_expect_tx(&bars[i], pl.bytes[i]);
         if (pl.bytes[i]) {
             const int rb = row_bytes(phase_type(L, kind, i), phase_cols(kind));
-            bulk_g2s(s.wbuf[buf] + pl.off[i], phase_src(L, kind, i) + static_cast<size_t>(pl.row0[i]) * rb,
-                     pl.bytes[i], &bars[i]);
+            bulk_g2s_stream(s.wbuf[buf] + pl.off[i], phase_src(L, kind, i) + static_cast<size_t>(pl.row0[i]) * rb,
+                            pl.bytes[i], &bars[i], pol);
         }
     }
     mbar_expect_tx(&bars[3], 0);
@@ -138,7 +138,7 @@ __device__ void issue_lm_stage(const DecodeParams& p, const Smem& s, const LmPla
     const int a = q.r0 + st * q.sr, n = min(q.sr, q.r1 - a);
     const uint32_t bytes = n > 0 ? static_cast<uint32_t>(n) * q.rb : 0;
     mbar_expect_tx(&s.lmbar[slot], bytes);
-    if (bytes) bulk_g2s(lm_slot(s, slot), p.lm + static_cast<size_t>(a) * q.rb, bytes, &s.lmbar[slot]);
+    if (bytes) bulk_g2s_stream(lm_slot(s, slot), p.lm + static_cast<size_t>(a) * q.rb, bytes, &s.lmbar[slot], l2_evict_first_policy());
 }
 
 // Bounded grid barrier (all CTAs co-resident: cooperative launch).  A monotonic arrival
@@ -189,6 +189,8 @@ __device__ __forceinline__ void trace_mark(const DecodeParams& p, int slot) {
 // Sub-step marks inside the phases of layer 1 (phase kind ph: 0 QKV .. 4 D, 5 LM).
 __device__ __forceinline__ void trace_step(const DecodeParams& p, int l, int ph, int step) {
     if (l == 1) trace_mark(p, TRACE_DETAIL + 10 * ph + step);
+    if (l == 1 && ph == 0 && step <= 3 && p.trace && threadIdx.x == 0 && blockIdx.x < 148)
+        p.trace[2400 + 148 * (step - 1) + blockIdx.x] = globaltimer();
 }
 
 template <typename F>
@@ -325,10 +327,8 @@ __device__ void phase_qkv(const DecodeParams& p, const Smem& s, int l, int token
     trace_step(p, l, 0, 2);
     const PhaseLayout pl = phase_layout(L, 0, cta, ncta);
     const int lo[3] = {0, N_EMBD, N_EMBD + KV_DIM};
-    int a, b;
-    split_range(QKV_ROWS / 2, cta, ncta, a, b);
-    a *= 2;
-    b *= 2;
+    const int a = 2 * qkv_pair_boundary(L.tq, L.tk, L.tv, cta, ncta);   // same split as phase_layout
+    const int b = 2 * qkv_pair_boundary(L.tq, L.tk, L.tv, cta + 1, ncta);
     float* rv = s.rowval;
     for (int i = 0; i < 3; ++i) {
         if (pl.nrows[i] == 0) continue;   // uniform across the CTA

@@ -127,9 +127,26 @@ bool phases_fit(const mcpm_engine* e, int n, std::string& why) {
         rb_gu = std::max(rb_gu, row_bytes(L.tg, N_EMBD) + row_bytes(L.tu, N_EMBD));
         rb_d = std::max(rb_d, row_bytes(L.td, N_FF));
     }
-    const int qkv_rows = 2 * ceil_div(QKV_ROWS / 2, n), gu_rows = ceil_div(N_FF, n), od_rows = ceil_div(N_EMBD, n);
-    const long long need[4] = {(long long)qkv_rows * rb_qkv + 48, (long long)od_rows * rb_o,
-                               (long long)gu_rows * rb_gu + 16, (long long)od_rows * rb_d};
+    // QKV: the exact cost-weighted split of every layer (three 16-byte aligned segments)
+    int qkv_rows = 0;
+    long long qkv_bytes = 0;
+    for (const auto& L : e->layers)
+        for (int c = 0; c < n; ++c) {
+            const int a = 2 * qkv_pair_boundary(L.tq, L.tk, L.tv, c, n), b = 2 * qkv_pair_boundary(L.tq, L.tk, L.tv, c + 1, n);
+            qkv_rows = std::max(qkv_rows, b - a);
+            const int lo[3] = {0, N_EMBD, N_EMBD + KV_DIM}, hi[3] = {N_EMBD, N_EMBD + KV_DIM, QKV_ROWS};
+            const int ty[3] = {L.tq, L.tk, L.tv};
+            long long bytes = 0;
+            for (int i = 0; i < 3; ++i) {
+                const int rows = std::max(0, std::min(b, hi[i]) - std::max(a, lo[i]));
+                bytes += (static_cast<long long>(rows) * row_bytes(ty[i], N_EMBD) + 15) / 16 * 16;
+            }
+            qkv_bytes = std::max(qkv_bytes, bytes);
+        }
+    (void)rb_qkv;
+    const int gu_rows = ceil_div(N_FF, n), od_rows = ceil_div(N_EMBD, n);
+    const long long need[4] = {qkv_bytes, (long long)od_rows * rb_o, (long long)gu_rows * rb_gu + 16,
+                               (long long)od_rows * rb_d};
     for (long long b : need)
         if (b > WBUF_BYTES) {
             why = "decode grid of " + std::to_string(n) + " CTAs needs " + std::to_string(b) +

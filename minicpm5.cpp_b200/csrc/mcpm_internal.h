@@ -23,9 +23,25 @@ constexpr int ATT_MAX_CHUNKS = 64;         // attention chunks per head (chunk =
 constexpr int ATT_PART_STRIDE = 2 + HEAD_DIM;
 constexpr int ATT_SC_STRIDE = 256;         // chunk-length bound: 32*ceil(MAX_SEQ/2048)
 constexpr int MAX_SEQ = 16384;
-constexpr int TRACE_WORDS = 2400;         // 2 + 2*(5*layers+1) phase marks, detail marks from 650, per-CTA from 720
+constexpr int TRACE_WORDS = 3400;         // 2 + 2*(5*layers+1) phase marks, detail marks from 650, per-CTA from 720
 constexpr int TRACE_DETAIL = 650;         // sub-step marks of layer 1: 650 + 10*phase + step
-constexpr int TRACE_CTA = 720;            // layer-1 barrier k, CTA c: arrival 720 + 148k + c, release 1460 + 148k + c, SM id 2200 + c
+constexpr int TRACE_CTA = 720;            // layer-1 barrier k, CTA c: arrival 720 + 148k + c, release 1460 + 148k + c, SM id 2200 + c,
+                                          // QKV sub-steps m = 0..2 of layer 1 at 2400 + 148m + c
+
+// QKV row pairs [0, 1280) (Q pairs, then K, then V) are split over the CTAs in proportion
+// to their GEMV cost: a Q6_K row costs about 1.6 Q4_K rows (unaligned 210-byte blocks), so
+// CTAs holding Q6_K V rows get fewer of them and every CTA reaches the barrier together.
+__host__ __device__ inline int qkv_row_cost(int type) { return type == 14 ? 16 : 10; }
+__host__ __device__ inline int qkv_pair_boundary(int tq, int tk, int tv, int c, int ncta) {
+    const long long cq = qkv_row_cost(tq), ck = qkv_row_cost(tk), cv = qkv_row_cost(tv);
+    const int nq = N_EMBD / 2, nk = KV_DIM / 2, nv = KV_DIM / 2;
+    const long long total = cq * nq + ck * nk + cv * nv;
+    const long long t = total * c / ncta;
+    if (t <= cq * nq) return static_cast<int>(t / cq);
+    if (t <= cq * nq + ck * nk) return nq + static_cast<int>((t - cq * nq) / ck);
+    const int pv = nq + nk + static_cast<int>((t - cq * nq - ck * nk) / cv);
+    return pv < nq + nk + nv ? pv : nq + nk + nv;
+}
 
 struct LayerDev {
     const uint8_t *wq, *wk, *wv, *wo, *wg, *wu, *wd;
