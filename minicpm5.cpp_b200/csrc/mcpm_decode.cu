@@ -22,6 +22,15 @@
 namespace mcpm {
 namespace {
 
+// Per-layer fields the phases read on their critical path, copied to shared memory at
+// kernel start: a field read from global memory costs a full L2 round trip there
+// (the L1 is almost all carved out for shared memory).
+struct LayerMeta {
+    const float* attn_norm;
+    const float* ffn_norm;
+    uint8_t tq, tk, tv, to, tg, tu, td, pad;
+};
+
 // GEMV partials and the staged fp32 activation share one scratch region.
 constexpr int SCRATCH_BYTES = MAX_TASKS * PART_WORDS * 4 > N_EMBD * 4 ? MAX_TASKS * PART_WORDS * 4 : N_EMBD * 4;
 
@@ -35,6 +44,7 @@ struct Smem {
     uint64_t* wbar;  // [2][4]
     uint64_t* lmbar; // [4]
     int* flag;
+    LayerMeta* meta;   // [n_layer]
 };
 
 __device__ __forceinline__ void split_range(int n, int cta, int ncta, int& a, int& b) {
@@ -50,7 +60,8 @@ struct PhaseLayout {
 
 __device__ __forceinline__ uint32_t align16(uint32_t v) { return (v + 15u) & ~15u; }
 
-__device__ PhaseLayout phase_layout(const LayerDev& L, int kind, int cta, int ncta) {
+template <class LT>
+__device__ PhaseLayout phase_layout(const LT& L, int kind, int cta, int ncta) {
     PhaseLayout pl;
     for (int i = 0; i < 3; ++i) pl.row0[i] = pl.nrows[i] = 0, pl.off[i] = pl.bytes[i] = 0;
     int a, b;
@@ -91,7 +102,8 @@ __device__ const uint8_t* phase_src(const LayerDev& L, int kind, int i) {
     return L.wd;
 }
 
-__device__ int phase_type(const LayerDev& L, int kind, int i) {
+template <class LT>
+__device__ int phase_type(const LT& L, int kind, int i) {
     if (kind == 0) return i == 0 ? L.tq : i == 1 ? L.tk : L.tv;
     if (kind == 1) return L.to;
     if (kind == 2) return i == 0 ? L.tg : L.tu;
@@ -106,12 +118,13 @@ __device__ void issue_weight_phase(const DecodeParams& p, const Smem& s, int wp,
     uint64_t* bars = s.wbar + 4 * buf;
     const int l = wp >> 2, kind = wp & 3;
     const LayerDev& L = p.layers[l];
-    const PhaseLayout pl = phase_layout(L, kind, cta, ncta);
+    const LayerMeta& M = s.meta[l];
+    const PhaseLayout pl = phase_layout(M, kind, cta, ncta);
     const uint64_t pol = l2_evict_first_policy();
     for (int i = 0; i < 3; ++i) {
         mbar_expect_tx(&bars[i], pl.bytes[i]);
         if (pl.bytes[i]) {
-            const int rb = row_bytes(phase_type(L, kind, i), phase_cols(kind));
+            const int rb = row_bytes(phase_type(M, kind, i), phase_cols(kind));
             bulk_g2s_stream(s.wbuf[buf] + pl.off[i], phase_src(L, kind, i) + static_cast<size_t>(pl.row0[i]) * rb,
                             pl.bytes[i], &bars[i], pol);
         }
@@ -222,10 +235,10 @@ __device__ void prefetch_attention(const DecodeParams& p, int l, int cta) {
 }
 
 // L2 prefetch of layer l's two norm weight vectors (8 KB each), by CTA 0 only.
-__device__ void prefetch_norms(const DecodeParams& p, int l, int cta) {
+__device__ void prefetch_norms(const Smem& s, int l, int cta) {
     if (cta != 0) return;
-    bulk_prefetch_l2(p.layers[l].attn_norm, N_EMBD * 4);
-    bulk_prefetch_l2(p.layers[l].ffn_norm, N_EMBD * 4);
+    bulk_prefetch_l2(s.meta[l].attn_norm, N_EMBD * 4);
+    bulk_prefetch_l2(s.meta[l].ffn_norm, N_EMBD * 4);
 }
 
 // Waits for this CTA's part of weight phase wp; false on timeout.
@@ -312,7 +325,14 @@ __device__ void norm_quant(const float* x, const float* w, const Smem& s) {
 
 // ------------------------------------------------------------------------ phases
 __device__ void phase_qkv(const DecodeParams& p, const Smem& s, int l, int token, int cta, int ncta) {
-    const LayerDev& L = p.layers[l];
+    const LayerMeta& L = s.meta[l];
+    const int a = 2 * qkv_pair_boundary(L.tq, L.tk, L.tv, cta, ncta);   // same split as phase_layout
+    const int b = 2 * qkv_pair_boundary(L.tq, L.tk, L.tv, cta + 1, ncta);
+    // this thread's RoPE factors (pair pr = threadIdx.x), fetched before the norm
+    const int pr0 = threadIdx.x, R0 = a + 2 * pr0;
+    float2 cs0 = make_float2(0.0f, 0.0f);
+    if (pr0 < (b - a) / 2 && R0 < N_EMBD + KV_DIM)
+        cs0 = __ldg(p.rope + static_cast<size_t>(p.pos) * (HEAD_DIM / 2) + ((R0 & (HEAD_DIM - 1)) >> 1));
     if (l == 0) {
         embed_row(p, token, s.xs);
         __syncthreads();
@@ -327,8 +347,6 @@ __device__ void phase_qkv(const DecodeParams& p, const Smem& s, int l, int token
     trace_step(p, l, 0, 2);
     const PhaseLayout pl = phase_layout(L, 0, cta, ncta);
     const int lo[3] = {0, N_EMBD, N_EMBD + KV_DIM};
-    const int a = 2 * qkv_pair_boundary(L.tq, L.tk, L.tv, cta, ncta);   // same split as phase_layout
-    const int b = 2 * qkv_pair_boundary(L.tq, L.tk, L.tv, cta + 1, ncta);
     float* rv = s.rowval;
     for (int i = 0; i < 3; ++i) {
         if (pl.nrows[i] == 0) continue;   // uniform across the CTA
@@ -339,14 +357,14 @@ __device__ void phase_qkv(const DecodeParams& p, const Smem& s, int l, int token
     trace_step(p, l, 0, 3);
     // RoPE on Q/K pairs (interleaved, ops.cpp:502-516 with the build's FMA contraction),
     // then Q to the query buffer and K/V into the cache at pos (ops.cpp:557-563).
-    const float2* cs = p.rope + static_cast<size_t>(p.pos) * (HEAD_DIM / 2);
     float* kdst = p.kc + (static_cast<size_t>(l) * p.max_seq + p.pos) * KV_DIM;
     float* vdst = p.vc + (static_cast<size_t>(l) * p.max_seq + p.pos) * KV_DIM;
     for (int pr = threadIdx.x; pr < (b - a) / 2; pr += blockDim.x) {
         const int R = a + 2 * pr;
         const float v0 = rv[2 * pr], v1 = rv[2 * pr + 1];
         if (R < N_EMBD + KV_DIM) {
-            const float2 c = cs[(R & (HEAD_DIM - 1)) >> 1];
+            const float2 c = pr == pr0 ? cs0 : __ldg(p.rope + static_cast<size_t>(p.pos) * (HEAD_DIM / 2) +
+                                                     ((R & (HEAD_DIM - 1)) >> 1));
             const float r0 = __fmaf_rn(c.x, v0, -__fmul_rn(c.y, v1));
             const float r1 = __fmaf_rn(c.y, v0, __fmul_rn(c.x, v1));
             if (R < N_EMBD) {
@@ -709,7 +727,7 @@ __device__ void combine_attention(const DecodeParams& p, const Smem& s, int l, i
 }
 
 __device__ void phase_o(const DecodeParams& p, const Smem& s, int l, int cta, int ncta) {
-    const LayerDev& L = p.layers[l];
+    const LayerMeta& L = s.meta[l];
     const PhaseLayout pl = phase_layout(L, 1, cta, ncta);
     const int r0 = pl.row0[0], n = pl.nrows[0];
     const float xr = threadIdx.x < n ? __ldcg(p.x + r0 + threadIdx.x) : 0.0f;   // residual rows, early
@@ -726,7 +744,7 @@ __device__ void phase_o(const DecodeParams& p, const Smem& s, int l, int cta, in
 }
 
 __device__ void phase_gu(const DecodeParams& p, const Smem& s, int l, int cta, int ncta) {
-    const LayerDev& L = p.layers[l];
+    const LayerMeta& L = s.meta[l];
     norm_quant<true, false>(p.x, L.ffn_norm, s);
     trace_step(p, l, 3, 1);
     if (!wait_weights(p, s, 4 * l + 2)) return;
@@ -743,7 +761,7 @@ __device__ void phase_gu(const DecodeParams& p, const Smem& s, int l, int cta, i
 }
 
 __device__ void phase_down(const DecodeParams& p, const Smem& s, int l, int cta, int ncta) {
-    const LayerDev& L = p.layers[l];
+    const LayerMeta& L = s.meta[l];
     const PhaseLayout pl = phase_layout(L, 3, cta, ncta);
     const int r0 = pl.row0[0], n = pl.nrows[0];
     const float xr = threadIdx.x < n ? __ldcg(p.x + r0 + threadIdx.x) : 0.0f;   // residual rows, early
@@ -856,6 +874,19 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
     s.lmbar = reinterpret_cast<uint64_t*>(ptr);
     ptr += 4 * 8;
     s.flag = reinterpret_cast<int*>(ptr);
+    ptr += 16;
+    s.meta = reinterpret_cast<LayerMeta*>(ptr);
+    for (int i = threadIdx.x; i < p.n_layer; i += blockDim.x) {
+        const LayerDev& L = p.layers[i];
+        LayerMeta m;
+        m.attn_norm = L.attn_norm;
+        m.ffn_norm = L.ffn_norm;
+        m.tq = static_cast<uint8_t>(L.tq), m.tk = static_cast<uint8_t>(L.tk), m.tv = static_cast<uint8_t>(L.tv);
+        m.to = static_cast<uint8_t>(L.to), m.tg = static_cast<uint8_t>(L.tg), m.tu = static_cast<uint8_t>(L.tu);
+        m.td = static_cast<uint8_t>(L.td), m.pad = 0;
+        s.meta[i] = m;
+    }
+    __syncthreads();
 
     const int cta = blockIdx.x, ncta = gridDim.x;
     const int token = p.token >= 0 ? p.token : *reinterpret_cast<volatile int*>(p.token_dev);
@@ -872,7 +903,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
         fence_mbar_init();
         issue_weight_phase(p, s, 0, cta, ncta);
         prefetch_attention(p, 0, cta);
-        prefetch_norms(p, 0, cta);
+        prefetch_norms(s, 0, cta);
     }
     __syncthreads();
     trace_mark(p, 0);
@@ -902,7 +933,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
                     issue_lm_stage(p, s, lmq, 1);
                 } else {
                     prefetch_attention(p, l + 1, cta);
-                    prefetch_norms(p, l + 1, cta);
+                    prefetch_norms(s, l + 1, cta);
                 }
             }))
             return;
@@ -937,7 +968,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_attention(const DecodeParams
 size_t decode_smem_bytes() {
     size_t b = 2 * (WBUF_BYTES + WBUF_SLACK);
     b += (sizeof(XQSmem) + 127) & ~size_t(127);
-    b += SCRATCH_BYTES + ROWVAL_FLOATS * 4 + 32 * 4 + 12 * 8 + 16;
+    b += SCRATCH_BYTES + ROWVAL_FLOATS * 4 + 32 * 4 + 12 * 8 + 16 + MAX_LAYERS * sizeof(LayerMeta);
     return b;
 }
 
