@@ -54,17 +54,28 @@ def measured_peaks():
         return 6650.0, "fallback"
 
 
-def profiled_traffic():
-    """DRAM bytes per decode launch from the committed ncu summary, if present."""
+def profiled_traffic(avg_positions: float):
+    """DRAM bytes (read + write) per decode launch from the committed ncu summary.
+
+    The summary records one captured launch at `positions` attended positions; the K/V
+    cache read grows by KV_BYTES_PER_POSITION per position, so the figure is moved to the
+    benchmark's mean position by that amount (weights dominate: 1.41 GB vs 86 KB/position).
+    """
+    from mcpm import spec
     p = os.path.join(REPO, "profiles", "decode_kernel_traffic.txt")
+    vals = {}
     try:
         with open(p) as f:
             for line in f:
-                if line.startswith("bytes_per_launch"):
-                    return int(float(line.split("=")[1]))
-    except (OSError, ValueError):
-        pass
-    return None
+                if "=" in line and not line.startswith("#"):
+                    k, v = line.split("=", 1)
+                    vals[k.strip()] = v.strip()
+        b = float(vals["bytes_per_launch"])
+        if "positions" in vals:
+            b += (avg_positions - float(vals["positions"])) * spec.KV_BYTES_PER_POSITION
+        return int(b)
+    except (OSError, KeyError, ValueError):
+        return None
 
 
 class ClockSampler:
@@ -257,7 +268,7 @@ def main():
                        "parallelism": f"dp{world} (independent sequences)",
                        "l2": "inputs larger than L2 (1.41 GB of weights per token)"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": profiled_traffic(),
+                         "frac": round(achieved / peak, 4), "traffic": profiled_traffic(sum(n_pos) / len(n_pos)),
                          "peak_kind": peak_kind, "kernel": "k_decode",
                          "algorithmic_bytes_per_launch": int(bytes_per_tok)},
             "cpu_baseline": cb,
