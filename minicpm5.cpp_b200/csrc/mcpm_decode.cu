@@ -280,10 +280,42 @@ __device__ void embed_row(const DecodeParams& p, int token, float* xs) {
     }
 }
 
+// Reads x[tid + 256 i] (i < 8) from epoch-tagged words, polling until every word carries
+// `epoch` (written by the phase that produced x).  False after the 1 s bound.
+__device__ bool load8_epoch(const unsigned long long* src, unsigned epoch, int tid, float (&xv)[8], unsigned* err) {
+    unsigned long long w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w[i] = ld_epoch(src + tid + 256 * i);
+    unsigned pending = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) pending |= static_cast<unsigned>((w[i] >> 32) != epoch) << i;
+    if (pending) {
+        const uint64_t t0 = globaltimer();
+        while (pending) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (pending & (1u << i)) w[i] = ld_epoch(src + tid + 256 * i);
+            pending = 0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) pending |= static_cast<unsigned>((w[i] >> 32) != epoch) << i;
+            if (pending && globaltimer() - t0 > 1000000000ull) {
+                atomicOr(err, ERR_TIMEOUT);
+                return false;
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xv[i] = __uint_as_float(static_cast<unsigned>(w[i]));
+    return true;
+}
+
 // xq <- Q8_K of (x * w) * rms(x), canonical order; rounding per template argument.
-// FROM_SMEM: x already staged in s.xs; otherwise x is read from global (L2) and staged.
-template <bool AWAY, bool FROM_SMEM>
-__device__ void norm_quant(const float* x, const float* w, const Smem& s) {
+// SRC: X_SMEM (x already staged in s.xs), X_EPOCH (x published by the previous phase as
+// epoch-tagged words in p.xll; x is staged in s.xs).  False (for the whole CTA) when the
+// wait for x timed out.
+enum { X_SMEM = 1, X_EPOCH = 2 };
+template <bool AWAY, int SRC>
+__device__ bool norm_quant(const DecodeParams& p, const float* x, unsigned epoch, const float* w, const Smem& s) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     float4 w0 = make_float4(0.f, 0.f, 0.f, 0.f), w1 = w0;
     if (warp < N_EMBD / 256) {   // norm weights first: independent of x
@@ -291,13 +323,16 @@ __device__ void norm_quant(const float* x, const float* w, const Smem& s) {
         w1 = __ldg(reinterpret_cast<const float4*>(w + 256 * warp + 8 * lane + 4));
     }
     float* red = s.red;
+    bool ok = true;
     if (tid < 256) {
         float xv[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) xv[i] = FROM_SMEM ? x[tid + 256 * i] : __ldcg(x + tid + 256 * i);
-        if (!FROM_SMEM) {
+        if (SRC == X_EPOCH) {
+            ok = load8_epoch(p.xll, epoch, tid, xv, p.err);
 #pragma unroll
             for (int i = 0; i < 8; ++i) s.xs[tid + 256 * i] = xv[i];
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) xv[i] = x[tid + 256 * i];
         }
         float a = 0.0f;
 #pragma unroll
@@ -306,7 +341,7 @@ __device__ void norm_quant(const float* x, const float* w, const Smem& s) {
         for (int o = 16; o >= 1; o >>= 1) a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
         if (lane == 0) red[warp] = a;
     }
-    __syncthreads();
+    if (__syncthreads_or(!ok)) return false;
     if (warp < N_EMBD / 256) {
         const float ss = __fadd_rn(__fadd_rn(__fadd_rn(red[0], red[1]), __fadd_rn(red[2], red[3])),
                                    __fadd_rn(__fadd_rn(red[4], red[5]), __fadd_rn(red[6], red[7])));
@@ -321,10 +356,15 @@ __device__ void norm_quant(const float* x, const float* w, const Smem& s) {
         quant_block_warp<AWAY>(y, s.xq->qs[warp], &s.xq->d[warp], s.xq->bsums[warp]);
     }
     __syncthreads();
+    return true;
 }
 
+// Epoch of the residual published by layer l's o_proj (k = 2l+1) or down (k = 2l+2) in
+// launch `seq` (24 bits, never 0 after the host zeroes the words).
+__device__ __forceinline__ unsigned x_epoch(unsigned seq, int k) { return (seq << 8) | static_cast<unsigned>(k); }
+
 // ------------------------------------------------------------------------ phases
-__device__ void phase_qkv(const DecodeParams& p, const Smem& s, int l, int token, int cta, int ncta) {
+__device__ bool phase_qkv(const DecodeParams& p, const Smem& s, int l, int token, int cta, int ncta, unsigned seq) {
     const LayerMeta& L = s.meta[l];
     const int a = 2 * qkv_pair_boundary(L.tq, L.tk, L.tv, cta, ncta);   // same split as phase_layout
     const int b = 2 * qkv_pair_boundary(L.tq, L.tk, L.tv, cta + 1, ncta);
@@ -338,12 +378,13 @@ __device__ void phase_qkv(const DecodeParams& p, const Smem& s, int l, int token
         __syncthreads();
         if (cta == 0)
             for (int i = threadIdx.x; i < N_EMBD; i += blockDim.x) p.x[i] = s.xs[i];
-        norm_quant<true, true>(s.xs, L.attn_norm, s);
+        norm_quant<true, X_SMEM>(p, s.xs, 0, L.attn_norm, s);
     } else {
-        norm_quant<true, false>(p.x, L.attn_norm, s);
+        if (!norm_quant<true, X_EPOCH>(p, nullptr, x_epoch(seq, 2 * l), L.attn_norm, s)) return false;
+        trace_mark(p, 3 + 2 * (5 * (l - 1) + 4));
     }
     trace_step(p, l, 0, 1);
-    if (!wait_weights(p, s, 4 * l)) return;
+    if (!wait_weights(p, s, 4 * l)) return false;
     trace_step(p, l, 0, 2);
     const PhaseLayout pl = phase_layout(L, 0, cta, ncta);
     const int lo[3] = {0, N_EMBD, N_EMBD + KV_DIM};
@@ -379,6 +420,7 @@ __device__ void phase_qkv(const DecodeParams& p, const Smem& s, int l, int token
             vdst[R - N_EMBD - KV_DIM + 1] = v1;
         }
     }
+    return true;
 }
 
 // Canonical q.k over 128 dims by an 8-lane group (lane j: dims 4j + 32i + c, then the
@@ -726,7 +768,9 @@ __device__ void combine_attention(const DecodeParams& p, const Smem& s, int l, i
     __syncthreads();
 }
 
-__device__ void phase_o(const DecodeParams& p, const Smem& s, int l, int cta, int ncta) {
+// o_proj + residual; the new residual rows are published as epoch-tagged words (k = 2l+1)
+// and the down weights are issued into the buffer this phase just released.
+__device__ bool phase_o(const DecodeParams& p, const Smem& s, int l, int cta, int ncta, unsigned seq) {
     const LayerMeta& L = s.meta[l];
     const PhaseLayout pl = phase_layout(L, 1, cta, ncta);
     const int r0 = pl.row0[0], n = pl.nrows[0];
@@ -736,18 +780,25 @@ __device__ void phase_o(const DecodeParams& p, const Smem& s, int l, int cta, in
     else
         load_q8k_blocks(p.att_q8k, N_EMBD / 256, s);
     trace_step(p, l, 2, 1);
-    if (!wait_weights(p, s, 4 * l + 1)) return;
+    if (!wait_weights(p, s, 4 * l + 1)) return false;
     trace_step(p, l, 2, 2);
     gemv_rows(L.to, s.wbuf[1], n, N_EMBD / 256, *s.xq, s.part, MAX_TASKS, s.rowval,
               (p.trace && l == 1 && cta == 0) ? p.trace + TRACE_DETAIL + 60 : nullptr);
-    if (threadIdx.x < n) p.x[r0 + threadIdx.x] = __fadd_rn(xr, s.rowval[threadIdx.x]);
+    if (threadIdx.x < n) {
+        const float xn = __fadd_rn(xr, s.rowval[threadIdx.x]);
+        p.x[r0 + threadIdx.x] = xn;
+        st_epoch(p.xll + r0 + threadIdx.x, xn, x_epoch(seq, 2 * l + 1));
+    }
+    if (threadIdx.x == 0) issue_weight_phase(p, s, 4 * l + 3, cta, ncta);
+    return true;
 }
 
-__device__ void phase_gu(const DecodeParams& p, const Smem& s, int l, int cta, int ncta) {
+__device__ bool phase_gu(const DecodeParams& p, const Smem& s, int l, int cta, int ncta, unsigned seq) {
     const LayerMeta& L = s.meta[l];
-    norm_quant<true, false>(p.x, L.ffn_norm, s);
+    if (!norm_quant<true, X_EPOCH>(p, nullptr, x_epoch(seq, 2 * l + 1), L.ffn_norm, s)) return false;
+    trace_mark(p, 3 + 2 * (5 * l + 2));
     trace_step(p, l, 3, 1);
-    if (!wait_weights(p, s, 4 * l + 2)) return;
+    if (!wait_weights(p, s, 4 * l + 2)) return false;
     trace_step(p, l, 3, 2);
     const PhaseLayout pl = phase_layout(L, 2, cta, ncta);
     const int n = pl.nrows[0];
@@ -758,9 +809,13 @@ __device__ void phase_gu(const DecodeParams& p, const Smem& s, int l, int cta, i
     gemv_rows(L.tu, s.wbuf[0] + pl.off[1], n, N_EMBD / 256, *s.xq, s.part, MAX_TASKS, rv + 128);
     trace_step(p, l, 3, 4);
     for (int r = threadIdx.x; r < n; r += blockDim.x) p.h[pl.row0[0] + r] = canon_silu_mul(rv[r], rv[128 + r]);
+    return true;
 }
 
-__device__ void phase_down(const DecodeParams& p, const Smem& s, int l, int cta, int ncta) {
+// down + residual; the new residual rows are published as epoch-tagged words (k = 2l+2);
+// then the next layer's K/V and norm prefetches (or the LM head's second stage).
+__device__ bool phase_down(const DecodeParams& p, const Smem& s, int l, int cta, int ncta, unsigned seq,
+                           const LmPlan& lmq) {
     const LayerMeta& L = s.meta[l];
     const PhaseLayout pl = phase_layout(L, 3, cta, ncta);
     const int r0 = pl.row0[0], n = pl.nrows[0];
@@ -774,16 +829,30 @@ __device__ void phase_down(const DecodeParams& p, const Smem& s, int l, int cta,
     }
     __syncthreads();
     trace_step(p, l, 4, 1);
-    if (!wait_weights(p, s, 4 * l + 3)) return;
+    if (!wait_weights(p, s, 4 * l + 3)) return false;
     trace_step(p, l, 4, 2);
     gemv_rows(L.td, s.wbuf[1], n, N_FF / 256, *s.xq, s.part, MAX_TASKS, s.rowval,
               (p.trace && l == 1 && cta == 0) ? p.trace + TRACE_DETAIL + 62 : nullptr);
-    if (threadIdx.x < n) p.x[r0 + threadIdx.x] = __fadd_rn(xr, s.rowval[threadIdx.x]);
+    if (threadIdx.x < n) {
+        const float xn = __fadd_rn(xr, s.rowval[threadIdx.x]);
+        p.x[r0 + threadIdx.x] = xn;
+        st_epoch(p.xll + r0 + threadIdx.x, xn, x_epoch(seq, 2 * l + 2));
+    }
+    if (threadIdx.x == 0) {
+        if (l + 1 == p.n_layer) {
+            issue_lm_stage(p, s, lmq, 1);
+        } else {
+            prefetch_attention(p, l + 1, cta);
+            prefetch_norms(s, l + 1, cta);
+        }
+    }
+    return true;
 }
 
-__device__ void phase_lm(const DecodeParams& p, const Smem& s, int cta, int ncta) {
+__device__ void phase_lm(const DecodeParams& p, const Smem& s, int cta, int ncta, unsigned seq) {
     const LmPlan q = lm_plan(p, cta, ncta);
-    norm_quant<false, false>(p.x, p.out_norm, s);
+    if (!norm_quant<false, X_EPOCH>(p, nullptr, x_epoch(seq, 2 * p.n_layer), p.out_norm, s)) return;
+    trace_mark(p, 3 + 2 * (5 * (p.n_layer - 1) + 4));
     trace_step(p, 1, 5, 1);   // rmsnorm (ops.cpp:468-481) + quantize_row_q8_K_avx2
     float best = -__int_as_float(0x7f800000);
     int besti = 0x7fffffff;
@@ -896,6 +965,8 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
     }
     BarState bs;
     bs.base = *reinterpret_cast<volatile unsigned*>(p.bar + 1);
+    unsigned seq = (*reinterpret_cast<volatile unsigned*>(p.bar + 2) + 1u) & 0xffffffu;   // epochs of xll
+    if (seq == 0) seq = 1;
     bs.idx = 0;
     if (threadIdx.x == 0) {
         for (int i = 0; i < 8; ++i) mbar_init(&s.wbar[i], 1);
@@ -911,13 +982,15 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
     // Weight phase w+1 is issued while waiting at the barrier in front of phase w: its
     // buffer was last used by phase w-1, which every thread of this CTA has finished.
     for (int l = 0; l < p.n_layer; ++l) {
-        phase_qkv(p, s, l, token, cta, ncta);
+        if (!phase_qkv(p, s, l, token, cta, ncta, seq)) return;
         if (!traced_barrier(p, bs, 5 * l, [&] { issue_weight_phase(p, s, 4 * l + 1, cta, ncta); })) return;
         phase_attention(p, s, l, cta, ncta, attn_chunks(p.pos + 1) > DIST_COMBINE_MAX);
         if (!traced_barrier(p, bs, 5 * l + 1, [&] { issue_weight_phase(p, s, 4 * l + 2, cta, ncta); })) return;
-        phase_o(p, s, l, cta, ncta);
-        if (!traced_barrier(p, bs, 5 * l + 2, [&] { issue_weight_phase(p, s, 4 * l + 3, cta, ncta); })) return;
-        phase_gu(p, s, l, cta, ncta);
+        // o_proj -> gate/up and down -> next QKV exchange the residual through epoch-tagged
+        // words: no grid barrier (every consumer needs all of x, which orders all reuse).
+        if (!phase_o(p, s, l, cta, ncta, seq)) return;
+        trace_mark(p, 2 + 2 * (5 * l + 2));
+        if (!phase_gu(p, s, l, cta, ncta, seq)) return;
         if (!traced_barrier(p, bs, 5 * l + 3, [&] {
                 if (l + 1 < p.n_layer) {
                     issue_weight_phase(p, s, 4 * (l + 1), cta, ncta);
@@ -927,19 +1000,14 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
                 }
             }))
             return;
-        phase_down(p, s, l, cta, ncta);
-        if (!traced_barrier(p, bs, 5 * l + 4, [&] {
-                if (l + 1 == p.n_layer) {
-                    issue_lm_stage(p, s, lmq, 1);
-                } else {
-                    prefetch_attention(p, l + 1, cta);
-                    prefetch_norms(s, l + 1, cta);
-                }
-            }))
-            return;
+        if (!phase_down(p, s, l, cta, ncta, seq, lmq)) return;
+        trace_mark(p, 2 + 2 * (5 * l + 4));
     }
-    if (cta == 0 && threadIdx.x == 0) p.bar[1] = bs.base + bs.idx * gridDim.x;   // next launch's base
-    phase_lm(p, s, cta, ncta);
+    if (cta == 0 && threadIdx.x == 0) {
+        p.bar[1] = bs.base + bs.idx * gridDim.x;   // next launch's barrier base
+        p.bar[2] = seq;                            // next launch uses seq + 1
+    }
+    phase_lm(p, s, cta, ncta, seq);
     trace_mark(p, 2 + 2 * (5 * p.n_layer));
 }
 

@@ -105,6 +105,18 @@ __device__ __forceinline__ float ld_cg_f32(const float* p) {
     asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p));
     return v;
 }
+// Epoch-tagged element (value + epoch in one naturally aligned 64-bit word, which is
+// single-copy atomic): the consumer's load is also its synchronisation, with no fence on
+// the producer side and no separate flag round trip.
+__device__ __forceinline__ void st_epoch(unsigned long long* p, float v, unsigned epoch) {
+    const unsigned long long w = (static_cast<unsigned long long>(epoch) << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_epoch(const unsigned long long* p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
 __device__ __forceinline__ uint32_t ld_acquire_u32(const unsigned* p) {
     uint32_t v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");

@@ -51,6 +51,7 @@ struct mcpm_engine {
     int max_seq = 0;
     float2* rope = nullptr;
     float *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr, *att_part = nullptr, *logits = nullptr;
+    unsigned long long* xll = nullptr;   // residual stream with per-element epochs
     float* am_val = nullptr;
     int* am_idx = nullptr;
     uint8_t* att_q8k = nullptr;
@@ -94,6 +95,7 @@ void free_model(mcpm_engine* e) {
     free_dev(e->q);
     free_dev(e->att);
     free_dev(e->h);
+    free_dev(e->xll);
     free_dev(e->att_part);
     free_dev(e->logits);
     free_dev(e->am_val);
@@ -162,6 +164,8 @@ bool phases_fit(const mcpm_engine* e, int n, std::string& why) {
 
 mcpm_status reset_ctl(mcpm_engine* e) {
     MCPM_CUDA(cudaMemsetAsync(e->ctl, 0, CTL_WORDS * sizeof(int), e->stream));
+    // the launch sequence restarts, so no epoch of an aborted launch may remain
+    if (e->xll) MCPM_CUDA(cudaMemsetAsync(e->xll, 0, N_EMBD * sizeof(unsigned long long), e->stream));
     MCPM_CUDA(cudaStreamSynchronize(e->stream));
     return MCPM_OK;
 }
@@ -197,6 +201,7 @@ DecodeParams make_params(const mcpm_engine* e, int token, int pos, int write_log
     p.att = e->att;
     p.att_q8k = e->att_q8k;
     p.h = e->h;
+    p.xll = e->xll;
     p.att_part = e->att_part;
     p.logits = e->logits;
     p.am_val = e->am_val;
@@ -413,6 +418,8 @@ mcpm_status mcpm_load_gguf(mcpm_engine* e, const char* path) {
     MCPM_CUDA(cudaMalloc(&e->q, N_EMBD * 4));
     MCPM_CUDA(cudaMalloc(&e->att, N_EMBD * 4));
     MCPM_CUDA(cudaMalloc(&e->h, N_FF * 4));
+    MCPM_CUDA(cudaMalloc(&e->xll, N_EMBD * sizeof(unsigned long long)));
+    MCPM_CUDA(cudaMemset(e->xll, 0, N_EMBD * sizeof(unsigned long long)));
     MCPM_CUDA(cudaMalloc(&e->att_part, sizeof(float) * N_HEAD * ATT_MAX_CHUNKS * ATT_PART_STRIDE));
     MCPM_CUDA(cudaMalloc(&e->logits, sizeof(float) * e->n_vocab));
     MCPM_CUDA(cudaMalloc(&e->am_val, sizeof(float) * e->n_ctas));

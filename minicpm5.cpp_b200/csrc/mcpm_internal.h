@@ -67,13 +67,14 @@ struct DecodeParams {
     float* att;         // attention output [N_EMBD] (fp32, for inspection)
     uint8_t* att_q8k;   // attention output as 8 block_q8_K
     float* h;           // SwiGLU output [N_FF]
+    unsigned long long* xll;   // residual stream published per element as (epoch << 32) | fp32 bits [N_EMBD]
     float* att_part;    // [N_HEAD][ATT_MAX_CHUNKS][ATT_PART_STRIDE]
     float* logits;      // [n_vocab]
     float* am_val;      // per-CTA argmax partials
     int* am_idx;
     int* argmax_out;
     int* token_dev;     // token id for the next step (greedy chaining)
-    unsigned* bar;      // grid barrier {count, generation}
+    unsigned* bar;      // grid barrier {count, base}, [2] launch sequence (epochs of xll)
     unsigned* cnt;      // [0..1] attention combine counters, [2] argmax counter
     unsigned* err;      // error bits
     unsigned long long* trace;   // optional: CTA 0 phase timestamps (2 per phase + 2)
