@@ -26,10 +26,13 @@ namespace {
 // kernel start: a field read from global memory costs a full L2 round trip there
 // (the L1 is almost all carved out for shared memory).
 struct LayerMeta {
-    const float* attn_norm;
-    const float* ffn_norm;
+    uint32_t w[7];                  // arena offsets of wq, wk, wv, wo, wg, wu, wd
+    uint32_t attn_norm, ffn_norm;   // arena offsets of the norm weights
     uint8_t tq, tk, tv, to, tg, tu, td, pad;
 };
+__device__ __forceinline__ const float* meta_f32(const DecodeParams& p, uint32_t off) {
+    return reinterpret_cast<const float*>(p.arena + off);
+}
 
 // GEMV partials and the staged fp32 activation share one scratch region.
 constexpr int SCRATCH_BYTES = MAX_TASKS * PART_WORDS * 4 > N_EMBD * 4 ? MAX_TASKS * PART_WORDS * 4 : N_EMBD * 4;
@@ -95,11 +98,9 @@ __device__ PhaseLayout phase_layout(const LT& L, int kind, int cta, int ncta) {
     return pl;
 }
 
-__device__ const uint8_t* phase_src(const LayerDev& L, int kind, int i) {
-    if (kind == 0) return i == 0 ? L.wq : i == 1 ? L.wk : L.wv;
-    if (kind == 1) return L.wo;
-    if (kind == 2) return i == 0 ? L.wg : L.wu;
-    return L.wd;
+__device__ const uint8_t* phase_src(const DecodeParams& p, const LayerMeta& M, int kind, int i) {
+    const int k = kind == 0 ? i : kind == 1 ? 3 : kind == 2 ? 4 + i : 6;
+    return p.arena + M.w[k];
 }
 
 template <class LT>
@@ -117,7 +118,6 @@ __device__ void issue_weight_phase(const DecodeParams& p, const Smem& s, int wp,
     const int buf = wp & 1;
     uint64_t* bars = s.wbar + 4 * buf;
     const int l = wp >> 2, kind = wp & 3;
-    const LayerDev& L = p.layers[l];
     const LayerMeta& M = s.meta[l];
     const PhaseLayout pl = phase_layout(M, kind, cta, ncta);
     const uint64_t pol = l2_evict_first_policy();
@@ -125,7 +125,7 @@ __device__ void issue_weight_phase(const DecodeParams& p, const Smem& s, int wp,
         mbar_expect_tx(&bars[i], pl.bytes[i]);
         if (pl.bytes[i]) {
             const int rb = row_bytes(phase_type(M, kind, i), phase_cols(kind));
-            bulk_g2s_stream(s.wbuf[buf] + pl.off[i], phase_src(L, kind, i) + static_cast<size_t>(pl.row0[i]) * rb,
+            bulk_g2s_stream(s.wbuf[buf] + pl.off[i], phase_src(p, M, kind, i) + static_cast<size_t>(pl.row0[i]) * rb,
                             pl.bytes[i], &bars[i], pol);
         }
     }
@@ -235,10 +235,10 @@ __device__ void prefetch_attention(const DecodeParams& p, int l, int cta) {
 }
 
 // L2 prefetch of layer l's two norm weight vectors (8 KB each), by CTA 0 only.
-__device__ void prefetch_norms(const Smem& s, int l, int cta) {
+__device__ void prefetch_norms(const DecodeParams& p, const Smem& s, int l, int cta) {
     if (cta != 0) return;
-    bulk_prefetch_l2(s.meta[l].attn_norm, N_EMBD * 4);
-    bulk_prefetch_l2(s.meta[l].ffn_norm, N_EMBD * 4);
+    bulk_prefetch_l2(meta_f32(p, s.meta[l].attn_norm), N_EMBD * 4);
+    bulk_prefetch_l2(meta_f32(p, s.meta[l].ffn_norm), N_EMBD * 4);
 }
 
 // Waits for this CTA's part of weight phase wp; false on timeout.
@@ -378,9 +378,9 @@ __device__ bool phase_qkv(const DecodeParams& p, const Smem& s, int l, int token
         __syncthreads();
         if (cta == 0)
             for (int i = threadIdx.x; i < N_EMBD; i += blockDim.x) p.x[i] = s.xs[i];
-        norm_quant<true, X_SMEM>(p, s.xs, 0, L.attn_norm, s);
+        norm_quant<true, X_SMEM>(p, s.xs, 0, meta_f32(p, L.attn_norm), s);
     } else {
-        if (!norm_quant<true, X_EPOCH>(p, nullptr, x_epoch(seq, 2 * l), L.attn_norm, s)) return false;
+        if (!norm_quant<true, X_EPOCH>(p, nullptr, x_epoch(seq, 2 * l), meta_f32(p, L.attn_norm), s)) return false;
         trace_mark(p, 3 + 2 * (5 * (l - 1) + 4));
     }
     trace_step(p, l, 0, 1);
@@ -520,8 +520,9 @@ __device__ void attention_unit32(const DecodeParams& p, const Smem& s, int l, in
         for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         const float pr = lane < np ? canon_expf(__fsub_rn(v, m)) : 0.0f;
         if (lane < np) sc[warp * 32 + lane] = pr;
-        float sum = 0.0f;
-        for (int t = 0; t < np; ++t) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, pr, t));
+        float sum = pr;   // canonical chunk sum: lane sums (one position each here), then a butterfly
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
         if (lane == 0) stat[warp] = m, stat[8 + warp] = sum;
     }
     cp_async_wait_all();
@@ -603,9 +604,12 @@ __device__ void phase_attention(const DecodeParams& p, const Smem& s, int l, int
                 for (int t = lane; t < np; t += 32)
                     sc[warp * ATT_SC_STRIDE + t] = canon_expf(__fsub_rn(sc[warp * ATT_SC_STRIDE + t], m));
                 __syncwarp();
+                // canonical chunk sum: lane sums over t = lane (mod 32) in order, then a butterfly
+                float sum = 0.0f;
+                for (int t = lane; t < np; t += 32) sum = __fadd_rn(sum, sc[warp * ATT_SC_STRIDE + t]);
+#pragma unroll
+                for (int o = 16; o >= 1; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
                 if (lane == 0) {
-                    float sum = 0.0f;
-                    for (int t = 0; t < np; ++t) sum = __fadd_rn(sum, sc[warp * ATT_SC_STRIDE + t]);
                     stat[warp] = m;
                     stat[8 + warp] = sum;
                 }
@@ -795,7 +799,7 @@ __device__ bool phase_o(const DecodeParams& p, const Smem& s, int l, int cta, in
 
 __device__ bool phase_gu(const DecodeParams& p, const Smem& s, int l, int cta, int ncta, unsigned seq) {
     const LayerMeta& L = s.meta[l];
-    if (!norm_quant<true, X_EPOCH>(p, nullptr, x_epoch(seq, 2 * l + 1), L.ffn_norm, s)) return false;
+    if (!norm_quant<true, X_EPOCH>(p, nullptr, x_epoch(seq, 2 * l + 1), meta_f32(p, L.ffn_norm), s)) return false;
     trace_mark(p, 3 + 2 * (5 * l + 2));
     trace_step(p, l, 3, 1);
     if (!wait_weights(p, s, 4 * l + 2)) return false;
@@ -843,7 +847,7 @@ __device__ bool phase_down(const DecodeParams& p, const Smem& s, int l, int cta,
             issue_lm_stage(p, s, lmq, 1);
         } else {
             prefetch_attention(p, l + 1, cta);
-            prefetch_norms(s, l + 1, cta);
+            prefetch_norms(p, s, l + 1, cta);
         }
     }
     return true;
@@ -948,8 +952,10 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
     for (int i = threadIdx.x; i < p.n_layer; i += blockDim.x) {
         const LayerDev& L = p.layers[i];
         LayerMeta m;
-        m.attn_norm = L.attn_norm;
-        m.ffn_norm = L.ffn_norm;
+        const uint8_t* const wp[7] = {L.wq, L.wk, L.wv, L.wo, L.wg, L.wu, L.wd};
+        for (int k = 0; k < 7; ++k) m.w[k] = static_cast<uint32_t>(wp[k] - p.arena);
+        m.attn_norm = static_cast<uint32_t>(reinterpret_cast<const uint8_t*>(L.attn_norm) - p.arena);
+        m.ffn_norm = static_cast<uint32_t>(reinterpret_cast<const uint8_t*>(L.ffn_norm) - p.arena);
         m.tq = static_cast<uint8_t>(L.tq), m.tk = static_cast<uint8_t>(L.tk), m.tv = static_cast<uint8_t>(L.tv);
         m.to = static_cast<uint8_t>(L.to), m.tg = static_cast<uint8_t>(L.tg), m.tu = static_cast<uint8_t>(L.tu);
         m.td = static_cast<uint8_t>(L.td), m.pad = 0;
@@ -974,7 +980,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
         fence_mbar_init();
         issue_weight_phase(p, s, 0, cta, ncta);
         prefetch_attention(p, 0, cta);
-        prefetch_norms(s, 0, cta);
+        prefetch_norms(p, s, 0, cta);
     }
     __syncthreads();
     trace_mark(p, 0);

@@ -185,6 +185,7 @@ mcpm_status check_ctl(mcpm_engine* e) {
 DecodeParams make_params(const mcpm_engine* e, int token, int pos, int write_logits) {
     DecodeParams p{};
     p.layers = e->d_layers;
+    p.arena = e->arena;
     p.n_layer = e->n_layer;
     p.embd = e->embd;
     p.embd_type = e->embd_type;
@@ -327,6 +328,10 @@ mcpm_status mcpm_load_gguf(mcpm_engine* e, const char* path) {
     }
     e->arena_base = lo;
     e->arena_bytes = hi - lo;
+    if (e->arena_bytes >= (1ull << 32)) {   // the decode kernel addresses tensors by 32-bit arena offsets
+        std::fprintf(stderr, "[mcpm] weight arena of %llu bytes exceeds 4 GiB\n", (unsigned long long)e->arena_bytes);
+        return MCPM_UNSUPPORTED_TYPE;
+    }
     MCPM_CUDA(cudaMalloc(&e->arena, e->arena_bytes + 256));
     {
         std::unique_ptr<FILE, int (*)(FILE*)> f(std::fopen(path, "rb"), &std::fclose);

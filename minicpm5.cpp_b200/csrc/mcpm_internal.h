@@ -51,6 +51,7 @@ struct LayerDev {
 
 struct DecodeParams {
     const LayerDev* layers;
+    const uint8_t* arena;   // base of the weight arena (LayerDev pointers point into it)
     int n_layer;
     const uint8_t* embd;
     int embd_type;

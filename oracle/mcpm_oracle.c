@@ -441,7 +441,8 @@ static float dot128(const float* q, const float* k) {
 
 /* execute_attention (ops.cpp:537-628): appends k, v at pos, then softmax(q.k/sqrt(d)).V
  * per head over positions 0..pos in chunks of orc_attn_chunk(pos+1):
- *   per chunk: m = max s, p_t = exp(s_t - m), l = sum p_t (position order),
+ *   per chunk: m = max s, p_t = exp(s_t - m), l = sum p_t (32 lane sums over
+ *              t = lane mod 32 in position order, then a 32-lane butterfly),
  *              o[d] = fma chain over t of p_t*v_t[d];
  *   combine:   M = max m_c, w_c = exp(m_c - M), L = fma chain of w_c*l_c,
  *              O[d] = fma chain of w_c*o_c[d] (chunk order), out = O * (1/L). */
@@ -467,11 +468,21 @@ int orc_attention(float* out, const float* q, const float* k, const float* v, fl
                 pt[t - t0] = dot128(qh, kc + (size_t)t * kvd + g * head_dim) * scale;
                 if (pt[t - t0] > m) m = pt[t - t0];
             }
-            float l = 0.0f;
-            for (int t = t0; t < t1; ++t) {
-                pt[t - t0] = orc_expf(pt[t - t0] - m);
-                l = l + pt[t - t0];
+            for (int t = t0; t < t1; ++t) pt[t - t0] = orc_expf(pt[t - t0] - m);
+            /* chunk sum: 32 lane sums over positions t = lane (mod 32) in order, then a
+               butterfly over lane bits 4..0 (every lane ends with the same value) */
+            float lane_sum[32];
+            for (int ln = 0; ln < 32; ++ln) {
+                float a = 0.0f;
+                for (int t = t0 + ln; t < t1; t += 32) a = a + pt[t - t0];
+                lane_sum[ln] = a;
             }
+            for (int o = 16; o >= 1; o >>= 1) {
+                float nx[32];
+                for (int ln = 0; ln < 32; ++ln) nx[ln] = lane_sum[ln] + lane_sum[ln ^ o];
+                memcpy(lane_sum, nx, sizeof(nx));
+            }
+            const float l = lane_sum[0];
             for (int d = 0; d < 128; ++d) {
                 float o = 0.0f;
                 for (int t = t0; t < t1; ++t) o = fmaf(pt[t - t0], vc[(size_t)t * kvd + g * head_dim + d], o);
