@@ -359,6 +359,9 @@ __device__ bool norm_quant(const DecodeParams& p, const float* x, unsigned epoch
     return true;
 }
 
+// Epoch of layer l's q and K/V rows in p.qll (own buffer, so the same numbering is free).
+__device__ __forceinline__ unsigned qkv_epoch(unsigned seq, int l) { return (seq << 8) | static_cast<unsigned>(l + 1); }
+
 // Epoch of the residual published by layer l's o_proj (k = 2l+1) or down (k = 2l+2) in
 // launch `seq` (24 bits, never 0 after the host zeroes the words).
 __device__ __forceinline__ unsigned x_epoch(unsigned seq, int k) { return (seq << 8) | static_cast<unsigned>(k); }
@@ -415,9 +418,13 @@ __device__ bool phase_qkv(const DecodeParams& p, const Smem& s, int l, int token
                 kdst[R - N_EMBD] = r0;
                 kdst[R - N_EMBD + 1] = r1;
             }
+            st_epoch(p.qll + R, r0, qkv_epoch(seq, l));
+            st_epoch(p.qll + R + 1, r1, qkv_epoch(seq, l));
         } else {
             vdst[R - N_EMBD - KV_DIM] = v0;
             vdst[R - N_EMBD - KV_DIM + 1] = v1;
+            st_epoch(p.qll + R, v0, qkv_epoch(seq, l));
+            st_epoch(p.qll + R + 1, v1, qkv_epoch(seq, l));
         }
     }
     return true;
@@ -458,29 +465,71 @@ __device__ __forceinline__ int attn_chunks(int n) {
 // dims 4j + 32i + c of each dot (the canonical 8-lane split of dot128_group).
 // Same numerics as the general path below: scores, chunk max, exp, position-ordered
 // sum and fma chains, partials [head][chunk][m, l, o[128]].
-__device__ void attention_unit32(const DecodeParams& p, const Smem& s, int l, int g, int c, int t0, int np) {
+// In the decode kernel (p.qll set) q and this position's K/V rows are read from their
+// epoch-tagged copies, so no grid barrier separates the QKV phase from attention.
+__device__ void attention_unit32(const DecodeParams& p, const Smem& s, int l, int g, int c, int t0, int np,
+                                 unsigned seq) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, j = lane & 7, G = lane >> 3;
     float* vb = reinterpret_cast<float*>(s.wbuf[0]);   // [32][128] V rows of the chunk
     float* sc = vb + 32 * HEAD_DIM;                     // [8][32] scores -> probabilities
     float* stat = sc + 8 * 32;                          // m[8], l[8]
+    float* qsm = stat + 32;                             // [8][128] q of the group (epoch path)
+    float* krow = qsm + 8 * HEAD_DIM;                   // [128] K row at pos (epoch path)
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(HEAD_DIM)));
     const float* kl = p.kc + static_cast<size_t>(l) * p.max_seq * KV_DIM + g * HEAD_DIM;
     const float* vl = p.vc + static_cast<size_t>(l) * p.max_seq * KV_DIM + g * HEAD_DIM;
-    for (int i = tid; i < np * 32; i += blockDim.x)
+    const bool epoch_in = p.qll != nullptr;
+    const int cur = epoch_in && t0 + np - 1 == p.pos ? np - 1 : -1;   // chunk row published this launch
+    const int ncache = cur >= 0 ? np - 1 : np;                         // rows read from the cache
+    for (int i = tid; i < ncache * 32; i += blockDim.x)
         cp_async16(vb + 4 * i, vl + static_cast<size_t>(t0 + (i >> 5)) * KV_DIM + 4 * (i & 31));
     cp_async_commit();
     const int tA = 2 * warp, tB = tA + 1;
     const bool va = tA < np, vbv = tB < np;
-    const float* q0 = p.q + (8 * g + 2 * G) * HEAD_DIM + 4 * j;
-    const float* kA = kl + static_cast<size_t>(t0 + (va ? tA : 0)) * KV_DIM + 4 * j;
-    const float* kB = kl + static_cast<size_t>(t0 + (vbv ? tB : 0)) * KV_DIM + 4 * j;
+    const float* kA = kl + static_cast<size_t>(t0 + (va && tA != cur ? tA : 0)) * KV_DIM + 4 * j;
+    const float* kB = kl + static_cast<size_t>(t0 + (vbv && tB != cur ? tB : 0)) * KV_DIM + 4 * j;
     float4 qa[4], qb[4], ka[4], kb[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        qa[i] = ld_cg_f4(q0 + 32 * i);
-        qb[i] = ld_cg_f4(q0 + HEAD_DIM + 32 * i);
+    for (int i = 0; i < 4; ++i) {   // cached K rows first: their loads overlap the waits below
         ka[i] = ld_cg_f4(kA + 32 * i);
         kb[i] = ld_cg_f4(kB + 32 * i);
+    }
+    if (epoch_in) {
+        const unsigned ep = qkv_epoch(seq, l);
+        bool ok = true;
+        if (tid < 256) {
+            float4 v;
+            ok = load4_epoch(p.qll + 8 * g * HEAD_DIM + 4 * tid, ep, v, p.err);
+            reinterpret_cast<float4*>(qsm)[tid] = v;
+        } else if (cur >= 0 && tid < 256 + 32) {
+            float4 v;
+            ok = load4_epoch(p.qll + N_EMBD + g * HEAD_DIM + 4 * (tid - 256), ep, v, p.err);
+            reinterpret_cast<float4*>(krow)[tid - 256] = v;
+        } else if (cur >= 0 && tid < 256 + 64) {
+            float4 v;
+            ok = load4_epoch(p.qll + N_EMBD + KV_DIM + g * HEAD_DIM + 4 * (tid - 288), ep, v, p.err);
+            reinterpret_cast<float4*>(vb + cur * HEAD_DIM)[tid - 288] = v;
+        }
+        if (__syncthreads_or(!ok)) {
+            cp_async_wait_all();
+            return;   // ERR_TIMEOUT is set; the next grid barrier stops every CTA
+        }
+        trace_mark(p, 3 + 2 * (5 * l));   // inputs of this unit published
+        const float* q0 = qsm + (2 * G) * HEAD_DIM + 4 * j;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            qa[i] = *reinterpret_cast<const float4*>(q0 + 32 * i);
+            qb[i] = *reinterpret_cast<const float4*>(q0 + HEAD_DIM + 32 * i);
+            if (tA == cur) ka[i] = *reinterpret_cast<const float4*>(krow + 4 * j + 32 * i);
+            if (tB == cur) kb[i] = *reinterpret_cast<const float4*>(krow + 4 * j + 32 * i);
+        }
+    } else {
+        const float* q0 = p.q + (8 * g + 2 * G) * HEAD_DIM + 4 * j;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            qa[i] = ld_cg_f4(q0 + 32 * i);
+            qb[i] = ld_cg_f4(q0 + HEAD_DIM + 32 * i);
+        }
     }
     float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};   // (h0,tA) (h0,tB) (h1,tA) (h1,tB)
 #pragma unroll
@@ -547,7 +596,8 @@ __device__ void attention_unit32(const DecodeParams& p, const Smem& s, int l, in
     trace_step(p, l, 1, 2);
 }
 
-__device__ void phase_attention(const DecodeParams& p, const Smem& s, int l, int cta, int ncta, bool combine_here) {
+__device__ void phase_attention(const DecodeParams& p, const Smem& s, int l, int cta, int ncta, bool combine_here,
+                                unsigned seq) {
     const int n = p.pos + 1;
     const int P = 32 * ((n + 2047) / 2048);
     const int C = (n + P - 1) / P;
@@ -575,7 +625,7 @@ __device__ void phase_attention(const DecodeParams& p, const Smem& s, int l, int
         const bool single = np <= 32;   // q, K and V of the chunk staged in one round trip
         __syncthreads();
         if (P == 32) {
-            attention_unit32(p, s, l, g, c, t0, np);
+            attention_unit32(p, s, l, g, c, t0, np, seq);
         } else {
             if (tid < 256)
                 reinterpret_cast<float4*>(qh)[tid] = __ldcg(reinterpret_cast<const float4*>(p.q + 8 * g * HEAD_DIM) + tid);
@@ -985,12 +1035,18 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
     __syncthreads();
     trace_mark(p, 0);
     const LmPlan lmq = lm_plan(p, cta, ncta);
+    const bool att32 = 32 * ((p.pos + 1 + 2047) / 2048) == 32;   // chunk length (uniform over CTAs)
     // Weight phase w+1 is issued while waiting at the barrier in front of phase w: its
     // buffer was last used by phase w-1, which every thread of this CTA has finished.
     for (int l = 0; l < p.n_layer; ++l) {
         if (!phase_qkv(p, s, l, token, cta, ncta, seq)) return;
-        if (!traced_barrier(p, bs, 5 * l, [&] { issue_weight_phase(p, s, 4 * l + 1, cta, ncta); })) return;
-        phase_attention(p, s, l, cta, ncta, attn_chunks(p.pos + 1) > DIST_COMBINE_MAX);
+        if (att32) {   // 32-position units wait on q/K/V epochs themselves: no barrier
+            trace_mark(p, 2 + 2 * (5 * l));
+            if (threadIdx.x == 0) issue_weight_phase(p, s, 4 * l + 1, cta, ncta);
+        } else if (!traced_barrier(p, bs, 5 * l, [&] { issue_weight_phase(p, s, 4 * l + 1, cta, ncta); })) {
+            return;
+        }
+        phase_attention(p, s, l, cta, ncta, attn_chunks(p.pos + 1) > DIST_COMBINE_MAX, seq);
         if (!traced_barrier(p, bs, 5 * l + 1, [&] { issue_weight_phase(p, s, 4 * l + 2, cta, ncta); })) return;
         // o_proj -> gate/up and down -> next QKV exchange the residual through epoch-tagged
         // words: no grid barrier (every consumer needs all of x, which orders all reuse).
@@ -1034,7 +1090,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_attention(const DecodeParams
     Smem s{};
     s.wbuf[0] = smem_raw;
     s.flag = reinterpret_cast<int*>(smem_raw + ATT_SMEM_FLOATS * 4);
-    phase_attention(p, s, 0, blockIdx.x, gridDim.x, true);
+    phase_attention(p, s, 0, blockIdx.x, gridDim.x, true, 0u);
 }
 
 }  // namespace

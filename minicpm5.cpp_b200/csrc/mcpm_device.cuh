@@ -117,6 +117,33 @@ __device__ __forceinline__ unsigned long long ld_epoch(const unsigned long long*
     asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
     return w;
 }
+__device__ __forceinline__ ulonglong2 ld_epoch2(const unsigned long long* p) {   // each element atomic
+    ulonglong2 w;
+    asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(w.x), "=l"(w.y) : "l"(p) : "memory");
+    return w;
+}
+// Four consecutive epoch-tagged values (16-byte aligned), polled until all carry `epoch`;
+// false (and ERR_TIMEOUT raised) after 1 s.
+__device__ __forceinline__ bool load4_epoch(const unsigned long long* src, unsigned epoch, float4& v, unsigned* err) {
+    ulonglong2 a = ld_epoch2(src), b = ld_epoch2(src + 2);
+    auto ready = [&]() {
+        return (a.x >> 32) == epoch && (a.y >> 32) == epoch && (b.x >> 32) == epoch && (b.y >> 32) == epoch;
+    };
+    if (!ready()) {
+        const uint64_t t0 = globaltimer();
+        do {
+            a = ld_epoch2(src);
+            b = ld_epoch2(src + 2);
+            if (!ready() && globaltimer() - t0 > 1000000000ull) {
+                atomicOr(err, ERR_TIMEOUT);
+                return false;
+            }
+        } while (!ready());
+    }
+    v = make_float4(__uint_as_float(static_cast<unsigned>(a.x)), __uint_as_float(static_cast<unsigned>(a.y)),
+                    __uint_as_float(static_cast<unsigned>(b.x)), __uint_as_float(static_cast<unsigned>(b.y)));
+    return true;
+}
 __device__ __forceinline__ uint32_t ld_acquire_u32(const unsigned* p) {
     uint32_t v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");

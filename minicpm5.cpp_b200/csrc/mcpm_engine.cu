@@ -52,6 +52,7 @@ struct mcpm_engine {
     float2* rope = nullptr;
     float *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr, *att_part = nullptr, *logits = nullptr;
     unsigned long long* xll = nullptr;   // residual stream with per-element epochs
+    unsigned long long* qll = nullptr;   // q, K row, V row with per-element epochs
     float* am_val = nullptr;
     int* am_idx = nullptr;
     uint8_t* att_q8k = nullptr;
@@ -96,6 +97,7 @@ void free_model(mcpm_engine* e) {
     free_dev(e->att);
     free_dev(e->h);
     free_dev(e->xll);
+    free_dev(e->qll);
     free_dev(e->att_part);
     free_dev(e->logits);
     free_dev(e->am_val);
@@ -166,6 +168,7 @@ mcpm_status reset_ctl(mcpm_engine* e) {
     MCPM_CUDA(cudaMemsetAsync(e->ctl, 0, CTL_WORDS * sizeof(int), e->stream));
     // the launch sequence restarts, so no epoch of an aborted launch may remain
     if (e->xll) MCPM_CUDA(cudaMemsetAsync(e->xll, 0, N_EMBD * sizeof(unsigned long long), e->stream));
+    if (e->qll) MCPM_CUDA(cudaMemsetAsync(e->qll, 0, (N_EMBD + 2 * KV_DIM) * sizeof(unsigned long long), e->stream));
     MCPM_CUDA(cudaStreamSynchronize(e->stream));
     return MCPM_OK;
 }
@@ -203,6 +206,7 @@ DecodeParams make_params(const mcpm_engine* e, int token, int pos, int write_log
     p.att_q8k = e->att_q8k;
     p.h = e->h;
     p.xll = e->xll;
+    p.qll = e->qll;
     p.att_part = e->att_part;
     p.logits = e->logits;
     p.am_val = e->am_val;
@@ -425,6 +429,8 @@ mcpm_status mcpm_load_gguf(mcpm_engine* e, const char* path) {
     MCPM_CUDA(cudaMalloc(&e->h, N_FF * 4));
     MCPM_CUDA(cudaMalloc(&e->xll, N_EMBD * sizeof(unsigned long long)));
     MCPM_CUDA(cudaMemset(e->xll, 0, N_EMBD * sizeof(unsigned long long)));
+    MCPM_CUDA(cudaMalloc(&e->qll, (N_EMBD + 2 * KV_DIM) * sizeof(unsigned long long)));
+    MCPM_CUDA(cudaMemset(e->qll, 0, (N_EMBD + 2 * KV_DIM) * sizeof(unsigned long long)));
     MCPM_CUDA(cudaMalloc(&e->att_part, sizeof(float) * N_HEAD * ATT_MAX_CHUNKS * ATT_PART_STRIDE));
     MCPM_CUDA(cudaMalloc(&e->logits, sizeof(float) * e->n_vocab));
     MCPM_CUDA(cudaMalloc(&e->am_val, sizeof(float) * e->n_ctas));

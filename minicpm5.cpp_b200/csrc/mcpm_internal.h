@@ -69,6 +69,8 @@ struct DecodeParams {
     uint8_t* att_q8k;   // attention output as 8 block_q8_K
     float* h;           // SwiGLU output [N_FF]
     unsigned long long* xll;   // residual stream published per element as (epoch << 32) | fp32 bits [N_EMBD]
+    unsigned long long* qll;   // rotated q [N_EMBD] then this position's K and V rows [2*KV_DIM], same encoding;
+                               // null outside the decode kernel (q and the cache are then final)
     float* att_part;    // [N_HEAD][ATT_MAX_CHUNKS][ATT_PART_STRIDE]
     float* logits;      // [n_vocab]
     float* am_val;      // per-CTA argmax partials
