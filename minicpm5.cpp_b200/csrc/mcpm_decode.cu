@@ -29,6 +29,11 @@ struct LayerMeta {
     uint32_t w[7];                  // arena offsets of wq, wk, wv, wo, wg, wu, wd
     uint32_t attn_norm, ffn_norm;   // arena offsets of the norm weights
     uint8_t tq, tk, tv, to, tg, tu, td, pad;
+    int16_t qkv0, qkv1;             // this CTA's rows of the combined [Q; K; V] (cost-weighted split)
+};
+// This CTA's rows of the 2048-row (o_proj, down) and 6144-row (gate/up) phases.
+struct CtaRows {
+    int od0, od1, gu0, gu1;
 };
 __device__ __forceinline__ const float* meta_f32(const DecodeParams& p, uint32_t off) {
     return reinterpret_cast<const float*>(p.arena + off);
@@ -47,6 +52,7 @@ struct Smem {
     uint64_t* wbar;  // [2][4]
     uint64_t* lmbar; // [4]
     int* flag;
+    CtaRows* rows;
     LayerMeta* meta;   // [n_layer]
 };
 
@@ -63,17 +69,20 @@ struct PhaseLayout {
 
 __device__ __forceinline__ uint32_t align16(uint32_t v) { return (v + 15u) & ~15u; }
 
-template <class LT>
-__device__ PhaseLayout phase_layout(const LT& L, int kind, int cta, int ncta) {
+// Row splits are precomputed at kernel start (CtaRows, LayerMeta::qkv0/1): the 64-bit
+// divisions they need would otherwise sit on every phase's critical path.
+__device__ PhaseLayout phase_layout(const LayerMeta& L, const CtaRows& cr, int kind) {
     PhaseLayout pl;
+#pragma unroll
     for (int i = 0; i < 3; ++i) pl.row0[i] = pl.nrows[i] = 0, pl.off[i] = pl.bytes[i] = 0;
     int a, b;
     if (kind == 0) {   // QKV: row pairs of the combined [Q; K; V] rows, cost-weighted split
-        a = 2 * qkv_pair_boundary(L.tq, L.tk, L.tv, cta, ncta);
-        b = 2 * qkv_pair_boundary(L.tq, L.tk, L.tv, cta + 1, ncta);
+        a = L.qkv0;
+        b = L.qkv1;
         const int lo[3] = {0, N_EMBD, N_EMBD + KV_DIM}, hi[3] = {N_EMBD, N_EMBD + KV_DIM, QKV_ROWS};
         const int types[3] = {L.tq, L.tk, L.tv};
         uint32_t off = 0;
+#pragma unroll
         for (int i = 0; i < 3; ++i) {
             const int s = max(a, lo[i]), e = min(b, hi[i]);
             pl.row0[i] = max(0, s - lo[i]);
@@ -83,12 +92,14 @@ __device__ PhaseLayout phase_layout(const LT& L, int kind, int cta, int ncta) {
             off = align16(off + pl.bytes[i]);
         }
     } else if (kind == 1 || kind == 3) {   // O, D: 2048 output rows
-        split_range(N_EMBD, cta, ncta, a, b);
+        a = cr.od0;
+        b = cr.od1;
         pl.row0[0] = a;
         pl.nrows[0] = b - a;
         pl.bytes[0] = (b - a) * (kind == 1 ? row_bytes(L.to, N_EMBD) : row_bytes(L.td, N_FF));
     } else {   // GU: gate rows then up rows
-        split_range(N_FF, cta, ncta, a, b);
+        a = cr.gu0;
+        b = cr.gu1;
         pl.row0[0] = pl.row0[1] = a;
         pl.nrows[0] = pl.nrows[1] = b - a;
         pl.bytes[0] = (b - a) * row_bytes(L.tg, N_EMBD);
@@ -103,8 +114,7 @@ __device__ const uint8_t* phase_src(const DecodeParams& p, const LayerMeta& M, i
     return p.arena + M.w[k];
 }
 
-template <class LT>
-__device__ int phase_type(const LT& L, int kind, int i) {
+__device__ int phase_type(const LayerMeta& L, int kind, int i) {
     if (kind == 0) return i == 0 ? L.tq : i == 1 ? L.tk : L.tv;
     if (kind == 1) return L.to;
     if (kind == 2) return i == 0 ? L.tg : L.tu;
@@ -119,8 +129,9 @@ __device__ void issue_weight_phase(const DecodeParams& p, const Smem& s, int wp,
     uint64_t* bars = s.wbar + 4 * buf;
     const int l = wp >> 2, kind = wp & 3;
     const LayerMeta& M = s.meta[l];
-    const PhaseLayout pl = phase_layout(M, kind, cta, ncta);
+    const PhaseLayout pl = phase_layout(M, *s.rows, kind);
     const uint64_t pol = l2_evict_first_policy();
+#pragma unroll
     for (int i = 0; i < 3; ++i) {
         mbar_expect_tx(&bars[i], pl.bytes[i]);
         if (pl.bytes[i]) {
@@ -369,8 +380,7 @@ __device__ __forceinline__ unsigned x_epoch(unsigned seq, int k) { return (seq <
 // ------------------------------------------------------------------------ phases
 __device__ bool phase_qkv(const DecodeParams& p, const Smem& s, int l, int token, int cta, int ncta, unsigned seq) {
     const LayerMeta& L = s.meta[l];
-    const int a = 2 * qkv_pair_boundary(L.tq, L.tk, L.tv, cta, ncta);   // same split as phase_layout
-    const int b = 2 * qkv_pair_boundary(L.tq, L.tk, L.tv, cta + 1, ncta);
+    const int a = L.qkv0, b = L.qkv1;   // same split as phase_layout
     // this thread's RoPE factors (pair pr = threadIdx.x), fetched before the norm
     const int pr0 = threadIdx.x, R0 = a + 2 * pr0;
     float2 cs0 = make_float2(0.0f, 0.0f);
@@ -389,14 +399,15 @@ __device__ bool phase_qkv(const DecodeParams& p, const Smem& s, int l, int token
     trace_step(p, l, 0, 1);
     if (!wait_weights(p, s, 4 * l)) return false;
     trace_step(p, l, 0, 2);
-    const PhaseLayout pl = phase_layout(L, 0, cta, ncta);
+    const PhaseLayout pl = phase_layout(L, *s.rows, 0);
     const int lo[3] = {0, N_EMBD, N_EMBD + KV_DIM};
     float* rv = s.rowval;
+#pragma unroll
     for (int i = 0; i < 3; ++i) {
         if (pl.nrows[i] == 0) continue;   // uniform across the CTA
         const int base = lo[i] + pl.row0[i] - a;
         gemv_rows(phase_type(L, 0, i), s.wbuf[0] + pl.off[i], pl.nrows[i], N_EMBD / 256, *s.xq, s.part, MAX_TASKS,
-                  rv + base);
+                  rv + base, (p.trace && l == 1 && cta == 0 && i == 0) ? p.trace + TRACE_GEMV + 9 : nullptr);
     }
     trace_step(p, l, 0, 3);
     // RoPE on Q/K pairs (interleaved, ops.cpp:502-516 with the build's FMA contraction),
@@ -826,7 +837,7 @@ __device__ void combine_attention(const DecodeParams& p, const Smem& s, int l, i
 // and the down weights are issued into the buffer this phase just released.
 __device__ bool phase_o(const DecodeParams& p, const Smem& s, int l, int cta, int ncta, unsigned seq) {
     const LayerMeta& L = s.meta[l];
-    const PhaseLayout pl = phase_layout(L, 1, cta, ncta);
+    const PhaseLayout pl = phase_layout(L, *s.rows, 1);
     const int r0 = pl.row0[0], n = pl.nrows[0];
     const float xr = threadIdx.x < n ? __ldcg(p.x + r0 + threadIdx.x) : 0.0f;   // residual rows, early
     if (attn_chunks(p.pos + 1) <= DIST_COMBINE_MAX)
@@ -837,7 +848,7 @@ __device__ bool phase_o(const DecodeParams& p, const Smem& s, int l, int cta, in
     if (!wait_weights(p, s, 4 * l + 1)) return false;
     trace_step(p, l, 2, 2);
     gemv_rows(L.to, s.wbuf[1], n, N_EMBD / 256, *s.xq, s.part, MAX_TASKS, s.rowval,
-              (p.trace && l == 1 && cta == 0) ? p.trace + TRACE_DETAIL + 60 : nullptr);
+              (p.trace && l == 1 && cta == 0) ? p.trace + TRACE_GEMV + 0 : nullptr);
     if (threadIdx.x < n) {
         const float xn = __fadd_rn(xr, s.rowval[threadIdx.x]);
         p.x[r0 + threadIdx.x] = xn;
@@ -854,11 +865,11 @@ __device__ bool phase_gu(const DecodeParams& p, const Smem& s, int l, int cta, i
     trace_step(p, l, 3, 1);
     if (!wait_weights(p, s, 4 * l + 2)) return false;
     trace_step(p, l, 3, 2);
-    const PhaseLayout pl = phase_layout(L, 2, cta, ncta);
+    const PhaseLayout pl = phase_layout(L, *s.rows, 2);
     const int n = pl.nrows[0];
     float* rv = s.rowval;
     gemv_rows(L.tg, s.wbuf[0] + pl.off[0], n, N_EMBD / 256, *s.xq, s.part, MAX_TASKS, rv,
-              (p.trace && l == 1 && cta == 0) ? p.trace + TRACE_DETAIL + 64 : nullptr);
+              (p.trace && l == 1 && cta == 0) ? p.trace + TRACE_GEMV + 6 : nullptr);
     trace_step(p, l, 3, 3);
     gemv_rows(L.tu, s.wbuf[0] + pl.off[1], n, N_EMBD / 256, *s.xq, s.part, MAX_TASKS, rv + 128);
     trace_step(p, l, 3, 4);
@@ -871,7 +882,7 @@ __device__ bool phase_gu(const DecodeParams& p, const Smem& s, int l, int cta, i
 __device__ bool phase_down(const DecodeParams& p, const Smem& s, int l, int cta, int ncta, unsigned seq,
                            const LmPlan& lmq) {
     const LayerMeta& L = s.meta[l];
-    const PhaseLayout pl = phase_layout(L, 3, cta, ncta);
+    const PhaseLayout pl = phase_layout(L, *s.rows, 3);
     const int r0 = pl.row0[0], n = pl.nrows[0];
     const float xr = threadIdx.x < n ? __ldcg(p.x + r0 + threadIdx.x) : 0.0f;   // residual rows, early
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -886,7 +897,7 @@ __device__ bool phase_down(const DecodeParams& p, const Smem& s, int l, int cta,
     if (!wait_weights(p, s, 4 * l + 3)) return false;
     trace_step(p, l, 4, 2);
     gemv_rows(L.td, s.wbuf[1], n, N_FF / 256, *s.xq, s.part, MAX_TASKS, s.rowval,
-              (p.trace && l == 1 && cta == 0) ? p.trace + TRACE_DETAIL + 62 : nullptr);
+              (p.trace && l == 1 && cta == 0) ? p.trace + TRACE_GEMV + 3 : nullptr);
     if (threadIdx.x < n) {
         const float xn = __fadd_rn(xr, s.rowval[threadIdx.x]);
         p.x[r0 + threadIdx.x] = xn;
@@ -998,17 +1009,28 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
     ptr += 4 * 8;
     s.flag = reinterpret_cast<int*>(ptr);
     ptr += 16;
+    s.rows = reinterpret_cast<CtaRows*>(ptr);
+    ptr += 16;
     s.meta = reinterpret_cast<LayerMeta*>(ptr);
+    if (threadIdx.x == 0) {
+        CtaRows cr;
+        split_range(N_EMBD, blockIdx.x, gridDim.x, cr.od0, cr.od1);
+        split_range(N_FF, blockIdx.x, gridDim.x, cr.gu0, cr.gu1);
+        *s.rows = cr;
+    }
     for (int i = threadIdx.x; i < p.n_layer; i += blockDim.x) {
         const LayerDev& L = p.layers[i];
         LayerMeta m;
         const uint8_t* const wp[7] = {L.wq, L.wk, L.wv, L.wo, L.wg, L.wu, L.wd};
+#pragma unroll
         for (int k = 0; k < 7; ++k) m.w[k] = static_cast<uint32_t>(wp[k] - p.arena);
         m.attn_norm = static_cast<uint32_t>(reinterpret_cast<const uint8_t*>(L.attn_norm) - p.arena);
         m.ffn_norm = static_cast<uint32_t>(reinterpret_cast<const uint8_t*>(L.ffn_norm) - p.arena);
         m.tq = static_cast<uint8_t>(L.tq), m.tk = static_cast<uint8_t>(L.tk), m.tv = static_cast<uint8_t>(L.tv);
         m.to = static_cast<uint8_t>(L.to), m.tg = static_cast<uint8_t>(L.tg), m.tu = static_cast<uint8_t>(L.tu);
         m.td = static_cast<uint8_t>(L.td), m.pad = 0;
+        m.qkv0 = static_cast<int16_t>(2 * qkv_pair_boundary(L.tq, L.tk, L.tv, blockIdx.x, gridDim.x));
+        m.qkv1 = static_cast<int16_t>(2 * qkv_pair_boundary(L.tq, L.tk, L.tv, blockIdx.x + 1, gridDim.x));
         s.meta[i] = m;
     }
     __syncthreads();
@@ -1098,7 +1120,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_attention(const DecodeParams
 size_t decode_smem_bytes() {
     size_t b = 2 * (WBUF_BYTES + WBUF_SLACK);
     b += (sizeof(XQSmem) + 127) & ~size_t(127);
-    b += SCRATCH_BYTES + ROWVAL_FLOATS * 4 + 32 * 4 + 12 * 8 + 16 + MAX_LAYERS * sizeof(LayerMeta);
+    b += SCRATCH_BYTES + ROWVAL_FLOATS * 4 + 32 * 4 + 12 * 8 + 16 + 16 + MAX_LAYERS * sizeof(LayerMeta);
     return b;
 }
 

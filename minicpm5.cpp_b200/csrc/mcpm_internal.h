@@ -27,6 +27,7 @@ constexpr int TRACE_WORDS = 3400;         // 2 + 2*(5*layers+1) phase marks, det
 constexpr int TRACE_DETAIL = 650;         // sub-step marks of layer 1: 650 + 10*phase + step
 constexpr int TRACE_CTA = 720;            // layer-1 barrier k, CTA c: arrival 720 + 148k + c, release 1460 + 148k + c, SM id 2200 + c,
                                           // QKV sub-steps m = 0..2 of layer 1 at 2400 + 148m + c
+constexpr int TRACE_GEMV = 2848;          // layer-1 GEMV marks of CTA 0 (pass 1, pass 2, entry): O, D, gate, QKV
 
 // QKV row pairs [0, 1280) (Q pairs, then K, then V) are split over the CTAs in proportion
 // to their GEMV cost: a Q6_K row costs about 1.6 Q4_K rows (unaligned 210-byte blocks), so
