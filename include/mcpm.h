@@ -123,7 +123,7 @@ mcpm_status mcpm_attention(const float* q, const float* k, const float* v, float
 /* Same computation and results as mcpm_attention, for callers that cannot allocate device
  * memory (code running inside someone else's graph capture, hosts that own every
  * allocation, loops that must not call the allocator).  No counterpart in the reference.
- * The split-KV workspace is a fixed 532,480-byte array in the library's static device
+ * The split-KV workspace is a fixed 540,672-byte array in the library's static device
  * memory (held by every GPU that loads the library until exit), so contexts are limited to
  * pos + 1 <= 16384 and max_seq <= 16384 (MCPM_BAD_ARG beyond).  No call allocates; the
  * first call on a device looks up the workspace address, so make it before any stream

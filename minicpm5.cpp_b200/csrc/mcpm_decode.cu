@@ -596,8 +596,8 @@ __device__ void attention_unit32(const DecodeParams& p, const Smem& s, int l, in
     }
     float* pa0 = p.att_part + (static_cast<size_t>(8 * g + h0) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
     float* pa1 = p.att_part + (static_cast<size_t>(8 * g + h1) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
-    __stcg(pa0 + 2 + dd, acc0);
-    __stcg(pa1 + 2 + dd, acc1);
+    __stcg(pa0 + ATT_PART_O + dd, acc0);
+    __stcg(pa1 + ATT_PART_O + dd, acc1);
     if (tid < 8) {
         float* pm = p.att_part + (static_cast<size_t>(8 * g + tid) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
         __stcg(pm, stat[tid]);
@@ -693,8 +693,8 @@ __device__ void phase_attention(const DecodeParams& p, const Smem& s, int l, int
             // partials: [head][chunk][m, l, o[128]]
             float* pa0 = p.att_part + (static_cast<size_t>(8 * g + h0) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
             float* pa1 = p.att_part + (static_cast<size_t>(8 * g + h1) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
-            __stcg(pa0 + 2 + dd, acc0);
-            __stcg(pa1 + 2 + dd, acc1);
+            __stcg(pa0 + ATT_PART_O + dd, acc0);
+            __stcg(pa1 + ATT_PART_O + dd, acc1);
             if (tid < 8) {
                 float* pm = p.att_part + (static_cast<size_t>(8 * g + tid) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
                 __stcg(pm, stat[tid]);
@@ -743,7 +743,7 @@ __device__ void phase_attention(const DecodeParams& p, const Smem& s, int l, int
             float O = 0.0f;
 #pragma unroll 8
             for (int cc = 0; cc < C; ++cc)
-                O = __fmaf_rn(wts[h * ATT_MAX_CHUNKS + cc], __ldcg(ph + cc * ATT_PART_STRIDE + 2 + d), O);
+                O = __fmaf_rn(wts[h * ATT_MAX_CHUNKS + cc], __ldcg(ph + cc * ATT_PART_STRIDE + ATT_PART_O + d), O);
             const float out = __fmul_rn(O, stat[16 + h]);
             ab[o] = out;
             p.att[8 * g * HEAD_DIM + o] = out;
@@ -781,60 +781,49 @@ __device__ void load_q8k_blocks(const uint8_t* src, int nblocks, const Smem& s) 
 // Every CTA combines the attention chunks of all 16 heads (same operations and order as
 // the last-CTA combine) and quantises the result ties-to-even straight into s.xq.
 __device__ void combine_attention(const DecodeParams& p, const Smem& s, int l, int cta) {
+    // warp = head h, lane = dims 4*lane .. 4*lane+3: the chunk weights of a head never leave
+    // its warp, so loads, max, exp, the L chain and the O chains run without a CTA barrier.
     const int n = p.pos + 1, C = attn_chunks(n);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    float* wts = s.rowval;   // [16][16]
-    float* invl = s.red;     // [16]
-    float* ab = s.xs;        // [2048]
-    // outputs o = tid + 512 i; h = o >> 7, d = o & 127: issue every chunk-partial load first
-    float v[4][DIST_COMBINE_MAX];
+    const int tid = threadIdx.x, lane = tid & 31, h = tid >> 5;
+    float* ab = s.xs;   // [2048]
+    const float* ph = p.att_part + static_cast<size_t>(h) * ATT_MAX_CHUNKS * ATT_PART_STRIDE;
+    const float2 ml = lane < C ? *reinterpret_cast<const float2*>(ph + lane * ATT_PART_STRIDE) : make_float2(0.f, 0.f);
+    float4 v[DIST_COMBINE_MAX];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int o = tid + 512 * i, h = o >> 7, d = o & 127;
-        const float* ph = p.att_part + static_cast<size_t>(h) * ATT_MAX_CHUNKS * ATT_PART_STRIDE + 2 + d;
+    for (int cc = 0; cc < DIST_COMBINE_MAX; ++cc)
+        v[cc] = cc < C ? ld_cg_f4(ph + cc * ATT_PART_STRIDE + ATT_PART_O + 4 * lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+    float M = lane < C ? ml.x : -__int_as_float(0x7f800000);
+    for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    const float wv = lane < C ? canon_expf(__fsub_rn(ml.x, M)) : 0.0f;
+    float Ls = 0.0f;
+    float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int cc = 0; cc < DIST_COMBINE_MAX; ++cc) v[i][cc] = cc < C ? ld_cg_f32(ph + cc * ATT_PART_STRIDE) : 0.0f;
+    for (int cc = 0; cc < DIST_COMBINE_MAX; ++cc) {
+        if (cc < C) {
+            const float w = __shfl_sync(0xffffffffu, wv, cc);
+            Ls = __fmaf_rn(w, __shfl_sync(0xffffffffu, ml.y, cc), Ls);
+            O.x = __fmaf_rn(w, v[cc].x, O.x);
+            O.y = __fmaf_rn(w, v[cc].y, O.y);
+            O.z = __fmaf_rn(w, v[cc].z, O.z);
+            O.w = __fmaf_rn(w, v[cc].w, O.w);
+        }
     }
-    if (warp < N_HEAD) {
-        const float* ph = p.att_part + static_cast<size_t>(warp) * ATT_MAX_CHUNKS * ATT_PART_STRIDE;
-        const float mc = lane < C ? ld_cg_f32(ph + lane * ATT_PART_STRIDE) : 0.0f;
-        const float lc = lane < C ? ld_cg_f32(ph + lane * ATT_PART_STRIDE + 1) : 0.0f;
-        float M = lane < C ? mc : -__int_as_float(0x7f800000);
-        for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-        const float wv = lane < C ? canon_expf(__fsub_rn(mc, M)) : 0.0f;
-        if (lane < C) wts[warp * 16 + lane] = wv;
-        float Ls = 0.0f;
-        for (int cc = 0; cc < C; ++cc)
-            Ls = __fmaf_rn(__shfl_sync(0xffffffffu, wv, cc), __shfl_sync(0xffffffffu, lc, cc), Ls);
-        if (lane == 0) invl[warp] = __fdiv_rn(1.0f, Ls);
-    }
-    if (warp == 0) trace_step(p, l, 2, 4);
-    __syncthreads();
-    trace_step(p, l, 2, 5);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int o = tid + 512 * i, h = o >> 7;
-        float O = 0.0f;
-#pragma unroll
-        for (int cc = 0; cc < DIST_COMBINE_MAX; ++cc)
-            if (cc < C) O = __fmaf_rn(wts[h * 16 + cc], v[i][cc], O);
-        const float out = __fmul_rn(O, invl[h]);
-        ab[o] = out;
-        if (cta == 0) p.att[o] = out;
-    }
+    const float inv = __fdiv_rn(1.0f, Ls);
+    const float4 out = make_float4(__fmul_rn(O.x, inv), __fmul_rn(O.y, inv), __fmul_rn(O.z, inv), __fmul_rn(O.w, inv));
+    *reinterpret_cast<float4*>(ab + 128 * h + 4 * lane) = out;
+    if (cta == 0) *reinterpret_cast<float4*>(p.att + 128 * h + 4 * lane) = out;
+    if (h == 0) trace_step(p, l, 2, 4);
     __syncthreads();
     trace_step(p, l, 2, 6);
-    if (warp < N_EMBD / 256) {
-        const float4 a = *reinterpret_cast<const float4*>(ab + 256 * warp + 8 * lane);
-        const float4 b = *reinterpret_cast<const float4*>(ab + 256 * warp + 8 * lane + 4);
+    if (h < N_EMBD / 256) {
+        const float4 a = *reinterpret_cast<const float4*>(ab + 256 * h + 8 * lane);
+        const float4 b = *reinterpret_cast<const float4*>(ab + 256 * h + 8 * lane + 4);
         const float y[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-        quant_block_warp<false>(y, s.xq->qs[warp], &s.xq->d[warp], s.xq->bsums[warp]);
+        quant_block_warp<false>(y, s.xq->qs[h], &s.xq->d[h], s.xq->bsums[h]);
     }
     __syncthreads();
 }
 
-// o_proj + residual; the new residual rows are published as epoch-tagged words (k = 2l+1)
-// and the down weights are issued into the buffer this phase just released.
 __device__ bool phase_o(const DecodeParams& p, const Smem& s, int l, int cta, int ncta, unsigned seq) {
     const LayerMeta& L = s.meta[l];
     const PhaseLayout pl = phase_layout(L, *s.rows, 1);

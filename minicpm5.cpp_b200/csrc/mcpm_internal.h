@@ -20,7 +20,8 @@ constexpr int MAX_TASKS = 512;             // (row, super-block) tasks per GEMV 
 constexpr int ROWVAL_FLOATS = 256;
 constexpr int LM_SLOT_BYTES = WBUF_BYTES;   // LM head: one stage per weight buffer
 constexpr int ATT_MAX_CHUNKS = 64;         // attention chunks per head (chunk = 32*ceil(n/2048))
-constexpr int ATT_PART_STRIDE = 2 + HEAD_DIM;
+constexpr int ATT_PART_STRIDE = 4 + HEAD_DIM;   // m, l, 2 pad, o[128]: o 16-byte aligned
+constexpr int ATT_PART_O = 4;
 constexpr int ATT_SC_STRIDE = 256;         // chunk-length bound: 32*ceil(MAX_SEQ/2048)
 constexpr int MAX_SEQ = 16384;
 constexpr int TRACE_WORDS = 3400;         // 2 + 2*(5*layers+1) phase marks, detail marks from 650, per-CTA from 720

@@ -9,7 +9,7 @@
 // static device memory instead, so no call ever allocates.
 //
 // The workspace below is the chunk partials of 16 query heads x 64 chunks x (2 + 128)
-// floats (532,480 bytes), the combine counters and a Q8_K sink: enough for any context
+// floats (540,672 bytes), the combine counters and a Q8_K sink: enough for any context
 // up to MAX_SEQ = 16384 positions.  Every GPU that loads the library holds it until the
 // process exits.  All calls on a device share it, so calls that overlap on the GPU race
 // and must be serialised by the caller (one stream, or events).
