@@ -875,11 +875,23 @@ __device__ bool phase_down(const DecodeParams& p, const Smem& s, int l, int cta,
     const int r0 = pl.row0[0], n = pl.nrows[0];
     const float xr = threadIdx.x < n ? __ldcg(p.x + r0 + threadIdx.x) : 0.0f;   // residual rows, early
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int b = warp; b < N_FF / 256; b += blockDim.x >> 5) {   // Q8_K of h straight from L2
-        const float4 a = __ldcg(reinterpret_cast<const float4*>(p.h + 256 * b + 8 * lane));
-        const float4 c = __ldcg(reinterpret_cast<const float4*>(p.h + 256 * b + 8 * lane + 4));
-        const float y[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
-        quant_block_warp<true>(y, s.xq->qs[b], &s.xq->d[b], s.xq->bsums[b]);
+    {   // Q8_K of h straight from L2: warp w quantises blocks w and w+16 (24 blocks), both loads first
+        static_assert(N_FF / 256 <= 2 * (DEC_THREADS / 32), "two h blocks per warp");
+        const int b0 = warp, b1 = warp + (DEC_THREADS >> 5);
+        const bool two = b1 < N_FF / 256;
+        const float4 a0 = ld_cg_f4(p.h + 256 * b0 + 8 * lane);
+        const float4 c0 = ld_cg_f4(p.h + 256 * b0 + 8 * lane + 4);
+        float4 a1 = make_float4(0.f, 0.f, 0.f, 0.f), c1 = a1;
+        if (two) {
+            a1 = ld_cg_f4(p.h + 256 * b1 + 8 * lane);
+            c1 = ld_cg_f4(p.h + 256 * b1 + 8 * lane + 4);
+        }
+        const float y0[8] = {a0.x, a0.y, a0.z, a0.w, c0.x, c0.y, c0.z, c0.w};
+        quant_block_warp<true>(y0, s.xq->qs[b0], &s.xq->d[b0], s.xq->bsums[b0]);
+        if (two) {
+            const float y1[8] = {a1.x, a1.y, a1.z, a1.w, c1.x, c1.y, c1.z, c1.w};
+            quant_block_warp<true>(y1, s.xq->qs[b1], &s.xq->d[b1], s.xq->bsums[b1]);
+        }
     }
     __syncthreads();
     trace_step(p, l, 4, 1);
