@@ -217,6 +217,17 @@ __device__ __forceinline__ void trace_step(const DecodeParams& p, int l, int ph,
         p.trace[2400 + 148 * (step - 1) + blockIdx.x] = globaltimer();
 }
 
+// Thread that issues weight copies and prefetches at the end of o_proj and down: outside
+// warps 0-7, which poll the epoch-tagged residual in the following norm.
+constexpr int ISSUE_THREAD = 256;
+
+// Per-CTA marks of layer 1 for boundaries without a grid barrier (k as in traced_barrier:
+// 0 QKV, 2 o_proj, 4 down): `rel` 0 when the phase finished, 1 when its consumer's wait ended.
+__device__ __forceinline__ void trace_cta(const DecodeParams& p, int l, int k, int rel) {
+    if (p.trace && l == 1 && threadIdx.x == 0 && blockIdx.x < 148)
+        p.trace[TRACE_CTA + 740 * rel + 148 * k + blockIdx.x] = globaltimer();
+}
+
 template <typename F>
 __device__ bool traced_barrier(const DecodeParams& p, BarState& bs, int ph, F&& during) {
     trace_mark(p, 2 + 2 * ph);
@@ -395,6 +406,7 @@ __device__ bool phase_qkv(const DecodeParams& p, const Smem& s, int l, int token
     } else {
         if (!norm_quant<true, X_EPOCH>(p, nullptr, x_epoch(seq, 2 * l), meta_f32(p, L.attn_norm), s)) return false;
         trace_mark(p, 3 + 2 * (5 * (l - 1) + 4));
+        trace_cta(p, l - 1, 4, 1);
     }
     trace_step(p, l, 0, 1);
     if (!wait_weights(p, s, 4 * l)) return false;
@@ -585,15 +597,28 @@ __device__ void attention_unit32(const DecodeParams& p, const Smem& s, int l, in
         for (int o = 16; o >= 1; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
         if (lane == 0) stat[warp] = m, stat[8 + warp] = sum;
     }
+    if (warp == 0) trace_step(p, l, 1, 5);
     cp_async_wait_all();
     __syncthreads();
+    trace_step(p, l, 1, 6);
     float acc0 = 0.0f, acc1 = 0.0f;   // o[h][dd] = fma chain over positions
     const int h0 = tid >> 7, h1 = h0 + 4, dd = tid & 127;
-    for (int t = 0; t < np; ++t) {
-        const float v = vb[t * HEAD_DIM + dd];
-        acc0 = __fmaf_rn(sc[h0 * 32 + t], v, acc0);
-        acc1 = __fmaf_rn(sc[h1 * 32 + t], v, acc1);
+    for (int t = 0; t < np; t += 4) {   // four positions per step: loads first, chain in order
+        const float4 s0 = *reinterpret_cast<const float4*>(sc + h0 * 32 + t);
+        const float4 s1 = *reinterpret_cast<const float4*>(sc + h1 * 32 + t);
+        float v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[k] = t + k < np ? vb[(t + k) * HEAD_DIM + dd] : 0.0f;
+        const float a0[4] = {s0.x, s0.y, s0.z, s0.w}, a1[4] = {s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            if (t + k < np) {
+                acc0 = __fmaf_rn(a0[k], v[k], acc0);
+                acc1 = __fmaf_rn(a1[k], v[k], acc1);
+            }
+        }
     }
+    trace_step(p, l, 1, 7);
     float* pa0 = p.att_part + (static_cast<size_t>(8 * g + h0) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
     float* pa1 = p.att_part + (static_cast<size_t>(8 * g + h1) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
     __stcg(pa0 + ATT_PART_O + dd, acc0);
@@ -843,7 +868,10 @@ __device__ bool phase_o(const DecodeParams& p, const Smem& s, int l, int cta, in
         p.x[r0 + threadIdx.x] = xn;
         st_epoch(p.xll + r0 + threadIdx.x, xn, x_epoch(seq, 2 * l + 1));
     }
-    if (threadIdx.x == 0) issue_weight_phase(p, s, 4 * l + 3, cta, ncta);
+    trace_cta(p, l, 2, 0);
+    // down weights into the buffer just released, by a thread outside warps 0-7 (which
+    // poll the residual in the next norm)
+    if (threadIdx.x == ISSUE_THREAD) issue_weight_phase(p, s, 4 * l + 3, cta, ncta);
     return true;
 }
 
@@ -851,6 +879,7 @@ __device__ bool phase_gu(const DecodeParams& p, const Smem& s, int l, int cta, i
     const LayerMeta& L = s.meta[l];
     if (!norm_quant<true, X_EPOCH>(p, nullptr, x_epoch(seq, 2 * l + 1), meta_f32(p, L.ffn_norm), s)) return false;
     trace_mark(p, 3 + 2 * (5 * l + 2));
+    trace_cta(p, l, 2, 1);
     trace_step(p, l, 3, 1);
     if (!wait_weights(p, s, 4 * l + 2)) return false;
     trace_step(p, l, 3, 2);
@@ -904,7 +933,8 @@ __device__ bool phase_down(const DecodeParams& p, const Smem& s, int l, int cta,
         p.x[r0 + threadIdx.x] = xn;
         st_epoch(p.xll + r0 + threadIdx.x, xn, x_epoch(seq, 2 * l + 2));
     }
-    if (threadIdx.x == 0) {
+    trace_cta(p, l, 4, 0);
+    if (threadIdx.x == ISSUE_THREAD) {
         if (l + 1 == p.n_layer) {
             issue_lm_stage(p, s, lmq, 1);
         } else {
