@@ -99,6 +99,11 @@ mcpm_status mcpm_quantize_q8k(const float* x, void* y, int n, int rounding, void
 /* y = W xq for Q4_K / Q6_K weights: gemv_q4_K_q8_K_avx2 / gemv_q6_K_q8_K_avx2
  * (ops_avx2.cpp:278-298) behind matmul_q8k (ops.cpp:317-349); bit-identical results. */
 mcpm_status mcpm_gemv_q8k(int type, const void* w, const void* xq, float* y, int rows, int cols, void* stream);
+/* y = W x for Q8_0 weights and fp32 activations: gemv_q8_0 (ops.cpp:58-79) behind matmul
+ * (ops.cpp:264-290); bit-identical to the reference build (its -ffast-math AVX2 evaluation
+ * order: eight lanes per 32-block, pairwise lane reduction, one fma per block along the row).
+ * cols % 256 == 0, cols <= 8192, w and x 16-byte aligned. */
+mcpm_status mcpm_gemv_q8_0_f32(const void* w, const float* x, float* y, int rows, int cols, void* stream);
 /* Integer block sums of the same product, [rows][cols/256] each: Q4_K isum = sum_j sc_j*dot_j,
  * aux = sum_g mn_g*(bsums[2g]+bsums[2g+1]); Q6_K isum = sum sc*q*x over unsigned q,
  * aux = 32*sum_g sc_g*bsums_g (dot_row_q{4,6}_K_q8_K_scalar, ops_scalar_optimized.cpp:139-404). */

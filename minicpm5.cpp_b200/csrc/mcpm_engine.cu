@@ -574,6 +574,12 @@ mcpm_status mcpm_quantize_q8k(const float* x, void* y, int n, int rounding, void
     return cuda_status(op_quantize_q8k(x, y, n, rounding, static_cast<cudaStream_t>(stream)));
 }
 
+mcpm_status mcpm_gemv_q8_0_f32(const void* w, const float* x, float* y, int rows, int cols, void* stream) {
+    if (!w || !x || !y || rows <= 0 || cols <= 0 || cols % 256 != 0 || cols > 8192) return MCPM_BAD_ARG;
+    if ((reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(x) & 15)) return MCPM_BAD_ARG;
+    return cuda_status(op_gemv_q8_0(w, x, y, rows, cols, static_cast<cudaStream_t>(stream)));
+}
+
 mcpm_status mcpm_gemv_q8k(int type, const void* w, const void* xq, float* y, int rows, int cols, void* stream) {
     if (!w || !xq || !y) return MCPM_BAD_ARG;
     if (type != GGML_Q4_K && type != GGML_Q6_K) return MCPM_UNSUPPORTED_TYPE;

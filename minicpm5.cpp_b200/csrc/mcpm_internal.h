@@ -101,6 +101,7 @@ cudaError_t launch_attention(const float* q, const float* k, const float* v, flo
 
 // Standalone op launchers (mcpm_ops.cu).
 cudaError_t op_quantize_q8k(const float* x, void* y, int n, int rounding, cudaStream_t s);
+cudaError_t op_gemv_q8_0(const void* w, const float* x, float* y, int rows, int cols, cudaStream_t s);
 cudaError_t op_gemv_q8k(int type, const void* w, const void* xq, float* y, int32_t* isum, int32_t* aux, int rows,
                         int cols, cudaStream_t s);
 cudaError_t op_rmsnorm_q8k(const float* x, const float* w, void* out, float eps, cudaStream_t s);

@@ -57,6 +57,7 @@ SIGNATURES = {
     "mcpm_engine_destroy": (None, [P]),
     "mcpm_quantize_q8k": (I, [P, P, I, I, P]),
     "mcpm_gemv_q8k": (I, [I, P, P, P, I, I, P]),
+    "mcpm_gemv_q8_0_f32": (I, [P, P, P, I, I, P]),
     "mcpm_gemv_blocksums": (I, [I, P, P, P, P, I, I, P]),
     "mcpm_gemv_gate_up_q8k": (I, [P, P, P, P, P, I, I, P]),
     "mcpm_rmsnorm_q8k": (I, [P, P, P, I, F, P]),
@@ -200,6 +201,10 @@ def quantize_q8k(x_ptr: int, y_ptr: int, n: int, rounding: int, stream: int = 0)
 
 def gemv_q8k(ggml_type: int, w_ptr: int, xq_ptr: int, y_ptr: int, rows: int, cols: int, stream: int = 0) -> None:
     check(load_library().mcpm_gemv_q8k(ggml_type, w_ptr, xq_ptr, y_ptr, rows, cols, stream), "mcpm_gemv_q8k")
+
+
+def gemv_q8_0(w_ptr: int, x_ptr: int, y_ptr: int, rows: int, cols: int, stream: int = 0) -> None:
+    check(load_library().mcpm_gemv_q8_0_f32(w_ptr, x_ptr, y_ptr, rows, cols, stream), "mcpm_gemv_q8_0_f32")
 
 
 def gemv_blocksums(ggml_type: int, w_ptr: int, xq_ptr: int, isum_ptr: int, aux_ptr: int, rows: int, cols: int,

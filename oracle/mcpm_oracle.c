@@ -275,6 +275,11 @@ void orc_gemv_q6k_q8k(const void* w, const void* xq, float* y, int rows, int col
 }
 
 /* gemv_q8_0 (ops.cpp:58-79). */
+/* gemv_q8_0 (src/ops/ops.cpp:58-79) as the reference build evaluates it (-O3 -ffast-math
+ * -mavx2 -mfma; verified bit for bit against that build): per 32-block, eight fp32 lanes
+ * k: A_k = fma(q[k], x[k], q[k+8]*x[k+8]), B_k = fma(q[k+16], x[k+16], q[k+24]*x[k+24]),
+ * v_k = B_k + A_k; c_k = v_{k+4} + v_k, e_k = c_{k+2} + c_k, local = e_1 + e_0;
+ * row = fma(fp16(d), local, row) over the blocks in order. */
 void orc_gemv_q8_0(const void* w, const float* x, float* y, int rows, int cols) {
     const int nb = cols / 32;
 #pragma omp parallel for schedule(static)
@@ -282,9 +287,19 @@ void orc_gemv_q8_0(const void* w, const float* x, float* y, int rows, int cols) 
         const blk_q8_0* row = (const blk_q8_0*)w + (size_t)r * nb;
         float sum = 0.0f;
         for (int b = 0; b < nb; ++b) {
-            float local = 0.0f;
-            for (int i = 0; i < 32; ++i) local += (float)row[b].qs[i] * x[32 * b + i];
-            sum += local * orc_fp16_to_fp32(row[b].d);
+            const int8_t* q = row[b].qs;
+            const float* xb = x + 32 * b;
+            float v[8];
+            for (int k = 0; k < 8; ++k) {
+                const float a = fmaf((float)q[k], xb[k], (float)q[k + 8] * xb[k + 8]);
+                const float bb = fmaf((float)q[k + 16], xb[k + 16], (float)q[k + 24] * xb[k + 24]);
+                v[k] = bb + a;
+            }
+            float c[4], e[2];
+            for (int k = 0; k < 4; ++k) c[k] = v[k + 4] + v[k];
+            for (int k = 0; k < 2; ++k) e[k] = c[k + 2] + c[k];
+            const float local = e[1] + e[0];
+            sum = fmaf(orc_fp16_to_fp32(row[b].d), local, sum);
         }
         y[r] = sum;
     }

@@ -12,6 +12,10 @@ Fixtures:
                               on the seed-0 synthetic Q4_K_M model: greedy tokens, top-32
                               logits per step and every 256th logit
   reference_variability.json  reference at 1 vs 4 OpenMP threads on the same steps
+  reference_q8_0.npz          gemv_q8_0 of the reference build (fp32 activations) on seeded
+                              Q8_0 matrices with the config-1 distributions
+
+    python tests/golden/make_golden.py --q8_0     # only reference_q8_0.npz
 """
 import json
 import os
@@ -67,6 +71,29 @@ def kernels():
     return out
 
 
+Q8_0_CASES = [(64, 2048, 301), (40, 6144, 302), (16, 256, 303)]
+
+
+def q8_0_inputs(rows, cols, seed):
+    rng = np.random.Generator(np.random.PCG64([seed, 3]))
+    nb = rows * cols // 32
+    blk = np.zeros(nb, dtype=[("d", "<f2"), ("qs", "i1", 32)])
+    blk["d"] = np.abs(rng.normal(0, 2e-3, nb)).astype(np.float16)
+    blk["qs"] = rng.integers(-127, 128, (nb, 32))
+    x = rng.normal(0, 1, cols).astype(np.float32)
+    return blk.view(np.uint8), x
+
+
+def q8_0_kernels():
+    import oracle as O
+    ref = O.Ref()
+    out = {}
+    for rows, cols, seed in Q8_0_CASES:
+        w, x = q8_0_inputs(rows, cols, seed)
+        out[f"q8_0_{rows}x{cols}_y"] = ref.gemv_f32(8, w, x, rows, cols)
+    return out
+
+
 DECODE_CHILD = r"""
 import sys, json, numpy as np
 sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[2])
@@ -102,6 +129,9 @@ def main():
     from mcpm import synth
     O.build(reference=True)
     assert O.have_ref(), "needs the reference tree"
+    np.savez_compressed(os.path.join(HERE, "reference_q8_0.npz"), **q8_0_kernels())
+    if "--q8_0" in sys.argv:
+        return
     ref_tree = O.REFERENCE_TREE
     with open(os.path.join(HERE, "metadata_digest.json"), "w") as f:
         json.dump(metadata_digest(ref_tree), f, indent=1)

@@ -86,6 +86,43 @@ def test_gemv_matches_reference_build(cuda, oracle, ref, ggml_type):
     assert np.array_equal(yd.cpu().numpy(), ref.gemv_q8k(ggml_type, w, xq, rows, cols))
 
 
+def q8_0_matrix(rows, cols, seed):
+    """Q8_0 blocks with the config-1 distributions: fp16 d ~ |N(0, 2e-3)|, int8 uniform -127..127."""
+    rng = np.random.default_rng(seed)
+    nb = rows * cols // 32
+    blk = np.zeros(nb, dtype=[("d", "<f2"), ("qs", "i1", 32)])
+    blk["d"] = np.abs(rng.normal(0, 2e-3, nb)).astype(np.float16)
+    blk["qs"] = rng.integers(-127, 128, (nb, 32))
+    return blk.view(np.uint8)
+
+
+@pytest.mark.parametrize("rows,cols", [(2048, 2048), (256, 2048), (12288, 2048), (2048, 6144), (1, 256), (37, 8192)])
+def test_gemv_q8_0_bitexact(cuda, oracle, rows, cols):
+    """Q8_0 x fp32 GEMV against the restatement of the reference build's evaluation order."""
+    from mcpm import engine as E
+    w = q8_0_matrix(rows, cols, rows + cols)
+    x = np.random.default_rng(cols).normal(0, 1, cols).astype(np.float32)
+    wd, xd = _dev(cuda, w), _dev(cuda, x)
+    yd = cuda.zeros(rows, dtype=cuda.float32, device="cuda")
+    E.gemv_q8_0(wd.data_ptr(), xd.data_ptr(), yd.data_ptr(), rows, cols)
+    cuda.cuda.synchronize()
+    want = oracle.gemv_q8_0(w, x, rows, cols)
+    got = yd.cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), np.max(np.abs(got - want))
+
+
+def test_gemv_q8_0_matches_reference_build(cuda, ref):
+    from mcpm import engine as E
+    rows, cols = 300, 6144
+    w = q8_0_matrix(rows, cols, 5)
+    x = np.random.default_rng(6).normal(0, 1, cols).astype(np.float32)
+    wd, xd = _dev(cuda, w), _dev(cuda, x)
+    yd = cuda.zeros(rows, dtype=cuda.float32, device="cuda")
+    E.gemv_q8_0(wd.data_ptr(), xd.data_ptr(), yd.data_ptr(), rows, cols)
+    cuda.cuda.synchronize()
+    assert np.array_equal(yd.cpu().numpy().view(np.uint32), ref.gemv_f32(8, w, x, rows, cols).view(np.uint32))
+
+
 @pytest.mark.parametrize("ggml_type", [12, 14])
 def test_blocksums_exact(cuda, oracle, ggml_type):
     from mcpm import engine as E

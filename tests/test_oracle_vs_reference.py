@@ -49,6 +49,16 @@ def test_gemv_and_quantize_bitexact_vs_reference_golden(oracle, rows, cols, name
     assert np.array_equal(y.view(np.uint32), g[f"{name}_{rows}x{cols}_y"].view(np.uint32))
 
 
+@pytest.mark.parametrize("rows,cols,seed", [(64, 2048, 301), (40, 6144, 302), (16, 256, 303)])
+def test_gemv_q8_0_bitexact_vs_reference_golden(oracle, rows, cols, seed):
+    """Q8_0 x fp32 GEMV (gemv_q8_0 as the reference build evaluates it)."""
+    import make_golden as mg
+    g = np.load(golden("reference_q8_0.npz"))
+    w, x = mg.q8_0_inputs(rows, cols, seed)
+    y = oracle.gemv_q8_0(w, x, rows, cols)
+    assert np.array_equal(y.view(np.uint32), g[f"q8_0_{rows}x{cols}_y"].view(np.uint32))
+
+
 def test_rmsnorm_quantize_vs_reference_golden(oracle):
     """Integer-valued input: the sum of squares is exact in any order, so only the
     reference's rsqrt estimate can differ; the int8 values and block sums must match."""
@@ -141,6 +151,12 @@ def test_live_reference_gemv_bitexact(oracle, ref, t, rows, cols):
     xq = ref.quantize_q8k(x)
     assert np.array_equal(xq.view(np.uint8), oracle.quantize_q8k(x, 0, 1).view(np.uint8))
     assert np.array_equal(ref.gemv_q8k(t, w, xq, rows, cols), oracle.gemv_q8k(t, w, xq, rows, cols, 1, 1))
+
+
+def test_live_reference_gemv_q8_0_bitexact(oracle, ref):
+    import make_golden as mg
+    w, x = mg.q8_0_inputs(200, 2048, 777)
+    assert np.array_equal(ref.gemv_f32(8, w, x, 200, 2048).view(np.uint32), oracle.gemv_q8_0(w, x, 200, 2048).view(np.uint32))
 
 
 def test_live_reference_embedding_exact(oracle, ref, model_path):
