@@ -2,6 +2,8 @@
 batch 1 per GPU).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py --config 1        # config 1: isolated GEMV sweep, one JSON line per case
+    python bench.py --config 2        # config 2: decode after an 8192-position prefill
 
 A step is one greedy decode token.  Each rank prefills its own seeded 128-token prompt
 (untimed), runs W warm-up tokens, then K timed tokens chained on the device (the argmax of
@@ -38,6 +40,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prefill length (untimed)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", type=int, default=0, choices=[0, 1, 2],
+                    help="0: batch-1 decode (headline); 1: GEMV sweep; 2: long-context decode")
     return ap.parse_args()
 
 
@@ -178,12 +182,106 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+GEMV_CASES = [   # (name, ggml type, rows, cols): the config-1 shapes (rows x cols = out x in)
+    ("o_proj 2048x2048", 12, 2048, 2048), ("k/v 256x2048", 12, 256, 2048), ("v 256x2048", 14, 256, 2048),
+    ("gate+up 12288x2048", 12, 12288, 2048), ("down 2048x6144", 12, 2048, 6144), ("down 2048x6144", 14, 2048, 6144),
+    ("lm_head 130560x2048", 14, 130560, 2048),
+    ("o_proj 2048x2048", 8, 2048, 2048), ("k/v 256x2048", 8, 256, 2048), ("gate+up 12288x2048", 8, 12288, 2048),
+    ("down 2048x6144", 8, 2048, 6144), ("lm_head 130560x2048", 8, 130560, 2048),
+]
+TYPE_NAME = {8: "Q8_0", 12: "Q4_K", 14: "Q6_K"}
+
+
+def run_gemv_sweep(args):
+    """Config 1: each GEMV alone, weights rotated over enough copies that every launch reads
+    them from HBM (> 256 MB in flight), timed with CUDA events; the reference build's GEMV on
+    the host cores is timed on the same matrix for comparison (fp32 activations for Q8_0,
+    Q8_K activations otherwise, as the reference's matmul / matmul_q8k)."""
+    import numpy as np
+    import torch
+    from mcpm import engine as E, spec, synth
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle as O
+    torch.cuda.set_device(0)
+    peak, peak_kind = measured_peaks()
+    ref = O.Ref() if O.have_ref() else None
+    orc = O.Oracle()
+    for name, t, rows, cols in GEMV_CASES:
+        w = synth.tensor_bytes(spec.TensorInfo("w", t, (cols, rows)), np.random.Generator(np.random.PCG64([rows, cols, t])))
+        nbytes = w.size
+        copies = max(1, -(-(256 << 20) // nbytes))
+        wd = torch.from_numpy(w).cuda().repeat(copies)
+        x = np.random.default_rng(cols).normal(0, 1, cols).astype(np.float32)
+        xd = torch.from_numpy(x).cuda()
+        xq = orc.quantize_q8k(x, 0, 1)
+        xqd = torch.from_numpy(xq.view(np.uint8).copy()).cuda()
+        yd = torch.zeros(rows, dtype=torch.float32, device="cuda")
+
+        def launch(i, stream=0):
+            ptr = wd.data_ptr() + (i % copies) * nbytes
+            if t == 8:
+                E.gemv_q8_0(ptr, xd.data_ptr(), yd.data_ptr(), rows, cols, stream)
+            else:
+                E.gemv_q8k(t, ptr, xqd.data_ptr(), yd.data_ptr(), rows, cols, stream)
+        for i in range(max(3, args.warmup)):
+            launch(i)
+        torch.cuda.synchronize()
+        # the timed launches replay as one CUDA graph, so host launch cost does not show
+        reps = max(20, min(args.steps, 200))
+        side = torch.cuda.Stream()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            for i in range(reps):
+                launch(i, side.cuda_stream)
+        graph.replay()
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(side):   # replay() launches on the current stream
+            ev0.record()
+            graph.replay()
+            ev1.record()
+        ev1.synchronize()
+        ms = ev0.elapsed_time(ev1) / reps
+        del graph
+        act = cols * 4 if t == 8 else (cols // 256) * 292
+        gbs = (nbytes + act + rows * 4) / (ms * 1e-3) / 1e9
+        cpu = None
+        if ref is not None:
+            nrep = 3 if nbytes > (64 << 20) else 20
+            t0 = time.perf_counter()
+            for _ in range(nrep):
+                if t == 8:
+                    ref.gemv_f32(8, w, x, rows, cols)
+                else:
+                    ref.gemv_q8k(t, w, xq, rows, cols)
+            cpu_ms = (time.perf_counter() - t0) / nrep * 1e3
+            cpu = {"value": round(nbytes / (cpu_ms * 1e-3) / 1e9, 2), "unit": "GB/s", "cores": ref.threads(),
+                   "kind": "reference", "sample": f"{nrep} calls of the reference build's GEMV on the same matrix"}
+        print(json.dumps({
+            "metric": "GEMV weight-stream GB/s (batch 1)", "config": {"workload": "config1", "case": name,
+                                                                      "type": TYPE_NAME[t], "rows": rows, "cols": cols,
+                                                                      "l2": f"{copies} weight copies rotated", "timing": "CUDA graph of repeated launches"},
+            "value": round(gbs, 1), "unit": "GB/s", "us_per_launch": round(ms * 1e3, 2), "higher_is_better": True,
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 4), "peak_kind": peak_kind},
+            "cpu_baseline": cpu}), flush=True)
+        del wd
+
+
 def main():
     args = parse()
     rank, world, local = dist_env()
     if args.impl == "reference":
         run_reference(args, rank, world)
         return
+    if args.config == 1:
+        if rank == 0:
+            run_gemv_sweep(args)
+        return
+    if args.config == 2 and args.prompt == PROMPT:   # config 2: 8192-position context
+        args.prompt = 8192
+        if args.steps == 256:
+            args.steps = 128
     import numpy as np
     import torch
     from mcpm import engine as E, spec, synth
@@ -257,13 +355,16 @@ def main():
         per_launch_ms = ms_max / args.steps
         achieved = bytes_per_tok / (per_launch_ms * 1e-3) / 1e9
         value = world * args.steps / (ms_max * 1e-3)
-        cb = None if args.no_cpu_baseline else cpu_baseline(path)
+        # config 2: the reference's CPU prefill of 8192 positions alone takes minutes; no CPU line
+        cb = None if (args.no_cpu_baseline or args.config == 2) else cpu_baseline(path)
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_launch_ms, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 dot / fp32",
             "data": "synthetic (seeded random-init GGUF, Q4_K_M layout)",
-            "config": {"workload": "config0: MiniCPM5-2B Q4_K_M greedy decode, batch 1 per GPU",
+            "config": {"workload": ("config2: MiniCPM5-2B Q4_K_M greedy decode after a long prefill, batch 1 per GPU"
+                                    if args.config == 2 else
+                                    "config0: MiniCPM5-2B Q4_K_M greedy decode, batch 1 per GPU"),
                        "prompt": args.prompt, "positions": [first_pos, first_pos + args.steps - 1],
                        "parallelism": f"dp{world} (independent sequences)",
                        "l2": "inputs larger than L2 (1.41 GB of weights per token)"},
