@@ -49,6 +49,16 @@ def dist_env():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
 
 
+def max_over_ranks(x: float, pg, device: str = "cuda") -> float:
+    """Largest value of `x` over the ranks of process group `pg` (x itself without one).
+    Timings are reduced this way: the job is as slow as its slowest rank."""
+    import torch
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    if pg is not None:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    return float(t.item())
+
+
 def measured_peaks():
     try:
         with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
@@ -324,10 +334,7 @@ def main():
     eng.sync()
     ms = ev0.elapsed_time(ev1)
     clocks = clk.stop() if clk else None
-    t_dev = torch.tensor([ms], dtype=torch.float64, device="cuda")
-    if pg:
-        pg.all_reduce(t_dev, op=pg.ReduceOp.MAX)
-    ms_max = float(t_dev.item())
+    ms_max = max_over_ranks(ms, pg)
 
     # e2e: the reference-facing call with host buffers (token in, argmax out), synchronous per step
     e2e_steps = min(args.steps, 64)
@@ -339,11 +346,7 @@ def main():
     for _ in range(e2e_steps):
         tok = eng.forward_greedy(tok, pos)
         pos += 1
-    e2e_s = time.perf_counter() - t0
-    e2e_t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
-    if pg:
-        pg.all_reduce(e2e_t, op=pg.ReduceOp.MAX)
-    e2e_s = float(e2e_t.item())
+    e2e_s = max_over_ranks(time.perf_counter() - t0, pg)
 
     if rank == 0:
         tensors = spec.q4km_table()

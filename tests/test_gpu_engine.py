@@ -94,3 +94,24 @@ def test_bad_file(cuda, tmp_path):
         e.forward(1, 0)
     assert ei.value.status == E.NOT_LOADED
     e.close()
+
+
+def test_cpp_facade_token_loop(cuda, model_path, tmp_path):
+    """A token loop written against the reference's MiniCPM5Engine interface (C++ facade over
+    the C ABI) produces the same greedy tokens as the Python binding."""
+    import subprocess
+    from mcpm import engine as E, synth
+    from test_abi import facade_build
+    exe = facade_build(tmp_path)
+    prompt = [int(t) for t in synth.prompt_ids(5)]
+    r = subprocess.run([exe, model_path, "4"] + [str(t) for t in prompt], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    got = [int(v) for v in r.stdout.split()]
+    e = E.MiniCPM5Engine(device=0, max_seq=16)
+    assert e.load_model(model_path)
+    want, tok = [], None
+    for pos in range(9):
+        tok = e.forward_greedy(prompt[pos] if pos < 5 else tok, pos)
+        want.append(tok)
+    e.close()
+    assert got == want
