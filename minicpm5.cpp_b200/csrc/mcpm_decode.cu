@@ -42,18 +42,34 @@ __device__ __forceinline__ const float* meta_f32(const DecodeParams& p, uint32_t
 // GEMV partials and the staged fp32 activation share one scratch region.
 constexpr int SCRATCH_BYTES = MAX_TASKS * PART_WORDS * 4 > N_EMBD * 4 ? MAX_TASKS * PART_WORDS * 4 : N_EMBD * 4;
 
+// Dynamic shared memory of the decode kernel (and of k_attention, launched with the same
+// size): fixed offsets from one base, so no pointer to it is held in a register.
+extern __shared__ __align__(1024) uint8_t smem_raw[];
+constexpr int SM_WBUF0 = 0;
+constexpr int SM_WBUF1 = WBUF_BYTES + WBUF_SLACK;
+constexpr int SM_XQ = 2 * (WBUF_BYTES + WBUF_SLACK);
+constexpr int SM_SCRATCH = SM_XQ + ((static_cast<int>(sizeof(XQSmem)) + 127) & ~127);
+constexpr int SM_ROWVAL = SM_SCRATCH + SCRATCH_BYTES;
+constexpr int SM_RED = SM_ROWVAL + ROWVAL_FLOATS * 4;
+constexpr int SM_WBAR = SM_RED + 32 * 4;
+constexpr int SM_LMBAR = SM_WBAR + 8 * 8;
+constexpr int SM_FLAG = SM_LMBAR + 4 * 8;
+constexpr int SM_ROWS = SM_FLAG + 16;
+constexpr int SM_META = SM_ROWS + 16;
+constexpr int SM_BYTES = SM_META + MAX_LAYERS * static_cast<int>(sizeof(LayerMeta));
+
 struct Smem {
-    uint8_t* wbuf[2];
-    XQSmem* xq;
-    int* part;
-    float* xs;       // staged fp32 activation vector (N_EMBD); same storage as part
-    float* rowval;
-    float* red;      // 32 floats
-    uint64_t* wbar;  // [2][4]
-    uint64_t* lmbar; // [4]
-    int* flag;
-    CtaRows* rows;
-    LayerMeta* meta;   // [n_layer]
+    __device__ uint8_t* wbuf(int i) const { return smem_raw + (i ? SM_WBUF1 : SM_WBUF0); }
+    __device__ XQSmem* xq() const { return reinterpret_cast<XQSmem*>(smem_raw + SM_XQ); }
+    __device__ int* part() const { return reinterpret_cast<int*>(smem_raw + SM_SCRATCH); }   // GEMV scratch
+    __device__ float* xs() const { return reinterpret_cast<float*>(smem_raw + SM_SCRATCH); }  // same storage
+    __device__ float* rowval() const { return reinterpret_cast<float*>(smem_raw + SM_ROWVAL); }
+    __device__ float* red() const { return reinterpret_cast<float*>(smem_raw + SM_RED); }      // 32 floats
+    __device__ uint64_t* wbar() const { return reinterpret_cast<uint64_t*>(smem_raw + SM_WBAR); }   // [2][4]
+    __device__ uint64_t* lmbar() const { return reinterpret_cast<uint64_t*>(smem_raw + SM_LMBAR); } // [4]
+    __device__ int* flag() const { return reinterpret_cast<int*>(smem_raw + SM_FLAG); }
+    __device__ CtaRows* rows() const { return reinterpret_cast<CtaRows*>(smem_raw + SM_ROWS); }
+    __device__ LayerMeta* meta() const { return reinterpret_cast<LayerMeta*>(smem_raw + SM_META); }   // [n_layer]
 };
 
 __device__ __forceinline__ void split_range(int n, int cta, int ncta, int& a, int& b) {
@@ -126,17 +142,17 @@ __device__ int phase_cols(int kind) { return kind == 3 ? N_FF : N_EMBD; }
 // Thread 0 only: arm the four barriers of buffer (wp & 1) and issue weight phase `wp`.
 __device__ void issue_weight_phase(const DecodeParams& p, const Smem& s, int wp, int cta, int ncta) {
     const int buf = wp & 1;
-    uint64_t* bars = s.wbar + 4 * buf;
+    uint64_t* bars = s.wbar() + 4 * buf;
     const int l = wp >> 2, kind = wp & 3;
-    const LayerMeta& M = s.meta[l];
-    const PhaseLayout pl = phase_layout(M, *s.rows, kind);
+    const LayerMeta& M = s.meta()[l];
+    const PhaseLayout pl = phase_layout(M, *s.rows(), kind);
     const uint64_t pol = l2_evict_first_policy();
 #pragma unroll
     for (int i = 0; i < 3; ++i) {
         mbar_expect_tx(&bars[i], pl.bytes[i]);
         if (pl.bytes[i]) {
             const int rb = row_bytes(phase_type(M, kind, i), phase_cols(kind));
-            bulk_g2s_stream(s.wbuf[buf] + pl.off[i], phase_src(p, M, kind, i) + static_cast<size_t>(pl.row0[i]) * rb,
+            bulk_g2s_stream(s.wbuf(buf) + pl.off[i], phase_src(p, M, kind, i) + static_cast<size_t>(pl.row0[i]) * rb,
                             pl.bytes[i], &bars[i], pol);
         }
     }
@@ -156,13 +172,13 @@ __device__ LmPlan lm_plan(const DecodeParams& p, int cta, int ncta) {
     q.nstages = (q.r1 - q.r0 + q.sr - 1) / q.sr;
     return q;
 }
-__device__ uint8_t* lm_slot(const Smem& s, int slot) { return s.wbuf[slot]; }
+__device__ uint8_t* lm_slot(const Smem& s, int slot) { return s.wbuf(slot); }
 __device__ void issue_lm_stage(const DecodeParams& p, const Smem& s, const LmPlan& q, int st) {
     const int slot = st & 1;
     const int a = q.r0 + st * q.sr, n = min(q.sr, q.r1 - a);
     const uint32_t bytes = n > 0 ? static_cast<uint32_t>(n) * q.rb : 0;
-    mbar_expect_tx(&s.lmbar[slot], bytes);
-    if (bytes) bulk_g2s_stream(lm_slot(s, slot), p.lm + static_cast<size_t>(a) * q.rb, bytes, &s.lmbar[slot], l2_evict_first_policy());
+    mbar_expect_tx(&s.lmbar()[slot], bytes);
+    if (bytes) bulk_g2s_stream(lm_slot(s, slot), p.lm + static_cast<size_t>(a) * q.rb, bytes, &s.lmbar()[slot], l2_evict_first_policy());
 }
 
 // Bounded grid barrier (all CTAs co-resident: cooperative launch).  A monotonic arrival
@@ -259,8 +275,8 @@ __device__ void prefetch_attention(const DecodeParams& p, int l, int cta) {
 // L2 prefetch of layer l's two norm weight vectors (8 KB each), by CTA 0 only.
 __device__ void prefetch_norms(const DecodeParams& p, const Smem& s, int l, int cta) {
     if (cta != 0) return;
-    bulk_prefetch_l2(meta_f32(p, s.meta[l].attn_norm), N_EMBD * 4);
-    bulk_prefetch_l2(meta_f32(p, s.meta[l].ffn_norm), N_EMBD * 4);
+    bulk_prefetch_l2(meta_f32(p, s.meta()[l].attn_norm), N_EMBD * 4);
+    bulk_prefetch_l2(meta_f32(p, s.meta()[l].ffn_norm), N_EMBD * 4);
 }
 
 // Waits for this CTA's part of weight phase wp; false on timeout.
@@ -268,7 +284,7 @@ __device__ bool wait_weights(const DecodeParams& p, const Smem& s, int wp) {
     const int buf = wp & 1;
     const uint32_t parity = (wp >> 1) & 1;
     bool ok = true;
-    for (int i = 0; i < 4; ++i) ok &= mbar_wait(&s.wbar[4 * buf + i], parity, p.err);
+    for (int i = 0; i < 4; ++i) ok &= mbar_wait(&s.wbar()[4 * buf + i], parity, p.err);
     return !__syncthreads_or(!ok);   // one decision for the whole CTA
 }
 
@@ -332,8 +348,8 @@ __device__ bool load8_epoch(const unsigned long long* src, unsigned epoch, int t
 }
 
 // xq <- Q8_K of (x * w) * rms(x), canonical order; rounding per template argument.
-// SRC: X_SMEM (x already staged in s.xs), X_EPOCH (x published by the previous phase as
-// epoch-tagged words in p.xll; x is staged in s.xs).  False (for the whole CTA) when the
+// SRC: X_SMEM (x already staged in s.xs()), X_EPOCH (x published by the previous phase as
+// epoch-tagged words in p.xll; x is staged in s.xs()).  False (for the whole CTA) when the
 // wait for x timed out.
 enum { X_SMEM = 1, X_EPOCH = 2 };
 template <bool AWAY, int SRC>
@@ -344,14 +360,14 @@ __device__ bool norm_quant(const DecodeParams& p, const float* x, unsigned epoch
         w0 = __ldg(reinterpret_cast<const float4*>(w + 256 * warp + 8 * lane));
         w1 = __ldg(reinterpret_cast<const float4*>(w + 256 * warp + 8 * lane + 4));
     }
-    float* red = s.red;
+    float* red = s.red();
     bool ok = true;
     if (tid < 256) {
         float xv[8];
         if (SRC == X_EPOCH) {
             ok = load8_epoch(p.xll, epoch, tid, xv, p.err);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) s.xs[tid + 256 * i] = xv[i];
+            for (int i = 0; i < 8; ++i) s.xs()[tid + 256 * i] = xv[i];
         } else {
 #pragma unroll
             for (int i = 0; i < 8; ++i) xv[i] = x[tid + 256 * i];
@@ -368,14 +384,14 @@ __device__ bool norm_quant(const DecodeParams& p, const float* x, unsigned epoch
         const float ss = __fadd_rn(__fadd_rn(__fadd_rn(red[0], red[1]), __fadd_rn(red[2], red[3])),
                                    __fadd_rn(__fadd_rn(red[4], red[5]), __fadd_rn(red[6], red[7])));
         const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(N_EMBD)), 1e-6f)));
-        const float4 xa = *reinterpret_cast<const float4*>(s.xs + 256 * warp + 8 * lane);
-        const float4 xc = *reinterpret_cast<const float4*>(s.xs + 256 * warp + 8 * lane + 4);
+        const float4 xa = *reinterpret_cast<const float4*>(s.xs() + 256 * warp + 8 * lane);
+        const float4 xc = *reinterpret_cast<const float4*>(s.xs() + 256 * warp + 8 * lane + 4);
         const float xb[8] = {xa.x, xa.y, xa.z, xa.w, xc.x, xc.y, xc.z, xc.w};
         const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
         float y[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) y[k] = __fmul_rn(__fmul_rn(xb[k], wv[k]), rms);
-        quant_block_warp<AWAY>(y, s.xq->qs[warp], &s.xq->d[warp], s.xq->bsums[warp]);
+        quant_block_warp<AWAY>(y, s.xq()->qs[warp], &s.xq()->d[warp], s.xq()->bsums[warp]);
     }
     __syncthreads();
     return true;
@@ -390,7 +406,7 @@ __device__ __forceinline__ unsigned x_epoch(unsigned seq, int k) { return (seq <
 
 // ------------------------------------------------------------------------ phases
 __device__ bool phase_qkv(const DecodeParams& p, const Smem& s, int l, int token, int cta, int ncta, unsigned seq) {
-    const LayerMeta& L = s.meta[l];
+    const LayerMeta& L = s.meta()[l];
     const int a = L.qkv0, b = L.qkv1;   // same split as phase_layout
     // this thread's RoPE factors (pair pr = threadIdx.x), fetched before the norm
     const int pr0 = threadIdx.x, R0 = a + 2 * pr0;
@@ -398,11 +414,11 @@ __device__ bool phase_qkv(const DecodeParams& p, const Smem& s, int l, int token
     if (pr0 < (b - a) / 2 && R0 < N_EMBD + KV_DIM)
         cs0 = __ldg(p.rope + static_cast<size_t>(p.pos) * (HEAD_DIM / 2) + ((R0 & (HEAD_DIM - 1)) >> 1));
     if (l == 0) {
-        embed_row(p, token, s.xs);
+        embed_row(p, token, s.xs());
         __syncthreads();
         if (cta == 0)
-            for (int i = threadIdx.x; i < N_EMBD; i += blockDim.x) p.x[i] = s.xs[i];
-        norm_quant<true, X_SMEM>(p, s.xs, 0, meta_f32(p, L.attn_norm), s);
+            for (int i = threadIdx.x; i < N_EMBD; i += blockDim.x) p.x[i] = s.xs()[i];
+        norm_quant<true, X_SMEM>(p, s.xs(), 0, meta_f32(p, L.attn_norm), s);
     } else {
         if (!norm_quant<true, X_EPOCH>(p, nullptr, x_epoch(seq, 2 * l), meta_f32(p, L.attn_norm), s)) return false;
         trace_mark(p, 3 + 2 * (5 * (l - 1) + 4));
@@ -411,14 +427,14 @@ __device__ bool phase_qkv(const DecodeParams& p, const Smem& s, int l, int token
     trace_step(p, l, 0, 1);
     if (!wait_weights(p, s, 4 * l)) return false;
     trace_step(p, l, 0, 2);
-    const PhaseLayout pl = phase_layout(L, *s.rows, 0);
+    const PhaseLayout pl = phase_layout(L, *s.rows(), 0);
     const int lo[3] = {0, N_EMBD, N_EMBD + KV_DIM};
-    float* rv = s.rowval;
+    float* rv = s.rowval();
 #pragma unroll
     for (int i = 0; i < 3; ++i) {
         if (pl.nrows[i] == 0) continue;   // uniform across the CTA
         const int base = lo[i] + pl.row0[i] - a;
-        gemv_rows(phase_type(L, 0, i), s.wbuf[0] + pl.off[i], pl.nrows[i], N_EMBD / 256, *s.xq, s.part, MAX_TASKS,
+        gemv_rows(phase_type(L, 0, i), s.wbuf(0) + pl.off[i], pl.nrows[i], N_EMBD / 256, *s.xq(), s.part(), MAX_TASKS,
                   rv + base, (p.trace && l == 1 && cta == 0 && i == 0) ? p.trace + TRACE_GEMV + 9 : nullptr);
     }
     trace_step(p, l, 0, 3);
@@ -493,7 +509,7 @@ __device__ __forceinline__ int attn_chunks(int n) {
 __device__ void attention_unit32(const DecodeParams& p, const Smem& s, int l, int g, int c, int t0, int np,
                                  unsigned seq) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, j = lane & 7, G = lane >> 3;
-    float* vb = reinterpret_cast<float*>(s.wbuf[0]);   // [32][128] V rows of the chunk
+    float* vb = reinterpret_cast<float*>(s.wbuf(0));   // [32][128] V rows of the chunk
     float* sc = vb + 32 * HEAD_DIM;                     // [8][32] scores -> probabilities
     float* stat = sc + 8 * 32;                          // m[8], l[8]
     float* qsm = stat + 32;                             // [8][128] q of the group (epoch path)
@@ -638,7 +654,7 @@ __device__ void phase_attention(const DecodeParams& p, const Smem& s, int l, int
     const int P = 32 * ((n + 2047) / 2048);
     const int C = (n + P - 1) / P;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    float* qh = reinterpret_cast<float*>(s.wbuf[0]);   // [8][128]
+    float* qh = reinterpret_cast<float*>(s.wbuf(0));   // [8][128]
     float* kb = qh + 8 * HEAD_DIM;                      // [32][128] staged K rows
     float* vb = kb + 32 * HEAD_DIM;                     // [32][128] staged V rows
     float* sc = vb + 32 * HEAD_DIM;                     // [8][ATT_SC_STRIDE] scores -> probabilities
@@ -732,11 +748,11 @@ __device__ void phase_attention(const DecodeParams& p, const Smem& s, int l, int
         if (tid == 0) {
             __threadfence();
             const unsigned old = atomicAdd(&p.cnt[g], 1u);
-            *s.flag = (old == static_cast<unsigned>(C - 1));
+            *s.flag() = (old == static_cast<unsigned>(C - 1));
             if (old == static_cast<unsigned>(C - 1)) atomicExch(&p.cnt[g], 0u);
         }
         __syncthreads();
-        if (!*s.flag) continue;
+        if (!*s.flag()) continue;
         // ---- last CTA of this KV group combines the chunks of its 8 heads
         __threadfence();
         if (warp < 8) {
@@ -791,26 +807,26 @@ __device__ void load_q8k_blocks(const uint8_t* src, int nblocks, const Smem& s) 
     const int tid = threadIdx.x;
     for (int i = tid; i < nblocks * 64; i += blockDim.x) {   // qs words
         const int b = i >> 6, wd = i & 63;
-        reinterpret_cast<uint32_t*>(s.xq->qs[b])[wd] =
+        reinterpret_cast<uint32_t*>(s.xq()->qs[b])[wd] =
             __ldcg(reinterpret_cast<const unsigned int*>(src + static_cast<size_t>(b) * Q8K_BYTES + 4) + wd);
     }
     for (int i = tid; i < nblocks * 8; i += blockDim.x) {    // bsums (8 words per block)
         const int b = i >> 3, wd = i & 7;
-        reinterpret_cast<uint32_t*>(s.xq->bsums[b])[wd] =
+        reinterpret_cast<uint32_t*>(s.xq()->bsums[b])[wd] =
             __ldcg(reinterpret_cast<const unsigned int*>(src + static_cast<size_t>(b) * Q8K_BYTES + 260) + wd);
     }
-    if (tid < nblocks) s.xq->d[tid] = __ldcg(reinterpret_cast<const float*>(src + static_cast<size_t>(tid) * Q8K_BYTES));
+    if (tid < nblocks) s.xq()->d[tid] = __ldcg(reinterpret_cast<const float*>(src + static_cast<size_t>(tid) * Q8K_BYTES));
     __syncthreads();
 }
 
 // Every CTA combines the attention chunks of all 16 heads (same operations and order as
-// the last-CTA combine) and quantises the result ties-to-even straight into s.xq.
+// the last-CTA combine) and quantises the result ties-to-even straight into s.xq().
 __device__ void combine_attention(const DecodeParams& p, const Smem& s, int l, int cta) {
     // warp = head h, lane = dims 4*lane .. 4*lane+3: the chunk weights of a head never leave
     // its warp, so loads, max, exp, the L chain and the O chains run without a CTA barrier.
     const int n = p.pos + 1, C = attn_chunks(n);
     const int tid = threadIdx.x, lane = tid & 31, h = tid >> 5;
-    float* ab = s.xs;   // [2048]
+    float* ab = s.xs();   // [2048]
     const float* ph = p.att_part + static_cast<size_t>(h) * ATT_MAX_CHUNKS * ATT_PART_STRIDE;
     const float2 ml = lane < C ? *reinterpret_cast<const float2*>(ph + lane * ATT_PART_STRIDE) : make_float2(0.f, 0.f);
     float4 v[DIST_COMBINE_MAX];
@@ -844,14 +860,14 @@ __device__ void combine_attention(const DecodeParams& p, const Smem& s, int l, i
         const float4 a = *reinterpret_cast<const float4*>(ab + 256 * h + 8 * lane);
         const float4 b = *reinterpret_cast<const float4*>(ab + 256 * h + 8 * lane + 4);
         const float y[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-        quant_block_warp<false>(y, s.xq->qs[h], &s.xq->d[h], s.xq->bsums[h]);
+        quant_block_warp<false>(y, s.xq()->qs[h], &s.xq()->d[h], s.xq()->bsums[h]);
     }
     __syncthreads();
 }
 
 __device__ bool phase_o(const DecodeParams& p, const Smem& s, int l, int cta, int ncta, unsigned seq) {
-    const LayerMeta& L = s.meta[l];
-    const PhaseLayout pl = phase_layout(L, *s.rows, 1);
+    const LayerMeta& L = s.meta()[l];
+    const PhaseLayout pl = phase_layout(L, *s.rows(), 1);
     const int r0 = pl.row0[0], n = pl.nrows[0];
     const float xr = threadIdx.x < n ? __ldcg(p.x + r0 + threadIdx.x) : 0.0f;   // residual rows, early
     if (attn_chunks(p.pos + 1) <= DIST_COMBINE_MAX)
@@ -861,10 +877,10 @@ __device__ bool phase_o(const DecodeParams& p, const Smem& s, int l, int cta, in
     trace_step(p, l, 2, 1);
     if (!wait_weights(p, s, 4 * l + 1)) return false;
     trace_step(p, l, 2, 2);
-    gemv_rows(L.to, s.wbuf[1], n, N_EMBD / 256, *s.xq, s.part, MAX_TASKS, s.rowval,
+    gemv_rows(L.to, s.wbuf(1), n, N_EMBD / 256, *s.xq(), s.part(), MAX_TASKS, s.rowval(),
               (p.trace && l == 1 && cta == 0) ? p.trace + TRACE_GEMV + 0 : nullptr);
     if (threadIdx.x < n) {
-        const float xn = __fadd_rn(xr, s.rowval[threadIdx.x]);
+        const float xn = __fadd_rn(xr, s.rowval()[threadIdx.x]);
         p.x[r0 + threadIdx.x] = xn;
         st_epoch(p.xll + r0 + threadIdx.x, xn, x_epoch(seq, 2 * l + 1));
     }
@@ -876,20 +892,20 @@ __device__ bool phase_o(const DecodeParams& p, const Smem& s, int l, int cta, in
 }
 
 __device__ bool phase_gu(const DecodeParams& p, const Smem& s, int l, int cta, int ncta, unsigned seq) {
-    const LayerMeta& L = s.meta[l];
+    const LayerMeta& L = s.meta()[l];
     if (!norm_quant<true, X_EPOCH>(p, nullptr, x_epoch(seq, 2 * l + 1), meta_f32(p, L.ffn_norm), s)) return false;
     trace_mark(p, 3 + 2 * (5 * l + 2));
     trace_cta(p, l, 2, 1);
     trace_step(p, l, 3, 1);
     if (!wait_weights(p, s, 4 * l + 2)) return false;
     trace_step(p, l, 3, 2);
-    const PhaseLayout pl = phase_layout(L, *s.rows, 2);
+    const PhaseLayout pl = phase_layout(L, *s.rows(), 2);
     const int n = pl.nrows[0];
-    float* rv = s.rowval;
-    gemv_rows(L.tg, s.wbuf[0] + pl.off[0], n, N_EMBD / 256, *s.xq, s.part, MAX_TASKS, rv,
+    float* rv = s.rowval();
+    gemv_rows(L.tg, s.wbuf(0) + pl.off[0], n, N_EMBD / 256, *s.xq(), s.part(), MAX_TASKS, rv,
               (p.trace && l == 1 && cta == 0) ? p.trace + TRACE_GEMV + 6 : nullptr);
     trace_step(p, l, 3, 3);
-    gemv_rows(L.tu, s.wbuf[0] + pl.off[1], n, N_EMBD / 256, *s.xq, s.part, MAX_TASKS, rv + 128);
+    gemv_rows(L.tu, s.wbuf(0) + pl.off[1], n, N_EMBD / 256, *s.xq(), s.part(), MAX_TASKS, rv + 128);
     trace_step(p, l, 3, 4);
     for (int r = threadIdx.x; r < n; r += blockDim.x) p.h[pl.row0[0] + r] = canon_silu_mul(rv[r], rv[128 + r]);
     return true;
@@ -899,8 +915,8 @@ __device__ bool phase_gu(const DecodeParams& p, const Smem& s, int l, int cta, i
 // then the next layer's K/V and norm prefetches (or the LM head's second stage).
 __device__ bool phase_down(const DecodeParams& p, const Smem& s, int l, int cta, int ncta, unsigned seq,
                            const LmPlan& lmq) {
-    const LayerMeta& L = s.meta[l];
-    const PhaseLayout pl = phase_layout(L, *s.rows, 3);
+    const LayerMeta& L = s.meta()[l];
+    const PhaseLayout pl = phase_layout(L, *s.rows(), 3);
     const int r0 = pl.row0[0], n = pl.nrows[0];
     const float xr = threadIdx.x < n ? __ldcg(p.x + r0 + threadIdx.x) : 0.0f;   // residual rows, early
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -916,20 +932,20 @@ __device__ bool phase_down(const DecodeParams& p, const Smem& s, int l, int cta,
             c1 = ld_cg_f4(p.h + 256 * b1 + 8 * lane + 4);
         }
         const float y0[8] = {a0.x, a0.y, a0.z, a0.w, c0.x, c0.y, c0.z, c0.w};
-        quant_block_warp<true>(y0, s.xq->qs[b0], &s.xq->d[b0], s.xq->bsums[b0]);
+        quant_block_warp<true>(y0, s.xq()->qs[b0], &s.xq()->d[b0], s.xq()->bsums[b0]);
         if (two) {
             const float y1[8] = {a1.x, a1.y, a1.z, a1.w, c1.x, c1.y, c1.z, c1.w};
-            quant_block_warp<true>(y1, s.xq->qs[b1], &s.xq->d[b1], s.xq->bsums[b1]);
+            quant_block_warp<true>(y1, s.xq()->qs[b1], &s.xq()->d[b1], s.xq()->bsums[b1]);
         }
     }
     __syncthreads();
     trace_step(p, l, 4, 1);
     if (!wait_weights(p, s, 4 * l + 3)) return false;
     trace_step(p, l, 4, 2);
-    gemv_rows(L.td, s.wbuf[1], n, N_FF / 256, *s.xq, s.part, MAX_TASKS, s.rowval,
+    gemv_rows(L.td, s.wbuf(1), n, N_FF / 256, *s.xq(), s.part(), MAX_TASKS, s.rowval(),
               (p.trace && l == 1 && cta == 0) ? p.trace + TRACE_GEMV + 3 : nullptr);
     if (threadIdx.x < n) {
-        const float xn = __fadd_rn(xr, s.rowval[threadIdx.x]);
+        const float xn = __fadd_rn(xr, s.rowval()[threadIdx.x]);
         p.x[r0 + threadIdx.x] = xn;
         st_epoch(p.xll + r0 + threadIdx.x, xn, x_epoch(seq, 2 * l + 2));
     }
@@ -955,15 +971,15 @@ __device__ void phase_lm(const DecodeParams& p, const Smem& s, int cta, int ncta
     int nan0 = 0;
     for (int st = 0; st < q.nstages; ++st) {
         const int slot = st & 1;
-        const bool ok = mbar_wait(&s.lmbar[slot], (st >> 1) & 1, p.err);
+        const bool ok = mbar_wait(&s.lmbar()[slot], (st >> 1) & 1, p.err);
         if (__syncthreads_or(!ok)) return;
         const int a = q.r0 + st * q.sr, n = min(q.sr, q.r1 - a);
         float* lg = p.logits;
         const int wl = p.write_logits;
-        gemv_rows(p.lm_type, lm_slot(s, slot), n, q.nb, *s.xq, s.part, MAX_TASKS, s.rowval);
+        gemv_rows(p.lm_type, lm_slot(s, slot), n, q.nb, *s.xq(), s.part(), MAX_TASKS, s.rowval());
         if (threadIdx.x < n) {
             const int row = a + threadIdx.x;
-            const float v = s.rowval[threadIdx.x];
+            const float v = s.rowval()[threadIdx.x];
             if (wl) lg[row] = v;
             if (row == 0 && v != v) nan0 = 1;
             if (v > best || (v == best && row < besti)) best = v, besti = row;
@@ -974,8 +990,8 @@ __device__ void phase_lm(const DecodeParams& p, const Smem& s, int cta, int ncta
     trace_step(p, 1, 5, 6);
     // CTA argmax (lowest index on ties; NaN never wins; a NaN logit 0 forces 0 like the
     // reference's `if (lg[i] > lg[best])` scan)
-    float* red = s.red;
-    int* redi = reinterpret_cast<int*>(s.rowval);
+    float* red = s.red();
+    int* redi = reinterpret_cast<int*>(s.rowval());
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     for (int o = 16; o >= 1; o >>= 1) {
         const float ob = __shfl_xor_sync(0xffffffffu, best, o);
@@ -1018,36 +1034,12 @@ __device__ void phase_lm(const DecodeParams& p, const Smem& s, int cta, int ncta
 }
 
 __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p) {
-    extern __shared__ __align__(1024) uint8_t smem_raw[];
-    Smem s;
-    uint8_t* ptr = smem_raw;
-    s.wbuf[0] = ptr;
-    ptr += WBUF_BYTES + WBUF_SLACK;
-    s.wbuf[1] = ptr;
-    ptr += WBUF_BYTES + WBUF_SLACK;
-    s.xq = reinterpret_cast<XQSmem*>(ptr);
-    ptr += (sizeof(XQSmem) + 127) & ~size_t(127);
-    s.part = reinterpret_cast<int*>(ptr);   // GEMV scratch; aliased by xs (never live across a GEMV)
-    s.xs = reinterpret_cast<float*>(ptr);
-    ptr += SCRATCH_BYTES;
-    s.rowval = reinterpret_cast<float*>(ptr);
-    ptr += ROWVAL_FLOATS * 4;
-    s.red = reinterpret_cast<float*>(ptr);
-    ptr += 32 * 4;
-    s.wbar = reinterpret_cast<uint64_t*>(ptr);
-    ptr += 8 * 8;
-    s.lmbar = reinterpret_cast<uint64_t*>(ptr);
-    ptr += 4 * 8;
-    s.flag = reinterpret_cast<int*>(ptr);
-    ptr += 16;
-    s.rows = reinterpret_cast<CtaRows*>(ptr);
-    ptr += 16;
-    s.meta = reinterpret_cast<LayerMeta*>(ptr);
+    const Smem s;
     if (threadIdx.x == 0) {
         CtaRows cr;
         split_range(N_EMBD, blockIdx.x, gridDim.x, cr.od0, cr.od1);
         split_range(N_FF, blockIdx.x, gridDim.x, cr.gu0, cr.gu1);
-        *s.rows = cr;
+        *s.rows() = cr;
     }
     for (int i = threadIdx.x; i < p.n_layer; i += blockDim.x) {
         const LayerDev& L = p.layers[i];
@@ -1062,7 +1054,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
         m.td = static_cast<uint8_t>(L.td), m.pad = 0;
         m.qkv0 = static_cast<int16_t>(2 * qkv_pair_boundary(L.tq, L.tk, L.tv, blockIdx.x, gridDim.x));
         m.qkv1 = static_cast<int16_t>(2 * qkv_pair_boundary(L.tq, L.tk, L.tv, blockIdx.x + 1, gridDim.x));
-        s.meta[i] = m;
+        s.meta()[i] = m;
     }
     __syncthreads();
 
@@ -1078,8 +1070,8 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
     if (seq == 0) seq = 1;
     bs.idx = 0;
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 8; ++i) mbar_init(&s.wbar[i], 1);
-        for (int i = 0; i < 4; ++i) mbar_init(&s.lmbar[i], 1);
+        for (int i = 0; i < 8; ++i) mbar_init(&s.wbar()[i], 1);
+        for (int i = 0; i < 4; ++i) mbar_init(&s.lmbar()[i], 1);
         fence_mbar_init();
         issue_weight_phase(p, s, 0, cta, ncta);
         prefetch_attention(p, 0, cta);
@@ -1128,7 +1120,6 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
 
 // ---- standalone attention op (execute_attention, ops.cpp:537-628): K/V append at pos,
 // then the same split-KV chunks and combine as the decode kernel's attention phase.
-constexpr int ATT_SMEM_FLOATS = 8 * HEAD_DIM + 64 * HEAD_DIM + 8 * ATT_SC_STRIDE + 32 + 8 * ATT_MAX_CHUNKS + 8 * HEAD_DIM;
 
 __global__ void k_kv_append(const float* __restrict__ k, const float* __restrict__ v, float* kc, float* vc, int pos) {
     const int i = threadIdx.x;
@@ -1139,21 +1130,13 @@ __global__ void k_kv_append(const float* __restrict__ k, const float* __restrict
 }
 
 __global__ void __launch_bounds__(DEC_THREADS, 1) k_attention(const DecodeParams p) {
-    extern __shared__ __align__(1024) uint8_t smem_raw[];
-    Smem s{};
-    s.wbuf[0] = smem_raw;
-    s.flag = reinterpret_cast<int*>(smem_raw + ATT_SMEM_FLOATS * 4);
+    const Smem s;
     phase_attention(p, s, 0, blockIdx.x, gridDim.x, true, 0u);
 }
 
 }  // namespace
 
-size_t decode_smem_bytes() {
-    size_t b = 2 * (WBUF_BYTES + WBUF_SLACK);
-    b += (sizeof(XQSmem) + 127) & ~size_t(127);
-    b += SCRATCH_BYTES + ROWVAL_FLOATS * 4 + 32 * 4 + 12 * 8 + 16 + 16 + MAX_LAYERS * sizeof(LayerMeta);
-    return b;
-}
+size_t decode_smem_bytes() { return SM_BYTES; }
 
 cudaError_t decode_prepare() {
     return cudaFuncSetAttribute(k_decode, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1194,12 +1177,12 @@ cudaError_t launch_attention(const float* q, const float* k, const float* v, flo
     cudaGetDevice(&dev);
     if (prepared_dev != dev) {
         const cudaError_t e = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   ATT_SMEM_FLOATS * 4 + 16);
+                                                   SM_BYTES);
         if (e != cudaSuccess) return e;
         prepared_dev = dev;
     }
     const int n = pos + 1, P = 32 * ((n + 2047) / 2048), C = (n + P - 1) / P;
-    k_attention<<<2 * C, DEC_THREADS, ATT_SMEM_FLOATS * 4 + 16, stream>>>(p);
+    k_attention<<<2 * C, DEC_THREADS, SM_BYTES, stream>>>(p);
     return cudaGetLastError();
 }
 }  // namespace mcpm
