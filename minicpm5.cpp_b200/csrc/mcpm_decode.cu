@@ -140,13 +140,30 @@ __device__ int phase_type(const LayerMeta& L, int kind, int i) {
 __device__ int phase_cols(int kind) { return kind == 3 ? N_FF : N_EMBD; }
 
 // Thread 0 only: arm the four barriers of buffer (wp & 1) and issue weight phase `wp`.
-__device__ void issue_weight_phase(const DecodeParams& p, const Smem& s, int wp, int cta, int ncta) {
+// `half`: -1 issues the whole phase; 0 / 1 issue the first / second half of the rows of a
+// single-segment phase (down), on barriers 0 / 3, so its copy can be spread over time.
+__device__ void issue_weight_phase(const DecodeParams& p, const Smem& s, int wp, int cta, int ncta, int half = -1) {
     const int buf = wp & 1;
     uint64_t* bars = s.wbar() + 4 * buf;
     const int l = wp >> 2, kind = wp & 3;
     const LayerMeta& M = s.meta()[l];
     const PhaseLayout pl = phase_layout(M, *s.rows(), kind);
     const uint64_t pol = l2_evict_first_policy();
+    if (half >= 0) {   // down: rows [0, n/2) on barrier 0, [n/2, n) on barrier 3
+        const int rb = row_bytes(phase_type(M, kind, 0), phase_cols(kind));
+        const int n0 = pl.nrows[0] / 2, a = half ? n0 : 0, n = half ? pl.nrows[0] - n0 : n0;
+        const uint32_t bytes = static_cast<uint32_t>(n) * rb;
+        uint64_t* bar = &bars[half ? 3 : 0];
+        mbar_expect_tx(bar, bytes);
+        if (bytes)
+            bulk_g2s_stream(s.wbuf(buf) + static_cast<size_t>(a) * rb,
+                            phase_src(p, M, kind, 0) + static_cast<size_t>(pl.row0[0] + a) * rb, bytes, bar, pol);
+        if (half == 0) {
+            mbar_expect_tx(&bars[1], 0);
+            mbar_expect_tx(&bars[2], 0);
+        }
+        return;
+    }
 #pragma unroll
     for (int i = 0; i < 3; ++i) {
         mbar_expect_tx(&bars[i], pl.bytes[i]);
@@ -887,7 +904,7 @@ __device__ bool phase_o(const DecodeParams& p, const Smem& s, int l, int cta, in
     trace_cta(p, l, 2, 0);
     // down weights into the buffer just released, by a thread outside warps 0-7 (which
     // poll the residual in the next norm)
-    if (threadIdx.x == ISSUE_THREAD) issue_weight_phase(p, s, 4 * l + 3, cta, ncta);
+    if (threadIdx.x == ISSUE_THREAD) issue_weight_phase(p, s, 4 * l + 3, cta, ncta, 0);   // first half now
     return true;
 }
 
@@ -896,6 +913,9 @@ __device__ bool phase_gu(const DecodeParams& p, const Smem& s, int l, int cta, i
     if (!norm_quant<true, X_EPOCH>(p, nullptr, x_epoch(seq, 2 * l + 1), meta_f32(p, L.ffn_norm), s)) return false;
     trace_mark(p, 3 + 2 * (5 * l + 2));
     trace_cta(p, l, 2, 1);
+    // second half of the down weights, after the residual wait: halving each burst of weight
+    // traffic shortens the epoch polls that run beside it
+    if (threadIdx.x == ISSUE_THREAD) issue_weight_phase(p, s, 4 * l + 3, cta, ncta, 1);
     trace_step(p, l, 3, 1);
     if (!wait_weights(p, s, 4 * l + 2)) return false;
     trace_step(p, l, 3, 2);
