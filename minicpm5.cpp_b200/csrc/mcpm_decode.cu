@@ -486,25 +486,6 @@ __device__ bool phase_qkv(const DecodeParams& p, const Smem& s, int l, int token
     return true;
 }
 
-// Canonical q.k over 128 dims by an 8-lane group (lane j: dims 4j + 32i + c, then the
-// butterfly v += v^4, v += v^2, v += v^1).  Called by all 32 lanes of the warp.
-__device__ __forceinline__ float dot128_group(const float* q, const float* k, int j) {
-    float a = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float4 qv = *reinterpret_cast<const float4*>(q + 4 * j + 32 * i);
-        const float4 kv = *reinterpret_cast<const float4*>(k + 4 * j + 32 * i);
-        a = __fmaf_rn(qv.x, kv.x, a);
-        a = __fmaf_rn(qv.y, kv.y, a);
-        a = __fmaf_rn(qv.z, kv.z, a);
-        a = __fmaf_rn(qv.w, kv.w, a);
-    }
-    a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 4));
-    a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 2));
-    a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 1));
-    return a;
-}
-
 // Chunk counts up to DIST_COMBINE_MAX are combined by every CTA in the o_proj prologue
 // (no atomics, no serial combiner); longer contexts use the last-CTA combine below.
 constexpr int DIST_COMBINE_MAX = 16;
@@ -518,7 +499,8 @@ __device__ __forceinline__ int attn_chunks(int n) {
 // the 8 query heads of KV head g against positions [t0, t0+np).  q and K go straight from
 // L2 into registers (one round trip), V streams into shared memory meanwhile (cp.async).
 // Thread (warp w, group G = lane/8, j = lane%8): heads 2G, 2G+1 x positions t0+2w, t0+2w+1,
-// dims 4j + 32i + c of each dot (the canonical 8-lane split of dot128_group).
+// dims 4j + 32i + c of each dot, then the butterfly v += v^4, v += v^2, v += v^1 (the
+// canonical 8-lane q.k split).
 // Same numerics as the general path below: scores, chunk max, exp, position-ordered
 // sum and fma chains, partials [head][chunk][m, l, o[128]].
 // In the decode kernel (p.qll set) q and this position's K/V rows are read from their
@@ -665,102 +647,143 @@ __device__ void attention_unit32(const DecodeParams& p, const Smem& s, int l, in
     trace_step(p, l, 1, 2);
 }
 
+// One attention unit of a chunk longer than 32 positions (contexts above 2048): the 8 query
+// heads of KV head g against positions [t0, t0+np), np <= 256.  K rows stream into shared
+// memory with cp.async, up to 128 rows per round trip, then V rows through the same buffer.
+// Warp w: head pair w&3 (q in registers), positions (w>>2)*4 + group + 16i; lane j of an
+// 8-lane group owns dims 4j + 32i + c of each dot (the canonical 8-lane split).  Same
+// numerics as attention_unit32.  q is final here: a grid barrier follows the QKV phase.
+constexpr int ATT_BIG_ROWS = 128;
+// q, K/V rows, scores, then the combine's stat / weights / output (phase_attention)
+static_assert((8 * HEAD_DIM + ATT_BIG_ROWS * HEAD_DIM + 8 * ATT_SC_STRIDE + 32 + 8 * ATT_MAX_CHUNKS + 8 * HEAD_DIM) *
+                      sizeof(float) <= WBUF_BYTES,
+              "attention scratch exceeds weight buffer 0");
+__device__ void attention_unit_big(const DecodeParams& p, const Smem& s, int l, int g, int c, int t0, int np) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, j = lane & 7, G = lane >> 3;
+    float* qh = reinterpret_cast<float*>(s.wbuf(0));   // [8][128]
+    float* kv = qh + 8 * HEAD_DIM;                      // [ATT_BIG_ROWS][128] K, then V rows
+    float* sc = kv + ATT_BIG_ROWS * HEAD_DIM;           // [8][ATT_SC_STRIDE] scores -> probabilities
+    float* stat = sc + 8 * ATT_SC_STRIDE;               // m[8], l[8]
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(HEAD_DIM)));
+    const float* kl = p.kc + static_cast<size_t>(l) * p.max_seq * KV_DIM + g * HEAD_DIM;
+    const float* vl = p.vc + static_cast<size_t>(l) * p.max_seq * KV_DIM + g * HEAD_DIM;
+    if (tid < 256) reinterpret_cast<float4*>(qh)[tid] = ld_cg_f4(p.q + 8 * g * HEAD_DIM + 4 * tid);
+    const int hp = warp & 3, ps = warp >> 2;
+    for (int s0 = 0; s0 < np; s0 += ATT_BIG_ROWS) {   // scores
+        const int ns = min(ATT_BIG_ROWS, np - s0);
+        for (int i = tid; i < ns * 32; i += blockDim.x)
+            cp_async16(kv + 4 * i, kl + static_cast<size_t>(t0 + s0 + (i >> 5)) * KV_DIM + 4 * (i & 31));
+        cp_async_commit();
+        cp_async_wait_all();
+        __syncthreads();
+        float4 qa[4], qb[4];   // reloaded per round: registers stay free between rounds
+        const float* q0 = qh + (2 * hp) * HEAD_DIM + 4 * j;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            qa[i] = *reinterpret_cast<const float4*>(q0 + 32 * i);
+            qb[i] = *reinterpret_cast<const float4*>(q0 + HEAD_DIM + 32 * i);
+        }
+        for (int base = ps * 4; base < ns; base += 16) {   // warp-uniform trip count
+            const int tt = base + G;
+            const bool valid = tt < ns;
+            const float* kr = kv + (valid ? tt : 0) * HEAD_DIM + 4 * j;
+            float d0 = 0.0f, d1 = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float4 k = *reinterpret_cast<const float4*>(kr + 32 * i);
+                d0 = __fmaf_rn(qa[i].x, k.x, d0);
+                d0 = __fmaf_rn(qa[i].y, k.y, d0);
+                d0 = __fmaf_rn(qa[i].z, k.z, d0);
+                d0 = __fmaf_rn(qa[i].w, k.w, d0);
+                d1 = __fmaf_rn(qb[i].x, k.x, d1);
+                d1 = __fmaf_rn(qb[i].y, k.y, d1);
+                d1 = __fmaf_rn(qb[i].z, k.z, d1);
+                d1 = __fmaf_rn(qb[i].w, k.w, d1);
+            }
+#pragma unroll
+            for (int o = 4; o >= 1; o >>= 1) {
+                d0 = __fadd_rn(d0, __shfl_xor_sync(0xffffffffu, d0, o));
+                d1 = __fadd_rn(d1, __shfl_xor_sync(0xffffffffu, d1, o));
+            }
+            if (valid && j == 0) {
+                sc[(2 * hp) * ATT_SC_STRIDE + s0 + tt] = __fmul_rn(d0, scale);
+                sc[(2 * hp + 1) * ATT_SC_STRIDE + s0 + tt] = __fmul_rn(d1, scale);
+            }
+        }
+        __syncthreads();   // kv is overwritten next
+    }
+    trace_step(p, l, 1, 1);
+    if (warp < 8) {   // chunk max, probabilities, canonical chunk sum (warp = head)
+        float m = -__int_as_float(0x7f800000);
+        for (int t = lane; t < np; t += 32) m = fmaxf(m, sc[warp * ATT_SC_STRIDE + t]);
+        for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float sum = 0.0f;
+        for (int t = lane; t < np; t += 32) {
+            const float e = canon_expf(__fsub_rn(sc[warp * ATT_SC_STRIDE + t], m));
+            sc[warp * ATT_SC_STRIDE + t] = e;
+            sum = __fadd_rn(sum, e);
+        }
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+        if (lane == 0) stat[warp] = m, stat[8 + warp] = sum;
+    }
+    float acc0 = 0.0f, acc1 = 0.0f;   // o[h][d] = fma chain over positions
+    const int h0 = tid >> 7, h1 = h0 + 4, dd = tid & 127;
+    for (int s0 = 0; s0 < np; s0 += ATT_BIG_ROWS) {
+        const int ns = min(ATT_BIG_ROWS, np - s0);
+        for (int i = tid; i < ns * 32; i += blockDim.x)
+            cp_async16(kv + 4 * i, vl + static_cast<size_t>(t0 + s0 + (i >> 5)) * KV_DIM + 4 * (i & 31));
+        cp_async_commit();
+        cp_async_wait_all();
+        __syncthreads();   // V rows, and (first round) the probabilities
+        const float* p0 = sc + h0 * ATT_SC_STRIDE + s0;
+        const float* p1 = sc + h1 * ATT_SC_STRIDE + s0;
+        int tt = 0;
+        for (; tt + 4 <= ns; tt += 4) {
+            float v[4], a0[4], a1[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) v[k] = kv[(tt + k) * HEAD_DIM + dd], a0[k] = p0[tt + k], a1[k] = p1[tt + k];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) acc0 = __fmaf_rn(a0[k], v[k], acc0), acc1 = __fmaf_rn(a1[k], v[k], acc1);
+        }
+        for (; tt < ns; ++tt) {
+            const float v = kv[tt * HEAD_DIM + dd];
+            acc0 = __fmaf_rn(p0[tt], v, acc0);
+            acc1 = __fmaf_rn(p1[tt], v, acc1);
+        }
+        __syncthreads();
+    }
+    float* pa0 = p.att_part + (static_cast<size_t>(8 * g + h0) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
+    float* pa1 = p.att_part + (static_cast<size_t>(8 * g + h1) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
+    __stcg(pa0 + ATT_PART_O + dd, acc0);
+    __stcg(pa1 + ATT_PART_O + dd, acc1);
+    if (tid < 8) {
+        float* pm = p.att_part + (static_cast<size_t>(8 * g + tid) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
+        __stcg(pm, stat[tid]);
+        __stcg(pm + 1, stat[8 + tid]);
+    }
+    __syncthreads();
+    trace_step(p, l, 1, 2);
+}
+
 __device__ void phase_attention(const DecodeParams& p, const Smem& s, int l, int cta, int ncta, bool combine_here,
                                 unsigned seq) {
     const int n = p.pos + 1;
     const int P = 32 * ((n + 2047) / 2048);
     const int C = (n + P - 1) / P;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    float* qh = reinterpret_cast<float*>(s.wbuf(0));   // [8][128]
-    float* kb = qh + 8 * HEAD_DIM;                      // [32][128] staged K rows
-    float* vb = kb + 32 * HEAD_DIM;                     // [32][128] staged V rows
-    float* sc = vb + 32 * HEAD_DIM;                     // [8][ATT_SC_STRIDE] scores -> probabilities
-    float* stat = sc + 8 * ATT_SC_STRIDE;               // m[8], l[8], 1/L[8]
+    // combine scratch after the units' buffers (q, K/V rows, scores)
+    float* stat = reinterpret_cast<float*>(s.wbuf(0)) + 8 * HEAD_DIM + ATT_BIG_ROWS * HEAD_DIM + 8 * ATT_SC_STRIDE;
     float* wts = stat + 32;                             // [8][ATT_MAX_CHUNKS]
     float* ab = wts + 8 * ATT_MAX_CHUNKS;               // [1024] combined output
-    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(HEAD_DIM)));
-    const float* kl = p.kc + static_cast<size_t>(l) * p.max_seq * KV_DIM;
-    const float* vl = p.vc + static_cast<size_t>(l) * p.max_seq * KV_DIM;
-    auto stage_rows = [&](const float* src, float* dst, int s0, int ns, int g) {
-        for (int i = tid; i < ns * 32; i += blockDim.x) {
-            const int tt = i >> 5, f = i & 31;
-            reinterpret_cast<float4*>(dst)[i] =
-                __ldcg(reinterpret_cast<const float4*>(src + static_cast<size_t>(s0 + tt) * KV_DIM + g * HEAD_DIM) + f);
-        }
-    };
     for (int item = cta; item < 2 * C; item += ncta) {
         const int g = item / C, c = item % C;
         const int t0 = c * P, t1 = min(t0 + P, n), np = t1 - t0;
-        const bool single = np <= 32;   // q, K and V of the chunk staged in one round trip
         __syncthreads();
-        if (P == 32) {
+        if (P == 32)
             attention_unit32(p, s, l, g, c, t0, np, seq);
-        } else {
-            if (tid < 256)
-                reinterpret_cast<float4*>(qh)[tid] = __ldcg(reinterpret_cast<const float4*>(p.q + 8 * g * HEAD_DIM) + tid);
-            for (int s0 = t0; s0 < t1; s0 += 32) {   // scores, 32 positions at a time
-                const int ns = min(32, t1 - s0);
-                if (s0 != t0) __syncthreads();
-                stage_rows(kl, kb, s0, ns, g);
-                if (single) stage_rows(vl, vb, s0, ns, g);
-                __syncthreads();
-                if (s0 == t0) trace_step(p, l, 1, 4);
-                const int ndots = ns * 8;
-                for (int it = 0; it < (ndots + 63) / 64; ++it) {
-                    const int di = it * 64 + (tid >> 3);
-                    const bool valid = di < ndots;
-                    const int h = di & 7, tt = valid ? (di >> 3) : 0;
-                    const float d = dot128_group(qh + h * HEAD_DIM, kb + tt * HEAD_DIM, tid & 7);
-                    if (valid && (tid & 7) == 0) sc[h * ATT_SC_STRIDE + (s0 - t0) + tt] = __fmul_rn(d, scale);
-                }
-            }
-            __syncthreads();
-            trace_step(p, l, 1, 1);
-            if (warp < 8) {   // chunk max, probabilities, position-ordered sum (warp = head)
-                float m = -__int_as_float(0x7f800000);
-                for (int t = lane; t < np; t += 32) m = fmaxf(m, sc[warp * ATT_SC_STRIDE + t]);
-                for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-                for (int t = lane; t < np; t += 32)
-                    sc[warp * ATT_SC_STRIDE + t] = canon_expf(__fsub_rn(sc[warp * ATT_SC_STRIDE + t], m));
-                __syncwarp();
-                // canonical chunk sum: lane sums over t = lane (mod 32) in order, then a butterfly
-                float sum = 0.0f;
-                for (int t = lane; t < np; t += 32) sum = __fadd_rn(sum, sc[warp * ATT_SC_STRIDE + t]);
-#pragma unroll
-                for (int o = 16; o >= 1; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
-                if (lane == 0) {
-                    stat[warp] = m;
-                    stat[8 + warp] = sum;
-                }
-            }
-            float acc0 = 0.0f, acc1 = 0.0f;   // o[h][d] = fma chain over positions
-            const int h0 = tid >> 7, h1 = h0 + 4, dd = tid & 127;
-            for (int s0 = t0; s0 < t1; s0 += 32) {
-                const int ns = min(32, t1 - s0);
-                __syncthreads();
-                if (!single) {
-                    stage_rows(vl, vb, s0, ns, g);
-                    __syncthreads();
-                }
-                for (int tt = 0; tt < ns; ++tt) {
-                    const float v = vb[tt * HEAD_DIM + dd];
-                    acc0 = __fmaf_rn(sc[h0 * ATT_SC_STRIDE + (s0 - t0) + tt], v, acc0);
-                    acc1 = __fmaf_rn(sc[h1 * ATT_SC_STRIDE + (s0 - t0) + tt], v, acc1);
-                }
-            }
-            // partials: [head][chunk][m, l, o[128]]
-            float* pa0 = p.att_part + (static_cast<size_t>(8 * g + h0) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
-            float* pa1 = p.att_part + (static_cast<size_t>(8 * g + h1) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
-            __stcg(pa0 + ATT_PART_O + dd, acc0);
-            __stcg(pa1 + ATT_PART_O + dd, acc1);
-            if (tid < 8) {
-                float* pm = p.att_part + (static_cast<size_t>(8 * g + tid) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
-                __stcg(pm, stat[tid]);
-                __stcg(pm + 1, stat[8 + tid]);
-            }
-            __syncthreads();
-            trace_step(p, l, 1, 2);
-        }
+        else
+            attention_unit_big(p, s, l, g, c, t0, np);
         if (!combine_here) continue;
         if (tid == 0) {
             __threadfence();
@@ -795,16 +818,32 @@ __device__ void phase_attention(const DecodeParams& p, const Smem& s, int l, int
             if (lane == 0) stat[16 + warp] = __fdiv_rn(1.0f, Ls);
         }
         __syncthreads();
-        for (int o = tid; o < 8 * HEAD_DIM; o += blockDim.x) {
-            const int h = o >> 7, d = o & 127;
-            const float* ph = p.att_part + static_cast<size_t>(8 * g + h) * ATT_MAX_CHUNKS * ATT_PART_STRIDE;
-            float O = 0.0f;
-#pragma unroll 8
-            for (int cc = 0; cc < C; ++cc)
-                O = __fmaf_rn(wts[h * ATT_MAX_CHUNKS + cc], __ldcg(ph + cc * ATT_PART_STRIDE + ATT_PART_O + d), O);
-            const float out = __fmul_rn(O, stat[16 + h]);
-            ab[o] = out;
-            p.att[8 * g * HEAD_DIM + o] = out;
+        if (warp < 8) {   // warp = head, lane = dims 4*lane .. 4*lane+3; chunk chains, 16 loads in flight
+            const float* ph = p.att_part + static_cast<size_t>(8 * g + warp) * ATT_MAX_CHUNKS * ATT_PART_STRIDE +
+                              ATT_PART_O + 4 * lane;
+            float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int c0 = 0; c0 < C; c0 += 16) {
+                float4 v[16];
+#pragma unroll
+                for (int k = 0; k < 16; ++k)
+                    v[k] = c0 + k < C ? ld_cg_f4(ph + (c0 + k) * ATT_PART_STRIDE) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int k = 0; k < 16; ++k) {
+                    if (c0 + k < C) {
+                        const float w = wts[warp * ATT_MAX_CHUNKS + c0 + k];
+                        O.x = __fmaf_rn(w, v[k].x, O.x);
+                        O.y = __fmaf_rn(w, v[k].y, O.y);
+                        O.z = __fmaf_rn(w, v[k].z, O.z);
+                        O.w = __fmaf_rn(w, v[k].w, O.w);
+                    }
+                }
+            }
+            const float inv = stat[16 + warp];
+            const float4 out = make_float4(__fmul_rn(O.x, inv), __fmul_rn(O.y, inv), __fmul_rn(O.z, inv),
+                                           __fmul_rn(O.w, inv));
+            *reinterpret_cast<float4*>(ab + warp * HEAD_DIM + 4 * lane) = out;
+            float* dst = p.att + 8 * g * HEAD_DIM + warp * HEAD_DIM + 4 * lane;   // caller's buffer: 4-byte aligned
+            dst[0] = out.x, dst[1] = out.y, dst[2] = out.z, dst[3] = out.w;
         }
         __syncthreads();
         if (warp < 4) {   // four Q8_K blocks, ties-to-even (quantize_row_q8_K_avx2)
