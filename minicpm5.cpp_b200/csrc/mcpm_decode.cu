@@ -67,7 +67,6 @@ struct Smem {
     __device__ float* red() const { return reinterpret_cast<float*>(smem_raw + SM_RED); }      // 32 floats
     __device__ uint64_t* wbar() const { return reinterpret_cast<uint64_t*>(smem_raw + SM_WBAR); }   // [2][4]
     __device__ uint64_t* lmbar() const { return reinterpret_cast<uint64_t*>(smem_raw + SM_LMBAR); } // [4]
-    __device__ int* flag() const { return reinterpret_cast<int*>(smem_raw + SM_FLAG); }
     __device__ CtaRows* rows() const { return reinterpret_cast<CtaRows*>(smem_raw + SM_ROWS); }
     __device__ LayerMeta* meta() const { return reinterpret_cast<LayerMeta*>(smem_raw + SM_META); }   // [n_layer]
 };
@@ -421,6 +420,19 @@ __device__ __forceinline__ unsigned qkv_epoch(unsigned seq, int l) { return (seq
 // launch `seq` (24 bits, never 0 after the host zeroes the words).
 __device__ __forceinline__ unsigned x_epoch(unsigned seq, int k) { return (seq << 8) | static_cast<unsigned>(k); }
 
+// Epoch of layer l's attention records (chunk headers in p.att_part, combined values in
+// p.attw).  The standalone attention op uses seq = 1.
+__device__ __forceinline__ unsigned att_epoch(unsigned seq, int l) { return (seq << 8) | static_cast<unsigned>(l); }
+
+// Chunk record [head][chunk] in p.att_part: a 16-byte header of two epoch-tagged words
+// (chunk max m, chunk sum l), then o[128].  Up to DIST_COMBINE_MAX chunks a grid barrier
+// separates the records from their readers; beyond, the head-pair combiners poll the
+// headers, which are then written after the record's o values with a fence in between.
+__device__ __forceinline__ unsigned long long* att_header(const DecodeParams& p, int h, int c) {
+    return reinterpret_cast<unsigned long long*>(p.att_part + (static_cast<size_t>(h) * ATT_MAX_CHUNKS + c) *
+                                                                  ATT_PART_STRIDE);
+}
+
 // ------------------------------------------------------------------------ phases
 __device__ bool phase_qkv(const DecodeParams& p, const Smem& s, int l, int token, int cta, int ncta, unsigned seq) {
     const LayerMeta& L = s.meta()[l];
@@ -493,6 +505,11 @@ constexpr int DIST_COMBINE_MAX = 16;
 __device__ __forceinline__ int attn_chunks(int n) {
     const int P = 32 * ((n + 2047) / 2048);
     return (n + P - 1) / P;
+}
+
+// Decode kernel with more than DIST_COMBINE_MAX chunks: no grid barrier after attention.
+__device__ __forceinline__ bool att_flagged(const DecodeParams& p) {
+    return p.attw != nullptr && attn_chunks(p.pos + 1) > DIST_COMBINE_MAX;
 }
 
 // One attention unit of at most 32 positions (chunk length P = 32, contexts up to 2048):
@@ -638,12 +655,14 @@ __device__ void attention_unit32(const DecodeParams& p, const Smem& s, int l, in
     float* pa1 = p.att_part + (static_cast<size_t>(8 * g + h1) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
     __stcg(pa0 + ATT_PART_O + dd, acc0);
     __stcg(pa1 + ATT_PART_O + dd, acc1);
+    __syncthreads();   // every o value of the chunk is stored (program order), then the headers
     if (tid < 8) {
-        float* pm = p.att_part + (static_cast<size_t>(8 * g + tid) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
-        __stcg(pm, stat[tid]);
-        __stcg(pm + 1, stat[8 + tid]);
+        if (att_flagged(p)) __threadfence();   // combiners poll the headers (no grid barrier)
+        unsigned long long* hdr = att_header(p, 8 * g + tid, c);
+        const unsigned e = att_epoch(seq, l);
+        st_epoch(hdr, stat[tid], e);
+        st_epoch(hdr + 1, stat[8 + tid], e);
     }
-    __syncthreads();
     trace_step(p, l, 1, 2);
 }
 
@@ -658,7 +677,8 @@ constexpr int ATT_BIG_ROWS = 128;
 static_assert((8 * HEAD_DIM + ATT_BIG_ROWS * HEAD_DIM + 8 * ATT_SC_STRIDE + 32 + 8 * ATT_MAX_CHUNKS + 8 * HEAD_DIM) *
                       sizeof(float) <= WBUF_BYTES,
               "attention scratch exceeds weight buffer 0");
-__device__ void attention_unit_big(const DecodeParams& p, const Smem& s, int l, int g, int c, int t0, int np) {
+__device__ void attention_unit_big(const DecodeParams& p, const Smem& s, int l, int g, int c, int t0, int np,
+                                   unsigned seq) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, j = lane & 7, G = lane >> 3;
     float* qh = reinterpret_cast<float*>(s.wbuf(0));   // [8][128]
     float* kv = qh + 8 * HEAD_DIM;                      // [ATT_BIG_ROWS][128] K, then V rows
@@ -676,6 +696,7 @@ __device__ void attention_unit_big(const DecodeParams& p, const Smem& s, int l, 
         cp_async_commit();
         cp_async_wait_all();
         __syncthreads();
+        if (s0 == 0) trace_step(p, l, 1, 4);
         float4 qa[4], qb[4];   // reloaded per round: registers stay free between rounds
         const float* q0 = qh + (2 * hp) * HEAD_DIM + 4 * j;
 #pragma unroll
@@ -729,6 +750,7 @@ __device__ void attention_unit_big(const DecodeParams& p, const Smem& s, int l, 
     }
     float acc0 = 0.0f, acc1 = 0.0f;   // o[h][d] = fma chain over positions
     const int h0 = tid >> 7, h1 = h0 + 4, dd = tid & 127;
+    trace_step(p, l, 1, 8);
     for (int s0 = 0; s0 < np; s0 += ATT_BIG_ROWS) {
         const int ns = min(ATT_BIG_ROWS, np - s0);
         for (int i = tid; i < ns * 32; i += blockDim.x)
@@ -736,6 +758,7 @@ __device__ void attention_unit_big(const DecodeParams& p, const Smem& s, int l, 
         cp_async_commit();
         cp_async_wait_all();
         __syncthreads();   // V rows, and (first round) the probabilities
+        if (s0 == 0) trace_step(p, l, 1, 9);
         const float* p0 = sc + h0 * ATT_SC_STRIDE + s0;
         const float* p1 = sc + h1 * ATT_SC_STRIDE + s0;
         int tt = 0;
@@ -757,25 +780,114 @@ __device__ void attention_unit_big(const DecodeParams& p, const Smem& s, int l, 
     float* pa1 = p.att_part + (static_cast<size_t>(8 * g + h1) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
     __stcg(pa0 + ATT_PART_O + dd, acc0);
     __stcg(pa1 + ATT_PART_O + dd, acc1);
+    __syncthreads();   // every o value of the chunk is stored (program order), then the headers
     if (tid < 8) {
-        float* pm = p.att_part + (static_cast<size_t>(8 * g + tid) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
-        __stcg(pm, stat[tid]);
-        __stcg(pm + 1, stat[8 + tid]);
+        if (att_flagged(p)) __threadfence();   // combiners poll the headers (no grid barrier)
+        unsigned long long* hdr = att_header(p, 8 * g + tid, c);
+        const unsigned e = att_epoch(seq, l);
+        st_epoch(hdr, stat[tid], e);
+        st_epoch(hdr + 1, stat[8 + tid], e);
     }
-    __syncthreads();
     trace_step(p, l, 1, 2);
 }
 
-__device__ void phase_attention(const DecodeParams& p, const Smem& s, int l, int cta, int ncta, bool combine_here,
-                                unsigned seq) {
+// Combiner of head pair b (heads 2b, 2b+1: one Q8_K block of the attention output) for
+// contexts of more than DIST_COMBINE_MAX chunks.  Waits for the chunk headers of its two
+// heads, stages their o vectors in shared memory (one round trip), then
+//   M = max_c m_c, w_c = exp(m_c - M), L = fma chain of w_c*l_c over c, o = fma chain of
+//   w_c*o_c over c, out = o * (1/L)
+// (ops.cpp:590-611 restated per chunk), and writes p.att, the Q8_K block b of p.att_q8k
+// and, in the decode kernel (p.attw set), the epoch-tagged values o_proj waits for.
+__device__ bool combine_pair(const DecodeParams& p, const Smem& s, int l, int b, unsigned seq) {
+    const int n = p.pos + 1, C = attn_chunks(n);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const unsigned e = att_epoch(seq, l);
+    float* po = reinterpret_cast<float*>(s.wbuf(0));   // [2][C][128] chunk o vectors
+    float* wts = po + 2 * ATT_MAX_CHUNKS * HEAD_DIM;    // [2][ATT_MAX_CHUNKS]
+    float* lsm = wts + 2 * ATT_MAX_CHUNKS;              // [2][ATT_MAX_CHUNKS]
+    float* inv = lsm + 2 * ATT_MAX_CHUNKS;              // [2] (+2 pad)
+    float* ab = inv + 4;                                // [256]
+    if (p.trace && l == 1 && tid == 0 && (b & 3) == 0) p.trace[2870 + 4 * (b >> 2)] = globaltimer();
+    bool ok = true;
+    if (warp < 2) {   // warp = head of the pair; lanes own chunks lane, lane + 32
+        const int h = 2 * b + warp;
+        float m0 = -__int_as_float(0x7f800000), m1 = m0, l0 = 0.0f, l1 = 0.0f;
+        if (lane < C) ok = load2_epoch(att_header(p, h, lane), e, m0, l0, p.err);
+        if (ok && lane + 32 < C) ok = load2_epoch(att_header(p, h, lane + 32), e, m1, l1, p.err);
+        float M = fmaxf(m0, m1);
+        for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        if (lane < C) {
+            wts[warp * ATT_MAX_CHUNKS + lane] = canon_expf(__fsub_rn(m0, M));
+            lsm[warp * ATT_MAX_CHUNKS + lane] = l0;
+        }
+        if (lane + 32 < C) {
+            wts[warp * ATT_MAX_CHUNKS + lane + 32] = canon_expf(__fsub_rn(m1, M));
+            lsm[warp * ATT_MAX_CHUNKS + lane + 32] = l1;
+        }
+        __syncwarp();
+        if (lane == 0) {   // chunk-ordered fma chain
+            float Ls = 0.0f;
+            for (int c = 0; c < C; ++c) Ls = __fmaf_rn(wts[warp * ATT_MAX_CHUNKS + c], lsm[warp * ATT_MAX_CHUNKS + c], Ls);
+            inv[warp] = __fdiv_rn(1.0f, Ls);
+        }
+        __threadfence();   // headers seen before the o vectors are read
+    }
+    if (!__syncthreads_and(ok)) return false;
+    if (p.trace && l == 1 && tid == 0 && (b & 3) == 0) p.trace[2871 + 4 * (b >> 2)] = globaltimer();
+    for (int i = tid; i < 2 * C * 32; i += blockDim.x) {
+        const int hh = i / (32 * C), r = i - hh * 32 * C, c = r >> 5, f = r & 31;
+        cp_async16(po + (hh * C + c) * HEAD_DIM + 4 * f,
+                   p.att_part + (static_cast<size_t>(2 * b + hh) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE + ATT_PART_O +
+                       4 * f);
+    }
+    cp_async_commit();
+    cp_async_wait_all();
+    __syncthreads();
+    if (p.trace && l == 1 && tid == 0 && (b & 3) == 0) p.trace[2872 + 4 * (b >> 2)] = globaltimer();
+    if (tid < 2 * HEAD_DIM) {
+        const int hh = tid >> 7, dd = tid & 127;
+        const float* w = wts + hh * ATT_MAX_CHUNKS;
+        const float* o = po + hh * C * HEAD_DIM + dd;
+        float O = 0.0f;
+        int c = 0;
+        for (; c + 4 <= C; c += 4) {
+            const float4 w4 = *reinterpret_cast<const float4*>(w + c);
+            float v[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) v[k] = o[(c + k) * HEAD_DIM];
+            O = __fmaf_rn(w4.x, v[0], O);
+            O = __fmaf_rn(w4.y, v[1], O);
+            O = __fmaf_rn(w4.z, v[2], O);
+            O = __fmaf_rn(w4.w, v[3], O);
+        }
+        for (; c < C; ++c) O = __fmaf_rn(w[c], o[c * HEAD_DIM], O);
+        const float out = __fmul_rn(O, inv[hh]);
+        ab[tid] = out;
+        if (p.attw) st_epoch(p.attw + 256 * b + tid, out, e);
+        p.att[256 * b + tid] = out;
+    }
+    __syncthreads();
+    if (warp == 0) {   // Q8_K block b, ties-to-even (quantize_row_q8_K_avx2)
+        float y[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) y[k] = ab[8 * lane + k];
+        uint8_t* blk = p.att_q8k + static_cast<size_t>(b) * Q8K_BYTES;
+        quant_block_warp<false>(y, reinterpret_cast<int8_t*>(blk + 4), reinterpret_cast<float*>(blk),
+                                reinterpret_cast<int16_t*>(blk + 260));
+    }
+    if (p.trace && l == 1 && tid == 0 && (b & 3) == 0) p.trace[2873 + 4 * (b >> 2)] = globaltimer();
+    __syncthreads();   // po / ab reused by the caller
+    return true;
+}
+
+// Attention of layer l: units (KV group g, chunk c) over the CTAs, then, for more than
+// DIST_COMBINE_MAX chunks in the decode kernel, the head-pair combiners on the last CTAs
+// (usually CTAs without a unit).  Shorter contexts are combined in the o_proj prologue;
+// the standalone op combines in k_att_combine.
+__device__ bool phase_attention(const DecodeParams& p, const Smem& s, int l, int cta, int ncta, unsigned seq) {
     const int n = p.pos + 1;
     const int P = 32 * ((n + 2047) / 2048);
     const int C = (n + P - 1) / P;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    // combine scratch after the units' buffers (q, K/V rows, scores)
-    float* stat = reinterpret_cast<float*>(s.wbuf(0)) + 8 * HEAD_DIM + ATT_BIG_ROWS * HEAD_DIM + 8 * ATT_SC_STRIDE;
-    float* wts = stat + 32;                             // [8][ATT_MAX_CHUNKS]
-    float* ab = wts + 8 * ATT_MAX_CHUNKS;               // [1024] combined output
     for (int item = cta; item < 2 * C; item += ncta) {
         const int g = item / C, c = item % C;
         const int t0 = c * P, t1 = min(t0 + P, n), np = t1 - t0;
@@ -783,108 +895,28 @@ __device__ void phase_attention(const DecodeParams& p, const Smem& s, int l, int
         if (P == 32)
             attention_unit32(p, s, l, g, c, t0, np, seq);
         else
-            attention_unit_big(p, s, l, g, c, t0, np);
-        if (!combine_here) continue;
-        if (tid == 0) {
-            __threadfence();
-            const unsigned old = atomicAdd(&p.cnt[g], 1u);
-            *s.flag() = (old == static_cast<unsigned>(C - 1));
-            if (old == static_cast<unsigned>(C - 1)) atomicExch(&p.cnt[g], 0u);
-        }
-        __syncthreads();
-        if (!*s.flag()) continue;
-        // ---- last CTA of this KV group combines the chunks of its 8 heads
-        __threadfence();
-        if (warp < 8) {
-            const float* ph = p.att_part + static_cast<size_t>(8 * g + warp) * ATT_MAX_CHUNKS * ATT_PART_STRIDE;
-            const float mc0 = lane < C ? __ldcg(ph + lane * ATT_PART_STRIDE) : 0.0f;
-            const float mc1 = lane + 32 < C ? __ldcg(ph + (lane + 32) * ATT_PART_STRIDE) : 0.0f;
-            const float lc0 = lane < C ? __ldcg(ph + lane * ATT_PART_STRIDE + 1) : 0.0f;
-            const float lc1 = lane + 32 < C ? __ldcg(ph + (lane + 32) * ATT_PART_STRIDE + 1) : 0.0f;
-            float M = -__int_as_float(0x7f800000);
-            if (lane < C) M = mc0;
-            if (lane + 32 < C) M = fmaxf(M, mc1);
-            for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-            const float w0 = lane < C ? canon_expf(__fsub_rn(mc0, M)) : 0.0f;
-            const float w1 = lane + 32 < C ? canon_expf(__fsub_rn(mc1, M)) : 0.0f;
-            if (lane < C) wts[warp * ATT_MAX_CHUNKS + lane] = w0;
-            if (lane + 32 < C) wts[warp * ATT_MAX_CHUNKS + lane + 32] = w1;
-            float Ls = 0.0f;   // chunk-ordered fma chain, operands gathered by shuffles
-            for (int cc = 0; cc < C; ++cc) {
-                const float wv = __shfl_sync(0xffffffffu, cc < 32 ? w0 : w1, cc & 31);
-                const float lv = __shfl_sync(0xffffffffu, cc < 32 ? lc0 : lc1, cc & 31);
-                Ls = __fmaf_rn(wv, lv, Ls);
-            }
-            if (lane == 0) stat[16 + warp] = __fdiv_rn(1.0f, Ls);
-        }
-        __syncthreads();
-        if (warp < 8) {   // warp = head, lane = dims 4*lane .. 4*lane+3; chunk chains, 16 loads in flight
-            const float* ph = p.att_part + static_cast<size_t>(8 * g + warp) * ATT_MAX_CHUNKS * ATT_PART_STRIDE +
-                              ATT_PART_O + 4 * lane;
-            float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int c0 = 0; c0 < C; c0 += 16) {
-                float4 v[16];
-#pragma unroll
-                for (int k = 0; k < 16; ++k)
-                    v[k] = c0 + k < C ? ld_cg_f4(ph + (c0 + k) * ATT_PART_STRIDE) : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-                for (int k = 0; k < 16; ++k) {
-                    if (c0 + k < C) {
-                        const float w = wts[warp * ATT_MAX_CHUNKS + c0 + k];
-                        O.x = __fmaf_rn(w, v[k].x, O.x);
-                        O.y = __fmaf_rn(w, v[k].y, O.y);
-                        O.z = __fmaf_rn(w, v[k].z, O.z);
-                        O.w = __fmaf_rn(w, v[k].w, O.w);
-                    }
-                }
-            }
-            const float inv = stat[16 + warp];
-            const float4 out = make_float4(__fmul_rn(O.x, inv), __fmul_rn(O.y, inv), __fmul_rn(O.z, inv),
-                                           __fmul_rn(O.w, inv));
-            *reinterpret_cast<float4*>(ab + warp * HEAD_DIM + 4 * lane) = out;
-            float* dst = p.att + 8 * g * HEAD_DIM + warp * HEAD_DIM + 4 * lane;   // caller's buffer: 4-byte aligned
-            dst[0] = out.x, dst[1] = out.y, dst[2] = out.z, dst[3] = out.w;
-        }
-        __syncthreads();
-        if (warp < 4) {   // four Q8_K blocks, ties-to-even (quantize_row_q8_K_avx2)
-            float y[8];
-#pragma unroll
-            for (int k = 0; k < 8; ++k) y[k] = ab[256 * warp + 8 * lane + k];
-            uint8_t* blk = p.att_q8k + static_cast<size_t>(4 * g + warp) * Q8K_BYTES;
-            quant_block_warp<false>(y, reinterpret_cast<int8_t*>(blk + 4), reinterpret_cast<float*>(blk),
-                                    reinterpret_cast<int16_t*>(blk + 260));
-        }
-        trace_step(p, l, 1, 3);
+            attention_unit_big(p, s, l, g, c, t0, np, seq);
     }
-}
-
-// xq <- global Q8_K blocks (block_q8_K layout) written by another phase.
-__device__ void load_q8k_blocks(const uint8_t* src, int nblocks, const Smem& s) {
-    const int tid = threadIdx.x;
-    for (int i = tid; i < nblocks * 64; i += blockDim.x) {   // qs words
-        const int b = i >> 6, wd = i & 63;
-        reinterpret_cast<uint32_t*>(s.xq()->qs[b])[wd] =
-            __ldcg(reinterpret_cast<const unsigned int*>(src + static_cast<size_t>(b) * Q8K_BYTES + 4) + wd);
+    if (C > DIST_COMBINE_MAX && p.attw) {
+        for (int b = ncta - 1 - cta; b < N_EMBD / 256; b += ncta) {
+            __syncthreads();
+            if (!combine_pair(p, s, l, b, seq)) return false;
+        }
     }
-    for (int i = tid; i < nblocks * 8; i += blockDim.x) {    // bsums (8 words per block)
-        const int b = i >> 3, wd = i & 7;
-        reinterpret_cast<uint32_t*>(s.xq()->bsums[b])[wd] =
-            __ldcg(reinterpret_cast<const unsigned int*>(src + static_cast<size_t>(b) * Q8K_BYTES + 260) + wd);
-    }
-    if (tid < nblocks) s.xq()->d[tid] = __ldcg(reinterpret_cast<const float*>(src + static_cast<size_t>(tid) * Q8K_BYTES));
-    __syncthreads();
+    return true;
 }
 
 // Every CTA combines the attention chunks of all 16 heads (same operations and order as
 // the last-CTA combine) and quantises the result ties-to-even straight into s.xq().
-__device__ void combine_attention(const DecodeParams& p, const Smem& s, int l, int cta) {
+__device__ bool combine_attention(const DecodeParams& p, const Smem& s, int l, int cta, unsigned seq) {
     // warp = head h, lane = dims 4*lane .. 4*lane+3: the chunk weights of a head never leave
     // its warp, so loads, max, exp, the L chain and the O chains run without a CTA barrier.
     const int n = p.pos + 1, C = attn_chunks(n);
     const int tid = threadIdx.x, lane = tid & 31, h = tid >> 5;
     float* ab = s.xs();   // [2048]
     const float* ph = p.att_part + static_cast<size_t>(h) * ATT_MAX_CHUNKS * ATT_PART_STRIDE;
-    const float2 ml = lane < C ? *reinterpret_cast<const float2*>(ph + lane * ATT_PART_STRIDE) : make_float2(0.f, 0.f);
+    float2 ml = make_float2(0.f, 0.f);   // lane c < C: chunk c's header (m, l), final after the grid barrier
+    const bool ok = lane >= C || load2_epoch(att_header(p, h, lane), att_epoch(seq, l), ml.x, ml.y, p.err);
     float4 v[DIST_COMBINE_MAX];
 #pragma unroll
     for (int cc = 0; cc < DIST_COMBINE_MAX; ++cc)
@@ -918,7 +950,23 @@ __device__ void combine_attention(const DecodeParams& p, const Smem& s, int l, i
         const float y[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
         quant_block_warp<false>(y, s.xq()->qs[h], &s.xq()->d[h], s.xq()->bsums[h]);
     }
-    __syncthreads();
+    return __syncthreads_and(ok);
+}
+
+// o_proj input for contexts combined by the head-pair combiners: the 2048 epoch-tagged
+// attention values (polled), quantized here to Q8_K ties-to-even, one block per warp --
+// the same bytes as the combiners' p.att_q8k blocks.
+__device__ bool load_att_epoch(const DecodeParams& p, const Smem& s, unsigned epoch) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    bool ok = true;
+    if (warp < N_EMBD / 256) {
+        const unsigned long long* src = p.attw + 256 * warp + 8 * lane;
+        float4 a, b;
+        ok = load4_epoch(src, epoch, a, p.err) && load4_epoch(src + 4, epoch, b, p.err);
+        const float y[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        quant_block_warp<false>(y, s.xq()->qs[warp], &s.xq()->d[warp], s.xq()->bsums[warp]);
+    }
+    return __syncthreads_and(ok);
 }
 
 __device__ bool phase_o(const DecodeParams& p, const Smem& s, int l, int cta, int ncta, unsigned seq) {
@@ -926,10 +974,11 @@ __device__ bool phase_o(const DecodeParams& p, const Smem& s, int l, int cta, in
     const PhaseLayout pl = phase_layout(L, *s.rows(), 1);
     const int r0 = pl.row0[0], n = pl.nrows[0];
     const float xr = threadIdx.x < n ? __ldcg(p.x + r0 + threadIdx.x) : 0.0f;   // residual rows, early
-    if (attn_chunks(p.pos + 1) <= DIST_COMBINE_MAX)
-        combine_attention(p, s, l, cta);
-    else
-        load_q8k_blocks(p.att_q8k, N_EMBD / 256, s);
+    if (attn_chunks(p.pos + 1) <= DIST_COMBINE_MAX) {
+        if (!combine_attention(p, s, l, cta, seq)) return false;
+    } else if (!load_att_epoch(p, s, att_epoch(seq, l))) {
+        return false;
+    }
     trace_step(p, l, 2, 1);
     if (!wait_weights(p, s, 4 * l + 1)) return false;
     trace_step(p, l, 2, 2);
@@ -1140,6 +1189,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
     trace_mark(p, 0);
     const LmPlan lmq = lm_plan(p, cta, ncta);
     const bool att32 = 32 * ((p.pos + 1 + 2047) / 2048) == 32;   // chunk length (uniform over CTAs)
+    const bool flagged = att_flagged(p);
     // Weight phase w+1 is issued while waiting at the barrier in front of phase w: its
     // buffer was last used by phase w-1, which every thread of this CTA has finished.
     for (int l = 0; l < p.n_layer; ++l) {
@@ -1150,8 +1200,18 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
         } else if (!traced_barrier(p, bs, 5 * l, [&] { issue_weight_phase(p, s, 4 * l + 1, cta, ncta); })) {
             return;
         }
-        phase_attention(p, s, l, cta, ncta, attn_chunks(p.pos + 1) > DIST_COMBINE_MAX, seq);
-        if (!traced_barrier(p, bs, 5 * l + 1, [&] { issue_weight_phase(p, s, 4 * l + 2, cta, ncta); })) return;
+        if (!phase_attention(p, s, l, cta, ncta, seq)) return;
+        if (flagged) {   // no grid barrier: o_proj waits for the combiners' epoch-tagged values
+            __syncthreads();   // buffer 0 (attention scratch) is free once this CTA's units are done
+            if (threadIdx.x == 0) {
+                fence_proxy_async_smem();
+                issue_weight_phase(p, s, 4 * l + 2, cta, ncta);
+            }
+            trace_mark(p, 2 + 2 * (5 * l + 1));
+            trace_mark(p, 3 + 2 * (5 * l + 1));
+        } else if (!traced_barrier(p, bs, 5 * l + 1, [&] { issue_weight_phase(p, s, 4 * l + 2, cta, ncta); })) {
+            return;
+        }
         // o_proj -> gate/up and down -> next QKV exchange the residual through epoch-tagged
         // words: no grid barrier (every consumer needs all of x, which orders all reuse).
         if (!phase_o(p, s, l, cta, ncta, seq)) return;
@@ -1190,7 +1250,13 @@ __global__ void k_kv_append(const float* __restrict__ k, const float* __restrict
 
 __global__ void __launch_bounds__(DEC_THREADS, 1) k_attention(const DecodeParams p) {
     const Smem s;
-    phase_attention(p, s, 0, blockIdx.x, gridDim.x, true, 0u);
+    phase_attention(p, s, 0, blockIdx.x, gridDim.x, 1u);
+}
+
+// Standalone op: head pair blockIdx.x of the chunks written by k_attention (stream order).
+__global__ void __launch_bounds__(DEC_THREADS, 1) k_att_combine(const DecodeParams p) {
+    const Smem s;
+    combine_pair(p, s, 0, blockIdx.x, 1u);
 }
 
 }  // namespace
@@ -1219,7 +1285,7 @@ cudaError_t launch_decode(const DecodeParams& p, int n_ctas, cudaStream_t stream
 
 namespace mcpm {
 cudaError_t launch_attention(const float* q, const float* k, const float* v, float* kc, float* vc, int pos, int max_seq,
-                             float* out, uint8_t* out_q8k, float* part, unsigned* cnt, cudaStream_t stream) {
+                             float* out, uint8_t* out_q8k, float* part, cudaStream_t stream) {
     k_kv_append<<<1, KV_DIM, 0, stream>>>(k, v, kc, vc, pos);
     DecodeParams p{};
     p.q = const_cast<float*>(q);
@@ -1230,18 +1296,19 @@ cudaError_t launch_attention(const float* q, const float* k, const float* v, flo
     p.att = out;
     p.att_q8k = out_q8k;
     p.att_part = part;
-    p.cnt = cnt;
     static int prepared_dev = -1;
     int dev = 0;
     cudaGetDevice(&dev);
     if (prepared_dev != dev) {
-        const cudaError_t e = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   SM_BYTES);
+        cudaError_t e = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, SM_BYTES);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k_att_combine, cudaFuncAttributeMaxDynamicSharedMemorySize, SM_BYTES);
         if (e != cudaSuccess) return e;
         prepared_dev = dev;
     }
     const int n = pos + 1, P = 32 * ((n + 2047) / 2048), C = (n + P - 1) / P;
-    k_attention<<<2 * C, DEC_THREADS, SM_BYTES, stream>>>(p);
+    k_attention<<<2 * C, DEC_THREADS, SM_BYTES, stream>>>(p);   // chunk records (headers with epoch 1<<8)
+    k_att_combine<<<N_EMBD / 256, DEC_THREADS, SM_BYTES, stream>>>(p);
     return cudaGetLastError();
 }
 }  // namespace mcpm

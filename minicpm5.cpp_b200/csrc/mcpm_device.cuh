@@ -48,6 +48,9 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
 __device__ __forceinline__ void fence_mbar_init() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
+// Orders this thread's earlier generic-proxy shared-memory accesses before its later
+// async-proxy (bulk copy) writes to the same buffer.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                  : "memory");
@@ -144,6 +147,25 @@ __device__ __forceinline__ bool load4_epoch(const unsigned long long* src, unsig
                     __uint_as_float(static_cast<unsigned>(b.x)), __uint_as_float(static_cast<unsigned>(b.y)));
     return true;
 }
+// Two consecutive epoch-tagged values (16-byte aligned), polled until both carry `epoch`;
+// false (and ERR_TIMEOUT raised) after 1 s.
+__device__ __forceinline__ bool load2_epoch(const unsigned long long* src, unsigned epoch, float& a, float& b,
+                                            unsigned* err) {
+    ulonglong2 w = ld_epoch2(src);
+    if ((w.x >> 32) != epoch || (w.y >> 32) != epoch) {
+        const uint64_t t0 = globaltimer();
+        do {
+            w = ld_epoch2(src);
+            if (((w.x >> 32) != epoch || (w.y >> 32) != epoch) && globaltimer() - t0 > 1000000000ull) {
+                if (err) atomicOr(err, ERR_TIMEOUT);
+                return false;
+            }
+        } while ((w.x >> 32) != epoch || (w.y >> 32) != epoch);
+    }
+    a = __uint_as_float(static_cast<unsigned>(w.x));
+    b = __uint_as_float(static_cast<unsigned>(w.y));
+    return true;
+}
 __device__ __forceinline__ uint32_t ld_acquire_u32(const unsigned* p) {
     uint32_t v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -172,13 +194,14 @@ __device__ __forceinline__ float h2f(uint32_t bits16) {
 __device__ __forceinline__ int sbyte(uint32_t w, int i) { return static_cast<int>(w << (24 - 8 * i)) >> 24; }
 __device__ __forceinline__ int ubyte(uint32_t w, int i) { return (w >> (8 * i)) & 0xff; }
 
-// Bounded wait on an mbarrier phase.  Returns false (and sets ERR_TIMEOUT) after ~1 s.
+// Bounded wait on an mbarrier phase.  Returns false (and sets ERR_TIMEOUT in *err when err
+// is given) after ~1 s.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* err) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     while (!mbar_try_wait(bar, parity)) {
         if (globaltimer() - t0 > 1000000000ull) {
-            atomicOr(err, ERR_TIMEOUT);
+            if (err) atomicOr(err, ERR_TIMEOUT);
             return false;
         }
     }

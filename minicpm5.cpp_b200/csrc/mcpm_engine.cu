@@ -53,6 +53,7 @@ struct mcpm_engine {
     float *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr, *att_part = nullptr, *logits = nullptr;
     unsigned long long* xll = nullptr;   // residual stream with per-element epochs
     unsigned long long* qll = nullptr;   // q, K row, V row with per-element epochs
+    unsigned long long* attw = nullptr;  // combined attention with per-element epochs
     float* am_val = nullptr;
     int* am_idx = nullptr;
     uint8_t* att_q8k = nullptr;
@@ -98,6 +99,7 @@ void free_model(mcpm_engine* e) {
     free_dev(e->h);
     free_dev(e->xll);
     free_dev(e->qll);
+    free_dev(e->attw);
     free_dev(e->att_part);
     free_dev(e->logits);
     free_dev(e->am_val);
@@ -169,6 +171,8 @@ mcpm_status reset_ctl(mcpm_engine* e) {
     // the launch sequence restarts, so no epoch of an aborted launch may remain
     if (e->xll) MCPM_CUDA(cudaMemsetAsync(e->xll, 0, N_EMBD * sizeof(unsigned long long), e->stream));
     if (e->qll) MCPM_CUDA(cudaMemsetAsync(e->qll, 0, (N_EMBD + 2 * KV_DIM) * sizeof(unsigned long long), e->stream));
+    if (e->attw) MCPM_CUDA(cudaMemsetAsync(e->attw, 0, N_EMBD * sizeof(unsigned long long), e->stream));
+    if (e->att_part) MCPM_CUDA(cudaMemsetAsync(e->att_part, 0, ATT_PART_FLOATS * sizeof(float), e->stream));   // headers
     MCPM_CUDA(cudaStreamSynchronize(e->stream));
     return MCPM_OK;
 }
@@ -207,6 +211,7 @@ DecodeParams make_params(const mcpm_engine* e, int token, int pos, int write_log
     p.h = e->h;
     p.xll = e->xll;
     p.qll = e->qll;
+    p.attw = e->attw;
     p.att_part = e->att_part;
     p.logits = e->logits;
     p.am_val = e->am_val;
@@ -431,7 +436,10 @@ mcpm_status mcpm_load_gguf(mcpm_engine* e, const char* path) {
     MCPM_CUDA(cudaMemset(e->xll, 0, N_EMBD * sizeof(unsigned long long)));
     MCPM_CUDA(cudaMalloc(&e->qll, (N_EMBD + 2 * KV_DIM) * sizeof(unsigned long long)));
     MCPM_CUDA(cudaMemset(e->qll, 0, (N_EMBD + 2 * KV_DIM) * sizeof(unsigned long long)));
-    MCPM_CUDA(cudaMalloc(&e->att_part, sizeof(float) * N_HEAD * ATT_MAX_CHUNKS * ATT_PART_STRIDE));
+    MCPM_CUDA(cudaMalloc(&e->attw, N_EMBD * sizeof(unsigned long long)));
+    MCPM_CUDA(cudaMemset(e->attw, 0, N_EMBD * sizeof(unsigned long long)));
+    MCPM_CUDA(cudaMalloc(&e->att_part, ATT_PART_FLOATS * sizeof(float)));
+    MCPM_CUDA(cudaMemset(e->att_part, 0, ATT_PART_FLOATS * sizeof(float)));
     MCPM_CUDA(cudaMalloc(&e->logits, sizeof(float) * e->n_vocab));
     MCPM_CUDA(cudaMalloc(&e->am_val, sizeof(float) * e->n_ctas));
     MCPM_CUDA(cudaMalloc(&e->am_idx, sizeof(int) * e->n_ctas));
@@ -612,12 +620,11 @@ mcpm_status mcpm_swiglu_q8k(const float* gate, const float* up, void* out, int n
     return cuda_status(op_swiglu_q8k(gate, up, out, n, static_cast<cudaStream_t>(stream)));
 }
 
-// Attention workspace (chunk partials, combine counters, Q8_K sink), one per device,
-// allocated on first use and kept until exit.
+// Attention workspace (chunk records, Q8_K sink), one per device, allocated on first use
+// and kept until exit.
 namespace {
 struct AttWorkspace {
     float* part = nullptr;
-    unsigned* cnt = nullptr;
     uint8_t* q8k = nullptr;
 };
 AttWorkspace g_att_ws[64];
@@ -635,13 +642,11 @@ mcpm_status mcpm_attention(const float* q, const float* k, const float* v, float
     AttWorkspace& ws = g_att_ws[dev];
     if (!ws.part) {
         MCPM_CUDA(cudaMalloc(&ws.part, ATT_PART_FLOATS * sizeof(float)));
-        MCPM_CUDA(cudaMalloc(&ws.cnt, 4 * sizeof(unsigned)));
         MCPM_CUDA(cudaMalloc(&ws.q8k, (N_EMBD / 256) * Q8K_BYTES));
-        MCPM_CUDA(cudaMemset(ws.cnt, 0, 4 * sizeof(unsigned)));
     }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     return cuda_status(launch_attention(q, k, v, kcache, vcache, pos, max_seq, out,
-                                        out_q8k ? static_cast<uint8_t*>(out_q8k) : ws.q8k, ws.part, ws.cnt, s));
+                                        out_q8k ? static_cast<uint8_t*>(out_q8k) : ws.q8k, ws.part, s));
 }
 
 mcpm_status mcpm_gemv_q8k_timed(int type, const void* w, int n_copies, const void* xq, float* y, int rows, int cols,

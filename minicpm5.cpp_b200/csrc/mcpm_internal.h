@@ -73,14 +73,15 @@ struct DecodeParams {
     unsigned long long* xll;   // residual stream published per element as (epoch << 32) | fp32 bits [N_EMBD]
     unsigned long long* qll;   // rotated q [N_EMBD] then this position's K and V rows [2*KV_DIM], same encoding;
                                // null outside the decode kernel (q and the cache are then final)
-    float* att_part;    // [N_HEAD][ATT_MAX_CHUNKS][ATT_PART_STRIDE]
+    float* att_part;    // [N_HEAD][ATT_MAX_CHUNKS][ATT_PART_STRIDE]: epoch-tagged (m, l) header, o[128]
+    unsigned long long* attw;   // combined attention [N_EMBD], epoch-tagged (decode kernel, > 16 chunks)
     float* logits;      // [n_vocab]
     float* am_val;      // per-CTA argmax partials
     int* am_idx;
     int* argmax_out;
     int* token_dev;     // token id for the next step (greedy chaining)
     unsigned* bar;      // grid barrier {count, base}, [2] launch sequence (epochs of xll)
-    unsigned* cnt;      // [0..1] attention combine counters, [2] argmax counter
+    unsigned* cnt;      // [2] argmax counter
     unsigned* err;      // error bits
     unsigned long long* trace;   // optional: CTA 0 phase timestamps (2 per phase + 2)
     int token;          // < 0: read *token_dev
@@ -97,7 +98,7 @@ int decode_max_ctas_per_sm();
 // the decode kernel's numerics.  part: ATT_PART_FLOATS floats, cnt: 3 zeroed words.
 constexpr size_t ATT_PART_FLOATS = static_cast<size_t>(N_HEAD) * ATT_MAX_CHUNKS * ATT_PART_STRIDE;
 cudaError_t launch_attention(const float* q, const float* k, const float* v, float* kc, float* vc, int pos, int max_seq,
-                             float* out, uint8_t* out_q8k, float* part, unsigned* cnt, cudaStream_t stream);
+                             float* out, uint8_t* out_q8k, float* part, cudaStream_t stream);
 
 // Standalone op launchers (mcpm_ops.cu).
 cudaError_t op_quantize_q8k(const float* x, void* y, int n, int rounding, cudaStream_t s);

@@ -8,9 +8,9 @@
 // on its first call; this variant uses a fixed workspace that lives in this library's
 // static device memory instead, so no call ever allocates.
 //
-// The workspace below is the chunk partials of 16 query heads x 64 chunks x (2 + 128)
-// floats (540,672 bytes), the combine counters and a Q8_K sink: enough for any context
-// up to MAX_SEQ = 16384 positions.  Every GPU that loads the library holds it until the
+// The workspace below is the chunk records of 16 query heads x 64 chunks (a 16-byte
+// header and 128 floats each, 540,672 bytes) and a Q8_K sink: enough for any context up
+// to MAX_SEQ = 16384 positions.  Every GPU that loads the library holds it until the
 // process exits.  All calls on a device share it, so calls that overlap on the GPU race
 // and must be serialised by the caller (one stream, or events).
 #include <cstdio>
@@ -24,7 +24,6 @@ using namespace mcpm;
 namespace {
 
 static __device__ __align__(256) float g_att_part[ATT_PART_FLOATS];
-static __device__ __align__(256) unsigned g_att_cnt[4];
 static __device__ __align__(256) uint8_t g_att_q8k[(N_EMBD / 256) * Q8K_BYTES];
 
 // Device addresses of the arrays above, looked up once per device.  In host code the
@@ -32,7 +31,6 @@ static __device__ __align__(256) uint8_t g_att_q8k[(N_EMBD / 256) * Q8K_BYTES];
 struct ScratchAddr {
     bool ready = false;
     float* part = nullptr;
-    unsigned* cnt = nullptr;
     uint8_t* q8k = nullptr;
 };
 ScratchAddr g_addr[64];
@@ -41,7 +39,6 @@ mcpm_status setup_scratch(int dev) {
     ScratchAddr& a = g_addr[dev];
     if (a.ready) return MCPM_OK;
     if (cudaGetSymbolAddress(reinterpret_cast<void**>(&a.part), g_att_part) != cudaSuccess ||
-        cudaGetSymbolAddress(reinterpret_cast<void**>(&a.cnt), g_att_cnt) != cudaSuccess ||
         cudaGetSymbolAddress(reinterpret_cast<void**>(&a.q8k), g_att_q8k) != cudaSuccess) {
         std::fprintf(stderr, "[mcpm] mcpm_attention_noalloc: cudaGetSymbolAddress failed on device %d\n", dev);
         return MCPM_CUDA_ERROR;
@@ -74,9 +71,7 @@ extern "C" mcpm_status mcpm_attention_noalloc(const float* q, const float* k, co
     if (st != MCPM_OK) return st;
     const ScratchAddr& a = g_addr[dev];
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    // the combine counters must start at zero; the partials are fully rewritten by each call
-    if (cudaMemsetAsync(a.cnt, 0, sizeof(unsigned) * 4, s) != cudaSuccess) return MCPM_CUDA_ERROR;
     const cudaError_t e = launch_attention(q, k, v, kcache, vcache, pos, max_seq, out,
-                                           out_q8k ? static_cast<uint8_t*>(out_q8k) : a.q8k, a.part, a.cnt, s);
+                                           out_q8k ? static_cast<uint8_t*>(out_q8k) : a.q8k, a.part, s);
     return e == cudaSuccess ? MCPM_OK : MCPM_CUDA_ERROR;
 }
