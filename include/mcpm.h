@@ -71,6 +71,9 @@ const int* mcpm_argmax_device(mcpm_engine* e);
 /* Internal state for parity checks: residual x (n_embd floats), one K and V row. */
 mcpm_status mcpm_read_x(mcpm_engine* e, float* x_host);
 mcpm_status mcpm_read_kv(mcpm_engine* e, int layer, int pos, float* k_host, float* v_host);
+/* Writes n_pos K and V rows ([n_pos][n_head_kv * head_dim] floats each) of one layer from
+ * position pos0: restores a saved cache, or seeds one for a parity check of a late step. */
+mcpm_status mcpm_write_kv(mcpm_engine* e, int layer, int pos0, int n_pos, const float* k_host, const float* v_host);
 /* n_layer, n_embd, n_ff, n_head, n_head_kv, n_vocab of the loaded model. */
 mcpm_status mcpm_model_dims(mcpm_engine* e, int dims[6]);
 /* Phase trace (no reference counterpart; the reference only times whole loops,

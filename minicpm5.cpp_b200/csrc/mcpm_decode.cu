@@ -668,15 +668,18 @@ __device__ void attention_unit32(const DecodeParams& p, const Smem& s, int l, in
 
 // One attention unit of a chunk longer than 32 positions (contexts above 2048): the 8 query
 // heads of KV head g against positions [t0, t0+np), np <= 256.  K rows stream into shared
-// memory with cp.async, up to 128 rows per round trip, then V rows through the same buffer.
+// memory with cp.async, up to ATT_BIG_ROWS rows per round trip, then V rows through the same
+// buffer.
 // Warp w: head pair w&3 (q in registers), positions (w>>2)*4 + group + 16i; lane j of an
 // 8-lane group owns dims 4j + 32i + c of each dot (the canonical 8-lane split).  Same
 // numerics as attention_unit32.  q is final here: a grid barrier follows the QKV phase.
-constexpr int ATT_BIG_ROWS = 128;
-// q, K/V rows, scores, then the combine's stat / weights / output (phase_attention)
-static_assert((8 * HEAD_DIM + ATT_BIG_ROWS * HEAD_DIM + 8 * ATT_SC_STRIDE + 32 + 8 * ATT_MAX_CHUNKS + 8 * HEAD_DIM) *
-                      sizeof(float) <= WBUF_BYTES,
+constexpr int ATT_BIG_ROWS = 160;   // one round trip per chunk up to 10240 positions (chunk 160)
+// q, K/V rows, scores, stat
+static_assert((8 * HEAD_DIM + ATT_BIG_ROWS * HEAD_DIM + 8 * ATT_SC_STRIDE + 16) * sizeof(float) <= WBUF_BYTES,
               "attention scratch exceeds weight buffer 0");
+// combine_pair: chunk o vectors of two heads, weights, chunk sums, 1/L, output
+static_assert((2 * ATT_MAX_CHUNKS * HEAD_DIM + 4 * ATT_MAX_CHUNKS + 4 + 256) * sizeof(float) <= WBUF_BYTES,
+              "combine scratch exceeds weight buffer 0");
 __device__ void attention_unit_big(const DecodeParams& p, const Smem& s, int l, int g, int c, int t0, int np,
                                    unsigned seq) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, j = lane & 7, G = lane >> 3;
@@ -704,32 +707,46 @@ __device__ void attention_unit_big(const DecodeParams& p, const Smem& s, int l, 
             qa[i] = *reinterpret_cast<const float4*>(q0 + 32 * i);
             qb[i] = *reinterpret_cast<const float4*>(q0 + HEAD_DIM + 32 * i);
         }
-        for (int base = ps * 4; base < ns; base += 16) {   // warp-uniform trip count
-            const int tt = base + G;
-            const bool valid = tt < ns;
-            const float* kr = kv + (valid ? tt : 0) * HEAD_DIM + 4 * j;
-            float d0 = 0.0f, d1 = 0.0f;
+        // positions ta = base + G, tb = ta + 16 for heads a = 2hp, b = 2hp+1: four dots per
+        // lane group; the 8-lane butterfly runs reduce-scatter (a lane sends the value its
+        // partner keeps), the same additions as v += shfl_xor(v, 4 / 2 / 1) on each dot.
+        for (int base = ps * 4; base < ns; base += 32) {   // warp-uniform trip count
+            const int ta = base + G, tb = ta + 16;
+            const float* ka = kv + min(ta, ns - 1) * HEAD_DIM + 4 * j;
+            const float* kb = kv + min(tb, ns - 1) * HEAD_DIM + 4 * j;
+            float aa = 0.0f, ba = 0.0f, ab = 0.0f, bb = 0.0f;   // (head a|b, position ta|tb)
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const float4 k = *reinterpret_cast<const float4*>(kr + 32 * i);
-                d0 = __fmaf_rn(qa[i].x, k.x, d0);
-                d0 = __fmaf_rn(qa[i].y, k.y, d0);
-                d0 = __fmaf_rn(qa[i].z, k.z, d0);
-                d0 = __fmaf_rn(qa[i].w, k.w, d0);
-                d1 = __fmaf_rn(qb[i].x, k.x, d1);
-                d1 = __fmaf_rn(qb[i].y, k.y, d1);
-                d1 = __fmaf_rn(qb[i].z, k.z, d1);
-                d1 = __fmaf_rn(qb[i].w, k.w, d1);
+                const float4 x = *reinterpret_cast<const float4*>(ka + 32 * i);
+                const float4 y = *reinterpret_cast<const float4*>(kb + 32 * i);
+                aa = __fmaf_rn(qa[i].x, x.x, aa);
+                aa = __fmaf_rn(qa[i].y, x.y, aa);
+                aa = __fmaf_rn(qa[i].z, x.z, aa);
+                aa = __fmaf_rn(qa[i].w, x.w, aa);
+                ba = __fmaf_rn(qb[i].x, x.x, ba);
+                ba = __fmaf_rn(qb[i].y, x.y, ba);
+                ba = __fmaf_rn(qb[i].z, x.z, ba);
+                ba = __fmaf_rn(qb[i].w, x.w, ba);
+                ab = __fmaf_rn(qa[i].x, y.x, ab);
+                ab = __fmaf_rn(qa[i].y, y.y, ab);
+                ab = __fmaf_rn(qa[i].z, y.z, ab);
+                ab = __fmaf_rn(qa[i].w, y.w, ab);
+                bb = __fmaf_rn(qb[i].x, y.x, bb);
+                bb = __fmaf_rn(qb[i].y, y.y, bb);
+                bb = __fmaf_rn(qb[i].z, y.z, bb);
+                bb = __fmaf_rn(qb[i].w, y.w, bb);
             }
-#pragma unroll
-            for (int o = 4; o >= 1; o >>= 1) {
-                d0 = __fadd_rn(d0, __shfl_xor_sync(0xffffffffu, d0, o));
-                d1 = __fadd_rn(d1, __shfl_xor_sync(0xffffffffu, d1, o));
-            }
-            if (valid && j == 0) {
-                sc[(2 * hp) * ATT_SC_STRIDE + s0 + tt] = __fmul_rn(d0, scale);
-                sc[(2 * hp + 1) * ATT_SC_STRIDE + s0 + tt] = __fmul_rn(d1, scale);
-            }
+            const bool lo4 = j < 4;   // keeps head a
+            const float r1 = __shfl_xor_sync(0xffffffffu, lo4 ? ba : aa, 4);
+            const float r2 = __shfl_xor_sync(0xffffffffu, lo4 ? bb : ab, 4);
+            const float X = __fadd_rn(lo4 ? aa : ba, r1);   // position ta
+            const float Y = __fadd_rn(lo4 ? ab : bb, r2);   // position tb
+            const bool lo2 = (j & 2) == 0;                  // keeps ta
+            const float r3 = __shfl_xor_sync(0xffffffffu, lo2 ? Y : X, 2);
+            float Z = __fadd_rn(lo2 ? X : Y, r3);
+            Z = __fadd_rn(Z, __shfl_xor_sync(0xffffffffu, Z, 1));
+            const int t = lo2 ? ta : tb;
+            if ((j & 1) == 0 && t < ns) sc[(2 * hp + (lo4 ? 0 : 1)) * ATT_SC_STRIDE + s0 + t] = __fmul_rn(Z, scale);
         }
         __syncthreads();   // kv is overwritten next
     }
@@ -748,8 +765,10 @@ __device__ void attention_unit_big(const DecodeParams& p, const Smem& s, int l, 
         for (int o = 16; o >= 1; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
         if (lane == 0) stat[warp] = m, stat[8 + warp] = sum;
     }
-    float acc0 = 0.0f, acc1 = 0.0f;   // o[h][d] = fma chain over positions
-    const int h0 = tid >> 7, h1 = h0 + 4, dd = tid & 127;
+    // o[h][d] = fma chain over positions: threads 0-127 own heads 4hq..4hq+3 x dims 2dp, 2dp+1
+    // (float2 V rows, float4 probabilities): the fewest shared-memory wavefronts per position.
+    const int hq = (tid >> 6) & 1, dp = tid & 63;
+    float acc[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
     trace_step(p, l, 1, 8);
     for (int s0 = 0; s0 < np; s0 += ATT_BIG_ROWS) {
         const int ns = min(ATT_BIG_ROWS, np - s0);
@@ -759,27 +778,48 @@ __device__ void attention_unit_big(const DecodeParams& p, const Smem& s, int l, 
         cp_async_wait_all();
         __syncthreads();   // V rows, and (first round) the probabilities
         if (s0 == 0) trace_step(p, l, 1, 9);
-        const float* p0 = sc + h0 * ATT_SC_STRIDE + s0;
-        const float* p1 = sc + h1 * ATT_SC_STRIDE + s0;
-        int tt = 0;
-        for (; tt + 4 <= ns; tt += 4) {
-            float v[4], a0[4], a1[4];
+        if (tid < 128) {
+            const float* pr = sc + 4 * hq * ATT_SC_STRIDE + s0;
+            const float* vr = kv + 2 * dp;
+            int tt = 0;
+            for (; tt + 4 <= ns; tt += 4) {
+                float4 pw[4];
+                float2 v[4];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) v[k] = kv[(tt + k) * HEAD_DIM + dd], a0[k] = p0[tt + k], a1[k] = p1[tt + k];
+                for (int h = 0; h < 4; ++h) pw[h] = *reinterpret_cast<const float4*>(pr + h * ATT_SC_STRIDE + tt);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) acc0 = __fmaf_rn(a0[k], v[k], acc0), acc1 = __fmaf_rn(a1[k], v[k], acc1);
-        }
-        for (; tt < ns; ++tt) {
-            const float v = kv[tt * HEAD_DIM + dd];
-            acc0 = __fmaf_rn(p0[tt], v, acc0);
-            acc1 = __fmaf_rn(p1[tt], v, acc1);
+                for (int k = 0; k < 4; ++k) v[k] = *reinterpret_cast<const float2*>(vr + (tt + k) * HEAD_DIM);
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    const float w[4] = {pw[h].x, pw[h].y, pw[h].z, pw[h].w};
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        acc[h][0] = __fmaf_rn(w[k], v[k].x, acc[h][0]);
+                        acc[h][1] = __fmaf_rn(w[k], v[k].y, acc[h][1]);
+                    }
+                }
+            }
+            for (; tt < ns; ++tt) {
+                const float2 v = *reinterpret_cast<const float2*>(vr + tt * HEAD_DIM);
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    const float w = pr[h * ATT_SC_STRIDE + tt];
+                    acc[h][0] = __fmaf_rn(w, v.x, acc[h][0]);
+                    acc[h][1] = __fmaf_rn(w, v.y, acc[h][1]);
+                }
+            }
         }
         __syncthreads();
     }
-    float* pa0 = p.att_part + (static_cast<size_t>(8 * g + h0) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
-    float* pa1 = p.att_part + (static_cast<size_t>(8 * g + h1) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
-    __stcg(pa0 + ATT_PART_O + dd, acc0);
-    __stcg(pa1 + ATT_PART_O + dd, acc1);
+    trace_step(p, l, 1, 3);
+    if (tid < 128) {
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+            float* pa = p.att_part + (static_cast<size_t>(8 * g + 4 * hq + h) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE +
+                        ATT_PART_O + 2 * dp;
+            __stcg(reinterpret_cast<float2*>(pa), make_float2(acc[h][0], acc[h][1]));
+        }
+    }
     __syncthreads();   // every o value of the chunk is stored (program order), then the headers
     if (tid < 8) {
         if (att_flagged(p)) __threadfence();   // combiners poll the headers (no grid barrier)

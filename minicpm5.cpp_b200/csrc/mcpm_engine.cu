@@ -519,6 +519,19 @@ mcpm_status mcpm_read_kv(mcpm_engine* e, int layer, int pos, float* k_host, floa
     return MCPM_OK;
 }
 
+mcpm_status mcpm_write_kv(mcpm_engine* e, int layer, int pos0, int n_pos, const float* k_host, const float* v_host) {
+    if (!e || !k_host || !v_host) return MCPM_BAD_ARG;
+    if (!e->loaded || !e->kc) return MCPM_NOT_LOADED;
+    if (layer < 0 || layer >= e->n_layer || pos0 < 0 || n_pos < 0 || pos0 > e->max_seq - n_pos) return MCPM_BAD_ARG;
+    MCPM_CUDA(cudaSetDevice(e->device));
+    const size_t off = (static_cast<size_t>(layer) * e->max_seq + pos0) * KV_DIM;
+    const size_t bytes = static_cast<size_t>(n_pos) * KV_DIM * 4;
+    MCPM_CUDA(cudaMemcpyAsync(e->kc + off, k_host, bytes, cudaMemcpyHostToDevice, e->stream));
+    MCPM_CUDA(cudaMemcpyAsync(e->vc + off, v_host, bytes, cudaMemcpyHostToDevice, e->stream));
+    MCPM_CUDA(cudaStreamSynchronize(e->stream));
+    return MCPM_OK;
+}
+
 mcpm_status mcpm_model_dims(mcpm_engine* e, int dims[6]) {
     if (!e || !dims) return MCPM_BAD_ARG;
     if (!e->loaded) return MCPM_NOT_LOADED;

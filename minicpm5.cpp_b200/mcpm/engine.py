@@ -51,6 +51,7 @@ SIGNATURES = {
     "mcpm_argmax_device": (P, [P]),
     "mcpm_read_x": (I, [P, C.POINTER(F)]),
     "mcpm_read_kv": (I, [P, I, I, C.POINTER(F), C.POINTER(F)]),
+    "mcpm_write_kv": (I, [P, I, I, I, C.POINTER(F), C.POINTER(F)]),
     "mcpm_model_dims": (I, [P, C.POINTER(I)]),
     "mcpm_engine_stream": (P, [P]),
     "mcpm_engine_n_ctas": (I, [P]),
@@ -160,6 +161,12 @@ class MiniCPM5Engine:
         v = np.zeros(256, np.float32)
         check(self.lib.mcpm_read_kv(self.h, layer, pos, _fptr(k), _fptr(v)), "mcpm_read_kv")
         return k, v
+
+    def write_kv(self, layer: int, pos0: int, k: np.ndarray, v: np.ndarray) -> None:
+        k = np.ascontiguousarray(k, dtype=np.float32)
+        v = np.ascontiguousarray(v, dtype=np.float32)
+        assert k.shape == v.shape and k.ndim == 2 and k.shape[1] == 256
+        check(self.lib.mcpm_write_kv(self.h, layer, pos0, k.shape[0], _fptr(k), _fptr(v)), "mcpm_write_kv")
 
     def trace_enable(self, on: bool = True) -> None:
         check(self.lib.mcpm_trace_enable(self.h, int(on)), "mcpm_trace_enable")

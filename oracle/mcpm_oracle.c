@@ -657,3 +657,9 @@ void orc_get_kv(const orc_state* s, int layer, float* k, float* v, int n_pos) {
     memcpy(k, s->kc[layer], sizeof(float) * (size_t)n_pos * kvd);
     memcpy(v, s->vc[layer], sizeof(float) * (size_t)n_pos * kvd);
 }
+
+void orc_set_kv(orc_state* s, int layer, const float* k, const float* v, int n_pos) {
+    const int kvd = s->d.n_head_kv * (s->d.n_embd / s->d.n_head);
+    memcpy(s->kc[layer], k, sizeof(float) * (size_t)n_pos * kvd);
+    memcpy(s->vc[layer], v, sizeof(float) * (size_t)n_pos * kvd);
+}

@@ -84,6 +84,8 @@ int orc_forward(orc_state* s, int token, int pos, float* logits);
 /* Copies of internal state for debugging parity: the fp32 residual x after the last call. */
 void orc_get_x(const orc_state* s, float* x);
 void orc_get_kv(const orc_state* s, int layer, float* k, float* v, int n_pos);
+/* Overwrites rows [0, n_pos) of one layer's K/V cache (seeds a late-position check). */
+void orc_set_kv(orc_state* s, int layer, const float* k, const float* v, int n_pos);
 
 #ifdef __cplusplus
 }

@@ -207,6 +207,7 @@ class Oracle:
         L.orc_forward.argtypes = [P, C.c_int, C.c_int, F]
         L.orc_get_x.argtypes = [P, F]
         L.orc_get_kv.argtypes = [P, C.c_int, F, F, C.c_int]
+        L.orc_set_kv.argtypes = [P, C.c_int, F, F, C.c_int]
 
     def fp16(self, h: int) -> float:
         return self.lib.orc_fp16_to_fp32(h)
@@ -308,6 +309,11 @@ class OracleModel:
         out = np.zeros(spec.N_EMBD, np.float32)
         self.o.lib.orc_get_x(self.h, _fptr(out))
         return out
+
+    def set_kv(self, layer: int, k: np.ndarray, v: np.ndarray) -> None:
+        k = np.ascontiguousarray(k, dtype=np.float32)
+        v = np.ascontiguousarray(v, dtype=np.float32)
+        self.o.lib.orc_set_kv(self.h, layer, _fptr(k), _fptr(v), k.shape[0])
 
     def tensor(self, name: str) -> np.ndarray:
         t = self.tensors[name]

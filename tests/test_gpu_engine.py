@@ -46,6 +46,45 @@ def test_forward_bitexact_vs_restatement(engine, oracle_model):
         tok = want_tok
 
 
+@pytest.mark.parametrize("pos", [300, 1000, 3000, 8200, 10300])
+def test_late_steps_bitexact_vs_restatement(cuda, oracle, model_path, pos):
+    """Two decode steps at a late position over a seeded cache (the same random K/V rows
+    0..pos-1 in the engine and in the restatement), covering every attention path of the
+    decode kernel: 300 positions (32-row chunks, 10 chunks combined in the o_proj prologue
+    behind a grid barrier), 1000 (32-row chunks, 32 chunks: head-pair combiners polled
+    without a barrier), 3000 / 8200 (64- / 160-row chunks), 10300 (192-row chunks, two
+    staging rounds)."""
+    import oracle as O
+    from mcpm import engine as E, spec
+    max_seq = pos + 2
+    e = E.MiniCPM5Engine(device=0, max_seq=max_seq)
+    assert e.load_model(model_path)
+    om = O.OracleModel(oracle, model_path, max_seq)
+    try:
+        rng = np.random.default_rng(pos)
+        k = rng.normal(0, 1, (pos, 256)).astype(np.float32)
+        v = rng.normal(0, 1, (pos, 256)).astype(np.float32)
+        for layer in range(spec.N_LAYER):
+            kl, vl = np.roll(k, layer, axis=0), np.roll(v, 3 * layer, axis=0)
+            e.write_kv(layer, 0, kl, vl)
+            om.set_kv(layer, kl, vl)
+        ref_logits = np.zeros(e.n_vocab, np.float32)
+        tok = 7
+        for p in (pos, pos + 1):
+            got = e.forward(tok, p).copy()
+            want_tok = om.forward(tok, p, ref_logits)
+            gx, ox = e.read_x(), om.x()
+            assert np.array_equal(gx.view(np.uint32), ox.view(np.uint32)), \
+                f"pos {p}: residual differs in {np.sum(gx != ox)} elements"
+            diff = np.sum(got.view(np.uint32) != ref_logits.view(np.uint32))
+            assert diff == 0, f"pos {p}: {diff} logits differ, max {np.max(np.abs(got - ref_logits))}"
+            assert e.last_argmax == want_tok
+            tok = want_tok
+    finally:
+        e.close()
+        om.close()
+
+
 def test_kv_rows_written_at_pos(engine, oracle):
     k, v = engine.read_kv(3, 5)
     assert np.all(np.isfinite(k)) and np.any(k != 0) and np.any(v != 0)

@@ -196,14 +196,16 @@ def test_op_argument_errors(cuda):
         E.gemv_q8k(14, t.data_ptr(), t.data_ptr(), t.data_ptr(), 4, 256)   # Q6_K rows must be 16-byte multiples
 
 
-@pytest.mark.parametrize("pos", [0, 1, 31, 32, 100, 2047, 2048, 5000])
+@pytest.mark.parametrize("pos", [0, 1, 31, 32, 100, 2047, 2048, 5000, 8200, 12000, 16383])
 def test_attention_exact(cuda, oracle, pos):
     """Split-KV GQA attention (execute_attention) against the restatement, including the
-    K/V append at pos and the ties-to-even Q8_K of the output (the o_proj input)."""
+    K/V append at pos and the ties-to-even Q8_K of the output (the o_proj input).  Chunk
+    lengths 32 .. 256 (160-row staging: one round up to 10240 positions, two beyond), 1 .. 64
+    chunks."""
     import ctypes as C
     import oracle as O
     from mcpm import engine as E
-    max_seq = 6000
+    max_seq = max(6000, pos + 1)
     rng = np.random.default_rng(pos + 1)
     q = (rng.normal(0, 3, 2048)).astype(np.float32)
     k = (rng.normal(0, 3, 256)).astype(np.float32)
