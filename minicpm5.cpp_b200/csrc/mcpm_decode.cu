@@ -667,18 +667,20 @@ __device__ void attention_unit32(const DecodeParams& p, const Smem& s, int l, in
 }
 
 // One attention unit of a chunk longer than 32 positions (contexts above 2048): the 8 query
-// heads of KV head g against positions [t0, t0+np), np <= 256.  K rows stream into shared
-// memory with cp.async, up to ATT_BIG_ROWS rows per round trip, then V rows through the same
-// buffer.
+// heads of KV head g against positions [t0, t0+np), np <= 256.  Cached K rows stream into
+// shared memory with cp.async, up to ATT_BIG_ROWS rows per round trip, while q and this
+// launch's K/V rows are polled from their epoch-tagged copies (no grid barrier after the QKV
+// phase); then the V rows through the same buffer.
 // Warp w: head pair w&3 (q in registers), positions (w>>2)*4 + group + 16i; lane j of an
 // 8-lane group owns dims 4j + 32i + c of each dot (the canonical 8-lane split).  Same
-// numerics as attention_unit32.  q is final here: a grid barrier follows the QKV phase.
+// numerics as attention_unit32.
 constexpr int ATT_BIG_ROWS = 160;   // one round trip per chunk up to 10240 positions (chunk 160)
-// q, K/V rows, scores, stat
-static_assert((8 * HEAD_DIM + ATT_BIG_ROWS * HEAD_DIM + 8 * ATT_SC_STRIDE + 16) * sizeof(float) <= WBUF_BYTES,
+// q, K/V rows, scores, stat, this launch's K and V rows
+static_assert((8 * HEAD_DIM + ATT_BIG_ROWS * HEAD_DIM + 8 * ATT_SC_STRIDE + 16 + 2 * HEAD_DIM) * sizeof(float) <=
+                  WBUF_BYTES,
               "attention scratch exceeds weight buffer 0");
-// combine_pair: chunk o vectors of two heads, weights, chunk sums, 1/L, output
-static_assert((2 * ATT_MAX_CHUNKS * HEAD_DIM + 4 * ATT_MAX_CHUNKS + 4 + 256) * sizeof(float) <= WBUF_BYTES,
+// combine_pair: chunk o vectors of two heads, maxima, sums, weights, 1/L, output
+static_assert((2 * ATT_MAX_CHUNKS * HEAD_DIM + 6 * ATT_MAX_CHUNKS + 4 + 256) * sizeof(float) <= WBUF_BYTES,
               "combine scratch exceeds weight buffer 0");
 __device__ void attention_unit_big(const DecodeParams& p, const Smem& s, int l, int g, int c, int t0, int np,
                                    unsigned seq) {
@@ -687,16 +689,51 @@ __device__ void attention_unit_big(const DecodeParams& p, const Smem& s, int l, 
     float* kv = qh + 8 * HEAD_DIM;                      // [ATT_BIG_ROWS][128] K, then V rows
     float* sc = kv + ATT_BIG_ROWS * HEAD_DIM;           // [8][ATT_SC_STRIDE] scores -> probabilities
     float* stat = sc + 8 * ATT_SC_STRIDE;               // m[8], l[8]
+    float* krow = stat + 16;                            // [128] K row at pos (epoch path)
+    float* vrow = krow + HEAD_DIM;                      // [128] V row at pos (epoch path)
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(HEAD_DIM)));
     const float* kl = p.kc + static_cast<size_t>(l) * p.max_seq * KV_DIM + g * HEAD_DIM;
     const float* vl = p.vc + static_cast<size_t>(l) * p.max_seq * KV_DIM + g * HEAD_DIM;
-    if (tid < 256) reinterpret_cast<float4*>(qh)[tid] = ld_cg_f4(p.q + 8 * g * HEAD_DIM + 4 * tid);
+    const bool epoch_in = p.qll != nullptr;
+    const int cur = epoch_in && t0 + np - 1 == p.pos ? np - 1 : -1;   // chunk row published this launch
+    // Stages the cache rows of [s0, s0+ns) into kv and returns their count; the row
+    // published this launch (the chunk's last) is copied in from krow / vrow instead.
+    auto stage = [&](const float* src, int s0, int ns) {
+        const int nc = cur >= s0 && cur < s0 + ns ? ns - 1 : ns;   // cur is the chunk's last row
+        for (int i = tid; i < nc * 32; i += blockDim.x)
+            cp_async16(kv + 4 * i, src + static_cast<size_t>(t0 + s0 + (i >> 5)) * KV_DIM + 4 * (i & 31));
+        cp_async_commit();
+        return nc;
+    };
     const int hp = warp & 3, ps = warp >> 2;
     for (int s0 = 0; s0 < np; s0 += ATT_BIG_ROWS) {   // scores
         const int ns = min(ATT_BIG_ROWS, np - s0);
-        for (int i = tid; i < ns * 32; i += blockDim.x)
-            cp_async16(kv + 4 * i, kl + static_cast<size_t>(t0 + s0 + (i >> 5)) * KV_DIM + 4 * (i & 31));
-        cp_async_commit();
+        const int nc = stage(kl, s0, ns);
+        if (s0 == 0) {   // q of the group (and this launch's K/V rows) while the cache rows load
+            bool ok = true;
+            if (epoch_in) {
+                const unsigned ep = qkv_epoch(seq, l);
+                float4 v;
+                if (tid < 256) {
+                    ok = load4_epoch(p.qll + 8 * g * HEAD_DIM + 4 * tid, ep, v, p.err);
+                    reinterpret_cast<float4*>(qh)[tid] = v;
+                } else if (cur >= 0 && tid < 256 + 32) {
+                    ok = load4_epoch(p.qll + N_EMBD + g * HEAD_DIM + 4 * (tid - 256), ep, v, p.err);
+                    reinterpret_cast<float4*>(krow)[tid - 256] = v;
+                } else if (cur >= 0 && tid < 256 + 64) {
+                    ok = load4_epoch(p.qll + N_EMBD + KV_DIM + g * HEAD_DIM + 4 * (tid - 288), ep, v, p.err);
+                    reinterpret_cast<float4*>(vrow)[tid - 288] = v;
+                }
+            } else if (tid < 256) {
+                reinterpret_cast<float4*>(qh)[tid] = ld_cg_f4(p.q + 8 * g * HEAD_DIM + 4 * tid);
+            }
+            if (__syncthreads_or(!ok)) {
+                cp_async_wait_all();
+                return;   // ERR_TIMEOUT is set; every waiter downstream times out too
+            }
+            trace_mark(p, 3 + 2 * (5 * l));   // inputs of this unit published
+        }
+        if (nc < ns && tid < 32) reinterpret_cast<float4*>(kv + nc * HEAD_DIM)[tid] = reinterpret_cast<float4*>(krow)[tid];
         cp_async_wait_all();
         __syncthreads();
         if (s0 == 0) trace_step(p, l, 1, 4);
@@ -751,15 +788,24 @@ __device__ void attention_unit_big(const DecodeParams& p, const Smem& s, int l, 
         __syncthreads();   // kv is overwritten next
     }
     trace_step(p, l, 1, 1);
-    if (warp < 8) {   // chunk max, probabilities, canonical chunk sum (warp = head)
+    if (warp < 8) {   // chunk max, probabilities, canonical chunk sum (warp = head); np <= 256
+        float* sh = sc + warp * ATT_SC_STRIDE;
+        float x[ATT_SC_STRIDE / 32];
         float m = -__int_as_float(0x7f800000);
-        for (int t = lane; t < np; t += 32) m = fmaxf(m, sc[warp * ATT_SC_STRIDE + t]);
+#pragma unroll
+        for (int k = 0; k < ATT_SC_STRIDE / 32; ++k) {
+            x[k] = lane + 32 * k < np ? sh[lane + 32 * k] : 0.0f;
+            if (lane + 32 * k < np) m = fmaxf(m, x[k]);
+        }
         for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        float sum = 0.0f;
-        for (int t = lane; t < np; t += 32) {
-            const float e = canon_expf(__fsub_rn(sc[warp * ATT_SC_STRIDE + t], m));
-            sc[warp * ATT_SC_STRIDE + t] = e;
-            sum = __fadd_rn(sum, e);
+        float sum = 0.0f;   // lane sum over t = lane (mod 32) in position order
+#pragma unroll
+        for (int k = 0; k < ATT_SC_STRIDE / 32; ++k) {
+            if (lane + 32 * k < np) {
+                const float e = canon_expf(__fsub_rn(x[k], m));
+                sh[lane + 32 * k] = e;
+                sum = __fadd_rn(sum, e);
+            }
         }
 #pragma unroll
         for (int o = 16; o >= 1; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
@@ -772,9 +818,8 @@ __device__ void attention_unit_big(const DecodeParams& p, const Smem& s, int l, 
     trace_step(p, l, 1, 8);
     for (int s0 = 0; s0 < np; s0 += ATT_BIG_ROWS) {
         const int ns = min(ATT_BIG_ROWS, np - s0);
-        for (int i = tid; i < ns * 32; i += blockDim.x)
-            cp_async16(kv + 4 * i, vl + static_cast<size_t>(t0 + s0 + (i >> 5)) * KV_DIM + 4 * (i & 31));
-        cp_async_commit();
+        const int nc = stage(vl, s0, ns);
+        if (nc < ns && tid < 32) reinterpret_cast<float4*>(kv + nc * HEAD_DIM)[tid] = reinterpret_cast<float4*>(vrow)[tid];
         cp_async_wait_all();
         __syncthreads();   // V rows, and (first round) the probabilities
         if (s0 == 0) trace_step(p, l, 1, 9);
@@ -782,6 +827,7 @@ __device__ void attention_unit_big(const DecodeParams& p, const Smem& s, int l, 
             const float* pr = sc + 4 * hq * ATT_SC_STRIDE + s0;
             const float* vr = kv + 2 * dp;
             int tt = 0;
+#pragma unroll 2
             for (; tt + 4 <= ns; tt += 4) {
                 float4 pw[4];
                 float2 v[4];
@@ -842,52 +888,55 @@ __device__ bool combine_pair(const DecodeParams& p, const Smem& s, int l, int b,
     const int n = p.pos + 1, C = attn_chunks(n);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const unsigned e = att_epoch(seq, l);
-    float* po = reinterpret_cast<float*>(s.wbuf(0));   // [2][C][128] chunk o vectors
-    float* wts = po + 2 * ATT_MAX_CHUNKS * HEAD_DIM;    // [2][ATT_MAX_CHUNKS]
-    float* lsm = wts + 2 * ATT_MAX_CHUNKS;              // [2][ATT_MAX_CHUNKS]
-    float* inv = lsm + 2 * ATT_MAX_CHUNKS;              // [2] (+2 pad)
+    float* po = reinterpret_cast<float*>(s.wbuf(0));   // [2][ATT_MAX_CHUNKS][128] chunk o vectors
+    float* msm = po + 2 * ATT_MAX_CHUNKS * HEAD_DIM;    // [2][ATT_MAX_CHUNKS] chunk maxima
+    float* lsm = msm + 2 * ATT_MAX_CHUNKS;              // [2][ATT_MAX_CHUNKS] chunk sums
+    float* wts = lsm + 2 * ATT_MAX_CHUNKS;              // [2][ATT_MAX_CHUNKS] exp(m_c - M)
+    float* inv = wts + 2 * ATT_MAX_CHUNKS;              // [2] (+2 pad)
     float* ab = inv + 4;                                // [256]
     if (p.trace && l == 1 && tid == 0 && (b & 3) == 0) p.trace[2870 + 4 * (b >> 2)] = globaltimer();
+    // one thread per (head, chunk) header, then the o vectors in one round trip
     bool ok = true;
-    if (warp < 2) {   // warp = head of the pair; lanes own chunks lane, lane + 32
-        const int h = 2 * b + warp;
-        float m0 = -__int_as_float(0x7f800000), m1 = m0, l0 = 0.0f, l1 = 0.0f;
-        if (lane < C) ok = load2_epoch(att_header(p, h, lane), e, m0, l0, p.err);
-        if (ok && lane + 32 < C) ok = load2_epoch(att_header(p, h, lane + 32), e, m1, l1, p.err);
-        float M = fmaxf(m0, m1);
-        for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-        if (lane < C) {
-            wts[warp * ATT_MAX_CHUNKS + lane] = canon_expf(__fsub_rn(m0, M));
-            lsm[warp * ATT_MAX_CHUNKS + lane] = l0;
-        }
-        if (lane + 32 < C) {
-            wts[warp * ATT_MAX_CHUNKS + lane + 32] = canon_expf(__fsub_rn(m1, M));
-            lsm[warp * ATT_MAX_CHUNKS + lane + 32] = l1;
-        }
-        __syncwarp();
-        if (lane == 0) {   // chunk-ordered fma chain
-            float Ls = 0.0f;
-            for (int c = 0; c < C; ++c) Ls = __fmaf_rn(wts[warp * ATT_MAX_CHUNKS + c], lsm[warp * ATT_MAX_CHUNKS + c], Ls);
-            inv[warp] = __fdiv_rn(1.0f, Ls);
-        }
-        __threadfence();   // headers seen before the o vectors are read
+    if (tid < 2 * C) {
+        const int hh = tid & 1, c = tid >> 1;
+        float m = 0.0f, lv = 0.0f;
+        ok = load2_epoch(att_header(p, 2 * b + hh, c), e, m, lv, p.err);
+        msm[hh * ATT_MAX_CHUNKS + c] = m;
+        lsm[hh * ATT_MAX_CHUNKS + c] = lv;
+        fence_acq_rel_gpu();   // the header is seen before its o vector is read
     }
     if (!__syncthreads_and(ok)) return false;
-    if (p.trace && l == 1 && tid == 0 && (b & 3) == 0) p.trace[2871 + 4 * (b >> 2)] = globaltimer();
     for (int i = tid; i < 2 * C * 32; i += blockDim.x) {
         const int hh = i / (32 * C), r = i - hh * 32 * C, c = r >> 5, f = r & 31;
-        cp_async16(po + (hh * C + c) * HEAD_DIM + 4 * f,
+        cp_async16(po + (hh * ATT_MAX_CHUNKS + c) * HEAD_DIM + 4 * f,
                    p.att_part + (static_cast<size_t>(2 * b + hh) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE + ATT_PART_O +
                        4 * f);
     }
     cp_async_commit();
     cp_async_wait_all();
     __syncthreads();
+    if (p.trace && l == 1 && tid == 0 && (b & 3) == 0) p.trace[2871 + 4 * (b >> 2)] = globaltimer();
+    if (warp < 2) {   // warp = head of the pair: M, w_c, and the chunk-ordered L chain
+        const float* mh = msm + warp * ATT_MAX_CHUNKS;
+        float m0 = lane < C ? mh[lane] : -__int_as_float(0x7f800000);
+        const float m1 = lane + 32 < C ? mh[lane + 32] : -__int_as_float(0x7f800000);
+        float M = fmaxf(m0, m1);
+        for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        if (lane < C) wts[warp * ATT_MAX_CHUNKS + lane] = canon_expf(__fsub_rn(m0, M));
+        if (lane + 32 < C) wts[warp * ATT_MAX_CHUNKS + lane + 32] = canon_expf(__fsub_rn(m1, M));
+        __syncwarp();
+        if (lane == 0) {
+            float Ls = 0.0f;
+            for (int c = 0; c < C; ++c) Ls = __fmaf_rn(wts[warp * ATT_MAX_CHUNKS + c], lsm[warp * ATT_MAX_CHUNKS + c], Ls);
+            inv[warp] = __fdiv_rn(1.0f, Ls);
+        }
+    }
+    __syncthreads();
     if (p.trace && l == 1 && tid == 0 && (b & 3) == 0) p.trace[2872 + 4 * (b >> 2)] = globaltimer();
     if (tid < 2 * HEAD_DIM) {
         const int hh = tid >> 7, dd = tid & 127;
         const float* w = wts + hh * ATT_MAX_CHUNKS;
-        const float* o = po + hh * C * HEAD_DIM + dd;
+        const float* o = po + hh * ATT_MAX_CHUNKS * HEAD_DIM + dd;
         float O = 0.0f;
         int c = 0;
         for (; c + 4 <= C; c += 4) {
@@ -1000,10 +1049,8 @@ __device__ bool load_att_epoch(const DecodeParams& p, const Smem& s, unsigned ep
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     bool ok = true;
     if (warp < N_EMBD / 256) {
-        const unsigned long long* src = p.attw + 256 * warp + 8 * lane;
-        float4 a, b;
-        ok = load4_epoch(src, epoch, a, p.err) && load4_epoch(src + 4, epoch, b, p.err);
-        const float y[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        float y[8];
+        ok = load8c_epoch(p.attw + 256 * warp + 8 * lane, epoch, y, p.err);
         quant_block_warp<false>(y, s.xq()->qs[warp], &s.xq()->d[warp], s.xq()->bsums[warp]);
     }
     return __syncthreads_and(ok);
@@ -1228,18 +1275,14 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
     __syncthreads();
     trace_mark(p, 0);
     const LmPlan lmq = lm_plan(p, cta, ncta);
-    const bool att32 = 32 * ((p.pos + 1 + 2047) / 2048) == 32;   // chunk length (uniform over CTAs)
     const bool flagged = att_flagged(p);
     // Weight phase w+1 is issued while waiting at the barrier in front of phase w: its
     // buffer was last used by phase w-1, which every thread of this CTA has finished.
     for (int l = 0; l < p.n_layer; ++l) {
         if (!phase_qkv(p, s, l, token, cta, ncta, seq)) return;
-        if (att32) {   // 32-position units wait on q/K/V epochs themselves: no barrier
-            trace_mark(p, 2 + 2 * (5 * l));
-            if (threadIdx.x == 0) issue_weight_phase(p, s, 4 * l + 1, cta, ncta);
-        } else if (!traced_barrier(p, bs, 5 * l, [&] { issue_weight_phase(p, s, 4 * l + 1, cta, ncta); })) {
-            return;
-        }
+        // attention units wait on the q/K/V epochs themselves: no grid barrier
+        trace_mark(p, 2 + 2 * (5 * l));
+        if (threadIdx.x == 0) issue_weight_phase(p, s, 4 * l + 1, cta, ncta);
         if (!phase_attention(p, s, l, cta, ncta, seq)) return;
         if (flagged) {   // no grid barrier: o_proj waits for the combiners' epoch-tagged values
             __syncthreads();   // buffer 0 (attention scratch) is free once this CTA's units are done

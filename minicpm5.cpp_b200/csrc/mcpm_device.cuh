@@ -166,6 +166,39 @@ __device__ __forceinline__ bool load2_epoch(const unsigned long long* src, unsig
     b = __uint_as_float(static_cast<unsigned>(w.y));
     return true;
 }
+// Eight consecutive epoch-tagged values (16-byte aligned), polled until all carry `epoch`.
+__device__ __forceinline__ bool load8c_epoch(const unsigned long long* src, unsigned epoch, float (&y)[8],
+                                             unsigned* err) {
+    ulonglong2 w[4];
+    auto pending = [&]() {
+        unsigned m = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            m |= static_cast<unsigned>((w[i].x >> 32) != epoch) | static_cast<unsigned>((w[i].y >> 32) != epoch);
+        return m != 0;
+    };
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = ld_epoch2(src + 2 * i);
+    if (pending()) {
+        const uint64_t t0 = globaltimer();
+        do {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) w[i] = ld_epoch2(src + 2 * i);
+            if (pending() && globaltimer() - t0 > 1000000000ull) {
+                if (err) atomicOr(err, ERR_TIMEOUT);
+                return false;
+            }
+        } while (pending());
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        y[2 * i] = __uint_as_float(static_cast<unsigned>(w[i].x));
+        y[2 * i + 1] = __uint_as_float(static_cast<unsigned>(w[i].y));
+    }
+    return true;
+}
+// Acquire side of a flag handshake: loads after it see what the flag's writer published.
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 __device__ __forceinline__ uint32_t ld_acquire_u32(const unsigned* p) {
     uint32_t v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
