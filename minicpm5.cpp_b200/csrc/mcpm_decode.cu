@@ -381,7 +381,7 @@ __device__ bool norm_quant(const DecodeParams& p, const float* x, unsigned epoch
     if (tid < 256) {
         float xv[8];
         if (SRC == X_EPOCH) {
-            ok = load8_epoch(p.xll, epoch, tid, xv, p.err);
+            ok = load8_epoch(p.xll + (blockIdx.x % XLL_COPIES) * N_EMBD, epoch, tid, xv, p.err);
 #pragma unroll
             for (int i = 0; i < 8; ++i) s.xs()[tid + 256 * i] = xv[i];
         } else {
@@ -512,6 +512,29 @@ __device__ __forceinline__ bool att_flagged(const DecodeParams& p) {
     return p.attw != nullptr && attn_chunks(p.pos + 1) > DIST_COMBINE_MAX;
 }
 
+// Unit tail: the (m, l) headers of the chunk's 8 heads (stat[0..7] maxima, stat[8..15]
+// sums), after every o value of the chunk.  Called by all threads after their o stores.
+// Without a grid barrier to follow (combiners poll), the headers wait for a CTA barrier and
+// a fence; with one they are stored right away.
+__device__ __forceinline__ void publish_headers(const DecodeParams& p, const float* stat, int g, int c, int l,
+                                                unsigned seq, bool flagged) {
+    const int tid = threadIdx.x;
+    if (flagged) __syncthreads();
+    if (tid < 8) {
+        unsigned long long* hdr = att_header(p, 8 * g + tid, c);
+        const unsigned long long e = static_cast<unsigned long long>(att_epoch(seq, l)) << 32;
+        if (flagged) {
+            __threadfence();
+            st_epoch(hdr, stat[tid], static_cast<unsigned>(e >> 32));
+            st_epoch(hdr + 1, stat[8 + tid], static_cast<unsigned>(e >> 32));
+        } else {   // a grid barrier orders them: plain stores
+            __stcg(reinterpret_cast<ulonglong2*>(hdr),
+                   make_ulonglong2(e | __float_as_uint(stat[tid]), e | __float_as_uint(stat[8 + tid])));
+        }
+    }
+    if (!flagged) __syncthreads();
+}
+
 // One attention unit of at most 32 positions (chunk length P = 32, contexts up to 2048):
 // the 8 query heads of KV head g against positions [t0, t0+np).  q and K go straight from
 // L2 into registers (one round trip), V streams into shared memory meanwhile (cp.async).
@@ -523,7 +546,7 @@ __device__ __forceinline__ bool att_flagged(const DecodeParams& p) {
 // In the decode kernel (p.qll set) q and this position's K/V rows are read from their
 // epoch-tagged copies, so no grid barrier separates the QKV phase from attention.
 __device__ void attention_unit32(const DecodeParams& p, const Smem& s, int l, int g, int c, int t0, int np,
-                                 unsigned seq) {
+                                 unsigned seq, bool flagged) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, j = lane & 7, G = lane >> 3;
     float* vb = reinterpret_cast<float*>(s.wbuf(0));   // [32][128] V rows of the chunk
     float* sc = vb + 32 * HEAD_DIM;                     // [8][32] scores -> probabilities
@@ -655,14 +678,7 @@ __device__ void attention_unit32(const DecodeParams& p, const Smem& s, int l, in
     float* pa1 = p.att_part + (static_cast<size_t>(8 * g + h1) * ATT_MAX_CHUNKS + c) * ATT_PART_STRIDE;
     __stcg(pa0 + ATT_PART_O + dd, acc0);
     __stcg(pa1 + ATT_PART_O + dd, acc1);
-    __syncthreads();   // every o value of the chunk is stored (program order), then the headers
-    if (tid < 8) {
-        if (att_flagged(p)) __threadfence();   // combiners poll the headers (no grid barrier)
-        unsigned long long* hdr = att_header(p, 8 * g + tid, c);
-        const unsigned e = att_epoch(seq, l);
-        st_epoch(hdr, stat[tid], e);
-        st_epoch(hdr + 1, stat[8 + tid], e);
-    }
+    publish_headers(p, stat, g, c, l, seq, flagged);
     trace_step(p, l, 1, 2);
 }
 
@@ -683,7 +699,7 @@ static_assert((8 * HEAD_DIM + ATT_BIG_ROWS * HEAD_DIM + 8 * ATT_SC_STRIDE + 16 +
 static_assert((2 * ATT_MAX_CHUNKS * HEAD_DIM + 6 * ATT_MAX_CHUNKS + 4 + 256) * sizeof(float) <= WBUF_BYTES,
               "combine scratch exceeds weight buffer 0");
 __device__ void attention_unit_big(const DecodeParams& p, const Smem& s, int l, int g, int c, int t0, int np,
-                                   unsigned seq) {
+                                   unsigned seq, bool flagged) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, j = lane & 7, G = lane >> 3;
     float* qh = reinterpret_cast<float*>(s.wbuf(0));   // [8][128]
     float* kv = qh + 8 * HEAD_DIM;                      // [ATT_BIG_ROWS][128] K, then V rows
@@ -866,14 +882,7 @@ __device__ void attention_unit_big(const DecodeParams& p, const Smem& s, int l, 
             __stcg(reinterpret_cast<float2*>(pa), make_float2(acc[h][0], acc[h][1]));
         }
     }
-    __syncthreads();   // every o value of the chunk is stored (program order), then the headers
-    if (tid < 8) {
-        if (att_flagged(p)) __threadfence();   // combiners poll the headers (no grid barrier)
-        unsigned long long* hdr = att_header(p, 8 * g + tid, c);
-        const unsigned e = att_epoch(seq, l);
-        st_epoch(hdr, stat[tid], e);
-        st_epoch(hdr + 1, stat[8 + tid], e);
-    }
+    publish_headers(p, stat, g, c, l, seq, flagged);
     trace_step(p, l, 1, 2);
 }
 
@@ -894,7 +903,7 @@ __device__ bool combine_pair(const DecodeParams& p, const Smem& s, int l, int b,
     float* wts = lsm + 2 * ATT_MAX_CHUNKS;              // [2][ATT_MAX_CHUNKS] exp(m_c - M)
     float* inv = wts + 2 * ATT_MAX_CHUNKS;              // [2] (+2 pad)
     float* ab = inv + 4;                                // [256]
-    if (p.trace && l == 1 && tid == 0 && (b & 3) == 0) p.trace[2870 + 4 * (b >> 2)] = globaltimer();
+    if (p.trace && l == 1 && tid == 0) p.trace[2880 + 4 * b + 0] = globaltimer();
     // one thread per (head, chunk) header, then the o vectors in one round trip
     bool ok = true;
     if (tid < 2 * C) {
@@ -915,46 +924,51 @@ __device__ bool combine_pair(const DecodeParams& p, const Smem& s, int l, int b,
     cp_async_commit();
     cp_async_wait_all();
     __syncthreads();
-    if (p.trace && l == 1 && tid == 0 && (b & 3) == 0) p.trace[2871 + 4 * (b >> 2)] = globaltimer();
+    if (p.trace && l == 1 && tid == 0) p.trace[2880 + 4 * b + 1] = globaltimer();
+    const bool tr0 = p.trace && l == 1 && b == 0 && tid == 0;
+    if (tr0) p.trace[2940] = clock64(), p.trace[2941] = globaltimer();
     if (warp < 2) {   // warp = head of the pair: M, w_c, and the chunk-ordered L chain
         const float* mh = msm + warp * ATT_MAX_CHUNKS;
         float m0 = lane < C ? mh[lane] : -__int_as_float(0x7f800000);
         const float m1 = lane + 32 < C ? mh[lane + 32] : -__int_as_float(0x7f800000);
         float M = fmaxf(m0, m1);
         for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        if (tr0) p.trace[2942] = clock64();
         if (lane < C) wts[warp * ATT_MAX_CHUNKS + lane] = canon_expf(__fsub_rn(m0, M));
         if (lane + 32 < C) wts[warp * ATT_MAX_CHUNKS + lane + 32] = canon_expf(__fsub_rn(m1, M));
         __syncwarp();
-        if (lane == 0) {
+        if (tr0) p.trace[2943] = clock64();
+        if (lane == 0) {   // chunk-ordered chain; loads hoisted (fixed trip count, predicated)
+            const float* wh = wts + warp * ATT_MAX_CHUNKS;
+            const float* lh = lsm + warp * ATT_MAX_CHUNKS;
             float Ls = 0.0f;
-            for (int c = 0; c < C; ++c) Ls = __fmaf_rn(wts[warp * ATT_MAX_CHUNKS + c], lsm[warp * ATT_MAX_CHUNKS + c], Ls);
+#pragma unroll 16
+            for (int c = 0; c < ATT_MAX_CHUNKS; ++c)
+                if (c < C) Ls = __fmaf_rn(wh[c], lh[c], Ls);
             inv[warp] = __fdiv_rn(1.0f, Ls);
         }
+        if (tr0) p.trace[2944] = clock64();
     }
     __syncthreads();
-    if (p.trace && l == 1 && tid == 0 && (b & 3) == 0) p.trace[2872 + 4 * (b >> 2)] = globaltimer();
+    if (tr0) p.trace[2945] = clock64(), p.trace[2946] = globaltimer();
+    if (p.trace && l == 1 && tid == 0) p.trace[2880 + 4 * b + 2] = globaltimer();
     if (tid < 2 * HEAD_DIM) {
         const int hh = tid >> 7, dd = tid & 127;
         const float* w = wts + hh * ATT_MAX_CHUNKS;
         const float* o = po + hh * ATT_MAX_CHUNKS * HEAD_DIM + dd;
-        float O = 0.0f;
-        int c = 0;
-        for (; c + 4 <= C; c += 4) {
-            const float4 w4 = *reinterpret_cast<const float4*>(w + c);
-            float v[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) v[k] = o[(c + k) * HEAD_DIM];
-            O = __fmaf_rn(w4.x, v[0], O);
-            O = __fmaf_rn(w4.y, v[1], O);
-            O = __fmaf_rn(w4.z, v[2], O);
-            O = __fmaf_rn(w4.w, v[3], O);
-        }
-        for (; c < C; ++c) O = __fmaf_rn(w[c], o[c * HEAD_DIM], O);
+        float O = 0.0f;   // chunk-ordered chain; loads hoisted (fixed trip count, predicated)
+#pragma unroll 16
+        for (int c = 0; c < ATT_MAX_CHUNKS; ++c)
+            if (c < C) O = __fmaf_rn(w[c], o[c * HEAD_DIM], O);
         const float out = __fmul_rn(O, inv[hh]);
         ab[tid] = out;
-        if (p.attw) st_epoch(p.attw + 256 * b + tid, out, e);
+        if (p.attw) {   // one copy per group of polling CTAs (fewer pollers per L2 line)
+#pragma unroll
+            for (int r = 0; r < ATTW_COPIES; ++r) st_epoch(p.attw + r * N_EMBD + 256 * b + tid, out, e);
+        }
         p.att[256 * b + tid] = out;
     }
+    if (p.trace && l == 1 && tid == 0) p.trace[2912 + b] = globaltimer();   // published (thread 0's value)
     __syncthreads();
     if (warp == 0) {   // Q8_K block b, ties-to-even (quantize_row_q8_K_avx2)
         float y[8];
@@ -964,7 +978,7 @@ __device__ bool combine_pair(const DecodeParams& p, const Smem& s, int l, int b,
         quant_block_warp<false>(y, reinterpret_cast<int8_t*>(blk + 4), reinterpret_cast<float*>(blk),
                                 reinterpret_cast<int16_t*>(blk + 260));
     }
-    if (p.trace && l == 1 && tid == 0 && (b & 3) == 0) p.trace[2873 + 4 * (b >> 2)] = globaltimer();
+    if (p.trace && l == 1 && tid == 0) p.trace[2880 + 4 * b + 3] = globaltimer();
     __syncthreads();   // po / ab reused by the caller
     return true;
 }
@@ -977,16 +991,17 @@ __device__ bool phase_attention(const DecodeParams& p, const Smem& s, int l, int
     const int n = p.pos + 1;
     const int P = 32 * ((n + 2047) / 2048);
     const int C = (n + P - 1) / P;
+    const bool flagged = C > DIST_COMBINE_MAX && p.attw != nullptr;   // att_flagged(p)
     for (int item = cta; item < 2 * C; item += ncta) {
         const int g = item / C, c = item % C;
         const int t0 = c * P, t1 = min(t0 + P, n), np = t1 - t0;
         __syncthreads();
         if (P == 32)
-            attention_unit32(p, s, l, g, c, t0, np, seq);
+            attention_unit32(p, s, l, g, c, t0, np, seq, flagged);
         else
-            attention_unit_big(p, s, l, g, c, t0, np, seq);
+            attention_unit_big(p, s, l, g, c, t0, np, seq, flagged);
     }
-    if (C > DIST_COMBINE_MAX && p.attw) {
+    if (flagged) {
         for (int b = ncta - 1 - cta; b < N_EMBD / 256; b += ncta) {
             __syncthreads();
             if (!combine_pair(p, s, l, b, seq)) return false;
@@ -995,17 +1010,20 @@ __device__ bool phase_attention(const DecodeParams& p, const Smem& s, int l, int
     return true;
 }
 
-// Every CTA combines the attention chunks of all 16 heads (same operations and order as
-// the last-CTA combine) and quantises the result ties-to-even straight into s.xq().
-__device__ bool combine_attention(const DecodeParams& p, const Smem& s, int l, int cta, unsigned seq) {
+// Up to DIST_COMBINE_MAX chunks: every CTA combines the attention chunks of all 16 heads
+// (same operations and order as combine_pair) and quantises the result ties-to-even
+// straight into s.xq().
+__device__ void combine_attention(const DecodeParams& p, const Smem& s, int l, int cta) {
     // warp = head h, lane = dims 4*lane .. 4*lane+3: the chunk weights of a head never leave
     // its warp, so loads, max, exp, the L chain and the O chains run without a CTA barrier.
     const int n = p.pos + 1, C = attn_chunks(n);
     const int tid = threadIdx.x, lane = tid & 31, h = tid >> 5;
     float* ab = s.xs();   // [2048]
     const float* ph = p.att_part + static_cast<size_t>(h) * ATT_MAX_CHUNKS * ATT_PART_STRIDE;
-    float2 ml = make_float2(0.f, 0.f);   // lane c < C: chunk c's header (m, l), final after the grid barrier
-    const bool ok = lane >= C || load2_epoch(att_header(p, h, lane), att_epoch(seq, l), ml.x, ml.y, p.err);
+    // lane c < C: chunk c's header (m, l), final after the grid barrier: plain loads issued
+    // with the o vectors (one round trip)
+    const float2 ml = lane < C ? make_float2(ph[lane * ATT_PART_STRIDE], ph[lane * ATT_PART_STRIDE + 2])
+                               : make_float2(0.f, 0.f);   // low halves of the two header words
     float4 v[DIST_COMBINE_MAX];
 #pragma unroll
     for (int cc = 0; cc < DIST_COMBINE_MAX; ++cc)
@@ -1039,7 +1057,7 @@ __device__ bool combine_attention(const DecodeParams& p, const Smem& s, int l, i
         const float y[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
         quant_block_warp<false>(y, s.xq()->qs[h], &s.xq()->d[h], s.xq()->bsums[h]);
     }
-    return __syncthreads_and(ok);
+    __syncthreads();
 }
 
 // o_proj input for contexts combined by the head-pair combiners: the 2048 epoch-tagged
@@ -1050,7 +1068,8 @@ __device__ bool load_att_epoch(const DecodeParams& p, const Smem& s, unsigned ep
     bool ok = true;
     if (warp < N_EMBD / 256) {
         float y[8];
-        ok = load8c_epoch(p.attw + 256 * warp + 8 * lane, epoch, y, p.err);
+        ok = load8c_epoch(p.attw + (blockIdx.x % ATTW_COPIES) * N_EMBD + 256 * warp + 8 * lane, epoch, y, p.err);
+        if (p.trace && blockIdx.x == 0 && lane == 0 && epoch == (epoch & ~0xffu) + 1) p.trace[2920 + warp] = globaltimer();
         quant_block_warp<false>(y, s.xq()->qs[warp], &s.xq()->d[warp], s.xq()->bsums[warp]);
     }
     return __syncthreads_and(ok);
@@ -1062,8 +1081,8 @@ __device__ bool phase_o(const DecodeParams& p, const Smem& s, int l, int cta, in
     const int r0 = pl.row0[0], n = pl.nrows[0];
     const float xr = threadIdx.x < n ? __ldcg(p.x + r0 + threadIdx.x) : 0.0f;   // residual rows, early
     if (attn_chunks(p.pos + 1) <= DIST_COMBINE_MAX) {
-        if (!combine_attention(p, s, l, cta, seq)) return false;
-    } else if (!load_att_epoch(p, s, att_epoch(seq, l))) {
+        combine_attention(p, s, l, cta);
+    } else if (trace_step(p, l, 2, 5), !load_att_epoch(p, s, att_epoch(seq, l))) {
         return false;
     }
     trace_step(p, l, 2, 1);
@@ -1074,7 +1093,8 @@ __device__ bool phase_o(const DecodeParams& p, const Smem& s, int l, int cta, in
     if (threadIdx.x < n) {
         const float xn = __fadd_rn(xr, s.rowval()[threadIdx.x]);
         p.x[r0 + threadIdx.x] = xn;
-        st_epoch(p.xll + r0 + threadIdx.x, xn, x_epoch(seq, 2 * l + 1));
+#pragma unroll
+        for (int r = 0; r < XLL_COPIES; ++r) st_epoch(p.xll + r * N_EMBD + r0 + threadIdx.x, xn, x_epoch(seq, 2 * l + 1));
     }
     trace_cta(p, l, 2, 0);
     // down weights into the buffer just released, by a thread outside warps 0-7 (which
@@ -1142,7 +1162,8 @@ __device__ bool phase_down(const DecodeParams& p, const Smem& s, int l, int cta,
     if (threadIdx.x < n) {
         const float xn = __fadd_rn(xr, s.rowval()[threadIdx.x]);
         p.x[r0 + threadIdx.x] = xn;
-        st_epoch(p.xll + r0 + threadIdx.x, xn, x_epoch(seq, 2 * l + 2));
+#pragma unroll
+        for (int r = 0; r < XLL_COPIES; ++r) st_epoch(p.xll + r * N_EMBD + r0 + threadIdx.x, xn, x_epoch(seq, 2 * l + 2));
     }
     trace_cta(p, l, 4, 0);
     if (threadIdx.x == ISSUE_THREAD) {

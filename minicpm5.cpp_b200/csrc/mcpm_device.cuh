@@ -182,6 +182,7 @@ __device__ __forceinline__ bool load8c_epoch(const unsigned long long* src, unsi
     if (pending()) {
         const uint64_t t0 = globaltimer();
         do {
+            __nanosleep(64);   // back off: many CTAs poll the same lines
 #pragma unroll
             for (int i = 0; i < 4; ++i) w[i] = ld_epoch2(src + 2 * i);
             if (pending() && globaltimer() - t0 > 1000000000ull) {

@@ -169,9 +169,10 @@ bool phases_fit(const mcpm_engine* e, int n, std::string& why) {
 mcpm_status reset_ctl(mcpm_engine* e) {
     MCPM_CUDA(cudaMemsetAsync(e->ctl, 0, CTL_WORDS * sizeof(int), e->stream));
     // the launch sequence restarts, so no epoch of an aborted launch may remain
-    if (e->xll) MCPM_CUDA(cudaMemsetAsync(e->xll, 0, N_EMBD * sizeof(unsigned long long), e->stream));
+    if (e->xll) MCPM_CUDA(cudaMemsetAsync(e->xll, 0, XLL_COPIES * N_EMBD * sizeof(unsigned long long), e->stream));
     if (e->qll) MCPM_CUDA(cudaMemsetAsync(e->qll, 0, (N_EMBD + 2 * KV_DIM) * sizeof(unsigned long long), e->stream));
-    if (e->attw) MCPM_CUDA(cudaMemsetAsync(e->attw, 0, N_EMBD * sizeof(unsigned long long), e->stream));
+    if (e->attw)
+        MCPM_CUDA(cudaMemsetAsync(e->attw, 0, ATTW_COPIES * N_EMBD * sizeof(unsigned long long), e->stream));
     if (e->att_part) MCPM_CUDA(cudaMemsetAsync(e->att_part, 0, ATT_PART_FLOATS * sizeof(float), e->stream));   // headers
     MCPM_CUDA(cudaStreamSynchronize(e->stream));
     return MCPM_OK;
@@ -432,12 +433,12 @@ mcpm_status mcpm_load_gguf(mcpm_engine* e, const char* path) {
     MCPM_CUDA(cudaMalloc(&e->q, N_EMBD * 4));
     MCPM_CUDA(cudaMalloc(&e->att, N_EMBD * 4));
     MCPM_CUDA(cudaMalloc(&e->h, N_FF * 4));
-    MCPM_CUDA(cudaMalloc(&e->xll, N_EMBD * sizeof(unsigned long long)));
-    MCPM_CUDA(cudaMemset(e->xll, 0, N_EMBD * sizeof(unsigned long long)));
+    MCPM_CUDA(cudaMalloc(&e->xll, XLL_COPIES * N_EMBD * sizeof(unsigned long long)));
+    MCPM_CUDA(cudaMemset(e->xll, 0, XLL_COPIES * N_EMBD * sizeof(unsigned long long)));
     MCPM_CUDA(cudaMalloc(&e->qll, (N_EMBD + 2 * KV_DIM) * sizeof(unsigned long long)));
     MCPM_CUDA(cudaMemset(e->qll, 0, (N_EMBD + 2 * KV_DIM) * sizeof(unsigned long long)));
-    MCPM_CUDA(cudaMalloc(&e->attw, N_EMBD * sizeof(unsigned long long)));
-    MCPM_CUDA(cudaMemset(e->attw, 0, N_EMBD * sizeof(unsigned long long)));
+    MCPM_CUDA(cudaMalloc(&e->attw, ATTW_COPIES * N_EMBD * sizeof(unsigned long long)));
+    MCPM_CUDA(cudaMemset(e->attw, 0, ATTW_COPIES * N_EMBD * sizeof(unsigned long long)));
     MCPM_CUDA(cudaMalloc(&e->att_part, ATT_PART_FLOATS * sizeof(float)));
     MCPM_CUDA(cudaMemset(e->att_part, 0, ATT_PART_FLOATS * sizeof(float)));
     MCPM_CUDA(cudaMalloc(&e->logits, sizeof(float) * e->n_vocab));

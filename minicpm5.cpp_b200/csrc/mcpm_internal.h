@@ -22,6 +22,8 @@ constexpr int LM_SLOT_BYTES = WBUF_BYTES;   // LM head: one stage per weight buf
 constexpr int ATT_MAX_CHUNKS = 64;         // attention chunks per head (chunk = 32*ceil(n/2048))
 constexpr int ATT_PART_STRIDE = 4 + HEAD_DIM;   // m, l, 2 pad, o[128]: o 16-byte aligned
 constexpr int ATT_PART_O = 4;
+constexpr int ATTW_COPIES = 8;           // copies of the combined attention: CTA c polls copy c % 8
+constexpr int XLL_COPIES = 1;            // copies of the published residual: CTA c polls copy c % 8
 constexpr int ATT_SC_STRIDE = 256;         // chunk-length bound: 32*ceil(MAX_SEQ/2048)
 constexpr int MAX_SEQ = 16384;
 constexpr int TRACE_WORDS = 3400;         // 2 + 2*(5*layers+1) phase marks, detail marks from 650, per-CTA from 720
@@ -70,11 +72,12 @@ struct DecodeParams {
     float* att;         // attention output [N_EMBD] (fp32, for inspection)
     uint8_t* att_q8k;   // attention output as 8 block_q8_K
     float* h;           // SwiGLU output [N_FF]
-    unsigned long long* xll;   // residual stream published per element as (epoch << 32) | fp32 bits [N_EMBD]
+    unsigned long long* xll;   // residual stream published per element as (epoch << 32) | fp32 bits
+                               // [XLL_COPIES][N_EMBD]
     unsigned long long* qll;   // rotated q [N_EMBD] then this position's K and V rows [2*KV_DIM], same encoding;
                                // null outside the decode kernel (q and the cache are then final)
     float* att_part;    // [N_HEAD][ATT_MAX_CHUNKS][ATT_PART_STRIDE]: epoch-tagged (m, l) header, o[128]
-    unsigned long long* attw;   // combined attention [N_EMBD], epoch-tagged (decode kernel, > 16 chunks)
+    unsigned long long* attw;   // combined attention [ATTW_COPIES][N_EMBD], epoch-tagged (decode kernel, > 16 chunks)
     float* logits;      // [n_vocab]
     float* am_val;      // per-CTA argmax partials
     int* am_idx;
