@@ -74,6 +74,16 @@ mcpm_status mcpm_read_kv(mcpm_engine* e, int layer, int pos, float* k_host, floa
 /* Writes n_pos K and V rows ([n_pos][n_head_kv * head_dim] floats each) of one layer from
  * position pos0: restores a saved cache, or seeds one for a parity check of a late step. */
 mcpm_status mcpm_write_kv(mcpm_engine* e, int layer, int pos0, int n_pos, const float* k_host, const float* v_host);
+/* Batched decode (the reference's forward once per sequence, for n_seq independent
+ * sequences in lockstep).  mcpm_batch_init allocates a KV cache of max_seq positions for
+ * each of n_seq <= 64 sequences (zeroed; positions restart at 0).  mcpm_batch_step_async
+ * advances every sequence by one token on the engine's stream: tokens (host, n_seq ids) or
+ * NULL for each sequence's previous greedy token; pos (host, n_seq) or NULL for the
+ * previous positions + 1.  mcpm_batch_read waits and copies the last step's logits
+ * ([n_seq][n_vocab], optional) and greedy tokens ([n_seq], optional). */
+mcpm_status mcpm_batch_init(mcpm_engine* e, int n_seq, int max_seq);
+mcpm_status mcpm_batch_step_async(mcpm_engine* e, const int* tokens, const int* pos);
+mcpm_status mcpm_batch_read(mcpm_engine* e, float* logits, int* argmax);
 /* n_layer, n_embd, n_ff, n_head, n_head_kv, n_vocab of the loaded model. */
 mcpm_status mcpm_model_dims(mcpm_engine* e, int dims[6]);
 /* Phase trace (no reference counterpart; the reference only times whole loops,

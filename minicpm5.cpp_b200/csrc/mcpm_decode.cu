@@ -18,6 +18,8 @@
 // ERR_TIMEOUT instead of hanging.
 #include "mcpm_device.cuh"
 #include "mcpm_internal.h"
+#include <algorithm>
+#include <initializer_list>
 
 namespace mcpm {
 namespace {
@@ -306,11 +308,11 @@ __device__ bool wait_weights(const DecodeParams& p, const Smem& s, int wp) {
 
 // ------------------------------------------------------------- activation prologues
 // xs <- embedding row of `token` (get_embedding, ops.cpp:631-673; Q4_K rows).
-__device__ void embed_row(const DecodeParams& p, int token, float* xs) {
+__device__ void embed_row(const uint8_t* embd, int token, float* xs) {
     const int tid = threadIdx.x;
     if (tid < 256) {
         const int b = tid >> 5, l = tid & 31;   // block b, elements 8l .. 8l+7
-        const uint8_t* blk = p.embd + (static_cast<size_t>(token) * (N_EMBD / 256) + b) * Q4K_BYTES;
+        const uint8_t* blk = embd + (static_cast<size_t>(token) * (N_EMBD / 256) + b) * Q4K_BYTES;
         const uint32_t w0 = *reinterpret_cast<const uint32_t*>(blk);
         const float d = h2f(w0), dmin = h2f(w0 >> 16);
         const int j = (8 * l) >> 6, i0 = (8 * l) & 63;   // 64-element chunk, offset inside it
@@ -443,7 +445,7 @@ __device__ bool phase_qkv(const DecodeParams& p, const Smem& s, int l, int token
     if (pr0 < (b - a) / 2 && R0 < N_EMBD + KV_DIM)
         cs0 = __ldg(p.rope + static_cast<size_t>(p.pos) * (HEAD_DIM / 2) + ((R0 & (HEAD_DIM - 1)) >> 1));
     if (l == 0) {
-        embed_row(p, token, s.xs());
+        embed_row(p.embd, token, s.xs());
         __syncthreads();
         if (cta == 0)
             for (int i = threadIdx.x; i < N_EMBD; i += blockDim.x) p.x[i] = s.xs()[i];
@@ -499,7 +501,7 @@ __device__ bool phase_qkv(const DecodeParams& p, const Smem& s, int l, int token
 }
 
 // Chunk counts up to DIST_COMBINE_MAX are combined by every CTA in the o_proj prologue
-// (no atomics, no serial combiner); longer contexts use the last-CTA combine below.
+// (no atomics, no serial combiner); longer contexts use the head-pair combiners.
 constexpr int DIST_COMBINE_MAX = 16;
 
 __device__ __forceinline__ int attn_chunks(int n) {
@@ -974,9 +976,13 @@ __device__ bool combine_pair(const DecodeParams& p, const Smem& s, int l, int b,
         float y[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) y[k] = ab[8 * lane + k];
-        uint8_t* blk = p.att_q8k + static_cast<size_t>(b) * Q8K_BYTES;
-        quant_block_warp<false>(y, reinterpret_cast<int8_t*>(blk + 4), reinterpret_cast<float*>(blk),
-                                reinterpret_cast<int16_t*>(blk + 260));
+        if (p.att_qs) {
+            quant_block_warp<false>(y, p.att_qs + 256 * b, p.att_d + b, p.att_bs + 16 * b);
+        } else {
+            uint8_t* blk = p.att_q8k + static_cast<size_t>(b) * Q8K_BYTES;
+            quant_block_warp<false>(y, reinterpret_cast<int8_t*>(blk + 4), reinterpret_cast<float*>(blk),
+                                    reinterpret_cast<int16_t*>(blk + 260));
+        }
     }
     if (p.trace && l == 1 && tid == 0) p.trace[2880 + 4 * b + 3] = globaltimer();
     __syncthreads();   // po / ab reused by the caller
@@ -1363,6 +1369,8 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_att_combine(const DecodePara
     combine_pair(p, s, 0, blockIdx.x, 1u);
 }
 
+#include "mcpm_batch.cuh"
+
 }  // namespace
 
 size_t decode_smem_bytes() { return SM_BYTES; }
@@ -1377,6 +1385,73 @@ int decode_max_ctas_per_sm() {
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_decode, DEC_THREADS, decode_smem_bytes()) != cudaSuccess)
         return 0;
     return n;
+}
+
+// One batched decode step (every sequence one token), as a sequence of stream-ordered
+// launches: per layer QKV GEMM, RoPE + K/V append, attention units, head-pair combine,
+// o_proj GEMM, residual + norm, gate/up GEMM, SwiGLU, down GEMM, residual + norm; then the
+// LM head GEMM and the per-sequence argmax.
+cudaError_t launch_batch_step(const BatchLaunch& b, cudaStream_t stream) {
+    static int prepared_dev = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    constexpr int UNIT_SMEM_BIG = 98304, COMBINE_SMEM = 68608;
+    if (prepared_dev != dev) {
+        cudaError_t e = cudaFuncSetAttribute(k_b_att_units, cudaFuncAttributeMaxDynamicSharedMemorySize, UNIT_SMEM_BIG);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k_b_att_combine, cudaFuncAttributeMaxDynamicSharedMemorySize, COMBINE_SMEM);
+        if (e != cudaSuccess) return e;
+        prepared_dev = dev;
+    }
+    static_assert((2 * ATT_MAX_CHUNKS * HEAD_DIM + 6 * ATT_MAX_CHUNKS + 4 + 256) * 4 <= COMBINE_SMEM, "combine smem");
+    static_assert((8 * HEAD_DIM + ATT_BIG_ROWS * HEAD_DIM + 8 * ATT_SC_STRIDE + 16 + 2 * HEAD_DIM) * 4 <= UNIT_SMEM_BIG,
+                  "unit smem");
+    BStepArgs a{};
+    a.n_seq = b.n_seq, a.max_seq = b.max_seq, a.n_layer = b.n_layer, a.n_vocab = b.n_vocab;
+    a.kc = b.kc, a.vc = b.vc, a.x = b.x, a.y = b.y, a.q = b.q, a.att_part = b.att_part, a.att = b.att;
+    a.logits = b.logits, a.aqs = b.aqs, a.ad = b.ad, a.abs = b.abs;
+    a.tokens = b.tokens, a.pos = b.pos, a.argmax = b.argmax, a.embd = b.embd, a.rope = b.rope, a.err = b.err;
+    const int n = b.n_seq;
+    const int nmax = b.max_pos + 1, Pmax = 32 * ((nmax + 2047) / 2048), Cmax = (nmax + Pmax - 1) / Pmax;
+    const int unit_smem = Pmax == 32 ? 24576 : UNIT_SMEM_BIG;
+    auto gemm = [&](std::initializer_list<BGemmSeg> segs, int nb, float* y, int y_stride) {
+        BGemmArgs g{};
+        int tiles = 0, i = 0;
+        for (BGemmSeg sg : segs) {
+            sg.tile0 = tiles;
+            tiles += (sg.rows + BG_ROWS - 1) / BG_ROWS;
+            g.seg[i++] = sg;
+        }
+        g.nseg = i, g.ntiles = tiles, g.nb = nb;
+        g.aqs = b.aqs, g.ad = b.ad, g.abs = b.abs, g.y = y, g.y_stride = y_stride, g.n_seq = n;
+        k_b_gemm<<<std::min(tiles, 2 * b.n_sm), BG_THREADS, BGS_BYTES, stream>>>(g);
+    };
+    a.norm = b.layers[0].attn_norm;
+    k_b_embed<<<n, 256, 0, stream>>>(a);
+    for (int l = 0; l < b.n_layer; ++l) {
+        const LayerDev& L = b.layers[l];
+        gemm({{L.wq, L.tq, N_EMBD, 0, 0}, {L.wk, L.tk, KV_DIM, N_EMBD, 0}, {L.wv, L.tv, KV_DIM, N_EMBD + KV_DIM, 0}},
+             N_EMBD / 256, b.y, 2 * N_FF);
+        k_b_rope_kv<<<n, 256, 0, stream>>>(a, l);
+        k_b_att_units<<<dim3(n, 2 * Cmax), DEC_THREADS, unit_smem, stream>>>(a, l);
+        k_b_att_combine<<<dim3(n, N_EMBD / 256), DEC_THREADS, COMBINE_SMEM, stream>>>(a, l);
+        gemm({{L.wo, L.to, N_EMBD, 0, 0}}, N_EMBD / 256, b.y, 2 * N_FF);
+        a.norm = L.ffn_norm;
+        k_b_res_norm<true><<<n, 256, 0, stream>>>(a);
+        gemm({{L.wg, L.tg, N_FF, 0, 0}, {L.wu, L.tu, N_FF, N_FF, 0}}, N_EMBD / 256, b.y, 2 * N_FF);
+        k_b_swiglu<<<n, 256, 0, stream>>>(a);
+        gemm({{L.wd, L.td, N_EMBD, 0, 0}}, N_FF / 256, b.y, 2 * N_FF);
+        if (l + 1 < b.n_layer) {
+            a.norm = b.layers[l + 1].attn_norm;
+            k_b_res_norm<true><<<n, 256, 0, stream>>>(a);
+        } else {
+            a.norm = b.out_norm;
+            k_b_res_norm<false><<<n, 256, 0, stream>>>(a);
+        }
+    }
+    gemm({{b.lm, b.lm_type, b.n_vocab, 0, 0}}, N_EMBD / 256, b.logits, b.n_vocab);
+    k_b_argmax<<<n, 1024, 0, stream>>>(a, b.chain);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_decode(const DecodeParams& p, int n_ctas, cudaStream_t stream) {

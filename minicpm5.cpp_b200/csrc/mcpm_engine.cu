@@ -12,6 +12,8 @@
 #include <memory>
 #include <string>
 #include <vector>
+#include <utility>
+#include <initializer_list>
 
 #include "../../include/mcpm.h"
 #include "gguf.h"
@@ -60,6 +62,16 @@ struct mcpm_engine {
     int* ctl = nullptr;       // device control words
     int* ctl_host = nullptr;  // pinned mirror
     unsigned long long* trace = nullptr;   // phase timestamps when tracing is on
+    // batched decode: b_n independent sequences, each with its own KV cache of b_max_seq positions
+    int b_n = 0, b_max_seq = 0;
+    float *b_kc = nullptr, *b_vc = nullptr, *b_x = nullptr, *b_y = nullptr, *b_q = nullptr;
+    float *b_part = nullptr, *b_att = nullptr, *b_logits = nullptr;
+    float2* b_rope = nullptr;
+    int8_t* b_aqs = nullptr;
+    float* b_ad = nullptr;
+    int16_t* b_abs = nullptr;
+    int *b_tokens = nullptr, *b_pos = nullptr, *b_argmax = nullptr;
+    std::vector<int> b_pos_host;   // positions of the next step
 };
 
 namespace {
@@ -88,6 +100,19 @@ void free_kv(mcpm_engine* e) {
     free_dev(e->vc);
     free_dev(e->rope);
     e->max_seq = 0;
+}
+
+void free_batch(mcpm_engine* e) {
+    for (float** b : {&e->b_kc, &e->b_vc, &e->b_x, &e->b_y, &e->b_q, &e->b_part, &e->b_att, &e->b_logits}) free_dev(*b);
+    free_dev(e->b_rope);
+    free_dev(e->b_aqs);
+    free_dev(e->b_ad);
+    free_dev(e->b_abs);
+    free_dev(e->b_tokens);
+    free_dev(e->b_pos);
+    free_dev(e->b_argmax);
+    e->b_n = e->b_max_seq = 0;
+    e->b_pos_host.clear();
 }
 
 void free_model(mcpm_engine* e) {
@@ -571,6 +596,7 @@ void mcpm_engine_destroy(mcpm_engine* e) {
     if (!e) return;
     cudaSetDevice(e->device);
     if (e->stream) cudaStreamSynchronize(e->stream);
+    free_batch(e);
     free_kv(e);
     free_model(e);
     free_dev(e->ctl);
@@ -578,6 +604,90 @@ void mcpm_engine_destroy(mcpm_engine* e) {
     if (e->ctl_host) cudaFreeHost(e->ctl_host);
     if (e->stream) cudaStreamDestroy(e->stream);
     delete e;
+}
+
+// ------------------------------------------------------------------ batched decode
+mcpm_status mcpm_batch_init(mcpm_engine* e, int n_seq, int max_seq) {
+    if (!e || n_seq <= 0 || n_seq > BATCH_MAX || max_seq <= 0 || max_seq > MAX_SEQ) return MCPM_BAD_ARG;
+    if (!e->loaded) return MCPM_NOT_LOADED;
+    MCPM_CUDA(cudaSetDevice(e->device));
+    MCPM_CUDA(cudaStreamSynchronize(e->stream));
+    free_batch(e);
+    const size_t kv = static_cast<size_t>(n_seq) * e->n_layer * max_seq * KV_DIM;
+    auto alloc = [&](auto** ptr, size_t bytes) -> cudaError_t {
+        cudaError_t err = cudaMalloc(reinterpret_cast<void**>(ptr), bytes);
+        if (err == cudaSuccess) err = cudaMemset(*ptr, 0, bytes);
+        return err;
+    };
+    const size_t ns = n_seq;
+    cudaError_t err = cudaSuccess;
+    for (auto& [ptr, bytes] : std::initializer_list<std::pair<float**, size_t>>{
+             {&e->b_kc, kv * 4}, {&e->b_vc, kv * 4}, {&e->b_x, ns * N_EMBD * 4}, {&e->b_y, ns * 2 * N_FF * 4},
+             {&e->b_q, ns * N_EMBD * 4}, {&e->b_part, ns * ATT_PART_FLOATS * 4}, {&e->b_att, ns * N_EMBD * 4},
+             {&e->b_logits, ns * e->n_vocab * 4}})
+        if (err == cudaSuccess) err = alloc(ptr, bytes);
+    if (err == cudaSuccess) err = alloc(&e->b_aqs, ns * (N_FF / 256) * 256);
+    if (err == cudaSuccess) err = alloc(&e->b_ad, ns * (N_FF / 256) * 4);
+    if (err == cudaSuccess) err = alloc(&e->b_abs, ns * (N_FF / 256) * 16 * 2);
+    if (err == cudaSuccess) err = alloc(&e->b_tokens, ns * 4);
+    if (err == cudaSuccess) err = alloc(&e->b_pos, ns * 4);
+    if (err == cudaSuccess) err = alloc(&e->b_argmax, ns * 4);
+    if (err == cudaSuccess) {
+        std::vector<float2> table(static_cast<size_t>(max_seq) * (HEAD_DIM / 2));
+        for (int p = 0; p < max_seq; ++p) rope_row(p, e->rope_base, table.data() + static_cast<size_t>(p) * (HEAD_DIM / 2));
+        err = cudaMalloc(&e->b_rope, table.size() * sizeof(float2));
+        if (err == cudaSuccess)
+            err = cudaMemcpy(e->b_rope, table.data(), table.size() * sizeof(float2), cudaMemcpyHostToDevice);
+    }
+    if (err != cudaSuccess) {
+        free_batch(e);
+        return cuda_status(err);
+    }
+    e->b_n = n_seq;
+    e->b_max_seq = max_seq;
+    e->b_pos_host.assign(n_seq, 0);
+    return MCPM_OK;
+}
+
+mcpm_status mcpm_batch_step_async(mcpm_engine* e, const int* tokens, const int* pos) {
+    if (!e) return MCPM_BAD_ARG;
+    if (!e->loaded || e->b_n == 0) return MCPM_NOT_LOADED;
+    const int n = e->b_n;
+    if (tokens)
+        for (int i = 0; i < n; ++i)
+            if (tokens[i] < 0 || tokens[i] >= e->n_vocab) return MCPM_BAD_TOKEN;
+    std::vector<int> next = pos ? std::vector<int>(pos, pos + n) : e->b_pos_host;
+    int max_pos = 0;
+    for (int i = 0; i < n; ++i) {
+        if (next[i] < 0 || next[i] >= e->b_max_seq) return MCPM_CTX_OVERFLOW;
+        max_pos = std::max(max_pos, next[i]);
+    }
+    MCPM_CUDA(cudaSetDevice(e->device));
+    if (tokens) MCPM_CUDA(cudaMemcpyAsync(e->b_tokens, tokens, n * sizeof(int), cudaMemcpyHostToDevice, e->stream));
+    if (pos) MCPM_CUDA(cudaMemcpyAsync(e->b_pos, pos, n * sizeof(int), cudaMemcpyHostToDevice, e->stream));
+    BatchLaunch b{};
+    b.n_seq = n, b.max_seq = e->b_max_seq, b.n_layer = e->n_layer, b.n_vocab = e->n_vocab, b.lm_type = e->lm_type;
+    b.max_pos = max_pos, b.chain = 1, b.n_sm = e->n_sm;
+    b.layers = e->layers.data(), b.embd = e->embd, b.out_norm = e->out_norm, b.lm = e->lm, b.rope = e->b_rope;
+    b.kc = e->b_kc, b.vc = e->b_vc, b.x = e->b_x, b.y = e->b_y, b.q = e->b_q, b.att_part = e->b_part;
+    b.att = e->b_att, b.logits = e->b_logits, b.aqs = e->b_aqs, b.ad = e->b_ad, b.abs = e->b_abs;
+    b.tokens = e->b_tokens, b.pos = e->b_pos, b.argmax = e->b_argmax;
+    b.err = reinterpret_cast<unsigned*>(e->ctl + CTL_ERR);
+    MCPM_CUDA(launch_batch_step(b, e->stream));
+    for (int i = 0; i < n; ++i) next[i] += 1;   // the argmax kernel advances the device copy the same way
+    e->b_pos_host = next;
+    return MCPM_OK;
+}
+
+mcpm_status mcpm_batch_read(mcpm_engine* e, float* logits, int* argmax) {
+    if (!e) return MCPM_BAD_ARG;
+    if (!e->loaded || e->b_n == 0) return MCPM_NOT_LOADED;
+    MCPM_CUDA(cudaSetDevice(e->device));
+    const size_t n = e->b_n;
+    if (logits)
+        MCPM_CUDA(cudaMemcpyAsync(logits, e->b_logits, n * e->n_vocab * sizeof(float), cudaMemcpyDeviceToHost, e->stream));
+    if (argmax) MCPM_CUDA(cudaMemcpyAsync(argmax, e->b_argmax, n * sizeof(int), cudaMemcpyDeviceToHost, e->stream));
+    return check_ctl(e);
 }
 
 // ------------------------------------------------------------------ ops

@@ -22,6 +22,7 @@ constexpr int LM_SLOT_BYTES = WBUF_BYTES;   // LM head: one stage per weight buf
 constexpr int ATT_MAX_CHUNKS = 64;         // attention chunks per head (chunk = 32*ceil(n/2048))
 constexpr int ATT_PART_STRIDE = 4 + HEAD_DIM;   // m, l, 2 pad, o[128]: o 16-byte aligned
 constexpr int ATT_PART_O = 4;
+constexpr int BATCH_MAX = 64;            // sequences of one batched-decode engine
 constexpr int ATTW_COPIES = 8;           // copies of the combined attention: CTA c polls copy c % 8
 constexpr int XLL_COPIES = 1;            // copies of the published residual: CTA c polls copy c % 8
 constexpr int ATT_SC_STRIDE = 256;         // chunk-length bound: 32*ceil(MAX_SEQ/2048)
@@ -78,6 +79,9 @@ struct DecodeParams {
                                // null outside the decode kernel (q and the cache are then final)
     float* att_part;    // [N_HEAD][ATT_MAX_CHUNKS][ATT_PART_STRIDE]: epoch-tagged (m, l) header, o[128]
     unsigned long long* attw;   // combined attention [ATTW_COPIES][N_EMBD], epoch-tagged (decode kernel, > 16 chunks)
+    int8_t* att_qs;     // optional split Q8_K output of combine_pair (batched decode): values [8][256],
+    float* att_d;       //   scales [8], block sums [8][16]; null: block_q8_K blocks in att_q8k
+    int16_t* att_bs;
     float* logits;      // [n_vocab]
     float* am_val;      // per-CTA argmax partials
     int* am_idx;
@@ -100,6 +104,23 @@ int decode_max_ctas_per_sm();
 // Standalone attention (mcpm_decode.cu): appends k/v at pos, then split-KV attention with
 // the decode kernel's numerics.  part: ATT_PART_FLOATS floats, cnt: 3 zeroed words.
 constexpr size_t ATT_PART_FLOATS = static_cast<size_t>(N_HEAD) * ATT_MAX_CHUNKS * ATT_PART_STRIDE;
+// Batched decode (n_seq independent sequences): one step of every sequence.
+struct BatchLaunch {
+    int n_seq, max_seq, n_layer, n_vocab, lm_type, max_pos, chain, n_sm;
+    const LayerDev* layers;   // host array; weight pointers are device pointers
+    const uint8_t* embd;
+    const float* out_norm;
+    const uint8_t* lm;
+    const float2* rope;
+    float *kc, *vc, *x, *y, *q, *att_part, *att, *logits;   // [n_seq][...] device buffers
+    int8_t* aqs;
+    float* ad;
+    int16_t* abs;
+    int *tokens, *pos, *argmax;
+    unsigned* err;
+};
+cudaError_t launch_batch_step(const BatchLaunch& b, cudaStream_t stream);
+
 cudaError_t launch_attention(const float* q, const float* k, const float* v, float* kc, float* vc, int pos, int max_seq,
                              float* out, uint8_t* out_q8k, float* part, cudaStream_t stream);
 

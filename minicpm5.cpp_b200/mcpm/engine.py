@@ -52,6 +52,9 @@ SIGNATURES = {
     "mcpm_read_x": (I, [P, C.POINTER(F)]),
     "mcpm_read_kv": (I, [P, I, I, C.POINTER(F), C.POINTER(F)]),
     "mcpm_write_kv": (I, [P, I, I, I, C.POINTER(F), C.POINTER(F)]),
+    "mcpm_batch_init": (I, [P, I, I]),
+    "mcpm_batch_step_async": (I, [P, C.POINTER(I), C.POINTER(I)]),
+    "mcpm_batch_read": (I, [P, C.POINTER(F), C.POINTER(I)]),
     "mcpm_model_dims": (I, [P, C.POINTER(I)]),
     "mcpm_engine_stream": (P, [P]),
     "mcpm_engine_n_ctas": (I, [P]),
@@ -161,6 +164,29 @@ class MiniCPM5Engine:
         v = np.zeros(256, np.float32)
         check(self.lib.mcpm_read_kv(self.h, layer, pos, _fptr(k), _fptr(v)), "mcpm_read_kv")
         return k, v
+
+    # batched decode: n_seq independent sequences in lockstep
+    def batch_init(self, n_seq: int, max_seq: int) -> None:
+        check(self.lib.mcpm_batch_init(self.h, n_seq, max_seq), "mcpm_batch_init")
+        self.batch_n = n_seq
+
+    def batch_step_async(self, tokens=None, pos=None) -> None:
+        t = None if tokens is None else np.ascontiguousarray(tokens, dtype=np.int32)
+        p = None if pos is None else np.ascontiguousarray(pos, dtype=np.int32)
+        ip = C.POINTER(C.c_int)
+        check(self.lib.mcpm_batch_step_async(self.h, None if t is None else t.ctypes.data_as(ip),
+                                             None if p is None else p.ctypes.data_as(ip)), "mcpm_batch_step_async")
+
+    def batch_read(self, logits: bool = False):
+        am = np.zeros(self.batch_n, np.int32)
+        lg = np.zeros((self.batch_n, self.n_vocab), np.float32) if logits else None
+        check(self.lib.mcpm_batch_read(self.h, None if lg is None else _fptr(lg),
+                                       am.ctypes.data_as(C.POINTER(C.c_int))), "mcpm_batch_read")
+        return am, lg
+
+    def batch_step(self, tokens=None, pos=None, logits: bool = False):
+        self.batch_step_async(tokens, pos)
+        return self.batch_read(logits)
 
     def write_kv(self, layer: int, pos0: int, k: np.ndarray, v: np.ndarray) -> None:
         k = np.ascontiguousarray(k, dtype=np.float32)
