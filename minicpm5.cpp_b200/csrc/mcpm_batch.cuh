@@ -5,10 +5,11 @@
 // bit for bit (MiniCPM5Engine::forward, src/model.cpp:142-242, once per sequence).
 //
 // Activations between GEMMs are Q8_K blocks split into arrays per sequence: values
-// [seq][B_NBA][256] int8, scales [seq][B_NBA] fp32, block sums [seq][B_NBA][16] int16.
+// [seq][B_NBA][256] int8 (stored lane-major by their producers, see below), scales
+// [seq][B_NBA] fp32, block sums [seq][B_NBA][16] int16.
 //
-// GEMM (k_b_gemm): a CTA owns 16 weight rows x 64 sequences; warp w owns sequences
-// 8w..8w+7.  Per 256-weight block the reference's AVX2 row kernel keeps eight int32 lane
+// GEMMs (k_b_gemm8 / k_b_gemm24): a tile is 16 weight rows x 64 sequences; warp w owns
+// sequences 8w..8w+7.  Per 256-weight block the reference's AVX2 row kernel keeps eight int32 lane
 // partials (ops_avx2.cpp:153-196 Q4_K, :201-276 Q6_K): lane k sums the elements 32s + 4k + t
 // (s = 0..7 sub-blocks, t = 0..3) times their sub-block scale.  The block is staged with its
 // K dimension permuted lane-major (position 32k + 4s + t), so lane k is the contiguous K range
@@ -18,11 +19,13 @@
 // sequence): acc[k] = fma(xd*d, lane_k, acc[k]) over blocks, the fused min chain, and the
 // hsum_f32_8 tree.
 
-constexpr int B_NBA = N_FF / 256;   // activation blocks per sequence (24)
-constexpr int BG_ROWS = 16;         // GEMM tile rows
-constexpr int BG_SEQ = BATCH_MAX;   // GEMM tile sequences (64)
-constexpr int BG_STRIDE = 272;      // smem bytes per staged 256-byte row (+16: conflict-free fragment loads)
+constexpr int B_NBA = N_FF / 256;          // activation blocks per sequence (24)
+constexpr int BG_ROWS = 16;                // GEMM tile rows
+constexpr int BG_SEQ = BATCH_MAX;          // GEMM tile sequences (64)
+constexpr int BG_STRIDE = 272;             // smem bytes per staged 256-byte block row (+16: conflict-free fragments)
 constexpr int BG_THREADS = 256;
+constexpr int BG_WROW8 = 8 * Q6K_BYTES;    // smem bytes per staged weight row of an 8-block matrix
+constexpr int BG_WROW24 = 24 * Q6K_BYTES;  // ... of a 24-block matrix
 
 struct BGemmSeg {
     const uint8_t* w;
@@ -38,17 +41,23 @@ struct BGemmArgs {
     int y_stride, n_seq;
 };
 
-// smem layout of k_b_gemm
-constexpr int BGS_AHI = 0;
-constexpr int BGS_ALO = BGS_AHI + BG_ROWS * BG_STRIDE;
-constexpr int BGS_X = BGS_ALO + BG_ROWS * BG_STRIDE;
-constexpr int BGS_XD = BGS_X + BG_SEQ * BG_STRIDE;       // float [64]
-constexpr int BGS_PAIR = BGS_XD + BG_SEQ * 4;             // int [64][8] bsums[2g] + bsums[2g+1]
-constexpr int BGS_BS = BGS_PAIR + BG_SEQ * 8 * 4;         // int16 [64][16]
-constexpr int BGS_RD = BGS_BS + BG_SEQ * 16 * 2;          // float [16] d
-constexpr int BGS_RM = BGS_RD + BG_ROWS * 4;              // float [16] dmin
-constexpr int BGS_MN = BGS_RM + BG_ROWS * 4;              // uint8 [16][8] Q4_K mins / int8 [16][16] Q6_K scales
-constexpr int BGS_BYTES = BGS_MN + BG_ROWS * 16;
+// k_b_gemm8 (8 blocks per row: QKV, o_proj, gate/up, LM head): the activations of every
+// sequence stay resident; weight tiles are double-buffered.
+constexpr int GA_X = 0;                                   // [8][64][272] activation values
+constexpr int GA_XD = GA_X + 8 * BG_SEQ * BG_STRIDE;      // float [8][64] scales
+constexpr int GA_XB = GA_XD + 8 * BG_SEQ * 4;             // int16 [8][64][16] block sums
+constexpr int GA_W = GA_XB + 8 * BG_SEQ * 32;             // 2 x [16][BG_WROW8] raw weight rows
+constexpr int GA_A = GA_W + 2 * BG_ROWS * BG_WROW8;       // hi [16][272], lo [16][272]
+constexpr int GA_RM = GA_A + 2 * BG_ROWS * BG_STRIDE;     // d [16], dmin [16], mins / scales [16][16]
+constexpr int GA_BYTES = GA_RM + BG_ROWS * (8 + 16);
+// k_b_gemm24 (24 blocks per row: down): the tile's weight rows stay resident; activation
+// blocks stream through a 3-slot ring.
+constexpr int GB_W = 0;                                                // [16][BG_WROW24]
+constexpr int GB_SLOT = BG_SEQ * BG_STRIDE + BG_SEQ * 4 + BG_SEQ * 32;   // values, scales, block sums
+constexpr int GB_X = GB_W + BG_ROWS * BG_WROW24;
+constexpr int GB_A = GB_X + 3 * GB_SLOT;
+constexpr int GB_RM = GB_A + 2 * BG_ROWS * BG_STRIDE;
+constexpr int GB_BYTES = GB_RM + BG_ROWS * (8 + 16);
 
 __device__ __forceinline__ void mma_s8(int (&c)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
     asm volatile(
@@ -57,90 +66,63 @@ __device__ __forceinline__ void mma_s8(int (&c)[4], const uint32_t (&a)[4], cons
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 
-// Raw loads of one block for this thread's share (row r, sub-block s, half of it), taken one
-// block ahead so their latency overlaps the MMAs of the current block.
-struct BRaw {
-    uint4 x[4];        // activation chunks c = tid + 256 j
-    float xd;          // tid < 64: scale of sequence tid
-    uint4 bs;          // tid < 128: 8 block sums of sequence tid/2
-    uint32_t w[9];     // weight bytes of (r, s, half)
-};
+__device__ __forceinline__ BGemmSeg bg_seg(const BGemmArgs& a, int tile) {   // by value: no local copy of a.seg
+    return (a.nseg > 2 && tile >= a.seg[2].tile0) ? a.seg[2] : (a.nseg > 1 && tile >= a.seg[1].tile0) ? a.seg[1] : a.seg[0];
+}
 
-template <int TYPE>
-__device__ __forceinline__ void bg_load(const BGemmArgs& a, const uint8_t* w, int rows, int row0, int nb, int b,
-                                        BRaw& raw) {
+// Activation block b of every sequence (already lane-major) -> xs [64][272], xd [64],
+// xb [64][16]; zeros beyond n_seq.
+__device__ void bg_stage_x(const BGemmArgs& a, int b, uint8_t* xs, float* xd, int16_t* xb) {
     const int tid = threadIdx.x;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int c = tid + BG_THREADS * j, q = c >> 4, m = c & 15;
-        raw.x[j] = q < a.n_seq ? __ldcg(reinterpret_cast<const uint4*>(a.aqs + (static_cast<size_t>(q) * B_NBA + b) * 256) + m)
-                               : make_uint4(0u, 0u, 0u, 0u);
+    for (int i = tid; i < BG_SEQ * 16; i += BG_THREADS) {
+        const int q = i >> 4, m = i & 15;
+        uint8_t* dst = xs + q * BG_STRIDE + 16 * m;
+        if (q < a.n_seq)
+            cp_async16(dst, a.aqs + (static_cast<size_t>(q) * B_NBA + b) * 256 + 16 * m);
+        else
+            *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
     }
-    raw.xd = tid < a.n_seq ? __ldcg(a.ad + static_cast<size_t>(tid) * B_NBA + b) : 0.0f;
-    raw.bs = tid < 2 * a.n_seq
-                 ? __ldcg(reinterpret_cast<const uint4*>(a.abs + (static_cast<size_t>(tid >> 1) * B_NBA + b) * 16) + (tid & 1))
-                 : make_uint4(0u, 0u, 0u, 0u);
-    const int r = tid >> 4, s = (tid >> 1) & 7, half = tid & 1;
-    const int grow = row0 + r;
-#pragma unroll
-    for (int i = 0; i < 9; ++i) raw.w[i] = 0u;
-    if (grow >= rows) return;
-    if (TYPE == GGML_Q4_K) {
-        const uint8_t* blk = w + (static_cast<size_t>(grow) * nb + b) * Q4K_BYTES;
-        const uint4 head = __ldg(reinterpret_cast<const uint4*>(blk));                                  // d, dmin, scales
-        const uint4 qv = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 32 * (s >> 1) + 16 * half));   // 16 nibble pairs
-        raw.w[0] = head.x, raw.w[1] = head.y, raw.w[2] = head.z, raw.w[3] = head.w;
-        raw.w[4] = qv.x, raw.w[5] = qv.y, raw.w[6] = qv.z, raw.w[7] = qv.w;
-    } else {   // Q6_K blocks are 210 bytes: 2-byte aligned loads
-        const uint8_t* blk = w + (static_cast<size_t>(grow) * nb + b) * Q6K_BYTES;
-        const int h = s >> 2, kk = s & 3;
-        const uint16_t* ql = reinterpret_cast<const uint16_t*>(blk + 64 * h + 32 * (kk & 1) + 16 * half);
-        const uint16_t* qh = reinterpret_cast<const uint16_t*>(blk + 128 + 32 * h + 16 * half);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            raw.w[i] = static_cast<uint32_t>(__ldg(ql + 2 * i)) | (static_cast<uint32_t>(__ldg(ql + 2 * i + 1)) << 16);
-            raw.w[4 + i] = static_cast<uint32_t>(__ldg(qh + 2 * i)) | (static_cast<uint32_t>(__ldg(qh + 2 * i + 1)) << 16);
-        }
-        raw.w[8] = static_cast<uint32_t>(blk[192 + 2 * s + half]) |
-                   (static_cast<uint32_t>(__ldg(reinterpret_cast<const uint16_t*>(blk + 208))) << 16);   // scale, d
+    for (int i = tid; i < BG_SEQ * 2; i += BG_THREADS) {
+        const int q = i >> 1, h = i & 1;
+        int16_t* dst = xb + 16 * q + 8 * h;
+        if (q < a.n_seq)
+            cp_async16(dst, a.abs + (static_cast<size_t>(q) * B_NBA + b) * 16 + 8 * h);
+        else
+            *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+    }
+    if (tid < BG_SEQ) {
+        if (tid < a.n_seq)
+            cp_async4(xd + tid, a.ad + static_cast<size_t>(tid) * B_NBA + b);
+        else
+            xd[tid] = 0.0f;
     }
 }
 
-// Registers -> shared memory: activations permuted lane-major, weights dequantised into the
-// hi / lo int8 operands, row and sequence metadata.
+// Weight rows row0 .. row0+15 of a segment (all nb blocks) -> dst [16][wrow]; zeros past the end.
+__device__ void bg_stage_w(const BGemmSeg& sg, int row0, int nb, uint8_t* dst, int wrow) {
+    const int rb = row_bytes(sg.type, 256 * nb), nch = rb >> 4;
+    for (int i = threadIdx.x; i < BG_ROWS * nch; i += BG_THREADS) {
+        const int r = i / nch, c = i - r * nch;
+        uint8_t* d = dst + r * wrow + 16 * c;
+        if (row0 + r < sg.rows)
+            cp_async16(d, sg.w + static_cast<size_t>(row0 + r) * rb + 16 * c);
+        else
+            *reinterpret_cast<uint4*>(d) = make_uint4(0u, 0u, 0u, 0u);
+    }
+}
+
+// Block b of the staged rows -> the hi / lo int8 operands (lane-major) and the row metadata.
+// Thread (r, s, half): row r, sub-block s, elements 16 half .. 16 half + 15 of it.
 template <int TYPE>
-__device__ __forceinline__ void bg_store(const BRaw& raw, uint8_t* sm) {
-    const int tid = threadIdx.x;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int c = tid + BG_THREADS * j, q = c >> 4, m = c & 15, s = m >> 1;
-        const uint32_t wv[4] = {raw.x[j].x, raw.x[j].y, raw.x[j].z, raw.x[j].w};
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {   // word kk holds elements 32s + 4k + t, k = 4(m&1) + kk
-            const int k = 4 * (m & 1) + kk;
-            *reinterpret_cast<uint32_t*>(sm + BGS_X + q * BG_STRIDE + 32 * k + 4 * s) = wv[kk];
-        }
-    }
-    if (tid < BG_SEQ) reinterpret_cast<float*>(sm + BGS_XD)[tid] = raw.xd;
-    if (tid < 2 * BG_SEQ) {
-        const int q = tid >> 1, h = tid & 1;
-        const uint32_t bw[4] = {raw.bs.x, raw.bs.y, raw.bs.z, raw.bs.w};
-        int16_t* bs = reinterpret_cast<int16_t*>(sm + BGS_BS) + 16 * q + 8 * h;
-        int* pair = reinterpret_cast<int*>(sm + BGS_PAIR) + 8 * q + 4 * h;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int lo = static_cast<int16_t>(bw[i] & 0xffffu), hi = static_cast<int16_t>(bw[i] >> 16);
-            bs[2 * i] = static_cast<int16_t>(lo);
-            bs[2 * i + 1] = static_cast<int16_t>(hi);
-            pair[i] = lo + hi;
-        }
-    }
-    const int r = tid >> 4, s = (tid >> 1) & 7, half = tid & 1;
+__device__ __forceinline__ void bg_dequant(const uint8_t* w, int wrow, int b, uint8_t* ahi, uint8_t* alo, uint8_t* rm) {
+    const int tid = threadIdx.x, r = tid >> 4, s = (tid >> 1) & 7, half = tid & 1;
     uint32_t hw[4], lw[4];
     if (TYPE == GGML_Q4_K) {
-        // byte i of the 12 packed scale bytes (raw.w[1..3]), selected without indexing registers
-        auto sc8 = [&](int i) -> int {
-            const uint32_t wd = i < 4 ? raw.w[1] : i < 8 ? raw.w[2] : raw.w[3];
+        const uint8_t* blk = w + r * wrow + b * Q4K_BYTES;
+        const uint4 head = *reinterpret_cast<const uint4*>(blk);   // d, dmin, 12 packed scale bytes
+        const uint4 qv = *reinterpret_cast<const uint4*>(blk + 16 + 32 * (s >> 1) + 16 * half);
+        auto sc8 = [&](int i) -> int {   // byte i of the packed scales, selected without register indexing
+            const uint32_t wd = i < 4 ? head.y : i < 8 ? head.z : head.w;
             return static_cast<int>((wd >> (8 * (i & 3))) & 0xffu);
         };
         int sc, mn;   // get_scale_min_k4 (include/ops.h:67-75)
@@ -151,126 +133,118 @@ __device__ __forceinline__ void bg_store(const BRaw& raw, uint8_t* sm) {
             sc = (sc8(s + 4) & 15) | ((sc8(s - 4) >> 6) << 4);
             mn = (sc8(s + 4) >> 4) | ((sc8(s) >> 6) << 4);
         }
+        const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-            const uint32_t qb = raw.w[4 + kk];   // bytes for elements i = 16 half + 4kk + t
             uint32_t h4 = 0u, l4 = 0u;
 #pragma unroll
             for (int t = 0; t < 4; ++t) {
-                const int byte = (qb >> (8 * t)) & 0xff;
-                const int q = (s & 1) ? (byte >> 4) : (byte & 15);
-                const int wq = sc * q;
+                const int byte = (qw[kk] >> (8 * t)) & 0xff;
+                const int wq = sc * ((s & 1) ? (byte >> 4) : (byte & 15));
                 h4 |= static_cast<uint32_t>((wq >> 6) & 0xff) << (8 * t);
                 l4 |= static_cast<uint32_t>(wq & 63) << (8 * t);
             }
             hw[kk] = h4, lw[kk] = l4;
         }
-        if (half == 0) sm[BGS_MN + 8 * r + s] = static_cast<uint8_t>(mn);
+        if (half == 0) rm[8 * BG_ROWS + 16 * r + s] = static_cast<uint8_t>(mn);
         if (s == 0 && half == 0) {
-            reinterpret_cast<float*>(sm + BGS_RD)[r] = h2f(raw.w[0]);
-            reinterpret_cast<float*>(sm + BGS_RM)[r] = h2f(raw.w[0] >> 16);
+            reinterpret_cast<float*>(rm)[r] = h2f(head.x);
+            reinterpret_cast<float*>(rm)[BG_ROWS + r] = h2f(head.x >> 16);
         }
-    } else {
-        const int scale = static_cast<int8_t>(raw.w[8] & 0xff);
-        const int kk6 = s & 3;
+    } else {   // Q6_K: 210-byte blocks, 2-byte aligned
+        const uint8_t* blk = w + r * wrow + b * Q6K_BYTES;
+        const int h = s >> 2, kk6 = s & 3;
+        const uint16_t* ql = reinterpret_cast<const uint16_t*>(blk + 64 * h + 32 * (kk6 & 1) + 16 * half);
+        const uint16_t* qh = reinterpret_cast<const uint16_t*>(blk + 128 + 32 * h + 16 * half);
+        uint32_t lq[4], hq[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            lq[i] = static_cast<uint32_t>(ql[2 * i]) | (static_cast<uint32_t>(ql[2 * i + 1]) << 16);
+            hq[i] = static_cast<uint32_t>(qh[2 * i]) | (static_cast<uint32_t>(qh[2 * i + 1]) << 16);
+        }
+        const int scale = static_cast<int8_t>(blk[192 + 2 * s + half]);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
             uint32_t h4 = 0u, l4 = 0u;
 #pragma unroll
             for (int t = 0; t < 4; ++t) {
-                const int e = 4 * kk + t;   // element l = 16 half + e of quarter kk6 of half s>>2
-                const int qlb = (raw.w[e >> 2] >> (8 * (e & 3))) & 0xff;
-                const int qhb = (raw.w[4 + (e >> 2)] >> (8 * (e & 3))) & 0xff;
-                const int lo4 = (kk6 & 2) ? (qlb >> 4) : (qlb & 15);
-                const int q6 = lo4 | (((qhb >> (2 * kk6)) & 3) << 4);
+                const int qlb = (lq[kk] >> (8 * t)) & 0xff, qhb = (hq[kk] >> (8 * t)) & 0xff;
+                const int q6 = ((kk6 & 2) ? (qlb >> 4) : (qlb & 15)) | (((qhb >> (2 * kk6)) & 3) << 4);
                 const int wq = scale * q6;
                 h4 |= static_cast<uint32_t>((wq >> 6) & 0xff) << (8 * t);
                 l4 |= static_cast<uint32_t>(wq & 63) << (8 * t);
             }
             hw[kk] = h4, lw[kk] = l4;
         }
-        reinterpret_cast<int8_t*>(sm + BGS_MN)[16 * r + 2 * s + half] = static_cast<int8_t>(scale);
-        if (s == 0 && half == 0) reinterpret_cast<float*>(sm + BGS_RD)[r] = h2f(raw.w[8] >> 16);
+        reinterpret_cast<int8_t*>(rm + 8 * BG_ROWS)[16 * r + 2 * s + half] = static_cast<int8_t>(scale);
+        if (s == 0 && half == 0) reinterpret_cast<float*>(rm)[r] = h2f(*reinterpret_cast<const uint16_t*>(blk + 208));
     }
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {   // lane k = 4 half + kk, permuted position 32k + 4s
         const int k = 4 * half + kk;
-        *reinterpret_cast<uint32_t*>(sm + BGS_AHI + r * BG_STRIDE + 32 * k + 4 * s) = hw[kk];
-        *reinterpret_cast<uint32_t*>(sm + BGS_ALO + r * BG_STRIDE + 32 * k + 4 * s) = lw[kk];
+        *reinterpret_cast<uint32_t*>(ahi + r * BG_STRIDE + 32 * k + 4 * s) = hw[kk];
+        *reinterpret_cast<uint32_t*>(alo + r * BG_STRIDE + 32 * k + 4 * s) = lw[kk];
     }
 }
 
-template <int TYPE, int NB>
-__device__ void bg_tile(const BGemmArgs& a, const BGemmSeg& sg, int row0, uint8_t* sm) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
-    const bool active = 8 * warp < a.n_seq;   // warp-uniform
-    float acc[4][8], acc_min[4];
+// One block: two MMAs per AVX2 lane and the batch-1 GEMV's fp32 chains for this thread's
+// four (row, sequence) pairs: rows g, g+8 x sequences 8w + 2t, 8w + 2t + 1.
+template <int TYPE>
+__device__ __forceinline__ void bg_block(const uint8_t* xs, const float* xd, const int16_t* xb, const uint8_t* ahi,
+                                         const uint8_t* alo, const uint8_t* rm, float (&acc)[4][8], float (&acc_min)[4]) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, t = lane & 3;
+    const int rr[4] = {g, g, g + 8, g + 8};
+    const int qq[4] = {8 * warp + 2 * t, 8 * warp + 2 * t + 1, 8 * warp + 2 * t, 8 * warp + 2 * t + 1};
+    const float* rd = reinterpret_cast<const float*>(rm);
+    float ds[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-        acc_min[e] = 0.0f;
+    for (int e = 0; e < 4; ++e) ds[e] = __fmul_rn(xd[qq[e]], rd[rr[e]]);
+    if (TYPE == GGML_Q4_K) {   // minsum = sum_g mins[g] * (bsums[2g] + bsums[2g+1])
 #pragma unroll
-        for (int k = 0; k < 8; ++k) acc[e][k] = 0.0f;
-    }
-    BRaw raw;
-    bg_load<TYPE>(a, sg.w, sg.rows, row0, NB, 0, raw);
-    for (int b = 0; b < NB; ++b) {
-        bg_store<TYPE>(raw, sm);
-        __syncthreads();
-        if (b + 1 < NB) bg_load<TYPE>(a, sg.w, sg.rows, row0, NB, b + 1, raw);
-        if (active) {
-            const float* xd = reinterpret_cast<const float*>(sm + BGS_XD);
-            const float* rd = reinterpret_cast<const float*>(sm + BGS_RD);
-            const int rr[4] = {g, g, g + 8, g + 8};
-            const int qq[4] = {8 * warp + 2 * t, 8 * warp + 2 * t + 1, 8 * warp + 2 * t, 8 * warp + 2 * t + 1};
-            float ds[4];
+        for (int e = 0; e < 4; ++e) {
+            const uint8_t* mn = rm + 8 * BG_ROWS + 16 * rr[e];
+            const int16_t* bs = xb + 16 * qq[e];
+            int ms = 0;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) ds[e] = __fmul_rn(xd[qq[e]], rd[rr[e]]);
-            if (TYPE == GGML_Q4_K) {   // min term: minsum = sum_g mins[g] * (bsums[2g] + bsums[2g+1])
-                const float* rm = reinterpret_cast<const float*>(sm + BGS_RM);
-                const int* pair = reinterpret_cast<const int*>(sm + BGS_PAIR);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const uint8_t* mn = sm + BGS_MN + 8 * rr[e];
-                    const int* pr = pair + 8 * qq[e];
-                    int ms = 0;
-#pragma unroll
-                    for (int gg = 0; gg < 8; ++gg) ms += static_cast<int>(mn[gg]) * pr[gg];
-                    acc_min[e] = __fmaf_rn(-__fmul_rn(xd[qq[e]], rm[rr[e]]), __int2float_rn(ms), acc_min[e]);
-                }
-            }
-            const uint8_t* ah = sm + BGS_AHI + g * BG_STRIDE + 4 * t;
-            const uint8_t* al = sm + BGS_ALO + g * BG_STRIDE + 4 * t;
-            const uint8_t* xb = sm + BGS_X + (8 * warp + g) * BG_STRIDE + 4 * t;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const uint32_t fa_h[4] = {*reinterpret_cast<const uint32_t*>(ah + 32 * k),
-                                          *reinterpret_cast<const uint32_t*>(ah + 8 * BG_STRIDE + 32 * k),
-                                          *reinterpret_cast<const uint32_t*>(ah + 32 * k + 16),
-                                          *reinterpret_cast<const uint32_t*>(ah + 8 * BG_STRIDE + 32 * k + 16)};
-                const uint32_t fa_l[4] = {*reinterpret_cast<const uint32_t*>(al + 32 * k),
-                                          *reinterpret_cast<const uint32_t*>(al + 8 * BG_STRIDE + 32 * k),
-                                          *reinterpret_cast<const uint32_t*>(al + 32 * k + 16),
-                                          *reinterpret_cast<const uint32_t*>(al + 8 * BG_STRIDE + 32 * k + 16)};
-                const uint32_t fb[2] = {*reinterpret_cast<const uint32_t*>(xb + 32 * k),
-                                        *reinterpret_cast<const uint32_t*>(xb + 32 * k + 16)};
-                int ch[4], cl[4];
-                mma_s8(ch, fa_h, fb);
-                mma_s8(cl, fa_l, fb);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    int lv = ch[e] * 64 + cl[e];
-                    if (TYPE == GGML_Q6_K) {   // -32 * (bsums[2k] * sc[2k] + bsums[2k+1] * sc[2k+1])
-                        const int16_t* bs = reinterpret_cast<const int16_t*>(sm + BGS_BS) + 16 * qq[e];
-                        const int8_t* sc = reinterpret_cast<const int8_t*>(sm + BGS_MN) + 16 * rr[e];
-                        lv -= 32 * (bs[2 * k] * sc[2 * k] + bs[2 * k + 1] * sc[2 * k + 1]);
-                    }
-                    acc[e][k] = __fmaf_rn(ds[e], __int2float_rn(lv), acc[e][k]);
-                }
-            }
+            for (int gg = 0; gg < 8; ++gg) ms += static_cast<int>(mn[gg]) * (bs[2 * gg] + bs[2 * gg + 1]);
+            acc_min[e] = __fmaf_rn(-__fmul_rn(xd[qq[e]], rd[BG_ROWS + rr[e]]), __int2float_rn(ms), acc_min[e]);
         }
-        __syncthreads();
     }
-    if (!active) return;
+    const uint8_t* ah = ahi + g * BG_STRIDE + 4 * t;
+    const uint8_t* al = alo + g * BG_STRIDE + 4 * t;
+    const uint8_t* xp = xs + (8 * warp + g) * BG_STRIDE + 4 * t;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const uint32_t fh[4] = {*reinterpret_cast<const uint32_t*>(ah + 32 * k),
+                                *reinterpret_cast<const uint32_t*>(ah + 8 * BG_STRIDE + 32 * k),
+                                *reinterpret_cast<const uint32_t*>(ah + 32 * k + 16),
+                                *reinterpret_cast<const uint32_t*>(ah + 8 * BG_STRIDE + 32 * k + 16)};
+        const uint32_t fl[4] = {*reinterpret_cast<const uint32_t*>(al + 32 * k),
+                                *reinterpret_cast<const uint32_t*>(al + 8 * BG_STRIDE + 32 * k),
+                                *reinterpret_cast<const uint32_t*>(al + 32 * k + 16),
+                                *reinterpret_cast<const uint32_t*>(al + 8 * BG_STRIDE + 32 * k + 16)};
+        const uint32_t fb[2] = {*reinterpret_cast<const uint32_t*>(xp + 32 * k),
+                                *reinterpret_cast<const uint32_t*>(xp + 32 * k + 16)};
+        int ch[4], cl[4];
+        mma_s8(ch, fh, fb);
+        mma_s8(cl, fl, fb);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            int lv = ch[e] * 64 + cl[e];
+            if (TYPE == GGML_Q6_K) {   // -32 * (bsums[2k] * sc[2k] + bsums[2k+1] * sc[2k+1])
+                const int16_t* bs = xb + 16 * qq[e];
+                const int8_t* sc = reinterpret_cast<const int8_t*>(rm + 8 * BG_ROWS) + 16 * rr[e];
+                lv -= 32 * (bs[2 * k] * sc[2 * k] + bs[2 * k + 1] * sc[2 * k + 1]);
+            }
+            acc[e][k] = __fmaf_rn(ds[e], __int2float_rn(lv), acc[e][k]);
+        }
+    }
+}
+
+template <int TYPE>
+__device__ __forceinline__ void bg_store_out(const BGemmArgs& a, const BGemmSeg& sg, int row0, const float (&acc)[4][8],
+                                             const float (&acc_min)[4]) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, t = lane & 3;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
         const int row = row0 + (e < 2 ? g : g + 8), q = 8 * warp + 2 * t + (e & 1);
@@ -283,25 +257,103 @@ __device__ void bg_tile(const BGemmArgs& a, const BGemmSeg& sg, int row0, uint8_
     }
 }
 
-__global__ void __launch_bounds__(BG_THREADS, 2) k_b_gemm(const BGemmArgs a) {
+template <int TYPE, int NB>
+__device__ void bg_tile(const BGemmArgs& a, const BGemmSeg& sg, int row0, const uint8_t* w, int wrow, uint8_t* xs0,
+                        int xs_step, float* xd0, int16_t* xb0, uint8_t* sm_a, uint8_t* rm, bool ring) {
+    const bool active = 8 * (threadIdx.x >> 5) < a.n_seq;   // warp-uniform
+    float acc[4][8], acc_min[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        acc_min[e] = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[e][k] = 0.0f;
+    }
+    for (int b = 0; b < NB; ++b) {
+        const int slot = ring ? b % 3 : b;
+        if (ring) {   // block b's activations are the oldest group but one in flight
+            cp_async_wait_group<1>();
+            __syncthreads();
+        }
+        bg_dequant<TYPE>(w, wrow, b, sm_a, sm_a + BG_ROWS * BG_STRIDE, rm);
+        __syncthreads();
+        if (active)
+            bg_block<TYPE>(xs0 + slot * xs_step, xd0 + slot * (ring ? GB_SLOT / 4 : BG_SEQ),
+                           reinterpret_cast<const int16_t*>(reinterpret_cast<const uint8_t*>(xb0) + slot * (ring ? GB_SLOT : BG_SEQ * 32)),
+                           sm_a, sm_a + BG_ROWS * BG_STRIDE, rm, acc, acc_min);
+        __syncthreads();
+        if (ring) {   // block b+2 into the slot block b-1 used
+            if (b + 2 < NB) {
+                uint8_t* sl = xs0 + ((b + 2) % 3) * xs_step;
+                bg_stage_x(a, b + 2, sl, reinterpret_cast<float*>(sl + BG_SEQ * BG_STRIDE),
+                           reinterpret_cast<int16_t*>(sl + BG_SEQ * BG_STRIDE + BG_SEQ * 4));
+            }
+            cp_async_commit();
+        }
+    }
+    if (active) bg_store_out<TYPE>(a, sg, row0, acc, acc_min);
+}
+
+__global__ void __launch_bounds__(BG_THREADS, 1) k_b_gemm8(const BGemmArgs a) {
+    extern __shared__ __align__(1024) uint8_t smg[];
+    for (int b = 0; b < 8; ++b)
+        bg_stage_x(a, b, smg + GA_X + b * BG_SEQ * BG_STRIDE, reinterpret_cast<float*>(smg + GA_XD) + b * BG_SEQ,
+                   reinterpret_cast<int16_t*>(smg + GA_XB) + b * BG_SEQ * 16);
+    cp_async_commit();
+    int tile = blockIdx.x;
+    if (tile < a.ntiles) {
+        const BGemmSeg sg = bg_seg(a, tile);
+        bg_stage_w(sg, (tile - sg.tile0) * BG_ROWS, 8, smg + GA_W, BG_WROW8);
+    }
+    cp_async_commit();
+    for (int it = 0; tile < a.ntiles; tile += gridDim.x, ++it) {
+        const int nxt = tile + gridDim.x;
+        if (nxt < a.ntiles) {   // next tile's rows into the other buffer (read last by tile it-1)
+            const BGemmSeg sn = bg_seg(a, nxt);
+            bg_stage_w(sn, (nxt - sn.tile0) * BG_ROWS, 8, smg + GA_W + ((it + 1) & 1) * BG_ROWS * BG_WROW8, BG_WROW8);
+        }
+        cp_async_commit();
+        cp_async_wait_group<1>();   // activations and this tile's rows landed
+        __syncthreads();
+        const BGemmSeg sg = bg_seg(a, tile);
+        const int row0 = (tile - sg.tile0) * BG_ROWS;
+        const uint8_t* w = smg + GA_W + (it & 1) * BG_ROWS * BG_WROW8;
+        if (sg.type == GGML_Q4_K)
+            bg_tile<GGML_Q4_K, 8>(a, sg, row0, w, BG_WROW8, smg + GA_X, BG_SEQ * BG_STRIDE,
+                                  reinterpret_cast<float*>(smg + GA_XD), reinterpret_cast<int16_t*>(smg + GA_XB),
+                                  smg + GA_A, smg + GA_RM, false);
+        else
+            bg_tile<GGML_Q6_K, 8>(a, sg, row0, w, BG_WROW8, smg + GA_X, BG_SEQ * BG_STRIDE,
+                                  reinterpret_cast<float*>(smg + GA_XD), reinterpret_cast<int16_t*>(smg + GA_XB),
+                                  smg + GA_A, smg + GA_RM, false);
+    }
+    cp_async_wait_all();
+}
+
+__global__ void __launch_bounds__(BG_THREADS, 1) k_b_gemm24(const BGemmArgs a) {
     extern __shared__ __align__(1024) uint8_t smg[];
     for (int tile = blockIdx.x; tile < a.ntiles; tile += gridDim.x) {
-        // segment by value (a runtime index into the parameter array would copy it to local memory)
-        const BGemmSeg sg = (a.nseg > 2 && tile >= a.seg[2].tile0) ? a.seg[2]
-                            : (a.nseg > 1 && tile >= a.seg[1].tile0) ? a.seg[1]
-                                                                     : a.seg[0];
+        const BGemmSeg sg = bg_seg(a, tile);
         const int row0 = (tile - sg.tile0) * BG_ROWS;
-        if (sg.type == GGML_Q4_K) {
-            if (a.nb == 8)
-                bg_tile<GGML_Q4_K, 8>(a, sg, row0, smg);
-            else
-                bg_tile<GGML_Q4_K, 24>(a, sg, row0, smg);
-        } else {
-            if (a.nb == 8)
-                bg_tile<GGML_Q6_K, 8>(a, sg, row0, smg);
-            else
-                bg_tile<GGML_Q6_K, 24>(a, sg, row0, smg);
+        bg_stage_w(sg, row0, 24, smg + GB_W, BG_WROW24);
+        cp_async_commit();
+        for (int b = 0; b < 2; ++b) {
+            uint8_t* sl = smg + GB_X + b * GB_SLOT;
+            bg_stage_x(a, b, sl, reinterpret_cast<float*>(sl + BG_SEQ * BG_STRIDE),
+                       reinterpret_cast<int16_t*>(sl + BG_SEQ * BG_STRIDE + BG_SEQ * 4));
+            cp_async_commit();
         }
+        if (sg.type == GGML_Q4_K)
+            bg_tile<GGML_Q4_K, 24>(a, sg, row0, smg + GB_W, BG_WROW24, smg + GB_X, GB_SLOT,
+                                   reinterpret_cast<float*>(smg + GB_X + BG_SEQ * BG_STRIDE),
+                                   reinterpret_cast<int16_t*>(smg + GB_X + BG_SEQ * BG_STRIDE + BG_SEQ * 4), smg + GB_A,
+                                   smg + GB_RM, true);
+        else
+            bg_tile<GGML_Q6_K, 24>(a, sg, row0, smg + GB_W, BG_WROW24, smg + GB_X, GB_SLOT,
+                                   reinterpret_cast<float*>(smg + GB_X + BG_SEQ * BG_STRIDE),
+                                   reinterpret_cast<int16_t*>(smg + GB_X + BG_SEQ * BG_STRIDE + BG_SEQ * 4), smg + GB_A,
+                                   smg + GB_RM, true);
+        cp_async_wait_all();
+        __syncthreads();
     }
 }
 
@@ -325,7 +377,7 @@ __device__ void b_norm_quant(const float* xs, const float* w, int8_t* qs, float*
 #pragma unroll
     for (int k = 0; k < 8; ++k)
         y[k] = __fmul_rn(__fmul_rn(xs[256 * warp + 8 * lane + k], __ldg(w + 256 * warp + 8 * lane + k)), rms);
-    quant_block_warp<AWAY>(y, qs + 256 * warp, d + warp, bs + 16 * warp);
+    quant_block_warp<AWAY, true>(y, qs + 256 * warp, d + warp, bs + 16 * warp);
     __syncthreads();
 }
 
@@ -366,10 +418,14 @@ __global__ void __launch_bounds__(256) k_b_res_norm(const BStepArgs a) {
     const int s = blockIdx.x;
     float* x = a.x + static_cast<size_t>(s) * N_EMBD;
     const float* y = a.y + static_cast<size_t>(s) * 2 * N_FF;
-    for (int i = threadIdx.x; i < N_EMBD; i += blockDim.x) {
-        const float v = __fadd_rn(x[i], y[i]);
-        x[i] = v;
-        xs[i] = v;
+    float xv[8], yv[8];   // every load before any store (x and y could alias for the compiler)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) xv[k] = __ldcg(x + threadIdx.x + 256 * k), yv[k] = __ldcg(y + threadIdx.x + 256 * k);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const float v = __fadd_rn(xv[k], yv[k]);
+        x[threadIdx.x + 256 * k] = v;
+        xs[threadIdx.x + 256 * k] = v;
     }
     __syncthreads();
     b_norm_quant<AWAY>(xs, a.norm, a.aqs + static_cast<size_t>(s) * B_NBA * 256, a.ad + static_cast<size_t>(s) * B_NBA,
@@ -383,11 +439,21 @@ __global__ void __launch_bounds__(256) k_b_rope_kv(const BStepArgs a, int l) {
     const float* y = a.y + static_cast<size_t>(s) * 2 * N_FF;
     float* kdst = a.kc + b_kv_off(a, s, l) + static_cast<size_t>(pos) * KV_DIM;
     float* vdst = a.vc + b_kv_off(a, s, l) + static_cast<size_t>(pos) * KV_DIM;
-    for (int pr = threadIdx.x; pr < (N_EMBD + 2 * KV_DIM) / 2; pr += blockDim.x) {
-        const int R = 2 * pr;
-        const float v0 = y[R], v1 = y[R + 1];
+    constexpr int NPAIR = (N_EMBD + 2 * KV_DIM) / 2, PER = NPAIR / 256;   // 5 pairs per thread
+    static_assert(NPAIR % 256 == 0, "pairs per thread");
+    float2 vv[PER], cc[PER];   // every load before any store
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        const int R = 2 * (threadIdx.x + 256 * j);
+        vv[j] = __ldcg(reinterpret_cast<const float2*>(y + R));
+        cc[j] = __ldg(a.rope + static_cast<size_t>(pos) * (HEAD_DIM / 2) + ((R & (HEAD_DIM - 1)) >> 1));
+    }
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        const int R = 2 * (threadIdx.x + 256 * j);
+        const float v0 = vv[j].x, v1 = vv[j].y;
         if (R < N_EMBD + KV_DIM) {
-            const float2 c = __ldg(a.rope + static_cast<size_t>(pos) * (HEAD_DIM / 2) + ((R & (HEAD_DIM - 1)) >> 1));
+            const float2 c = cc[j];
             const float r0 = __fmaf_rn(c.x, v0, -__fmul_rn(c.y, v1));
             const float r1 = __fmaf_rn(c.y, v0, __fmul_rn(c.x, v1));
             if (R < N_EMBD) {
@@ -442,20 +508,21 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_b_att_combine(const BStepArg
     combine_pair(p, sm, l, blockIdx.y, 1u);
 }
 
-// h = silu(gate) * up (canon_silu_mul), Q8_K ties away, 24 blocks per sequence.
+// h = silu(gate) * up (canon_silu_mul), Q8_K ties away: one warp per 256-element block
+// (blockIdx.y selects blocks 8y .. 8y+7 of sequence blockIdx.x).
 __global__ void __launch_bounds__(256) k_b_swiglu(const BStepArgs a) {
-    const int s = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const float* y = a.y + static_cast<size_t>(s) * 2 * N_FF;
-    for (int b = warp; b < N_FF / 256; b += 8) {
-        float h[8];
+    const int s = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, b = 8 * blockIdx.y + warp;
+    const float* y = a.y + static_cast<size_t>(s) * 2 * N_FF + 256 * b + 8 * lane;
+    const float4 g0 = __ldcg(reinterpret_cast<const float4*>(y)), g1 = __ldcg(reinterpret_cast<const float4*>(y + 4));
+    const float4 u0 = __ldcg(reinterpret_cast<const float4*>(y + N_FF)),
+                 u1 = __ldcg(reinterpret_cast<const float4*>(y + N_FF + 4));
+    const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+    const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+    float h[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const int i = 256 * b + 8 * lane + k;
-            h[k] = canon_silu_mul(y[i], y[N_FF + i]);
-        }
-        quant_block_warp<true>(h, a.aqs + (static_cast<size_t>(s) * B_NBA + b) * 256,
-                               a.ad + static_cast<size_t>(s) * B_NBA + b, a.abs + (static_cast<size_t>(s) * B_NBA + b) * 16);
-    }
+    for (int k = 0; k < 8; ++k) h[k] = canon_silu_mul(g[k], u[k]);
+    quant_block_warp<true, true>(h, a.aqs + (static_cast<size_t>(s) * B_NBA + b) * 256, a.ad + static_cast<size_t>(s) * B_NBA + b,
+                           a.abs + (static_cast<size_t>(s) * B_NBA + b) * 16);
 }
 
 // Greedy token per sequence over its logits (lowest index on ties; NaN never wins; a NaN

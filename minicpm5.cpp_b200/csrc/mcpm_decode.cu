@@ -977,7 +977,7 @@ __device__ bool combine_pair(const DecodeParams& p, const Smem& s, int l, int b,
 #pragma unroll
         for (int k = 0; k < 8; ++k) y[k] = ab[8 * lane + k];
         if (p.att_qs) {
-            quant_block_warp<false>(y, p.att_qs + 256 * b, p.att_d + b, p.att_bs + 16 * b);
+            quant_block_warp<false, true>(y, p.att_qs + 256 * b, p.att_d + b, p.att_bs + 16 * b);   // lane-major
         } else {
             uint8_t* blk = p.att_q8k + static_cast<size_t>(b) * Q8K_BYTES;
             quant_block_warp<false>(y, reinterpret_cast<int8_t*>(blk + 4), reinterpret_cast<float*>(blk),
@@ -1400,6 +1400,8 @@ cudaError_t launch_batch_step(const BatchLaunch& b, cudaStream_t stream) {
         cudaError_t e = cudaFuncSetAttribute(k_b_att_units, cudaFuncAttributeMaxDynamicSharedMemorySize, UNIT_SMEM_BIG);
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(k_b_att_combine, cudaFuncAttributeMaxDynamicSharedMemorySize, COMBINE_SMEM);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(k_b_gemm8, cudaFuncAttributeMaxDynamicSharedMemorySize, GA_BYTES);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(k_b_gemm24, cudaFuncAttributeMaxDynamicSharedMemorySize, GB_BYTES);
         if (e != cudaSuccess) return e;
         prepared_dev = dev;
     }
@@ -1424,7 +1426,10 @@ cudaError_t launch_batch_step(const BatchLaunch& b, cudaStream_t stream) {
         }
         g.nseg = i, g.ntiles = tiles, g.nb = nb;
         g.aqs = b.aqs, g.ad = b.ad, g.abs = b.abs, g.y = y, g.y_stride = y_stride, g.n_seq = n;
-        k_b_gemm<<<std::min(tiles, 2 * b.n_sm), BG_THREADS, BGS_BYTES, stream>>>(g);
+        if (nb == 8)
+            k_b_gemm8<<<std::min(tiles, b.n_sm), BG_THREADS, GA_BYTES, stream>>>(g);
+        else
+            k_b_gemm24<<<std::min(tiles, b.n_sm), BG_THREADS, GB_BYTES, stream>>>(g);
     };
     a.norm = b.layers[0].attn_norm;
     k_b_embed<<<n, 256, 0, stream>>>(a);
@@ -1439,7 +1444,7 @@ cudaError_t launch_batch_step(const BatchLaunch& b, cudaStream_t stream) {
         a.norm = L.ffn_norm;
         k_b_res_norm<true><<<n, 256, 0, stream>>>(a);
         gemm({{L.wg, L.tg, N_FF, 0, 0}, {L.wu, L.tu, N_FF, N_FF, 0}}, N_EMBD / 256, b.y, 2 * N_FF);
-        k_b_swiglu<<<n, 256, 0, stream>>>(a);
+        k_b_swiglu<<<dim3(n, N_FF / 256 / 8), 256, 0, stream>>>(a);
         gemm({{L.wd, L.td, N_EMBD, 0, 0}}, N_FF / 256, b.y, 2 * N_FF);
         if (l + 1 < b.n_layer) {
             a.norm = b.layers[l + 1].attn_norm;

@@ -95,6 +95,13 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
+// 4-byte global->shared copy (LDGSTS through L1).
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+// Waits until at most N of this thread's committed cp.async groups are still in flight.
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 // 16-byte L2 load that the compiler keeps in program order (issued where written).
@@ -307,7 +314,7 @@ struct XQSmem {
 // canonical Q8_K block.  Block amax follows the reference build's NaN-sensitive
 // eight-lane maximum (orc_block_amax); d = amax*(1/127); mul = 127/amax.
 // Writes qs/d/bsums through the supplied pointers (shared or global, 4-byte aligned).
-template <bool AWAY>
+template <bool AWAY, bool PERM = false>
 __device__ __forceinline__ void quant_block_warp(const float (&y)[8], int8_t* qs_out, float* d_out,
                                                  int16_t* bsums_out) {
     const int lane = threadIdx.x & 31;
@@ -355,9 +362,14 @@ __device__ __forceinline__ void quant_block_warp(const float (&y)[8], int8_t* qs
     }
     const uint32_t w0 = (q[0] & 0xff) | ((q[1] & 0xff) << 8) | ((q[2] & 0xff) << 16) | ((uint32_t)(q[3] & 0xff) << 24);
     const uint32_t w1 = (q[4] & 0xff) | ((q[5] & 0xff) << 8) | ((q[6] & 0xff) << 16) | ((uint32_t)(q[7] & 0xff) << 24);
-    uint32_t* qw = reinterpret_cast<uint32_t*>(qs_out + 8 * lane);
-    qw[0] = w0;
-    qw[1] = w1;
+    if (PERM) {   // lane-major order of the batched GEMM: element 32s + 4k + t at 32k + 4s + t
+        *reinterpret_cast<uint32_t*>(qs_out + 64 * (lane & 3) + 4 * (lane >> 2)) = w0;
+        *reinterpret_cast<uint32_t*>(qs_out + 64 * (lane & 3) + 32 + 4 * (lane >> 2)) = w1;
+    } else {
+        uint32_t* qw = reinterpret_cast<uint32_t*>(qs_out + 8 * lane);
+        qw[0] = w0;
+        qw[1] = w1;
+    }
     int s = q[0] + q[1] + q[2] + q[3] + q[4] + q[5] + q[6] + q[7];
     s += __shfl_xor_sync(0xffffffffu, s, 1);
     if ((lane & 1) == 0) bsums_out[lane >> 1] = static_cast<int16_t>(s);
