@@ -305,22 +305,23 @@ def run_batch(args, rank, world, local):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
         pg = dist
     n = BATCH_TOTAL // world
+    n_prompt = BATCH_PROMPT if args.prompt == PROMPT else args.prompt   # --prompt: a smaller case for profiling
     path = synth.ensure_model("q4_k_m", 0)
     if pg:
         pg.barrier()
-    max_seq = BATCH_PROMPT + args.warmup + args.steps + 80
+    max_seq = n_prompt + args.warmup + args.steps + 80
     eng = E.MiniCPM5Engine(device=local, max_seq=64)
     if not eng.load_model(path):
         raise SystemExit("load_model failed")
     eng.batch_init(n, max_seq)
     stream = torch.cuda.ExternalStream(eng.stream)
-    prompts = np.stack([synth.prompt_ids(BATCH_PROMPT, seed=5000 + rank * n + i) for i in range(n)]).astype(np.int32)
-    for pos in range(BATCH_PROMPT):   # prefill (untimed)
+    prompts = np.stack([synth.prompt_ids(n_prompt, seed=5000 + rank * n + i) for i in range(n)]).astype(np.int32)
+    for pos in range(n_prompt):   # prefill (untimed)
         eng.batch_step_async(prompts[:, pos], np.full(n, pos, np.int32))
     for _ in range(args.warmup):
         eng.batch_step_async()
     eng.batch_read()
-    first_pos = BATCH_PROMPT + args.warmup
+    first_pos = n_prompt + args.warmup
     if pg:
         pg.barrier()
     torch.cuda.synchronize()
@@ -362,7 +363,7 @@ def run_batch(args, rank, world, local):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8 mma / fp32",
             "data": "synthetic (seeded random-init GGUF, Q4_K_M layout)",
             "config": {"workload": "config3: MiniCPM5-2B Q4_K_M batched greedy decode, 64 sequences",
-                       "sequences_per_gpu": n, "prompt": BATCH_PROMPT,
+                       "sequences_per_gpu": n, "prompt": n_prompt,
                        "positions": [first_pos, first_pos + args.steps - 1],
                        "parallelism": f"dp{world} (sequences split over GPUs)",
                        "l2": "inputs larger than L2 (1.41 GB of weights + K/V per step)"},

@@ -112,7 +112,18 @@ __device__ void bg_stage_w(const BGemmSeg& sg, int row0, int nb, uint8_t* dst, i
 }
 
 // Block b of the staged rows -> the hi / lo int8 operands (lane-major) and the row metadata.
-// Thread (r, s, half): row r, sub-block s, elements 16 half .. 16 half + 15 of it.
+// Thread (r, s, half): row r, sub-block s, elements 16 half .. 16 half + 15 of it.  Four
+// elements at a time in two words of 16-bit lanes (elements t, t+2 and t+1, t+3):
+// w' = sc * q stays below 2^16 per lane (Q4_K: 63 * 15; Q6_K: W = q (sc + 128) + 8192 - 128 q,
+// i.e. sc * q + 8192 in [128, 24257], so hi = (W >> 6) - 128 and lo = W & 63 exactly).
+__device__ __forceinline__ void bg_pack(uint32_t wa, uint32_t wb, int bias_hi, uint32_t& h4, uint32_t& l4) {
+    // wa: elements 0 / 2, wb: 1 / 3 (16-bit lanes) -> bytes 0..3
+    uint32_t ha = (wa >> 6) & 0x00ff00ffu, hb = (wb >> 6) & 0x00ff00ffu;
+    if (bias_hi) ha ^= 0x00800080u, hb ^= 0x00800080u;
+    h4 = __byte_perm(ha, hb, 0x6240);
+    l4 = __byte_perm(wa & 0x003f003fu, wb & 0x003f003fu, 0x6240);
+}
+
 template <int TYPE>
 __device__ __forceinline__ void bg_dequant(const uint8_t* w, int wrow, int b, uint8_t* ahi, uint8_t* alo, uint8_t* rm) {
     const int tid = threadIdx.x, r = tid >> 4, s = (tid >> 1) & 7, half = tid & 1;
@@ -136,17 +147,13 @@ __device__ __forceinline__ void bg_dequant(const uint8_t* w, int wrow, int b, ui
         const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-            uint32_t h4 = 0u, l4 = 0u;
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                const int byte = (qw[kk] >> (8 * t)) & 0xff;
-                const int wq = sc * ((s & 1) ? (byte >> 4) : (byte & 15));
-                h4 |= static_cast<uint32_t>((wq >> 6) & 0xff) << (8 * t);
-                l4 |= static_cast<uint32_t>(wq & 63) << (8 * t);
-            }
-            hw[kk] = h4, lw[kk] = l4;
+            const uint32_t nib = (s & 1) ? (qw[kk] >> 4) & 0x0f0f0f0fu : qw[kk] & 0x0f0f0f0fu;
+            const uint32_t wa = __byte_perm(nib, 0u, 0x4240) * static_cast<uint32_t>(sc);
+            const uint32_t wb = __byte_perm(nib, 0u, 0x4341) * static_cast<uint32_t>(sc);
+            bg_pack(wa, wb, 0, hw[kk], lw[kk]);
         }
-        if (half == 0) rm[8 * BG_ROWS + 16 * r + s] = static_cast<uint8_t>(mn);
+        if (half == 0)   // min m[s] twice in a 16-bit word (dp2a operand)
+            reinterpret_cast<uint16_t*>(rm + 8 * BG_ROWS)[8 * r + s] = static_cast<uint16_t>(mn * 0x0101);
         if (s == 0 && half == 0) {
             reinterpret_cast<float*>(rm)[r] = h2f(head.x);
             reinterpret_cast<float*>(rm)[BG_ROWS + r] = h2f(head.x >> 16);
@@ -156,25 +163,17 @@ __device__ __forceinline__ void bg_dequant(const uint8_t* w, int wrow, int b, ui
         const int h = s >> 2, kk6 = s & 3;
         const uint16_t* ql = reinterpret_cast<const uint16_t*>(blk + 64 * h + 32 * (kk6 & 1) + 16 * half);
         const uint16_t* qh = reinterpret_cast<const uint16_t*>(blk + 128 + 32 * h + 16 * half);
-        uint32_t lq[4], hq[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            lq[i] = static_cast<uint32_t>(ql[2 * i]) | (static_cast<uint32_t>(ql[2 * i + 1]) << 16);
-            hq[i] = static_cast<uint32_t>(qh[2 * i]) | (static_cast<uint32_t>(qh[2 * i + 1]) << 16);
-        }
         const int scale = static_cast<int8_t>(blk[192 + 2 * s + half]);
+        const uint32_t sc1 = static_cast<uint32_t>(scale + 128);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-            uint32_t h4 = 0u, l4 = 0u;
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                const int qlb = (lq[kk] >> (8 * t)) & 0xff, qhb = (hq[kk] >> (8 * t)) & 0xff;
-                const int q6 = ((kk6 & 2) ? (qlb >> 4) : (qlb & 15)) | (((qhb >> (2 * kk6)) & 3) << 4);
-                const int wq = scale * q6;
-                h4 |= static_cast<uint32_t>((wq >> 6) & 0xff) << (8 * t);
-                l4 |= static_cast<uint32_t>(wq & 63) << (8 * t);
-            }
-            hw[kk] = h4, lw[kk] = l4;
+            const uint32_t lq = static_cast<uint32_t>(ql[2 * kk]) | (static_cast<uint32_t>(ql[2 * kk + 1]) << 16);
+            const uint32_t hq = static_cast<uint32_t>(qh[2 * kk]) | (static_cast<uint32_t>(qh[2 * kk + 1]) << 16);
+            const uint32_t lo4 = (kk6 & 2) ? (lq >> 4) & 0x0f0f0f0fu : lq & 0x0f0f0f0fu;
+            const uint32_t q6 = lo4 | (((hq >> (2 * kk6)) & 0x03030303u) << 4);   // four values 0..63
+            const uint32_t qa = __byte_perm(q6, 0u, 0x4240), qb = __byte_perm(q6, 0u, 0x4341);
+            const uint32_t wa = qa * sc1 + 0x20002000u - (qa << 7), wb = qb * sc1 + 0x20002000u - (qb << 7);
+            bg_pack(wa, wb, 1, hw[kk], lw[kk]);
         }
         reinterpret_cast<int8_t*>(rm + 8 * BG_ROWS)[16 * r + 2 * s + half] = static_cast<int8_t>(scale);
         if (s == 0 && half == 0) reinterpret_cast<float*>(rm)[r] = h2f(*reinterpret_cast<const uint16_t*>(blk + 208));
@@ -187,57 +186,89 @@ __device__ __forceinline__ void bg_dequant(const uint8_t* w, int wrow, int b, ui
     }
 }
 
+// signed dp2a: two int16 of a times the low / high two int8 of b, plus c
+__device__ __forceinline__ int dp2lo(uint32_t a, uint32_t b, int c) {
+    return __dp2a_lo(static_cast<int>(a), static_cast<int>(b), c);
+}
+__device__ __forceinline__ int dp2hi(uint32_t a, uint32_t b, int c) {
+    return __dp2a_hi(static_cast<int>(a), static_cast<int>(b), c);
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t (&r)[2], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(smem_u32(p)));
+}
+
 // One block: two MMAs per AVX2 lane and the batch-1 GEMV's fp32 chains for this thread's
-// four (row, sequence) pairs: rows g, g+8 x sequences 8w + 2t, 8w + 2t + 1.
+// four (row, sequence) pairs: rows g, g+8 x sequences 8w + 2t, 8w + 2t + 1.  Fragments come
+// from ldmatrix (int8 m16n8k32 operands have the b16 8x8 layout); the Q6_K lane offset and
+// the Q4_K min sum are dp2a dot products of block-sum pairs with scale bytes.
 template <int TYPE>
 __device__ __forceinline__ void bg_block(const uint8_t* xs, const float* xd, const int16_t* xb, const uint8_t* ahi,
                                          const uint8_t* alo, const uint8_t* rm, float (&acc)[4][8], float (&acc_min)[4]) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, t = lane & 3;
-    const int rr[4] = {g, g, g + 8, g + 8};
-    const int qq[4] = {8 * warp + 2 * t, 8 * warp + 2 * t + 1, 8 * warp + 2 * t, 8 * warp + 2 * t + 1};
+    const int q0 = 8 * warp + 2 * t;
     const float* rd = reinterpret_cast<const float*>(rm);
-    float ds[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) ds[e] = __fmul_rn(xd[qq[e]], rd[rr[e]]);
+    const float xd0 = xd[q0], xd1 = xd[q0 + 1];
+    const float d0 = rd[g], d1 = rd[g + 8];
+    const float ds[4] = {__fmul_rn(xd0, d0), __fmul_rn(xd1, d0), __fmul_rn(xd0, d1), __fmul_rn(xd1, d1)};
+    // block sums of the two sequences as int16 pairs: word k = (bsums[2k], bsums[2k+1])
+    const uint4 b0a = *reinterpret_cast<const uint4*>(xb + 16 * q0), b0b = *reinterpret_cast<const uint4*>(xb + 16 * q0 + 8);
+    const uint4 b1a = *reinterpret_cast<const uint4*>(xb + 16 * (q0 + 1)),
+                b1b = *reinterpret_cast<const uint4*>(xb + 16 * (q0 + 1) + 8);
+    const uint32_t bw0[8] = {b0a.x, b0a.y, b0a.z, b0a.w, b0b.x, b0b.y, b0b.z, b0b.w};
+    const uint32_t bw1[8] = {b1a.x, b1a.y, b1a.z, b1a.w, b1b.x, b1b.y, b1b.z, b1b.w};
+    const uint4 sr0 = *reinterpret_cast<const uint4*>(rm + 8 * BG_ROWS + 16 * g);        // row g: Q6_K scales /
+    const uint4 sr1 = *reinterpret_cast<const uint4*>(rm + 8 * BG_ROWS + 16 * (g + 8));  // Q4_K doubled mins
+    const uint32_t sw0[4] = {sr0.x, sr0.y, sr0.z, sr0.w}, sw1[4] = {sr1.x, sr1.y, sr1.z, sr1.w};
     if (TYPE == GGML_Q4_K) {   // minsum = sum_g mins[g] * (bsums[2g] + bsums[2g+1])
+        int ms[4] = {0, 0, 0, 0};
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const uint8_t* mn = rm + 8 * BG_ROWS + 16 * rr[e];
-            const int16_t* bs = xb + 16 * qq[e];
-            int ms = 0;
-#pragma unroll
-            for (int gg = 0; gg < 8; ++gg) ms += static_cast<int>(mn[gg]) * (bs[2 * gg] + bs[2 * gg + 1]);
-            acc_min[e] = __fmaf_rn(-__fmul_rn(xd[qq[e]], rd[BG_ROWS + rr[e]]), __int2float_rn(ms), acc_min[e]);
+        for (int j = 0; j < 4; ++j) {
+            ms[0] = dp2hi(bw0[2 * j + 1], sw0[j], dp2lo(bw0[2 * j], sw0[j], ms[0]));
+            ms[1] = dp2hi(bw1[2 * j + 1], sw0[j], dp2lo(bw1[2 * j], sw0[j], ms[1]));
+            ms[2] = dp2hi(bw0[2 * j + 1], sw1[j], dp2lo(bw0[2 * j], sw1[j], ms[2]));
+            ms[3] = dp2hi(bw1[2 * j + 1], sw1[j], dp2lo(bw1[2 * j], sw1[j], ms[3]));
         }
+        const float m0 = rd[BG_ROWS + g], m1 = rd[BG_ROWS + g + 8];
+        const float dm[4] = {-__fmul_rn(xd0, m0), -__fmul_rn(xd1, m0), -__fmul_rn(xd0, m1), -__fmul_rn(xd1, m1)};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc_min[e] = __fmaf_rn(dm[e], __int2float_rn(ms[e]), acc_min[e]);
     }
-    const uint8_t* ah = ahi + g * BG_STRIDE + 4 * t;
-    const uint8_t* al = alo + g * BG_STRIDE + 4 * t;
-    const uint8_t* xp = xs + (8 * warp + g) * BG_STRIDE + 4 * t;
+    // ldmatrix row addresses: A rows (lane & 7) + 8 ((lane >> 3) & 1), K half lane >> 4;
+    // B sequence rows lane & 7, K half (lane >> 3) & 1
+    const int ar = (lane & 7) + 8 * ((lane >> 3) & 1), ak = 16 * (lane >> 4);
+    const uint8_t* pah = ahi + ar * BG_STRIDE + ak;
+    const uint8_t* pal = alo + ar * BG_STRIDE + ak;
+    const uint8_t* pb = xs + (8 * warp + (lane & 7)) * BG_STRIDE + 16 * ((lane >> 3) & 1);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-        const uint32_t fh[4] = {*reinterpret_cast<const uint32_t*>(ah + 32 * k),
-                                *reinterpret_cast<const uint32_t*>(ah + 8 * BG_STRIDE + 32 * k),
-                                *reinterpret_cast<const uint32_t*>(ah + 32 * k + 16),
-                                *reinterpret_cast<const uint32_t*>(ah + 8 * BG_STRIDE + 32 * k + 16)};
-        const uint32_t fl[4] = {*reinterpret_cast<const uint32_t*>(al + 32 * k),
-                                *reinterpret_cast<const uint32_t*>(al + 8 * BG_STRIDE + 32 * k),
-                                *reinterpret_cast<const uint32_t*>(al + 32 * k + 16),
-                                *reinterpret_cast<const uint32_t*>(al + 8 * BG_STRIDE + 32 * k + 16)};
-        const uint32_t fb[2] = {*reinterpret_cast<const uint32_t*>(xp + 32 * k),
-                                *reinterpret_cast<const uint32_t*>(xp + 32 * k + 16)};
+        uint32_t fh[4], fl[4], fb[2];
+        ldsm_x4(fh, pah + 32 * k);
+        ldsm_x4(fl, pal + 32 * k);
+        ldsm_x2(fb, pb + 32 * k);
         int ch[4], cl[4];
         mma_s8(ch, fh, fb);
         mma_s8(cl, fl, fb);
+        int lv[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            int lv = ch[e] * 64 + cl[e];
-            if (TYPE == GGML_Q6_K) {   // -32 * (bsums[2k] * sc[2k] + bsums[2k+1] * sc[2k+1])
-                const int16_t* bs = xb + 16 * qq[e];
-                const int8_t* sc = reinterpret_cast<const int8_t*>(rm + 8 * BG_ROWS) + 16 * rr[e];
-                lv -= 32 * (bs[2 * k] * sc[2 * k] + bs[2 * k + 1] * sc[2 * k + 1]);
+        for (int e = 0; e < 4; ++e) lv[e] = ch[e] * 64 + cl[e];
+        if (TYPE == GGML_Q6_K) {   // -32 * (bsums[2k] * sc[2k] + bsums[2k+1] * sc[2k+1])
+            const uint32_t s0 = sw0[k >> 1], s1 = sw1[k >> 1];
+            if (k & 1) {
+                lv[0] -= 32 * dp2hi(bw0[k], s0, 0), lv[1] -= 32 * dp2hi(bw1[k], s0, 0);
+                lv[2] -= 32 * dp2hi(bw0[k], s1, 0), lv[3] -= 32 * dp2hi(bw1[k], s1, 0);
+            } else {
+                lv[0] -= 32 * dp2lo(bw0[k], s0, 0), lv[1] -= 32 * dp2lo(bw1[k], s0, 0);
+                lv[2] -= 32 * dp2lo(bw0[k], s1, 0), lv[3] -= 32 * dp2lo(bw1[k], s1, 0);
             }
-            acc[e][k] = __fmaf_rn(ds[e], __int2float_rn(lv), acc[e][k]);
         }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[e][k] = __fmaf_rn(ds[e], __int2float_rn(lv[e]), acc[e][k]);
     }
 }
 
