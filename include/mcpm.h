@@ -84,6 +84,17 @@ mcpm_status mcpm_write_kv(mcpm_engine* e, int layer, int pos0, int n_pos, const 
 mcpm_status mcpm_batch_init(mcpm_engine* e, int n_seq, int max_seq);
 mcpm_status mcpm_batch_step_async(mcpm_engine* e, const int* tokens, const int* pos);
 mcpm_status mcpm_batch_read(mcpm_engine* e, float* logits, int* argmax);
+/* Top-p sampling on the device (Sampler::sample, src/sampler.cpp:8-72): logits (device,
+ * n <= 1048576 floats), temperature (applied when > 0 and != 1), top_p (truncation when in
+ * (0, 1)), r: the uniform draw in [0, 1) (the reference draws it from mt19937 seeded by
+ * random_device; here the caller supplies it).  out (device, 2 ints): the token and the number
+ * of tokens kept.  Fixed canonical order (ties by index, blocked fp32 sums) shared with the C
+ * restatement.  A per-device workspace is allocated on the first call. */
+mcpm_status mcpm_sample_top_p(const float* logits, int n, float temperature, float top_p, float r, int* out,
+                              void* stream);
+/* Samples the last decode step's logits (the step must have written them) and makes the
+ * token the next step's input (forward with token < 0).  token_out (host) is optional. */
+mcpm_status mcpm_sample(mcpm_engine* e, float temperature, float top_p, float r, int* token_out);
 /* n_layer, n_embd, n_ff, n_head, n_head_kv, n_vocab of the loaded model. */
 mcpm_status mcpm_model_dims(mcpm_engine* e, int dims[6]);
 /* Phase trace (no reference counterpart; the reference only times whole loops,

@@ -606,6 +606,65 @@ void mcpm_engine_destroy(mcpm_engine* e) {
     delete e;
 }
 
+// ------------------------------------------------------------------ sampler
+namespace {
+struct SampleWorkspace {
+    int n = 0;
+    float* p = nullptr;
+    uint32_t* gk = nullptr;
+    int* gi = nullptr;
+    int* out = nullptr;
+};
+SampleWorkspace g_sample_ws[64];
+
+mcpm_status sample_workspace(int n, SampleWorkspace*& ws) {
+    int dev = 0;
+    MCPM_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return MCPM_BAD_ARG;
+    ws = &g_sample_ws[dev];
+    if (ws->n < n) {
+        free_dev(ws->p);
+        free_dev(ws->gk);
+        free_dev(ws->gi);
+        free_dev(ws->out);
+        ws->n = 0;
+        MCPM_CUDA(cudaMalloc(&ws->p, sizeof(float) * n));
+        MCPM_CUDA(cudaMalloc(&ws->gk, sizeof(uint32_t) * 2 * n));
+        MCPM_CUDA(cudaMalloc(&ws->gi, sizeof(int) * 2 * n));
+        MCPM_CUDA(cudaMalloc(&ws->out, sizeof(int) * 2));
+        ws->n = n;
+    }
+    return MCPM_OK;
+}
+}  // namespace
+
+mcpm_status mcpm_sample_top_p(const float* logits, int n, float temperature, float top_p, float r, int* out,
+                              void* stream) {
+    if (!logits || !out || n <= 0 || n > (1 << 20)) return MCPM_BAD_ARG;
+    SampleWorkspace* ws = nullptr;
+    mcpm_status st = sample_workspace(n, ws);
+    if (st != MCPM_OK) return st;
+    return cuda_status(launch_sample_top_p(logits, n, temperature, top_p, r, out, ws->p, ws->gk, ws->gi,
+                                           static_cast<cudaStream_t>(stream)));
+}
+
+mcpm_status mcpm_sample(mcpm_engine* e, float temperature, float top_p, float r, int* token_out) {
+    if (!e) return MCPM_BAD_ARG;
+    if (!e->loaded) return MCPM_NOT_LOADED;
+    MCPM_CUDA(cudaSetDevice(e->device));
+    SampleWorkspace* ws = nullptr;
+    mcpm_status st = sample_workspace(e->n_vocab, ws);
+    if (st != MCPM_OK) return st;
+    MCPM_CUDA(launch_sample_top_p(e->logits, e->n_vocab, temperature, top_p, r, ws->out, ws->p, ws->gk, ws->gi,
+                                  e->stream));
+    MCPM_CUDA(cudaMemcpyAsync(e->ctl + CTL_TOKEN, ws->out, sizeof(int), cudaMemcpyDeviceToDevice, e->stream));
+    if (token_out) {
+        MCPM_CUDA(cudaMemcpyAsync(token_out, ws->out, sizeof(int), cudaMemcpyDeviceToHost, e->stream));
+        MCPM_CUDA(cudaStreamSynchronize(e->stream));
+    }
+    return MCPM_OK;
+}
+
 // ------------------------------------------------------------------ batched decode
 mcpm_status mcpm_batch_init(mcpm_engine* e, int n_seq, int max_seq) {
     if (!e || n_seq <= 0 || n_seq > BATCH_MAX || max_seq <= 0 || max_seq > MAX_SEQ) return MCPM_BAD_ARG;

@@ -121,6 +121,9 @@ struct BatchLaunch {
 };
 cudaError_t launch_batch_step(const BatchLaunch& b, cudaStream_t stream);
 
+cudaError_t launch_sample_top_p(const float* logits, int n, float temperature, float top_p, float r, int* out, float* p,
+                                uint32_t* gk, int* gi, cudaStream_t stream);
+
 cudaError_t launch_attention(const float* q, const float* k, const float* v, float* kc, float* vc, int pos, int max_seq,
                              float* out, uint8_t* out_q8k, float* part, cudaStream_t stream);
 

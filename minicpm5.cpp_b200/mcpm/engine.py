@@ -53,6 +53,8 @@ SIGNATURES = {
     "mcpm_read_kv": (I, [P, I, I, C.POINTER(F), C.POINTER(F)]),
     "mcpm_write_kv": (I, [P, I, I, I, C.POINTER(F), C.POINTER(F)]),
     "mcpm_batch_init": (I, [P, I, I]),
+    "mcpm_sample_top_p": (I, [P, I, F, F, F, P, P]),
+    "mcpm_sample": (I, [P, F, F, F, C.POINTER(I)]),
     "mcpm_batch_step_async": (I, [P, C.POINTER(I), C.POINTER(I)]),
     "mcpm_batch_read": (I, [P, C.POINTER(F), C.POINTER(I)]),
     "mcpm_model_dims": (I, [P, C.POINTER(I)]),
@@ -93,6 +95,13 @@ def load_library(build_if_needed: bool = True) -> C.CDLL:
         fn.argtypes = args
     _lib = lib
     return lib
+
+
+def sample_top_p(logits_ptr: int, n: int, temperature: float, top_p: float, r: float, out_ptr: int,
+                 stream: int = 0) -> None:
+    """Device top-p sampler (logits and out are device pointers; out receives token, kept)."""
+    check(load_library().mcpm_sample_top_p(logits_ptr, n, temperature, top_p, r, out_ptr, stream),
+          "mcpm_sample_top_p")
 
 
 def check(status: int, what: str) -> None:
@@ -164,6 +173,13 @@ class MiniCPM5Engine:
         v = np.zeros(256, np.float32)
         check(self.lib.mcpm_read_kv(self.h, layer, pos, _fptr(k), _fptr(v)), "mcpm_read_kv")
         return k, v
+
+    # reference: Sampler::sample on the last step's logits (forward with write_logits); the
+    # token also becomes the next step's input (forward with token < 0)
+    def sample(self, temperature: float = 1.0, top_p: float = 0.95, r: float = 0.5) -> int:
+        tok = C.c_int(-1)
+        check(self.lib.mcpm_sample(self.h, temperature, top_p, r, C.byref(tok)), "mcpm_sample")
+        return tok.value
 
     # batched decode: n_seq independent sequences in lockstep
     def batch_init(self, n_seq: int, max_seq: int) -> None:

@@ -663,3 +663,90 @@ void orc_set_kv(orc_state* s, int layer, const float* k, const float* v, int n_p
     memcpy(s->kc[layer], k, sizeof(float) * (size_t)n_pos * kvd);
     memcpy(s->vc[layer], v, sizeof(float) * (size_t)n_pos * kvd);
 }
+
+/* ---------------------------------------------------------------- top-p sampler */
+/* Blocked running sums over a[0..m): 1024 ranges of L = ceil(m/1024) positions; range c is
+ * summed sequentially from 0 (T_c), the prefix E_c of the T's is sequential, and the running
+ * value at position k of range c is E_c + a[cL] + ... + a[k], added in order. */
+static void blocked_running(const float* a, int m, float* run) {
+    const int L = (m + 1023) / 1024;
+    float E = 0.0f;
+    for (int c = 0; c < 1024 && c * L < m; ++c) {
+        const int b = c * L, e = b + L < m ? b + L : m;
+        float T = 0.0f;
+        for (int k = b; k < e; ++k) T += a[k];
+        float cur = E;
+        for (int k = b; k < e; ++k) {
+            cur += a[k];
+            run[k] = cur;
+        }
+        E += T;
+    }
+}
+
+typedef struct {
+    float p;
+    int i;
+} orc_pi;
+
+static int cmp_pi(const void* x, const void* y) {   /* p descending, index ascending */
+    const orc_pi* a = (const orc_pi*)x;
+    const orc_pi* b = (const orc_pi*)y;
+    if (a->p > b->p) return -1;
+    if (a->p < b->p) return 1;
+    return (a->i > b->i) - (a->i < b->i);
+}
+
+int orc_sample_top_p(const float* logits, int n, float temperature, float top_p, float r, int* kept) {
+    const float inv_temp = temperature > 0.0f ? 1.0f / temperature : 1.0f;
+    const int apply = temperature != 1.0f && temperature > 0.0f;
+    float* v = (float*)malloc(sizeof(float) * n);
+    float* run = (float*)malloc(sizeof(float) * n);
+    orc_pi* pi = (orc_pi*)malloc(sizeof(orc_pi) * n);
+    float mx = -1e9f;
+    for (int i = 0; i < n; ++i) {
+        v[i] = apply ? logits[i] * inv_temp : logits[i];
+        if (v[i] > mx) mx = v[i];
+    }
+    for (int i = 0; i < n; ++i) v[i] = orc_expf(v[i] - mx);   /* e_i */
+    blocked_running(v, n, run);
+    const float S = run[n - 1];   /* the last range's running value is the blocked total */
+    float* p = run;               /* reuse: p_i = e_i / S */
+    for (int i = 0; i < n; ++i) p[i] = v[i] / S;
+    int result, K = n;
+    if (top_p > 0.0f && top_p < 1.0f) {
+        for (int i = 0; i < n; ++i) pi[i].p = p[i], pi[i].i = i;
+        qsort(pi, n, sizeof(orc_pi), cmp_pi);
+        for (int k = 0; k < n; ++k) v[k] = pi[k].p;
+        blocked_running(v, n, run);
+        K = n;
+        for (int k = 0; k < n; ++k)
+            if (run[k] >= top_p) {
+                K = k + 1;
+                break;
+            }
+        const float C = run[K - 1];
+        for (int k = 0; k < K; ++k) v[k] = v[k] / C;
+        blocked_running(v, K, run);   /* ranges over the kept prefix */
+        result = pi[K - 1].i;
+        for (int k = 0; k < K; ++k)
+            if (r <= run[k]) {
+                result = pi[k].i;
+                break;
+            }
+    } else {
+        for (int i = 0; i < n; ++i) v[i] = p[i];
+        blocked_running(v, n, run);
+        result = n - 1;
+        for (int i = 0; i < n; ++i)
+            if (r <= run[i]) {
+                result = i;
+                break;
+            }
+    }
+    if (kept) *kept = K;
+    free(v);
+    free(run);
+    free(pi);
+    return result;
+}

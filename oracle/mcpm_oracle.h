@@ -87,6 +87,16 @@ void orc_get_kv(const orc_state* s, int layer, float* k, float* v, int n_pos);
 /* Overwrites rows [0, n_pos) of one layer's K/V cache (seeds a late-position check). */
 void orc_set_kv(orc_state* s, int layer, const float* k, const float* v, int n_pos);
 
+/* Top-p sampling (Sampler::sample, src/sampler.cpp:8-72) in the canonical form the device
+ * sampler computes: temperature as the reference (applied only for t > 0, t != 1), max from
+ * -1e9, e = orc_expf(v - max), p = e / S; order by p descending then index ascending; every
+ * fp32 sum blocked over 1024 ranges of ceil(m / 1024) positions (each range sequential from
+ * the running prefix of the range totals); keep the shortest prefix whose running sum reaches
+ * top_p (0 < top_p < 1; otherwise all tokens in index order, not renormalised); q = p / C;
+ * return the first kept token whose running sum of q is >= r, else the last kept token.
+ * kept (optional) receives the number of kept tokens. */
+int orc_sample_top_p(const float* logits, int n, float temperature, float top_p, float r, int* kept);
+
 #ifdef __cplusplus
 }
 #endif

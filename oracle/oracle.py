@@ -208,9 +208,18 @@ class Oracle:
         L.orc_get_x.argtypes = [P, F]
         L.orc_get_kv.argtypes = [P, C.c_int, F, F, C.c_int]
         L.orc_set_kv.argtypes = [P, C.c_int, F, F, C.c_int]
+        L.orc_sample_top_p.restype = C.c_int
+        L.orc_sample_top_p.argtypes = [F, C.c_int, C.c_float, C.c_float, C.c_float, C.POINTER(C.c_int)]
 
     def fp16(self, h: int) -> float:
         return self.lib.orc_fp16_to_fp32(h)
+
+    def sample_top_p(self, logits, temperature: float, top_p: float, r: float):
+        """Canonical top-p draw (token, number of tokens kept)."""
+        lg = np.ascontiguousarray(logits, np.float32)
+        kept = C.c_int(0)
+        tok = self.lib.orc_sample_top_p(_fptr(lg), lg.size, temperature, top_p, r, C.byref(kept))
+        return tok, kept.value
 
     def quantize_q8k(self, x, rounding=0, recip_d=0):
         x = np.ascontiguousarray(x, np.float32)
