@@ -5,6 +5,7 @@ batch 1 per GPU).
     python bench.py --config 1        # config 1: isolated GEMV sweep, one JSON line per case
     python bench.py --config 2        # config 2: decode after an 8192-position prefill
     python bench.py --config 3        # config 3: batched decode, 64 sequences split over the GPUs
+    python bench.py --config 4        # config 4: all-Q8_0 tensor-parallel batch-1 decode over the GPUs
 
 A step is one greedy decode token.  Each rank prefills its own seeded 128-token prompt
 (untimed), runs W warm-up tokens, then K timed tokens chained on the device (the argmax of
@@ -41,8 +42,10 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prefill length (untimed)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", type=int, default=0, choices=[0, 1, 2, 3],
-                    help="0: batch-1 decode (headline); 1: GEMV sweep; 2: long-context decode; 3: batched decode")
+    ap.add_argument("--config", type=int, default=0, choices=[0, 1, 2, 3, 4],
+                    help="0: batch-1 decode (headline); 1: GEMV sweep; 2: long-context decode; 3: batched decode; "
+                         "4: all-Q8_0 tensor-parallel decode")
+    ap.add_argument("--comm", default="p2p", choices=["p2p", "nccl"], help="config 4: exchange of partial sums")
     return ap.parse_args()
 
 
@@ -137,16 +140,17 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_baseline(model_path: str, n_prompt: int = 16, n_gen: int = 32):
+def cpu_baseline(model_path: str, n_prompt: int = 16, n_gen: int = 32, port_only: bool = False):
     """Reference CPU build (oracle/_ref, AVX2 + OpenMP) on a bounded sample of the same
-    workload, in a child process so OMP settings apply; falls back to the C restatement."""
+    workload, in a child process so OMP settings apply; falls back to the C restatement
+    (always for the all-Q8_0 model, which the reference build cannot run)."""
     cores = os.cpu_count() or 1
     code = f"""
 import sys, time, json, numpy as np
 sys.path.insert(0, {os.path.join(REPO, 'oracle')!r}); sys.path.insert(0, {os.path.join(REPO, 'minicpm5.cpp_b200')!r})
 import oracle as O
 from mcpm import synth
-kind = 'reference' if O.have_ref() else 'port'
+kind = 'reference' if (O.have_ref() and not {port_only!r}) else 'port'
 if kind == 'reference':
     e = O.RefEngine(O.Ref(), {model_path!r}, {n_prompt + n_gen + 1})
 else:
@@ -177,12 +181,25 @@ def run_reference(args, rank, world):
         return
     sys.path.insert(0, os.path.join(REPO, "oracle"))
     from mcpm import spec, synth
-    path = synth.ensure_model("q4_k_m", 0)
+    tp = args.config == 4   # all-Q8_0: the reference build cannot run it, so its C restatement is timed
+    path = synth.ensure_model("q8_0" if tp else "q4_k_m", 0)
     n_prompt = 32   # bounded prefill so the CPU run ends within minutes
     steps = args.steps
-    cb = cpu_baseline(path, n_prompt=n_prompt, n_gen=args.warmup + steps)
+    cb = cpu_baseline(path, n_prompt=n_prompt, n_gen=args.warmup + steps, port_only=tp)
     value = cb["value"]
     batch = args.config == 3   # the reference decodes one sequence at a time: its batch rate is its batch-1 rate
+    if tp:
+        line = {"impl": "reference", "metric": TP_METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+                "steps": steps, "warmup": args.warmup, "ms_per_step": round(1000.0 / value, 3) if value else None,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
+                "data": "synthetic",
+                "config": {"workload": "config4: all-Q8_0 MiniCPM5-2B greedy decode, batch 1, CPU restatement "
+                                       "(the reference build cannot run an all-Q8_0 model)",
+                           "prompt": n_prompt, "parallelism": "openmp"},
+                "cpu_baseline": cb,
+                "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
     line = {"impl": "reference", "metric": BATCH_METRIC if batch else METRIC, "value": value, "unit": "tokens/s",
             "n_gpus": args.gpus,
             "steps": steps, "warmup": args.warmup,
@@ -383,6 +400,137 @@ def run_batch(args, rank, world, local):
         pg.barrier()
         pg.destroy_process_group()
 
+TP_METRIC = "decode tokens/s (batch 1, all-Q8_0 MiniCPM5-2B shape, tensor parallel over the GPUs)"
+TP_PROMPT = 512
+TP_LAUNCHES_PER_STEP = 6 * 42 + 2   # per layer QKV, attention units, combine, o_proj, Gate+Up, down; LM head, pick
+
+
+def tp_bytes_per_step(world: int, n_pos: float) -> int:
+    """Weight + KV bytes one rank reads per token (its shards, the replicated norms and one
+    embedding row, the K/V rows of its KV head(s) at n_pos positions)."""
+    from mcpm import spec
+    rb = spec.N_EMBD // 32 * 34
+    hq, nf, ng = spec.N_HEAD // world, spec.N_FF // world, (2 if world == 1 else 1)
+    nq, nkv = hq * spec.HEAD_DIM, ng * spec.HEAD_DIM
+    layer = ((nq + 2 * nkv) * rb + spec.N_EMBD * (hq * spec.HEAD_DIM // 32 * 34) + 2 * nf * rb
+             + spec.N_EMBD * (nf // 32 * 34) + 2 * 4 * spec.N_EMBD)
+    kv = 2 * nkv * 4 * n_pos
+    return int(spec.N_LAYER * (layer + kv) + spec.N_VOCAB // world * rb + 4 * spec.N_EMBD + rb)
+
+
+def run_tp(args, rank, world, local):
+    """Config 4: one all-Q8_0 sequence decoded tensor-parallel over the ranks (every rank
+    holds 1/N of each matrix; the o_proj and down partial sums are exchanged after every
+    layer).  Seeded 512-token prompt (untimed, token by token as the reference does), W
+    warm-up tokens, then K timed greedy tokens chained on the device.  `value` = K tokens over
+    the slowest rank's device time (strong scaling: the same sequence at every N)."""
+    import datetime
+    import numpy as np
+    import torch
+    from mcpm import synth
+    from mcpm.tp import TPEngine
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))   # setup exchange, timing max
+        pg = dist
+    n_prompt = TP_PROMPT if args.prompt == PROMPT else args.prompt
+    path = synth.ensure_model("q8_0", 0)
+    if pg:
+        pg.barrier()
+    max_seq = n_prompt + args.warmup + args.steps + 80 + 64 + 8
+    eng = TPEngine(local, rank, world, max_seq, args.comm)
+    eng.load(path)
+    eng.connect(pg)
+    prompt = synth.prompt_ids(n_prompt, seed=2468)
+    tok = 0
+    for pos in range(n_prompt):   # prefill (untimed)
+        tok, _ = eng.forward(int(prompt[pos]), pos, logits=False)
+    eng.generate_async(args.warmup)
+    eng.sync()
+    first_pos = n_prompt + args.warmup
+    if pg:
+        pg.barrier()
+    stream = torch.cuda.ExternalStream(eng.stream)
+    torch.cuda.synchronize()
+    clk = ClockSampler(local) if rank == 0 else None
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    eng.generate_async(args.steps)
+    ev1.record(stream)
+    ev1.synchronize()
+    eng.sync()
+    ms = ev0.elapsed_time(ev1)
+    clocks = clk.stop() if clk else None
+    ms_max = max_over_ranks(ms, pg, device="cpu")
+    toks = eng.read_tokens(first_pos, args.steps)
+    # per-token exchange cost: a kernel-by-kernel run with timing of the collectives / waits
+    prof_steps = min(16, args.steps)
+    ms_tok_eager, ms_comm = eng.profile(prof_steps)
+    ms_comm_max = max_over_ranks(ms_comm, pg, device="cpu")
+    ms_tok_eager = max_over_ranks(ms_tok_eager, pg, device="cpu")
+    # e2e: the C-ABI call with host buffers (token in, greedy token out), synchronous per step
+    e2e_steps = min(args.steps, 64)
+    pos = first_pos + args.steps + prof_steps
+    tok = int(eng.read_tokens(pos - 1, 1)[0])
+    if pg:
+        pg.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        tok, _ = eng.forward(tok, pos, logits=False)
+        pos += 1
+    e2e_s = max_over_ranks(time.perf_counter() - t0, pg, device="cpu")
+    same = True
+    if pg:   # every rank must have produced the same greedy stream
+        digest = torch.tensor([int(np.sum(toks.astype(np.int64) * np.arange(1, len(toks) + 1)))], dtype=torch.int64)
+        lo, hi = digest.clone(), digest.clone()
+        pg.all_reduce(lo, op=pg.ReduceOp.MIN)
+        pg.all_reduce(hi, op=pg.ReduceOp.MAX)
+        same = bool(lo.item() == hi.item())
+    if rank == 0:
+        mean_pos = first_pos + (args.steps - 1) / 2 + 1
+        bytes_per_step = tp_bytes_per_step(world, mean_pos)
+        peak, peak_kind = measured_peaks()
+        per_step_ms = ms_max / args.steps
+        achieved = bytes_per_step / (per_step_ms * 1e-3) / 1e9
+        value = args.steps / (ms_max * 1e-3)
+        cb = None if (args.no_cpu_baseline or world > 1) else cpu_baseline(path, port_only=True)
+        if cb is not None:
+            cb["sample"] += "; C restatement (the reference build cannot run an all-Q8_0 model)"
+        line = {
+            "metric": TP_METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step_ms, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32 (Q8_0 weights)",
+            "data": "synthetic (seeded random-init all-Q8_0 GGUF)",
+            "config": {"workload": "config4: all-Q8_0 MiniCPM5-2B greedy decode, batch 1, tensor parallel",
+                       "prompt": n_prompt, "positions": [first_pos, first_pos + args.steps - 1],
+                       "parallelism": f"tp{world}", "exchange": args.comm,
+                       "l2": f"inputs larger than L2 ({bytes_per_step / 1e6:.0f} MB per GPU per token)"},
+            "per_token_latency_ms": round(per_step_ms, 4),
+            "comm": {"ms_per_token": round(ms_comm_max, 4), "eager_ms_per_token": round(ms_tok_eager, 4),
+                     "fraction": round(ms_comm_max / ms_tok_eager, 4) if ms_tok_eager else None,
+                     "how": ("device time of the NCCL collectives" if args.comm == "nccl" else
+                             "time the consuming kernels waited for the exchanged partial sums") +
+                            f" over {prof_steps} kernel-by-kernel steps, max over ranks",
+                     "ranks_agree": same},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
+                         "kernel": "token sequence (k_tp_gemv, attention)",
+                         "algorithmic_bytes_per_step_per_gpu": bytes_per_step},
+            "cpu_baseline": cb,
+            "e2e": {"value": round(e2e_steps / e2e_s, 2), "unit": "tokens/s",
+                    "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 32},
+            "gpu_launches": TP_LAUNCHES_PER_STEP * args.steps,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if pg:
+        pg.barrier()   # no rank frees its receive buffer while a peer may still store into it
+    eng.close()
+    if pg:
+        pg.destroy_process_group()
+
 
 def main():
     args = parse()
@@ -396,6 +544,9 @@ def main():
         return
     if args.config == 3:
         run_batch(args, rank, world, local)
+        return
+    if args.config == 4:
+        run_tp(args, rank, world, local)
         return
     if args.config == 2 and args.prompt == PROMPT:   # config 2: 8192-position context
         args.prompt = 8192

@@ -109,6 +109,65 @@ void* mcpm_engine_stream(mcpm_engine* e);
 int mcpm_engine_n_ctas(mcpm_engine* e);
 void mcpm_engine_destroy(mcpm_engine* e);
 
+/* ------------------------------------------------------------------ tensor-parallel engine
+ * Batch-1 decode of an all-Q8_0 model over `world` GPUs (1, 2, 4 or 8), one engine per GPU
+ * (one process or host thread each).  The reference has no multi-GPU path; this is the
+ * Megatron partition of MiniCPM5Engine::forward (model.cpp:142-242) with every projection
+ * gemv_q8_0 (ops.cpp:58-79): QKV, Gate+Up and the LM head split by output rows, o_proj and
+ * down by input columns, their partial sums exchanged between the ranks after each of the
+ * two (84 exchanges per token for 42 layers), and the greedy argmax reduced over the ranks'
+ * vocabulary slices.  Every rank returns the same token.
+ * Setup: rank 0 makes an NCCL id (MCPM_TP_NCCL) or every rank makes an IPC handle of its
+ * receive buffer after loading (MCPM_TP_P2P); the caller distributes them (any host
+ * channel) and every rank calls mcpm_tp_connect with the full set. */
+typedef struct mcpm_tp mcpm_tp;
+enum { MCPM_TP_P2P = 0, MCPM_TP_NCCL = 1 };
+typedef struct {
+    int device;    /* CUDA device of this rank */
+    int rank;      /* 0 .. world-1 */
+    int world;     /* 1, 2, 4 or 8 */
+    int max_seq;   /* KV-cache positions, <= 16384 */
+    int comm;      /* MCPM_TP_P2P: epoch-tagged partial sums stored into every rank's receive
+                      buffer over CUDA IPC and summed in rank order by the consuming kernel;
+                      MCPM_TP_NCCL: ncclAllReduce / ncclAllGather (libnccl.so.2 at run time) */
+    int eager;     /* 0: each token is one CUDA graph launch; 1: kernels launched one by one */
+    int reserved[2];
+} mcpm_tp_config;
+/* 128-byte NCCL unique id (rank 0, MCPM_TP_NCCL). */
+mcpm_status mcpm_tp_nccl_id(void* id128);
+mcpm_status mcpm_tp_create(const mcpm_tp_config* cfg, mcpm_tp** out);
+/* Loads this rank's shards of an all-Q8_0 MiniCPM5 GGUF (MCPM_UNSUPPORTED_TYPE for other
+ * mixes) and allocates its KV cache; the embedding and norms are replicated. */
+mcpm_status mcpm_tp_load_gguf(mcpm_tp* t, const char* path);
+/* 64-byte cudaIpcMemHandle_t of this rank's receive buffer (MCPM_TP_P2P, after load). */
+mcpm_status mcpm_tp_ipc_handle(mcpm_tp* t, void* handle64);
+/* nccl_id128: rank 0's id (MCPM_TP_NCCL); ipc_handles: world x 64 bytes in rank order
+ * (MCPM_TP_P2P).  A single-GPU engine needs neither. */
+mcpm_status mcpm_tp_connect(mcpm_tp* t, const void* nccl_id128, const void* ipc_handles);
+/* One decode step on every rank (each rank calls it with the same arguments): token at pos,
+ * or token < 0 for the previous step's greedy token at the next position.  logits_slice
+ * (host, optional) receives this rank's vocabulary rows [lo, hi) (mcpm_tp_info);
+ * next_token (host, optional) the greedy token over the whole vocabulary. */
+mcpm_status mcpm_tp_forward(mcpm_tp* t, int token, int pos, float* logits_slice, int* next_token);
+/* n greedy steps chained on the device after the last step, without host round trips;
+ * mcpm_tp_read_tokens (which waits) returns the tokens, logged by the position whose step
+ * produced them.  Errors surface at mcpm_tp_sync / mcpm_tp_read_tokens. */
+mcpm_status mcpm_tp_generate_async(mcpm_tp* t, int n);
+mcpm_status mcpm_tp_sync(mcpm_tp* t);
+mcpm_status mcpm_tp_read_tokens(mcpm_tp* t, int pos0, int n, int* tokens);
+/* n_layer, n_vocab, vocabulary rows [lo, hi), first query head and head count, first FFN
+ * row and row count of this rank. */
+mcpm_status mcpm_tp_info(mcpm_tp* t, int info[8]);
+/* Zeroes the KV cache and the token log; positions restart at 0. */
+mcpm_status mcpm_tp_reset(mcpm_tp* t);
+/* n greedy steps launched kernel by kernel with timing: ms_token = mean device time per
+ * step; ms_comm = per step, the device time of the NCCL collectives (MCPM_TP_NCCL) or the
+ * time CTA 0 of the consuming kernels waited for the exchanged partials (MCPM_TP_P2P). */
+mcpm_status mcpm_tp_profile(mcpm_tp* t, int n, float* ms_token, float* ms_comm);
+/* The engine's CUDA stream (cudaStream_t). */
+void* mcpm_tp_stream(mcpm_tp* t);
+void mcpm_tp_destroy(mcpm_tp* t);
+
 /* ------------------------------------------------------------------ ops (device pointers)
  * Block layouts are the reference's: block_q4_K 144 B, block_q6_K 210 B, block_q8_0 34 B,
  * block_q8_K 292 B (include/ops.h:33-65).  `type` is the ggml type id (12 = Q4_K,

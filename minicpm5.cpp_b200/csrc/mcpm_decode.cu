@@ -1371,7 +1371,62 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_att_combine(const DecodePara
 
 #include "mcpm_batch.cuh"
 
+// Tensor-parallel attention (one rank's KV group(s) and head pairs).  The position is read
+// from device memory so a whole token can be captured in one CUDA graph; the grid covers the
+// largest chunk count of the cache and units past the current one return at once.
+__global__ void __launch_bounds__(DEC_THREADS, 1) k_tp_att_units(DecodeParams p, const int* pos, int g0) {
+    grid_dep_launch();
+    grid_dep_wait();
+    p.pos = *pos;
+    const int n = p.pos + 1, P = 32 * ((n + 2047) / 2048), C = (n + P - 1) / P;
+    const int c = blockIdx.x, g = g0 + blockIdx.y;
+    if (c >= C) return;
+    const Smem sm;
+    const int t0 = c * P, np = min(t0 + P, n) - t0;
+    if (P == 32)
+        attention_unit32(p, sm, 0, g, c, t0, np, 1u, false);
+    else
+        attention_unit_big(p, sm, 0, g, c, t0, np, 1u, false);
+}
+
+__global__ void __launch_bounds__(DEC_THREADS, 1) k_tp_att_combine(DecodeParams p, const int* pos, int b0) {
+    grid_dep_launch();
+    grid_dep_wait();
+    p.pos = *pos;
+    const Smem sm;
+    combine_pair(p, sm, 0, b0 + blockIdx.x, 1u);
+}
+
 }  // namespace
+
+cudaError_t launch_tp_attention(const DecodeParams& p, const int* pos_dev, int g0, int ng, int b0, int nb,
+                                cudaStream_t stream) {
+    static int prepared_dev = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (prepared_dev != dev) {
+        cudaError_t e = cudaFuncSetAttribute(k_tp_att_units, cudaFuncAttributeMaxDynamicSharedMemorySize, SM_BYTES);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k_tp_att_combine, cudaFuncAttributeMaxDynamicSharedMemorySize, SM_BYTES);
+        if (e != cudaSuccess) return e;
+        prepared_dev = dev;
+    }
+    const int cmax = std::min(ATT_MAX_CHUNKS, (p.max_seq + 31) / 32);   // most chunks of any length <= max_seq
+    cudaLaunchAttribute attr[1];   // programmatic dependents of the preceding kernel
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.blockDim = dim3(DEC_THREADS);
+    cfg.dynamicSmemBytes = SM_BYTES;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cfg.gridDim = dim3(cmax, ng);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k_tp_att_units, p, pos_dev, g0);
+    if (e != cudaSuccess) return e;
+    cfg.gridDim = dim3(nb);
+    return cudaLaunchKernelEx(&cfg, k_tp_att_combine, p, pos_dev, b0);
+}
 
 size_t decode_smem_bytes() { return SM_BYTES; }
 

@@ -115,6 +115,11 @@ __device__ __forceinline__ float ld_cg_f32(const float* p) {
     asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p));
     return v;
 }
+// Programmatic dependent launch: wait until the preceding kernel in the stream has finished
+// and its writes are visible (returns at once without a programmatic dependency), and allow
+// the next kernel to start launching its CTAs.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 // Epoch-tagged element (value + epoch in one naturally aligned 64-bit word, which is
 // single-copy atomic): the consumer's load is also its synchronisation, with no fence on
 // the producer side and no separate flag round trip.

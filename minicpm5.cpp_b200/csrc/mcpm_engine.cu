@@ -134,10 +134,12 @@ void free_model(mcpm_engine* e) {
     e->loaded = false;
 }
 
+}  // namespace
+
 // RoPE factors: theta_i = base^(-(i * (1/head_dim))), angle = theta * pos, (cos, sin)
 // from the C library (the reference build's pow(base, -(i/head_dim)) / cosf / sinf,
 // ops.cpp:502-516).  The CPU restatement computes the same table.
-__attribute__((noinline)) void rope_row(int pos, float base, float2* out) {
+__attribute__((noinline)) void mcpm::rope_row(int pos, float base, float2* out) {
     const float inv = 1.0f / static_cast<float>(HEAD_DIM);
     for (int i = 0; i < HEAD_DIM; i += 2) {
         const float theta = powf(base, -(static_cast<float>(i) * inv));
@@ -147,6 +149,8 @@ __attribute__((noinline)) void rope_row(int pos, float base, float2* out) {
         out[i / 2] = make_float2(c, s);
     }
 }
+
+namespace {
 
 // Largest per-CTA byte counts of the decode kernel's weight phases for n CTAs.
 bool phases_fit(const mcpm_engine* e, int n, std::string& why) {

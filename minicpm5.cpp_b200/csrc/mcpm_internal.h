@@ -96,6 +96,9 @@ struct DecodeParams {
     int write_logits;
 };
 
+// RoPE (cos, sin) factors of one position: HEAD_DIM / 2 pairs (host, C library functions).
+void rope_row(int pos, float base, float2* out);
+
 size_t decode_smem_bytes();
 cudaError_t decode_prepare();
 cudaError_t launch_decode(const DecodeParams& p, int n_ctas, cudaStream_t stream);
@@ -123,6 +126,11 @@ cudaError_t launch_batch_step(const BatchLaunch& b, cudaStream_t stream);
 
 cudaError_t launch_sample_top_p(const float* logits, int n, float temperature, float top_p, float r, int* out, float* p,
                                 uint32_t* gk, int* gi, cudaStream_t stream);
+
+// Attention of one tensor-parallel rank: units of KV groups g0 .. g0+ng-1, combine of head
+// pairs b0 .. b0+nb-1; p.pos is taken from pos_dev on the device.
+cudaError_t launch_tp_attention(const DecodeParams& p, const int* pos_dev, int g0, int ng, int b0, int nb,
+                                cudaStream_t stream);
 
 cudaError_t launch_attention(const float* q, const float* k, const float* v, float* kc, float* vc, int pos, int max_seq,
                              float* out, uint8_t* out_q8k, float* part, cudaStream_t stream);

@@ -4,6 +4,7 @@
 // decode path's arithmetic.
 #include "mcpm_device.cuh"
 #include "mcpm_internal.h"
+#include "mcpm_q80.cuh"
 
 namespace mcpm {
 namespace {
@@ -135,98 +136,23 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
     }
 }
 
-// ---- Q8_0 x fp32 GEMV (gemv_q8_0, ops.cpp:58-79, in the reference build's evaluation order:
-// per 32-block eight lanes k with A_k = fma(q_k, x_k, q_{k+8} x_{k+8}),
-// B_k = fma(q_{k+16}, x_{k+16}, q_{k+24} x_{k+24}), v_k = B_k + A_k, then the pairs
-// (k, k+4), (k, k+2), (k, k+1); row = fma(fp16 d, local, row) over the blocks in order).
-// Each CTA streams its row range through a 3-slot TMA ring; pass 1 gives one thread per
-// (row, block) its local sum, pass 2 one thread per row the block chain.
-constexpr int Q80_SLOTS = 3;
-constexpr int Q80_SLOT_BYTES = 40960;
-constexpr int Q80_SLOT_STRIDE = Q80_SLOT_BYTES + 128;   // readable tail for the funnel-shifted reads
-constexpr int Q80_MAX_TASKS = 1536;
-constexpr int Q80_MAX_COLS = 8192;
-
-__global__ void __launch_bounds__(OP_THREADS, 1)
+// ---- Q8_0 x fp32 GEMV (mcpm_q80.cuh): each CTA streams a contiguous row range.
+__global__ void __launch_bounds__(Q80_THREADS, 1)
     k_gemv_q8_0(const uint8_t* __restrict__ w, const float* __restrict__ x, float* __restrict__ y, int rows, int nb,
                 unsigned* err) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* ring = smem_raw;
-    float* xs = reinterpret_cast<float*>(ring + Q80_SLOTS * Q80_SLOT_STRIDE);
-    float2* part = reinterpret_cast<float2*>(xs + Q80_MAX_COLS);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(part + Q80_MAX_TASKS);
-    const int tid = threadIdx.x, cols = nb * 32, rb = nb * Q8_0_BYTES;
-    const int sr = min(Q80_SLOT_BYTES / rb, Q80_MAX_TASKS / nb);
+    const Q80Smem s(smem_raw);
+    const int tid = threadIdx.x, cols = nb * 32;
+    const int sr = q80_pick_stage(nb, (rows + gridDim.x - 1) / gridDim.x);
     const int r0 = (rows * blockIdx.x) / gridDim.x, r1 = (rows * (blockIdx.x + 1)) / gridDim.x;
-    const int nstages = (r1 - r0 + sr - 1) / sr;
+    if (tid == 0) q80_start(w, r0, r1, nb, sr, s);
     for (int i = tid; i < cols / 4; i += blockDim.x)
-        reinterpret_cast<float4*>(xs)[i] = reinterpret_cast<const float4*>(x)[i];
-    auto issue = [&](int st) {
-        const int slot = st % Q80_SLOTS, a = r0 + st * sr, n = min(sr, r1 - a);
-        const uint32_t bytes = static_cast<uint32_t>(n) * rb;
-        mbar_expect_tx(&bars[slot], bytes);
-        bulk_g2s(ring + slot * Q80_SLOT_STRIDE, w + static_cast<size_t>(a) * rb, bytes, &bars[slot]);
-    };
-    if (tid == 0) {
-        for (int i = 0; i < Q80_SLOTS; ++i) mbar_init(&bars[i], 1);
-        fence_mbar_init();
-        for (int st = 0; st < min(nstages, Q80_SLOTS); ++st) issue(st);
-    }
+        *reinterpret_cast<float4*>(s.xs + q80_xpos(4 * i)) = reinterpret_cast<const float4*>(x)[i];
     __syncthreads();
-    for (int st = 0; st < nstages; ++st) {
-        const int slot = st % Q80_SLOTS, a = r0 + st * sr, n = min(sr, r1 - a);
-        const uint8_t* sw = ring + slot * Q80_SLOT_STRIDE;
-        const bool ok = mbar_wait(&bars[slot], (st / Q80_SLOTS) & 1, err);
-        if (__syncthreads_or(!ok)) return;
-        for (int t = tid; t < n * nb; t += blockDim.x) {
-            const int b = t % nb;
-            const uint8_t* blk = sw + static_cast<size_t>(t) * Q8_0_BYTES;
-            const float d = h2f(*reinterpret_cast<const uint16_t*>(blk));
-            const uintptr_t qa = reinterpret_cast<uintptr_t>(blk + 2);
-            const uint32_t* base = reinterpret_cast<const uint32_t*>(qa & ~uintptr_t(3));
-            const uint32_t sh = static_cast<uint32_t>(qa & 3) * 8;
-            uint32_t qw[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) qw[i] = __funnelshift_r(base[i], base[i + 1], sh);
-            const float* xb = xs + 32 * b;
-            float q[32], xv[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) q[i] = static_cast<float>(sbyte(qw[i >> 2], i & 3));
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const float4 f = *reinterpret_cast<const float4*>(xb + 4 * i);
-                xv[4 * i] = f.x, xv[4 * i + 1] = f.y, xv[4 * i + 2] = f.z, xv[4 * i + 3] = f.w;
-            }
-            float v[8];
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const float A = __fmaf_rn(q[k], xv[k], __fmul_rn(q[k + 8], xv[k + 8]));
-                const float B = __fmaf_rn(q[k + 16], xv[k + 16], __fmul_rn(q[k + 24], xv[k + 24]));
-                v[k] = __fadd_rn(B, A);
-            }
-            float c[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) c[k] = __fadd_rn(v[k + 4], v[k]);
-            const float local = __fadd_rn(__fadd_rn(c[3], c[1]), __fadd_rn(c[2], c[0]));
-            part[t] = make_float2(local, d);
-        }
-        __syncthreads();
-        for (int r = tid; r < n; r += blockDim.x) {
-            float acc = 0.0f;
-            for (int b = 0; b < nb; ++b) {
-                const float2 ld = part[r * nb + b];
-                acc = __fmaf_rn(ld.y, ld.x, acc);
-            }
-            y[a + r] = acc;
-        }
-        __syncthreads();
-        if (tid == 0 && st + Q80_SLOTS < nstages) issue(st + Q80_SLOTS);
-    }
+    q80_run(w, r0, r1, nb, sr, s, err, [&](int r, float v, float) { y[r] = v; });
 }
 
-size_t gemv_q8_0_smem_bytes() {
-    return Q80_SLOTS * Q80_SLOT_STRIDE + Q80_MAX_COLS * 4 + Q80_MAX_TASKS * 8 + Q80_SLOTS * 8;
-}
+size_t gemv_q8_0_smem_bytes() { return q80_smem_bytes(); }
 
 size_t gemv_smem_bytes() {
     return RING_SLOTS * SLOT_STRIDE + ((sizeof(XQSmem) + 127) & ~size_t(127)) + MAX_TASKS * PART_WORDS * 4 +
@@ -256,7 +182,7 @@ cudaError_t op_gemv_q8_0(const void* w, const float* x, float* y, int rows, int 
         prepared[dev] = true;
     }
     const int grid = rows < n_sms[dev] ? rows : n_sms[dev];
-    k_gemv_q8_0<<<grid, OP_THREADS, gemv_q8_0_smem_bytes(), s>>>(static_cast<const uint8_t*>(w), x, y, rows, cols / 32,
+    k_gemv_q8_0<<<grid, Q80_THREADS, gemv_q8_0_smem_bytes(), s>>>(static_cast<const uint8_t*>(w), x, y, rows, cols / 32,
                                                                   d_err[dev]);
     return cudaGetLastError();
 }

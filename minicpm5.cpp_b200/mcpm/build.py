@@ -48,7 +48,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
         subprocess.run(cmd, check=True)
         objs.append(obj)
     tmp = LIB + ".tmp"
-    subprocess.run([NVCC] + ARCH + ["-shared", "-o", tmp] + objs + ["-lcudart"], check=True)
+    subprocess.run([NVCC] + ARCH + ["-shared", "-o", tmp] + objs + ["-lcudart", "-ldl"], check=True)
     os.replace(tmp, LIB)
     return LIB
 

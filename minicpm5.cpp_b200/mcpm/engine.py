@@ -73,6 +73,20 @@ SIGNATURES = {
     "mcpm_attention_noalloc": (I, [P, P, P, P, P, I, I, P, P, P]),
     "mcpm_trace_enable": (I, [P, I]),
     "mcpm_trace_read": (I, [P, C.POINTER(C.c_uint64), I]),
+    "mcpm_tp_nccl_id": (I, [P]),
+    "mcpm_tp_create": (I, [P, C.POINTER(P)]),
+    "mcpm_tp_load_gguf": (I, [P, C.c_char_p]),
+    "mcpm_tp_ipc_handle": (I, [P, P]),
+    "mcpm_tp_connect": (I, [P, P, P]),
+    "mcpm_tp_forward": (I, [P, I, I, C.POINTER(F), C.POINTER(I)]),
+    "mcpm_tp_generate_async": (I, [P, I]),
+    "mcpm_tp_sync": (I, [P]),
+    "mcpm_tp_read_tokens": (I, [P, I, I, C.POINTER(I)]),
+    "mcpm_tp_info": (I, [P, C.POINTER(I)]),
+    "mcpm_tp_reset": (I, [P]),
+    "mcpm_tp_profile": (I, [P, I, C.POINTER(F), C.POINTER(F)]),
+    "mcpm_tp_stream": (P, [P]),
+    "mcpm_tp_destroy": (None, [P]),
 }
 
 
