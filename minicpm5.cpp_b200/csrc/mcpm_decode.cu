@@ -12,7 +12,7 @@
 //   D    : SwiGLU output -> Q8_K (every CTA), down GEMV + residual (model.cpp:220-225)
 // then the LM head (final RMSNorm, Q8_K ties-to-even, GEMV, greedy argmax).
 //
-// Weights move with TMA bulk copies (cp.async.bulk, no multicast) into two shared
+// Weights move with TMA bulk copies (cp.async.bulk into this CTA's own shared memory) into two shared
 // buffers; the copy for weight phase w+1 is issued when phase w starts, so HBM keeps
 // streaming through the grid barriers.  All waits are bounded (~1 s) and report
 // ERR_TIMEOUT instead of hanging.

@@ -64,7 +64,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bulk global->shared copy (TMA, no tensor map, no multicast).  dst, src 16-byte aligned,
+// Bulk global->shared copy (TMA, no tensor map, this CTA's shared memory only).  dst, src 16-byte aligned,
 // bytes a multiple of 16; completion is signalled on `bar` as transaction bytes.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile(

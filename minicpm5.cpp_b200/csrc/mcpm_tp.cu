@@ -63,8 +63,10 @@ constexpr int TP_MAX_WORLD = 8;
 constexpr int PRO_PLAIN = 0, PRO_NORM = 1, PRO_SWIGLU = 2;
 constexpr int EPI_STORE = 0, EPI_ROPE = 1, EPI_PUBLISH = 2, EPI_ARGMAX = 3;
 constexpr unsigned STEP_ARGMAX = 255;
-// Waits on other GPUs: the ranks launch independently, so allow for host-side skew.
-constexpr unsigned long long PEER_WAIT_NS = 10000000000ull;
+// Waits on other GPUs: the ranks launch independently, so allow for host-side skew.  Once one
+// wait of the engine has timed out (ERR_TIMEOUT in the control word), every later wait gives up
+// at once, so a rank that stopped costs one bound, not one per exchange.
+constexpr unsigned long long PEER_WAIT_NS = 5000000000ull;
 
 struct TPCtl {
     int token;         // input token of the next step
@@ -132,11 +134,12 @@ __device__ __forceinline__ bool load_epoch_sys(const unsigned long long* src, un
             __nanosleep(32);
 #pragma unroll
             for (int i = 0; i < N2; ++i) w[i] = ld_epoch2_sys(src + 2 * i);
-            if (!ready() && globaltimer() - t0 > PEER_WAIT_NS) {
+            if (ready()) break;
+            if ((ld_relaxed_u32(err) & ERR_TIMEOUT) || globaltimer() - t0 > PEER_WAIT_NS) {
                 atomicOr(err, ERR_TIMEOUT);
                 return false;
             }
-        } while (!ready());
+        } while (true);
     }
 #pragma unroll
     for (int i = 0; i < N2; ++i) {
