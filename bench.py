@@ -46,6 +46,8 @@ def parse():
                     help="0: batch-1 decode (headline); 1: GEMV sweep; 2: long-context decode; 3: batched decode; "
                          "4: all-Q8_0 tensor-parallel decode")
     ap.add_argument("--comm", default="p2p", choices=["p2p", "nccl"], help="config 4: exchange of partial sums")
+    ap.add_argument("--batch-gemm", default="mma", choices=["mma", "tcgen05"],
+                    help="config 3: batched GEMM kernel (int8 mma.sync or tcgen05; identical results)")
     return ap.parse_args()
 
 
@@ -327,7 +329,7 @@ def run_batch(args, rank, world, local):
     if pg:
         pg.barrier()
     max_seq = n_prompt + args.warmup + args.steps + 80
-    eng = E.MiniCPM5Engine(device=local, max_seq=64)
+    eng = E.MiniCPM5Engine(device=local, max_seq=64, batch_gemm=1 if args.batch_gemm == "tcgen05" else 0)
     if not eng.load_model(path):
         raise SystemExit("load_model failed")
     eng.batch_init(n, max_seq)
@@ -377,10 +379,11 @@ def run_batch(args, rank, world, local):
         line = {
             "metric": BATCH_METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step_ms, 4),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8 mma / fp32",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": ("int8 tcgen05" if args.batch_gemm == "tcgen05" else "int8 mma") + " / fp32",
             "data": "synthetic (seeded random-init GGUF, Q4_K_M layout)",
             "config": {"workload": "config3: MiniCPM5-2B Q4_K_M batched greedy decode, 64 sequences",
-                       "sequences_per_gpu": n, "prompt": n_prompt,
+                       "sequences_per_gpu": n, "prompt": n_prompt, "gemm": args.batch_gemm,
                        "positions": [first_pos, first_pos + args.steps - 1],
                        "parallelism": f"dp{world} (sequences split over GPUs)",
                        "l2": "inputs larger than L2 (1.41 GB of weights + K/V per step)"},

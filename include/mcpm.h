@@ -38,11 +38,15 @@ const char* mcpm_status_string(mcpm_status s);
 /* ------------------------------------------------------------------ engine */
 typedef struct mcpm_engine mcpm_engine;
 
+enum { MCPM_GEMM_MMA = 0, MCPM_GEMM_TCGEN05 = 1 };
 typedef struct {
     int device;      /* CUDA device ordinal */
     int max_seq;     /* KV-cache positions (reference init_kv_cache(max_seq_len), model.cpp:17-24); <= 16384 */
     int n_ctas;      /* persistent CTAs of the decode kernel; 0 = one per SM */
-    int reserved[5];
+    int batch_gemm;  /* batched-decode GEMM (mcpm_batch_*): MCPM_GEMM_MMA (0, int8 mma.sync, the faster
+                        today) or MCPM_GEMM_TCGEN05 (1, 5th-generation tensor cores, TMEM accumulators);
+                        both give bit-identical results */
+    int reserved[4];
 } mcpm_config;
 
 /* Creates an engine bound to cfg->device (MiniCPM5Engine constructor + init_kv_cache). */

@@ -1457,6 +1457,7 @@ cudaError_t launch_batch_step(const BatchLaunch& b, cudaStream_t stream) {
             e = cudaFuncSetAttribute(k_b_att_combine, cudaFuncAttributeMaxDynamicSharedMemorySize, COMBINE_SMEM);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(k_b_gemm8, cudaFuncAttributeMaxDynamicSharedMemorySize, GA_BYTES);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(k_b_gemm24, cudaFuncAttributeMaxDynamicSharedMemorySize, GB_BYTES);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(k_b_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_BYTES);
         if (e != cudaSuccess) return e;
         prepared_dev = dev;
     }
@@ -1471,16 +1472,23 @@ cudaError_t launch_batch_step(const BatchLaunch& b, cudaStream_t stream) {
     const int n = b.n_seq;
     const int nmax = b.max_pos + 1, Pmax = 32 * ((nmax + 2047) / 2048), Cmax = (nmax + Pmax - 1) / Pmax;
     const int unit_smem = Pmax == 32 ? 24576 : UNIT_SMEM_BIG;
+    const bool gemm_kind = b.tcgen05 != 0;
     auto gemm = [&](std::initializer_list<BGemmSeg> segs, int nb, float* y, int y_stride) {
         BGemmArgs g{};
+        const int rows_per_tile = gemm_kind ? TC_M : BG_ROWS;
         int tiles = 0, i = 0;
         for (BGemmSeg sg : segs) {
             sg.tile0 = tiles;
-            tiles += (sg.rows + BG_ROWS - 1) / BG_ROWS;
+            tiles += (sg.rows + rows_per_tile - 1) / rows_per_tile;
             g.seg[i++] = sg;
         }
         g.nseg = i, g.ntiles = tiles, g.nb = nb;
-        g.aqs = b.aqs, g.ad = b.ad, g.abs = b.abs, g.y = y, g.y_stride = y_stride, g.n_seq = n;
+        g.aqs = b.aqs, g.ad = b.ad, g.abs = b.abs, g.y = y, g.y_stride = y_stride, g.n_seq = n, g.err = b.err;
+        if (gemm_kind) {
+            const int total = tiles * ((n + TC_NT - 1) / TC_NT);
+            k_b_gemm_tc<<<std::min(total, b.n_sm), TC_THREADS, TC_BYTES, stream>>>(g);
+            return;
+        }
         if (nb == 8)
             k_b_gemm8<<<std::min(tiles, b.n_sm), BG_THREADS, GA_BYTES, stream>>>(g);
         else

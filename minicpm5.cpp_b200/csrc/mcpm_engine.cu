@@ -36,6 +36,7 @@ struct mcpm_engine {
     int n_sm = 0;
     int n_ctas = 0;
     int req_ctas = 0;
+    int batch_gemm = 0;   // MCPM_GEMM_MMA / MCPM_GEMM_TCGEN05
     bool loaded = false;
     GGUFFile gguf;
     uint8_t* arena = nullptr;
@@ -293,12 +294,14 @@ mcpm_status mcpm_engine_create(const mcpm_config* cfg, mcpm_engine** out) {
     if (!cfg || !out) return MCPM_BAD_ARG;
     *out = nullptr;
     if (cfg->max_seq < 0 || cfg->max_seq > MAX_SEQ || cfg->n_ctas < 0) return MCPM_BAD_ARG;
+    if (cfg->batch_gemm != MCPM_GEMM_MMA && cfg->batch_gemm != MCPM_GEMM_TCGEN05) return MCPM_BAD_ARG;
     int ndev = 0;
     MCPM_CUDA(cudaGetDeviceCount(&ndev));
     if (cfg->device < 0 || cfg->device >= ndev) return MCPM_BAD_ARG;
     auto e = std::make_unique<mcpm_engine>();
     e->device = cfg->device;
     e->req_ctas = cfg->n_ctas;
+    e->batch_gemm = cfg->batch_gemm;
     e->max_seq = 0;
     MCPM_CUDA(cudaSetDevice(e->device));
     MCPM_CUDA(cudaDeviceGetAttribute(&e->n_sm, cudaDevAttrMultiProcessorCount, e->device));
@@ -730,7 +733,7 @@ mcpm_status mcpm_batch_step_async(mcpm_engine* e, const int* tokens, const int* 
     if (pos) MCPM_CUDA(cudaMemcpyAsync(e->b_pos, pos, n * sizeof(int), cudaMemcpyHostToDevice, e->stream));
     BatchLaunch b{};
     b.n_seq = n, b.max_seq = e->b_max_seq, b.n_layer = e->n_layer, b.n_vocab = e->n_vocab, b.lm_type = e->lm_type;
-    b.max_pos = max_pos, b.chain = 1, b.n_sm = e->n_sm;
+    b.max_pos = max_pos, b.chain = 1, b.n_sm = e->n_sm, b.tcgen05 = e->batch_gemm == MCPM_GEMM_TCGEN05;
     b.layers = e->layers.data(), b.embd = e->embd, b.out_norm = e->out_norm, b.lm = e->lm, b.rope = e->b_rope;
     b.kc = e->b_kc, b.vc = e->b_vc, b.x = e->b_x, b.y = e->b_y, b.q = e->b_q, b.att_part = e->b_part;
     b.att = e->b_att, b.logits = e->b_logits, b.aqs = e->b_aqs, b.ad = e->b_ad, b.abs = e->b_abs;

@@ -110,6 +110,7 @@ constexpr size_t ATT_PART_FLOATS = static_cast<size_t>(N_HEAD) * ATT_MAX_CHUNKS 
 // Batched decode (n_seq independent sequences): one step of every sequence.
 struct BatchLaunch {
     int n_seq, max_seq, n_layer, n_vocab, lm_type, max_pos, chain, n_sm;
+    int tcgen05;              // GEMMs on k_b_gemm_tc instead of the mma.sync kernels
     const LayerDev* layers;   // host array; weight pointers are device pointers
     const uint8_t* embd;
     const float* out_norm;

@@ -33,7 +33,8 @@ class MCPMError(RuntimeError):
 
 
 class mcpm_config(C.Structure):
-    _fields_ = [("device", C.c_int), ("max_seq", C.c_int), ("n_ctas", C.c_int), ("reserved", C.c_int * 5)]
+    _fields_ = [("device", C.c_int), ("max_seq", C.c_int), ("n_ctas", C.c_int), ("batch_gemm", C.c_int),
+                ("reserved", C.c_int * 4)]
 
 
 P, I, F = C.c_void_p, C.c_int, C.c_float
@@ -131,9 +132,10 @@ def _fptr(a: np.ndarray):
 class MiniCPM5Engine:
     """Device engine behind the reference's MiniCPM5Engine interface."""
 
-    def __init__(self, device: int = 0, max_seq: int = 0, n_ctas: int = 0):
+    def __init__(self, device: int = 0, max_seq: int = 0, n_ctas: int = 0, batch_gemm: int = 0):
+        """batch_gemm: 0 = int8 mma.sync batched GEMMs, 1 = tcgen05 (bit-identical results)."""
         self.lib = load_library()
-        cfg = mcpm_config(device, max_seq, n_ctas)
+        cfg = mcpm_config(device, max_seq, n_ctas, batch_gemm)
         h = P()
         check(self.lib.mcpm_engine_create(C.byref(cfg), C.byref(h)), "mcpm_engine_create")
         self.h = h

@@ -8,12 +8,14 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("n_seq,n_prompt,n_gen,check", [(5, 6, 4, None), (64, 2, 1, (0, 9, 31, 40, 63))])
-def test_batch_decode_bitexact(cuda, oracle, model_path, n_seq, n_prompt, n_gen, check):
+@pytest.mark.parametrize("gemm", [0, 1], ids=["mma", "tcgen05"])
+@pytest.mark.parametrize("n_seq,n_prompt,n_gen,check", [(5, 6, 4, None), (64, 2, 1, (0, 9, 31, 40, 63)),
+                                                        (37, 2, 1, (0, 31, 32, 36))])
+def test_batch_decode_bitexact(cuda, oracle, model_path, n_seq, n_prompt, n_gen, check, gemm):
     import oracle as O
     from mcpm import engine as E
     max_seq = 32
-    e = E.MiniCPM5Engine(device=0, max_seq=max_seq)
+    e = E.MiniCPM5Engine(device=0, max_seq=max_seq, batch_gemm=gemm)
     assert e.load_model(model_path)
     e.batch_init(n_seq, max_seq)
     seqs = list(range(n_seq)) if check is None else list(check)
