@@ -46,6 +46,8 @@ def parse():
                     help="0: batch-1 decode (headline); 1: GEMV sweep; 2: long-context decode; 3: batched decode; "
                          "4: all-Q8_0 tensor-parallel decode")
     ap.add_argument("--comm", default="p2p", choices=["p2p", "nccl"], help="config 4: exchange of partial sums")
+    ap.add_argument("--seqs", type=int, default=64, help="config 3: sequences in total (64 = the config; fewer for a "
+                    "smaller case, e.g. one data-parallel rank's share on one GPU)")
     ap.add_argument("--batch-gemm", default="mma", choices=["mma", "tcgen05"],
                     help="config 3: batched GEMM kernel (int8 mma.sync or tcgen05; identical results)")
     return ap.parse_args()
@@ -323,7 +325,8 @@ def run_batch(args, rank, world, local):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
         pg = dist
-    n = BATCH_TOTAL // world
+    total = args.seqs
+    n = total // world
     n_prompt = BATCH_PROMPT if args.prompt == PROMPT else args.prompt   # --prompt: a smaller case for profiling
     path = synth.ensure_model("q4_k_m", 0)
     if pg:
@@ -372,7 +375,7 @@ def run_batch(args, rank, world, local):
         peak, peak_kind = measured_peaks()
         per_step_ms = ms_max / args.steps
         achieved = bytes_per_step / (per_step_ms * 1e-3) / 1e9
-        value = BATCH_TOTAL * args.steps / (ms_max * 1e-3)
+        value = total * args.steps / (ms_max * 1e-3)
         cb = None if args.no_cpu_baseline else cpu_baseline(path)
         if cb is not None:
             cb["sample"] += "; the reference decodes one sequence at a time, so its batch rate is its batch-1 rate"
@@ -382,7 +385,7 @@ def run_batch(args, rank, world, local):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": ("int8 tcgen05" if args.batch_gemm == "tcgen05" else "int8 mma") + " / fp32",
             "data": "synthetic (seeded random-init GGUF, Q4_K_M layout)",
-            "config": {"workload": "config3: MiniCPM5-2B Q4_K_M batched greedy decode, 64 sequences",
+            "config": {"workload": f"config3: MiniCPM5-2B Q4_K_M batched greedy decode, {total} sequences",
                        "sequences_per_gpu": n, "prompt": n_prompt, "gemm": args.batch_gemm,
                        "positions": [first_pos, first_pos + args.steps - 1],
                        "parallelism": f"dp{world} (sequences split over GPUs)",
@@ -392,7 +395,7 @@ def run_batch(args, rank, world, local):
                          "kernel": "batched step (k_b_gemm + attention units)",
                          "algorithmic_bytes_per_step": int(bytes_per_step)},
             "cpu_baseline": cb,
-            "e2e": {"value": round(BATCH_TOTAL * e2e_steps / e2e_s, 1), "unit": "tokens/s",
+            "e2e": {"value": round(total * e2e_steps / e2e_s, 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": 4 * n, "d2h_bytes_per_step": 4 * n},
             "gpu_launches": BATCH_LAUNCHES_PER_STEP * args.steps,
             "clocks": clocks,

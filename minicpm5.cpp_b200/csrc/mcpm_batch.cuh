@@ -867,7 +867,9 @@ __device__ DecodeParams b_att_params(const BStepArgs& a, int s) {
 }
 
 // Attention units of every sequence: blockIdx.x = sequence, blockIdx.y = (KV group, chunk).
-__global__ void __launch_bounds__(DEC_THREADS, 1) k_b_att_units(const BStepArgs a, int l) {
+// Two CTAs per SM (64 registers, no spills; shared memory 2 x 24 KB, or 2 x 96 KB for chunks
+// longer than 32): thousands of short units, so the second CTA hides the first one's loads.
+__global__ void __launch_bounds__(DEC_THREADS, 2) k_b_att_units(const BStepArgs a, int l) {
     const int s = blockIdx.x, item = blockIdx.y;
     const int n = a.pos[s] + 1, P = 32 * ((n + 2047) / 2048), C = (n + P - 1) / P;
     if (item >= 2 * C) return;

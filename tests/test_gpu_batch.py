@@ -10,7 +10,8 @@ pytestmark = pytest.mark.gpu
 
 @pytest.mark.parametrize("gemm", [0, 1], ids=["mma", "tcgen05"])
 @pytest.mark.parametrize("n_seq,n_prompt,n_gen,check", [(5, 6, 4, None), (64, 2, 1, (0, 9, 31, 40, 63)),
-                                                        (37, 2, 1, (0, 31, 32, 36))])
+                                                        (37, 2, 1, (0, 31, 32, 36)), (20, 2, 1, (0, 7, 8, 19)),
+                                                        (12, 2, 1, (0, 8, 11))])
 def test_batch_decode_bitexact(cuda, oracle, model_path, n_seq, n_prompt, n_gen, check, gemm):
     import oracle as O
     from mcpm import engine as E
