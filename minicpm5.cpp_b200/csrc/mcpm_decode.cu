@@ -1123,12 +1123,18 @@ __device__ bool phase_gu(const DecodeParams& p, const Smem& s, int l, int cta, i
     const PhaseLayout pl = phase_layout(L, *s.rows(), 2);
     const int n = pl.nrows[0];
     float* rv = s.rowval();
-    gemv_rows(L.tg, s.wbuf(0) + pl.off[0], n, N_EMBD / 256, *s.xq(), s.part(), MAX_TASKS, rv,
-              (p.trace && l == 1 && cta == 0) ? p.trace + TRACE_GEMV + 6 : nullptr);
-    trace_step(p, l, 3, 3);
-    gemv_rows(L.tu, s.wbuf(0) + pl.off[1], n, N_EMBD / 256, *s.xq(), s.part(), MAX_TASKS, rv + 128);
+    unsigned long long* tr = (p.trace && l == 1 && cta == 0) ? p.trace + TRACE_GEMV + 6 : nullptr;
+    if (L.tg == L.tu) {   // gate rows then up rows in one pass: rv[0, n) gate, rv[n, 2n) up
+        gemv_rows2(L.tg, s.wbuf(0) + pl.off[0], n, s.wbuf(0) + pl.off[1], 2 * n, N_EMBD / 256, *s.xq(), s.part(),
+                   MAX_TASKS, rv, tr);
+        trace_step(p, l, 3, 3);
+    } else {
+        gemv_rows(L.tg, s.wbuf(0) + pl.off[0], n, N_EMBD / 256, *s.xq(), s.part(), MAX_TASKS, rv, tr);
+        trace_step(p, l, 3, 3);
+        gemv_rows(L.tu, s.wbuf(0) + pl.off[1], n, N_EMBD / 256, *s.xq(), s.part(), MAX_TASKS, rv + n);
+    }
     trace_step(p, l, 3, 4);
-    for (int r = threadIdx.x; r < n; r += blockDim.x) p.h[pl.row0[0] + r] = canon_silu_mul(rv[r], rv[128 + r]);
+    for (int r = threadIdx.x; r < n; r += blockDim.x) p.h[pl.row0[0] + r] = canon_silu_mul(rv[r], rv[n + r]);
     return true;
 }
 

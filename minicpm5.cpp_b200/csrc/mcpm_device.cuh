@@ -521,42 +521,44 @@ __device__ __forceinline__ void block_scales(int type, const uint8_t* blk, float
 }
 
 // ---------------------------------------------------------------- GEMV over staged rows
-// Rows [0, R) of one matrix (TYPE, NB super-blocks per row) are staged contiguously in
-// shared memory at `w`.  Pass 1, one (row, block) task per thread: the task's integer
-// partials split into the eight AVX2 lanes, its min term (Q4_K) or offset (Q6_K), and
-// the two fp32 scale products dx = xd*d and dm = -(xd*dmin) go to `part` (PART_WORDS
-// words per task).  Pass 2: lane k of a row group loads every operand of its chain, then
-// runs the reference's fp32 accumulator chain for AVX2 lane k over the blocks
-// (acc = fma(dx, isum_k, acc); Q4_K also acc_min = fma(dm, minsum, acc_min)); the eight
-// lanes are reduced with hsum_f32_8's tree (a butterfly over lane bits 2, 1, 0) and the
-// min term is added.  Row r's value goes to out[r] (shared memory), visible to every
-// thread on return.  Not inlined: one copy per (TYPE, NB) serves every phase.
-// Must be called by all threads of the CTA (contains __syncthreads).
+// Rows [0, R) of one or two matrices of the same TYPE and NB super-blocks per row, staged
+// contiguously in shared memory: rows [0, R0) at w0, rows [R0, R) at w1.  Pass 1, one
+// (row, block) task per thread (q4k_task / q6k_task): the task's integer partials split into the
+// eight AVX2 lanes, its min term (Q4_K) or offset (Q6_K), and the two fp32 scale products
+// dx = xd*d and dm = -(xd*dmin) go to `part` (PART_WORDS words per task).  Pass 2: lane k of
+// a row group loads every operand of its chain, then runs the reference's fp32 accumulator
+// chain for AVX2 lane k over the blocks (acc = fma(dx, isum_k, acc); Q4_K also
+// acc_min = fma(dm, minsum, acc_min)); the eight lanes are reduced with hsum_f32_8's tree
+// (a butterfly over lane bits 2, 1, 0) and the min term is added.  Row r's value goes to
+// out[r] (shared memory), visible to every thread on return.  Not inlined: one copy per
+// (TYPE, NB) serves every phase.  Must be called by all threads of the CTA (contains
+// __syncthreads).
 constexpr int PART_WORDS = 11;   // k0..k7, minsum, dx, dm (odd stride: conflict-free stores)
 
 template <int TYPE, int NB>
-__device__ __noinline__ void gemv_rows_t(const uint8_t* w, int R, const XQSmem& xq, int* part, int max_tasks,
-                                         float* out, unsigned long long* tr) {
+__device__ __noinline__ void gemv_rows_t(const uint8_t* w0, int R0, const uint8_t* w1, int R, const XQSmem& xq,
+                                         int* part, int max_tasks, float* out, unsigned long long* tr) {
     constexpr int RB = TYPE == GGML_Q4_K ? Q4K_BYTES : Q6K_BYTES;
     const int tid = threadIdx.x, nthr = blockDim.x;
     const int mt = (max_tasks / NB) * NB;   // whole rows per chunk
     for (int t0 = 0; t0 < R * NB; t0 += mt) {
         const int ntask = min(mt, R * NB - t0);
         for (int t = tid; t < ntask; t += nthr) {
-            const int task = t0 + t, b = task % NB;
-            const uint8_t* blk = w + static_cast<size_t>(task) * RB;
-            Partials p;
+            const int task = t0 + t, row = task / NB, b = task - row * NB;
+            const uint8_t* blk = row < R0 ? w0 + static_cast<size_t>(task) * RB
+                                          : w1 + static_cast<size_t>(task - R0 * NB) * RB;
+            Partials pt;
             if (TYPE == GGML_Q4_K)
-                q4k_task(blk, xq, b, p);
+                q4k_task(blk, xq, b, pt);
             else
-                q6k_task(blk, xq, b, p);
+                q6k_task(blk, xq, b, pt);
             float d, dmin;
             block_scales(TYPE, blk, d, dmin);
             const float xd = xq.d[b];
             int* dst = part + t * PART_WORDS;
 #pragma unroll
-            for (int k = 0; k < 8; ++k) dst[k] = p.k[k];
-            dst[8] = p.minsum;
+            for (int k = 0; k < 8; ++k) dst[k] = pt.k[k];
+            dst[8] = pt.minsum;
             dst[9] = __float_as_int(__fmul_rn(xd, d));
             dst[10] = __float_as_int(-__fmul_rn(xd, dmin));
         }
@@ -596,20 +598,27 @@ __device__ __noinline__ void gemv_rows_t(const uint8_t* w, int R, const XQSmem& 
 }
 
 // Dispatch on the weight type (Q4_K / Q6_K) and the row length (8 or 24 super-blocks).
-// `tr` (optional): thread 0 stores globaltimer after pass 1 (tr[0]) and pass 2 (tr[1]).
-static __device__ __forceinline__ void gemv_rows(int type, const uint8_t* w, int R, int nb, const XQSmem& xq, int* part,
-                                                 int max_tasks, float* out, unsigned long long* tr = nullptr) {
+// Rows [0, R0) at w0 and, optionally, rows [R0, R) of a second matrix of the same type at
+// w1 (gate and up in one pass).  `tr` (optional): thread 0 stores globaltimer after pass 1
+// (tr[0]) and pass 2 (tr[1]).
+__device__ __forceinline__ void gemv_rows2(int type, const uint8_t* w0, int R0, const uint8_t* w1, int R, int nb,
+                                           const XQSmem& xq, int* part, int max_tasks, float* out,
+                                           unsigned long long* tr = nullptr) {
     if (type == GGML_Q4_K) {
         if (nb == 8)
-            gemv_rows_t<GGML_Q4_K, 8>(w, R, xq, part, max_tasks, out, tr);
+            gemv_rows_t<GGML_Q4_K, 8>(w0, R0, w1, R, xq, part, max_tasks, out, tr);
         else
-            gemv_rows_t<GGML_Q4_K, 24>(w, R, xq, part, max_tasks, out, tr);
+            gemv_rows_t<GGML_Q4_K, 24>(w0, R0, w1, R, xq, part, max_tasks, out, tr);
     } else {
         if (nb == 8)
-            gemv_rows_t<GGML_Q6_K, 8>(w, R, xq, part, max_tasks, out, tr);
+            gemv_rows_t<GGML_Q6_K, 8>(w0, R0, w1, R, xq, part, max_tasks, out, tr);
         else
-            gemv_rows_t<GGML_Q6_K, 24>(w, R, xq, part, max_tasks, out, tr);
+            gemv_rows_t<GGML_Q6_K, 24>(w0, R0, w1, R, xq, part, max_tasks, out, tr);
     }
+}
+__device__ __forceinline__ void gemv_rows(int type, const uint8_t* w, int R, int nb, const XQSmem& xq, int* part,
+                                          int max_tasks, float* out, unsigned long long* tr = nullptr) {
+    gemv_rows2(type, w, R, w, R, nb, xq, part, max_tasks, out, tr);
 }
 
 }  // namespace mcpm

@@ -14,6 +14,7 @@
 // process exits.  All calls on a device share it, so calls that overlap on the GPU race
 // and must be serialised by the caller (one stream, or events).
 #include <cstdio>
+#include <mutex>
 
 #include "../../include/mcpm.h"
 #include "mcpm_device.cuh"
@@ -34,8 +35,10 @@ struct ScratchAddr {
     uint8_t* q8k = nullptr;
 };
 ScratchAddr g_addr[64];
+std::mutex g_addr_mu;   // host threads making their first call on one device at the same time
 
 mcpm_status setup_scratch(int dev) {
+    std::lock_guard<std::mutex> lock(g_addr_mu);
     ScratchAddr& a = g_addr[dev];
     if (a.ready) return MCPM_OK;
     if (cudaGetSymbolAddress(reinterpret_cast<void**>(&a.part), g_att_part) != cudaSuccess ||
@@ -56,15 +59,17 @@ extern "C" mcpm_status mcpm_attention_noalloc(const float* q, const float* k, co
                                               void* stream) {
     if (!q || !k || !v || !kcache || !vcache || !out || !aligned16(q) || !aligned16(kcache) || !aligned16(vcache))
         return MCPM_BAD_ARG;
+    // Same checks in the same order as mcpm_attention, so both ops return the same status
+    // for the same arguments: the cache size first, then the position.
     if (max_seq <= 0) return MCPM_BAD_ARG;
-    if (pos < 0 || pos >= max_seq) return MCPM_CTX_OVERFLOW;
-    if (pos + 1 > MAX_SEQ || max_seq > MAX_SEQ) {
+    if (max_seq > MAX_SEQ) {
         std::fprintf(stderr,
-                     "[mcpm] mcpm_attention_noalloc: context of %d positions (cache %d) exceeds the fixed "
-                     "workspace limit of %d positions\n",
-                     pos + 1, max_seq, MAX_SEQ);
+                     "[mcpm] mcpm_attention_noalloc: cache of %d positions exceeds the fixed workspace limit of %d "
+                     "positions\n",
+                     max_seq, MAX_SEQ);
         return MCPM_BAD_ARG;
     }
+    if (pos < 0 || pos >= max_seq) return MCPM_CTX_OVERFLOW;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MCPM_CUDA_ERROR;
     const mcpm_status st = setup_scratch(dev);

@@ -67,21 +67,29 @@ def _fp16_absnormal(rng: np.random.Generator, n: int, sigma: float = 2e-3) -> np
     return np.abs(rng.normal(0.0, sigma, n)).astype(np.float16).view(np.uint16)
 
 
-def tensor_bytes(t: spec.TensorInfo, rng: np.random.Generator) -> np.ndarray:
-    """Random contents of one tensor as a flat uint8 array."""
+def tensor_bytes(t: spec.TensorInfo, rng: np.random.Generator, sigma: float = 2e-3, balanced: bool = False) -> np.ndarray:
+    """Random contents of one tensor as a flat uint8 array (fp16 block scales |N(0, sigma)|).
+
+    ``balanced``: a Q4_K block's ``dmin`` is 7.5 * ``d`` instead of an independent draw, so
+    the expected value of every dequantised weight, d*sc*q - dmin*m with sc, m uniform on
+    0..63 and q on 0..15, is zero."""
     if t.ggml_type == spec.GGML_F32:
         return (1.0 + rng.normal(0.0, 0.02, t.n_elements)).astype(np.float32).view(np.uint8)
     per, nb = spec.BLOCK_GEOM[t.ggml_type]
     nblk = t.n_elements // per
     raw = np.frombuffer(rng.bytes(nblk * nb), dtype=np.uint8).reshape(nblk, nb).copy()
     if t.ggml_type == spec.GGML_Q4_K:
-        raw[:, 0:2] = _fp16_absnormal(rng, nblk).view(np.uint8).reshape(nblk, 2)
-        raw[:, 2:4] = _fp16_absnormal(rng, nblk).view(np.uint8).reshape(nblk, 2)
+        d = _fp16_absnormal(rng, nblk, sigma)
+        dmin = _fp16_absnormal(rng, nblk, sigma)
+        if balanced:
+            dmin = (d.view(np.float16).astype(np.float32) * 7.5).astype(np.float16).view(np.uint16)
+        raw[:, 0:2] = d.view(np.uint8).reshape(nblk, 2)
+        raw[:, 2:4] = dmin.view(np.uint8).reshape(nblk, 2)
     elif t.ggml_type == spec.GGML_Q6_K:
         raw[:, 192:208] = rng.integers(-32, 32, (nblk, 16), dtype=np.int8).view(np.uint8)
-        raw[:, 208:210] = _fp16_absnormal(rng, nblk).view(np.uint8).reshape(nblk, 2)
+        raw[:, 208:210] = _fp16_absnormal(rng, nblk, sigma).view(np.uint8).reshape(nblk, 2)
     elif t.ggml_type == spec.GGML_Q8_0:
-        raw[:, 0:2] = _fp16_absnormal(rng, nblk).view(np.uint8).reshape(nblk, 2)
+        raw[:, 0:2] = _fp16_absnormal(rng, nblk, sigma).view(np.uint8).reshape(nblk, 2)
         raw[:, 2:34] = rng.integers(-127, 128, (nblk, 32), dtype=np.int8).view(np.uint8)
     else:
         raise ValueError(t.ggml_type)
@@ -126,8 +134,16 @@ def _header(tensors: List[spec.TensorInfo], data_start: Optional[int], variant: 
     return hdr
 
 
-def write_model(path: str, variant: str = "q4_k_m", seed: int = 0) -> dict:
-    """Write a synthetic model; returns its manifest (also stored as path + '.json')."""
+def write_model(path: str, variant: str = "q4_k_m", seed: int = 0, dscale: float = 1.0) -> dict:
+    """Write a synthetic model; returns its manifest (also stored as path + '.json').
+
+    ``dscale`` = 1.0: the benchmark distribution.  Its Q4_K weights have a positive mean
+    (nibbles 0..15 against small mins), so every layer amplifies the all-ones direction of
+    the residual stream, SwiGLU's exp overflows in many blocks, and the greedy stream
+    hardly depends on the prompt.  ``dscale`` != 1.0: a parity model with the same layout
+    and types whose Q4_K blocks are balanced (zero-mean weights, see ``tensor_bytes``) and
+    whose per-layer block scales (``blk.*``) are multiplied by ``dscale``, so activations
+    stay near unit size and the logits depend on the input."""
     base = spec.tensor_list(variant)
     if variant == "q4_k_m":
         data_start = spec.Q4KM_DATA_START
@@ -147,13 +163,13 @@ def write_model(path: str, variant: str = "q4_k_m", seed: int = 0) -> dict:
                 f.write(b"\0" * (t.offset - pos))
                 pos = t.offset
             rng = np.random.Generator(np.random.PCG64([seed, i]))
-            b = tensor_bytes(t, rng)
+            b = tensor_bytes(t, rng, 2e-3 * (dscale if t.name.startswith("blk.") else 1.0), balanced=dscale != 1.0)
             assert b.size == t.nbytes
             digest.update(b[:4096].tobytes())
             f.write(b.tobytes())
             pos += b.size
     os.replace(tmp, path)
-    manifest = {"variant": variant, "seed": seed, "size": os.path.getsize(path),
+    manifest = {"variant": variant, "seed": seed, "dscale": dscale, "size": os.path.getsize(path),
                 "data_start": data_start, "table": spec.table_digest(tensors),
                 "content_digest": digest.hexdigest()}
     with open(path + ".json", "w") as f:
@@ -161,25 +177,26 @@ def write_model(path: str, variant: str = "q4_k_m", seed: int = 0) -> dict:
     return manifest
 
 
-def model_path(variant: str = "q4_k_m", seed: int = 0, directory: Optional[str] = None) -> str:
+def model_path(variant: str = "q4_k_m", seed: int = 0, directory: Optional[str] = None, dscale: float = 1.0) -> str:
     directory = directory or DEFAULT_DIR
-    return os.path.join(directory, f"minicpm5-2b-synth-{variant}-s{seed}.gguf")
+    tag = "" if dscale == 1.0 else f"-d{dscale:g}"
+    return os.path.join(directory, f"minicpm5-2b-synth-{variant}-s{seed}{tag}.gguf")
 
 
-def ensure_model(variant: str = "q4_k_m", seed: int = 0, directory: Optional[str] = None) -> str:
+def ensure_model(variant: str = "q4_k_m", seed: int = 0, directory: Optional[str] = None, dscale: float = 1.0) -> str:
     """Path of the synthetic model, writing it first if it is absent or stale."""
-    path = model_path(variant, seed, directory)
+    path = model_path(variant, seed, directory, dscale)
     meta = path + ".json"
     if os.path.exists(path) and os.path.exists(meta):
         try:
             with open(meta) as f:
                 m = json.load(f)
-            if m.get("size") == os.path.getsize(path) and m.get("seed") == seed:
+            if m.get("size") == os.path.getsize(path) and m.get("seed") == seed and m.get("dscale", 1.0) == dscale:
                 return path
         except (OSError, ValueError):
             pass
     os.makedirs(os.path.dirname(path), exist_ok=True)
-    write_model(path, variant, seed)
+    write_model(path, variant, seed, dscale)
     return path
 
 

@@ -20,7 +20,10 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF_SO = os.path.join(HERE, "_ref", "libref_minicpm5.so")
 ORACLE_SO = os.path.join(HERE, "_build", "liboracle.so")
-REFERENCE_TREE = os.environ.get("MCPM_REFERENCE_TREE", "/root/reference")
+# The reference source tree: $MCPM_REFERENCE_TREE, else a directory `reference` beside this
+# repository's root.  Only the build of the checker library reads it.
+REFERENCE_TREE = os.environ.get("MCPM_REFERENCE_TREE") or os.path.join(os.path.dirname(os.path.dirname(HERE)),
+                                                                         "reference")
 
 _pkg = os.path.join(os.path.dirname(HERE), "minicpm5.cpp_b200")
 if _pkg not in sys.path:

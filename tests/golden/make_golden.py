@@ -12,10 +12,20 @@ Fixtures:
                               on the seed-0 synthetic Q4_K_M model: greedy tokens, top-32
                               logits per step and every 256th logit
   reference_variability.json  reference at 1 vs 4 OpenMP threads on the same steps
+  reference_decode_wc.npz     MiniCPM5Engine::forward of the reference build at OMP_NUM_THREADS=1
+                              on the seed-0 parity model (same layout and types, balanced Q4_K
+                              mins, per-layer block scales x PARITY_DSCALE): the config-0 shape,
+                              a 128-id prompt (seed 1234) then 64 greedy tokens; argmax at every
+                              position, top-32 logits and every 256th logit per position, all
+                              logits at the last prompt position
+  reference_variability_wc.json  the reference's own spread on the parity run: eight teacher-forced
+                              runs at 4 OpenMP threads against the 1-thread run (per position)
+  restatement_decode_wc.npz   the C restatement on the same teacher-forced inputs
   reference_q8_0.npz          gemv_q8_0 of the reference build (fp32 activations) on seeded
                               Q8_0 matrices with the config-1 distributions
 
     python tests/golden/make_golden.py --q8_0     # only reference_q8_0.npz
+    python tests/golden/make_golden.py --wc       # only the parity-model files
 """
 import json
 import os
@@ -31,6 +41,9 @@ sys.path.insert(0, os.path.join(REPO, "minicpm5.cpp_b200"))
 sys.path.insert(0, os.path.join(REPO, "oracle"))
 
 N_PROMPT, N_GEN, PROMPT_SEED = 16, 16, 1234
+# Parity model (synth.write_model dscale): the config-0 shape, 128 prompt ids + 64 greedy tokens.
+PARITY_DSCALE, WC_PROMPT, WC_GEN = 0.04, 128, 64
+N_SPREAD_RUNS = 8   # 4-thread reference runs that measure its own spread
 KERNEL_CASES = [("q4k", 12, 64, 2048, 101), ("q4k", 12, 48, 6144, 102), ("q6k", 14, 64, 2048, 103),
                 ("q6k", 14, 40, 6144, 104)]
 
@@ -99,29 +112,106 @@ import sys, json, numpy as np
 sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[2])
 import oracle as O
 from mcpm import synth
-path = synth.ensure_model("q4_k_m", 0)
 n_prompt, n_gen, seed = int(sys.argv[3]), int(sys.argv[4]), int(sys.argv[5])
+dscale = float(sys.argv[7]) if len(sys.argv) > 7 else 1.0
+path = synth.ensure_model("q4_k_m", 0, dscale=dscale)
 e = O.RefEngine(O.Ref(), path, n_prompt + n_gen + 1)
 prompt = synth.prompt_ids(n_prompt, seed=seed)
 lg = np.zeros(130560, np.float32)
 toks, top_i, top_v, strided = [], [], [], []
 tok = None
+full = None
 for pos in range(n_prompt + n_gen):
     t = int(prompt[pos]) if pos < n_prompt else tok
     tok = e.forward(t, pos, lg)
     toks.append(tok)
     idx = np.argsort(-lg, kind="stable")[:32]
     top_i.append(idx.astype(np.int32)); top_v.append(lg[idx].copy()); strided.append(lg[::256].copy())
+    if pos == n_prompt - 1:
+        full = lg.copy()
+extra = {"full_last_prompt": full, "dscale": np.float64(dscale)} if dscale != 1.0 else {}
 np.savez_compressed(sys.argv[6], prompt=prompt, tokens=np.array(toks, np.int32), top_idx=np.array(top_i),
-                    top_val=np.array(top_v), strided=np.array(strided))
+                    top_val=np.array(top_v), strided=np.array(strided), **extra)
 """
 
 
-def decode(threads, out_path):
+def decode(threads, out_path, n_prompt=N_PROMPT, n_gen=N_GEN, dscale=1.0):
     env = dict(os.environ, OMP_NUM_THREADS=str(threads))
     subprocess.run([sys.executable, "-c", DECODE_CHILD, os.path.join(REPO, "oracle"),
-                    os.path.join(REPO, "minicpm5.cpp_b200"), str(N_PROMPT), str(N_GEN), str(PROMPT_SEED), out_path],
+                    os.path.join(REPO, "minicpm5.cpp_b200"), str(n_prompt), str(n_gen), str(PROMPT_SEED), out_path,
+                    str(dscale)], env=env, check=True)
+
+
+TF_CHILD = r"""
+import sys, json, numpy as np
+sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[2])
+import oracle as O
+from mcpm import synth
+golden, which, out, dscale = sys.argv[3], sys.argv[4], sys.argv[5], float(sys.argv[6])
+g = np.load(golden)
+toks, prompt = g["tokens"], g["prompt"]
+n = len(toks)
+inputs = list(prompt) + list(toks[len(prompt) - 1:n - 1])   # teacher forcing: the 1-thread run's tokens
+path = synth.ensure_model("q4_k_m", 0, dscale=dscale)
+eng = O.OracleModel(O.Oracle(), path, n + 1) if which == "restatement" else O.RefEngine(O.Ref(), path, n + 1)
+lg = np.zeros(130560, np.float32)
+am, top = [], []
+for pos in range(n):
+    am.append(eng.forward(int(inputs[pos]), pos, lg))
+    top.append(lg[g["top_idx"][pos]].copy())
+np.savez_compressed(out, argmax=np.array(am, np.int32), top_val=np.array(top))
+"""
+
+
+def teacher_forced(which, threads, out_path):
+    """`which` ("reference" or "restatement") over the parity run's inputs, fed the 1-thread
+    reference's own tokens: argmax and the logits at the 1-thread run's top-32 indices."""
+    env = dict(os.environ, OMP_NUM_THREADS=str(threads))
+    subprocess.run([sys.executable, "-c", TF_CHILD, os.path.join(REPO, "oracle"), os.path.join(REPO, "minicpm5.cpp_b200"),
+                    os.path.join(HERE, "reference_decode_wc.npz"), which, out_path, str(PARITY_DSCALE)],
                    env=env, check=True)
+
+
+def parity_model_goldens():
+    """The config-0 shape on the parity model.
+
+    reference_decode_wc.npz: the reference at 1 OpenMP thread (deterministic), free-running.
+    reference_variability_wc.json: N_SPREAD_RUNS teacher-forced runs of the reference at 4 threads.  At
+    more than one thread the reference does not repeat itself (its OpenMP reduction of the
+    RMSNorm sum combines per-thread partials in arrival order), and the int8 re-quantisation
+    in front of every GEMV turns those last-bit differences into logit differences of several
+    units on this model; per position, `spread` is the largest |difference| over the top-32
+    logits of either run against the 1-thread run.  A position is `decidable` when the
+    1-thread run's top-2 margin exceeds that spread.
+    restatement_decode_wc.npz: this project's C restatement, teacher-forced the same way (the
+    CUDA engine must reproduce it bit for bit).
+    """
+    from mcpm import synth
+    man = json.load(open(synth.ensure_model("q4_k_m", 0, dscale=PARITY_DSCALE) + ".json"))
+    out = os.path.join(HERE, "reference_decode_wc.npz")
+    decode(1, out, WC_PROMPT, WC_GEN, PARITY_DSCALE)
+    a = np.load(out)
+    runs = []
+    for r in range(N_SPREAD_RUNS):
+        tmp = os.path.join(HERE, f"_tmp_tf4_{r}.npz")
+        teacher_forced("reference", 4, tmp)
+        runs.append(dict(np.load(tmp)))
+        os.unlink(tmp)
+    teacher_forced("restatement", 8, os.path.join(HERE, "restatement_decode_wc.npz"))
+    d = [np.abs(r["top_val"] - a["top_val"]) for r in runs]
+    spread = np.max([x.max(1) for x in d], axis=0)
+    margin = a["top_val"][:, 0] - a["top_val"][:, 1]
+    gen = a["tokens"][WC_PROMPT - 1:]
+    var = {"threads": [1, 4], "teacher_forced": True,
+           "distinct_generated_tokens": int(len(set(gen.tolist()))), "generated": int(len(gen)),
+           "argmax_agree_4_vs_1": [int(np.sum(r["argmax"] == a["tokens"])) for r in runs], "positions": int(len(margin)),
+           "mean_abs_top32_4_vs_1": [float(x.mean()) for x in d],
+           "spread": [round(float(x), 4) for x in spread],
+           "decidable": [bool(x) for x in margin > spread],
+           "model_manifest": man}
+    with open(os.path.join(HERE, "reference_variability_wc.json"), "w") as f:
+        json.dump(var, f)
+    print(json.dumps({k: v for k, v in var.items() if k not in ("spread", "decidable")}))
 
 
 def main():
@@ -129,6 +219,9 @@ def main():
     from mcpm import synth
     O.build(reference=True)
     assert O.have_ref(), "needs the reference tree"
+    if "--wc" in sys.argv:
+        parity_model_goldens()
+        return
     np.savez_compressed(os.path.join(HERE, "reference_q8_0.npz"), **q8_0_kernels())
     if "--q8_0" in sys.argv:
         return
@@ -150,6 +243,7 @@ def main():
     with open(os.path.join(HERE, "reference_variability.json"), "w") as f:
         json.dump(var, f, indent=1)
     print(json.dumps(var))
+    parity_model_goldens()
 
 
 if __name__ == "__main__":

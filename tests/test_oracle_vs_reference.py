@@ -174,3 +174,54 @@ def test_live_reference_swiglu_nan_semantics(oracle, ref):
     u = (rng.normal(0, 1, 6144) * 1500).astype(np.float32)
     a, b = ref.swiglu_q8k(g, u), oracle.swiglu_q8k(g, u)
     assert np.array_equal(a["qs"], b["qs"]) and np.array_equal(a["bsums"], b["bsums"])
+
+
+# ---- floating-point ops against the reference build, per element: |a - b| <= 2e-3 + 1e-3 |b|
+def _close(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return bool(np.all(np.abs(a - b) <= 2e-3 + 1e-3 * np.abs(b)))
+
+
+@pytest.mark.parametrize("pos", [0, 31, 300, 3000, 16383])
+def test_attention_vs_reference(oracle, ref, pos):
+    """execute_attention (ops.cpp:537-628): K/V append at pos, then softmax(q.K^T/sqrt(128)) V
+    over positions 0..pos; the restatement's split-KV chunks and combine order against the
+    reference's single pass, with the reference build's expf."""
+    from oracle import _fptr
+    rng = np.random.default_rng(pos + 11)
+    max_seq = pos + 1
+    q = rng.normal(0, 1, 2048).astype(np.float32)
+    k = rng.normal(0, 1, 256).astype(np.float32)
+    v = rng.normal(0, 1, 256).astype(np.float32)
+    kc = rng.normal(0, 1, (max_seq, 256)).astype(np.float32)
+    vc = rng.normal(0, 1, (max_seq, 256)).astype(np.float32)
+    outs = []
+    for lib, fn in ((ref.lib, "ref_attention"), (oracle.lib, "orc_attention")):
+        o = np.zeros(2048, np.float32)
+        kk, vv = kc.copy(), vc.copy()
+        getattr(lib, fn)(_fptr(o), _fptr(q), _fptr(k), _fptr(v), _fptr(kk), _fptr(vv), pos, max_seq, 16, 2, 128)
+        assert np.array_equal(kk[pos], k) and np.array_equal(vv[pos], v)
+        outs.append(o)
+    assert _close(outs[1], outs[0])
+
+
+@pytest.mark.parametrize("pos", [1, 100, 5000, 16383])
+def test_rope_vs_reference(oracle, ref, pos):
+    """apply_rope (ops.cpp:502-516), interleaved pairs, theta = 5e6^(-i/128), on 16 query
+    heads and 2 key heads."""
+    rng = np.random.default_rng(pos)
+    for n_heads in (16, 2):
+        x = rng.normal(0, 3, n_heads * 128).astype(np.float32)
+        want = ref.rope(x, pos, n_heads)
+        got = oracle.rope(x, pos, n_heads)
+        assert _close(got, want)
+
+
+def test_rmsnorm_vs_reference(oracle, ref):
+    """rmsnorm (ops.cpp:468-481) on real-valued input: the reference's reciprocal square-root
+    estimate and summation order against the restatement's canonical order."""
+    rng = np.random.default_rng(5)
+    for scale in (0.01, 1.0, 300.0):
+        x = (rng.normal(0, 1, 2048) * scale).astype(np.float32)
+        w = (1 + rng.normal(0, 0.02, 2048)).astype(np.float32)
+        assert _close(oracle.rmsnorm(x, w), ref.rmsnorm(x, w))

@@ -49,4 +49,8 @@ def test_noalloc_attention_rejects_context_beyond_workspace(cuda):
     t = cuda.zeros(4096, dtype=cuda.float32, device="cuda")
     p = t.data_ptr()
     assert lib.mcpm_attention_noalloc(p, p, p, p, p, 16384, 20000, p, None, None) == E.BAD_ARG
+    # pos beyond a cache that is itself too large: both ops report the cache size first
+    assert lib.mcpm_attention(p, p, p, p, p, 20000, 20000, p, None, None) == E.BAD_ARG
+    assert lib.mcpm_attention_noalloc(p, p, p, p, p, 20000, 20000, p, None, None) == E.BAD_ARG
+    assert lib.mcpm_attention(p, p, p, p, p, 9, 9, p, None, None) == E.CTX_OVERFLOW
     assert lib.mcpm_attention_noalloc(p, p, p, p, p, 9, 9, p, None, None) == E.CTX_OVERFLOW
