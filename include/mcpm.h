@@ -135,7 +135,9 @@ typedef struct {
                       buffer over CUDA IPC and summed in rank order by the consuming kernel;
                       MCPM_TP_NCCL: ncclAllReduce / ncclAllGather (libnccl.so.2 at run time) */
     int eager;     /* 0: each token is one CUDA graph launch; 1: kernels launched one by one */
-    int reserved[2];
+    int peer_wait_us; /* bound of every device-side wait for another rank's values, microseconds
+                         (0: 5 s); a wait that runs out fails the step with MCPM_TIMEOUT */
+    int reserved[1];
 } mcpm_tp_config;
 /* 128-byte NCCL unique id (rank 0, MCPM_TP_NCCL). */
 mcpm_status mcpm_tp_nccl_id(void* id128);
@@ -162,7 +164,10 @@ mcpm_status mcpm_tp_read_tokens(mcpm_tp* t, int pos0, int n, int* tokens);
 /* n_layer, n_vocab, vocabulary rows [lo, hi), first query head and head count, first FFN
  * row and row count of this rank. */
 mcpm_status mcpm_tp_info(mcpm_tp* t, int info[8]);
-/* Zeroes the KV cache and the token log; positions restart at 0. */
+/* Zeroes the KV cache and the token log; positions restart at 0.  Also restarts the step
+ * counter that tags exchanged values and clears this rank's receive slots, which is how the
+ * ranks recover after MCPM_TIMEOUT: every rank calls mcpm_tp_reset between steps, and no rank
+ * steps again before all have reset (a host-side barrier). */
 mcpm_status mcpm_tp_reset(mcpm_tp* t);
 /* n greedy steps launched kernel by kernel with timing: ms_token = mean device time per
  * step; ms_comm = per step, the device time of the NCCL collectives (MCPM_TP_NCCL) or the

@@ -63,10 +63,11 @@ constexpr int TP_MAX_WORLD = 8;
 constexpr int PRO_PLAIN = 0, PRO_NORM = 1, PRO_SWIGLU = 2;
 constexpr int EPI_STORE = 0, EPI_ROPE = 1, EPI_PUBLISH = 2, EPI_ARGMAX = 3;
 constexpr unsigned STEP_ARGMAX = 255;
-// Waits on other GPUs: the ranks launch independently, so allow for host-side skew.  Once one
-// wait of the engine has timed out (ERR_TIMEOUT in the control word), every later wait gives up
-// at once, so a rank that stopped costs one bound, not one per exchange.
-constexpr unsigned long long PEER_WAIT_NS = 5000000000ull;
+// Waits on other GPUs: the ranks launch independently, so allow for host-side skew
+// (mcpm_tp_config::peer_wait_us, default 5 s).  Once one wait of the engine has timed out
+// (ERR_TIMEOUT in the control word), every later wait gives up at once, so a rank that
+// stopped costs one bound, not one per exchange.
+constexpr unsigned DEFAULT_PEER_WAIT_US = 5000000u;
 
 struct TPCtl {
     int token;         // input token of the next step
@@ -74,7 +75,8 @@ struct TPCtl {
     unsigned seq;      // steps run so far + 1: epoch of the exchanged values (seq << 8 | step)
     unsigned err;      // ERR_* bits
     unsigned am_cnt;   // LM-head CTAs whose argmax partial is stored
-    unsigned pad[3];
+    unsigned wait_us;  // bound of every wait for another rank's values
+    unsigned pad[2];
 };
 
 struct TPGemv {
@@ -115,10 +117,12 @@ __device__ __forceinline__ ulonglong2 ld_epoch2_sys(const unsigned long long* p)
     return w;
 }
 // n2 pairs of epoch-tagged values (16-byte aligned) written by any GPU, polled until all
-// carry `epoch`; false (and ERR_TIMEOUT) after PEER_WAIT_NS.
+// carry `epoch`; false (and ERR_TIMEOUT) after ctl->wait_us, or at once when an earlier wait
+// of this engine timed out.
 template <int N2>
 __device__ __forceinline__ bool load_epoch_sys(const unsigned long long* src, unsigned epoch, float (&v)[2 * N2],
-                                               unsigned* err) {
+                                               TPCtl* ctl) {
+    unsigned* err = &ctl->err;
     ulonglong2 w[N2];
     auto ready = [&]() {
         bool r = true;
@@ -130,12 +134,13 @@ __device__ __forceinline__ bool load_epoch_sys(const unsigned long long* src, un
     for (int i = 0; i < N2; ++i) w[i] = ld_epoch2_sys(src + 2 * i);
     if (!ready()) {
         const uint64_t t0 = globaltimer();
+        const unsigned long long limit = 1000ull * ctl->wait_us;
         do {
             __nanosleep(32);
 #pragma unroll
             for (int i = 0; i < N2; ++i) w[i] = ld_epoch2_sys(src + 2 * i);
             if (ready()) break;
-            if ((ld_relaxed_u32(err) & ERR_TIMEOUT) || globaltimer() - t0 > PEER_WAIT_NS) {
+            if ((ld_relaxed_u32(err) & ERR_TIMEOUT) || globaltimer() - t0 > limit) {
                 atomicOr(err, ERR_TIMEOUT);
                 return false;
             }
@@ -187,10 +192,10 @@ __device__ bool tp_prologue(const TPGemv& g, const Q80Smem& s, unsigned seq) {
         if (g.slots) {   // partials of every rank, summed in rank order
             const unsigned e = (seq << 8) | static_cast<unsigned>(g.red_step);
             const uint64_t t0 = (g.wait_ns && blockIdx.x == 0 && tid == 0) ? globaltimer() : 0;
-            ok = load_epoch_sys<2>(g.slots + i0, e, r, &g.ctl->err);
+            ok = load_epoch_sys<2>(g.slots + i0, e, r, g.ctl);
             for (int k = 1; k < g.world && ok; ++k) {
                 float t[4];
-                ok = load_epoch_sys<2>(g.slots + static_cast<size_t>(k) * N_EMBD + i0, e, t, &g.ctl->err);
+                ok = load_epoch_sys<2>(g.slots + static_cast<size_t>(k) * N_EMBD + i0, e, t, g.ctl);
 #pragma unroll
                 for (int j = 0; j < 4; ++j) r[j] = __fadd_rn(r[j], t[j]);
             }
@@ -341,7 +346,7 @@ __global__ void k_tp_pick(TPCtl* ctl, int world, const unsigned long long* am_sl
     if (lane < world) {
         if (am_slots) {
             float v[2];
-            ok = load_epoch_sys<1>(am_slots + 2 * lane, (seq << 8) | STEP_ARGMAX, v, &ctl->err);
+            ok = load_epoch_sys<1>(am_slots + 2 * lane, (seq << 8) | STEP_ARGMAX, v, ctl);
             bv = v[0], bi = __float_as_int(v[1]);
         } else {
             bv = gathered[2 * lane], bi = __float_as_int(gathered[2 * lane + 1]);
@@ -408,6 +413,7 @@ NcclApi* nccl() {
 
 struct mcpm_tp {
     int device = 0, rank = 0, world = 1, max_seq = 0, comm = MCPM_TP_P2P, use_graph = 1;
+    unsigned wait_us = DEFAULT_PEER_WAIT_US;
     cudaStream_t stream = nullptr;
     int n_sm = 0;
     bool loaded = false, connected = false;
@@ -727,13 +733,14 @@ mcpm_status mcpm_tp_create(const mcpm_tp_config* cfg, mcpm_tp** out) {
     *out = nullptr;
     const int w = cfg->world;
     if (!(w == 1 || w == 2 || w == 4 || w == 8) || cfg->rank < 0 || cfg->rank >= w) return MCPM_BAD_ARG;
-    if (cfg->max_seq <= 0 || cfg->max_seq > MAX_SEQ) return MCPM_BAD_ARG;
+    if (cfg->max_seq <= 0 || cfg->max_seq > MAX_SEQ || cfg->peer_wait_us < 0) return MCPM_BAD_ARG;
     if (cfg->comm != MCPM_TP_P2P && cfg->comm != MCPM_TP_NCCL) return MCPM_BAD_ARG;
     int ndev = 0;
     TP_CUDA(cudaGetDeviceCount(&ndev));
     if (cfg->device < 0 || cfg->device >= ndev) return MCPM_BAD_ARG;
     auto t = std::make_unique<mcpm_tp>();
     t->device = cfg->device, t->rank = cfg->rank, t->world = w, t->max_seq = cfg->max_seq, t->comm = cfg->comm;
+    t->wait_us = cfg->peer_wait_us > 0 ? static_cast<unsigned>(cfg->peer_wait_us) : DEFAULT_PEER_WAIT_US;
     t->use_graph = cfg->eager ? 0 : 1;
     TP_CUDA(cudaSetDevice(t->device));
     TP_CUDA(cudaDeviceGetAttribute(&t->n_sm, cudaDevAttrMultiProcessorCount, t->device));
@@ -917,6 +924,7 @@ mcpm_status mcpm_tp_load_gguf(mcpm_tp* t, const char* path) {
     if (!t->wait_ns) TP_CUDA(cudaMalloc(&t->wait_ns, sizeof(unsigned long long)));
     TPCtl c{};
     c.seq = 1;
+    c.wait_us = t->wait_us;
     TP_CUDA(cudaMemcpy(t->ctl, &c, sizeof(TPCtl), cudaMemcpyHostToDevice));
     TP_CUDA(cudaMemset(t->wait_ns, 0, sizeof(unsigned long long)));
     t->peer_recv[t->rank] = t->recv;
@@ -1041,7 +1049,17 @@ mcpm_status mcpm_tp_reset(mcpm_tp* t) {
     TP_CUDA(cudaMemsetAsync(t->kc, 0, kv * 4, t->stream));
     TP_CUDA(cudaMemsetAsync(t->vc, 0, kv * 4, t->stream));
     TP_CUDA(cudaMemsetAsync(t->tok_log, 0xff, t->max_seq * 4, t->stream));
-    TP_CUDA(cudaMemsetAsync(&t->ctl->err, 0, sizeof(unsigned), t->stream));   // seq keeps counting
+    // Step counter back to 1 and the receive slots cleared: after a timeout the ranks may have
+    // run different numbers of steps, and values of an earlier step must not match a new epoch.
+    // Every rank resets between steps (none in flight) before any rank steps again.
+    TPCtl c{};
+    c.seq = 1;
+    c.wait_us = t->wait_us;
+    TP_CUDA(cudaMemcpyAsync(t->ctl, &c, sizeof(TPCtl), cudaMemcpyHostToDevice, t->stream));
+    if (t->recv) {
+        const size_t recv_words = static_cast<size_t>(2) * t->world * N_EMBD + 2 * t->world;
+        TP_CUDA(cudaMemsetAsync(t->recv, 0, recv_words * 8, t->stream));
+    }
     TP_CUDA(cudaStreamSynchronize(t->stream));
     t->pos_next = 0;
     return MCPM_OK;

@@ -20,7 +20,7 @@ P2P, NCCL = 0, 1
 
 class mcpm_tp_config(C.Structure):
     _fields_ = [("device", C.c_int), ("rank", C.c_int), ("world", C.c_int), ("max_seq", C.c_int),
-                ("comm", C.c_int), ("eager", C.c_int), ("reserved", C.c_int * 2)]
+                ("comm", C.c_int), ("eager", C.c_int), ("peer_wait_us", C.c_int), ("reserved", C.c_int * 1)]
 
 
 def nccl_id() -> bytes:
@@ -31,10 +31,12 @@ def nccl_id() -> bytes:
 
 
 class TPEngine:
-    def __init__(self, device: int, rank: int, world: int, max_seq: int, comm: str = "p2p", eager: bool = False):
+    def __init__(self, device: int, rank: int, world: int, max_seq: int, comm: str = "p2p", eager: bool = False,
+                 peer_wait_us: int = 0):
+        """peer_wait_us: bound of every device-side wait for another rank (0 = 5 s)."""
         self.lib = load_library()
         self.rank, self.world, self.comm = rank, world, comm
-        cfg = mcpm_tp_config(device, rank, world, max_seq, P2P if comm == "p2p" else NCCL, int(eager))
+        cfg = mcpm_tp_config(device, rank, world, max_seq, P2P if comm == "p2p" else NCCL, int(eager), int(peer_wait_us))
         h = C.c_void_p()
         check(self.lib.mcpm_tp_create(C.byref(cfg), C.byref(h)), "mcpm_tp_create")
         self.h = h
