@@ -101,7 +101,8 @@ def profiled_traffic(avg_positions: float):
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks/throttle reasons sampled every 20 ms during the timed region (a
+    config-0 run times 256 tokens, about 0.3 s)."""
 
     def __init__(self, device: int):
         self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
@@ -110,7 +111,7 @@ class ClockSampler:
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
             self.p = subprocess.Popen(["nvidia-smi", "-i", str(device), f"--query-gpu={q}",
-                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                       "--format=csv,noheader,nounits", "-lms", "20"],
                                       stdout=self.out, stderr=subprocess.DEVNULL)
         except OSError:
             self.p = None
@@ -144,10 +145,12 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_baseline(model_path: str, n_prompt: int = 16, n_gen: int = 32, port_only: bool = False):
+def cpu_baseline(model_path: str, n_prompt: int = 16, n_gen: int = 32, port_only: bool = False, n_skip: int = 0):
     """Reference CPU build (oracle/_ref, AVX2 + OpenMP) on a bounded sample of the same
     workload, in a child process so OMP settings apply; falls back to the C restatement
-    (always for the all-Q8_0 model, which the reference build cannot run)."""
+    (always for the all-Q8_0 model, which the reference build cannot run).  The prompt is
+    prefilled token by token (untimed, as the reference's chat loop does), `n_skip` greedy
+    tokens follow untimed (the GPU arm's warm-up), then `n_gen` greedy tokens are timed."""
     cores = os.cpu_count() or 1
     code = f"""
 import sys, time, json, numpy as np
@@ -156,15 +159,17 @@ import oracle as O
 from mcpm import synth
 kind = 'reference' if (O.have_ref() and not {port_only!r}) else 'port'
 if kind == 'reference':
-    e = O.RefEngine(O.Ref(), {model_path!r}, {n_prompt + n_gen + 1})
+    e = O.RefEngine(O.Ref(), {model_path!r}, {n_prompt + n_skip + n_gen + 1})
 else:
-    e = O.OracleModel(O.Oracle(), {model_path!r}, {n_prompt + n_gen + 1})
-p = synth.prompt_ids({n_prompt}, seed=4321)
+    e = O.OracleModel(O.Oracle(), {model_path!r}, {n_prompt + n_skip + n_gen + 1})
+p = synth.prompt_ids({n_prompt}, seed=1234)
 tok = 0
 for pos in range({n_prompt}):
     tok = e.forward(int(p[pos]), pos)
+for pos in range({n_prompt}, {n_prompt + n_skip}):
+    tok = e.forward(tok, pos)
 t0 = time.perf_counter()
-for pos in range({n_prompt}, {n_prompt + n_gen}):
+for pos in range({n_prompt + n_skip}, {n_prompt + n_skip + n_gen}):
     tok = e.forward(tok, pos)
 dt = time.perf_counter() - t0
 print(json.dumps({{"kind": kind, "tok_s": {n_gen} / dt}}))
@@ -176,7 +181,9 @@ print(json.dumps({{"kind": kind, "tok_s": {n_gen} / dt}}))
     except Exception as ex:  # noqa: BLE001
         return {"value": None, "unit": "tokens/s", "cores": cores, "kind": "reference", "sample": f"failed: {ex}"}
     return {"value": round(d["tok_s"], 3), "unit": "tokens/s", "cores": cores, "kind": d["kind"],
-            "sample": f"{n_prompt}-token prompt then {n_gen} greedy tokens timed (decode only), OMP_NUM_THREADS={cores}"}
+            "sample": f"{n_prompt}-token prompt, {n_skip} untimed greedy tokens, then {n_gen} greedy tokens timed "
+                      f"(positions {n_prompt + n_skip}..{n_prompt + n_skip + n_gen - 1}, decode only), "
+                      f"OMP_NUM_THREADS={cores}"}
 
 
 def run_reference(args, rank, world):
@@ -187,9 +194,11 @@ def run_reference(args, rank, world):
     from mcpm import spec, synth
     tp = args.config == 4   # all-Q8_0: the reference build cannot run it, so its C restatement is timed
     path = synth.ensure_model("q8_0" if tp else "q4_k_m", 0)
-    n_prompt = 32   # bounded prefill so the CPU run ends within minutes
+    # the GPU arm's workload: its prompt, its warm-up tokens untimed, its timed steps (the
+    # all-Q8_0 restatement is slower, so its prompt is bounded to keep the run within minutes)
+    n_prompt = 32 if tp else args.prompt
     steps = args.steps
-    cb = cpu_baseline(path, n_prompt=n_prompt, n_gen=args.warmup + steps, port_only=tp)
+    cb = cpu_baseline(path, n_prompt=n_prompt, n_gen=steps, port_only=tp, n_skip=args.warmup)
     value = cb["value"]
     batch = args.config == 3   # the reference decodes one sequence at a time: its batch rate is its batch-1 rate
     if tp:
@@ -209,9 +218,11 @@ def run_reference(args, rank, world):
             "steps": steps, "warmup": args.warmup,
             "ms_per_step": round(1000.0 / value, 3) if value else None, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8 dot / fp32", "data": "synthetic",
-            "config": {"workload": ("config3: 64 sequences decoded one at a time, CPU reference" if batch else
-                                    "config0: MiniCPM5-2B Q4_K_M greedy decode, batch 1, CPU reference"),
-                       "prompt": n_prompt, "parallelism": "openmp"},
+            "config": ({"workload": "config3: 64 sequences decoded one at a time, CPU reference", "prompt": n_prompt,
+                        "parallelism": "openmp"} if batch else
+                       {"workload": "config0: MiniCPM5-2B Q4_K_M greedy decode, batch 1 per GPU", "prompt": n_prompt,
+                        "positions": [n_prompt + args.warmup, n_prompt + args.warmup + steps - 1],
+                        "parallelism": "openmp (the reference CPU build on the host cores)"}),
             "cpu_baseline": cb,
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -625,7 +636,8 @@ def main():
         achieved = bytes_per_tok / (per_launch_ms * 1e-3) / 1e9
         value = world * args.steps / (ms_max * 1e-3)
         # config 2: the reference's CPU prefill of 8192 positions alone takes minutes; no CPU line
-        cb = None if (args.no_cpu_baseline or args.config == 2) else cpu_baseline(path)
+        cb = None if (args.no_cpu_baseline or args.config == 2) else cpu_baseline(
+            path, n_prompt=args.prompt, n_gen=args.steps, n_skip=args.warmup)
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_launch_ms, 4),

@@ -46,8 +46,11 @@ typedef struct {
     int batch_gemm;  /* batched-decode GEMM (mcpm_batch_*): MCPM_GEMM_MMA (0, int8 mma.sync, the faster
                         today) or MCPM_GEMM_TCGEN05 (1, 5th-generation tensor cores, TMEM accumulators);
                         both give bit-identical results */
-    int reserved[4];
+    int sched;       /* decode schedule options, for measurement: MCPM_SCHED_L2_PREFETCH (1) prefetches each
+                        layer's weight rows into L2 one layer ahead; every option gives the same results */
+    int reserved[3];
 } mcpm_config;
+enum { MCPM_SCHED_L2_PREFETCH = 1 };
 
 /* Creates an engine bound to cfg->device (MiniCPM5Engine constructor + init_kv_cache). */
 mcpm_status mcpm_engine_create(const mcpm_config* cfg, mcpm_engine** out);
@@ -96,6 +99,11 @@ mcpm_status mcpm_batch_read(mcpm_engine* e, float* logits, int* argmax);
  * restatement.  A per-device workspace is allocated on the first call. */
 mcpm_status mcpm_sample_top_p(const float* logits, int n, float temperature, float top_p, float r, int* out,
                               void* stream);
+/* Sampler::sample (src/sampler.cpp:8-72) on host logits: copies the n floats to the
+ * device and runs mcpm_sample_top_p there (same canonical order, same draw r); writes the
+ * token to *token_out (host).  Synchronous, on the current device. */
+mcpm_status mcpm_sample_top_p_host(const float* logits, int n, float temperature, float top_p, float r,
+                                   int* token_out);
 /* Samples the last decode step's logits (the step must have written them) and makes the
  * token the next step's input (forward with token < 0).  token_out (host) is optional. */
 mcpm_status mcpm_sample(mcpm_engine* e, float temperature, float top_p, float r, int* token_out);
@@ -208,6 +216,14 @@ mcpm_status mcpm_gemv_gate_up_q8k(const void* wg, const void* wu, const void* xq
 mcpm_status mcpm_rmsnorm_q8k(const float* x, const float* w, void* out, int n, float eps, void* stream);
 /* swiglu_and_quantize_q8k (ops.cpp:725-765); n % 256 == 0. */
 mcpm_status mcpm_swiglu_q8k(const float* gate, const float* up, void* out, int n, void* stream);
+/* RoPE and the K/V append of one decode step (apply_rope, ops.cpp:502-516, on the 16 query
+ * heads and 2 key heads; the KV write of execute_attention, ops.cpp:557-563): q[2048] and
+ * k[256] are rotated in place (interleaved pairs, theta_i = rope_base^(-2i/128), angle
+ * pos*theta_i; factors from the host C library, as the engine's table), then k and v are
+ * written to row pos of kcache / vcache ([max_seq][256] fp32).  Device pointers; pos must
+ * lie in [0, max_seq) (MCPM_CTX_OVERFLOW).  Bit-identical to the decode kernel's QKV epilogue. */
+mcpm_status mcpm_rope_kv_append(float* q, float* k, const float* v, float* kcache, float* vcache, int pos, int max_seq,
+                                float rope_base, void* stream);
 /* GQA decode attention for one layer (execute_attention, ops.cpp:537-628): writes k, v
  * (256 floats each, already rotated) into kcache/vcache ([max_seq][256] fp32) at pos,
  * then out[16*128] = softmax(q.K^T / sqrt(128)) V over positions 0..pos, 8 query heads

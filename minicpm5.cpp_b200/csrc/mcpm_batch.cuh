@@ -877,9 +877,9 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) k_b_att_units(const BStepArgs 
     const Smem sm;
     const int g = item / C, c = item % C, t0 = c * P, np = min(t0 + P, n) - t0;
     if (P == 32)
-        attention_unit32(p, sm, l, g, c, t0, np, 1u, false);
+        attention_unit32(p, reinterpret_cast<float*>(sm.wbuf(0)), l, g, c, t0, np, 1u, false);
     else
-        attention_unit_big(p, sm, l, g, c, t0, np, 1u, false);
+        attention_unit_big(p, reinterpret_cast<float*>(sm.wbuf(0)), l, g, c, t0, np, 1u, false);
 }
 
 // Head-pair combine of every sequence: blockIdx.x = sequence, blockIdx.y = head pair.  The
@@ -887,7 +887,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) k_b_att_units(const BStepArgs 
 __global__ void __launch_bounds__(DEC_THREADS, 1) k_b_att_combine(const BStepArgs a, int l) {
     const DecodeParams p = b_att_params(a, blockIdx.x);
     const Smem sm;
-    combine_pair(p, sm, l, blockIdx.y, 1u);
+    combine_pair(p, reinterpret_cast<float*>(sm.wbuf(0)), l, blockIdx.y, 1u);
 }
 
 // h = silu(gate) * up (canon_silu_mul), Q8_K ties away: one warp per 256-element block

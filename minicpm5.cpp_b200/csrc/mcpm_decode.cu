@@ -71,6 +71,7 @@ struct Smem {
     __device__ uint64_t* lmbar() const { return reinterpret_cast<uint64_t*>(smem_raw + SM_LMBAR); } // [4]
     __device__ CtaRows* rows() const { return reinterpret_cast<CtaRows*>(smem_raw + SM_ROWS); }
     __device__ LayerMeta* meta() const { return reinterpret_cast<LayerMeta*>(smem_raw + SM_META); }   // [n_layer]
+    __device__ int* flags() const { return reinterpret_cast<int*>(smem_raw + SM_FLAG); }   // [0]: early_gu
 };
 
 __device__ __forceinline__ void split_range(int n, int cta, int ncta, int& a, int& b) {
@@ -297,6 +298,47 @@ __device__ void prefetch_norms(const DecodeParams& p, const Smem& s, int l, int 
     bulk_prefetch_l2(meta_f32(p, s.meta()[l].ffn_norm), N_EMBD * 4);
 }
 
+// L2 prefetch of this CTA's rows of layer l's weight phases kind0..3, fire and forget, no
+// multicast: their shared-memory copies, one layer later, then read L2.
+__device__ __noinline__ void prefetch_layer_l2(const DecodeParams& p, const Smem& s, int l, int kind0) {
+    if (!(p.sched & SCHED_L2_PREFETCH)) return;
+    const LayerMeta& M = s.meta()[l];
+    for (int kind = kind0; kind < 4; ++kind) {
+        const PhaseLayout pl = phase_layout(M, *s.rows(), kind);
+        for (int i = 0; i < 3; ++i) {
+            if (pl.bytes[i] == 0) continue;
+            const int rb = row_bytes(phase_type(M, kind, i), phase_cols(kind));
+            bulk_prefetch_l2(phase_src(p, M, kind, i) + static_cast<size_t>(pl.row0[i]) * rb, pl.bytes[i]);
+        }
+    }
+}
+
+// Weight copies into shared memory are issued while a GEMV computes, never in front of a
+// handoff: on an SM whose TMA copy is in flight, the loads of a handoff (epoch polls, the
+// attention partials, h) queue behind the copy's bytes.  Phase w+1's copy goes into the
+// buffer of phase w-1 when phase w's weights have arrived; gate/up (buffer 0) goes right
+// after the QKV GEMV, which needs the attention scratch out of buffer 0: behind o_proj's rows
+// in buffer 1 (`early_gu`, contexts up to 2048 positions) -- longer contexts stage more K/V
+// rows and keep buffer 0, and their gate/up copy waits until attention is done.
+constexpr int ATT_B1_OFF = 28672;   // attention scratch offset inside buffer 1
+static_assert(ATT_B1_OFF + (32 * HEAD_DIM + 8 * 32 + 32 + 8 * HEAD_DIM + HEAD_DIM) * 4 <= WBUF_BYTES,
+              "32-position unit scratch behind o_proj's rows");
+static_assert(ATT_B1_OFF + (2 * ATT_MAX_CHUNKS * HEAD_DIM + 6 * ATT_MAX_CHUNKS + 4 + 256) * 4 <= WBUF_BYTES,
+              "head-pair combine scratch behind o_proj's rows");
+constexpr int COPY_THREAD = DEC_THREADS - 1;   // last warp: the fewest GEMV tasks
+
+// Weight phase wp (after the last layer: the LM head's first stage) into its buffer; the
+// fence orders this CTA's generic-proxy writes to the buffer (attention scratch) before it.
+__device__ __forceinline__ void issue_copy(const DecodeParams& p, const Smem& s, int wp, int cta, int ncta) {
+    fence_proxy_async_smem();
+    if (wp < 4 * p.n_layer) {
+        issue_weight_phase(p, s, wp, cta, ncta);
+    } else {
+        const LmPlan q = lm_plan(p, cta, ncta);
+        issue_lm_stage(p, s, q, 0);
+    }
+}
+
 // Waits for this CTA's part of weight phase wp; false on timeout.
 __device__ bool wait_weights(const DecodeParams& p, const Smem& s, int wp) {
     const int buf = wp & 1;
@@ -371,7 +413,8 @@ __device__ bool load8_epoch(const unsigned long long* src, unsigned epoch, int t
 // wait for x timed out.
 enum { X_SMEM = 1, X_EPOCH = 2 };
 template <bool AWAY, int SRC>
-__device__ bool norm_quant(const DecodeParams& p, const float* x, unsigned epoch, const float* w, const Smem& s) {
+__device__ bool norm_quant(const DecodeParams& p, const float* x, unsigned epoch, const float* w, const Smem& s,
+                           int trace_slot = -1) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     float4 w0 = make_float4(0.f, 0.f, 0.f, 0.f), w1 = w0;
     if (warp < N_EMBD / 256) {   // norm weights first: independent of x
@@ -398,6 +441,7 @@ __device__ bool norm_quant(const DecodeParams& p, const float* x, unsigned epoch
         if (lane == 0) red[warp] = a;
     }
     if (__syncthreads_or(!ok)) return false;
+    if (trace_slot >= 0 && p.trace && threadIdx.x == 0 && blockIdx.x < 148) p.trace[trace_slot + blockIdx.x] = globaltimer();
     if (warp < N_EMBD / 256) {
         const float ss = __fadd_rn(__fadd_rn(__fadd_rn(red[0], red[1]), __fadd_rn(red[2], red[3])),
                                    __fadd_rn(__fadd_rn(red[4], red[5]), __fadd_rn(red[6], red[7])));
@@ -444,6 +488,7 @@ __device__ bool phase_qkv(const DecodeParams& p, const Smem& s, int l, int token
     float2 cs0 = make_float2(0.0f, 0.0f);
     if (pr0 < (b - a) / 2 && R0 < N_EMBD + KV_DIM)
         cs0 = __ldg(p.rope + static_cast<size_t>(p.pos) * (HEAD_DIM / 2) + ((R0 & (HEAD_DIM - 1)) >> 1));
+    if (threadIdx.x == ISSUE_THREAD && l + 1 < p.n_layer) prefetch_layer_l2(p, s, l + 1, 0);
     if (l == 0) {
         embed_row(p.embd, token, s.xs());
         __syncthreads();
@@ -451,12 +496,15 @@ __device__ bool phase_qkv(const DecodeParams& p, const Smem& s, int l, int token
             for (int i = threadIdx.x; i < N_EMBD; i += blockDim.x) p.x[i] = s.xs()[i];
         norm_quant<true, X_SMEM>(p, s.xs(), 0, meta_f32(p, L.attn_norm), s);
     } else {
-        if (!norm_quant<true, X_EPOCH>(p, nullptr, x_epoch(seq, 2 * l), meta_f32(p, L.attn_norm), s)) return false;
+        if (!norm_quant<true, X_EPOCH>(p, nullptr, x_epoch(seq, 2 * l), meta_f32(p, L.attn_norm), s,
+                                       l == 2 ? TRACE_POLL + 148 : -1))
+            return false;
         trace_mark(p, 3 + 2 * (5 * (l - 1) + 4));
         trace_cta(p, l - 1, 4, 1);
     }
     trace_step(p, l, 0, 1);
     if (!wait_weights(p, s, 4 * l)) return false;
+    if (threadIdx.x == COPY_THREAD) issue_copy(p, s, 4 * l + 1, cta, ncta);   // o_proj rows: buffer 1
     trace_step(p, l, 0, 2);
     const PhaseLayout pl = phase_layout(L, *s.rows(), 0);
     const int lo[3] = {0, N_EMBD, N_EMBD + KV_DIM};
@@ -469,6 +517,8 @@ __device__ bool phase_qkv(const DecodeParams& p, const Smem& s, int l, int token
                   rv + base, (p.trace && l == 1 && cta == 0 && i == 0) ? p.trace + TRACE_GEMV + 9 : nullptr);
     }
     trace_step(p, l, 0, 3);
+    __syncthreads();   // buffer 0 read by every GEMV above
+    if (threadIdx.x == COPY_THREAD && s.flags()[0]) issue_copy(p, s, 4 * l + 2, cta, ncta);   // gate/up: buffer 0
     // RoPE on Q/K pairs (interleaved, ops.cpp:502-516 with the build's FMA contraction),
     // then Q to the query buffer and K/V into the cache at pos (ops.cpp:557-563).
     float* kdst = p.kc + (static_cast<size_t>(l) * p.max_seq + p.pos) * KV_DIM;
@@ -547,10 +597,10 @@ __device__ __forceinline__ void publish_headers(const DecodeParams& p, const flo
 // sum and fma chains, partials [head][chunk][m, l, o[128]].
 // In the decode kernel (p.qll set) q and this position's K/V rows are read from their
 // epoch-tagged copies, so no grid barrier separates the QKV phase from attention.
-__device__ void attention_unit32(const DecodeParams& p, const Smem& s, int l, int g, int c, int t0, int np,
+__device__ void attention_unit32(const DecodeParams& p, float* scratch, int l, int g, int c, int t0, int np,
                                  unsigned seq, bool flagged) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, j = lane & 7, G = lane >> 3;
-    float* vb = reinterpret_cast<float*>(s.wbuf(0));   // [32][128] V rows of the chunk
+    float* vb = scratch;                                // [32][128] V rows of the chunk
     float* sc = vb + 32 * HEAD_DIM;                     // [8][32] scores -> probabilities
     float* stat = sc + 8 * 32;                          // m[8], l[8]
     float* qsm = stat + 32;                             // [8][128] q of the group (epoch path)
@@ -700,10 +750,10 @@ static_assert((8 * HEAD_DIM + ATT_BIG_ROWS * HEAD_DIM + 8 * ATT_SC_STRIDE + 16 +
 // combine_pair: chunk o vectors of two heads, maxima, sums, weights, 1/L, output
 static_assert((2 * ATT_MAX_CHUNKS * HEAD_DIM + 6 * ATT_MAX_CHUNKS + 4 + 256) * sizeof(float) <= WBUF_BYTES,
               "combine scratch exceeds weight buffer 0");
-__device__ void attention_unit_big(const DecodeParams& p, const Smem& s, int l, int g, int c, int t0, int np,
+__device__ void attention_unit_big(const DecodeParams& p, float* scratch, int l, int g, int c, int t0, int np,
                                    unsigned seq, bool flagged) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, j = lane & 7, G = lane >> 3;
-    float* qh = reinterpret_cast<float*>(s.wbuf(0));   // [8][128]
+    float* qh = scratch;                                // [8][128]
     float* kv = qh + 8 * HEAD_DIM;                      // [ATT_BIG_ROWS][128] K, then V rows
     float* sc = kv + ATT_BIG_ROWS * HEAD_DIM;           // [8][ATT_SC_STRIDE] scores -> probabilities
     float* stat = sc + 8 * ATT_SC_STRIDE;               // m[8], l[8]
@@ -895,11 +945,11 @@ __device__ void attention_unit_big(const DecodeParams& p, const Smem& s, int l, 
 //   w_c*o_c over c, out = o * (1/L)
 // (ops.cpp:590-611 restated per chunk), and writes p.att, the Q8_K block b of p.att_q8k
 // and, in the decode kernel (p.attw set), the epoch-tagged values o_proj waits for.
-__device__ bool combine_pair(const DecodeParams& p, const Smem& s, int l, int b, unsigned seq) {
+__device__ bool combine_pair(const DecodeParams& p, float* scratch, int l, int b, unsigned seq) {
     const int n = p.pos + 1, C = attn_chunks(n);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const unsigned e = att_epoch(seq, l);
-    float* po = reinterpret_cast<float*>(s.wbuf(0));   // [2][ATT_MAX_CHUNKS][128] chunk o vectors
+    float* po = scratch;                                // [2][ATT_MAX_CHUNKS][128] chunk o vectors
     float* msm = po + 2 * ATT_MAX_CHUNKS * HEAD_DIM;    // [2][ATT_MAX_CHUNKS] chunk maxima
     float* lsm = msm + 2 * ATT_MAX_CHUNKS;              // [2][ATT_MAX_CHUNKS] chunk sums
     float* wts = lsm + 2 * ATT_MAX_CHUNKS;              // [2][ATT_MAX_CHUNKS] exp(m_c - M)
@@ -993,7 +1043,8 @@ __device__ bool combine_pair(const DecodeParams& p, const Smem& s, int l, int b,
 // DIST_COMBINE_MAX chunks in the decode kernel, the head-pair combiners on the last CTAs
 // (usually CTAs without a unit).  Shorter contexts are combined in the o_proj prologue;
 // the standalone op combines in k_att_combine.
-__device__ bool phase_attention(const DecodeParams& p, const Smem& s, int l, int cta, int ncta, unsigned seq) {
+__device__ bool phase_attention(const DecodeParams& p, const Smem& s, float* scratch, int l, int cta, int ncta,
+                                unsigned seq) {
     const int n = p.pos + 1;
     const int P = 32 * ((n + 2047) / 2048);
     const int C = (n + P - 1) / P;
@@ -1003,14 +1054,14 @@ __device__ bool phase_attention(const DecodeParams& p, const Smem& s, int l, int
         const int t0 = c * P, t1 = min(t0 + P, n), np = t1 - t0;
         __syncthreads();
         if (P == 32)
-            attention_unit32(p, s, l, g, c, t0, np, seq, flagged);
+            attention_unit32(p, scratch, l, g, c, t0, np, seq, flagged);
         else
-            attention_unit_big(p, s, l, g, c, t0, np, seq, flagged);
+            attention_unit_big(p, scratch, l, g, c, t0, np, seq, flagged);
     }
     if (flagged) {
         for (int b = ncta - 1 - cta; b < N_EMBD / 256; b += ncta) {
             __syncthreads();
-            if (!combine_pair(p, s, l, b, seq)) return false;
+            if (!combine_pair(p, scratch, l, b, seq)) return false;
         }
     }
     return true;
@@ -1103,22 +1154,19 @@ __device__ bool phase_o(const DecodeParams& p, const Smem& s, int l, int cta, in
         for (int r = 0; r < XLL_COPIES; ++r) st_epoch(p.xll + r * N_EMBD + r0 + threadIdx.x, xn, x_epoch(seq, 2 * l + 1));
     }
     trace_cta(p, l, 2, 0);
-    // down weights into the buffer just released, by a thread outside warps 0-7 (which
-    // poll the residual in the next norm)
-    if (threadIdx.x == ISSUE_THREAD) issue_weight_phase(p, s, 4 * l + 3, cta, ncta, 0);   // first half now
     return true;
 }
 
 __device__ bool phase_gu(const DecodeParams& p, const Smem& s, int l, int cta, int ncta, unsigned seq) {
     const LayerMeta& L = s.meta()[l];
-    if (!norm_quant<true, X_EPOCH>(p, nullptr, x_epoch(seq, 2 * l + 1), meta_f32(p, L.ffn_norm), s)) return false;
+    if (!norm_quant<true, X_EPOCH>(p, nullptr, x_epoch(seq, 2 * l + 1), meta_f32(p, L.ffn_norm), s,
+                                   l == 1 ? TRACE_POLL : -1))
+        return false;
     trace_mark(p, 3 + 2 * (5 * l + 2));
     trace_cta(p, l, 2, 1);
-    // second half of the down weights, after the residual wait: halving each burst of weight
-    // traffic shortens the epoch polls that run beside it
-    if (threadIdx.x == ISSUE_THREAD) issue_weight_phase(p, s, 4 * l + 3, cta, ncta, 1);
     trace_step(p, l, 3, 1);
     if (!wait_weights(p, s, 4 * l + 2)) return false;
+    if (threadIdx.x == COPY_THREAD) issue_copy(p, s, 4 * l + 3, cta, ncta);   // down rows: buffer 1
     trace_step(p, l, 3, 2);
     const PhaseLayout pl = phase_layout(L, *s.rows(), 2);
     const int n = pl.nrows[0];
@@ -1168,6 +1216,7 @@ __device__ bool phase_down(const DecodeParams& p, const Smem& s, int l, int cta,
     __syncthreads();
     trace_step(p, l, 4, 1);
     if (!wait_weights(p, s, 4 * l + 3)) return false;
+    if (threadIdx.x == COPY_THREAD) issue_copy(p, s, 4 * l + 4, cta, ncta);   // next QKV rows or LM stage 0: buffer 0
     trace_step(p, l, 4, 2);
     gemv_rows(L.td, s.wbuf(1), n, N_FF / 256, *s.xq(), s.part(), MAX_TASKS, s.rowval(),
               (p.trace && l == 1 && cta == 0) ? p.trace + TRACE_GEMV + 3 : nullptr);
@@ -1302,6 +1351,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
         for (int i = 0; i < 4; ++i) mbar_init(&s.lmbar()[i], 1);
         fence_mbar_init();
         issue_weight_phase(p, s, 0, cta, ncta);
+        prefetch_layer_l2(p, s, 0, 1);
         prefetch_attention(p, 0, cta);
         prefetch_norms(p, s, 0, cta);
     }
@@ -1309,23 +1359,29 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
     trace_mark(p, 0);
     const LmPlan lmq = lm_plan(p, cta, ncta);
     const bool flagged = att_flagged(p);
-    // Weight phase w+1 is issued while waiting at the barrier in front of phase w: its
-    // buffer was last used by phase w-1, which every thread of this CTA has finished.
+    // flags[0] (early_gu): the attention scratch fits behind this CTA's o_proj rows in buffer
+    // 1 (every layer), so gate/up can be copied into buffer 0 during attention.
+    if (threadIdx.x == 0) {
+        int ob = 0;
+        for (int l = 0; l < p.n_layer; ++l) ob = max(ob, row_bytes(s.meta()[l].to, N_EMBD));
+        s.flags()[0] = p.pos + 1 <= 2048 && (s.rows()->od1 - s.rows()->od0) * ob <= ATT_B1_OFF;
+    }
+    __syncthreads();
     for (int l = 0; l < p.n_layer; ++l) {
         if (!phase_qkv(p, s, l, token, cta, ncta, seq)) return;
         // attention units wait on the q/K/V epochs themselves: no grid barrier
         trace_mark(p, 2 + 2 * (5 * l));
-        if (threadIdx.x == 0) issue_weight_phase(p, s, 4 * l + 1, cta, ncta);
-        if (!phase_attention(p, s, l, cta, ncta, seq)) return;
+        if (!phase_attention(p, s, reinterpret_cast<float*>(s.flags()[0] ? s.wbuf(1) + ATT_B1_OFF : s.wbuf(0)), l, cta,
+                             ncta, seq))
+            return;
         if (flagged) {   // no grid barrier: o_proj waits for the combiners' epoch-tagged values
-            __syncthreads();   // buffer 0 (attention scratch) is free once this CTA's units are done
-            if (threadIdx.x == 0) {
-                fence_proxy_async_smem();
-                issue_weight_phase(p, s, 4 * l + 2, cta, ncta);
-            }
+            __syncthreads();   // the attention scratch is free once this CTA's units are done
+            if (threadIdx.x == COPY_THREAD && !s.flags()[0]) issue_copy(p, s, 4 * l + 2, cta, ncta);
             trace_mark(p, 2 + 2 * (5 * l + 1));
             trace_mark(p, 3 + 2 * (5 * l + 1));
-        } else if (!traced_barrier(p, bs, 5 * l + 1, [&] { issue_weight_phase(p, s, 4 * l + 2, cta, ncta); })) {
+        } else if (!traced_barrier(p, bs, 5 * l + 1, [&] {
+                       if (!s.flags()[0]) issue_copy(p, s, 4 * l + 2, cta, ncta);
+                   })) {
             return;
         }
         // o_proj -> gate/up and down -> next QKV exchange the residual through epoch-tagged
@@ -1334,12 +1390,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
         trace_mark(p, 2 + 2 * (5 * l + 2));
         if (!phase_gu(p, s, l, cta, ncta, seq)) return;
         if (!traced_barrier(p, bs, 5 * l + 3, [&] {
-                if (l + 1 < p.n_layer) {
-                    issue_weight_phase(p, s, 4 * (l + 1), cta, ncta);
-                } else {
-                    issue_lm_stage(p, s, lmq, 0);
-                    if (cta == 0) bulk_prefetch_l2(p.out_norm, N_EMBD * 4);
-                }
+                if (l + 1 == p.n_layer && cta == 0) bulk_prefetch_l2(p.out_norm, N_EMBD * 4);
             }))
             return;
         if (!phase_down(p, s, l, cta, ncta, seq, lmq)) return;
@@ -1366,13 +1417,13 @@ __global__ void k_kv_append(const float* __restrict__ k, const float* __restrict
 
 __global__ void __launch_bounds__(DEC_THREADS, 1) k_attention(const DecodeParams p) {
     const Smem s;
-    phase_attention(p, s, 0, blockIdx.x, gridDim.x, 1u);
+    phase_attention(p, s, reinterpret_cast<float*>(s.wbuf(0)), 0, blockIdx.x, gridDim.x, 1u);
 }
 
 // Standalone op: head pair blockIdx.x of the chunks written by k_attention (stream order).
 __global__ void __launch_bounds__(DEC_THREADS, 1) k_att_combine(const DecodeParams p) {
     const Smem s;
-    combine_pair(p, s, 0, blockIdx.x, 1u);
+    combine_pair(p, reinterpret_cast<float*>(s.wbuf(0)), 0, blockIdx.x, 1u);
 }
 
 #include "mcpm_batch.cuh"
@@ -1390,9 +1441,9 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_tp_att_units(DecodeParams p,
     const Smem sm;
     const int t0 = c * P, np = min(t0 + P, n) - t0;
     if (P == 32)
-        attention_unit32(p, sm, 0, g, c, t0, np, 1u, false);
+        attention_unit32(p, reinterpret_cast<float*>(sm.wbuf(0)), 0, g, c, t0, np, 1u, false);
     else
-        attention_unit_big(p, sm, 0, g, c, t0, np, 1u, false);
+        attention_unit_big(p, reinterpret_cast<float*>(sm.wbuf(0)), 0, g, c, t0, np, 1u, false);
 }
 
 __global__ void __launch_bounds__(DEC_THREADS, 1) k_tp_att_combine(DecodeParams p, const int* pos, int b0) {
@@ -1400,7 +1451,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_tp_att_combine(DecodeParams 
     grid_dep_wait();
     p.pos = *pos;
     const Smem sm;
-    combine_pair(p, sm, 0, b0 + blockIdx.x, 1u);
+    combine_pair(p, reinterpret_cast<float*>(sm.wbuf(0)), 0, b0 + blockIdx.x, 1u);
 }
 
 }  // namespace

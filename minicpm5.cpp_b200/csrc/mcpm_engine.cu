@@ -37,6 +37,7 @@ struct mcpm_engine {
     int n_ctas = 0;
     int req_ctas = 0;
     int batch_gemm = 0;   // MCPM_GEMM_MMA / MCPM_GEMM_TCGEN05
+    int sched = 0;        // decode schedule option bits (mcpm_config::sched)
     bool loaded = false;
     GGUFFile gguf;
     uint8_t* arena = nullptr;
@@ -253,6 +254,7 @@ DecodeParams make_params(const mcpm_engine* e, int token, int pos, int write_log
     p.bar = reinterpret_cast<unsigned*>(e->ctl + CTL_BAR);
     p.cnt = reinterpret_cast<unsigned*>(e->ctl + CTL_CNT);
     p.trace = e->trace;
+    p.sched = e->sched;
     p.token = token;
     p.pos = pos;
     p.write_logits = write_logits;
@@ -302,6 +304,7 @@ mcpm_status mcpm_engine_create(const mcpm_config* cfg, mcpm_engine** out) {
     e->device = cfg->device;
     e->req_ctas = cfg->n_ctas;
     e->batch_gemm = cfg->batch_gemm;
+    e->sched = cfg->sched;
     e->max_seq = 0;
     MCPM_CUDA(cudaSetDevice(e->device));
     MCPM_CUDA(cudaDeviceGetAttribute(&e->n_sm, cudaDevAttrMultiProcessorCount, e->device));
@@ -617,6 +620,7 @@ void mcpm_engine_destroy(mcpm_engine* e) {
 namespace {
 struct SampleWorkspace {
     int n = 0;
+    float* staged = nullptr;   // host logits copied in by mcpm_sample_top_p_host
     float* p = nullptr;
     uint32_t* gk = nullptr;
     int* gi = nullptr;
@@ -630,11 +634,13 @@ mcpm_status sample_workspace(int n, SampleWorkspace*& ws) {
     if (dev < 0 || dev >= 64) return MCPM_BAD_ARG;
     ws = &g_sample_ws[dev];
     if (ws->n < n) {
+        free_dev(ws->staged);
         free_dev(ws->p);
         free_dev(ws->gk);
         free_dev(ws->gi);
         free_dev(ws->out);
         ws->n = 0;
+        MCPM_CUDA(cudaMalloc(&ws->staged, sizeof(float) * n));
         MCPM_CUDA(cudaMalloc(&ws->p, sizeof(float) * n));
         MCPM_CUDA(cudaMalloc(&ws->gk, sizeof(uint32_t) * 2 * n));
         MCPM_CUDA(cudaMalloc(&ws->gi, sizeof(int) * 2 * n));
@@ -653,6 +659,25 @@ mcpm_status mcpm_sample_top_p(const float* logits, int n, float temperature, flo
     if (st != MCPM_OK) return st;
     return cuda_status(launch_sample_top_p(logits, n, temperature, top_p, r, out, ws->p, ws->gk, ws->gi,
                                            static_cast<cudaStream_t>(stream)));
+}
+
+mcpm_status mcpm_sample_top_p_host(const float* logits, int n, float temperature, float top_p, float r,
+                                   int* token_out) {
+    if (!logits || !token_out || n <= 0 || n > (1 << 20)) return MCPM_BAD_ARG;
+    SampleWorkspace* ws = nullptr;
+    mcpm_status st = sample_workspace(n, ws);
+    if (st != MCPM_OK) return st;
+    MCPM_CUDA(cudaMemcpy(ws->staged, logits, sizeof(float) * n, cudaMemcpyHostToDevice));
+    MCPM_CUDA(launch_sample_top_p(ws->staged, n, temperature, top_p, r, ws->out, ws->p, ws->gk, ws->gi, nullptr));
+    MCPM_CUDA(cudaMemcpy(token_out, ws->out, sizeof(int), cudaMemcpyDeviceToHost));
+    return MCPM_OK;
+}
+
+mcpm_status mcpm_rope_kv_append(float* q, float* k, const float* v, float* kcache, float* vcache, int pos, int max_seq,
+                                float rope_base, void* stream) {
+    if (!q || !k || !v || !kcache || !vcache || max_seq <= 0 || !(rope_base > 0.0f)) return MCPM_BAD_ARG;
+    if (pos < 0 || pos >= max_seq) return MCPM_CTX_OVERFLOW;
+    return cuda_status(op_rope_kv_append(q, k, v, kcache, vcache, pos, rope_base, static_cast<cudaStream_t>(stream)));
 }
 
 mcpm_status mcpm_sample(mcpm_engine* e, float temperature, float top_p, float r, int* token_out) {

@@ -32,6 +32,7 @@ constexpr int TRACE_DETAIL = 650;         // sub-step marks of layer 1: 650 + 10
 constexpr int TRACE_CTA = 720;            // layer-1 barrier k, CTA c: arrival 720 + 148k + c, release 1460 + 148k + c, SM id 2200 + c,
                                           // QKV sub-steps m = 0..2 of layer 1 at 2400 + 148m + c
 constexpr int TRACE_GEMV = 2848;          // layer-1 GEMV marks of CTA 0 (pass 1, pass 2, entry): O, D, gate, QKV
+constexpr int TRACE_POLL = 2960;          // per CTA: residual poll done, gate/up norm of layer 1 (+0), QKV norm of layer 2 (+148)
 
 // QKV row pairs [0, 1280) (Q pairs, then K, then V) are split over the CTAs in proportion
 // to their GEMV cost: a Q6_K row costs about 1.6 Q4_K rows (unaligned 210-byte blocks), so
@@ -47,6 +48,9 @@ __host__ __device__ inline int qkv_pair_boundary(int tq, int tk, int tv, int c, 
     const int pv = nq + nk + static_cast<int>((t - cq * nq - ck * nk) / cv);
     return pv < nq + nk + nv ? pv : nq + nk + nv;
 }
+
+// Decode schedule options (DecodeParams::sched, mcpm_config::sched bits).
+constexpr int SCHED_L2_PREFETCH = 1;   // L2 prefetch of the next layer's weight rows (measured slower: off)
 
 struct LayerDev {
     const uint8_t *wq, *wk, *wv, *wo, *wg, *wu, *wd;
@@ -91,6 +95,7 @@ struct DecodeParams {
     unsigned* cnt;      // [2] argmax counter
     unsigned* err;      // error bits
     unsigned long long* trace;   // optional: CTA 0 phase timestamps (2 per phase + 2)
+    int sched;          // SCHED_* option bits
     int token;          // < 0: read *token_dev
     int pos;
     int write_logits;
@@ -143,5 +148,7 @@ cudaError_t op_gemv_q8k(int type, const void* w, const void* xq, float* y, int32
                         int cols, cudaStream_t s);
 cudaError_t op_rmsnorm_q8k(const float* x, const float* w, void* out, float eps, cudaStream_t s);
 cudaError_t op_swiglu_q8k(const float* g, const float* u, void* out, int n, cudaStream_t s);
+cudaError_t op_rope_kv_append(float* q, float* k, const float* v, float* kc, float* vc, int pos, float base,
+                              cudaStream_t s);
 
 }  // namespace mcpm

@@ -199,6 +199,47 @@ cudaError_t op_swiglu_q8k(const float* g, const float* u, void* out, int n, cuda
     return cudaGetLastError();
 }
 
+namespace {
+// RoPE factors of one position (host C library, the same table the decode engine uses).
+struct RopeRow {
+    float2 cs[HEAD_DIM / 2];
+};
+
+// apply_rope (ops.cpp:502-516) on the 16 query heads and 2 key heads, pair (2i, 2i+1) of a
+// head rotated by factor i, with the reference build's contraction (one fma per output), then
+// the K and V rows written at `pos` of the cache (execute_attention, ops.cpp:557-563).
+__global__ void k_rope_kv_append(float* __restrict__ q, float* __restrict__ k, const float* __restrict__ v,
+                                 float* __restrict__ kc, float* __restrict__ vc, int pos, const RopeRow rr) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;   // pair index over [q pairs; k pairs]
+    constexpr int QP = N_EMBD / 2, KP = KV_DIM / 2;
+    if (t < QP + KP) {
+        float* vec = t < QP ? q + 2 * t : k + 2 * (t - QP);
+        const int i = (t < QP ? t : t - QP) & (HEAD_DIM / 2 - 1);
+        const float2 c = rr.cs[i];
+        const float v0 = vec[0], v1 = vec[1];
+        const float r0 = __fmaf_rn(c.x, v0, -__fmul_rn(c.y, v1));
+        const float r1 = __fmaf_rn(c.y, v0, __fmul_rn(c.x, v1));
+        vec[0] = r0;
+        vec[1] = r1;
+        if (t >= QP) {
+            float* kd = kc + static_cast<size_t>(pos) * KV_DIM + 2 * (t - QP);
+            kd[0] = r0;
+            kd[1] = r1;
+        }
+    }
+    if (t < KV_DIM) vc[static_cast<size_t>(pos) * KV_DIM + t] = v[t];
+}
+}  // namespace
+
+cudaError_t op_rope_kv_append(float* q, float* k, const float* v, float* kc, float* vc, int pos, float base,
+                              cudaStream_t s) {
+    RopeRow rr;
+    rope_row(pos, base, rr.cs);
+    constexpr int pairs = N_EMBD / 2 + KV_DIM / 2;
+    k_rope_kv_append<<<(pairs + 255) / 256, 256, 0, s>>>(q, k, v, kc, vc, pos, rr);
+    return cudaGetLastError();
+}
+
 cudaError_t op_rmsnorm_q8k(const float* x, const float* w, void* out, float eps, cudaStream_t s) {
     k_rmsnorm_q8k<<<1, 256, 0, s>>>(x, w, static_cast<uint8_t*>(out), eps);
     return cudaGetLastError();

@@ -34,7 +34,7 @@ class MCPMError(RuntimeError):
 
 class mcpm_config(C.Structure):
     _fields_ = [("device", C.c_int), ("max_seq", C.c_int), ("n_ctas", C.c_int), ("batch_gemm", C.c_int),
-                ("reserved", C.c_int * 4)]
+                ("sched", C.c_int), ("reserved", C.c_int * 3)]
 
 
 P, I, F = C.c_void_p, C.c_int, C.c_float
@@ -56,6 +56,8 @@ SIGNATURES = {
     "mcpm_batch_init": (I, [P, I, I]),
     "mcpm_sample_top_p": (I, [P, I, F, F, F, P, P]),
     "mcpm_sample": (I, [P, F, F, F, C.POINTER(I)]),
+    "mcpm_sample_top_p_host": (I, [C.POINTER(F), I, F, F, F, C.POINTER(I)]),
+    "mcpm_rope_kv_append": (I, [P, P, P, P, P, I, I, F, P]),
     "mcpm_batch_step_async": (I, [P, C.POINTER(I), C.POINTER(I)]),
     "mcpm_batch_read": (I, [P, C.POINTER(F), C.POINTER(I)]),
     "mcpm_model_dims": (I, [P, C.POINTER(I)]),
@@ -132,10 +134,11 @@ def _fptr(a: np.ndarray):
 class MiniCPM5Engine:
     """Device engine behind the reference's MiniCPM5Engine interface."""
 
-    def __init__(self, device: int = 0, max_seq: int = 0, n_ctas: int = 0, batch_gemm: int = 0):
-        """batch_gemm: 0 = int8 mma.sync batched GEMMs, 1 = tcgen05 (bit-identical results)."""
+    def __init__(self, device: int = 0, max_seq: int = 0, n_ctas: int = 0, batch_gemm: int = 0, sched: int = 0):
+        """batch_gemm: 0 = int8 mma.sync batched GEMMs, 1 = tcgen05 (bit-identical results).
+        sched: decode schedule option bits (include/mcpm.h MCPM_SCHED_*; results are the same)."""
         self.lib = load_library()
-        cfg = mcpm_config(device, max_seq, n_ctas, batch_gemm)
+        cfg = mcpm_config(device, max_seq, n_ctas, batch_gemm, sched)
         h = P()
         check(self.lib.mcpm_engine_create(C.byref(cfg), C.byref(h)), "mcpm_engine_create")
         self.h = h
@@ -296,6 +299,21 @@ def gemv_q8k_timed(ggml_type, w_ptr, n_copies, xq_ptr, y_ptr, rows, cols, reps, 
     check(load_library().mcpm_gemv_q8k_timed(ggml_type, w_ptr, n_copies, xq_ptr, y_ptr, rows, cols, reps,
                                              C.byref(ms), stream), "mcpm_gemv_q8k_timed")
     return ms.value
+
+
+def rope_kv_append(q_ptr, k_ptr, v_ptr, kc_ptr, vc_ptr, pos, max_seq, rope_base=5000000.0, stream=0) -> None:
+    """apply_rope on q (16 heads) and k (2 heads) in place, then k, v written at row pos."""
+    check(load_library().mcpm_rope_kv_append(q_ptr, k_ptr, v_ptr, kc_ptr, vc_ptr, pos, max_seq, rope_base, stream),
+          "mcpm_rope_kv_append")
+
+
+def sample_top_p_host(logits: np.ndarray, temperature: float, top_p: float, r: float) -> int:
+    """Sampler::sample on host logits, run on the device (same token as the device sampler)."""
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    tok = C.c_int()
+    check(load_library().mcpm_sample_top_p_host(_fptr(lg), lg.size, temperature, top_p, r, C.byref(tok)),
+          "mcpm_sample_top_p_host")
+    return tok.value
 
 
 def attention(q_ptr, k_ptr, v_ptr, kc_ptr, vc_ptr, pos, max_seq, out_ptr, out_q8k_ptr=None, stream=0) -> None:

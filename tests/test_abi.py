@@ -49,14 +49,14 @@ def test_ops_reject_bad_arguments_without_touching_memory():
     assert lib.mcpm_rmsnorm_q8k(16, 16, 16, 1024, 1e-6, None) == E.BAD_ARG
 
 
-def facade_build(out_dir):
-    """Compiles tests/cpp/facade_driver.cpp against include/minicpm5_engine.hpp and links it
-    with the in-tree libmcpm.so; returns the binary path."""
+def facade_build(out_dir, name="facade_driver"):
+    """Compiles tests/cpp/<name>.cpp against include/minicpm5_engine.hpp and links it with the
+    in-tree libmcpm.so; returns the binary path."""
     import subprocess
     from mcpm import engine as E
     lib = E.lib_path()
-    exe = os.path.join(str(out_dir), "facade_driver")
-    cmd = ["g++", "-std=c++17", "-O1", "-I", os.path.join(REPO, "include"), os.path.join(REPO, "tests", "cpp", "facade_driver.cpp"),
+    exe = os.path.join(str(out_dir), name)
+    cmd = ["g++", "-std=c++17", "-O1", "-I", os.path.join(REPO, "include"), os.path.join(REPO, "tests", "cpp", name + ".cpp"),
            "-o", exe, lib, "-L/usr/local/cuda/lib64", "-lcudart", "-Wl,-rpath," + os.path.dirname(lib) + ":/usr/local/cuda/lib64"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
@@ -64,5 +64,6 @@ def facade_build(out_dir):
 
 
 def test_cpp_facade_compiles_and_links(tmp_path):
-    """The reference-shaped C++ facade (init_kv_cache / load_model / forward) builds against the C ABI."""
+    """The reference-shaped C++ facades (MiniCPM5Engine, Sampler) build against the C ABI."""
     assert os.path.exists(facade_build(tmp_path))
+    assert os.path.exists(facade_build(tmp_path, "sampler_driver"))

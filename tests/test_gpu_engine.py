@@ -154,3 +154,37 @@ def test_cpp_facade_token_loop(cuda, model_path, tmp_path):
         want.append(tok)
     e.close()
     assert got == want
+
+
+def test_cpp_sampler_loop_device_logits(cuda, oracle, model_path, tmp_path):
+    """The reference's sampling loop (engine.forward, then Sampler::sample on the returned
+    vector) through the C++ facades: with the logits copied to the host, left on the device
+    (set_host_logits(false)), or copied into the caller's own vector, the same seeded draws
+    give the same tokens, and each equals the C restatement's top-p draw on its logits."""
+    import subprocess
+    import oracle as O
+    from mcpm import synth
+    from test_abi import facade_build
+    exe = facade_build(tmp_path, "sampler_driver")
+    prompt = [int(t) for t in synth.prompt_ids(5, seed=31)]
+    temp, top_p, seed, n_gen = 30.0, 0.95, 7, 4   # temperature 30 spreads this model's logits
+    runs = {}
+    for mode in ("host", "device", "copy"):
+        r = subprocess.run([exe, model_path, mode, str(n_gen), str(temp), str(top_p), str(seed)] +
+                           [str(t) for t in prompt], capture_output=True, text=True, timeout=300)
+        assert r.returncode == 0, r.stderr
+        runs[mode] = [(int(a), float(b)) for a, b in (ln.split() for ln in r.stdout.split("\n") if ln.strip())]
+    assert runs["host"] == runs["device"] == runs["copy"]
+    toks = [t for t, _ in runs["host"]]
+    assert len(set(toks)) > 1
+    om = O.OracleModel(oracle, model_path, 16)
+    lg = np.zeros(130560, np.float32)
+    inputs = prompt + toks[:-1]
+    k = 0
+    for pos, t in enumerate(inputs):
+        om.forward(t, pos, lg)
+        if pos >= len(prompt) - 1:
+            tok, r = runs["host"][k]
+            assert oracle.sample_top_p(lg, temp, top_p, r)[0] == tok
+            k += 1
+    om.close()

@@ -236,3 +236,32 @@ def test_attention_rejects_out_of_range(cuda):
     with pytest.raises(E.MCPMError) as ei:
         E.attention(t.data_ptr(), t.data_ptr(), t.data_ptr(), t.data_ptr(), t.data_ptr(), 1, 20000, t.data_ptr())
     assert ei.value.status == E.BAD_ARG
+
+
+def test_rope_kv_append_bitexact(cuda, oracle):
+    """mcpm_rope_kv_append: q (16 heads) and k (2 heads) rotated in place exactly as the
+    restatement's apply_rope, k and v written at row pos, every other cache row untouched."""
+    from mcpm import engine as E
+    rng = np.random.default_rng(21)
+    max_seq = 40
+    for pos in (0, 7, 39):
+        q = rng.normal(0, 3, 2048).astype(np.float32)
+        k = rng.normal(0, 3, 256).astype(np.float32)
+        v = rng.normal(0, 3, 256).astype(np.float32)
+        kc = rng.normal(0, 1, (max_seq, 256)).astype(np.float32)
+        vc = rng.normal(0, 1, (max_seq, 256)).astype(np.float32)
+        d = [cuda.from_numpy(a.copy()).cuda() for a in (q, k, v, kc, vc)]
+        E.rope_kv_append(*[t.data_ptr() for t in d], pos, max_seq)
+        cuda.cuda.synchronize()
+        want_q, want_k = oracle.rope(q, pos, 16), oracle.rope(k, pos, 2)
+        gq, gk, gkc, gvc = d[0].cpu().numpy(), d[1].cpu().numpy(), d[3].cpu().numpy(), d[4].cpu().numpy()
+        assert np.array_equal(gq.view(np.uint32), want_q.view(np.uint32))
+        assert np.array_equal(gk.view(np.uint32), want_k.view(np.uint32))
+        assert np.array_equal(gkc[pos], want_k) and np.array_equal(gvc[pos], v)
+        others = np.arange(max_seq) != pos
+        assert np.array_equal(gkc[others], kc[others]) and np.array_equal(gvc[others], vc[others])
+    lib = E.load_library()
+    t = cuda.zeros(4096, dtype=cuda.float32, device="cuda")
+    p = t.data_ptr()
+    assert lib.mcpm_rope_kv_append(p, p, p, p, p, 8, 8, 5e6, None) == E.CTX_OVERFLOW
+    assert lib.mcpm_rope_kv_append(None, p, p, p, p, 0, 8, 5e6, None) == E.BAD_ARG
