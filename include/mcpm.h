@@ -47,10 +47,17 @@ typedef struct {
                         today) or MCPM_GEMM_TCGEN05 (1, 5th-generation tensor cores, TMEM accumulators);
                         both give bit-identical results */
     int sched;       /* decode schedule options, for measurement: MCPM_SCHED_L2_PREFETCH (1) prefetches each
-                        layer's weight rows into L2 one layer ahead; every option gives the same results */
-    int reserved[3];
+                        layer's weight rows into L2 one layer ahead; MCPM_SCHED_ATT_COMBINERS (2) combines
+                        the attention chunks on 8 head-pair CTAs at every context length (by default only
+                        above 16 chunks; below, every CTA combines all heads); every option gives the same
+                        results */
+    int kv_type;     /* KV-cache element type: MCPM_KV_F32 (0, the reference's std::vector<float> cache,
+                        model.h:66-67) or MCPM_KV_F16 (1: K and V rounded to fp16 when written, half the
+                        cache bytes; the attention reads them back exactly and computes in fp32) */
+    int reserved[2];
 } mcpm_config;
-enum { MCPM_SCHED_L2_PREFETCH = 1 };
+enum { MCPM_SCHED_L2_PREFETCH = 1, MCPM_SCHED_ATT_COMBINERS = 2 };
+enum { MCPM_KV_F32 = 0, MCPM_KV_F16 = 1 };
 
 /* Creates an engine bound to cfg->device (MiniCPM5Engine constructor + init_kv_cache). */
 mcpm_status mcpm_engine_create(const mcpm_config* cfg, mcpm_engine** out);
@@ -75,12 +82,25 @@ mcpm_status mcpm_sync(mcpm_engine* e);
 /* Device pointers of the last step's logits (n_vocab floats) and argmax (one int). */
 const float* mcpm_logits_device(mcpm_engine* e);
 const int* mcpm_argmax_device(mcpm_engine* e);
-/* Internal state for parity checks: residual x (n_embd floats), one K and V row. */
+/* Internal state for parity checks: residual x (n_embd floats), one K and V row (widened to
+ * fp32 from an fp16 cache). */
 mcpm_status mcpm_read_x(mcpm_engine* e, float* x_host);
 mcpm_status mcpm_read_kv(mcpm_engine* e, int layer, int pos, float* k_host, float* v_host);
 /* Writes n_pos K and V rows ([n_pos][n_head_kv * head_dim] floats each) of one layer from
- * position pos0: restores a saved cache, or seeds one for a parity check of a late step. */
+ * position pos0: restores a saved cache, or seeds one for a parity check of a late step.
+ * An fp16 cache stores them rounded to nearest-even, as a decode step rounds its own rows. */
 mcpm_status mcpm_write_kv(mcpm_engine* e, int layer, int pos0, int n_pos, const float* k_host, const float* v_host);
+/* Session snapshot and restore (multi-turn sessions; the reference re-renders and
+ * re-prefills the whole conversation every turn, src/chat_session.cpp:126-160).  A snapshot
+ * holds the KV rows of positions [0, n_pos) of every layer, mcpm_kv_snapshot_bytes(e, n_pos)
+ * bytes laid out [layer][K, V][pos][256] in the cache's element type (fp32, or fp16 with
+ * kv_type MCPM_KV_F16; host memory).  After mcpm_kv_restore(e, n_pos, ...) -- into this engine
+ * or another one with the same model, kv_type and max_seq >= n_pos -- decoding
+ * or mcpm_prefill from position n_pos continues the session exactly as it was (the next step
+ * depends only on the cache rows below its position and on its token).  Synchronous. */
+size_t mcpm_kv_snapshot_bytes(mcpm_engine* e, int n_pos);
+mcpm_status mcpm_kv_snapshot(mcpm_engine* e, int n_pos, void* host, size_t bytes);
+mcpm_status mcpm_kv_restore(mcpm_engine* e, int n_pos, const void* host, size_t bytes);
 /* Batched decode (the reference's forward once per sequence, for n_seq independent
  * sequences in lockstep).  mcpm_batch_init allocates a KV cache of max_seq positions for
  * each of n_seq <= 64 sequences (zeroed; positions restart at 0).  mcpm_batch_step_async
@@ -89,6 +109,16 @@ mcpm_status mcpm_write_kv(mcpm_engine* e, int layer, int pos0, int n_pos, const 
  * previous positions + 1.  mcpm_batch_read waits and copies the last step's logits
  * ([n_seq][n_vocab], optional) and greedy tokens ([n_seq], optional). */
 mcpm_status mcpm_batch_init(mcpm_engine* e, int n_seq, int max_seq);
+/* Batched prefill of the engine's own sequence: positions pos0 .. pos0+n-1 of `tokens` (host,
+ * n ids) in chunks of up to 64 positions, each chunk one batched step whose rows share the
+ * engine's KV cache (row i attends to positions 0 .. pos0+i, causal), so every K/V row and
+ * the last position's logits equal n calls of mcpm_forward bit for bit (the reference
+ * prefills token by token, src/chat_session.cpp:154-160).  logits_out (host, n_vocab) and
+ * argmax_out (host) receive the last position's logits and greedy token; the device keeps
+ * them as a decode step would, so mcpm_sample and mcpm_forward(token < 0, pos0 + n) continue
+ * from the prompt.  Synchronous.  Row buffers for 64 positions are allocated on the first
+ * call and kept until the model is unloaded. */
+mcpm_status mcpm_prefill(mcpm_engine* e, const int* tokens, int n, int pos0, float* logits_out, int* argmax_out);
 mcpm_status mcpm_batch_step_async(mcpm_engine* e, const int* tokens, const int* pos);
 mcpm_status mcpm_batch_read(mcpm_engine* e, float* logits, int* argmax);
 /* Top-p sampling on the device (Sampler::sample, src/sampler.cpp:8-72): logits (device,

@@ -763,6 +763,7 @@ __device__ void b_norm_quant(const float* xs, const float* w, int8_t* qs, float*
 
 struct BStepArgs {
     int n_seq, max_seq, n_layer;
+    size_t kv_seq_stride;   // floats between two rows' caches; 0: every row one sequence's cache (prefill)
     float *kc, *vc, *x, *y, *q, *att_part, *att, *logits;
     int8_t* aqs;
     float* ad;
@@ -776,7 +777,7 @@ struct BStepArgs {
 };
 
 __device__ __forceinline__ size_t b_kv_off(const BStepArgs& a, int s, int l) {
-    return (static_cast<size_t>(s) * a.n_layer + l) * a.max_seq * KV_DIM;
+    return static_cast<size_t>(s) * a.kv_seq_stride + static_cast<size_t>(l) * a.max_seq * KV_DIM;
 }
 
 // Layer-0 input: embedding row of each sequence's token, then RMSNorm + Q8_K (ties away).
@@ -814,11 +815,12 @@ __global__ void __launch_bounds__(256) k_b_res_norm(const BStepArgs a) {
 
 // RoPE on q and k (interleaved pairs, as in phase_qkv), q to its buffer, K/V into the
 // sequence's cache at its position.
+template <typename KT>
 __global__ void __launch_bounds__(256) k_b_rope_kv(const BStepArgs a, int l) {
     const int s = blockIdx.x, pos = a.pos[s];
     const float* y = a.y + static_cast<size_t>(s) * 2 * N_FF;
-    float* kdst = a.kc + b_kv_off(a, s, l) + static_cast<size_t>(pos) * KV_DIM;
-    float* vdst = a.vc + b_kv_off(a, s, l) + static_cast<size_t>(pos) * KV_DIM;
+    KT* kdst = reinterpret_cast<KT*>(a.kc) + b_kv_off(a, s, l) + static_cast<size_t>(pos) * KV_DIM;
+    KT* vdst = reinterpret_cast<KT*>(a.vc) + b_kv_off(a, s, l) + static_cast<size_t>(pos) * KV_DIM;
     constexpr int NPAIR = (N_EMBD + 2 * KV_DIM) / 2, PER = NPAIR / 256;   // 5 pairs per thread
     static_assert(NPAIR % 256 == 0, "pairs per thread");
     float2 vv[PER], cc[PER];   // every load before any store
@@ -840,21 +842,22 @@ __global__ void __launch_bounds__(256) k_b_rope_kv(const BStepArgs a, int l) {
                 a.q[static_cast<size_t>(s) * N_EMBD + R] = r0;
                 a.q[static_cast<size_t>(s) * N_EMBD + R + 1] = r1;
             } else {
-                kdst[R - N_EMBD] = r0;
-                kdst[R - N_EMBD + 1] = r1;
+                kdst[R - N_EMBD] = KvElt<KT>::put(r0);
+                kdst[R - N_EMBD + 1] = KvElt<KT>::put(r1);
             }
         } else {
-            vdst[R - N_EMBD - KV_DIM] = v0;
-            vdst[R - N_EMBD - KV_DIM + 1] = v1;
+            vdst[R - N_EMBD - KV_DIM] = KvElt<KT>::put(v0);
+            vdst[R - N_EMBD - KV_DIM + 1] = KvElt<KT>::put(v1);
         }
     }
 }
 
+template <typename KT>
 __device__ DecodeParams b_att_params(const BStepArgs& a, int s) {
     DecodeParams p{};
     p.q = a.q + static_cast<size_t>(s) * N_EMBD;
-    p.kc = a.kc + b_kv_off(a, s, 0);
-    p.vc = a.vc + b_kv_off(a, s, 0);
+    p.kc = reinterpret_cast<float*>(reinterpret_cast<KT*>(a.kc) + b_kv_off(a, s, 0));
+    p.vc = reinterpret_cast<float*>(reinterpret_cast<KT*>(a.vc) + b_kv_off(a, s, 0));
     p.max_seq = a.max_seq;
     p.pos = a.pos[s];
     p.att_part = a.att_part + static_cast<size_t>(s) * ATT_PART_FLOATS;
@@ -869,23 +872,24 @@ __device__ DecodeParams b_att_params(const BStepArgs& a, int s) {
 // Attention units of every sequence: blockIdx.x = sequence, blockIdx.y = (KV group, chunk).
 // Two CTAs per SM (64 registers, no spills; shared memory 2 x 24 KB, or 2 x 96 KB for chunks
 // longer than 32): thousands of short units, so the second CTA hides the first one's loads.
+template <typename KT>
 __global__ void __launch_bounds__(DEC_THREADS, 2) k_b_att_units(const BStepArgs a, int l) {
     const int s = blockIdx.x, item = blockIdx.y;
     const int n = a.pos[s] + 1, P = 32 * ((n + 2047) / 2048), C = (n + P - 1) / P;
     if (item >= 2 * C) return;
-    const DecodeParams p = b_att_params(a, s);
+    const DecodeParams p = b_att_params<KT>(a, s);
     const Smem sm;
     const int g = item / C, c = item % C, t0 = c * P, np = min(t0 + P, n) - t0;
     if (P == 32)
-        attention_unit32(p, reinterpret_cast<float*>(sm.wbuf(0)), l, g, c, t0, np, 1u, false);
+        attention_unit32<KT>(p, reinterpret_cast<float*>(sm.wbuf(0)), l, g, c, t0, np, 1u, false);
     else
-        attention_unit_big(p, reinterpret_cast<float*>(sm.wbuf(0)), l, g, c, t0, np, 1u, false);
+        attention_unit_big<KT>(p, reinterpret_cast<float*>(sm.wbuf(0)), l, g, c, t0, np, 1u, false);
 }
 
 // Head-pair combine of every sequence: blockIdx.x = sequence, blockIdx.y = head pair.  The
 // Q8_K (ties to even) of the result is the o_proj input.
 __global__ void __launch_bounds__(DEC_THREADS, 1) k_b_att_combine(const BStepArgs a, int l) {
-    const DecodeParams p = b_att_params(a, blockIdx.x);
+    const DecodeParams p = b_att_params<float>(a, blockIdx.x);   // the combine reads no cache row
     const Smem sm;
     combine_pair(p, reinterpret_cast<float*>(sm.wbuf(0)), l, blockIdx.y, 1u);
 }

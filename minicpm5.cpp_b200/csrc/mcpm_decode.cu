@@ -281,14 +281,15 @@ __device__ bool traced_barrier(const DecodeParams& p, BarState& bs, int ph, F&& 
 
 // Thread 0: L2 prefetch of the K/V rows (both KV heads, contiguous) of this CTA's
 // attention chunk of layer l; the row at pos is written later by the QKV phase.
+template <typename KT>
 __device__ void prefetch_attention(const DecodeParams& p, int l, int cta) {
     const int n = p.pos + 1, P = 32 * ((n + 2047) / 2048), C = (n + P - 1) / P;
     if (cta >= 2 * C) return;
     const int c = cta % C, t0 = c * P, t1 = min(t0 + P, n);
     const size_t off = (static_cast<size_t>(l) * p.max_seq + t0) * KV_DIM;
-    const uint32_t bytes = static_cast<uint32_t>(t1 - t0) * KV_DIM * 4;
-    bulk_prefetch_l2(p.kc + off, bytes);
-    bulk_prefetch_l2(p.vc + off, bytes);
+    const uint32_t bytes = static_cast<uint32_t>(t1 - t0) * KV_DIM * sizeof(KT);
+    bulk_prefetch_l2(reinterpret_cast<const KT*>(p.kc) + off, bytes);
+    bulk_prefetch_l2(reinterpret_cast<const KT*>(p.vc) + off, bytes);
 }
 
 // L2 prefetch of layer l's two norm weight vectors (8 KB each), by CTA 0 only.
@@ -480,6 +481,7 @@ __device__ __forceinline__ unsigned long long* att_header(const DecodeParams& p,
 }
 
 // ------------------------------------------------------------------------ phases
+template <typename KT>
 __device__ bool phase_qkv(const DecodeParams& p, const Smem& s, int l, int token, int cta, int ncta, unsigned seq) {
     const LayerMeta& L = s.meta()[l];
     const int a = L.qkv0, b = L.qkv1;   // same split as phase_layout
@@ -521,30 +523,35 @@ __device__ bool phase_qkv(const DecodeParams& p, const Smem& s, int l, int token
     if (threadIdx.x == COPY_THREAD && s.flags()[0]) issue_copy(p, s, 4 * l + 2, cta, ncta);   // gate/up: buffer 0
     // RoPE on Q/K pairs (interleaved, ops.cpp:502-516 with the build's FMA contraction),
     // then Q to the query buffer and K/V into the cache at pos (ops.cpp:557-563).
-    float* kdst = p.kc + (static_cast<size_t>(l) * p.max_seq + p.pos) * KV_DIM;
-    float* vdst = p.vc + (static_cast<size_t>(l) * p.max_seq + p.pos) * KV_DIM;
+    // K and V as the cache stores them (fp16 rows: rounded once here, and the attention units
+    // read this launch's rows from the epoch-tagged copies in the same rounded form)
+    KT* kdst = reinterpret_cast<KT*>(p.kc) + (static_cast<size_t>(l) * p.max_seq + p.pos) * KV_DIM;
+    KT* vdst = reinterpret_cast<KT*>(p.vc) + (static_cast<size_t>(l) * p.max_seq + p.pos) * KV_DIM;
     for (int pr = threadIdx.x; pr < (b - a) / 2; pr += blockDim.x) {
         const int R = a + 2 * pr;
         const float v0 = rv[2 * pr], v1 = rv[2 * pr + 1];
         if (R < N_EMBD + KV_DIM) {
             const float2 c = pr == pr0 ? cs0 : __ldg(p.rope + static_cast<size_t>(p.pos) * (HEAD_DIM / 2) +
                                                      ((R & (HEAD_DIM - 1)) >> 1));
-            const float r0 = __fmaf_rn(c.x, v0, -__fmul_rn(c.y, v1));
-            const float r1 = __fmaf_rn(c.y, v0, __fmul_rn(c.x, v1));
+            float r0 = __fmaf_rn(c.x, v0, -__fmul_rn(c.y, v1));
+            float r1 = __fmaf_rn(c.y, v0, __fmul_rn(c.x, v1));
             if (R < N_EMBD) {
                 p.q[R] = r0;
                 p.q[R + 1] = r1;
             } else {
-                kdst[R - N_EMBD] = r0;
-                kdst[R - N_EMBD + 1] = r1;
+                r0 = kv_round<KT>(r0);
+                r1 = kv_round<KT>(r1);
+                kdst[R - N_EMBD] = KvElt<KT>::put(r0);
+                kdst[R - N_EMBD + 1] = KvElt<KT>::put(r1);
             }
             st_epoch(p.qll + R, r0, qkv_epoch(seq, l));
             st_epoch(p.qll + R + 1, r1, qkv_epoch(seq, l));
         } else {
-            vdst[R - N_EMBD - KV_DIM] = v0;
-            vdst[R - N_EMBD - KV_DIM + 1] = v1;
-            st_epoch(p.qll + R, v0, qkv_epoch(seq, l));
-            st_epoch(p.qll + R + 1, v1, qkv_epoch(seq, l));
+            const float w0 = kv_round<KT>(v0), w1 = kv_round<KT>(v1);
+            vdst[R - N_EMBD - KV_DIM] = KvElt<KT>::put(w0);
+            vdst[R - N_EMBD - KV_DIM + 1] = KvElt<KT>::put(w1);
+            st_epoch(p.qll + R, w0, qkv_epoch(seq, l));
+            st_epoch(p.qll + R + 1, w1, qkv_epoch(seq, l));
         }
     }
     return true;
@@ -559,9 +566,10 @@ __device__ __forceinline__ int attn_chunks(int n) {
     return (n + P - 1) / P;
 }
 
-// Decode kernel with more than DIST_COMBINE_MAX chunks: no grid barrier after attention.
+// Decode kernel with more than DIST_COMBINE_MAX chunks (or any number, with the
+// SCHED_ATT_COMBINERS option): head-pair combiners, no grid barrier after attention.
 __device__ __forceinline__ bool att_flagged(const DecodeParams& p) {
-    return p.attw != nullptr && attn_chunks(p.pos + 1) > DIST_COMBINE_MAX;
+    return p.attw != nullptr && ((p.sched & SCHED_ATT_COMBINERS) || attn_chunks(p.pos + 1) > DIST_COMBINE_MAX);
 }
 
 // Unit tail: the (m, l) headers of the chunk's 8 heads (stat[0..7] maxima, stat[8..15]
@@ -597,32 +605,35 @@ __device__ __forceinline__ void publish_headers(const DecodeParams& p, const flo
 // sum and fma chains, partials [head][chunk][m, l, o[128]].
 // In the decode kernel (p.qll set) q and this position's K/V rows are read from their
 // epoch-tagged copies, so no grid barrier separates the QKV phase from attention.
+template <typename KT>
 __device__ void attention_unit32(const DecodeParams& p, float* scratch, int l, int g, int c, int t0, int np,
                                  unsigned seq, bool flagged) {
+    using E = KvElt<KT>;
+    constexpr int CPR = HEAD_DIM / E::PER16;   // 16-byte copies per cache row
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, j = lane & 7, G = lane >> 3;
-    float* vb = scratch;                                // [32][128] V rows of the chunk
-    float* sc = vb + 32 * HEAD_DIM;                     // [8][32] scores -> probabilities
+    KT* vb = reinterpret_cast<KT*>(scratch);            // [32][128] V rows of the chunk (a float-sized slot)
+    float* sc = scratch + 32 * HEAD_DIM;                // [8][32] scores -> probabilities
     float* stat = sc + 8 * 32;                          // m[8], l[8]
     float* qsm = stat + 32;                             // [8][128] q of the group (epoch path)
     float* krow = qsm + 8 * HEAD_DIM;                   // [128] K row at pos (epoch path)
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(HEAD_DIM)));
-    const float* kl = p.kc + static_cast<size_t>(l) * p.max_seq * KV_DIM + g * HEAD_DIM;
-    const float* vl = p.vc + static_cast<size_t>(l) * p.max_seq * KV_DIM + g * HEAD_DIM;
+    const KT* kl = reinterpret_cast<const KT*>(p.kc) + static_cast<size_t>(l) * p.max_seq * KV_DIM + g * HEAD_DIM;
+    const KT* vl = reinterpret_cast<const KT*>(p.vc) + static_cast<size_t>(l) * p.max_seq * KV_DIM + g * HEAD_DIM;
     const bool epoch_in = p.qll != nullptr;
     const int cur = epoch_in && t0 + np - 1 == p.pos ? np - 1 : -1;   // chunk row published this launch
     const int ncache = cur >= 0 ? np - 1 : np;                         // rows read from the cache
-    for (int i = tid; i < ncache * 32; i += blockDim.x)
-        cp_async16(vb + 4 * i, vl + static_cast<size_t>(t0 + (i >> 5)) * KV_DIM + 4 * (i & 31));
+    for (int i = tid; i < ncache * CPR; i += blockDim.x)
+        cp_async16(vb + E::PER16 * i, vl + static_cast<size_t>(t0 + i / CPR) * KV_DIM + E::PER16 * (i % CPR));
     cp_async_commit();
     const int tA = 2 * warp, tB = tA + 1;
     const bool va = tA < np, vbv = tB < np;
-    const float* kA = kl + static_cast<size_t>(t0 + (va && tA != cur ? tA : 0)) * KV_DIM + 4 * j;
-    const float* kB = kl + static_cast<size_t>(t0 + (vbv && tB != cur ? tB : 0)) * KV_DIM + 4 * j;
+    const KT* kA = kl + static_cast<size_t>(t0 + (va && tA != cur ? tA : 0)) * KV_DIM + 4 * j;
+    const KT* kB = kl + static_cast<size_t>(t0 + (vbv && tB != cur ? tB : 0)) * KV_DIM + 4 * j;
     float4 qa[4], qb[4], ka[4], kb[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {   // cached K rows first: their loads overlap the waits below
-        ka[i] = ld_cg_f4(kA + 32 * i);
-        kb[i] = ld_cg_f4(kB + 32 * i);
+        ka[i] = E::ld4(kA + 32 * i);
+        kb[i] = E::ld4(kB + 32 * i);
     }
     if (epoch_in) {
         const unsigned ep = qkv_epoch(seq, l);
@@ -638,7 +649,7 @@ __device__ void attention_unit32(const DecodeParams& p, float* scratch, int l, i
         } else if (cur >= 0 && tid < 256 + 64) {
             float4 v;
             ok = load4_epoch(p.qll + N_EMBD + KV_DIM + g * HEAD_DIM + 4 * (tid - 288), ep, v, p.err);
-            reinterpret_cast<float4*>(vb + cur * HEAD_DIM)[tid - 288] = v;
+            E::st4(vb + cur * HEAD_DIM + 4 * (tid - 288), v);
         }
         if (__syncthreads_or(!ok)) {
             cp_async_wait_all();
@@ -715,7 +726,7 @@ __device__ void attention_unit32(const DecodeParams& p, float* scratch, int l, i
         const float4 s1 = *reinterpret_cast<const float4*>(sc + h1 * 32 + t);
         float v[4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) v[k] = t + k < np ? vb[(t + k) * HEAD_DIM + dd] : 0.0f;
+        for (int k = 0; k < 4; ++k) v[k] = t + k < np ? E::get(vb[(t + k) * HEAD_DIM + dd]) : 0.0f;
         const float a0[4] = {s0.x, s0.y, s0.z, s0.w}, a1[4] = {s1.x, s1.y, s1.z, s1.w};
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -750,26 +761,29 @@ static_assert((8 * HEAD_DIM + ATT_BIG_ROWS * HEAD_DIM + 8 * ATT_SC_STRIDE + 16 +
 // combine_pair: chunk o vectors of two heads, maxima, sums, weights, 1/L, output
 static_assert((2 * ATT_MAX_CHUNKS * HEAD_DIM + 6 * ATT_MAX_CHUNKS + 4 + 256) * sizeof(float) <= WBUF_BYTES,
               "combine scratch exceeds weight buffer 0");
+template <typename KT>
 __device__ void attention_unit_big(const DecodeParams& p, float* scratch, int l, int g, int c, int t0, int np,
                                    unsigned seq, bool flagged) {
+    using E = KvElt<KT>;
+    constexpr int CPR = HEAD_DIM / E::PER16;   // 16-byte copies per cache row
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, j = lane & 7, G = lane >> 3;
     float* qh = scratch;                                // [8][128]
-    float* kv = qh + 8 * HEAD_DIM;                      // [ATT_BIG_ROWS][128] K, then V rows
-    float* sc = kv + ATT_BIG_ROWS * HEAD_DIM;           // [8][ATT_SC_STRIDE] scores -> probabilities
+    KT* kv = reinterpret_cast<KT*>(qh + 8 * HEAD_DIM);  // [ATT_BIG_ROWS][128] K, then V rows (float-sized slot)
+    float* sc = qh + 8 * HEAD_DIM + ATT_BIG_ROWS * HEAD_DIM;   // [8][ATT_SC_STRIDE] scores -> probabilities
     float* stat = sc + 8 * ATT_SC_STRIDE;               // m[8], l[8]
     float* krow = stat + 16;                            // [128] K row at pos (epoch path)
     float* vrow = krow + HEAD_DIM;                      // [128] V row at pos (epoch path)
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(HEAD_DIM)));
-    const float* kl = p.kc + static_cast<size_t>(l) * p.max_seq * KV_DIM + g * HEAD_DIM;
-    const float* vl = p.vc + static_cast<size_t>(l) * p.max_seq * KV_DIM + g * HEAD_DIM;
+    const KT* kl = reinterpret_cast<const KT*>(p.kc) + static_cast<size_t>(l) * p.max_seq * KV_DIM + g * HEAD_DIM;
+    const KT* vl = reinterpret_cast<const KT*>(p.vc) + static_cast<size_t>(l) * p.max_seq * KV_DIM + g * HEAD_DIM;
     const bool epoch_in = p.qll != nullptr;
     const int cur = epoch_in && t0 + np - 1 == p.pos ? np - 1 : -1;   // chunk row published this launch
     // Stages the cache rows of [s0, s0+ns) into kv and returns their count; the row
     // published this launch (the chunk's last) is copied in from krow / vrow instead.
-    auto stage = [&](const float* src, int s0, int ns) {
+    auto stage = [&](const KT* src, int s0, int ns) {
         const int nc = cur >= s0 && cur < s0 + ns ? ns - 1 : ns;   // cur is the chunk's last row
-        for (int i = tid; i < nc * 32; i += blockDim.x)
-            cp_async16(kv + 4 * i, src + static_cast<size_t>(t0 + s0 + (i >> 5)) * KV_DIM + 4 * (i & 31));
+        for (int i = tid; i < nc * CPR; i += blockDim.x)
+            cp_async16(kv + E::PER16 * i, src + static_cast<size_t>(t0 + s0 + i / CPR) * KV_DIM + E::PER16 * (i % CPR));
         cp_async_commit();
         return nc;
     };
@@ -801,7 +815,7 @@ __device__ void attention_unit_big(const DecodeParams& p, float* scratch, int l,
             }
             trace_mark(p, 3 + 2 * (5 * l));   // inputs of this unit published
         }
-        if (nc < ns && tid < 32) reinterpret_cast<float4*>(kv + nc * HEAD_DIM)[tid] = reinterpret_cast<float4*>(krow)[tid];
+        if (nc < ns && tid < 32) E::st4(kv + nc * HEAD_DIM + 4 * tid, reinterpret_cast<float4*>(krow)[tid]);
         cp_async_wait_all();
         __syncthreads();
         if (s0 == 0) trace_step(p, l, 1, 4);
@@ -817,13 +831,13 @@ __device__ void attention_unit_big(const DecodeParams& p, float* scratch, int l,
         // partner keeps), the same additions as v += shfl_xor(v, 4 / 2 / 1) on each dot.
         for (int base = ps * 4; base < ns; base += 32) {   // warp-uniform trip count
             const int ta = base + G, tb = ta + 16;
-            const float* ka = kv + min(ta, ns - 1) * HEAD_DIM + 4 * j;
-            const float* kb = kv + min(tb, ns - 1) * HEAD_DIM + 4 * j;
+            const KT* ka = kv + min(ta, ns - 1) * HEAD_DIM + 4 * j;
+            const KT* kb = kv + min(tb, ns - 1) * HEAD_DIM + 4 * j;
             float aa = 0.0f, ba = 0.0f, ab = 0.0f, bb = 0.0f;   // (head a|b, position ta|tb)
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const float4 x = *reinterpret_cast<const float4*>(ka + 32 * i);
-                const float4 y = *reinterpret_cast<const float4*>(kb + 32 * i);
+                const float4 x = E::sm4(ka + 32 * i);
+                const float4 y = E::sm4(kb + 32 * i);
                 aa = __fmaf_rn(qa[i].x, x.x, aa);
                 aa = __fmaf_rn(qa[i].y, x.y, aa);
                 aa = __fmaf_rn(qa[i].z, x.z, aa);
@@ -887,13 +901,13 @@ __device__ void attention_unit_big(const DecodeParams& p, float* scratch, int l,
     for (int s0 = 0; s0 < np; s0 += ATT_BIG_ROWS) {
         const int ns = min(ATT_BIG_ROWS, np - s0);
         const int nc = stage(vl, s0, ns);
-        if (nc < ns && tid < 32) reinterpret_cast<float4*>(kv + nc * HEAD_DIM)[tid] = reinterpret_cast<float4*>(vrow)[tid];
+        if (nc < ns && tid < 32) E::st4(kv + nc * HEAD_DIM + 4 * tid, reinterpret_cast<float4*>(vrow)[tid]);
         cp_async_wait_all();
         __syncthreads();   // V rows, and (first round) the probabilities
         if (s0 == 0) trace_step(p, l, 1, 9);
         if (tid < 128) {
             const float* pr = sc + 4 * hq * ATT_SC_STRIDE + s0;
-            const float* vr = kv + 2 * dp;
+            const KT* vr = kv + 2 * dp;
             int tt = 0;
 #pragma unroll 2
             for (; tt + 4 <= ns; tt += 4) {
@@ -902,7 +916,7 @@ __device__ void attention_unit_big(const DecodeParams& p, float* scratch, int l,
 #pragma unroll
                 for (int h = 0; h < 4; ++h) pw[h] = *reinterpret_cast<const float4*>(pr + h * ATT_SC_STRIDE + tt);
 #pragma unroll
-                for (int k = 0; k < 4; ++k) v[k] = *reinterpret_cast<const float2*>(vr + (tt + k) * HEAD_DIM);
+                for (int k = 0; k < 4; ++k) v[k] = E::sm2(vr + (tt + k) * HEAD_DIM);
 #pragma unroll
                 for (int h = 0; h < 4; ++h) {
                     const float w[4] = {pw[h].x, pw[h].y, pw[h].z, pw[h].w};
@@ -914,7 +928,7 @@ __device__ void attention_unit_big(const DecodeParams& p, float* scratch, int l,
                 }
             }
             for (; tt < ns; ++tt) {
-                const float2 v = *reinterpret_cast<const float2*>(vr + tt * HEAD_DIM);
+                const float2 v = E::sm2(vr + tt * HEAD_DIM);
 #pragma unroll
                 for (int h = 0; h < 4; ++h) {
                     const float w = pr[h * ATT_SC_STRIDE + tt];
@@ -1043,20 +1057,21 @@ __device__ bool combine_pair(const DecodeParams& p, float* scratch, int l, int b
 // DIST_COMBINE_MAX chunks in the decode kernel, the head-pair combiners on the last CTAs
 // (usually CTAs without a unit).  Shorter contexts are combined in the o_proj prologue;
 // the standalone op combines in k_att_combine.
+template <typename KT>
 __device__ bool phase_attention(const DecodeParams& p, const Smem& s, float* scratch, int l, int cta, int ncta,
                                 unsigned seq) {
     const int n = p.pos + 1;
     const int P = 32 * ((n + 2047) / 2048);
     const int C = (n + P - 1) / P;
-    const bool flagged = C > DIST_COMBINE_MAX && p.attw != nullptr;   // att_flagged(p)
+    const bool flagged = att_flagged(p);
     for (int item = cta; item < 2 * C; item += ncta) {
         const int g = item / C, c = item % C;
         const int t0 = c * P, t1 = min(t0 + P, n), np = t1 - t0;
         __syncthreads();
         if (P == 32)
-            attention_unit32(p, scratch, l, g, c, t0, np, seq, flagged);
+            attention_unit32<KT>(p, scratch, l, g, c, t0, np, seq, flagged);
         else
-            attention_unit_big(p, scratch, l, g, c, t0, np, seq, flagged);
+            attention_unit_big<KT>(p, scratch, l, g, c, t0, np, seq, flagged);
     }
     if (flagged) {
         for (int b = ncta - 1 - cta; b < N_EMBD / 256; b += ncta) {
@@ -1137,7 +1152,7 @@ __device__ bool phase_o(const DecodeParams& p, const Smem& s, int l, int cta, in
     const PhaseLayout pl = phase_layout(L, *s.rows(), 1);
     const int r0 = pl.row0[0], n = pl.nrows[0];
     const float xr = threadIdx.x < n ? __ldcg(p.x + r0 + threadIdx.x) : 0.0f;   // residual rows, early
-    if (attn_chunks(p.pos + 1) <= DIST_COMBINE_MAX) {
+    if (!att_flagged(p)) {
         combine_attention(p, s, l, cta);
     } else if (trace_step(p, l, 2, 5), !load_att_epoch(p, s, att_epoch(seq, l))) {
         return false;
@@ -1188,6 +1203,7 @@ __device__ bool phase_gu(const DecodeParams& p, const Smem& s, int l, int cta, i
 
 // down + residual; the new residual rows are published as epoch-tagged words (k = 2l+2);
 // then the next layer's K/V and norm prefetches (or the LM head's second stage).
+template <typename KT>
 __device__ bool phase_down(const DecodeParams& p, const Smem& s, int l, int cta, int ncta, unsigned seq,
                            const LmPlan& lmq) {
     const LayerMeta& L = s.meta()[l];
@@ -1231,7 +1247,7 @@ __device__ bool phase_down(const DecodeParams& p, const Smem& s, int l, int cta,
         if (l + 1 == p.n_layer) {
             issue_lm_stage(p, s, lmq, 1);
         } else {
-            prefetch_attention(p, l + 1, cta);
+            prefetch_attention<KT>(p, l + 1, cta);
             prefetch_norms(p, s, l + 1, cta);
         }
     }
@@ -1310,6 +1326,7 @@ __device__ void phase_lm(const DecodeParams& p, const Smem& s, int cta, int ncta
     }
 }
 
+template <typename KT>
 __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p) {
     const Smem s;
     if (threadIdx.x == 0) {
@@ -1352,7 +1369,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
         fence_mbar_init();
         issue_weight_phase(p, s, 0, cta, ncta);
         prefetch_layer_l2(p, s, 0, 1);
-        prefetch_attention(p, 0, cta);
+        prefetch_attention<KT>(p, 0, cta);
         prefetch_norms(p, s, 0, cta);
     }
     __syncthreads();
@@ -1368,11 +1385,11 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
     }
     __syncthreads();
     for (int l = 0; l < p.n_layer; ++l) {
-        if (!phase_qkv(p, s, l, token, cta, ncta, seq)) return;
+        if (!phase_qkv<KT>(p, s, l, token, cta, ncta, seq)) return;
         // attention units wait on the q/K/V epochs themselves: no grid barrier
         trace_mark(p, 2 + 2 * (5 * l));
-        if (!phase_attention(p, s, reinterpret_cast<float*>(s.flags()[0] ? s.wbuf(1) + ATT_B1_OFF : s.wbuf(0)), l, cta,
-                             ncta, seq))
+        if (!phase_attention<KT>(p, s, reinterpret_cast<float*>(s.flags()[0] ? s.wbuf(1) + ATT_B1_OFF : s.wbuf(0)), l,
+                                 cta, ncta, seq))
             return;
         if (flagged) {   // no grid barrier: o_proj waits for the combiners' epoch-tagged values
             __syncthreads();   // the attention scratch is free once this CTA's units are done
@@ -1393,7 +1410,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
                 if (l + 1 == p.n_layer && cta == 0) bulk_prefetch_l2(p.out_norm, N_EMBD * 4);
             }))
             return;
-        if (!phase_down(p, s, l, cta, ncta, seq, lmq)) return;
+        if (!phase_down<KT>(p, s, l, cta, ncta, seq, lmq)) return;
         trace_mark(p, 2 + 2 * (5 * l + 4));
     }
     if (cta == 0 && threadIdx.x == 0) {
@@ -1417,7 +1434,7 @@ __global__ void k_kv_append(const float* __restrict__ k, const float* __restrict
 
 __global__ void __launch_bounds__(DEC_THREADS, 1) k_attention(const DecodeParams p) {
     const Smem s;
-    phase_attention(p, s, reinterpret_cast<float*>(s.wbuf(0)), 0, blockIdx.x, gridDim.x, 1u);
+    phase_attention<float>(p, s, reinterpret_cast<float*>(s.wbuf(0)), 0, blockIdx.x, gridDim.x, 1u);
 }
 
 // Standalone op: head pair blockIdx.x of the chunks written by k_attention (stream order).
@@ -1441,9 +1458,9 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_tp_att_units(DecodeParams p,
     const Smem sm;
     const int t0 = c * P, np = min(t0 + P, n) - t0;
     if (P == 32)
-        attention_unit32(p, reinterpret_cast<float*>(sm.wbuf(0)), 0, g, c, t0, np, 1u, false);
+        attention_unit32<float>(p, reinterpret_cast<float*>(sm.wbuf(0)), 0, g, c, t0, np, 1u, false);
     else
-        attention_unit_big(p, reinterpret_cast<float*>(sm.wbuf(0)), 0, g, c, t0, np, 1u, false);
+        attention_unit_big<float>(p, reinterpret_cast<float*>(sm.wbuf(0)), 0, g, c, t0, np, 1u, false);
 }
 
 __global__ void __launch_bounds__(DEC_THREADS, 1) k_tp_att_combine(DecodeParams p, const int* pos, int b0) {
@@ -1488,13 +1505,17 @@ cudaError_t launch_tp_attention(const DecodeParams& p, const int* pos_dev, int g
 size_t decode_smem_bytes() { return SM_BYTES; }
 
 cudaError_t decode_prepare() {
-    return cudaFuncSetAttribute(k_decode, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(k_decode<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(decode_smem_bytes()));
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(k_decode<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(decode_smem_bytes()));
 }
 
 int decode_max_ctas_per_sm() {
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_decode, DEC_THREADS, decode_smem_bytes()) != cudaSuccess)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_decode<float>, DEC_THREADS, decode_smem_bytes()) !=
+        cudaSuccess)
         return 0;
     return n;
 }
@@ -1509,7 +1530,9 @@ cudaError_t launch_batch_step(const BatchLaunch& b, cudaStream_t stream) {
     cudaGetDevice(&dev);
     constexpr int UNIT_SMEM_BIG = 98304, COMBINE_SMEM = 68608;
     if (prepared_dev != dev) {
-        cudaError_t e = cudaFuncSetAttribute(k_b_att_units, cudaFuncAttributeMaxDynamicSharedMemorySize, UNIT_SMEM_BIG);
+        cudaError_t e = cudaFuncSetAttribute(k_b_att_units<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, UNIT_SMEM_BIG);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k_b_att_units<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, UNIT_SMEM_BIG);
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(k_b_att_combine, cudaFuncAttributeMaxDynamicSharedMemorySize, COMBINE_SMEM);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(k_b_gemm8, cudaFuncAttributeMaxDynamicSharedMemorySize, GA_BYTES);
@@ -1523,6 +1546,7 @@ cudaError_t launch_batch_step(const BatchLaunch& b, cudaStream_t stream) {
                   "unit smem");
     BStepArgs a{};
     a.n_seq = b.n_seq, a.max_seq = b.max_seq, a.n_layer = b.n_layer, a.n_vocab = b.n_vocab;
+    a.kv_seq_stride = b.shared_kv ? 0 : static_cast<size_t>(b.n_layer) * b.max_seq * KV_DIM;
     a.kc = b.kc, a.vc = b.vc, a.x = b.x, a.y = b.y, a.q = b.q, a.att_part = b.att_part, a.att = b.att;
     a.logits = b.logits, a.aqs = b.aqs, a.ad = b.ad, a.abs = b.abs;
     a.tokens = b.tokens, a.pos = b.pos, a.argmax = b.argmax, a.embd = b.embd, a.rope = b.rope, a.err = b.err;
@@ -1557,8 +1581,13 @@ cudaError_t launch_batch_step(const BatchLaunch& b, cudaStream_t stream) {
         const LayerDev& L = b.layers[l];
         gemm({{L.wq, L.tq, N_EMBD, 0, 0}, {L.wk, L.tk, KV_DIM, N_EMBD, 0}, {L.wv, L.tv, KV_DIM, N_EMBD + KV_DIM, 0}},
              N_EMBD / 256, b.y, 2 * N_FF);
-        k_b_rope_kv<<<n, 256, 0, stream>>>(a, l);
-        k_b_att_units<<<dim3(n, 2 * Cmax), DEC_THREADS, unit_smem, stream>>>(a, l);
+        if (b.kv_f16) {
+            k_b_rope_kv<__half><<<n, 256, 0, stream>>>(a, l);
+            k_b_att_units<__half><<<dim3(n, 2 * Cmax), DEC_THREADS, unit_smem, stream>>>(a, l);
+        } else {
+            k_b_rope_kv<float><<<n, 256, 0, stream>>>(a, l);
+            k_b_att_units<float><<<dim3(n, 2 * Cmax), DEC_THREADS, unit_smem, stream>>>(a, l);
+        }
         k_b_att_combine<<<dim3(n, N_EMBD / 256), DEC_THREADS, COMBINE_SMEM, stream>>>(a, l);
         gemm({{L.wo, L.to, N_EMBD, 0, 0}}, N_EMBD / 256, b.y, 2 * N_FF);
         a.norm = L.ffn_norm;
@@ -1574,14 +1603,17 @@ cudaError_t launch_batch_step(const BatchLaunch& b, cudaStream_t stream) {
             k_b_res_norm<false><<<n, 256, 0, stream>>>(a);
         }
     }
-    gemm({{b.lm, b.lm_type, b.n_vocab, 0, 0}}, N_EMBD / 256, b.logits, b.n_vocab);
-    k_b_argmax<<<n, 1024, 0, stream>>>(a, b.chain);
+    if (!b.skip_lm) {
+        gemm({{b.lm, b.lm_type, b.n_vocab, 0, 0}}, N_EMBD / 256, b.logits, b.n_vocab);
+        k_b_argmax<<<n, 1024, 0, stream>>>(a, b.chain);
+    }
     return cudaGetLastError();
 }
 
 cudaError_t launch_decode(const DecodeParams& p, int n_ctas, cudaStream_t stream) {
     void* args[] = {const_cast<DecodeParams*>(&p)};
-    return cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(&k_decode), dim3(n_ctas), dim3(DEC_THREADS), args,
+    const void* fn = p.kv_f16 ? reinterpret_cast<const void*>(&k_decode<__half>) : reinterpret_cast<const void*>(&k_decode<float>);
+    return cudaLaunchCooperativeKernel(fn, dim3(n_ctas), dim3(DEC_THREADS), args,
                                        decode_smem_bytes(), stream);
 }
 

@@ -254,6 +254,53 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
     return true;
 }
 
+// ---------------------------------------------------------------- K/V cache elements
+// The cache holds fp32 rows (the reference's KVCacheLayer) or, as an option, fp16 rows: a
+// value enters the cache rounded to nearest-even half precision and is read back exactly, so
+// every later operation sees the same float as the C restatement's fp16 option.
+__device__ __forceinline__ float4 half4_to_float4(uint2 u) {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+}
+template <typename KT>
+struct KvElt;
+template <>
+struct KvElt<float> {
+    static constexpr int PER16 = 4;   // elements per 16-byte copy
+    __device__ static float4 ld4(const float* p) { return ld_cg_f4(p); }   // global, through L2
+    __device__ static float4 sm4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+    __device__ static float2 sm2(const float* p) { return *reinterpret_cast<const float2*>(p); }
+    __device__ static float get(float v) { return v; }
+    __device__ static float put(float v) { return v; }
+    __device__ static void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+};
+template <>
+struct KvElt<__half> {
+    static constexpr int PER16 = 8;
+    __device__ static float4 ld4(const __half* p) {
+        uint2 u;
+        asm volatile("ld.global.cg.v2.u32 {%0, %1}, [%2];" : "=r"(u.x), "=r"(u.y) : "l"(p));
+        return half4_to_float4(u);
+    }
+    __device__ static float4 sm4(const __half* p) { return half4_to_float4(*reinterpret_cast<const uint2*>(p)); }
+    __device__ static float2 sm2(const __half* p) { return __half22float2(*reinterpret_cast<const __half2*>(p)); }
+    __device__ static float get(__half v) { return __half2float(v); }
+    __device__ static __half put(float v) { return __float2half_rn(v); }
+    __device__ static void st4(__half* p, float4 v) {   // values already half-representable
+        const __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
+        uint2 u;
+        u.x = *reinterpret_cast<const uint32_t*>(&a);
+        u.y = *reinterpret_cast<const uint32_t*>(&b);
+        *reinterpret_cast<uint2*>(p) = u;
+    }
+};
+// The float a value becomes once stored in a cache of element type KT.
+template <typename KT>
+__device__ __forceinline__ float kv_round(float v) {
+    return KvElt<KT>::get(KvElt<KT>::put(v));
+}
+
 // ---------------------------------------------------------------- canonical scalar math
 // exp(x): k = rint(x*log2e), two-constant Cody-Waite reduction, degree-7 Taylor
 // polynomial in Horner form, 2^k applied as two exact power-of-two factors.

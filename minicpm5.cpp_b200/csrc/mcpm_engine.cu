@@ -15,6 +15,8 @@
 #include <utility>
 #include <initializer_list>
 
+#include <cuda_fp16.h>
+
 #include "../../include/mcpm.h"
 #include "gguf.h"
 #include "mcpm_device.cuh"
@@ -38,6 +40,10 @@ struct mcpm_engine {
     int req_ctas = 0;
     int batch_gemm = 0;   // MCPM_GEMM_MMA / MCPM_GEMM_TCGEN05
     int sched = 0;        // decode schedule option bits (mcpm_config::sched)
+    int kv_f16 = 0;       // mcpm_config::kv_type == MCPM_KV_F16: kc / vc / b_kc / b_vc hold fp16 rows
+    size_t kv_elt() const { return kv_f16 ? sizeof(__half) : sizeof(float); }
+    // address of cache element `idx` (in elements) of a K or V array of this engine's element type
+    uint8_t* kv_at(float* base, size_t idx) const { return reinterpret_cast<uint8_t*>(base) + idx * kv_elt(); }
     bool loaded = false;
     GGUFFile gguf;
     uint8_t* arena = nullptr;
@@ -74,6 +80,12 @@ struct mcpm_engine {
     int16_t* b_abs = nullptr;
     int *b_tokens = nullptr, *b_pos = nullptr, *b_argmax = nullptr;
     std::vector<int> b_pos_host;   // positions of the next step
+    // batched prefill: row buffers for BATCH_MAX prompt positions of the engine's own sequence
+    float *p_x = nullptr, *p_y = nullptr, *p_q = nullptr, *p_part = nullptr, *p_att = nullptr, *p_logits = nullptr;
+    int8_t* p_aqs = nullptr;
+    float* p_ad = nullptr;
+    int16_t* p_abs = nullptr;
+    int *p_tokens = nullptr, *p_pos = nullptr, *p_argmax = nullptr;
 };
 
 namespace {
@@ -117,7 +129,18 @@ void free_batch(mcpm_engine* e) {
     e->b_pos_host.clear();
 }
 
+void free_prefill(mcpm_engine* e) {
+    for (float** b : {&e->p_x, &e->p_y, &e->p_q, &e->p_part, &e->p_att, &e->p_logits}) free_dev(*b);
+    free_dev(e->p_aqs);
+    free_dev(e->p_ad);
+    free_dev(e->p_abs);
+    free_dev(e->p_tokens);
+    free_dev(e->p_pos);
+    free_dev(e->p_argmax);
+}
+
 void free_model(mcpm_engine* e) {
+    free_prefill(e);
     free_dev(e->arena);
     free_dev(e->d_layers);
     free_dev(e->x);
@@ -255,6 +278,7 @@ DecodeParams make_params(const mcpm_engine* e, int token, int pos, int write_log
     p.cnt = reinterpret_cast<unsigned*>(e->ctl + CTL_CNT);
     p.trace = e->trace;
     p.sched = e->sched;
+    p.kv_f16 = e->kv_f16;
     p.token = token;
     p.pos = pos;
     p.write_logits = write_logits;
@@ -297,6 +321,7 @@ mcpm_status mcpm_engine_create(const mcpm_config* cfg, mcpm_engine** out) {
     *out = nullptr;
     if (cfg->max_seq < 0 || cfg->max_seq > MAX_SEQ || cfg->n_ctas < 0) return MCPM_BAD_ARG;
     if (cfg->batch_gemm != MCPM_GEMM_MMA && cfg->batch_gemm != MCPM_GEMM_TCGEN05) return MCPM_BAD_ARG;
+    if (cfg->kv_type != MCPM_KV_F32 && cfg->kv_type != MCPM_KV_F16) return MCPM_BAD_ARG;
     int ndev = 0;
     MCPM_CUDA(cudaGetDeviceCount(&ndev));
     if (cfg->device < 0 || cfg->device >= ndev) return MCPM_BAD_ARG;
@@ -305,6 +330,7 @@ mcpm_status mcpm_engine_create(const mcpm_config* cfg, mcpm_engine** out) {
     e->req_ctas = cfg->n_ctas;
     e->batch_gemm = cfg->batch_gemm;
     e->sched = cfg->sched;
+    e->kv_f16 = cfg->kv_type == MCPM_KV_F16;
     e->max_seq = 0;
     MCPM_CUDA(cudaSetDevice(e->device));
     MCPM_CUDA(cudaDeviceGetAttribute(&e->n_sm, cudaDevAttrMultiProcessorCount, e->device));
@@ -497,10 +523,10 @@ mcpm_status mcpm_init_kv(mcpm_engine* e, int max_seq) {
     MCPM_CUDA(cudaSetDevice(e->device));
     free_kv(e);
     const size_t n = static_cast<size_t>(e->n_layer) * max_seq * KV_DIM;
-    MCPM_CUDA(cudaMalloc(&e->kc, n * sizeof(float)));
-    MCPM_CUDA(cudaMalloc(&e->vc, n * sizeof(float)));
-    MCPM_CUDA(cudaMemset(e->kc, 0, n * sizeof(float)));
-    MCPM_CUDA(cudaMemset(e->vc, 0, n * sizeof(float)));
+    MCPM_CUDA(cudaMalloc(&e->kc, n * e->kv_elt()));
+    MCPM_CUDA(cudaMalloc(&e->vc, n * e->kv_elt()));
+    MCPM_CUDA(cudaMemset(e->kc, 0, n * e->kv_elt()));
+    MCPM_CUDA(cudaMemset(e->vc, 0, n * e->kv_elt()));
     std::vector<float2> table(static_cast<size_t>(max_seq) * (HEAD_DIM / 2));
     for (int p = 0; p < max_seq; ++p) rope_row(p, e->rope_base, table.data() + static_cast<size_t>(p) * (HEAD_DIM / 2));
     MCPM_CUDA(cudaMalloc(&e->rope, table.size() * sizeof(float2)));
@@ -549,9 +575,17 @@ mcpm_status mcpm_read_kv(mcpm_engine* e, int layer, int pos, float* k_host, floa
     if (layer < 0 || layer >= e->n_layer || pos < 0 || pos >= e->max_seq) return MCPM_BAD_ARG;
     MCPM_CUDA(cudaSetDevice(e->device));
     const size_t off = (static_cast<size_t>(layer) * e->max_seq + pos) * KV_DIM;
-    MCPM_CUDA(cudaMemcpyAsync(k_host, e->kc + off, KV_DIM * 4, cudaMemcpyDeviceToHost, e->stream));
-    MCPM_CUDA(cudaMemcpyAsync(v_host, e->vc + off, KV_DIM * 4, cudaMemcpyDeviceToHost, e->stream));
+    if (!e->kv_f16) {
+        MCPM_CUDA(cudaMemcpyAsync(k_host, e->kc + off, KV_DIM * 4, cudaMemcpyDeviceToHost, e->stream));
+        MCPM_CUDA(cudaMemcpyAsync(v_host, e->vc + off, KV_DIM * 4, cudaMemcpyDeviceToHost, e->stream));
+        MCPM_CUDA(cudaStreamSynchronize(e->stream));
+        return MCPM_OK;
+    }
+    std::vector<__half> h(2 * KV_DIM);   // fp16 rows widen exactly to fp32
+    MCPM_CUDA(cudaMemcpyAsync(h.data(), e->kv_at(e->kc, off), KV_DIM * 2, cudaMemcpyDeviceToHost, e->stream));
+    MCPM_CUDA(cudaMemcpyAsync(h.data() + KV_DIM, e->kv_at(e->vc, off), KV_DIM * 2, cudaMemcpyDeviceToHost, e->stream));
     MCPM_CUDA(cudaStreamSynchronize(e->stream));
+    for (int i = 0; i < KV_DIM; ++i) k_host[i] = __half2float(h[i]), v_host[i] = __half2float(h[KV_DIM + i]);
     return MCPM_OK;
 }
 
@@ -561,11 +595,58 @@ mcpm_status mcpm_write_kv(mcpm_engine* e, int layer, int pos0, int n_pos, const 
     if (layer < 0 || layer >= e->n_layer || pos0 < 0 || n_pos < 0 || pos0 > e->max_seq - n_pos) return MCPM_BAD_ARG;
     MCPM_CUDA(cudaSetDevice(e->device));
     const size_t off = (static_cast<size_t>(layer) * e->max_seq + pos0) * KV_DIM;
-    const size_t bytes = static_cast<size_t>(n_pos) * KV_DIM * 4;
-    MCPM_CUDA(cudaMemcpyAsync(e->kc + off, k_host, bytes, cudaMemcpyHostToDevice, e->stream));
-    MCPM_CUDA(cudaMemcpyAsync(e->vc + off, v_host, bytes, cudaMemcpyHostToDevice, e->stream));
+    const size_t n = static_cast<size_t>(n_pos) * KV_DIM;
+    if (!e->kv_f16) {
+        MCPM_CUDA(cudaMemcpyAsync(e->kc + off, k_host, n * 4, cudaMemcpyHostToDevice, e->stream));
+        MCPM_CUDA(cudaMemcpyAsync(e->vc + off, v_host, n * 4, cudaMemcpyHostToDevice, e->stream));
+        MCPM_CUDA(cudaStreamSynchronize(e->stream));
+        return MCPM_OK;
+    }
+    std::vector<__half> h(2 * n);   // rounded to nearest-even, as the decode step rounds the rows it writes
+    for (size_t i = 0; i < n; ++i) h[i] = __float2half_rn(k_host[i]), h[n + i] = __float2half_rn(v_host[i]);
+    MCPM_CUDA(cudaMemcpyAsync(e->kv_at(e->kc, off), h.data(), n * 2, cudaMemcpyHostToDevice, e->stream));
+    MCPM_CUDA(cudaMemcpyAsync(e->kv_at(e->vc, off), h.data() + n, n * 2, cudaMemcpyHostToDevice, e->stream));
     MCPM_CUDA(cudaStreamSynchronize(e->stream));
     return MCPM_OK;
+}
+
+// Session snapshot: positions [0, n_pos) of every layer, [layer][K then V][pos][KV_DIM] fp32.
+size_t mcpm_kv_snapshot_bytes(mcpm_engine* e, int n_pos) {
+    if (!e || !e->loaded || n_pos < 0) return 0;
+    return static_cast<size_t>(e->n_layer) * 2 * n_pos * KV_DIM * e->kv_elt();
+}
+
+namespace {
+mcpm_status kv_copy(mcpm_engine* e, int n_pos, void* host, size_t bytes, bool to_host) {
+    if (!e || !host || n_pos < 0) return MCPM_BAD_ARG;
+    if (!e->loaded || !e->kc) return MCPM_NOT_LOADED;
+    if (n_pos > e->max_seq) return MCPM_CTX_OVERFLOW;
+    const size_t per = static_cast<size_t>(n_pos) * KV_DIM * e->kv_elt();
+    if (bytes < static_cast<size_t>(e->n_layer) * 2 * per) return MCPM_BAD_ARG;
+    MCPM_CUDA(cudaSetDevice(e->device));
+    uint8_t* h = static_cast<uint8_t*>(host);
+    for (int l = 0; l < e->n_layer; ++l) {   // one copy per layer and per K / V
+        const size_t lo = static_cast<size_t>(l) * e->max_seq * KV_DIM;
+        uint8_t* dev[2] = {e->kv_at(e->kc, lo), e->kv_at(e->vc, lo)};
+        for (int kv = 0; kv < 2; ++kv) {
+            uint8_t* hp = h + (2 * static_cast<size_t>(l) + kv) * per;
+            if (to_host)
+                MCPM_CUDA(cudaMemcpyAsync(hp, dev[kv], per, cudaMemcpyDeviceToHost, e->stream));
+            else
+                MCPM_CUDA(cudaMemcpyAsync(dev[kv], hp, per, cudaMemcpyHostToDevice, e->stream));
+        }
+    }
+    MCPM_CUDA(cudaStreamSynchronize(e->stream));
+    return MCPM_OK;
+}
+}  // namespace
+
+mcpm_status mcpm_kv_snapshot(mcpm_engine* e, int n_pos, void* host, size_t bytes) {
+    return kv_copy(e, n_pos, host, bytes, true);
+}
+
+mcpm_status mcpm_kv_restore(mcpm_engine* e, int n_pos, const void* host, size_t bytes) {
+    return kv_copy(e, n_pos, const_cast<void*>(host), bytes, false);
 }
 
 mcpm_status mcpm_model_dims(mcpm_engine* e, int dims[6]) {
@@ -713,7 +794,7 @@ mcpm_status mcpm_batch_init(mcpm_engine* e, int n_seq, int max_seq) {
     const size_t ns = n_seq;
     cudaError_t err = cudaSuccess;
     for (auto& [ptr, bytes] : std::initializer_list<std::pair<float**, size_t>>{
-             {&e->b_kc, kv * 4}, {&e->b_vc, kv * 4}, {&e->b_x, ns * N_EMBD * 4}, {&e->b_y, ns * 2 * N_FF * 4},
+             {&e->b_kc, kv * e->kv_elt()}, {&e->b_vc, kv * e->kv_elt()}, {&e->b_x, ns * N_EMBD * 4}, {&e->b_y, ns * 2 * N_FF * 4},
              {&e->b_q, ns * N_EMBD * 4}, {&e->b_part, ns * ATT_PART_FLOATS * 4}, {&e->b_att, ns * N_EMBD * 4},
              {&e->b_logits, ns * e->n_vocab * 4}})
         if (err == cudaSuccess) err = alloc(ptr, bytes);
@@ -759,6 +840,7 @@ mcpm_status mcpm_batch_step_async(mcpm_engine* e, const int* tokens, const int* 
     BatchLaunch b{};
     b.n_seq = n, b.max_seq = e->b_max_seq, b.n_layer = e->n_layer, b.n_vocab = e->n_vocab, b.lm_type = e->lm_type;
     b.max_pos = max_pos, b.chain = 1, b.n_sm = e->n_sm, b.tcgen05 = e->batch_gemm == MCPM_GEMM_TCGEN05;
+    b.kv_f16 = e->kv_f16;
     b.layers = e->layers.data(), b.embd = e->embd, b.out_norm = e->out_norm, b.lm = e->lm, b.rope = e->b_rope;
     b.kc = e->b_kc, b.vc = e->b_vc, b.x = e->b_x, b.y = e->b_y, b.q = e->b_q, b.att_part = e->b_part;
     b.att = e->b_att, b.logits = e->b_logits, b.aqs = e->b_aqs, b.ad = e->b_ad, b.abs = e->b_abs;
@@ -768,6 +850,71 @@ mcpm_status mcpm_batch_step_async(mcpm_engine* e, const int* tokens, const int* 
     for (int i = 0; i < n; ++i) next[i] += 1;   // the argmax kernel advances the device copy the same way
     e->b_pos_host = next;
     return MCPM_OK;
+}
+
+// ------------------------------------------------------------------ batched prefill
+mcpm_status mcpm_prefill(mcpm_engine* e, const int* tokens, int n, int pos0, float* logits_out, int* argmax_out) {
+    if (!e || !tokens || n <= 0 || pos0 < 0) return MCPM_BAD_ARG;
+    if (!e->loaded || !e->kc) return MCPM_NOT_LOADED;
+    if (pos0 + n > e->max_seq) return MCPM_CTX_OVERFLOW;
+    for (int i = 0; i < n; ++i)
+        if (tokens[i] < 0 || tokens[i] >= e->n_vocab) return MCPM_BAD_TOKEN;
+    MCPM_CUDA(cudaSetDevice(e->device));
+    if (!e->p_x) {   // row buffers of BATCH_MAX positions, kept until the model is unloaded
+        const size_t ns = BATCH_MAX;
+        auto alloc = [&](auto** ptr, size_t bytes) { return cudaMalloc(reinterpret_cast<void**>(ptr), bytes); };
+        cudaError_t err = cudaSuccess;
+        for (auto& [ptr, bytes] : std::initializer_list<std::pair<float**, size_t>>{
+                 {&e->p_x, ns * N_EMBD * 4}, {&e->p_y, ns * 2 * N_FF * 4}, {&e->p_q, ns * N_EMBD * 4},
+                 {&e->p_part, ns * ATT_PART_FLOATS * 4}, {&e->p_att, ns * N_EMBD * 4},
+                 {&e->p_logits, ns * e->n_vocab * 4}})
+            if (err == cudaSuccess) err = alloc(ptr, bytes);
+        if (err == cudaSuccess) err = alloc(&e->p_aqs, ns * (N_FF / 256) * 256);
+        if (err == cudaSuccess) err = alloc(&e->p_ad, ns * (N_FF / 256) * 4);
+        if (err == cudaSuccess) err = alloc(&e->p_abs, ns * (N_FF / 256) * 16 * 2);
+        if (err == cudaSuccess) err = alloc(&e->p_tokens, ns * 4);
+        if (err == cudaSuccess) err = alloc(&e->p_pos, ns * 4);
+        if (err == cudaSuccess) err = alloc(&e->p_argmax, ns * 4);
+        if (err != cudaSuccess) {
+            free_prefill(e);
+            return cuda_status(err);
+        }
+    }
+    std::vector<int> pos(BATCH_MAX);
+    for (int done = 0; done < n;) {
+        const int m = std::min(BATCH_MAX, n - done);
+        const bool last = done + m == n;
+        for (int i = 0; i < m; ++i) pos[i] = pos0 + done + i;
+        MCPM_CUDA(cudaMemcpyAsync(e->p_tokens, tokens + done, m * sizeof(int), cudaMemcpyHostToDevice, e->stream));
+        MCPM_CUDA(cudaMemcpyAsync(e->p_pos, pos.data(), m * sizeof(int), cudaMemcpyHostToDevice, e->stream));
+        BatchLaunch b{};
+        b.n_seq = m, b.max_seq = e->max_seq, b.n_layer = e->n_layer, b.n_vocab = e->n_vocab, b.lm_type = e->lm_type;
+        b.max_pos = pos[m - 1], b.chain = 0, b.n_sm = e->n_sm, b.tcgen05 = e->batch_gemm == MCPM_GEMM_TCGEN05;
+        b.shared_kv = 1, b.skip_lm = last ? 0 : 1, b.kv_f16 = e->kv_f16;
+        b.layers = e->layers.data(), b.embd = e->embd, b.out_norm = e->out_norm, b.lm = e->lm, b.rope = e->rope;
+        b.kc = e->kc, b.vc = e->vc, b.x = e->p_x, b.y = e->p_y, b.q = e->p_q, b.att_part = e->p_part;
+        b.att = e->p_att, b.aqs = e->p_aqs, b.ad = e->p_ad, b.abs = e->p_abs;
+        b.logits = e->p_logits;   // [m][n_vocab]: the LM head runs on the last chunk only
+        b.tokens = e->p_tokens, b.pos = e->p_pos, b.argmax = e->p_argmax;
+        b.err = reinterpret_cast<unsigned*>(e->ctl + CTL_ERR);
+        MCPM_CUDA(launch_batch_step(b, e->stream));
+        done += m;
+        if (last) {
+            // the last position's logits and greedy token, where a decode step leaves them, so
+            // mcpm_sample / mcpm_forward(token < 0) continue from the prompt
+            MCPM_CUDA(cudaMemcpyAsync(e->logits, e->p_logits + static_cast<size_t>(m - 1) * e->n_vocab,
+                                      static_cast<size_t>(e->n_vocab) * 4, cudaMemcpyDeviceToDevice, e->stream));
+            MCPM_CUDA(cudaMemcpyAsync(e->ctl + CTL_ARGMAX, e->p_argmax + (m - 1), sizeof(int), cudaMemcpyDeviceToDevice,
+                                      e->stream));
+            MCPM_CUDA(cudaMemcpyAsync(e->ctl + CTL_TOKEN, e->p_argmax + (m - 1), sizeof(int), cudaMemcpyDeviceToDevice,
+                                      e->stream));
+        }
+    }
+    if (logits_out)
+        MCPM_CUDA(cudaMemcpyAsync(logits_out, e->logits, static_cast<size_t>(e->n_vocab) * 4, cudaMemcpyDeviceToHost,
+                                  e->stream));
+    if (argmax_out) MCPM_CUDA(cudaMemcpyAsync(argmax_out, e->ctl + CTL_ARGMAX, sizeof(int), cudaMemcpyDeviceToHost, e->stream));
+    return check_ctl(e);
 }
 
 mcpm_status mcpm_batch_read(mcpm_engine* e, float* logits, int* argmax) {

@@ -51,6 +51,7 @@ __host__ __device__ inline int qkv_pair_boundary(int tq, int tk, int tv, int c, 
 
 // Decode schedule options (DecodeParams::sched, mcpm_config::sched bits).
 constexpr int SCHED_L2_PREFETCH = 1;   // L2 prefetch of the next layer's weight rows (measured slower: off)
+constexpr int SCHED_ATT_COMBINERS = 2; // head-pair combiners at every context length (default: above 16 chunks)
 
 struct LayerDev {
     const uint8_t *wq, *wk, *wv, *wo, *wg, *wu, *wd;
@@ -68,7 +69,7 @@ struct DecodeParams {
     const uint8_t* lm;
     int lm_type;
     int n_vocab;
-    float* kc;          // [n_layer][max_seq][KV_DIM]
+    float* kc;          // [n_layer][max_seq][KV_DIM] of fp32, or of fp16 when kv_f16 (cast before indexing)
     float* vc;
     int max_seq;
     const float2* rope; // [max_seq][HEAD_DIM/2] (cos, sin)
@@ -96,6 +97,7 @@ struct DecodeParams {
     unsigned* err;      // error bits
     unsigned long long* trace;   // optional: CTA 0 phase timestamps (2 per phase + 2)
     int sched;          // SCHED_* option bits
+    int kv_f16;         // kc / vc hold fp16 rows (their element offsets are the same)
     int token;          // < 0: read *token_dev
     int pos;
     int write_logits;
@@ -116,6 +118,10 @@ constexpr size_t ATT_PART_FLOATS = static_cast<size_t>(N_HEAD) * ATT_MAX_CHUNKS 
 struct BatchLaunch {
     int n_seq, max_seq, n_layer, n_vocab, lm_type, max_pos, chain, n_sm;
     int tcgen05;              // GEMMs on k_b_gemm_tc instead of the mma.sync kernels
+    int shared_kv;            // every row is a position of ONE sequence: one cache [n_layer][max_seq][KV_DIM]
+                              // (batched prefill: row i attends to positions 0 .. pos[i], causal)
+    int skip_lm;              // no LM head / argmax (prefill chunks before the last)
+    int kv_f16;               // the cache holds fp16 rows (mcpm_config::kv_type MCPM_KV_F16)
     const LayerDev* layers;   // host array; weight pointers are device pointers
     const uint8_t* embd;
     const float* out_norm;

@@ -34,7 +34,10 @@ class MCPMError(RuntimeError):
 
 class mcpm_config(C.Structure):
     _fields_ = [("device", C.c_int), ("max_seq", C.c_int), ("n_ctas", C.c_int), ("batch_gemm", C.c_int),
-                ("sched", C.c_int), ("reserved", C.c_int * 3)]
+                ("sched", C.c_int), ("kv_type", C.c_int), ("reserved", C.c_int * 2)]
+
+
+KV_F32, KV_F16 = 0, 1
 
 
 P, I, F = C.c_void_p, C.c_int, C.c_float
@@ -54,6 +57,10 @@ SIGNATURES = {
     "mcpm_read_kv": (I, [P, I, I, C.POINTER(F), C.POINTER(F)]),
     "mcpm_write_kv": (I, [P, I, I, I, C.POINTER(F), C.POINTER(F)]),
     "mcpm_batch_init": (I, [P, I, I]),
+    "mcpm_prefill": (I, [P, C.POINTER(I), I, I, C.POINTER(F), C.POINTER(I)]),
+    "mcpm_kv_snapshot_bytes": (C.c_size_t, [P, I]),
+    "mcpm_kv_snapshot": (I, [P, I, P, C.c_size_t]),
+    "mcpm_kv_restore": (I, [P, I, P, C.c_size_t]),
     "mcpm_sample_top_p": (I, [P, I, F, F, F, P, P]),
     "mcpm_sample": (I, [P, F, F, F, C.POINTER(I)]),
     "mcpm_sample_top_p_host": (I, [C.POINTER(F), I, F, F, F, C.POINTER(I)]),
@@ -134,11 +141,14 @@ def _fptr(a: np.ndarray):
 class MiniCPM5Engine:
     """Device engine behind the reference's MiniCPM5Engine interface."""
 
-    def __init__(self, device: int = 0, max_seq: int = 0, n_ctas: int = 0, batch_gemm: int = 0, sched: int = 0):
+    def __init__(self, device: int = 0, max_seq: int = 0, n_ctas: int = 0, batch_gemm: int = 0, sched: int = 0,
+                 kv_type: int = KV_F32):
         """batch_gemm: 0 = int8 mma.sync batched GEMMs, 1 = tcgen05 (bit-identical results).
-        sched: decode schedule option bits (include/mcpm.h MCPM_SCHED_*; results are the same)."""
+        sched: decode schedule option bits (include/mcpm.h MCPM_SCHED_*; results are the same).
+        kv_type: KV_F32 (the reference's fp32 cache) or KV_F16 (rows rounded to fp16 when written)."""
         self.lib = load_library()
-        cfg = mcpm_config(device, max_seq, n_ctas, batch_gemm, sched)
+        cfg = mcpm_config(device, max_seq, n_ctas, batch_gemm, sched, kv_type)
+        self.kv_type = kv_type
         h = P()
         check(self.lib.mcpm_engine_create(C.byref(cfg), C.byref(h)), "mcpm_engine_create")
         self.h = h
@@ -175,6 +185,29 @@ class MiniCPM5Engine:
         am = C.c_int()
         check(self.lib.mcpm_forward(self.h, token_id, pos, None, C.byref(am)), "mcpm_forward")
         return am.value
+
+    def prefill(self, tokens, pos0: int = 0, logits: bool = True):
+        """Batched prefill of positions pos0 .. pos0+len(tokens)-1: (greedy token after the last
+        position, its logits or None).  Equal to len(tokens) forward() calls bit for bit."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        am = C.c_int()
+        lg = _fptr(self._logits) if (logits and self._logits is not None) else None
+        check(self.lib.mcpm_prefill(self.h, t.ctypes.data_as(C.POINTER(C.c_int)), t.size, pos0, lg, C.byref(am)),
+              "mcpm_prefill")
+        return am.value, (self._logits.copy() if lg is not None else None)
+
+    def kv_snapshot(self, n_pos: int) -> np.ndarray:
+        """KV rows of positions [0, n_pos) of every layer ([layer][K, V][pos][256], fp32 or fp16 as the
+        cache holds them)."""
+        nbytes = self.lib.mcpm_kv_snapshot_bytes(self.h, n_pos)
+        dt = np.float16 if self.kv_type == KV_F16 else np.float32
+        buf = np.zeros(nbytes // np.dtype(dt).itemsize, dt)
+        check(self.lib.mcpm_kv_snapshot(self.h, n_pos, buf.ctypes.data_as(P), buf.nbytes), "mcpm_kv_snapshot")
+        return buf
+
+    def kv_restore(self, n_pos: int, snap: np.ndarray) -> None:
+        snap = np.ascontiguousarray(snap, dtype=np.float16 if self.kv_type == KV_F16 else np.float32)
+        check(self.lib.mcpm_kv_restore(self.h, n_pos, snap.ctypes.data_as(P), snap.nbytes), "mcpm_kv_restore")
 
     def forward_async(self, token_id: int, pos: int, write_logits: bool = False) -> None:
         check(self.lib.mcpm_forward_async(self.h, token_id, pos, int(write_logits)), "mcpm_forward_async")

@@ -621,6 +621,11 @@ int orc_forward(orc_state* s, int token, int pos, float* logits) {
         project(s, t[T_V], ty[T_V], kvd, E, s->xq, s->xn, s->v);
         orc_rope(s->q, d->n_head, hd, pos, d->rope_base);
         orc_rope(s->k, d->n_head_kv, hd, pos, d->rope_base);
+        if (d->kv_f16)
+            for (int i = 0; i < kvd; ++i) {   /* the cache holds half-precision K/V rows */
+                s->k[i] = (float)(_Float16)s->k[i];
+                s->v[i] = (float)(_Float16)s->v[i];
+            }
         orc_attention(s->att, s->q, s->k, s->v, s->kc[l], s->vc[l], pos, s->max_seq, d->n_head, d->n_head_kv, hd);
         if (ty[T_O] != ORC_Q8_0) orc_quantize_q8k(s->att, E, s->xq, ORC_ROUND_EVEN, 1);
         project(s, t[T_O], ty[T_O], E, E, s->xq, s->att, s->o);

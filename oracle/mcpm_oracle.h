@@ -74,6 +74,8 @@ typedef struct {
     int layer_type[64][9];
     int n_layer, n_embd, n_ff, n_head, n_head_kv, n_vocab;
     float rope_base, eps;
+    int kv_f16;   /* 1: K and V rows are rounded to IEEE half precision (nearest even) as they
+                     enter the cache -- the engine's fp16 KV-cache option; 0: fp32 (the reference) */
 } orc_model_desc;
 
 typedef struct orc_state orc_state;

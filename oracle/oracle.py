@@ -176,7 +176,8 @@ class orc_model_desc(C.Structure):
                 ("tok_embd_type", C.c_int), ("output_type", C.c_int),
                 ("layer", (C.c_uint64 * 9) * 64), ("layer_type", (C.c_int * 9) * 64),
                 ("n_layer", C.c_int), ("n_embd", C.c_int), ("n_ff", C.c_int), ("n_head", C.c_int),
-                ("n_head_kv", C.c_int), ("n_vocab", C.c_int), ("rope_base", C.c_float), ("eps", C.c_float)]
+                ("n_head_kv", C.c_int), ("n_vocab", C.c_int), ("rope_base", C.c_float), ("eps", C.c_float),
+                ("kv_f16", C.c_int)]
 
 
 class Oracle:
@@ -290,7 +291,8 @@ _LAYER_INDEX = {n: i for i, n in enumerate(spec.LAYER_TENSORS)}
 class OracleModel:
     """Whole-model forward of the C restatement over a mapped GGUF file."""
 
-    def __init__(self, oracle: Oracle, path: str, max_seq: int):
+    def __init__(self, oracle: Oracle, path: str, max_seq: int, kv_f16: bool = False):
+        """kv_f16: the K/V cache holds half-precision rows (the engine's fp16 KV option)."""
         self.o = oracle
         self.mm = np.memmap(path, dtype=np.uint8, mode="r")
         kv, tensors, _ = gguf.read_header(path)
@@ -310,6 +312,7 @@ class OracleModel:
         d.n_layer, d.n_embd, d.n_ff = spec.N_LAYER, spec.N_EMBD, spec.N_FF
         d.n_head, d.n_head_kv, d.n_vocab = spec.N_HEAD, spec.N_HEAD_KV, spec.N_VOCAB
         d.rope_base, d.eps = spec.ROPE_BASE, spec.RMS_EPS
+        d.kv_f16 = int(kv_f16)
         self.desc = d
         self.tensors = {t.name: t for t in tensors}
         self.h = oracle.lib.orc_create(C.byref(d), max_seq)

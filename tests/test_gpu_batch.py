@@ -45,6 +45,40 @@ def test_batch_decode_bitexact(cuda, oracle, model_path, n_seq, n_prompt, n_gen,
             om.close()
 
 
+@pytest.mark.parametrize("gemm", [0, 1], ids=["mma", "tcgen05"])
+def test_batch_decode_f16_kv_bitexact(cuda, oracle, model_path, gemm):
+    """Batched decode over fp16 cache rows (kv_type MCPM_KV_F16) against the restatement with
+    the same option."""
+    import oracle as O
+    from mcpm import engine as E
+    n_seq, max_seq, n_steps = 9, 24, 6
+    e = E.MiniCPM5Engine(device=0, max_seq=max_seq, batch_gemm=gemm, kv_type=E.KV_F16)
+    assert e.load_model(model_path)
+    e.batch_init(n_seq, max_seq)
+    seqs = (0, 4, 8)
+    oms = {s: O.OracleModel(oracle, model_path, max_seq, kv_f16=True) for s in seqs}
+    prompts = np.random.default_rng(3).integers(0, e.n_vocab, (n_seq, 3)).astype(np.int32)
+    ref = np.zeros(e.n_vocab, np.float32)
+    toks = None
+    try:
+        for step in range(n_steps):
+            if step < 3:
+                tin = prompts[:, step]
+                am, lg = e.batch_step(tin, np.full(n_seq, step, np.int32), logits=True)
+            else:
+                tin = toks
+                am, lg = e.batch_step(None, None, logits=True)
+            for s in seqs:
+                want = oms[s].forward(int(tin[s]), step, ref)
+                assert np.array_equal(lg[s].view(np.uint32), ref.view(np.uint32)), f"seq {s} step {step}"
+                assert am[s] == want
+            toks = am.copy()
+    finally:
+        e.close()
+        for om in oms.values():
+            om.close()
+
+
 def test_batch_rejects_bad_arguments(cuda, model_path):
     from mcpm import engine as E
     e = E.MiniCPM5Engine(device=0, max_seq=16)

@@ -188,3 +188,223 @@ def test_cpp_sampler_loop_device_logits(cuda, oracle, model_path, tmp_path):
             assert oracle.sample_top_p(lg, temp, top_p, r)[0] == tok
             k += 1
     om.close()
+
+
+@pytest.mark.parametrize("n_prompt,pos0", [(5, 0), (64, 0), (150, 0), (70, 9)])
+def test_batched_prefill_equals_token_by_token(cuda, model_path, n_prompt, pos0):
+    """mcpm_prefill (the prompt as batched steps of up to 64 positions sharing the engine's KV
+    cache) against one mcpm_forward per position: the last position's logits, every K/V row
+    written and the greedy continuation are bit-identical."""
+    from mcpm import engine as E, synth
+    prompt = [int(t) for t in synth.prompt_ids(pos0 + n_prompt, seed=77)]
+    max_seq = pos0 + n_prompt + 8
+    a = E.MiniCPM5Engine(device=0, max_seq=max_seq)
+    b = E.MiniCPM5Engine(device=0, max_seq=max_seq)
+    try:
+        assert a.load_model(model_path) and b.load_model(model_path)
+        for pos in range(pos0):   # both engines decode the first pos0 positions one by one
+            a.forward_async(prompt[pos], pos)
+            b.forward_async(prompt[pos], pos)
+        a.sync()
+        b.sync()
+        tok_a, lg_a = a.prefill(prompt[pos0:], pos0)
+        for pos in range(pos0, pos0 + n_prompt):
+            lg_b = b.forward(prompt[pos], pos)
+        assert np.array_equal(lg_a.view(np.uint32), lg_b.view(np.uint32))
+        assert tok_a == b.last_argmax
+        for layer in (0, 17, 41):
+            for pos in (pos0, pos0 + n_prompt // 2, pos0 + n_prompt - 1):
+                ka, va = a.read_kv(layer, pos)
+                kb, vb = b.read_kv(layer, pos)
+                assert np.array_equal(ka, kb) and np.array_equal(va, vb)
+        pos = pos0 + n_prompt
+        for _ in range(3):   # greedy continuation from the device-resident token
+            assert a.forward_greedy(-1, pos) == b.forward_greedy(-1, pos)
+            pos += 1
+    finally:
+        a.close()
+        b.close()
+
+
+def test_prefill_argument_errors(cuda, model_path):
+    from mcpm import engine as E
+    e = E.MiniCPM5Engine(device=0, max_seq=16)
+    try:
+        assert e.load_model(model_path)
+        with pytest.raises(E.MCPMError) as ei:
+            e.prefill([1] * 10, 8)
+        assert ei.value.status == E.CTX_OVERFLOW
+        with pytest.raises(E.MCPMError) as ei:
+            e.prefill([1, 130560], 0)
+        assert ei.value.status == E.BAD_TOKEN
+    finally:
+        e.close()
+
+
+def test_kv_snapshot_restore_session(cuda, model_path):
+    """A session snapshot restored into the same engine or into a second one continues the
+    decode exactly: a second turn prefilled after the restore gives the same logits as the
+    uninterrupted session."""
+    from mcpm import engine as E, synth
+    turn1 = [int(t) for t in synth.prompt_ids(40, seed=5)]
+    turn2 = [int(t) for t in synth.prompt_ids(12, seed=6)]
+    a = E.MiniCPM5Engine(device=0, max_seq=80)
+    b = E.MiniCPM5Engine(device=0, max_seq=64)
+    try:
+        assert a.load_model(model_path) and b.load_model(model_path)
+        a.prefill(turn1, 0, logits=False)
+        n = len(turn1)
+        snap = a.kv_snapshot(n)
+        assert snap.size == 42 * 2 * n * 256
+        _, want = a.prefill(turn2, n)            # the uninterrupted session
+        a.prefill([7, 8, 9], n)                  # another branch overwrites positions n..n+2
+        a.kv_restore(n, snap)
+        _, again = a.prefill(turn2, n)
+        assert np.array_equal(again.view(np.uint32), want.view(np.uint32))
+        b.kv_restore(n, snap)                    # a second engine continues the same session
+        _, other = b.prefill(turn2, n)
+        assert np.array_equal(other.view(np.uint32), want.view(np.uint32))
+        with pytest.raises(E.MCPMError) as ei:
+            b.kv_restore(65, np.zeros(42 * 2 * 65 * 256, np.float32))
+        assert ei.value.status == E.CTX_OVERFLOW
+    finally:
+        a.close()
+        b.close()
+
+
+# ------------------------------------------------------------------ fp16 KV cache option
+def _f16_engine(model_path, max_seq):
+    from mcpm import engine as E
+    e = E.MiniCPM5Engine(device=0, max_seq=max_seq, kv_type=E.KV_F16)
+    assert e.load_model(model_path)
+    return e
+
+
+def test_f16_kv_forward_bitexact_vs_restatement(cuda, oracle, model_path):
+    """kv_type MCPM_KV_F16: K and V rounded to half precision (nearest even) when a step writes
+    them, read back exactly, attention in fp32.  The restatement with the same option gives
+    bit-identical residuals, logits, cache rows and greedy tokens."""
+    import oracle as O
+    from mcpm import synth
+    e = _f16_engine(model_path, MAX_SEQ)
+    om = O.OracleModel(oracle, model_path, MAX_SEQ, kv_f16=True)
+    try:
+        prompt = synth.prompt_ids(N_PROMPT)
+        ref_logits = np.zeros(e.n_vocab, np.float32)
+        tok = None
+        for pos in range(N_PROMPT + N_GEN):
+            t = int(prompt[pos]) if pos < N_PROMPT else tok
+            got = e.forward(t, pos).copy()
+            want_tok = om.forward(t, pos, ref_logits)
+            assert np.array_equal(e.read_x().view(np.uint32), om.x().view(np.uint32)), f"pos {pos}"
+            diff = np.sum(got.view(np.uint32) != ref_logits.view(np.uint32))
+            assert diff == 0, f"pos {pos}: {diff} logits differ"
+            assert e.last_argmax == want_tok
+            tok = want_tok
+        k, v = e.read_kv(5, 3)   # stored rows are half-representable
+        assert np.array_equal(k.astype(np.float16).astype(np.float32), k)
+        assert np.array_equal(v.astype(np.float16).astype(np.float32), v)
+        assert np.any(k != 0)
+    finally:
+        e.close()
+        om.close()
+
+
+@pytest.mark.parametrize("pos", [300, 1000, 10300])
+def test_f16_kv_late_steps_bitexact_vs_restatement(cuda, oracle, model_path, pos):
+    """Late positions over a seeded fp16 cache: every attention chunking of the decode kernel
+    reading half rows (mcpm_write_kv rounds the seeded rows the way a step rounds its own)."""
+    import oracle as O
+    from mcpm import spec
+    max_seq = pos + 2
+    e = _f16_engine(model_path, max_seq)
+    om = O.OracleModel(oracle, model_path, max_seq, kv_f16=True)
+    try:
+        rng = np.random.default_rng(pos + 1)
+        k = rng.normal(0, 1, (pos, 256)).astype(np.float32)
+        v = rng.normal(0, 1, (pos, 256)).astype(np.float32)
+        kh, vh = k.astype(np.float16).astype(np.float32), v.astype(np.float16).astype(np.float32)
+        for layer in range(spec.N_LAYER):
+            e.write_kv(layer, 0, np.roll(k, layer, axis=0), np.roll(v, 3 * layer, axis=0))
+            om.set_kv(layer, np.roll(kh, layer, axis=0), np.roll(vh, 3 * layer, axis=0))
+        gk, gv = e.read_kv(7, pos - 1)
+        assert np.array_equal(gk, np.roll(kh, 7, axis=0)[pos - 1]) and np.array_equal(gv, np.roll(vh, 21, axis=0)[pos - 1])
+        ref_logits = np.zeros(e.n_vocab, np.float32)
+        tok = 7
+        for p in (pos, pos + 1):
+            got = e.forward(tok, p).copy()
+            want_tok = om.forward(tok, p, ref_logits)
+            assert np.array_equal(e.read_x().view(np.uint32), om.x().view(np.uint32)), f"pos {p}"
+            diff = np.sum(got.view(np.uint32) != ref_logits.view(np.uint32))
+            assert diff == 0, f"pos {p}: {diff} logits differ"
+            assert e.last_argmax == want_tok
+            tok = want_tok
+    finally:
+        e.close()
+        om.close()
+
+
+def test_f16_kv_prefill_snapshot_and_accuracy(cuda, model_path):
+    """fp16 cache: batched prefill equals one forward per position bit for bit, a snapshot is half
+    the fp32 size and restores exactly, and the logits stay close to the fp32 cache's (the only
+    change is the rounding of K and V to 11 significant bits)."""
+    from mcpm import engine as E, synth
+    prompt = [int(t) for t in synth.prompt_ids(90, seed=31)]
+    a = _f16_engine(model_path, 128)
+    b = _f16_engine(model_path, 128)
+    c = E.MiniCPM5Engine(device=0, max_seq=128)
+    try:
+        assert c.load_model(model_path)
+        tok_a, lg_a = a.prefill(prompt, 0)
+        for pos, t in enumerate(prompt):
+            lg_b = b.forward(t, pos).copy()
+            lg_c = c.forward(t, pos).copy()
+        assert np.array_equal(lg_a.view(np.uint32), lg_b.view(np.uint32)) and tok_a == b.last_argmax
+        snap = a.kv_snapshot(len(prompt))
+        assert snap.dtype == np.float16 and snap.nbytes == 42 * 2 * len(prompt) * 256 * 2
+        b.kv_restore(len(prompt), snap)
+        assert a.forward_greedy(-1, len(prompt)) == b.forward_greedy(-1, len(prompt))
+        # fp16 rounding of K and V against the fp32 cache: relative logit error well under 1%
+        rel = np.max(np.abs(lg_a - lg_c)) / np.max(np.abs(lg_c))
+        assert rel < 1e-2, rel
+    finally:
+        a.close()
+        b.close()
+        c.close()
+
+
+def test_kv_type_validated(cuda):
+    from mcpm import engine as E
+    with pytest.raises(E.MCPMError) as ei:
+        E.MiniCPM5Engine(device=0, max_seq=16, kv_type=2)
+    assert ei.value.status == E.BAD_ARG
+
+
+@pytest.mark.parametrize("pos0", [0, 290])
+def test_schedule_options_bitexact(cuda, model_path, pos0):
+    """Decode schedule options (mcpm_config::sched: L2 prefetch, head-pair attention combiners at
+    every context length) change when copies are issued and who combines the attention chunks,
+    never the arithmetic: logits are bit-identical to the default schedule.  pos0 = 290 runs 10
+    attention chunks, combined by every CTA by default and by the combiners with option 2."""
+    from mcpm import engine as E, spec, synth
+    scheds = (0, 1, 2, 3)
+    max_seq = pos0 + 40
+    engs = [E.MiniCPM5Engine(device=0, max_seq=max_seq, sched=s) for s in scheds]
+    try:
+        for e in engs:
+            assert e.load_model(model_path)
+        if pos0:
+            rng = np.random.default_rng(11)
+            k = rng.normal(0, 1, (pos0, 256)).astype(np.float32)
+            v = rng.normal(0, 1, (pos0, 256)).astype(np.float32)
+            for layer in range(spec.N_LAYER):
+                for e in engs:
+                    e.write_kv(layer, 0, np.roll(k, layer, axis=0), np.roll(v, layer, axis=0))
+        prompt = synth.prompt_ids(24, seed=99)
+        for i in range(24):
+            outs = [e.forward(int(prompt[i]), pos0 + i).copy() for e in engs]
+            for s, o in zip(scheds[1:], outs[1:]):
+                assert np.array_equal(o.view(np.uint32), outs[0].view(np.uint32)), f"sched {s} pos {pos0 + i}"
+    finally:
+        for e in engs:
+            e.close()
