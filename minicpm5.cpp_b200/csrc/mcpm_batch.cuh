@@ -40,6 +40,8 @@ struct BGemmArgs {
     float* y;
     int y_stride, n_seq;
     unsigned* err;   // k_b_gemm_tc: ERR_TIMEOUT when an MMA completion never arrives
+    float* part;     // k_b_gemm_tc: group partials (tb_scratch_floats(ntiles, nb / 4))
+    unsigned* cnt;   // k_b_gemm_tc: one counter per row tile, zero between launches
 };
 
 // k_b_gemm8 (8 blocks per row: QKV, o_proj, gate/up, LM head): the activations of every
@@ -389,353 +391,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1) k_b_gemm24(const BGemmArgs a) {
     }
 }
 
-// ---------------------------------------------------------------- tcgen05 GEMM
-// k_b_gemm_tc: the same products and the same fp32 chains as k_b_gemm8 / k_b_gemm24, with the
-// integer lane sums from the 5th-generation tensor cores.  A tile is 128 weight rows x 32
-// sequences.  Per 256-weight block every thread dequantises (row, sub-block, half) tasks
-// straight from global memory (the tile's rows are prefetched into L2 one tile ahead) into the
-// hi / lo int8 operands; one thread then issues 16 tcgen05.mma (kind::i8, M = 128, N = 32,
-// K = 32): lane k x {hi, lo}, each into its own 32-column int32 accumulator (all 512 TMEM
-// columns), and commits them to an mbarrier.  Operands are K-major without swizzle: 8-row x
-// 16-byte core matrices, 128 B apart along M / N (SBO), the two 16-byte halves of a lane's K
-// range LBO apart.  The epilogue (warp w: TMEM lanes = tile rows 32 (w % 4) .. +31, sequences
-// 8 (w / 4) .. +7) reads the accumulators with tcgen05.ld and runs, per (row, sequence), the
-// batch-1 GEMV's chain acc[k] = fma(xd*d, 64*hi_k + lo_k (- Q6_K offset), acc[k]), the min
-// chain and the hsum_f32_8 tree, in the same order as the mma.sync kernels.
-constexpr int TC_M = 128, TC_NT = 32, TC_THREADS = 512, TC_COLS = 512;
-constexpr int TC_A_LBO = (TC_M / 8) * 128;    // K-half stride of a weight operand (2048 B)
-constexpr int TC_B_LBO = (TC_NT / 8) * 128;   // K-half stride of the activation operand (512 B)
-constexpr int TC_AHI = 0;                                 // [16 K-halves][16 row groups][8][16] int8
-constexpr int TC_ALO = TC_AHI + 16 * TC_A_LBO;
-constexpr int TC_BX = TC_ALO + 16 * TC_A_LBO;             // 2 x [16 K-halves][4 seq groups][8][16] int8
-constexpr int TC_XD = TC_BX + 2 * 16 * TC_B_LBO;          // 2 x float [32]
-constexpr int TC_XB = TC_XD + 2 * TC_NT * 4;              // 2 x int16 [32][16]
-constexpr int TC_RM = TC_XB + 2 * TC_NT * 32;             // float d [128], dmin [128]; 16 B per row of mins / scales
-constexpr int TC_RAW_STRIDE = 432;                        // bytes per row of a staged block pair (>= 2 x 210, 16 | 432)
-constexpr int TC_RAW = TC_RM + TC_M * 8 + TC_M * 16;      // 2 x [128 rows][TC_RAW_STRIDE] raw block pairs
-constexpr int TC_BAR = TC_RAW + 2 * TC_M * TC_RAW_STRIDE; // mbarrier, TMEM base address
-constexpr int TC_BYTES = TC_BAR + 16;
-// instruction descriptor: S32 accumulator, S8 x S8, both K-major, N = 32, M = 128
-constexpr uint32_t TC_IDESC = (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(TC_NT >> 3) << 17) |
-                              (static_cast<uint32_t>(TC_M >> 4) << 24);
-static_assert(TC_BYTES <= 232448 && TC_BX % 16 == 0 && TC_RM % 16 == 0 && TC_RAW % 16 == 0 && TC_BAR % 8 == 0,
-              "k_b_gemm_tc layout");
-
-__device__ __forceinline__ uint64_t tc_desc(const void* p, uint32_t lbo, uint32_t sbo) {   // SWIZZLE_NONE, version 1
-    return static_cast<uint64_t>((smem_u32(p) & 0x3ffffu) >> 4) | (static_cast<uint64_t>(lbo >> 4) << 16) |
-           (static_cast<uint64_t>(sbo >> 4) << 32) | (1ull << 46);
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t adesc, uint64_t bdesc) {
-    asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d),
-        "l"(adesc), "l"(bdesc), "r"(TC_IDESC), "r"(0), "r"(0), "r"(0), "r"(0), "r"(0)
-        : "memory");
-}
-__device__ __forceinline__ void tc_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-__device__ __forceinline__ void tc_ld8(uint32_t taddr, uint32_t (&v)[8]) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
-                 : "r"(taddr)
-                 : "memory");
-}
-__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-// Activation block b of sequences seq0 .. seq0+31 -> operand buffer `buf` (K-major core
-// matrices; the values are already lane-major), scales and block sums; zeros beyond n_seq.
-__device__ void tc_stage_x(const BGemmArgs& a, int seq0, int b, int buf, uint8_t* smt) {
-    const int tid = threadIdx.x;
-    {   // 32 sequences x 16 chunks: one per thread
-        const int q = tid >> 4, c = tid & 15, sq = seq0 + q;
-        uint8_t* dst = smt + TC_BX + buf * 16 * TC_B_LBO + c * TC_B_LBO + (q >> 3) * 128 + (q & 7) * 16;
-        if (sq < a.n_seq)
-            cp_async16(dst, a.aqs + (static_cast<size_t>(sq) * B_NBA + b) * 256 + 16 * c);
-        else
-            *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
-    }
-    if (tid < 2 * TC_NT) {
-        const int q = tid >> 1, h = tid & 1, sq = seq0 + q;
-        int16_t* dst = reinterpret_cast<int16_t*>(smt + TC_XB + buf * TC_NT * 32) + 16 * q + 8 * h;
-        if (sq < a.n_seq)
-            cp_async16(dst, a.abs + (static_cast<size_t>(sq) * B_NBA + b) * 16 + 8 * h);
-        else
-            *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
-    } else if (tid < 3 * TC_NT) {
-        const int q = tid - 2 * TC_NT, sq = seq0 + q;
-        float* dst = reinterpret_cast<float*>(smt + TC_XD + buf * TC_NT * 4) + q;
-        if (sq < a.n_seq)
-            cp_async4(dst, a.ad + static_cast<size_t>(sq) * B_NBA + b);
-        else
-            *dst = 0.0f;
-    }
-}
-
-// Blocks 2p, 2p+1 of rows row0 .. row0+127 (a 16-byte aligned range of 288 B per row for
-// Q4_K, 4-byte aligned 420 B for Q6_K) -> raw buffer `buf`.  Rows past the segment are skipped.
-template <int TYPE>
-__device__ __forceinline__ void tc_stage_raw(const BGemmSeg& sg, int row0, int nb, int p, int buf, uint8_t* smt) {
-    constexpr int BYTES = TYPE == GGML_Q4_K ? Q4K_BYTES : Q6K_BYTES;
-    const size_t rb = static_cast<size_t>(nb) * BYTES;
-    uint8_t* dst0 = smt + TC_RAW + buf * TC_M * TC_RAW_STRIDE;
-    const int nr = min(TC_M, sg.rows - row0);
-    if (TYPE == GGML_Q4_K) {
-        constexpr int NCH = 2 * BYTES / 16;   // 18
-        for (int i = threadIdx.x; i < nr * NCH; i += TC_THREADS) {
-            const int r = i / NCH, c = i - r * NCH;
-            cp_async16(dst0 + r * TC_RAW_STRIDE + 16 * c,
-                       sg.w + static_cast<size_t>(row0 + r) * rb + static_cast<size_t>(p) * 2 * BYTES + 16 * c);
-        }
-    } else {
-        constexpr int NCH = 2 * BYTES / 4;    // 105
-        for (int i = threadIdx.x; i < nr * NCH; i += TC_THREADS) {
-            const int r = i / NCH, c = i - r * NCH;
-            cp_async4(dst0 + r * TC_RAW_STRIDE + 4 * c,
-                      sg.w + static_cast<size_t>(row0 + r) * rb + static_cast<size_t>(p) * 2 * BYTES + 4 * c);
-        }
-    }
-}
-
-// Block b of rows row0 .. row0+127 (staged in raw buffer (b >> 1) & 1) -> hi / lo operands and
-// the row metadata (bg_dequant's arithmetic).  Rows past the segment are left stale: their
-// outputs are never stored.
-template <int TYPE>
-__device__ __forceinline__ void tc_dequant(const BGemmSeg& sg, int row0, int b, uint8_t* smt) {
-    constexpr int BYTES = TYPE == GGML_Q4_K ? Q4K_BYTES : Q6K_BYTES;
-    const uint8_t* raw = smt + TC_RAW + ((b >> 1) & 1) * TC_M * TC_RAW_STRIDE + (b & 1) * BYTES;
-    float* rd = reinterpret_cast<float*>(smt + TC_RM);
-    uint8_t* rms = smt + TC_RM + 8 * TC_M;
-#pragma unroll 1
-    for (int task = threadIdx.x; task < TC_M * 16; task += TC_THREADS) {
-        const int r = task >> 4, s = (task >> 1) & 7, half = task & 1;
-        if (row0 + r >= sg.rows) continue;
-        const uint8_t* blk = raw + r * TC_RAW_STRIDE;
-        uint32_t hw[4], lw[4];
-        if (TYPE == GGML_Q4_K) {
-            const uint4 head = *reinterpret_cast<const uint4*>(blk);   // d, dmin, 12 packed scale bytes
-            const uint4 qv = *reinterpret_cast<const uint4*>(blk + 16 + 32 * (s >> 1) + 16 * half);
-            auto sc8 = [&](int i) -> int {
-                const uint32_t wd = i < 4 ? head.y : i < 8 ? head.z : head.w;
-                return static_cast<int>((wd >> (8 * (i & 3))) & 0xffu);
-            };
-            int sc, mn;   // get_scale_min_k4 (include/ops.h:67-75)
-            if (s < 4) {
-                sc = sc8(s) & 63;
-                mn = sc8(s + 4) & 63;
-            } else {
-                sc = (sc8(s + 4) & 15) | ((sc8(s - 4) >> 6) << 4);
-                mn = (sc8(s + 4) >> 4) | ((sc8(s) >> 6) << 4);
-            }
-            const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-                const uint32_t nib = (s & 1) ? (qw[kk] >> 4) & 0x0f0f0f0fu : qw[kk] & 0x0f0f0f0fu;
-                const uint32_t wa = __byte_perm(nib, 0u, 0x4240) * static_cast<uint32_t>(sc);
-                const uint32_t wb = __byte_perm(nib, 0u, 0x4341) * static_cast<uint32_t>(sc);
-                bg_pack(wa, wb, 0, hw[kk], lw[kk]);
-            }
-            if (half == 0) reinterpret_cast<uint16_t*>(rms + 16 * r)[s] = static_cast<uint16_t>(mn * 0x0101);
-            if (s == 0 && half == 0) {
-                rd[r] = h2f(head.x);
-                rd[TC_M + r] = h2f(head.x >> 16);
-            }
-        } else {
-            const int h = s >> 2, kk6 = s & 3;
-            const uint16_t* ql = reinterpret_cast<const uint16_t*>(blk + 64 * h + 32 * (kk6 & 1) + 16 * half);
-            const uint16_t* qh = reinterpret_cast<const uint16_t*>(blk + 128 + 32 * h + 16 * half);
-            const int scale = static_cast<int8_t>(blk[192 + 2 * s + half]);
-            const uint32_t sc1 = static_cast<uint32_t>(scale + 128);
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-                const uint32_t lq = static_cast<uint32_t>(ql[2 * kk]) | (static_cast<uint32_t>(ql[2 * kk + 1]) << 16);
-                const uint32_t hq = static_cast<uint32_t>(qh[2 * kk]) | (static_cast<uint32_t>(qh[2 * kk + 1]) << 16);
-                const uint32_t lo4 = (kk6 & 2) ? (lq >> 4) & 0x0f0f0f0fu : lq & 0x0f0f0f0fu;
-                const uint32_t q6 = lo4 | (((hq >> (2 * kk6)) & 0x03030303u) << 4);
-                const uint32_t qa = __byte_perm(q6, 0u, 0x4240), qb = __byte_perm(q6, 0u, 0x4341);
-                const uint32_t wa = qa * sc1 + 0x20002000u - (qa << 7), wb = qb * sc1 + 0x20002000u - (qb << 7);
-                bg_pack(wa, wb, 1, hw[kk], lw[kk]);
-            }
-            reinterpret_cast<int8_t*>(rms + 16 * r)[2 * s + half] = static_cast<int8_t>(scale);
-            if (s == 0 && half == 0) rd[r] = h2f(*reinterpret_cast<const uint16_t*>(blk + 208));
-        }
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {   // lane k = 4 half + kk: K bytes 32k + 4s .. +3 -> K-half 2k + (s >> 2)
-            const int k = 4 * half + kk;
-            const int off = (2 * k + (s >> 2)) * TC_A_LBO + (r >> 3) * 128 + (r & 7) * 16 + 4 * (s & 3);
-            *reinterpret_cast<uint32_t*>(smt + TC_AHI + off) = hw[kk];
-            *reinterpret_cast<uint32_t*>(smt + TC_ALO + off) = lw[kk];
-        }
-    }
-}
-
-// One (128-row, 32-sequence) tile.  false when an MMA completion timed out.
-template <int TYPE>
-__device__ bool tc_tile(const BGemmArgs& a, const BGemmSeg& sg, int row0, int seq0, uint32_t tmem, uint64_t* bar,
-                        uint32_t& phase, uint8_t* smt) {
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, qd = warp & 3, part = warp >> 2;
-    const int re = 32 * qd + lane;                      // this thread's tile row (TMEM lane)
-    const uint32_t tl = tmem + (static_cast<uint32_t>(32 * qd) << 16) + 8 * part;
-    const int nb = a.nb;
-    float acc[8][8], acc_min[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        acc_min[j] = 0.0f;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) acc[j][k] = 0.0f;
-    }
-    // copies: raw pair p+1 is issued in step 2p (behind X(2p+1)); the end of step b waits for
-    // what step b+1 reads (X(b+1), and for odd b the raw pair of b+1).
-    tc_stage_raw<TYPE>(sg, row0, nb, 0, 0, smt);
-    tc_stage_x(a, seq0, 0, 0, smt);
-    cp_async_commit();
-    cp_async_wait_all();
-    __syncthreads();
-    bool ok = true;
-    for (int b = 0; b < nb; ++b) {
-        const int buf = b & 1;
-        tc_dequant<TYPE>(sg, row0, b, smt);
-        fence_proxy_async_smem();  // operands written by the generic proxy -> visible to the tensor cores
-        __syncthreads();
-        if (tid == 0) {
-            tc_fence_after();
-            const uint8_t* bx = smt + TC_BX + buf * 16 * TC_B_LBO;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const uint64_t bd = tc_desc(bx + 2 * k * TC_B_LBO, TC_B_LBO, 128);
-                tc_mma(tmem + (2 * k) * TC_NT, tc_desc(smt + TC_AHI + 2 * k * TC_A_LBO, TC_A_LBO, 128), bd);
-                tc_mma(tmem + (2 * k + 1) * TC_NT, tc_desc(smt + TC_ALO + 2 * k * TC_A_LBO, TC_A_LBO, 128), bd);
-            }
-            tc_commit(bar);
-        }
-        if (b + 1 < nb) tc_stage_x(a, seq0, b + 1, buf ^ 1, smt);   // next activation block, other buffer
-        cp_async_commit();
-        if (!(b & 1) && b + 2 < nb) tc_stage_raw<TYPE>(sg, row0, nb, (b >> 1) + 1, ((b >> 1) + 1) & 1, smt);
-        cp_async_commit();
-        ok = __all_sync(0xffffffffu, mbar_wait(bar, phase, a.err));   // warp-uniform: tcgen05.ld is .aligned
-        phase ^= 1u;
-        tc_fence_after();
-        if (ok) {
-            const float* rd = reinterpret_cast<const float*>(smt + TC_RM);
-            const uint4 mw = *reinterpret_cast<const uint4*>(smt + TC_RM + 8 * TC_M + 16 * re);
-            const uint32_t msw[4] = {mw.x, mw.y, mw.z, mw.w};
-            const float* xd = reinterpret_cast<const float*>(smt + TC_XD + buf * TC_NT * 4) + 8 * part;
-            const uint32_t* xbw = reinterpret_cast<const uint32_t*>(smt + TC_XB + buf * TC_NT * 32) + 8 * 8 * part;
-            const float d = rd[re];
-            float ds[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) ds[j] = __fmul_rn(xd[j], d);
-            if (TYPE == GGML_Q4_K) {   // minsum = sum_g mins[g] * (bsums[2g] + bsums[2g+1])
-                const float dmin = rd[TC_M + re];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    int ms = 0;
-#pragma unroll
-                    for (int g = 0; g < 4; ++g)
-                        ms = dp2hi(xbw[8 * j + 2 * g + 1], msw[g], dp2lo(xbw[8 * j + 2 * g], msw[g], ms));
-                    acc_min[j] = __fmaf_rn(-__fmul_rn(xd[j], dmin), __int2float_rn(ms), acc_min[j]);
-                }
-            }
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                uint32_t hv[8], lv[8];
-                tc_ld8(tl + (2 * k) * TC_NT, hv);
-                tc_ld8(tl + (2 * k + 1) * TC_NT, lv);
-                tc_wait_ld();
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    int v = static_cast<int>(hv[j]) * 64 + static_cast<int>(lv[j]);
-                    if (TYPE == GGML_Q6_K) {   // -32 * (bsums[2k] * sc[2k] + bsums[2k+1] * sc[2k+1])
-                        const uint32_t bw = xbw[8 * j + k], sw = msw[k >> 1];
-                        v -= 32 * ((k & 1) ? dp2hi(bw, sw, 0) : dp2lo(bw, sw, 0));
-                    }
-                    acc[j][k] = __fmaf_rn(ds[j], __int2float_rn(v), acc[j][k]);
-                }
-            }
-        }
-        if (b & 1)
-            cp_async_wait_all();       // X(b+1) and the raw pair of b+1
-        else
-            cp_async_wait_group<1>();  // X(b+1); the raw pair issued in this step may stay in flight
-        tc_fence_before();
-        if (!__syncthreads_and(ok)) return false;   // operands and accumulators free for the next block
-    }
-    const int row = row0 + re;
-    if (row < sg.rows) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int q = seq0 + 8 * part + j;
-            if (q >= a.n_seq) continue;
-            const float* v = acc[j];   // hsum_f32_8 (ops_avx2.cpp:43-48)
-            float r = __fadd_rn(__fadd_rn(__fadd_rn(v[0], v[4]), __fadd_rn(v[2], v[6])),
-                                __fadd_rn(__fadd_rn(v[1], v[5]), __fadd_rn(v[3], v[7])));
-            if (TYPE == GGML_Q4_K) r = __fadd_rn(r, acc_min[j]);
-            a.y[static_cast<size_t>(q) * a.y_stride + sg.out_off + row] = r;
-        }
-    }
-    return true;
-}
-
-// L2 prefetch of a row tile's weight bytes (128-byte lines spread over the CTA).
-__device__ __forceinline__ void tc_prefetch_rows(const BGemmArgs& a, int mt) {
-    if (mt >= a.ntiles) return;
-    const BGemmSeg sg = bg_seg(a, mt);
-    const int row0 = (mt - sg.tile0) * TC_M, nr = min(TC_M, sg.rows - row0);
-    const size_t rb = static_cast<size_t>(a.nb) * (sg.type == GGML_Q4_K ? Q4K_BYTES : Q6K_BYTES);
-    const uint8_t* base = sg.w + static_cast<size_t>(row0) * rb;
-    const size_t lines = (static_cast<size_t>(nr) * rb + 127) / 128;
-    for (size_t i = threadIdx.x; i < lines; i += TC_THREADS)
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(base + 128 * i));
-}
-
-// Persistent: CTA c takes tiles c, c + grid, ...; tile t = (row tile t / n_ntiles, sequence
-// tile t % n_ntiles), so the CTAs of one row tile read the same weights from L2.  One CTA per
-// SM (512 threads at up to 128 registers fill the register file), so the 512-column TMEM
-// allocation never waits for another CTA.
-__global__ void __launch_bounds__(TC_THREADS, 1) k_b_gemm_tc(const BGemmArgs a) {
-    extern __shared__ __align__(1024) uint8_t smt[];
-    const int tid = threadIdx.x, warp = tid >> 5;
-    uint64_t* bar = reinterpret_cast<uint64_t*>(smt + TC_BAR);
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(smt + TC_BAR + 8);
-    const int ntn = (a.n_seq + TC_NT - 1) / TC_NT, ntiles = a.ntiles * ntn;
-    if (static_cast<int>(blockIdx.x) >= ntiles) return;
-    if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
-                     "r"(TC_COLS)
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-    }
-    if (tid == 32) {
-        mbar_init(bar, 1);
-        fence_mbar_init();
-    }
-    tc_prefetch_rows(a, blockIdx.x / ntn);
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = *tslot;
-    uint32_t phase = 0;
-    bool ok = true;
-    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-        const int mt = t / ntn, nt = t % ntn;
-        if ((t + static_cast<int>(gridDim.x)) / ntn != mt) tc_prefetch_rows(a, (t + gridDim.x) / ntn);
-        const BGemmSeg sg = bg_seg(a, mt);
-        const int row0 = (mt - sg.tile0) * TC_M;
-        ok = sg.type == GGML_Q4_K ? tc_tile<GGML_Q4_K>(a, sg, row0, nt * TC_NT, tmem, bar, phase, smt)
-                                  : tc_tile<GGML_Q6_K>(a, sg, row0, nt * TC_NT, tmem, bar, phase, smt);
-    }
-    cp_async_wait_all();
-    if (!ok && tid == 0) mbar_wait(bar, phase ^ 1u, nullptr);   // a late completion: let the MMAs drain
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (warp == 0)
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_COLS) : "memory");
-}
+#include "mcpm_batch_tc.cuh"
 
 // RMSNorm + Q8_K of one sequence (norm_quant's arithmetic: per-thread fma chains over
 // x[tid + 256 i], warp butterflies, an 8-leaf tree; y = (x * w) * rms) for a 256-thread CTA.

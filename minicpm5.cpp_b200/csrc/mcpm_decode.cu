@@ -379,6 +379,13 @@ __device__ void embed_row(const uint8_t* embd, int token, float* xs) {
     }
 }
 
+// Q8_K block `blk` of s.xq() from the warp's 256 values (lane l: a = y[8l..8l+3], b = y[8l+4..8l+7]).
+template <bool AWAY>
+__device__ __forceinline__ void quant_xq(float4 a, float4 b, XQSmem* xq, int blk) {
+    const float y[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    quant_block_warp<AWAY>(y, xq->qs[blk], &xq->d[blk], xq->bsums[blk]);
+}
+
 // Reads x[tid + 256 i] (i < 8) from epoch-tagged words, polling until every word carries
 // `epoch` (written by the phase that produced x).  False after the 1 s bound.
 __device__ bool load8_epoch(const unsigned long long* src, unsigned epoch, int tid, float (&xv)[8], unsigned* err) {
@@ -454,7 +461,7 @@ __device__ bool norm_quant(const DecodeParams& p, const float* x, unsigned epoch
         float y[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) y[k] = __fmul_rn(__fmul_rn(xb[k], wv[k]), rms);
-        quant_block_warp<AWAY>(y, s.xq()->qs[warp], &s.xq()->d[warp], s.xq()->bsums[warp]);
+        quant_xq<AWAY>(make_float4(y[0], y[1], y[2], y[3]), make_float4(y[4], y[5], y[6], y[7]), s.xq(), warp);
     }
     __syncthreads();
     return true;
@@ -1126,8 +1133,7 @@ __device__ void combine_attention(const DecodeParams& p, const Smem& s, int l, i
     if (h < N_EMBD / 256) {
         const float4 a = *reinterpret_cast<const float4*>(ab + 256 * h + 8 * lane);
         const float4 b = *reinterpret_cast<const float4*>(ab + 256 * h + 8 * lane + 4);
-        const float y[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-        quant_block_warp<false>(y, s.xq()->qs[h], &s.xq()->d[h], s.xq()->bsums[h]);
+        quant_xq<false>(a, b, s.xq(), h);
     }
     __syncthreads();
 }
@@ -1142,7 +1148,7 @@ __device__ bool load_att_epoch(const DecodeParams& p, const Smem& s, unsigned ep
         float y[8];
         ok = load8c_epoch(p.attw + (blockIdx.x % ATTW_COPIES) * N_EMBD + 256 * warp + 8 * lane, epoch, y, p.err);
         if (p.trace && blockIdx.x == 0 && lane == 0 && epoch == (epoch & ~0xffu) + 1) p.trace[2920 + warp] = globaltimer();
-        quant_block_warp<false>(y, s.xq()->qs[warp], &s.xq()->d[warp], s.xq()->bsums[warp]);
+        quant_xq<false>(make_float4(y[0], y[1], y[2], y[3]), make_float4(y[4], y[5], y[6], y[7]), s.xq(), warp);
     }
     return __syncthreads_and(ok);
 }
@@ -1222,12 +1228,8 @@ __device__ bool phase_down(const DecodeParams& p, const Smem& s, int l, int cta,
             a1 = ld_cg_f4(p.h + 256 * b1 + 8 * lane);
             c1 = ld_cg_f4(p.h + 256 * b1 + 8 * lane + 4);
         }
-        const float y0[8] = {a0.x, a0.y, a0.z, a0.w, c0.x, c0.y, c0.z, c0.w};
-        quant_block_warp<true>(y0, s.xq()->qs[b0], &s.xq()->d[b0], s.xq()->bsums[b0]);
-        if (two) {
-            const float y1[8] = {a1.x, a1.y, a1.z, a1.w, c1.x, c1.y, c1.z, c1.w};
-            quant_block_warp<true>(y1, s.xq()->qs[b1], &s.xq()->d[b1], s.xq()->bsums[b1]);
-        }
+        quant_xq<true>(a0, c0, s.xq(), b0);
+        if (two) quant_xq<true>(a1, c1, s.xq(), b1);
     }
     __syncthreads();
     trace_step(p, l, 4, 1);
@@ -1537,7 +1539,7 @@ cudaError_t launch_batch_step(const BatchLaunch& b, cudaStream_t stream) {
             e = cudaFuncSetAttribute(k_b_att_combine, cudaFuncAttributeMaxDynamicSharedMemorySize, COMBINE_SMEM);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(k_b_gemm8, cudaFuncAttributeMaxDynamicSharedMemorySize, GA_BYTES);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(k_b_gemm24, cudaFuncAttributeMaxDynamicSharedMemorySize, GB_BYTES);
-        if (e == cudaSuccess) e = cudaFuncSetAttribute(k_b_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_BYTES);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(k_b_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, TB_BYTES);
         if (e != cudaSuccess) return e;
         prepared_dev = dev;
     }
@@ -1556,7 +1558,7 @@ cudaError_t launch_batch_step(const BatchLaunch& b, cudaStream_t stream) {
     const bool gemm_kind = b.tcgen05 != 0;
     auto gemm = [&](std::initializer_list<BGemmSeg> segs, int nb, float* y, int y_stride) {
         BGemmArgs g{};
-        const int rows_per_tile = gemm_kind ? TC_M : BG_ROWS;
+        const int rows_per_tile = gemm_kind ? TB_M : BG_ROWS;
         int tiles = 0, i = 0;
         for (BGemmSeg sg : segs) {
             sg.tile0 = tiles;
@@ -1566,8 +1568,9 @@ cudaError_t launch_batch_step(const BatchLaunch& b, cudaStream_t stream) {
         g.nseg = i, g.ntiles = tiles, g.nb = nb;
         g.aqs = b.aqs, g.ad = b.ad, g.abs = b.abs, g.y = y, g.y_stride = y_stride, g.n_seq = n, g.err = b.err;
         if (gemm_kind) {
-            const int total = tiles * ((n + TC_NT - 1) / TC_NT);
-            k_b_gemm_tc<<<std::min(total, b.n_sm), TC_THREADS, TC_BYTES, stream>>>(g);
+            g.part = b.gemm_part, g.cnt = b.gemm_cnt;
+            const int units = tiles * (nb / TB_G);
+            k_b_gemm_tc<<<std::min(units, b.n_sm), TB_THREADS, TB_BYTES, stream>>>(g);
             return;
         }
         if (nb == 8)

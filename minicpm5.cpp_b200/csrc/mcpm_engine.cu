@@ -86,6 +86,9 @@ struct mcpm_engine {
     float* p_ad = nullptr;
     int16_t* p_abs = nullptr;
     int *p_tokens = nullptr, *p_pos = nullptr, *p_argmax = nullptr;
+    // tcgen05 batched GEMM scratch (group partials, row-tile counters), shared by batch and prefill
+    float* g_part = nullptr;
+    unsigned* g_cnt = nullptr;
 };
 
 namespace {
@@ -139,8 +142,23 @@ void free_prefill(mcpm_engine* e) {
     free_dev(e->p_argmax);
 }
 
+// Scratch of the tcgen05 batched GEMM, allocated on first use (counters zeroed).
+mcpm_status ensure_gemm_scratch(mcpm_engine* e) {
+    if (e->batch_gemm != MCPM_GEMM_TCGEN05 || e->g_part) return MCPM_OK;
+    cudaError_t err = cudaMalloc(&e->g_part, batch_gemm_scratch_floats(e->n_vocab) * sizeof(float));
+    if (err == cudaSuccess) err = cudaMalloc(&e->g_cnt, batch_gemm_counters(e->n_vocab) * sizeof(unsigned));
+    if (err == cudaSuccess) err = cudaMemset(e->g_cnt, 0, batch_gemm_counters(e->n_vocab) * sizeof(unsigned));
+    if (err != cudaSuccess) {
+        free_dev(e->g_part);
+        free_dev(e->g_cnt);
+    }
+    return cuda_status(err);
+}
+
 void free_model(mcpm_engine* e) {
     free_prefill(e);
+    free_dev(e->g_part);
+    free_dev(e->g_cnt);
     free_dev(e->arena);
     free_dev(e->d_layers);
     free_dev(e->x);
@@ -785,6 +803,7 @@ mcpm_status mcpm_batch_init(mcpm_engine* e, int n_seq, int max_seq) {
     MCPM_CUDA(cudaSetDevice(e->device));
     MCPM_CUDA(cudaStreamSynchronize(e->stream));
     free_batch(e);
+    if (const mcpm_status st = ensure_gemm_scratch(e); st != MCPM_OK) return st;
     const size_t kv = static_cast<size_t>(n_seq) * e->n_layer * max_seq * KV_DIM;
     auto alloc = [&](auto** ptr, size_t bytes) -> cudaError_t {
         cudaError_t err = cudaMalloc(reinterpret_cast<void**>(ptr), bytes);
@@ -841,6 +860,7 @@ mcpm_status mcpm_batch_step_async(mcpm_engine* e, const int* tokens, const int* 
     b.n_seq = n, b.max_seq = e->b_max_seq, b.n_layer = e->n_layer, b.n_vocab = e->n_vocab, b.lm_type = e->lm_type;
     b.max_pos = max_pos, b.chain = 1, b.n_sm = e->n_sm, b.tcgen05 = e->batch_gemm == MCPM_GEMM_TCGEN05;
     b.kv_f16 = e->kv_f16;
+    b.gemm_part = e->g_part, b.gemm_cnt = e->g_cnt;
     b.layers = e->layers.data(), b.embd = e->embd, b.out_norm = e->out_norm, b.lm = e->lm, b.rope = e->b_rope;
     b.kc = e->b_kc, b.vc = e->b_vc, b.x = e->b_x, b.y = e->b_y, b.q = e->b_q, b.att_part = e->b_part;
     b.att = e->b_att, b.logits = e->b_logits, b.aqs = e->b_aqs, b.ad = e->b_ad, b.abs = e->b_abs;
@@ -880,6 +900,7 @@ mcpm_status mcpm_prefill(mcpm_engine* e, const int* tokens, int n, int pos0, flo
             return cuda_status(err);
         }
     }
+    if (const mcpm_status st = ensure_gemm_scratch(e); st != MCPM_OK) return st;
     std::vector<int> pos(BATCH_MAX);
     for (int done = 0; done < n;) {
         const int m = std::min(BATCH_MAX, n - done);
@@ -891,6 +912,7 @@ mcpm_status mcpm_prefill(mcpm_engine* e, const int* tokens, int n, int pos0, flo
         b.n_seq = m, b.max_seq = e->max_seq, b.n_layer = e->n_layer, b.n_vocab = e->n_vocab, b.lm_type = e->lm_type;
         b.max_pos = pos[m - 1], b.chain = 0, b.n_sm = e->n_sm, b.tcgen05 = e->batch_gemm == MCPM_GEMM_TCGEN05;
         b.shared_kv = 1, b.skip_lm = last ? 0 : 1, b.kv_f16 = e->kv_f16;
+        b.gemm_part = e->g_part, b.gemm_cnt = e->g_cnt;
         b.layers = e->layers.data(), b.embd = e->embd, b.out_norm = e->out_norm, b.lm = e->lm, b.rope = e->rope;
         b.kc = e->kc, b.vc = e->vc, b.x = e->p_x, b.y = e->p_y, b.q = e->p_q, b.att_part = e->p_part;
         b.att = e->p_att, b.aqs = e->p_aqs, b.ad = e->p_ad, b.abs = e->p_abs;

@@ -1,6 +1,7 @@
 // Internal declarations shared by the decode kernel (mcpm_decode.cu), the op kernels
 // (mcpm_ops.cu) and the host engine (mcpm_engine.cu).
 #pragma once
+#include <algorithm>
 #include <cstddef>
 #include <cstdint>
 
@@ -114,10 +115,25 @@ int decode_max_ctas_per_sm();
 // Standalone attention (mcpm_decode.cu): appends k/v at pos, then split-KV attention with
 // the decode kernel's numerics.  part: ATT_PART_FLOATS floats, cnt: 3 zeroed words.
 constexpr size_t ATT_PART_FLOATS = static_cast<size_t>(N_HEAD) * ATT_MAX_CHUNKS * ATT_PART_STRIDE;
+// Scratch of the tcgen05 batched GEMM (128-row tiles, groups of 4 blocks, 64 sequences): the
+// group partials of the widest launch (units = row tiles x groups) and one counter per row tile.
+inline size_t batch_gemm_units(int n_vocab) {
+    auto tiles = [](int rows) { return static_cast<size_t>((rows + 127) / 128); };
+    size_t u = 2 * tiles(n_vocab);                                         // LM head, 8 blocks per row
+    u = std::max(u, 2 * (2 * tiles(N_FF)));                                // gate + up
+    u = std::max(u, (N_FF / 256 / 4) * tiles(N_EMBD));                     // down, 24 blocks per row
+    u = std::max(u, 2 * (tiles(N_EMBD) + 2 * tiles(KV_DIM)));              // q, k, v
+    return u;
+}
+inline size_t batch_gemm_scratch_floats(int n_vocab) { return batch_gemm_units(n_vocab) * 64 * 128; }
+inline size_t batch_gemm_counters(int n_vocab) { return batch_gemm_units(n_vocab); }
 // Batched decode (n_seq independent sequences): one step of every sequence.
 struct BatchLaunch {
     int n_seq, max_seq, n_layer, n_vocab, lm_type, max_pos, chain, n_sm;
-    int tcgen05;              // GEMMs on k_b_gemm_tc instead of the mma.sync kernels
+    int tcgen05;              // GEMMs on k_b_gemm_tc (batched block order) instead of the mma.sync
+                              // kernels (the batch-1 decode's eight-lane order)
+    float* gemm_part;         // k_b_gemm_tc scratch: batch_gemm_scratch_floats(n_vocab) floats
+    unsigned* gemm_cnt;       // k_b_gemm_tc tile counters: batch_gemm_counters(n_vocab) zeroed words
     int shared_kv;            // every row is a position of ONE sequence: one cache [n_layer][max_seq][KV_DIM]
                               // (batched prefill: row i attends to positions 0 .. pos[i], causal)
     int skip_lm;              // no LM head / argmax (prefill chunks before the last)

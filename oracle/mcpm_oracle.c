@@ -203,6 +203,21 @@ static float dot_q4k_row(const blk_q4_K* w, const blk_q8_K* a, int nb, int order
         }
         return result;
     }
+    if (order == ORC_ORDER_BATCH) {   /* groups of 4 blocks, one fma per block (k_b_gemm_tc) */
+        float row = 0.0f;
+        for (int g0 = 0; g0 < nb; g0 += 4) {
+            float acc = 0.0f, accm = 0.0f;
+            for (int b = g0; b < g0 + 4 && b < nb; ++b) {
+                int32_t isum, minsum;
+                orc_q4k_block_sums(w + b, a + b, &isum, &minsum);
+                acc = fmaf(a[b].d * orc_fp16_to_fp32(w[b].d), (float)isum, acc);
+                accm = fmaf(-(a[b].d * orc_fp16_to_fp32(w[b].dmin)), (float)minsum, accm);
+            }
+            const float g = acc + accm;
+            row = g0 == 0 ? g : row + g;
+        }
+        return row;
+    }
     /* AVX2 order (ops_avx2.cpp:153-196): lane k holds bytes 4k..4k+3 of each 32-byte qs group. */
     float acc[8] = {0};
     float acc_min = 0.0f;
@@ -242,6 +257,19 @@ static float dot_q6k_row(const blk_q6_K* w, const blk_q8_K* a, int nb, int order
             result += d * (float)(isum - off);
         }
         return result;
+    }
+    if (order == ORC_ORDER_BATCH) {   /* groups of 4 blocks, one fma per block (k_b_gemm_tc) */
+        float row = 0.0f;
+        for (int g0 = 0; g0 < nb; g0 += 4) {
+            float acc = 0.0f;
+            for (int b = g0; b < g0 + 4 && b < nb; ++b) {
+                int32_t isum, off;
+                orc_q6k_block_sums(w + b, a + b, &isum, &off);
+                acc = fmaf(a[b].d * orc_fp16_to_fp32(w[b].d), (float)(isum - off), acc);
+            }
+            row = g0 == 0 ? acc : row + acc;
+        }
+        return row;
     }
     /* AVX2 order (ops_avx2.cpp:201-276): lane k holds l in [4k, 4k+4) of every quarter. */
     float acc[8] = {0};
@@ -557,12 +585,16 @@ struct orc_state {
     float *x, *xn, *q, *k, *v, *att, *o, *gate, *up, *h, *ffo, *logits;
     float **kc, **vc;
     blk_q8_K *xq, *hq;
+    int order;   /* ORC_ORDER_AVX2 or ORC_ORDER_BATCH for the K-quant projections */
 };
+
+void orc_set_order(orc_state* s, int order) { s->order = order; }
 
 orc_state* orc_create(const orc_model_desc* d, int max_seq) {
     orc_state* s = (orc_state*)calloc(1, sizeof(orc_state));
     s->d = *d;
     s->max_seq = max_seq;
+    s->order = ORC_ORDER_AVX2;
     const int E = d->n_embd, F = d->n_ff, kvd = d->n_head_kv * (E / d->n_head);
     s->x = calloc(E, 4); s->xn = calloc(E, 4); s->q = calloc(E, 4);
     s->k = calloc(kvd, 4); s->v = calloc(kvd, 4); s->att = calloc(E, 4); s->o = calloc(E, 4);
@@ -594,9 +626,9 @@ static void project(const orc_state* s, uint64_t off, int type, int rows, int co
                     const void* xq, const float* xf, float* y) {
     const uint8_t* w = s->d.base + off;
     if (type == ORC_Q4_K)
-        orc_gemv_q4k_q8k(w, xq, y, rows, cols, ORC_ORDER_AVX2, 1);
+        orc_gemv_q4k_q8k(w, xq, y, rows, cols, s->order, 1);
     else if (type == ORC_Q6_K)
-        orc_gemv_q6k_q8k(w, xq, y, rows, cols, ORC_ORDER_AVX2);
+        orc_gemv_q6k_q8k(w, xq, y, rows, cols, s->order);
     else
         orc_gemv_q8_0(w, xf, y, rows, cols);
 }

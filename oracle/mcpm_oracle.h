@@ -16,7 +16,7 @@ extern "C" {
 #define ORC_QK8_0 32
 enum { ORC_F32 = 0, ORC_Q8_0 = 8, ORC_Q4_K = 12, ORC_Q6_K = 14 };
 enum { ORC_ROUND_EVEN = 0, ORC_ROUND_AWAY = 1 };
-enum { ORC_ORDER_SCALAR = 0, ORC_ORDER_AVX2 = 1 };
+enum { ORC_ORDER_SCALAR = 0, ORC_ORDER_AVX2 = 1, ORC_ORDER_BATCH = 2 };
 
 float orc_fp16_to_fp32(uint16_t h);
 void orc_q4k_scales_mins(const uint8_t q[12], uint8_t sc[8], uint8_t mn[8]);
@@ -35,8 +35,12 @@ void orc_blocksums(int type, const void* w, const void* xq, int rows, int cols, 
 
 /* GEMV over a pre-quantised Q8_K activation.  order selects the fp32 accumulation order:
  * ORC_ORDER_SCALAR follows dot_row_q*_K_q8_K_scalar, ORC_ORDER_AVX2 the eight-lane
- * accumulators + horizontal sum of dot_row_q*_K_q8_K_avx2.  fused_min: contract the
- * Q4_K min term into one fused multiply-subtract. */
+ * accumulators + horizontal sum of dot_row_q*_K_q8_K_avx2 (the batch-1 decode kernel),
+ * ORC_ORDER_BATCH the tcgen05 batched GEMM's order: the exact block sum isum (Q6_K: minus its
+ * -32 offset) scaled by one fma per block, acc = fma(xd*d, isum, acc) and (Q4_K)
+ * accm = fma(-(xd*dmin), minsum, accm) over groups of 4 consecutive blocks, g = acc + accm per
+ * group, row = ((g0 + g1) + g2) + ... .  fused_min: contract the Q4_K min term into one fused
+ * multiply-subtract (AVX2 order). */
 void orc_gemv_q4k_q8k(const void* w, const void* xq, float* y, int rows, int cols, int order, int fused_min);
 void orc_gemv_q6k_q8k(const void* w, const void* xq, float* y, int rows, int cols, int order);
 /* gemv_q8_0 (src/ops/ops.cpp:58-79): fp32 activations, per-32 sum then * fp16(d). */
@@ -83,6 +87,9 @@ orc_state* orc_create(const orc_model_desc* d, int max_seq);
 void orc_destroy(orc_state* s);
 /* Returns the greedy argmax (lowest index on ties), or -1 if pos >= max_seq. logits may be NULL. */
 int orc_forward(orc_state* s, int token, int pos, float* logits);
+/* GEMV order of the K-quant projections in later orc_forward calls (ORC_ORDER_AVX2, the
+ * default: batch-1 decode; ORC_ORDER_BATCH: batched decode and prefill on tcgen05). */
+void orc_set_order(orc_state* s, int order);
 /* Copies of internal state for debugging parity: the fp32 residual x after the last call. */
 void orc_get_x(const orc_state* s, float* x);
 void orc_get_kv(const orc_state* s, int layer, float* k, float* v, int n_pos);

@@ -184,7 +184,7 @@ class Oracle:
     """This project's plain-C restatement."""
 
     ROUND_EVEN, ROUND_AWAY = 0, 1
-    ORDER_SCALAR, ORDER_AVX2 = 0, 1
+    ORDER_SCALAR, ORDER_AVX2, ORDER_BATCH = 0, 1, 2
 
     def __init__(self, path: str = ORACLE_SO):
         if not os.path.exists(path):
@@ -212,6 +212,8 @@ class Oracle:
         L.orc_get_x.argtypes = [P, F]
         L.orc_get_kv.argtypes = [P, C.c_int, F, F, C.c_int]
         L.orc_set_kv.argtypes = [P, C.c_int, F, F, C.c_int]
+        L.orc_set_order.restype = None
+        L.orc_set_order.argtypes = [P, C.c_int]
         L.orc_sample_top_p.restype = C.c_int
         L.orc_sample_top_p.argtypes = [F, C.c_int, C.c_float, C.c_float, C.c_float, C.POINTER(C.c_int)]
 
@@ -324,6 +326,11 @@ class OracleModel:
         out = np.zeros(spec.N_EMBD, np.float32)
         self.o.lib.orc_get_x(self.h, _fptr(out))
         return out
+
+    def set_order(self, order: int) -> None:
+        """GEMV order of later forward calls: Oracle.ORDER_AVX2 (batch-1 decode, the default) or
+        Oracle.ORDER_BATCH (the tcgen05 batched GEMM: batched decode and prefill)."""
+        self.o.lib.orc_set_order(self.h, order)
 
     def set_kv(self, layer: int, k: np.ndarray, v: np.ndarray) -> None:
         k = np.ascontiguousarray(k, dtype=np.float32)

@@ -1,7 +1,8 @@
 """Batched decode (n_seq independent sequences in lockstep) on the GPU against the C
-restatement, one restatement model per sequence: every sequence's logits and greedy token
-must equal a batch-1 decode of that sequence bit for bit (the batched GEMM keeps the
-reference's eight AVX2 lane partials per block, so no order changes)."""
+restatement, one restatement model per sequence, bit for bit.  The mma.sync GEMMs keep the
+batch-1 decode's eight AVX2 lane partials per block (restatement order AVX2: every sequence
+equals a batch-1 decode of it); the tcgen05 GEMM scales exact block sums with one fma per
+block (restatement order BATCH)."""
 import numpy as np
 import pytest
 
@@ -21,6 +22,8 @@ def test_batch_decode_bitexact(cuda, oracle, model_path, n_seq, n_prompt, n_gen,
     e.batch_init(n_seq, max_seq)
     seqs = list(range(n_seq)) if check is None else list(check)
     oms = {s: O.OracleModel(oracle, model_path, max_seq) for s in seqs}
+    for om in oms.values():   # tcgen05: the batched path's own fp32 order over exact block sums
+        om.set_order(O.Oracle.ORDER_BATCH if gemm == 1 else O.Oracle.ORDER_AVX2)
     rng = np.random.default_rng(n_seq)
     prompts = rng.integers(0, e.n_vocab, (n_seq, n_prompt)).astype(np.int32)
     ref = np.zeros(e.n_vocab, np.float32)
@@ -57,6 +60,8 @@ def test_batch_decode_f16_kv_bitexact(cuda, oracle, model_path, gemm):
     e.batch_init(n_seq, max_seq)
     seqs = (0, 4, 8)
     oms = {s: O.OracleModel(oracle, model_path, max_seq, kv_f16=True) for s in seqs}
+    for om in oms.values():
+        om.set_order(O.Oracle.ORDER_BATCH if gemm == 1 else O.Oracle.ORDER_AVX2)
     prompts = np.random.default_rng(3).integers(0, e.n_vocab, (n_seq, 3)).astype(np.int32)
     ref = np.zeros(e.n_vocab, np.float32)
     toks = None

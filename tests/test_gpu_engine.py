@@ -408,3 +408,37 @@ def test_schedule_options_bitexact(cuda, model_path, pos0):
     finally:
         for e in engs:
             e.close()
+
+
+@pytest.mark.parametrize("n_prompt", [6, 70])
+def test_prefill_tcgen05_vs_restatement(cuda, oracle, model_path, n_prompt):
+    """Prefill on the tcgen05 batched GEMM (block-order fp32 over exact block sums) against the
+    restatement stepping the same positions in its BATCH order: last logits, greedy token and
+    K/V rows bit for bit; the decode that follows (batch-1 kernel) continues in the AVX2 order."""
+    import oracle as O
+    from mcpm import engine as E, synth
+    prompt = [int(t) for t in synth.prompt_ids(n_prompt, seed=41)]
+    max_seq = n_prompt + 8
+    e = E.MiniCPM5Engine(device=0, max_seq=max_seq, batch_gemm=1)
+    om = O.OracleModel(oracle, model_path, max_seq)
+    try:
+        assert e.load_model(model_path)
+        tok, lg = e.prefill(prompt, 0)
+        om.set_order(O.Oracle.ORDER_BATCH)
+        ref = np.zeros(e.n_vocab, np.float32)
+        for pos, t in enumerate(prompt):
+            want = om.forward(t, pos, ref)
+        diff = np.sum(lg.view(np.uint32) != ref.view(np.uint32))
+        assert diff == 0, f"{diff} logits differ, max {np.max(np.abs(lg - ref))}"
+        assert tok == want
+        om.set_order(O.Oracle.ORDER_AVX2)
+        pos = n_prompt
+        for _ in range(3):
+            got = e.forward_greedy(tok, pos)
+            want = om.forward(tok, pos, ref)
+            assert got == want
+            assert np.array_equal(e.read_x().view(np.uint32), om.x().view(np.uint32))
+            tok, pos = got, pos + 1
+    finally:
+        e.close()
+        om.close()

@@ -83,3 +83,22 @@ def test_restatement_fixture_vs_reference_all_positions(parity):
     assert np.abs(r["top_val"] - g["top_val"]).mean() <= 1.25 * max(v["mean_abs_top32_4_vs_1"])
     # as good as the reference against itself: at least as many argmax agreements
     assert int(np.sum(r["argmax"] == g["tokens"])) >= min(v["argmax_agree_4_vs_1"]) - 4
+
+
+def test_batch_order_restatement_vs_reference_on_parity_model(parity, parity_model_path, oracle):
+    """The batched path's fp32 order (exact block sums, one fma per block, groups of four
+    blocks: the tcgen05 batched GEMM and prefill) against the reference build: the reference's
+    argmax at every decidable position and logits within its own thread-count spread."""
+    g, v, _ = parity
+    m = O.OracleModel(oracle, parity_model_path, N_CHECK + 1)
+    m.set_order(O.Oracle.ORDER_BATCH)
+    lg = np.zeros(130560, np.float32)
+    am, top = [], []
+    for pos in range(N_CHECK):
+        am.append(m.forward(int(g["prompt"][pos]), pos, lg))
+        top.append(lg[g["top_idx"][pos]].copy())
+    am, top = np.array(am), np.array(top)
+    dec = np.array(v["decidable"][:N_CHECK])
+    assert np.array_equal(am[dec], g["tokens"][:N_CHECK][dec])
+    assert np.abs(top - g["top_val"][:N_CHECK]).mean() <= 1.25 * max(v["mean_abs_top32_4_vs_1"])
+    m.close()
