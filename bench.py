@@ -48,8 +48,8 @@ def parse():
     ap.add_argument("--comm", default="p2p", choices=["p2p", "nccl"], help="config 4: exchange of partial sums")
     ap.add_argument("--seqs", type=int, default=64, help="config 3: sequences in total (64 = the config; fewer for a "
                     "smaller case, e.g. one data-parallel rank's share on one GPU)")
-    ap.add_argument("--batch-gemm", default="mma", choices=["mma", "tcgen05"],
-                    help="config 3: batched GEMM kernel (int8 mma.sync or tcgen05; identical results)")
+    ap.add_argument("--batch-gemm", default="tcgen05", choices=["mma", "tcgen05"],
+                    help="config 3: batched GEMM kernel (tcgen05, the default, or int8 mma.sync in the batch-1 order)")
     ap.add_argument("--kv-type", default="f32", choices=["f32", "f16"],
                     help="configs 0 and 2: KV-cache element type (f32 = the reference's cache; f16 halves its bytes)")
     return ap.parse_args()
@@ -345,7 +345,8 @@ def run_batch(args, rank, world, local):
     if pg:
         pg.barrier()
     max_seq = n_prompt + args.warmup + args.steps + 80
-    eng = E.MiniCPM5Engine(device=local, max_seq=64, batch_gemm=1 if args.batch_gemm == "tcgen05" else 0)
+    eng = E.MiniCPM5Engine(device=local, max_seq=64,
+                           batch_gemm=E.GEMM_TCGEN05 if args.batch_gemm == "tcgen05" else E.GEMM_MMA)
     if not eng.load_model(path):
         raise SystemExit("load_model failed")
     eng.batch_init(n, max_seq)

@@ -38,14 +38,16 @@ const char* mcpm_status_string(mcpm_status s);
 /* ------------------------------------------------------------------ engine */
 typedef struct mcpm_engine mcpm_engine;
 
-enum { MCPM_GEMM_MMA = 0, MCPM_GEMM_TCGEN05 = 1 };
+enum { MCPM_GEMM_TCGEN05 = 0, MCPM_GEMM_MMA = 1 };
 typedef struct {
     int device;      /* CUDA device ordinal */
     int max_seq;     /* KV-cache positions (reference init_kv_cache(max_seq_len), model.cpp:17-24); <= 16384 */
     int n_ctas;      /* persistent CTAs of the decode kernel; 0 = one per SM */
-    int batch_gemm;  /* batched-decode GEMM (mcpm_batch_*): MCPM_GEMM_MMA (0, int8 mma.sync, the faster
-                        today) or MCPM_GEMM_TCGEN05 (1, 5th-generation tensor cores, TMEM accumulators);
-                        both give bit-identical results */
+    int batch_gemm;  /* GEMM of batched decode (mcpm_batch_*) and prompt prefill (mcpm_prefill):
+                        MCPM_GEMM_TCGEN05 (0, the default and the faster: 5th-generation tensor cores,
+                        exact block sums, fp32 scaled with one fma per block in groups of four blocks;
+                        within a few ulps of the batch-1 decode) or MCPM_GEMM_MMA (1, int8 mma.sync
+                        keeping the batch-1 decode's eight-lane order: bit-identical to mcpm_forward) */
     int sched;       /* decode schedule options, for measurement: MCPM_SCHED_L2_PREFETCH (1) prefetches each
                         layer's weight rows into L2 one layer ahead; MCPM_SCHED_ATT_COMBINERS (2) combines
                         the attention chunks on 8 head-pair CTAs at every context length (by default only

@@ -40,8 +40,9 @@ struct BGemmArgs {
     float* y;
     int y_stride, n_seq;
     unsigned* err;   // k_b_gemm_tc: ERR_TIMEOUT when an MMA completion never arrives
-    float* part;     // k_b_gemm_tc: group partials (tb_scratch_floats(ntiles, nb / 4))
+    float* part;     // k_b_gemm_tc: group partials, [tile][group][64][128] fp32
     unsigned* cnt;   // k_b_gemm_tc: one counter per row tile, zero between launches
+    unsigned long long* trace;   // k_b_gemm_tc, optional: globaltimer marks of CTA 0's first unit
 };
 
 // k_b_gemm8 (8 blocks per row: QKV, o_proj, gate/up, LM head): the activations of every

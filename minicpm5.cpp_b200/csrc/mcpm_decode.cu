@@ -1556,8 +1556,10 @@ cudaError_t launch_batch_step(const BatchLaunch& b, cudaStream_t stream) {
     const int nmax = b.max_pos + 1, Pmax = 32 * ((nmax + 2047) / 2048), Cmax = (nmax + Pmax - 1) / Pmax;
     const int unit_smem = Pmax == 32 ? 24576 : UNIT_SMEM_BIG;
     const bool gemm_kind = b.tcgen05 != 0;
-    auto gemm = [&](std::initializer_list<BGemmSeg> segs, int nb, float* y, int y_stride) {
+    auto gemm = [&](std::initializer_list<BGemmSeg> segs, int nb, float* y, int y_stride,
+                    unsigned long long* trace = nullptr) {
         BGemmArgs g{};
+        g.trace = trace;
         const int rows_per_tile = gemm_kind ? TB_M : BG_ROWS;
         int tiles = 0, i = 0;
         for (BGemmSeg sg : segs) {
@@ -1570,7 +1572,7 @@ cudaError_t launch_batch_step(const BatchLaunch& b, cudaStream_t stream) {
         if (gemm_kind) {
             g.part = b.gemm_part, g.cnt = b.gemm_cnt;
             const int units = tiles * (nb / TB_G);
-            k_b_gemm_tc<<<std::min(units, b.n_sm), TB_THREADS, TB_BYTES, stream>>>(g);
+            k_b_gemm_tc<<<std::min(units, b.n_sm), TB_CTA_THREADS, TB_BYTES, stream>>>(g);
             return;
         }
         if (nb == 8)
@@ -1595,7 +1597,8 @@ cudaError_t launch_batch_step(const BatchLaunch& b, cudaStream_t stream) {
         gemm({{L.wo, L.to, N_EMBD, 0, 0}}, N_EMBD / 256, b.y, 2 * N_FF);
         a.norm = L.ffn_norm;
         k_b_res_norm<true><<<n, 256, 0, stream>>>(a);
-        gemm({{L.wg, L.tg, N_FF, 0, 0}, {L.wu, L.tu, N_FF, N_FF, 0}}, N_EMBD / 256, b.y, 2 * N_FF);
+        gemm({{L.wg, L.tg, N_FF, 0, 0}, {L.wu, L.tu, N_FF, N_FF, 0}}, N_EMBD / 256, b.y, 2 * N_FF,
+             l == 1 && b.trace ? b.trace + TRACE_GEMM : nullptr);
         k_b_swiglu<<<dim3(n, N_FF / 256 / 8), 256, 0, stream>>>(a);
         gemm({{L.wd, L.td, N_EMBD, 0, 0}}, N_FF / 256, b.y, 2 * N_FF);
         if (l + 1 < b.n_layer) {

@@ -860,7 +860,7 @@ mcpm_status mcpm_batch_step_async(mcpm_engine* e, const int* tokens, const int* 
     b.n_seq = n, b.max_seq = e->b_max_seq, b.n_layer = e->n_layer, b.n_vocab = e->n_vocab, b.lm_type = e->lm_type;
     b.max_pos = max_pos, b.chain = 1, b.n_sm = e->n_sm, b.tcgen05 = e->batch_gemm == MCPM_GEMM_TCGEN05;
     b.kv_f16 = e->kv_f16;
-    b.gemm_part = e->g_part, b.gemm_cnt = e->g_cnt;
+    b.gemm_part = e->g_part, b.gemm_cnt = e->g_cnt, b.trace = e->trace;
     b.layers = e->layers.data(), b.embd = e->embd, b.out_norm = e->out_norm, b.lm = e->lm, b.rope = e->b_rope;
     b.kc = e->b_kc, b.vc = e->b_vc, b.x = e->b_x, b.y = e->b_y, b.q = e->b_q, b.att_part = e->b_part;
     b.att = e->b_att, b.logits = e->b_logits, b.aqs = e->b_aqs, b.ad = e->b_ad, b.abs = e->b_abs;

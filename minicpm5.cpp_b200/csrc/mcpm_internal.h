@@ -34,6 +34,7 @@ constexpr int TRACE_CTA = 720;            // layer-1 barrier k, CTA c: arrival 7
                                           // QKV sub-steps m = 0..2 of layer 1 at 2400 + 148m + c
 constexpr int TRACE_GEMV = 2848;          // layer-1 GEMV marks of CTA 0 (pass 1, pass 2, entry): O, D, gate, QKV
 constexpr int TRACE_POLL = 2960;          // per CTA: residual poll done, gate/up norm of layer 1 (+0), QKV norm of layer 2 (+148)
+constexpr int TRACE_GEMM = 3260;          // batched tcgen05 GEMM of layer 1's gate/up: CTA 0's first unit (28 marks)
 
 // QKV row pairs [0, 1280) (Q pairs, then K, then V) are split over the CTAs in proportion
 // to their GEMV cost: a Q6_K row costs about 1.6 Q4_K rows (unaligned 210-byte blocks), so
@@ -134,6 +135,7 @@ struct BatchLaunch {
                               // kernels (the batch-1 decode's eight-lane order)
     float* gemm_part;         // k_b_gemm_tc scratch: batch_gemm_scratch_floats(n_vocab) floats
     unsigned* gemm_cnt;       // k_b_gemm_tc tile counters: batch_gemm_counters(n_vocab) zeroed words
+    unsigned long long* trace;   // optional: TRACE_GEMM marks of one GEMM launch
     int shared_kv;            // every row is a position of ONE sequence: one cache [n_layer][max_seq][KV_DIM]
                               // (batched prefill: row i attends to positions 0 .. pos[i], causal)
     int skip_lm;              // no LM head / argmax (prefill chunks before the last)

@@ -38,6 +38,7 @@ class mcpm_config(C.Structure):
 
 
 KV_F32, KV_F16 = 0, 1
+GEMM_TCGEN05, GEMM_MMA = 0, 1
 
 
 P, I, F = C.c_void_p, C.c_int, C.c_float
@@ -143,7 +144,8 @@ class MiniCPM5Engine:
 
     def __init__(self, device: int = 0, max_seq: int = 0, n_ctas: int = 0, batch_gemm: int = 0, sched: int = 0,
                  kv_type: int = KV_F32):
-        """batch_gemm: 0 = int8 mma.sync batched GEMMs, 1 = tcgen05 (bit-identical results).
+        """batch_gemm (batched decode and prefill): GEMM_TCGEN05 (default; block-order fp32 over exact block
+        sums) or GEMM_MMA (int8 mma.sync in the batch-1 decode's order: bit-identical to forward()).
         sched: decode schedule option bits (include/mcpm.h MCPM_SCHED_*; results are the same).
         kv_type: KV_F32 (the reference's fp32 cache) or KV_F16 (rows rounded to fp16 when written)."""
         self.lib = load_library()

@@ -9,7 +9,7 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("gemm", [0, 1], ids=["mma", "tcgen05"])
+@pytest.mark.parametrize("gemm", [1, 0], ids=["mma", "tcgen05"])
 @pytest.mark.parametrize("n_seq,n_prompt,n_gen,check", [(5, 6, 4, None), (64, 2, 1, (0, 9, 31, 40, 63)),
                                                         (37, 2, 1, (0, 31, 32, 36)), (20, 2, 1, (0, 7, 8, 19)),
                                                         (12, 2, 1, (0, 8, 11))])
@@ -23,7 +23,7 @@ def test_batch_decode_bitexact(cuda, oracle, model_path, n_seq, n_prompt, n_gen,
     seqs = list(range(n_seq)) if check is None else list(check)
     oms = {s: O.OracleModel(oracle, model_path, max_seq) for s in seqs}
     for om in oms.values():   # tcgen05: the batched path's own fp32 order over exact block sums
-        om.set_order(O.Oracle.ORDER_BATCH if gemm == 1 else O.Oracle.ORDER_AVX2)
+        om.set_order(O.Oracle.ORDER_BATCH if gemm == E.GEMM_TCGEN05 else O.Oracle.ORDER_AVX2)
     rng = np.random.default_rng(n_seq)
     prompts = rng.integers(0, e.n_vocab, (n_seq, n_prompt)).astype(np.int32)
     ref = np.zeros(e.n_vocab, np.float32)
@@ -48,7 +48,7 @@ def test_batch_decode_bitexact(cuda, oracle, model_path, n_seq, n_prompt, n_gen,
             om.close()
 
 
-@pytest.mark.parametrize("gemm", [0, 1], ids=["mma", "tcgen05"])
+@pytest.mark.parametrize("gemm", [1, 0], ids=["mma", "tcgen05"])
 def test_batch_decode_f16_kv_bitexact(cuda, oracle, model_path, gemm):
     """Batched decode over fp16 cache rows (kv_type MCPM_KV_F16) against the restatement with
     the same option."""
@@ -61,7 +61,7 @@ def test_batch_decode_f16_kv_bitexact(cuda, oracle, model_path, gemm):
     seqs = (0, 4, 8)
     oms = {s: O.OracleModel(oracle, model_path, max_seq, kv_f16=True) for s in seqs}
     for om in oms.values():
-        om.set_order(O.Oracle.ORDER_BATCH if gemm == 1 else O.Oracle.ORDER_AVX2)
+        om.set_order(O.Oracle.ORDER_BATCH if gemm == E.GEMM_TCGEN05 else O.Oracle.ORDER_AVX2)
     prompts = np.random.default_rng(3).integers(0, e.n_vocab, (n_seq, 3)).astype(np.int32)
     ref = np.zeros(e.n_vocab, np.float32)
     toks = None

@@ -193,12 +193,14 @@ def test_cpp_sampler_loop_device_logits(cuda, oracle, model_path, tmp_path):
 @pytest.mark.parametrize("n_prompt,pos0", [(5, 0), (64, 0), (150, 0), (70, 9)])
 def test_batched_prefill_equals_token_by_token(cuda, model_path, n_prompt, pos0):
     """mcpm_prefill (the prompt as batched steps of up to 64 positions sharing the engine's KV
-    cache) against one mcpm_forward per position: the last position's logits, every K/V row
-    written and the greedy continuation are bit-identical."""
+    cache) on the mma.sync GEMMs (the batch-1 decode's order) against one mcpm_forward per
+    position: the last position's logits, every K/V row written and the greedy continuation are
+    bit-identical.  (The default tcgen05 prefill is pinned to the restatement's BATCH order in
+    test_prefill_tcgen05_vs_restatement.)"""
     from mcpm import engine as E, synth
     prompt = [int(t) for t in synth.prompt_ids(pos0 + n_prompt, seed=77)]
     max_seq = pos0 + n_prompt + 8
-    a = E.MiniCPM5Engine(device=0, max_seq=max_seq)
+    a = E.MiniCPM5Engine(device=0, max_seq=max_seq, batch_gemm=E.GEMM_MMA)   # the batch-1 order
     b = E.MiniCPM5Engine(device=0, max_seq=max_seq)
     try:
         assert a.load_model(model_path) and b.load_model(model_path)
@@ -273,9 +275,10 @@ def test_kv_snapshot_restore_session(cuda, model_path):
 
 
 # ------------------------------------------------------------------ fp16 KV cache option
-def _f16_engine(model_path, max_seq):
+def _f16_engine(model_path, max_seq, batch_gemm=None):
     from mcpm import engine as E
-    e = E.MiniCPM5Engine(device=0, max_seq=max_seq, kv_type=E.KV_F16)
+    e = E.MiniCPM5Engine(device=0, max_seq=max_seq, kv_type=E.KV_F16,
+                         batch_gemm=E.GEMM_MMA if batch_gemm is None else batch_gemm)
     assert e.load_model(model_path)
     return e
 
@@ -419,7 +422,7 @@ def test_prefill_tcgen05_vs_restatement(cuda, oracle, model_path, n_prompt):
     from mcpm import engine as E, synth
     prompt = [int(t) for t in synth.prompt_ids(n_prompt, seed=41)]
     max_seq = n_prompt + 8
-    e = E.MiniCPM5Engine(device=0, max_seq=max_seq, batch_gemm=1)
+    e = E.MiniCPM5Engine(device=0, max_seq=max_seq, batch_gemm=E.GEMM_TCGEN05)
     om = O.OracleModel(oracle, model_path, max_seq)
     try:
         assert e.load_model(model_path)
