@@ -50,6 +50,8 @@ def parse():
                     "smaller case, e.g. one data-parallel rank's share on one GPU)")
     ap.add_argument("--batch-gemm", default="tcgen05", choices=["mma", "tcgen05"],
                     help="config 3: batched GEMM kernel (tcgen05, the default, or int8 mma.sync in the batch-1 order)")
+    ap.add_argument("--case", default=None,
+                    help="config 1: only the cases whose 'name type' contains this text, e.g. 'gate+up 12288x2048 Q4_K'")
     ap.add_argument("--kv-type", default="f32", choices=["f32", "f16"],
                     help="configs 0 and 2: KV-cache element type (f32 = the reference's cache; f16 halves its bytes)")
     return ap.parse_args()
@@ -252,9 +254,11 @@ def run_gemv_sweep(args):
     import oracle as O
     torch.cuda.set_device(0)
     peak, peak_kind = measured_peaks()
-    ref = O.Ref() if O.have_ref() else None
+    ref = O.Ref() if (O.have_ref() and not args.no_cpu_baseline) else None
     orc = O.Oracle()
     for name, t, rows, cols in GEMV_CASES:
+        if args.case and args.case not in f"{name} {TYPE_NAME[t]}":
+            continue
         w = synth.tensor_bytes(spec.TensorInfo("w", t, (cols, rows)), np.random.Generator(np.random.PCG64([rows, cols, t])))
         nbytes = w.size
         copies = max(1, -(-(256 << 20) // nbytes))

@@ -1383,7 +1383,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
     if (threadIdx.x == 0) {
         int ob = 0;
         for (int l = 0; l < p.n_layer; ++l) ob = max(ob, row_bytes(s.meta()[l].to, N_EMBD));
-        s.flags()[0] = p.pos + 1 <= 2048 && (s.rows()->od1 - s.rows()->od0) * ob <= ATT_B1_OFF;
+        s.flags()[0] = !(p.sched & SCHED_LATE_GU) && p.pos + 1 <= 2048 && (s.rows()->od1 - s.rows()->od0) * ob <= ATT_B1_OFF;
     }
     __syncthreads();
     for (int l = 0; l < p.n_layer; ++l) {

@@ -390,7 +390,7 @@ def test_schedule_options_bitexact(cuda, model_path, pos0):
     never the arithmetic: logits are bit-identical to the default schedule.  pos0 = 290 runs 10
     attention chunks, combined by every CTA by default and by the combiners with option 2."""
     from mcpm import engine as E, spec, synth
-    scheds = (0, 1, 2, 3)
+    scheds = (0, 1, 2, 3, 4, 6)
     max_seq = pos0 + 40
     engs = [E.MiniCPM5Engine(device=0, max_seq=max_seq, sched=s) for s in scheds]
     try:
