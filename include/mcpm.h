@@ -51,15 +51,15 @@ typedef struct {
     int sched;       /* decode schedule options, for measurement: MCPM_SCHED_L2_PREFETCH (1) prefetches each
                         layer's weight rows into L2 one layer ahead; MCPM_SCHED_ATT_COMBINERS (2) combines
                         the attention chunks on 8 head-pair CTAs at every context length (by default only
-                        above 16 chunks; below, every CTA combines all heads); MCPM_SCHED_LATE_GU (4) copies
-                        the gate/up rows after attention instead of during it; every option gives the
+                        above 16 chunks; below, every CTA combines all heads); MCPM_SCHED_EARLY_GU (4) copies
+                        the gate/up rows during attention instead of after it; every option gives the
                         same results */
     int kv_type;     /* KV-cache element type: MCPM_KV_F32 (0, the reference's std::vector<float> cache,
                         model.h:66-67) or MCPM_KV_F16 (1: K and V rounded to fp16 when written, half the
                         cache bytes; the attention reads them back exactly and computes in fp32) */
     int reserved[2];
 } mcpm_config;
-enum { MCPM_SCHED_L2_PREFETCH = 1, MCPM_SCHED_ATT_COMBINERS = 2, MCPM_SCHED_LATE_GU = 4 };
+enum { MCPM_SCHED_L2_PREFETCH = 1, MCPM_SCHED_ATT_COMBINERS = 2, MCPM_SCHED_EARLY_GU = 4 };
 enum { MCPM_KV_F32 = 0, MCPM_KV_F16 = 1 };
 
 /* Creates an engine bound to cfg->device (MiniCPM5Engine constructor + init_kv_cache). */

@@ -317,10 +317,11 @@ __device__ __noinline__ void prefetch_layer_l2(const DecodeParams& p, const Smem
 // Weight copies into shared memory are issued while a GEMV computes, never in front of a
 // handoff: on an SM whose TMA copy is in flight, the loads of a handoff (epoch polls, the
 // attention partials, h) queue behind the copy's bytes.  Phase w+1's copy goes into the
-// buffer of phase w-1 when phase w's weights have arrived; gate/up (buffer 0) goes right
-// after the QKV GEMV, which needs the attention scratch out of buffer 0: behind o_proj's rows
-// in buffer 1 (`early_gu`, contexts up to 2048 positions) -- longer contexts stage more K/V
-// rows and keep buffer 0, and their gate/up copy waits until attention is done.
+// buffer of phase w-1 when phase w's weights have arrived; gate/up (buffer 0) goes when
+// attention is done (its copy during attention delayed the q/K/V hand-off more than it
+// saved).  With SCHED_EARLY_GU it goes right after the QKV GEMV, which needs the attention
+// scratch out of buffer 0: behind o_proj's rows in buffer 1 (`early_gu`, contexts up to 2048
+// positions; longer contexts stage more K/V rows and keep buffer 0).
 constexpr int ATT_B1_OFF = 28672;   // attention scratch offset inside buffer 1
 static_assert(ATT_B1_OFF + (32 * HEAD_DIM + 8 * 32 + 32 + 8 * HEAD_DIM + HEAD_DIM) * 4 <= WBUF_BYTES,
               "32-position unit scratch behind o_proj's rows");
@@ -1378,12 +1379,12 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const DecodeParams p)
     trace_mark(p, 0);
     const LmPlan lmq = lm_plan(p, cta, ncta);
     const bool flagged = att_flagged(p);
-    // flags[0] (early_gu): the attention scratch fits behind this CTA's o_proj rows in buffer
-    // 1 (every layer), so gate/up can be copied into buffer 0 during attention.
+    // flags[0] (early_gu, SCHED_EARLY_GU): the attention scratch fits behind this CTA's o_proj
+    // rows in buffer 1 (every layer), so gate/up is copied into buffer 0 during attention.
     if (threadIdx.x == 0) {
         int ob = 0;
         for (int l = 0; l < p.n_layer; ++l) ob = max(ob, row_bytes(s.meta()[l].to, N_EMBD));
-        s.flags()[0] = !(p.sched & SCHED_LATE_GU) && p.pos + 1 <= 2048 && (s.rows()->od1 - s.rows()->od0) * ob <= ATT_B1_OFF;
+        s.flags()[0] = (p.sched & SCHED_EARLY_GU) && p.pos + 1 <= 2048 && (s.rows()->od1 - s.rows()->od0) * ob <= ATT_B1_OFF;
     }
     __syncthreads();
     for (int l = 0; l < p.n_layer; ++l) {

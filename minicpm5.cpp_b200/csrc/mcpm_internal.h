@@ -54,7 +54,8 @@ __host__ __device__ inline int qkv_pair_boundary(int tq, int tk, int tv, int c, 
 // Decode schedule options (DecodeParams::sched, mcpm_config::sched bits).
 constexpr int SCHED_L2_PREFETCH = 1;   // L2 prefetch of the next layer's weight rows (measured slower: off)
 constexpr int SCHED_ATT_COMBINERS = 2; // head-pair combiners at every context length (default: above 16 chunks)
-constexpr int SCHED_LATE_GU = 4;       // gate/up rows copied after attention, not during it
+constexpr int SCHED_EARLY_GU = 4;      // gate/up rows copied during attention (default: after it; measured
+                                       // slower, the copy delays the q/K/V hand-off)
 
 struct LayerDev {
     const uint8_t *wq, *wk, *wv, *wo, *wg, *wu, *wd;
