@@ -256,8 +256,9 @@ def run_gemv_sweep(args):
     peak, peak_kind = measured_peaks()
     ref = O.Ref() if (O.have_ref() and not args.no_cpu_baseline) else None
     orc = O.Oracle()
-    for name, t, rows, cols in GEMV_CASES:
-        if args.case and args.case not in f"{name} {TYPE_NAME[t]}":
+    cases = [(n, t, r, c, o) for n, t, r, c in GEMV_CASES for o in ((None,) if t == 8 else ("block", "avx2"))]
+    for name, t, rows, cols, order in cases:
+        if args.case and args.case not in f"{name} {TYPE_NAME[t]}" + (f" {order}" if order else ""):
             continue
         w = synth.tensor_bytes(spec.TensorInfo("w", t, (cols, rows)), np.random.Generator(np.random.PCG64([rows, cols, t])))
         nbytes = w.size
@@ -273,7 +274,9 @@ def run_gemv_sweep(args):
             ptr = wd.data_ptr() + (i % copies) * nbytes
             if t == 8:
                 E.gemv_q8_0(ptr, xd.data_ptr(), yd.data_ptr(), rows, cols, stream)
-            else:
+            elif order == "block":   # the decode kernel's order (engine default)
+                E.gemv_q8k_block(t, ptr, xqd.data_ptr(), yd.data_ptr(), rows, cols, stream)
+            else:                    # the reference's eight-lane AVX2 order
                 E.gemv_q8k(t, ptr, xqd.data_ptr(), yd.data_ptr(), rows, cols, stream)
         for i in range(max(3, args.warmup)):
             launch(i)
@@ -312,6 +315,7 @@ def run_gemv_sweep(args):
         print(json.dumps({
             "metric": "GEMV weight-stream GB/s (batch 1)", "config": {"workload": "config1", "case": name,
                                                                       "type": TYPE_NAME[t], "rows": rows, "cols": cols,
+                                                                      "order": order or "q8_0 (reference order)",
                                                                       "l2": f"{copies} weight copies rotated", "timing": "CUDA graph of repeated launches"},
             "value": round(gbs, 1), "unit": "GB/s", "us_per_launch": round(ms * 1e3, 2), "higher_is_better": True,
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",

@@ -43,11 +43,15 @@ typedef struct {
     int device;      /* CUDA device ordinal */
     int max_seq;     /* KV-cache positions (reference init_kv_cache(max_seq_len), model.cpp:17-24); <= 16384 */
     int n_ctas;      /* persistent CTAs of the decode kernel; 0 = one per SM */
-    int batch_gemm;  /* GEMM of batched decode (mcpm_batch_*) and prompt prefill (mcpm_prefill):
-                        MCPM_GEMM_TCGEN05 (0, the default and the faster: 5th-generation tensor cores,
-                        exact block sums, fp32 scaled with one fma per block in groups of four blocks;
-                        within a few ulps of the batch-1 decode) or MCPM_GEMM_MMA (1, int8 mma.sync
-                        keeping the batch-1 decode's eight-lane order: bit-identical to mcpm_forward) */
+    int batch_gemm;  /* the engine's GEMV order and batched GEMM, for decode (mcpm_forward), batched decode
+                        (mcpm_batch_*) and prompt prefill (mcpm_prefill): MCPM_GEMM_TCGEN05 (0, the
+                        default and the faster) computes every (row, super-block) integer sum exactly and
+                        scales it with one fp32 fma per block in groups of four blocks -- the decode
+                        kernel's GEMVs and the 5th-generation tensor-core GEMM of batched decode and
+                        prefill; MCPM_GEMM_MMA (1) keeps the reference's eight-lane AVX2 order
+                        (dot_row_q*_K_q8_K_avx2) -- the decode kernel's eight-lane GEMVs and int8
+                        mma.sync batched GEMMs.  Either way a prefilled prompt gives the same bits as
+                        one mcpm_forward per position, and the two orders differ by a few ulps per row */
     int sched;       /* decode schedule options, for measurement: MCPM_SCHED_L2_PREFETCH (1) prefetches each
                         layer's weight rows into L2 one layer ahead; MCPM_SCHED_ATT_COMBINERS (2) combines
                         the attention chunks on 8 head-pair CTAs at every context length (by default only
@@ -232,6 +236,14 @@ mcpm_status mcpm_quantize_q8k(const float* x, void* y, int n, int rounding, void
 /* y = W xq for Q4_K / Q6_K weights: gemv_q4_K_q8_K_avx2 / gemv_q6_K_q8_K_avx2
  * (ops_avx2.cpp:278-298) behind matmul_q8k (ops.cpp:317-349); bit-identical results. */
 mcpm_status mcpm_gemv_q8k(int type, const void* w, const void* xq, float* y, int rows, int cols, void* stream);
+/* The same product in the engine's default block order (no reference counterpart: the order of
+ * the decode kernel's GEMVs and of the tcgen05 batched GEMM when mcpm_config::batch_gemm is
+ * MCPM_GEMM_TCGEN05).  Each (row, super-block) integer sum is exact -- the integers of
+ * dot_row_q{4,6}_K_q8_K_scalar (ops_scalar_optimized.cpp:139-404) -- and is scaled by one fp32 fma
+ * per block, acc = fma(xd*d, isum, acc) and, for Q4_K, accm = fma(-(xd*dmin), minsum, accm), over
+ * groups of four consecutive blocks; a row is ((g0 + g1) + g2) + ... with g = acc + accm.
+ * cols == 2048 or 6144. */
+mcpm_status mcpm_gemv_q8k_block(int type, const void* w, const void* xq, float* y, int rows, int cols, void* stream);
 /* y = W x for Q8_0 weights and fp32 activations: gemv_q8_0 (ops.cpp:58-79) behind matmul
  * (ops.cpp:264-290); bit-identical to the reference build (its -ffast-math AVX2 evaluation
  * order: eight lanes per 32-block, pairwise lane reduction, one fma per block along the row).
@@ -276,11 +288,13 @@ mcpm_status mcpm_attention(const float* q, const float* k, const float* v, float
  * capture.  All calls on a device share the workspace: calls that overlap on the GPU race. */
 mcpm_status mcpm_attention_noalloc(const float* q, const float* k, const float* v, float* kcache, float* vcache,
                                    int pos, int max_seq, float* out, void* out_q8k, void* stream);
-/* GEMV throughput probe: `reps` launches of mcpm_gemv_q8k rotating over `n_copies`
- * weight copies laid out back to back from `w` (stride rows*row_bytes), so successive
- * launches miss in L2; writes the mean device time per launch in milliseconds. */
+/* GEMV throughput probe: `reps` launches of mcpm_gemv_q8k (order MCPM_ORDER_AVX2) or
+ * mcpm_gemv_q8k_block (MCPM_ORDER_BLOCK) rotating over `n_copies` weight copies laid out back to
+ * back from `w` (stride rows*row_bytes), so successive launches miss in L2; writes the mean device
+ * time per launch in milliseconds. */
+enum { MCPM_ORDER_AVX2 = 0, MCPM_ORDER_BLOCK = 1 };
 mcpm_status mcpm_gemv_q8k_timed(int type, const void* w, int n_copies, const void* xq, float* y, int rows, int cols,
-                                int reps, float* ms_per_launch, void* stream);
+                                int order, int reps, float* ms_per_launch, void* stream);
 
 #ifdef __cplusplus
 }

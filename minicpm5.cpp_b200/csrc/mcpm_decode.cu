@@ -17,6 +17,7 @@
 // streaming through the grid barriers.  All waits are bounded (~1 s) and report
 // ERR_TIMEOUT instead of hanging.
 #include "mcpm_device.cuh"
+#include "mcpm_gemv_bo.cuh"
 #include "mcpm_internal.h"
 #include <algorithm>
 #include <initializer_list>
@@ -250,6 +251,17 @@ __device__ __forceinline__ void trace_step(const DecodeParams& p, int l, int ph,
     if (l == 1) trace_mark(p, TRACE_DETAIL + 10 * ph + step);
     if (l == 1 && ph == 0 && step <= 3 && p.trace && threadIdx.x == 0 && blockIdx.x < 148)
         p.trace[2400 + 148 * (step - 1) + blockIdx.x] = globaltimer();
+}
+
+// GEMV of a decode phase over rows staged in this CTA's shared memory: rows [0, R0) at w0 and
+// [R0, R) at w1 (same type), in the engine's order -- the block order (exact block sums, one fma
+// per block in groups of four) or the reference's eight-lane AVX2 order.
+__device__ __forceinline__ void dec_gemv(const DecodeParams& p, const Smem& s, int type, const uint8_t* w0, int R0,
+                                         const uint8_t* w1, int R, int nb, float* out, unsigned long long* tr) {
+    if (p.blk_order)
+        gemv_bo2(type, w0, R0, w1, R, nb, *s.xq(), s.part(), SCRATCH_BYTES / 4, out);
+    else
+        gemv_rows2(type, w0, R0, w1, R, nb, *s.xq(), s.part(), MAX_TASKS, out, tr);
 }
 
 // Thread that issues weight copies and prefetches at the end of o_proj and down: outside
@@ -523,8 +535,8 @@ __device__ bool phase_qkv(const DecodeParams& p, const Smem& s, int l, int token
     for (int i = 0; i < 3; ++i) {
         if (pl.nrows[i] == 0) continue;   // uniform across the CTA
         const int base = lo[i] + pl.row0[i] - a;
-        gemv_rows(phase_type(L, 0, i), s.wbuf(0) + pl.off[i], pl.nrows[i], N_EMBD / 256, *s.xq(), s.part(), MAX_TASKS,
-                  rv + base, (p.trace && l == 1 && cta == 0 && i == 0) ? p.trace + TRACE_GEMV + 9 : nullptr);
+        dec_gemv(p, s, phase_type(L, 0, i), s.wbuf(0) + pl.off[i], pl.nrows[i], s.wbuf(0) + pl.off[i], pl.nrows[i],
+                 N_EMBD / 256, rv + base, (p.trace && l == 1 && cta == 0 && i == 0) ? p.trace + TRACE_GEMV + 9 : nullptr);
     }
     trace_step(p, l, 0, 3);
     __syncthreads();   // buffer 0 read by every GEMV above
@@ -706,6 +718,7 @@ __device__ void attention_unit32(const DecodeParams& p, float* scratch, int l, i
         d[e] = __fadd_rn(d[e], __shfl_xor_sync(0xffffffffu, d[e], 2));
         d[e] = __fadd_rn(d[e], __shfl_xor_sync(0xffffffffu, d[e], 1));
     }
+    trace_step(p, l, 1, 3);   // thread 0's K rows have arrived
     if (j == 0) {
         if (va) sc[(2 * G) * 32 + tA] = __fmul_rn(d[0], scale), sc[(2 * G + 1) * 32 + tA] = __fmul_rn(d[2], scale);
         if (vbv) sc[(2 * G) * 32 + tB] = __fmul_rn(d[1], scale), sc[(2 * G + 1) * 32 + tB] = __fmul_rn(d[3], scale);
@@ -1110,6 +1123,7 @@ __device__ void combine_attention(const DecodeParams& p, const Smem& s, int l, i
         v[cc] = cc < C ? ld_cg_f4(ph + cc * ATT_PART_STRIDE + ATT_PART_O + 4 * lane) : make_float4(0.f, 0.f, 0.f, 0.f);
     float M = lane < C ? ml.x : -__int_as_float(0x7f800000);
     for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    if (h == 0) trace_step(p, l, 2, 3);   // chunk headers loaded
     const float wv = lane < C ? canon_expf(__fsub_rn(ml.x, M)) : 0.0f;
     float Ls = 0.0f;
     float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -1167,8 +1181,8 @@ __device__ bool phase_o(const DecodeParams& p, const Smem& s, int l, int cta, in
     trace_step(p, l, 2, 1);
     if (!wait_weights(p, s, 4 * l + 1)) return false;
     trace_step(p, l, 2, 2);
-    gemv_rows(L.to, s.wbuf(1), n, N_EMBD / 256, *s.xq(), s.part(), MAX_TASKS, s.rowval(),
-              (p.trace && l == 1 && cta == 0) ? p.trace + TRACE_GEMV + 0 : nullptr);
+    dec_gemv(p, s, L.to, s.wbuf(1), n, s.wbuf(1), n, N_EMBD / 256, s.rowval(),
+             (p.trace && l == 1 && cta == 0) ? p.trace + TRACE_GEMV + 0 : nullptr);
     if (threadIdx.x < n) {
         const float xn = __fadd_rn(xr, s.rowval()[threadIdx.x]);
         p.x[r0 + threadIdx.x] = xn;
@@ -1195,13 +1209,12 @@ __device__ bool phase_gu(const DecodeParams& p, const Smem& s, int l, int cta, i
     float* rv = s.rowval();
     unsigned long long* tr = (p.trace && l == 1 && cta == 0) ? p.trace + TRACE_GEMV + 6 : nullptr;
     if (L.tg == L.tu) {   // gate rows then up rows in one pass: rv[0, n) gate, rv[n, 2n) up
-        gemv_rows2(L.tg, s.wbuf(0) + pl.off[0], n, s.wbuf(0) + pl.off[1], 2 * n, N_EMBD / 256, *s.xq(), s.part(),
-                   MAX_TASKS, rv, tr);
+        dec_gemv(p, s, L.tg, s.wbuf(0) + pl.off[0], n, s.wbuf(0) + pl.off[1], 2 * n, N_EMBD / 256, rv, tr);
         trace_step(p, l, 3, 3);
     } else {
-        gemv_rows(L.tg, s.wbuf(0) + pl.off[0], n, N_EMBD / 256, *s.xq(), s.part(), MAX_TASKS, rv, tr);
+        dec_gemv(p, s, L.tg, s.wbuf(0) + pl.off[0], n, s.wbuf(0) + pl.off[0], n, N_EMBD / 256, rv, tr);
         trace_step(p, l, 3, 3);
-        gemv_rows(L.tu, s.wbuf(0) + pl.off[1], n, N_EMBD / 256, *s.xq(), s.part(), MAX_TASKS, rv + n);
+        dec_gemv(p, s, L.tu, s.wbuf(0) + pl.off[1], n, s.wbuf(0) + pl.off[1], n, N_EMBD / 256, rv + n, nullptr);
     }
     trace_step(p, l, 3, 4);
     for (int r = threadIdx.x; r < n; r += blockDim.x) p.h[pl.row0[0] + r] = canon_silu_mul(rv[r], rv[n + r]);
@@ -1230,6 +1243,7 @@ __device__ bool phase_down(const DecodeParams& p, const Smem& s, int l, int cta,
             c1 = ld_cg_f4(p.h + 256 * b1 + 8 * lane + 4);
         }
         quant_xq<true>(a0, c0, s.xq(), b0);
+        if (warp == 0) trace_step(p, l, 4, 3);   // h loaded, first block quantised
         if (two) quant_xq<true>(a1, c1, s.xq(), b1);
     }
     __syncthreads();
@@ -1237,8 +1251,8 @@ __device__ bool phase_down(const DecodeParams& p, const Smem& s, int l, int cta,
     if (!wait_weights(p, s, 4 * l + 3)) return false;
     if (threadIdx.x == COPY_THREAD) issue_copy(p, s, 4 * l + 4, cta, ncta);   // next QKV rows or LM stage 0: buffer 0
     trace_step(p, l, 4, 2);
-    gemv_rows(L.td, s.wbuf(1), n, N_FF / 256, *s.xq(), s.part(), MAX_TASKS, s.rowval(),
-              (p.trace && l == 1 && cta == 0) ? p.trace + TRACE_GEMV + 3 : nullptr);
+    dec_gemv(p, s, L.td, s.wbuf(1), n, s.wbuf(1), n, N_FF / 256, s.rowval(),
+             (p.trace && l == 1 && cta == 0) ? p.trace + TRACE_GEMV + 3 : nullptr);
     if (threadIdx.x < n) {
         const float xn = __fadd_rn(xr, s.rowval()[threadIdx.x]);
         p.x[r0 + threadIdx.x] = xn;
@@ -1272,7 +1286,7 @@ __device__ void phase_lm(const DecodeParams& p, const Smem& s, int cta, int ncta
         const int a = q.r0 + st * q.sr, n = min(q.sr, q.r1 - a);
         float* lg = p.logits;
         const int wl = p.write_logits;
-        gemv_rows(p.lm_type, lm_slot(s, slot), n, q.nb, *s.xq(), s.part(), MAX_TASKS, s.rowval());
+        dec_gemv(p, s, p.lm_type, lm_slot(s, slot), n, lm_slot(s, slot), n, q.nb, s.rowval(), nullptr);
         if (threadIdx.x < n) {
             const int row = a + threadIdx.x;
             const float v = s.rowval()[threadIdx.x];

@@ -297,6 +297,7 @@ DecodeParams make_params(const mcpm_engine* e, int token, int pos, int write_log
     p.trace = e->trace;
     p.sched = e->sched;
     p.kv_f16 = e->kv_f16;
+    p.blk_order = e->batch_gemm == MCPM_GEMM_TCGEN05;
     p.token = token;
     p.pos = pos;
     p.write_logits = write_logits;
@@ -976,7 +977,14 @@ mcpm_status mcpm_gemv_q8k(int type, const void* w, const void* xq, float* y, int
     if (!w || !xq || !y) return MCPM_BAD_ARG;
     if (type != GGML_Q4_K && type != GGML_Q6_K) return MCPM_UNSUPPORTED_TYPE;
     if (!gemv_shape_ok(type, w, rows, cols)) return MCPM_BAD_ARG;
-    return cuda_status(op_gemv_q8k(type, w, xq, y, nullptr, nullptr, rows, cols, static_cast<cudaStream_t>(stream)));
+    return cuda_status(op_gemv_q8k(type, w, xq, y, nullptr, nullptr, rows, cols, 0, static_cast<cudaStream_t>(stream)));
+}
+
+mcpm_status mcpm_gemv_q8k_block(int type, const void* w, const void* xq, float* y, int rows, int cols, void* stream) {
+    if (!w || !xq || !y) return MCPM_BAD_ARG;
+    if (type != GGML_Q4_K && type != GGML_Q6_K) return MCPM_UNSUPPORTED_TYPE;
+    if (!gemv_shape_ok(type, w, rows, cols) || (cols != 2048 && cols != 6144)) return MCPM_BAD_ARG;
+    return cuda_status(op_gemv_q8k(type, w, xq, y, nullptr, nullptr, rows, cols, 1, static_cast<cudaStream_t>(stream)));
 }
 
 mcpm_status mcpm_gemv_blocksums(int type, const void* w, const void* xq, int32_t* isum, int32_t* aux, int rows,
@@ -984,7 +992,7 @@ mcpm_status mcpm_gemv_blocksums(int type, const void* w, const void* xq, int32_t
     if (!w || !xq || !isum || !aux) return MCPM_BAD_ARG;
     if (type != GGML_Q4_K && type != GGML_Q6_K) return MCPM_UNSUPPORTED_TYPE;
     if (!gemv_shape_ok(type, w, rows, cols)) return MCPM_BAD_ARG;
-    return cuda_status(op_gemv_q8k(type, w, xq, nullptr, isum, aux, rows, cols, static_cast<cudaStream_t>(stream)));
+    return cuda_status(op_gemv_q8k(type, w, xq, nullptr, isum, aux, rows, cols, 0, static_cast<cudaStream_t>(stream)));
 }
 
 mcpm_status mcpm_gemv_gate_up_q8k(const void* wg, const void* wu, const void* xq, float* gate, float* up, int rows,
@@ -1034,19 +1042,21 @@ mcpm_status mcpm_attention(const float* q, const float* k, const float* v, float
 }
 
 mcpm_status mcpm_gemv_q8k_timed(int type, const void* w, int n_copies, const void* xq, float* y, int rows, int cols,
-                                int reps, float* ms_per_launch, void* stream) {
+                                int order, int reps, float* ms_per_launch, void* stream) {
     if (!w || !xq || !y || !ms_per_launch || n_copies <= 0 || reps <= 0) return MCPM_BAD_ARG;
     if (!gemv_shape_ok(type, w, rows, cols)) return MCPM_BAD_ARG;
+    if (order != MCPM_ORDER_AVX2 && order != MCPM_ORDER_BLOCK) return MCPM_BAD_ARG;
+    if (order == MCPM_ORDER_BLOCK && cols != 2048 && cols != 6144) return MCPM_BAD_ARG;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const size_t stride = static_cast<size_t>(rows) * row_bytes(type, cols);
     cudaEvent_t a, b;
     MCPM_CUDA(cudaEventCreate(&a));
     MCPM_CUDA(cudaEventCreate(&b));
-    MCPM_CUDA(op_gemv_q8k(type, w, xq, y, nullptr, nullptr, rows, cols, s));   // warm-up
+    MCPM_CUDA(op_gemv_q8k(type, w, xq, y, nullptr, nullptr, rows, cols, order, s));   // warm-up
     MCPM_CUDA(cudaEventRecord(a, s));
     for (int i = 0; i < reps; ++i)
         MCPM_CUDA(op_gemv_q8k(type, static_cast<const uint8_t*>(w) + (i % n_copies) * stride, xq, y, nullptr, nullptr,
-                              rows, cols, s));
+                              rows, cols, order, s));
     MCPM_CUDA(cudaEventRecord(b, s));
     MCPM_CUDA(cudaEventSynchronize(b));
     float ms = 0.0f;

@@ -101,6 +101,8 @@ struct DecodeParams {
     unsigned* err;      // error bits
     unsigned long long* trace;   // optional: CTA 0 phase timestamps (2 per phase + 2)
     int sched;          // SCHED_* option bits
+    int blk_order;      // GEMVs in the block order (warp per row, exact block sums, one fma per block in
+                        // groups of four); 0: the reference's eight-lane AVX2 order
     int kv_f16;         // kc / vc hold fp16 rows (their element offsets are the same)
     int token;          // < 0: read *token_dev
     int pos;
@@ -171,7 +173,7 @@ cudaError_t launch_attention(const float* q, const float* k, const float* v, flo
 cudaError_t op_quantize_q8k(const float* x, void* y, int n, int rounding, cudaStream_t s);
 cudaError_t op_gemv_q8_0(const void* w, const float* x, float* y, int rows, int cols, cudaStream_t s);
 cudaError_t op_gemv_q8k(int type, const void* w, const void* xq, float* y, int32_t* isum, int32_t* aux, int rows,
-                        int cols, cudaStream_t s);
+                        int cols, int blk_order, cudaStream_t s);
 cudaError_t op_rmsnorm_q8k(const float* x, const float* w, void* out, float eps, cudaStream_t s);
 cudaError_t op_swiglu_q8k(const float* g, const float* u, void* out, int n, cudaStream_t s);
 cudaError_t op_rope_kv_append(float* q, float* k, const float* v, float* kc, float* vc, int pos, float base,

@@ -3,6 +3,7 @@
 // the same device functions as the decode kernel, so the per-op parity tests cover the
 // decode path's arithmetic.
 #include "mcpm_device.cuh"
+#include "mcpm_gemv_bo.cuh"
 #include "mcpm_internal.h"
 #include "mcpm_q80.cuh"
 
@@ -69,7 +70,7 @@ __global__ void k_rmsnorm_q8k(const float* __restrict__ x, const float* __restri
 // isum/aux != null selects the block-sum probe (integer partials only).
 __global__ void __launch_bounds__(OP_THREADS, 1)
     k_gemv(int type, const uint8_t* __restrict__ w, const uint8_t* __restrict__ xq_g, float* __restrict__ y,
-           int32_t* __restrict__ isum, int32_t* __restrict__ aux, int rows, int nb, unsigned* err) {
+           int32_t* __restrict__ isum, int32_t* __restrict__ aux, int rows, int nb, int blk_order, unsigned* err) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* ring = smem_raw;
     XQSmem* xq = reinterpret_cast<XQSmem*>(ring + RING_SLOTS * SLOT_STRIDE);
@@ -129,7 +130,10 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
             }
             __syncthreads();
         } else {
-            gemv_rows(type, sw, n, nb, *xq, part, MAX_TASKS, rowval);
+            if (blk_order)
+                gemv_bo(type, sw, n, nb, *xq, part, MAX_TASKS * PART_WORDS, rowval);
+            else
+                gemv_rows(type, sw, n, nb, *xq, part, MAX_TASKS, rowval);
             if (tid < n) y[a + tid] = rowval[tid];
         }
         if (tid == 0 && st + RING_SLOTS < nstages) issue(st + RING_SLOTS);
@@ -246,7 +250,7 @@ cudaError_t op_rmsnorm_q8k(const float* x, const float* w, void* out, float eps,
 }
 
 cudaError_t op_gemv_q8k(int type, const void* w, const void* xq, float* y, int32_t* isum, int32_t* aux, int rows,
-                        int cols, cudaStream_t s) {
+                        int cols, int blk_order, cudaStream_t s) {
     static bool prepared = false;
     static unsigned* d_err = nullptr;
     if (!prepared) {
@@ -264,7 +268,8 @@ cudaError_t op_gemv_q8k(int type, const void* w, const void* xq, float* y, int32
     const int nb = cols / 256;
     const int grid = rows < g_num_sms ? rows : g_num_sms;
     k_gemv<<<grid, OP_THREADS, gemv_smem_bytes(), s>>>(type, static_cast<const uint8_t*>(w),
-                                                        static_cast<const uint8_t*>(xq), y, isum, aux, rows, nb, d_err);
+                                                        static_cast<const uint8_t*>(xq), y, isum, aux, rows, nb, blk_order,
+                                                        d_err);
     return cudaGetLastError();
 }
 

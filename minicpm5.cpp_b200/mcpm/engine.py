@@ -74,12 +74,13 @@ SIGNATURES = {
     "mcpm_engine_destroy": (None, [P]),
     "mcpm_quantize_q8k": (I, [P, P, I, I, P]),
     "mcpm_gemv_q8k": (I, [I, P, P, P, I, I, P]),
+    "mcpm_gemv_q8k_block": (I, [I, P, P, P, I, I, P]),
     "mcpm_gemv_q8_0_f32": (I, [P, P, P, I, I, P]),
     "mcpm_gemv_blocksums": (I, [I, P, P, P, P, I, I, P]),
     "mcpm_gemv_gate_up_q8k": (I, [P, P, P, P, P, I, I, P]),
     "mcpm_rmsnorm_q8k": (I, [P, P, P, I, F, P]),
     "mcpm_swiglu_q8k": (I, [P, P, P, I, P]),
-    "mcpm_gemv_q8k_timed": (I, [I, P, I, P, P, I, I, I, C.POINTER(F), P]),
+    "mcpm_gemv_q8k_timed": (I, [I, P, I, P, P, I, I, I, I, C.POINTER(F), P]),
     "mcpm_attention": (I, [P, P, P, P, P, I, I, P, P, P]),
     "mcpm_attention_noalloc": (I, [P, P, P, P, P, I, I, P, P, P]),
     "mcpm_trace_enable": (I, [P, I]),
@@ -306,6 +307,13 @@ def gemv_q8k(ggml_type: int, w_ptr: int, xq_ptr: int, y_ptr: int, rows: int, col
     check(load_library().mcpm_gemv_q8k(ggml_type, w_ptr, xq_ptr, y_ptr, rows, cols, stream), "mcpm_gemv_q8k")
 
 
+def gemv_q8k_block(ggml_type: int, w_ptr: int, xq_ptr: int, y_ptr: int, rows: int, cols: int, stream: int = 0) -> None:
+    """The same product in the engine's default block order (exact block sums, one fma per block in groups of
+    four blocks): the order of the decode kernel and of the batched GEMM with GEMM_TCGEN05."""
+    check(load_library().mcpm_gemv_q8k_block(ggml_type, w_ptr, xq_ptr, y_ptr, rows, cols, stream),
+          "mcpm_gemv_q8k_block")
+
+
 def gemv_q8_0(w_ptr: int, x_ptr: int, y_ptr: int, rows: int, cols: int, stream: int = 0) -> None:
     check(load_library().mcpm_gemv_q8_0_f32(w_ptr, x_ptr, y_ptr, rows, cols, stream), "mcpm_gemv_q8_0_f32")
 
@@ -329,9 +337,12 @@ def swiglu_q8k(g_ptr: int, u_ptr: int, out_ptr: int, n: int, stream: int = 0) ->
     check(load_library().mcpm_swiglu_q8k(g_ptr, u_ptr, out_ptr, n, stream), "mcpm_swiglu_q8k")
 
 
-def gemv_q8k_timed(ggml_type, w_ptr, n_copies, xq_ptr, y_ptr, rows, cols, reps, stream=0) -> float:
+ORDER_AVX2, ORDER_BLOCK = 0, 1
+
+
+def gemv_q8k_timed(ggml_type, w_ptr, n_copies, xq_ptr, y_ptr, rows, cols, reps, stream=0, order=ORDER_BLOCK) -> float:
     ms = C.c_float()
-    check(load_library().mcpm_gemv_q8k_timed(ggml_type, w_ptr, n_copies, xq_ptr, y_ptr, rows, cols, reps,
+    check(load_library().mcpm_gemv_q8k_timed(ggml_type, w_ptr, n_copies, xq_ptr, y_ptr, rows, cols, order, reps,
                                              C.byref(ms), stream), "mcpm_gemv_q8k_timed")
     return ms.value
 

@@ -20,12 +20,14 @@ Fixtures:
                               logits at the last prompt position
   reference_variability_wc.json  the reference's own spread on the parity run: eight teacher-forced
                               runs at 4 OpenMP threads against the 1-thread run (per position)
-  restatement_decode_wc.npz   the C restatement on the same teacher-forced inputs
+  restatement_decode_wc.npz   the C restatement on the same teacher-forced inputs (eight-lane order)
+  restatement_decode_wc_block.npz  the same in the block order (the engine's default GEMV order)
   reference_q8_0.npz          gemv_q8_0 of the reference build (fp32 activations) on seeded
                               Q8_0 matrices with the config-1 distributions
 
     python tests/golden/make_golden.py --q8_0     # only reference_q8_0.npz
     python tests/golden/make_golden.py --wc       # only the parity-model files
+    python tests/golden/make_golden.py --restatement   # only the two restatement fixtures
 """
 import json
 import os
@@ -153,7 +155,9 @@ toks, prompt = g["tokens"], g["prompt"]
 n = len(toks)
 inputs = list(prompt) + list(toks[len(prompt) - 1:n - 1])   # teacher forcing: the 1-thread run's tokens
 path = synth.ensure_model("q4_k_m", 0, dscale=dscale)
-eng = O.OracleModel(O.Oracle(), path, n + 1) if which == "restatement" else O.RefEngine(O.Ref(), path, n + 1)
+eng = O.OracleModel(O.Oracle(), path, n + 1) if which.startswith("restatement") else O.RefEngine(O.Ref(), path, n + 1)
+if which == "restatement_block":   # the engine's default GEMV order (ORC_ORDER_BATCH)
+    eng.set_order(O.Oracle.ORDER_BATCH)
 lg = np.zeros(130560, np.float32)
 am, top = [], []
 for pos in range(n):
@@ -164,12 +168,17 @@ np.savez_compressed(out, argmax=np.array(am, np.int32), top_val=np.array(top))
 
 
 def teacher_forced(which, threads, out_path):
-    """`which` ("reference" or "restatement") over the parity run's inputs, fed the 1-thread
+    """`which` ("reference", "restatement" or "restatement_block") over the parity run's inputs, fed the 1-thread
     reference's own tokens: argmax and the logits at the 1-thread run's top-32 indices."""
     env = dict(os.environ, OMP_NUM_THREADS=str(threads))
     subprocess.run([sys.executable, "-c", TF_CHILD, os.path.join(REPO, "oracle"), os.path.join(REPO, "minicpm5.cpp_b200"),
                     os.path.join(HERE, "reference_decode_wc.npz"), which, out_path, str(PARITY_DSCALE)],
                    env=env, check=True)
+
+
+def restatement_fixtures():
+    teacher_forced("restatement", 8, os.path.join(HERE, "restatement_decode_wc.npz"))
+    teacher_forced("restatement_block", 8, os.path.join(HERE, "restatement_decode_wc_block.npz"))
 
 
 def parity_model_goldens():
@@ -183,8 +192,10 @@ def parity_model_goldens():
     units on this model; per position, `spread` is the largest |difference| over the top-32
     logits of either run against the 1-thread run.  A position is `decidable` when the
     1-thread run's top-2 margin exceeds that spread.
-    restatement_decode_wc.npz: this project's C restatement, teacher-forced the same way (the
-    CUDA engine must reproduce it bit for bit).
+    restatement_decode_wc.npz: this project's C restatement, teacher-forced the same way, in the
+    reference's eight-lane GEMV order (the CUDA engine with MCPM_GEMM_MMA must reproduce it bit for
+    bit); restatement_decode_wc_block.npz: the same in the block order (ORC_ORDER_BATCH, the
+    engine's default).
     """
     from mcpm import synth
     man = json.load(open(synth.ensure_model("q4_k_m", 0, dscale=PARITY_DSCALE) + ".json"))
@@ -197,7 +208,7 @@ def parity_model_goldens():
         teacher_forced("reference", 4, tmp)
         runs.append(dict(np.load(tmp)))
         os.unlink(tmp)
-    teacher_forced("restatement", 8, os.path.join(HERE, "restatement_decode_wc.npz"))
+    restatement_fixtures()
     d = [np.abs(r["top_val"] - a["top_val"]) for r in runs]
     spread = np.max([x.max(1) for x in d], axis=0)
     margin = a["top_val"][:, 0] - a["top_val"][:, 1]
@@ -221,6 +232,9 @@ def main():
     assert O.have_ref(), "needs the reference tree"
     if "--wc" in sys.argv:
         parity_model_goldens()
+        return
+    if "--restatement" in sys.argv:   # only the restatement's teacher-forced fixtures (no reference run)
+        restatement_fixtures()
         return
     np.savez_compressed(os.path.join(HERE, "reference_q8_0.npz"), **q8_0_kernels())
     if "--q8_0" in sys.argv:

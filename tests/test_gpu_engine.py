@@ -1,8 +1,11 @@
 """Whole-forward parity on the GPU through the C ABI.
 
 The CUDA decode path and the C restatement follow the same canonical numerics, so logits,
-the residual stream, K/V cache rows and greedy tokens are compared for exact equality.
-The restatement itself is checked against the reference build in test_oracle_vs_reference.
+the residual stream, K/V cache rows and greedy tokens are compared for exact equality, in both
+GEMV orders of the engine: the block order (mcpm_config::batch_gemm MCPM_GEMM_TCGEN05, the
+default; the restatement's ORC_ORDER_BATCH) and the reference's eight-lane order (MCPM_GEMM_MMA;
+ORC_ORDER_AVX2).  The restatement itself is checked against the reference build in
+test_oracle_vs_reference and test_parity_model.
 """
 import numpy as np
 import pytest
@@ -11,21 +14,39 @@ pytestmark = pytest.mark.gpu
 
 N_PROMPT, N_GEN = 12, 8
 MAX_SEQ = 64
+ORDERS = ("block", "avx2")
+
+
+def gemm_of(order):
+    from mcpm import engine as E
+    return E.GEMM_TCGEN05 if order == "block" else E.GEMM_MMA
+
+
+def oracle_order(order):
+    import oracle as O
+    return O.Oracle.ORDER_BATCH if order == "block" else O.Oracle.ORDER_AVX2
+
+
+@pytest.fixture(scope="module", params=ORDERS)
+def order(request):
+    return request.param
 
 
 @pytest.fixture(scope="module")
-def engine(cuda, model_path):
+def engine(cuda, model_path, order):
     from mcpm import engine as E
-    e = E.MiniCPM5Engine(device=0, max_seq=MAX_SEQ)
+    e = E.MiniCPM5Engine(device=0, max_seq=MAX_SEQ, batch_gemm=gemm_of(order))
     assert e.load_model(model_path)
     yield e
     e.close()
 
 
 @pytest.fixture(scope="module")
-def oracle_model(oracle, model_path):
+def oracle_model(oracle, model_path, order):
     import oracle as O
-    return O.OracleModel(oracle, model_path, MAX_SEQ)
+    m = O.OracleModel(oracle, model_path, MAX_SEQ)
+    m.set_order(oracle_order(order))
+    return m
 
 
 def test_forward_bitexact_vs_restatement(engine, oracle_model):
@@ -46,8 +67,9 @@ def test_forward_bitexact_vs_restatement(engine, oracle_model):
         tok = want_tok
 
 
-@pytest.mark.parametrize("pos", [300, 1000, 3000, 8200, 10300])
-def test_late_steps_bitexact_vs_restatement(cuda, oracle, model_path, pos):
+@pytest.mark.parametrize("pos,order", [(300, "block"), (1000, "block"), (3000, "block"), (8200, "block"),
+                                       (10300, "block"), (300, "avx2"), (8200, "avx2")])
+def test_late_steps_bitexact_vs_restatement(cuda, oracle, model_path, pos, order):
     """Two decode steps at a late position over a seeded cache (the same random K/V rows
     0..pos-1 in the engine and in the restatement), covering every attention path of the
     decode kernel: 300 positions (32-row chunks, 10 chunks combined in the o_proj prologue
@@ -57,9 +79,10 @@ def test_late_steps_bitexact_vs_restatement(cuda, oracle, model_path, pos):
     import oracle as O
     from mcpm import engine as E, spec
     max_seq = pos + 2
-    e = E.MiniCPM5Engine(device=0, max_seq=max_seq)
+    e = E.MiniCPM5Engine(device=0, max_seq=max_seq, batch_gemm=gemm_of(order))
     assert e.load_model(model_path)
     om = O.OracleModel(oracle, model_path, max_seq)
+    om.set_order(oracle_order(order))
     try:
         rng = np.random.default_rng(pos)
         k = rng.normal(0, 1, (pos, 256)).astype(np.float32)
@@ -178,6 +201,7 @@ def test_cpp_sampler_loop_device_logits(cuda, oracle, model_path, tmp_path):
     toks = [t for t, _ in runs["host"]]
     assert len(set(toks)) > 1
     om = O.OracleModel(oracle, model_path, 16)
+    om.set_order(O.Oracle.ORDER_BATCH)   # the facade's engine runs the default (block) order
     lg = np.zeros(130560, np.float32)
     inputs = prompt + toks[:-1]
     k = 0
@@ -190,18 +214,19 @@ def test_cpp_sampler_loop_device_logits(cuda, oracle, model_path, tmp_path):
     om.close()
 
 
-@pytest.mark.parametrize("n_prompt,pos0", [(5, 0), (64, 0), (150, 0), (70, 9)])
-def test_batched_prefill_equals_token_by_token(cuda, model_path, n_prompt, pos0):
+@pytest.mark.parametrize("n_prompt,pos0,order", [(5, 0, "block"), (64, 0, "block"), (150, 0, "block"),
+                                                 (70, 9, "block"), (5, 0, "avx2"), (150, 0, "avx2"),
+                                                 (70, 9, "avx2")])
+def test_batched_prefill_equals_token_by_token(cuda, model_path, n_prompt, pos0, order):
     """mcpm_prefill (the prompt as batched steps of up to 64 positions sharing the engine's KV
-    cache) on the mma.sync GEMMs (the batch-1 decode's order) against one mcpm_forward per
-    position: the last position's logits, every K/V row written and the greedy continuation are
-    bit-identical.  (The default tcgen05 prefill is pinned to the restatement's BATCH order in
-    test_prefill_tcgen05_vs_restatement.)"""
+    cache) against one mcpm_forward per position, in either GEMV order (block: tcgen05 GEMMs and
+    the decode kernel's warp GEMVs; avx2: mma.sync GEMMs and the eight-lane GEMVs): the last
+    position's logits, every K/V row written and the greedy continuation are bit-identical."""
     from mcpm import engine as E, synth
     prompt = [int(t) for t in synth.prompt_ids(pos0 + n_prompt, seed=77)]
     max_seq = pos0 + n_prompt + 8
-    a = E.MiniCPM5Engine(device=0, max_seq=max_seq, batch_gemm=E.GEMM_MMA)   # the batch-1 order
-    b = E.MiniCPM5Engine(device=0, max_seq=max_seq)
+    a = E.MiniCPM5Engine(device=0, max_seq=max_seq, batch_gemm=gemm_of(order))
+    b = E.MiniCPM5Engine(device=0, max_seq=max_seq, batch_gemm=gemm_of(order))
     try:
         assert a.load_model(model_path) and b.load_model(model_path)
         for pos in range(pos0):   # both engines decode the first pos0 positions one by one
@@ -417,7 +442,7 @@ def test_schedule_options_bitexact(cuda, model_path, pos0):
 def test_prefill_tcgen05_vs_restatement(cuda, oracle, model_path, n_prompt):
     """Prefill on the tcgen05 batched GEMM (block-order fp32 over exact block sums) against the
     restatement stepping the same positions in its BATCH order: last logits, greedy token and
-    K/V rows bit for bit; the decode that follows (batch-1 kernel) continues in the AVX2 order."""
+    K/V rows bit for bit; the decode that follows (batch-1 kernel) continues in the same order."""
     import oracle as O
     from mcpm import engine as E, synth
     prompt = [int(t) for t in synth.prompt_ids(n_prompt, seed=41)]
@@ -434,7 +459,6 @@ def test_prefill_tcgen05_vs_restatement(cuda, oracle, model_path, n_prompt):
         diff = np.sum(lg.view(np.uint32) != ref.view(np.uint32))
         assert diff == 0, f"{diff} logits differ, max {np.max(np.abs(lg - ref))}"
         assert tok == want
-        om.set_order(O.Oracle.ORDER_AVX2)
         pos = n_prompt
         for _ in range(3):
             got = e.forward_greedy(tok, pos)

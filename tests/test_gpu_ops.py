@@ -74,6 +74,27 @@ def test_gemv_bitexact(cuda, oracle, ggml_type, rows, cols):
 
 
 @pytest.mark.parametrize("ggml_type", [12, 14])
+@pytest.mark.parametrize("rows,cols", SHAPES)
+def test_gemv_block_order_bitexact(cuda, oracle, ggml_type, rows, cols):
+    """The decode kernel's warp-per-row GEMV (block order) against the restatement's
+    ORC_ORDER_BATCH, bit for bit, including the Q6_K LM head shape."""
+    from mcpm import engine as E
+    if ggml_type == 12 and rows == 130560:
+        pytest.skip("LM head is Q6_K")
+    w = rand_tensor_bytes(ggml_type, rows, cols, seed=rows * 5 + cols + ggml_type)
+    x = np.random.default_rng(rows + cols + 1).normal(0, 1, cols).astype(np.float32)
+    xq = oracle.quantize_q8k(x, 0, 1)
+    wd, xqd = _dev(cuda, w), _dev(cuda, xq.view(np.uint8))
+    yd = cuda.zeros(rows, dtype=cuda.float32, device="cuda")
+    E.gemv_q8k_block(ggml_type, wd.data_ptr(), xqd.data_ptr(), yd.data_ptr(), rows, cols)
+    cuda.cuda.synchronize()
+    got = yd.cpu().numpy()
+    want = oracle.gemv_q8k(ggml_type, w, xq, rows, cols, order=2, fused_min=1)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), \
+        f"{np.sum(got != want)} of {rows} rows differ, max {np.max(np.abs(got - want))}"
+
+
+@pytest.mark.parametrize("ggml_type", [12, 14])
 def test_gemv_matches_reference_build(cuda, oracle, ref, ggml_type):
     from mcpm import engine as E
     rows, cols = 512, 6144

@@ -3,7 +3,8 @@ config 0's shape: a 128-id prompt, then 64 greedy tokens), teacher-forced with t
 reference's own tokens.  See test_parity_model.py for the model and for the reference's own
 run-to-run spread, which bounds what any implementation with other rounding can match.
 
-Checks, over all 192 positions:
+Checks, over all 192 positions, in both GEMV orders of the engine (the default block order
+against the restatement's ORC_ORDER_BATCH fixture, MCPM_GEMM_MMA against the eight-lane one):
   * the engine equals the C restatement bit for bit (logits at the reference's top-32 indices
     and the argmax), so every parity statement about the restatement holds for the engine;
   * at every position where the reference decides its argmax against its own spread, the
@@ -23,17 +24,19 @@ pytestmark = pytest.mark.gpu
 PARITY_DSCALE = 0.04
 
 
-def test_engine_vs_reference_on_parity_model(cuda):
+@pytest.mark.parametrize("order", ["block", "avx2"])
+def test_engine_vs_reference_on_parity_model(cuda, order):
     from mcpm import engine as E, synth
     g = np.load(os.path.join(GOLDEN, "reference_decode_wc.npz"))
     v = json.load(open(os.path.join(GOLDEN, "reference_variability_wc.json")))
-    r = np.load(os.path.join(GOLDEN, "restatement_decode_wc.npz"))
+    r = np.load(os.path.join(GOLDEN, "restatement_decode_wc_block.npz" if order == "block" else
+                             "restatement_decode_wc.npz"))
     path = synth.ensure_model("q4_k_m", 0, dscale=PARITY_DSCALE)
     assert json.load(open(path + ".json"))["content_digest"] == v["model_manifest"]["content_digest"]
     toks, prompt = g["tokens"], g["prompt"]
     n = len(toks)
     inputs = list(prompt) + list(toks[len(prompt) - 1:n - 1])
-    eng = E.MiniCPM5Engine(device=0, max_seq=n + 8)
+    eng = E.MiniCPM5Engine(device=0, max_seq=n + 8, batch_gemm=E.GEMM_TCGEN05 if order == "block" else E.GEMM_MMA)
     assert eng.load_model(path)
     am, top = [], []
     full = None

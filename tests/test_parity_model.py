@@ -85,6 +85,17 @@ def test_restatement_fixture_vs_reference_all_positions(parity):
     assert int(np.sum(r["argmax"] == g["tokens"])) >= min(v["argmax_agree_4_vs_1"]) - 4
 
 
+def test_block_order_fixture_vs_reference_all_positions(parity):
+    """The committed teacher-forced restatement run in the block order (the engine's default GEMV
+    order; all 192 positions) against the reference, at the same bar as the eight-lane order."""
+    g, v, _ = parity
+    r = np.load(os.path.join(GOLDEN, "restatement_decode_wc_block.npz"))
+    dec = np.array(v["decidable"])
+    assert np.array_equal(r["argmax"][dec], g["tokens"][dec])
+    assert np.abs(r["top_val"] - g["top_val"]).mean() <= 1.25 * max(v["mean_abs_top32_4_vs_1"])
+    assert int(np.sum(r["argmax"] == g["tokens"])) >= min(v["argmax_agree_4_vs_1"]) - 4
+
+
 def test_batch_order_restatement_vs_reference_on_parity_model(parity, parity_model_path, oracle):
     """The batched path's fp32 order (exact block sums, one fma per block, groups of four
     blocks: the tcgen05 batched GEMM and prefill) against the reference build: the reference's
@@ -98,6 +109,10 @@ def test_batch_order_restatement_vs_reference_on_parity_model(parity, parity_mod
         am.append(m.forward(int(g["prompt"][pos]), pos, lg))
         top.append(lg[g["top_idx"][pos]].copy())
     am, top = np.array(am), np.array(top)
+    # the committed block-order fixture is this restatement's own run (the GPU test pins the engine to it)
+    rb = np.load(os.path.join(GOLDEN, "restatement_decode_wc_block.npz"))
+    assert np.array_equal(top.view(np.uint32), rb["top_val"][:N_CHECK].view(np.uint32))
+    assert np.array_equal(am, rb["argmax"][:N_CHECK])
     dec = np.array(v["decidable"][:N_CHECK])
     assert np.array_equal(am[dec], g["tokens"][:N_CHECK][dec])
     assert np.abs(top - g["top_val"][:N_CHECK]).mean() <= 1.25 * max(v["mean_abs_top32_4_vs_1"])
