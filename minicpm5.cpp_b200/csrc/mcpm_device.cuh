@@ -334,21 +334,20 @@ __device__ __forceinline__ float canon_silu_mul(float g, float u) {
 }
 
 // lround + clamp as inlined by the reference build (ops.cpp:717); NaN/huge -> -127.
+// Branch-free: the conversion truncates and saturates, the clamp is integer min/max, and
+// values outside the build's 64-bit conversion range (and NaN) select -127.
 __device__ __forceinline__ int quant_away(float v) {
     const float a = __fadd_rn(v, copysignf(0.4999999701976776f, v));
-    if (!(a < 9223372036854775808.0f && a >= -9223372036854775808.0f)) return -127;
-    const float t = truncf(a);
-    if (t >= 127.0f) return 127;
-    if (t > -127.0f) return static_cast<int>(t);
-    return -127;
+    const bool ok = a < 9223372036854775808.0f && a >= -9223372036854775808.0f;
+    const int t = min(max(__float2int_rz(a), -127), 127);
+    return ok ? t : -127;
 }
-// _mm256_cvtps_epi32 (ties-to-even) + clamp (ops_avx2.cpp:118-121).
+// _mm256_cvtps_epi32 (ties-to-even; NaN and |v| >= 2^31 give INT_MIN) + clamp
+// (ops_avx2.cpp:118-121).  Branch-free, as quant_away.
 __device__ __forceinline__ int quant_even(float v) {
-    if (!(v < 2147483648.0f && v >= -2147483648.0f)) return -127;
-    const float t = rintf(v);
-    if (t >= 127.0f) return 127;
-    if (t <= -127.0f) return -127;
-    return static_cast<int>(t);
+    const bool ok = v < 2147483648.0f && v >= -2147483648.0f;
+    const int t = min(max(__float2int_rn(v), -127), 127);
+    return ok ? t : -127;
 }
 
 // ---------------------------------------------------------------- activation staging
