@@ -192,9 +192,9 @@ __device__ LmPlan lm_plan(const DecodeParams& p, int cta, int ncta) {
     q.nstages = (q.r1 - q.r0 + q.sr - 1) / q.sr;
     return q;
 }
-__device__ uint8_t* lm_slot(const Smem& s, int slot) { return s.wbuf(slot); }
+__device__ uint8_t* lm_slot(const Smem& s, int slot) { return s.wbuf(0) + slot * LM_SLOT_STRIDE; }
 __device__ void issue_lm_stage(const DecodeParams& p, const Smem& s, const LmPlan& q, int st) {
-    const int slot = st & 1;
+    const int slot = st % LM_SLOTS;
     const int a = q.r0 + st * q.sr, n = min(q.sr, q.r1 - a);
     const uint32_t bytes = n > 0 ? static_cast<uint32_t>(n) * q.rb : 0;
     mbar_expect_tx(&s.lmbar()[slot], bytes);
@@ -1262,7 +1262,9 @@ __device__ bool phase_down(const DecodeParams& p, const Smem& s, int l, int cta,
     trace_cta(p, l, 4, 0);
     if (threadIdx.x == ISSUE_THREAD) {
         if (l + 1 == p.n_layer) {
-            issue_lm_stage(p, s, lmq, 1);
+            fence_proxy_async_smem();
+            for (int st = 1; st < LM_SLOTS; ++st) issue_lm_stage(p, s, lmq, st);   // slots after stage 0's lie
+                                                                                  // over buffer 1, free now
         } else {
             prefetch_attention<KT>(p, l + 1, cta);
             prefetch_norms(p, s, l + 1, cta);
@@ -1280,8 +1282,8 @@ __device__ void phase_lm(const DecodeParams& p, const Smem& s, int cta, int ncta
     int besti = 0x7fffffff;
     int nan0 = 0;
     for (int st = 0; st < q.nstages; ++st) {
-        const int slot = st & 1;
-        const bool ok = mbar_wait(&s.lmbar()[slot], (st >> 1) & 1, p.err);
+        const int slot = st % LM_SLOTS;
+        const bool ok = mbar_wait(&s.lmbar()[slot], (st / LM_SLOTS) & 1, p.err);
         if (__syncthreads_or(!ok)) return;
         const int a = q.r0 + st * q.sr, n = min(q.sr, q.r1 - a);
         float* lg = p.logits;
@@ -1294,7 +1296,7 @@ __device__ void phase_lm(const DecodeParams& p, const Smem& s, int cta, int ncta
             if (row == 0 && v != v) nan0 = 1;
             if (v > best || (v == best && row < besti)) best = v, besti = row;
         }
-        if (threadIdx.x == 0 && st + 2 < q.nstages) issue_lm_stage(p, s, q, st + 2);
+        if (threadIdx.x == 0 && st + LM_SLOTS < q.nstages) issue_lm_stage(p, s, q, st + LM_SLOTS);
         if (st < 4) trace_step(p, 1, 5, 2 + st);
     }
     trace_step(p, 1, 5, 6);

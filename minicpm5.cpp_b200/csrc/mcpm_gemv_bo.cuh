@@ -21,6 +21,7 @@
 
 namespace mcpm {
 
+constexpr int GEMV_BO_LG = -1;   // log2 of the threads per task; -1: the largest that fits the CTA
 constexpr int BO_WORDS = 3;   // per (row, block): isum, minsum (Q4_K), fp16 scale bits (Q4_K: d | dmin << 16)
 
 __device__ __forceinline__ int dp2a_lo_ss(int a, int b, int c) {   // c + a.h0*b.b0 + a.h1*b.b1, signed
@@ -135,7 +136,7 @@ __device__ __noinline__ void gemv_bo_t(const uint8_t* w0, int R0, const uint8_t*
     const int mt = (part_words / BO_WORDS / NB) * NB;   // whole rows per pass
     for (int t0 = 0; t0 < R * NB; t0 += mt) {
         const int ntask = min(mt, R * NB - t0);
-        const int lg = 4 * ntask <= nthr ? 2 : 2 * ntask <= nthr ? 1 : 0;   // log2 of the split S
+        const int lg = GEMV_BO_LG >= 0 ? GEMV_BO_LG : 4 * ntask <= nthr ? 2 : 2 * ntask <= nthr ? 1 : 0;   // log2 of S
         const int S = 1 << lg, per = 4 >> lg;                                // threads per task, quarters each
         for (int u = tid; u < ntask * S; u += nthr) {   // a task's S threads are adjacent lanes of one warp
             const int t = u >> lg, k = u & (S - 1);

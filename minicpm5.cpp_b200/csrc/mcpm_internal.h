@@ -19,7 +19,10 @@ constexpr int WBUF_BYTES = 98304;          // one weight buffer (two per CTA)
 constexpr int WBUF_SLACK = 128;            // readable tail after each buffer (unaligned Q6_K reads)
 constexpr int MAX_TASKS = 512;             // (row, super-block) tasks per GEMV pass
 constexpr int ROWVAL_FLOATS = 256;
-constexpr int LM_SLOT_BYTES = WBUF_BYTES;   // LM head: one stage per weight buffer
+constexpr int LM_SLOTS = 2;                 // LM head: a ring of stages laid over both weight buffers
+constexpr int LM_SLOT_STRIDE = WBUF_BYTES + WBUF_SLACK;   // bytes per stage slot
+constexpr int LM_SLOT_BYTES = LM_SLOT_STRIDE - WBUF_SLACK;   // weight bytes per stage (the rest: readable tail)
+static_assert(LM_SLOTS * LM_SLOT_STRIDE <= 2 * (WBUF_BYTES + WBUF_SLACK), "LM ring inside the weight buffers");
 constexpr int ATT_MAX_CHUNKS = 64;         // attention chunks per head (chunk = 32*ceil(n/2048))
 constexpr int ATT_PART_STRIDE = 4 + HEAD_DIM;   // m, l, 2 pad, o[128]: o 16-byte aligned
 constexpr int ATT_PART_O = 4;
