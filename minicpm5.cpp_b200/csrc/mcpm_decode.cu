@@ -531,12 +531,26 @@ __device__ bool phase_qkv(const DecodeParams& p, const Smem& s, int l, int token
     const PhaseLayout pl = phase_layout(L, *s.rows(), 0);
     const int lo[3] = {0, N_EMBD, N_EMBD + KV_DIM};
     float* rv = s.rowval();
+    // A CTA's rows span at most two of Q, K, V; two spans of one type (Q and K, or K and V rows
+    // of the same quantisation) run as one GEMV call: their outputs are adjacent in rv.
+    bool done_next = false;   // segment i was taken by the call of segment i-1
 #pragma unroll
-    for (int i = 0; i < 3; ++i) {
+    for (int i = 0; i < 3; ++i) {   // unrolled: PhaseLayout stays in registers
+        if (done_next) {
+            done_next = false;
+            continue;
+        }
         if (pl.nrows[i] == 0) continue;   // uniform across the CTA
         const int base = lo[i] + pl.row0[i] - a;
-        dec_gemv(p, s, phase_type(L, 0, i), s.wbuf(0) + pl.off[i], pl.nrows[i], s.wbuf(0) + pl.off[i], pl.nrows[i],
-                 N_EMBD / 256, rv + base, (p.trace && l == 1 && cta == 0 && i == 0) ? p.trace + TRACE_GEMV + 9 : nullptr);
+        const int ti = phase_type(L, 0, i);
+        if (i < 2 && pl.nrows[i + 1] > 0 && phase_type(L, 0, i + 1) == ti) {
+            dec_gemv(p, s, ti, s.wbuf(0) + pl.off[i], pl.nrows[i], s.wbuf(0) + pl.off[i + 1],
+                     pl.nrows[i] + pl.nrows[i + 1], N_EMBD / 256, rv + base, nullptr);
+            done_next = true;
+            continue;
+        }
+        dec_gemv(p, s, ti, s.wbuf(0) + pl.off[i], pl.nrows[i], s.wbuf(0) + pl.off[i], pl.nrows[i], N_EMBD / 256,
+                 rv + base, (p.trace && l == 1 && cta == 0 && i == 0) ? p.trace + TRACE_GEMV + 9 : nullptr);
     }
     trace_step(p, l, 0, 3);
     __syncthreads();   // buffer 0 read by every GEMV above
