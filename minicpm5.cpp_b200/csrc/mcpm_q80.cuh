@@ -49,45 +49,77 @@ __device__ __forceinline__ int q80_xpos(int i) {
     return (b << 5) | ((j ^ (b & 7)) << 2) | (i & 3);
 }
 
-// int8 lane k of w as an exact float: (q + 128) is the low byte of w ^ 0x80 (two's
+// Packed fp32 pairs (sm_100 f32x2 arithmetic: two IEEE round-to-nearest operations per
+// instruction, each lane rounded exactly as the scalar operation).
+__device__ __forceinline__ unsigned long long f2_pack(float lo, float hi) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ float2 f2_unpack(unsigned long long v) {
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+    return r;
+}
+__device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b, unsigned long long c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ unsigned long long f2_mul(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+// int8 lanes k, k+1 of w as exact floats: (q + 128) is a low byte of w ^ 0x80 (two's
 // complement), 0x4B0000xx is 2^23 + q + 128, and subtracting 2^23 + 128 is exact.
-__device__ __forceinline__ float q80_i8f(uint32_t wx, int k) {
-    const uint32_t bits = __byte_perm(wx, 0x4B000000u, 0x7640u | static_cast<uint32_t>(k));
-    return __fadd_rn(__uint_as_float(bits), -8388736.0f);
+__device__ __forceinline__ unsigned long long q80_i8f2(uint32_t wx, int k) {
+    const uint32_t lo = __byte_perm(wx, 0x4B000000u, 0x7640u | static_cast<uint32_t>(k));
+    const uint32_t hi = __byte_perm(wx, 0x4B000000u, 0x7640u | static_cast<uint32_t>(k + 1));
+    return f2_add(f2_pack(__uint_as_float(lo), __uint_as_float(hi)), f2_pack(-8388736.0f, -8388736.0f));
 }
 
 // Local sum of 32-block b (34 bytes at blk: fp16 d, 32 int8) against the swizzled
-// activations xsw; d returned apart.
+// activations xsw; d returned apart.  Lanes k, k+1 of the reference's eight-lane order are
+// computed as one f32x2 pair at every step, so every lane sees the same operations in the
+// same order as the scalar form.
 __device__ __forceinline__ float q80_block_local(const uint8_t* blk, const float* xsw, int b, float& d) {
     d = h2f(*reinterpret_cast<const uint16_t*>(blk));
     const uintptr_t qa = reinterpret_cast<uintptr_t>(blk + 2);
     const uint32_t* base = reinterpret_cast<const uint32_t*>(qa & ~uintptr_t(3));
     const uint32_t sh = static_cast<uint32_t>(qa & 3) * 8;
-    float q[32], xv[32];
+    unsigned long long q[16], xv[16];   // element pairs (2m, 2m+1)
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const uint32_t w = __funnelshift_r(base[i], base[i + 1], sh) ^ 0x80808080u;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) q[4 * i + k] = q80_i8f(w, k);
+        q[2 * i] = q80_i8f2(w, 0);
+        q[2 * i + 1] = q80_i8f2(w, 2);
     }
     const float* xb = xsw + 32 * b;
     const int sw = b & 7;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const float4 f = *reinterpret_cast<const float4*>(xb + 4 * (i ^ sw));
-        xv[4 * i] = f.x, xv[4 * i + 1] = f.y, xv[4 * i + 2] = f.z, xv[4 * i + 3] = f.w;
+        xv[2 * i] = f2_pack(f.x, f.y);
+        xv[2 * i + 1] = f2_pack(f.z, f.w);
     }
-    float v[8];
+    unsigned long long v[4];   // (v_k, v_k+1), k = 0, 2, 4, 6
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        const float A = __fmaf_rn(q[k], xv[k], __fmul_rn(q[k + 8], xv[k + 8]));
-        const float B = __fmaf_rn(q[k + 16], xv[k + 16], __fmul_rn(q[k + 24], xv[k + 24]));
-        v[k] = __fadd_rn(B, A);
+    for (int m = 0; m < 4; ++m) {
+        const unsigned long long A = f2_fma(q[m], xv[m], f2_mul(q[m + 4], xv[m + 4]));       // lanes 2m, 2m+1 (+8)
+        const unsigned long long B = f2_fma(q[m + 8], xv[m + 8], f2_mul(q[m + 12], xv[m + 12]));   // (+16, +24)
+        v[m] = f2_add(B, A);
     }
-    float c[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) c[k] = __fadd_rn(v[k + 4], v[k]);
-    return __fadd_rn(__fadd_rn(c[3], c[1]), __fadd_rn(c[2], c[0]));
+    const unsigned long long c01 = f2_add(v[2], v[0]);   // (v4 + v0, v5 + v1)
+    const unsigned long long c23 = f2_add(v[3], v[1]);   // (v6 + v2, v7 + v3)
+    const float2 t = f2_unpack(f2_add(c23, c01));         // (c2 + c0, c3 + c1)
+    return __fadd_rn(t.y, t.x);
 }
 
 // Rows per stage for nb blocks per row: one slot of weights, and the (local, d) pairs of a
