@@ -311,8 +311,8 @@ __device__ void prefetch_norms(const DecodeParams& p, const Smem& s, int l, int 
     bulk_prefetch_l2(meta_f32(p, s.meta()[l].ffn_norm), N_EMBD * 4);
 }
 
-// L2 prefetch of this CTA's rows of layer l's weight phases kind0..3, fire and forget, no
-// multicast: their shared-memory copies, one layer later, then read L2.
+// L2 prefetch of this CTA's rows of layer l's weight phases kind0..3, fire and forget (each CTA
+// fetches its own rows): their shared-memory copies, one layer later, then read L2.
 __device__ __noinline__ void prefetch_layer_l2(const DecodeParams& p, const Smem& s, int l, int kind0) {
     if (!(p.sched & SCHED_L2_PREFETCH)) return;
     const LayerMeta& M = s.meta()[l];
